@@ -1,0 +1,415 @@
+"""Public op surface. CUDA tensors run the sm_100a kernels of ``csrc/``; CPU tensors run the fp32
+PyTorch implementations in ``reference.py``.
+
+Shapes follow the packed-varlen convention: activations are ``[T, features]`` row-major matrices,
+weights keep the HF ``[out_features, in_features]`` layout.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import reference
+from ._ext import available, check_status, native as _native_module, status_tensor
+
+
+class _Checked:
+    """Proxy over the extension: every kernel launch is followed by a check of its launch code
+    (argument validation or cudaError) so failures raise here with the op name."""
+
+    def __init__(self, ext):
+        self._ext = ext
+
+    def __getattr__(self, name):
+        fn = getattr(self._ext, name)
+
+        def call(*args):
+            fn(*args)
+            rc, msg = self._ext.last_error()
+            if rc != 0:
+                raise RuntimeError(f"native op {name} failed (code {rc}): {msg}")
+
+        return call
+
+
+_CHECKED = None
+
+
+def native():
+    global _CHECKED
+    if _CHECKED is None:
+        _CHECKED = _Checked(_native_module())
+    return _CHECKED
+
+__all__ = [
+    "available",
+    "check_status",
+    "gemm",
+    "linear",
+    "linear_dgrad",
+    "linear_wgrad",
+    "bias_grad",
+    "rmsnorm",
+    "rmsnorm_backward",
+    "rope_",
+    "swiglu",
+    "swiglu_backward",
+    "embedding",
+    "embedding_backward",
+    "attention_varlen",
+    "attention_varlen_backward",
+    "logsoftmax_label",
+    "logsoftmax_label_backward",
+    "policy_loss",
+    "grad_sumsq",
+    "adamw_step",
+    "paged_decode",
+    "kv_cache_write",
+    "sample",
+    "workspace",
+]
+
+_WORKSPACE: Dict[Tuple[int, str], torch.Tensor] = {}
+
+
+def workspace(device: torch.device, name: str, numel: int, dtype=torch.float32) -> torch.Tensor:
+    """Grow-only scratch buffers, one per (device, name). Callers use them within one stream."""
+    key = (device.index if device.index is not None else -1, name)
+    buf = _WORKSPACE.get(key)
+    if buf is None or buf.numel() < numel or buf.dtype != dtype:
+        buf = torch.empty(max(numel, 1), dtype=dtype, device=device)
+        _WORKSPACE[key] = buf
+    return buf[:numel]
+
+
+# ------------------------------------------------------------------------------------------------
+# GEMM / linear
+# ------------------------------------------------------------------------------------------------
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: Optional[torch.Tensor] = None,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+    bias: Optional[torch.Tensor] = None,
+    residual: Optional[torch.Tensor] = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    block_n: int = 0,
+    max_ctas: int = 0,
+) -> torch.Tensor:
+    """``out = alpha * A @ B^T + beta*out (+bias) (+residual)`` with A given as [M,K] (or [K,M] if
+    ``a_mn``) and B as [N,K] (or [K,N] if ``b_mn``)."""
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    if a.is_cuda:
+        native().gemm(a, a_mn, b, b_mn, out, alpha, beta, bias, residual, status_tensor(a.device), block_n, max_ctas)
+        return out
+    af = a.float().t() if a_mn else a.float()
+    bf = b.float() if b_mn else b.float().t()
+    acc = alpha * (af @ bf)
+    if beta != 0.0:
+        acc = acc + beta * out.float()
+    if bias is not None:
+        acc = acc + bias.float()
+    if residual is not None:
+        acc = acc + residual.float()
+    out.copy_(acc.to(out.dtype))
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, out=None) -> torch.Tensor:
+    """``y = x w^T (+b) (+residual)``; x [T, in], w [out, in]."""
+    return gemm(x, w, out, bias=bias, residual=residual, out_dtype=x.dtype)
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out=None, accumulate: bool = False) -> torch.Tensor:
+    """``dx = dy w`` (``+= `` into ``out`` when ``accumulate``); dy [T, out], w [out, in]."""
+    return gemm(dy, w, out, b_mn=True, beta=1.0 if accumulate else 0.0, out_dtype=dy.dtype)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, grad: torch.Tensor, accumulate: bool = True) -> torch.Tensor:
+    """``grad (+)= dy^T x`` in fp32; dy [T, out], x [T, in], grad [out, in] fp32."""
+    return gemm(dy, x, grad, a_mn=True, b_mn=True, beta=1.0 if accumulate else 0.0, out_dtype=torch.float32)
+
+
+def bias_grad(dy: torch.Tensor, grad: torch.Tensor, accumulate: bool = True) -> torch.Tensor:
+    if dy.is_cuda:
+        ws = workspace(dy.device, "colsum", ((dy.shape[0] + 63) // 64) * dy.shape[1])
+        native().bias_grad(dy, grad, ws, accumulate)
+        return grad
+    s = dy.float().sum(0)
+    if accumulate:
+        grad.add_(s)
+    else:
+        grad.copy_(s)
+    return grad
+
+
+# ------------------------------------------------------------------------------------------------
+# normalisation / positional / activation / embedding
+# ------------------------------------------------------------------------------------------------
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    if x.is_cuda:
+        y = out if out is not None else torch.empty_like(x)
+        rstd = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+        native().rmsnorm_fwd(x, w, y, rstd, eps)
+        return y, rstd
+    return reference.rmsnorm(x, w, eps)
+
+
+def rmsnorm_backward(dy, x, w, rstd, dx_accum=None, dw_grad=None, dw_accumulate: bool = True) -> torch.Tensor:
+    """Returns ``dx (+ dx_accum)``; adds the weight gradient into ``dw_grad`` (fp32) when given."""
+    if x.is_cuda:
+        dx = torch.empty_like(x)
+        ws = None
+        if dw_grad is not None:
+            ws = workspace(x.device, "rmsnorm_dw", ((x.shape[0] + 63) // 64) * x.shape[1])
+        native().rmsnorm_bwd(dy, x, w, rstd, dx_accum, dx, dw_grad, ws, dw_accumulate)
+        return dx
+    dx, dw = reference.rmsnorm_backward(dy, x, w, rstd)
+    if dw_grad is not None:
+        if dw_accumulate:
+            dw_grad.add_(dw)
+        else:
+            dw_grad.copy_(dw)
+    if dx_accum is not None:
+        dx = dx + dx_accum.float()
+    return dx.to(x.dtype)
+
+
+def rope_(qkv: torch.Tensor, pos: torch.Tensor, n_rot_heads: int, head_dim: int, theta: float, inverse: bool = False):
+    """Rotate the first ``n_rot_heads`` heads of each ``qkv`` row in place (q heads then k heads)."""
+    if qkv.is_cuda:
+        native().rope(qkv, pos, n_rot_heads, head_dim, theta, inverse)
+        return qkv
+    T = qkv.shape[0]
+    view = qkv[:, : n_rot_heads * head_dim].reshape(T, n_rot_heads, head_dim)
+    view.copy_(reference.apply_rope(view, pos.view(-1), theta, inverse))
+    return qkv
+
+
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    if gu.is_cuda:
+        h = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
+        native().swiglu_fwd(gu, h)
+        return h
+    return reference.swiglu(gu)
+
+
+def swiglu_backward(dh: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
+    if gu.is_cuda:
+        dgu = torch.empty_like(gu)
+        native().swiglu_bwd(dh, gu, dgu)
+        return dgu
+    return reference.swiglu_backward(dh, gu)
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+    if table.is_cuda:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+        native().embedding_fwd(ids.reshape(-1), table, out)
+        return out
+    return table[ids.reshape(-1)]
+
+
+def embedding_backward(ids: torch.Tensor, dout: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
+    if grad.is_cuda:
+        native().embedding_bwd(ids.reshape(-1), dout, grad)
+        return grad
+    grad.index_add_(0, ids.reshape(-1), dout.float())
+    return grad
+
+
+# ------------------------------------------------------------------------------------------------
+# attention
+# ------------------------------------------------------------------------------------------------
+def attention_varlen(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    max_seqlen: int,
+    n_heads: int,
+    n_kv_heads: int,
+    head_dim: int,
+    scale: Optional[float] = None,
+    causal: bool = True,
+    out: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """q: [T, Hq*D] (may be a strided view), k/v: [T, Hkv*D]. Returns (o [T, Hq*D], lse [Hq, T])."""
+    scale = reference.default_scale(head_dim) if scale is None else scale
+    T = q.shape[0]
+    if q.is_cuda:
+        if head_dim != 128:
+            raise ValueError("the native attention kernel supports head_dim 128")
+        o = out if out is not None else torch.empty(T, n_heads * head_dim, dtype=q.dtype, device=q.device)
+        lse = torch.empty(n_heads, T, dtype=torch.float32, device=q.device)
+        native().attn_fwd(q, k, v, o, lse, cu_seqlens, max_seqlen, n_heads, n_kv_heads, scale, causal,
+                          status_tensor(q.device))
+        return o, lse
+    o, lse = reference.attention_varlen(
+        q.reshape(T, n_heads, head_dim), k.reshape(T, n_kv_heads, head_dim), v.reshape(T, n_kv_heads, head_dim),
+        cu_seqlens, scale, causal,
+    )
+    return o.reshape(T, n_heads * head_dim), lse
+
+
+def attention_varlen_backward(
+    dout, q, k, v, o, lse, cu_seqlens, max_seqlen, n_heads, n_kv_heads, head_dim, scale=None, causal=True,
+    dq=None, dk=None, dv=None,
+):
+    """Gradients w.r.t. q, k, v. ``dq/dk/dv`` may be strided views into a fused d(qkv) buffer."""
+    scale = reference.default_scale(head_dim) if scale is None else scale
+    T = q.shape[0]
+    if q.is_cuda:
+        dq = dq if dq is not None else torch.empty(T, n_heads * head_dim, dtype=q.dtype, device=q.device)
+        dk = dk if dk is not None else torch.empty(T, n_kv_heads * head_dim, dtype=q.dtype, device=q.device)
+        dv = dv if dv is not None else torch.empty(T, n_kv_heads * head_dim, dtype=q.dtype, device=q.device)
+        acc = workspace(q.device, "attn_acc", 3 * T * n_heads * head_dim)
+        delta = workspace(q.device, "attn_delta", n_heads * T)
+        native().attn_bwd(q, k, v, o, dout, lse, delta, acc, dq, dk, dv, cu_seqlens, max_seqlen, n_heads,
+                          n_kv_heads, scale, causal, status_tensor(q.device))
+        return dq, dk, dv
+    with torch.enable_grad():
+        qf = q.detach().float().reshape(T, n_heads, head_dim).requires_grad_(True)
+        kf = k.detach().float().reshape(T, n_kv_heads, head_dim).requires_grad_(True)
+        vf = v.detach().float().reshape(T, n_kv_heads, head_dim).requires_grad_(True)
+        of, _ = reference.attention_varlen(qf, kf, vf, cu_seqlens, scale, causal)
+        gq, gk, gv = torch.autograd.grad(of, (qf, kf, vf), dout.float().reshape(T, n_heads, head_dim))
+    res = []
+    for g, dst in ((gq, dq), (gk, dk), (gv, dv)):
+        g = g.reshape(T, -1).to(q.dtype)
+        if dst is not None:
+            dst.copy_(g)
+            res.append(dst)
+        else:
+            res.append(g)
+    return tuple(res)
+
+
+# ------------------------------------------------------------------------------------------------
+# loss side
+# ------------------------------------------------------------------------------------------------
+def logsoftmax_label(logits: torch.Tensor, labels: torch.Tensor, with_entropy: bool = False):
+    """Per row: (label logprob, logsumexp, entropy or None). logits [n, V] bf16."""
+    if logits.is_cuda:
+        n = logits.shape[0]
+        lp = torch.empty(n, dtype=torch.float32, device=logits.device)
+        lse = torch.empty(n, dtype=torch.float32, device=logits.device)
+        ent = torch.empty(n, dtype=torch.float32, device=logits.device) if with_entropy else None
+        native().logsoftmax_label_fwd(logits, labels, lp, lse, ent)
+        return lp, lse, ent
+    lp, lse, ent = reference.logsoftmax_label(logits, labels)
+    return lp, lse, (ent if with_entropy else None)
+
+
+def logsoftmax_label_backward(logits: torch.Tensor, labels: torch.Tensor, lse: torch.Tensor, grad: torch.Tensor):
+    """Overwrites ``logits`` with d(logits) = grad * (onehot - softmax)."""
+    if logits.is_cuda:
+        native().logsoftmax_label_bwd(logits, labels, lse, grad)
+        return logits
+    probs = torch.exp(logits.float() - lse.unsqueeze(1))
+    d = -probs * grad.unsqueeze(1)
+    d[torch.arange(logits.shape[0]), labels] += grad
+    logits.copy_(d.to(logits.dtype))
+    return logits
+
+
+def policy_loss(lp, old_lp, adv, cfg, loss_scale: float):
+    """Fused objective. Returns (dlp [n] fp32 = d(loss*loss_scale)/d lp, stats float64[3])."""
+    if lp.is_cuda:
+        dlp = torch.empty_like(lp)
+        stats = torch.zeros(3, dtype=torch.float64, device=lp.device)
+        native().policy_loss(lp, old_lp.float(), adv.float(), dlp, stats, cfg.mode_id, cfg.clip_eps, cfg.gipo_sigma,
+                             cfg.sapo_tau_pos, cfg.sapo_tau_neg, cfg.kl_coef, loss_scale)
+        return dlp, stats
+    from ..algo.objectives import varlen_token_sum_loss
+
+    x = lp.detach().float().requires_grad_(True)
+    with torch.enable_grad():
+        loss, stats = varlen_token_sum_loss(x, old_lp, adv, cfg)
+        (g,) = torch.autograd.grad(loss * loss_scale, x)
+    return g, stats
+
+
+def grad_sumsq(flat_grad: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.zeros(1, dtype=torch.float64, device=flat_grad.device)
+    if flat_grad.is_cuda:
+        native().sumsq(flat_grad, out)
+        return out
+    out += flat_grad.double().pow(2).sum()
+    return out
+
+
+def adamw_step(master, m, v, grad, param_bf16, sumsq, lr, beta1, beta2, eps, weight_decay, max_norm, step):
+    """Fused clip (by the global norm in ``sumsq``) + AdamW; also zeroes ``grad``."""
+    bc1 = 1.0 - beta1 ** step
+    bc2_sqrt = math.sqrt(1.0 - beta2 ** step)
+    if master.is_cuda:
+        native().adamw(master, m, v, grad, param_bf16, sumsq, lr, beta1, beta2, eps, weight_decay, max_norm, bc1,
+                       bc2_sqrt)
+        return
+    coef = 1.0
+    if max_norm > 0:
+        norm = float(sumsq.sqrt())
+        coef = min(1.0, max_norm / (norm + 1e-6))
+    g = grad * coef
+    master.mul_(1 - lr * weight_decay)
+    m.mul_(beta1).add_(g, alpha=1 - beta1)
+    v.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+    denom = v.sqrt() / bc2_sqrt + eps
+    master.addcdiv_(m, denom, value=-lr / bc1)
+    param_bf16.copy_(master.to(param_bf16.dtype))
+    grad.zero_()
+
+
+# ------------------------------------------------------------------------------------------------
+# rollout
+# ------------------------------------------------------------------------------------------------
+def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads, scale, num_splits=1, out=None):
+    """q: [S, Hq*D] -> [S, Hq*D]."""
+    S = q.shape[0]
+    D = k_cache.shape[-1]
+    if q.is_cuda:
+        o = out if out is not None else torch.empty(S, n_heads * D, dtype=q.dtype, device=q.device)
+        part_o = workspace(q.device, "decode_o", S * n_heads * num_splits * D)
+        part_ml = workspace(q.device, "decode_ml", S * n_heads * num_splits * 2)
+        native().paged_decode(q, k_cache, v_cache, block_table, seq_lens, o, part_o, part_ml, n_heads, n_kv_heads,
+                              num_splits, scale)
+        return o
+    res = reference.paged_decode(q.reshape(S, n_heads, D), k_cache, v_cache, block_table, seq_lens, scale)
+    return res.reshape(S, n_heads * D)
+
+
+def kv_cache_write(k, v, k_cache, v_cache, slot_mapping, n_kv_heads):
+    if k.is_cuda:
+        native().kv_cache_write(k, v, k_cache, v_cache, slot_mapping, n_kv_heads)
+        return
+    valid = slot_mapping >= 0
+    slots = slot_mapping[valid].long()
+    D = k_cache.shape[-1]
+    kc = k_cache.view(-1, n_kv_heads, D)
+    vc = v_cache.view(-1, n_kv_heads, D)
+    kc[slots] = k[valid].reshape(-1, n_kv_heads, D).to(kc.dtype)
+    vc[slots] = v[valid].reshape(-1, n_kv_heads, D).to(vc.dtype)
+
+
+def sample(logits, temperature, seeds, offsets, num_chunks: int = 16, generator=None):
+    """Gumbel-max sampling per row; returns (tokens int64, logprob of the sampled token)."""
+    if logits.is_cuda:
+        rows = logits.shape[0]
+        tokens = torch.empty(rows, dtype=torch.long, device=logits.device)
+        lps = torch.empty(rows, dtype=torch.float32, device=logits.device)
+        part = workspace(logits.device, "sample_part", rows * num_chunks * 4)
+        native().sample_logits(logits, temperature, seeds, offsets, tokens, lps, part, num_chunks)
+        return tokens, lps
+    return reference.gumbel_sample_reference(logits, temperature, generator)

@@ -1,0 +1,692 @@
+// Packed-varlen causal attention (GQA) on the sm_100a tensor cores, head_dim 128.
+//
+// Forward, one CTA per (128-query tile, q head, sequence), 6 warps:
+//   warp 4     TMA producer: the Q tile once, then K/V tiles of 128 keys into a 2-stage ring.
+//   warp 5     MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers, then O += P_{j-1} V_{j-1}
+//              (P from shared memory, V as an MN-major operand) into a TMEM output accumulator.
+//   warps 0-3  softmax, one query row per thread (= one TMEM lane): tcgen05.ld the score row, mask,
+//              online max/sum in the log2 domain, write P (bf16, 128B-swizzled K-major) to smem.
+//              O is rescaled in TMEM only when the running max grows by more than 2^8, so most
+//              blocks need no correction pass; the final normalisation uses the same stale max.
+// Backward, one CTA per (128-key tile, q head, sequence): S^T = K Q^T and dP^T = V dO^T land in TMEM,
+// the softmax warps (one key row per thread) rebuild P^T and dS^T into smem, then dV += P^T dO,
+// dK += dS^T Q (accumulated in TMEM over all query tiles) and dQ_i = dS_i K (TMEM, drained with fp32
+// vector atomics). dS^T in smem serves both as the K-major A of dK and the MN-major A of dQ.
+// K/V gradients are written per q head in fp32 and summed over each GQA group by a reduction kernel.
+// No cluster multicast is used.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace accerl {
+
+constexpr int kHd = 128;        // head dim
+constexpr int kTile = 128;      // rows per q / kv tile
+constexpr int kChunk = 16384;   // one [128 rows x 64 bf16] 128B-swizzled chunk
+constexpr int kTileBytes = 2 * kChunk;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// K-major descriptor of a [128 rows x 128 elems] tile stored as two 64-element chunks; kk = 16-elem K step.
+ACCERL_DEVINL uint64_t desc_kmajor(uint32_t base, int kk) {
+  return make_sw128_desc(base + (kk >> 2) * kChunk + (kk & 3) * 32, 16, 1024);
+}
+// MN-major descriptor of the same physical tile when its rows are the K dimension.
+ACCERL_DEVINL uint64_t desc_mnmajor(uint32_t base, int kk) {
+  return make_sw128_desc(base + kk * 16 * 128, kChunk, 1024);
+}
+
+// Byte offset of 16-byte unit u (0..15) of row r inside a two-chunk swizzled tile.
+ACCERL_DEVINL uint32_t swz_offset(int r, int u) {
+  return (u >> 3) * kChunk + r * 128 + (((u & 7) ^ (r & 7)) << 4);
+}
+
+struct AttnFwdParams {
+  __nv_bfloat16* o;
+  float* lse;
+  const int* cu;
+  int max_tiles, T, Hq, Hkv;
+  long long ldo;
+  float scale_log2;
+  int causal;
+  int* status;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
+  const int head = blockIdx.x % p.Hq;
+  const int q_tile = p.max_tiles - 1 - static_cast<int>(blockIdx.x / p.Hq);
+  const int b = blockIdx.y;
+  const int seq_start = p.cu[b];
+  const int len = p.cu[b + 1] - seq_start;
+  if (q_tile * kTile >= len) return;
+  const int n_kv = p.causal ? q_tile + 1 : (len + kTile - 1) / kTile;
+  const int kvh = head / (p.Hq / p.Hkv);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + 2 * kTileBytes;
+  uint8_t* sP = sV + 2 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* v_full = bars + 3;     // [2]
+  uint64_t* kv_empty = bars + 5;   // [2]
+  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* s_free = bars + 9;     // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t tS = tbase;         // two score buffers: columns [0,128) and [128,256)
+  const uint32_t tO = tbase + 256;   // output accumulator: columns [256,384)
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const int qy = seq_start + q_tile * kTile;
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_2d(sQ, &tmQ, q_full, head * kHd, qy);
+      tma_load_2d(sQ + kChunk, &tmQ, q_full, head * kHd + 64, qy);
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1u, p.status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const int ky = seq_start + j * kTile;
+        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        tma_load_2d(sK + s * kTileBytes, &tmK, &k_full[s], kvh * kHd, ky);
+        tma_load_2d(sK + s * kTileBytes + kChunk, &tmK, &k_full[s], kvh * kHd + 64, ky);
+        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        tma_load_2d(sV + s * kTileBytes, &tmV, &v_full[s], kvh * kHd, ky);
+        tma_load_2d(sV + s * kTileBytes + kChunk, &tmV, &v_full[s], kvh * kHd + 64, ky);
+      }
+      if (!ok) {
+        mbar_wait(q_full, 0, nullptr, 0, 20000000ull);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, p.status, kStatusTimeoutMma);
+      for (int j = 0; j <= n_kv && ok; ++j) {
+        if (j < n_kv) {
+          const int s = j & 1;
+          if (!mbar_wait(&k_full[s], (j >> 1) & 1, p.status, kStatusTimeoutMma)) break;
+          if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1u, p.status, kStatusTimeoutMma)) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tS + s * 128, desc_kmajor(q_addr, kk), desc_kmajor(k_addr, kk), idesc_s, kk > 0);
+          umma_commit(&s_full[s]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int s2 = jj & 1;
+          if (!mbar_wait(p_full, jj & 1, p.status, kStatusTimeoutMma)) break;
+          if (!mbar_wait(&v_full[s2], (jj >> 1) & 1, p.status, kStatusTimeoutMma)) break;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sV + s2 * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tO, desc_kmajor(p_addr, kk), desc_mnmajor(v_addr, kk), idesc_o, (jj > 0) || (kk > 0));
+          umma_commit(o_done);
+          umma_commit(&kv_empty[s2]);
+        }
+      }
+    }
+  } else {
+    // ---------------- softmax warps 0..3: thread = query row ----------------
+    const int r = threadIdx.x;  // 0..127 == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int q_pos = q_tile * kTile + r;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int bsel = j & 1;
+      if (!mbar_wait(&s_full[bsel], (j >> 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + bsel * 128 + c * 32 + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * p.scale_log2;
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[bsel]);
+      if (j == n_kv - 1) {
+        const int kbase = j * kTile;
+#pragma unroll
+        for (int e = 0; e < 128; ++e) {
+          const int kp = kbase + e;
+          if ((p.causal && kp > q_pos) || kp >= len) x[e] = -INFINITY;
+        }
+      }
+      float mx = x[0];
+#pragma unroll
+      for (int e = 1; e < 128; ++e) mx = fmaxf(mx, x[e]);
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      const float m_new = fmaxf(m_used, mx);
+      const bool need = m_new > m_used + 8.0f;
+      float alpha = 1.f;
+      if (need) {
+        alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
+        m_used = m_new;
+        l *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tO + c * 32 + lane_off, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+          tmem_st32(tO + c * 32 + lane_off, v);
+        }
+        tmem_wait_st();
+      }
+      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float p0 = exp2f(x[u * 8 + 2 * h] - m_eff);
+          const float p1 = exp2f(x[u * 8 + 2 * h + 1] - m_eff);
+          l += p0 + p1;
+          w[h] = pack_bf16x2(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(sP + swz_offset(r, u)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_async_shared();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait(o_done, (n_kv - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      const bool row_ok = q_pos < len;
+      __nv_bfloat16* orow = p.o + static_cast<long long>(seq_start + q_pos) * p.ldo + head * kHd;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tO + c * 32 + lane_off, v);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 o;
+            o.x = pack_bf16x2(__uint_as_float(v[g * 8 + 0]) * inv_l, __uint_as_float(v[g * 8 + 1]) * inv_l);
+            o.y = pack_bf16x2(__uint_as_float(v[g * 8 + 2]) * inv_l, __uint_as_float(v[g * 8 + 3]) * inv_l);
+            o.z = pack_bf16x2(__uint_as_float(v[g * 8 + 4]) * inv_l, __uint_as_float(v[g * 8 + 5]) * inv_l);
+            o.w = pack_bf16x2(__uint_as_float(v[g * 8 + 6]) * inv_l, __uint_as_float(v[g * 8 + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = o;
+          }
+        }
+      }
+      if (row_ok) {
+        const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+        p.lse[static_cast<long long>(head) * p.T + seq_start + q_pos] = (m_eff + log2f(l)) * kLn2;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// backward
+// ------------------------------------------------------------------------------------------------
+struct AttnBwdParams {
+  const float* lse;    // [Hq, T]
+  const float* delta;  // [Hq, T]
+  float* dq_acc;       // [T, Hq*128] fp32, pre-zeroed
+  float* dk_part;      // [T, Hq*128] fp32
+  float* dv_part;      // [T, Hq*128] fp32
+  const int* cu;
+  int max_tiles, T, Hq, Hkv;
+  float scale, scale_log2;
+  int causal;
+  int* status;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const AttnBwdParams p) {
+  const int head = blockIdx.x % p.Hq;
+  const int kt = static_cast<int>(blockIdx.x / p.Hq);
+  const int b = blockIdx.y;
+  const int seq_start = p.cu[b];
+  const int len = p.cu[b + 1] - seq_start;
+  if (kt * kTile >= len) return;
+  const int ntiles = (len + kTile - 1) / kTile;
+  const int q_first = p.causal ? kt : 0;
+  const int nq = ntiles - q_first;
+  const int kvh = head / (p.Hq / p.Hkv);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTileBytes;
+  uint8_t* sQ = sV + kTileBytes;
+  uint8_t* sDO = sQ + kTileBytes;
+  uint8_t* sP = sDO + kTileBytes;
+  uint8_t* sDS = sP + kTileBytes;
+  float* s_lse = reinterpret_cast<float*>(sDS + kTileBytes);
+  float* s_delta = s_lse + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + 128);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* q_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* ps_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_free = bars + 6;
+  uint64_t* acc_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(ps_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(acc_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t tS = tbase;          // S^T, then dQ
+  const uint32_t tDP = tbase + 128;   // dP^T
+  const uint32_t tDV = tbase + 256;
+  const uint32_t tDK = tbase + 384;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const int ky = seq_start + kt * kTile;
+      mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
+      tma_load_2d(sK, &tmK, kv_full, kvh * kHd, ky);
+      tma_load_2d(sK + kChunk, &tmK, kv_full, kvh * kHd + 64, ky);
+      tma_load_2d(sV, &tmV, kv_full, kvh * kHd, ky);
+      tma_load_2d(sV + kChunk, &tmV, kv_full, kvh * kHd + 64, ky);
+      for (int i = 0; i < nq; ++i) {
+        if (!mbar_wait(q_empty, (i & 1) ^ 1u, p.status, kStatusTimeoutProducer)) break;
+        const int qy = seq_start + (q_first + i) * kTile;
+        mbar_arrive_expect_tx(q_full, 2 * kTileBytes);
+        tma_load_2d(sQ, &tmQ, q_full, head * kHd, qy);
+        tma_load_2d(sQ + kChunk, &tmQ, q_full, head * kHd + 64, qy);
+        tma_load_2d(sDO, &tmDO, q_full, head * kHd, qy);
+        tma_load_2d(sDO + kChunk, &tmDO, q_full, head * kHd + 64, qy);
+      }
+      mbar_wait(kv_full, 0, nullptr, 0, 20000000ull);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_kk = make_idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_kmn = make_idesc_bf16_f32(128, 128, false, true);
+      constexpr uint32_t idesc_mnmn = make_idesc_bf16_f32(128, 128, true, true);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
+      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0, p.status, kStatusTimeoutMma);
+      for (int i = 0; i < nq && ok; ++i) {
+        if (!mbar_wait(q_full, i & 1, p.status, kStatusTimeoutMma)) break;
+        if (!mbar_wait(dq_free, (i & 1) ^ 1u, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_bf16(tS, desc_kmajor(k_addr, kk), desc_kmajor(q_addr, kk), idesc_kk, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) umma_bf16(tDP, desc_kmajor(v_addr, kk), desc_kmajor(do_addr, kk), idesc_kk, kk > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(ps_full, i & 1, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tDV, desc_kmajor(p_addr, kk), desc_mnmajor(do_addr, kk), idesc_kmn, (i > 0) || (kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tDK, desc_kmajor(ds_addr, kk), desc_mnmajor(q_addr, kk), idesc_kmn, (i > 0) || (kk > 0));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tS, desc_mnmajor(ds_addr, kk), desc_mnmajor(k_addr, kk), idesc_mnmn, kk > 0);
+        umma_commit(dq_full);
+        umma_commit(q_empty);
+      }
+      umma_commit(acc_done);
+    }
+  } else {
+    const int r = threadIdx.x;  // key row for S^T/dP^T/dK/dV; query row for dQ
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int k_pos = kt * kTile + r;
+    const bool key_valid = k_pos < len;
+    const int ldacc = p.Hq * kHd;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int qt = q_first + i;
+      const int q_pos_t = qt * kTile + r;
+      named_bar_sync(1, 128);
+      if (q_pos_t < len) {
+        const long long idx = static_cast<long long>(head) * p.T + seq_start + q_pos_t;
+        s_lse[r] = p.lse[idx] * kLog2e;
+        s_delta[r] = p.delta[idx];
+      } else {
+        s_lse[r] = INFINITY;
+        s_delta[r] = 0.f;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(s_full, i & 1, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + c * 32 + lane_off, sv);
+        tmem_ld32(tDP + c * 32 + lane_off, dv);
+        tmem_wait_ld();
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int ql = c * 32 + e + h;
+            const int q_pos = qt * kTile + ql;
+            const bool valid = key_valid && q_pos < len && (!p.causal || q_pos >= k_pos);
+            const float pr = valid ? exp2f(__uint_as_float(sv[e + h]) * p.scale_log2 - s_lse[ql]) : 0.f;
+            pv[h] = pr;
+            dsv[h] = pr * (__uint_as_float(dv[e + h]) - s_delta[ql]) * p.scale;
+          }
+          pw[e >> 1] = pack_bf16x2(pv[0], pv[1]);
+          dw[e >> 1] = pack_bf16x2(dsv[0], dsv[1]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t off = swz_offset(r, c * 4 + u);
+          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
+          *reinterpret_cast<uint4*>(sDS + off) = make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
+        }
+      }
+      fence_async_shared();
+      tc_fence_before();
+      mbar_arrive(ps_full);
+      if (!mbar_wait(dq_full, i & 1, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q_pos = qt * kTile + r;
+      float* dqrow = p.dq_acc + static_cast<long long>(seq_start + q_pos) * ldacc + head * kHd;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + c * 32 + lane_off, v);
+        tmem_wait_ld();
+        if (q_pos < len) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            float4 val = make_float4(__uint_as_float(v[g * 4]), __uint_as_float(v[g * 4 + 1]),
+                                     __uint_as_float(v[g * 4 + 2]), __uint_as_float(v[g * 4 + 3]));
+            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + g * 4), val);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    if (ok && mbar_wait(acc_done, 0, p.status, kStatusTimeoutEpilogue)) {
+      tc_fence_after();
+      const long long rowoff = static_cast<long long>(seq_start + k_pos) * ldacc + head * kHd;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32], w[32];
+        tmem_ld32(tDV + c * 32 + lane_off, v);
+        tmem_ld32(tDK + c * 32 + lane_off, w);
+        tmem_wait_ld();
+        if (key_valid) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            *reinterpret_cast<float4*>(p.dv_part + rowoff + c * 32 + g * 4) =
+                make_float4(__uint_as_float(v[g * 4]), __uint_as_float(v[g * 4 + 1]), __uint_as_float(v[g * 4 + 2]),
+                            __uint_as_float(v[g * 4 + 3]));
+            *reinterpret_cast<float4*>(p.dk_part + rowoff + c * 32 + g * 4) =
+                make_float4(__uint_as_float(w[g * 4]), __uint_as_float(w[g * 4 + 1]), __uint_as_float(w[g * 4 + 2]),
+                            __uint_as_float(w[g * 4 + 3]));
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// delta[h, t] = sum_d dO[t, h, d] * O[t, h, d]; one warp per (t, h).
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                  float* __restrict__ delta, int T, int Hq, long long ldo, long long lddo) {
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<long long>(T) * Hq) return;
+  const int t = static_cast<int>(w / Hq);
+  const int h = static_cast<int>(w % Hq);
+  const uint2 a = *reinterpret_cast<const uint2*>(o + t * ldo + h * kHd + lane * 4);
+  const uint2 bb = *reinterpret_cast<const uint2*>(dout + t * lddo + h * kHd + lane * 4);
+  const float2 a0 = unpack_bf16x2(a.x), a1 = unpack_bf16x2(a.y), b0 = unpack_bf16x2(bb.x), b1 = unpack_bf16x2(bb.y);
+  float s = a0.x * b0.x + a0.y * b0.y + a1.x * b1.x + a1.y * b1.y;
+  s = warp_sum(s);
+  if (lane == 0) delta[static_cast<long long>(h) * T + t] = s;
+}
+
+// dq (bf16, strided) from the fp32 accumulator; dk/dv from per-q-head partials summed over the GQA group.
+__global__ void attn_bwd_finalize_kernel(const float* __restrict__ dq_acc, const float* __restrict__ dk_part,
+                                         const float* __restrict__ dv_part, __nv_bfloat16* __restrict__ dq,
+                                         __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int T, int Hq,
+                                         int Hkv, long long lddq, long long lddk, long long lddv) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // over T*Hq*128/4
+  const long long per_t = static_cast<long long>(Hq) * kHd / 4;
+  if (idx >= static_cast<long long>(T) * per_t) return;
+  const int t = static_cast<int>(idx / per_t);
+  const int c4 = static_cast<int>(idx % per_t) * 4;  // column inside the q-head space
+  const float4 q = *reinterpret_cast<const float4*>(dq_acc + static_cast<long long>(t) * Hq * kHd + c4);
+  uint2 qo;
+  qo.x = pack_bf16x2(q.x, q.y);
+  qo.y = pack_bf16x2(q.z, q.w);
+  *reinterpret_cast<uint2*>(dq + t * lddq + c4) = qo;
+  const int group = Hq / Hkv;
+  const int h = c4 / kHd;
+  if (h % group != 0) return;  // the first head of each group writes the group sum
+  const int d = c4 % kHd;
+  const int kvh = h / group;
+  float4 sk = make_float4(0, 0, 0, 0), sv = make_float4(0, 0, 0, 0);
+  for (int g = 0; g < group; ++g) {
+    const long long off = static_cast<long long>(t) * Hq * kHd + (h + g) * kHd + d;
+    const float4 a = *reinterpret_cast<const float4*>(dk_part + off);
+    const float4 b = *reinterpret_cast<const float4*>(dv_part + off);
+    sk.x += a.x; sk.y += a.y; sk.z += a.z; sk.w += a.w;
+    sv.x += b.x; sv.y += b.y; sv.z += b.z; sv.w += b.w;
+  }
+  uint2 ko, vo;
+  ko.x = pack_bf16x2(sk.x, sk.y);
+  ko.y = pack_bf16x2(sk.z, sk.w);
+  vo.x = pack_bf16x2(sv.x, sv.y);
+  vo.y = pack_bf16x2(sv.z, sv.w);
+  *reinterpret_cast<uint2*>(dk + t * lddk + kvh * kHd + d) = ko;
+  *reinterpret_cast<uint2*>(dv + t * lddv + kvh * kHd + d) = vo;
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Tile map over a [T, width] bf16 matrix with a 64-column x 128-row box, 128B swizzle.
+bool attn_map(CUtensorMap* m, const void* ptr, int T, int width, long long ld) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+constexpr int kFwdSmem = 6 * kTileBytes + 1024 + 256;
+constexpr int kBwdSmem = 6 * kTileBytes + 1024 + 1024 + 256;
+
+}  // namespace
+}  // namespace accerl
+
+using namespace accerl;
+
+extern "C" int accerl_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_seqlens,
+                               int num_seqs, int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq,
+                               long long ldk, long long ldv, long long ldo, float scale, int causal, int* status,
+                               cudaStream_t s) {
+  if (num_seqs <= 0 || total_tokens <= 0) return 0;
+  if (Hq % Hkv) return -1;
+  if ((ldq | ldk | ldv | ldo) & 7) return -2;
+  CUtensorMap mq, mk, mv;
+  if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq) || !attn_map(&mk, k, total_tokens, Hkv * kHd, ldk) ||
+      !attn_map(&mv, v, total_tokens, Hkv * kHd, ldv))
+    return -3;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  AttnFwdParams p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.lse = lse;
+  p.cu = cu_seqlens;
+  p.max_tiles = (max_seqlen + kTile - 1) / kTile;
+  p.T = total_tokens;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.ldo = ldo;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = causal;
+  p.status = status;
+  dim3 grid(p.max_tiles * Hq, num_seqs);
+  attn_fwd_kernel<<<grid, 192, kFwdSmem, s>>>(mq, mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout,
+                               const float* lse, float* delta, float* dq_acc, void* dq, void* dk, void* dv,
+                               const int* cu_seqlens, int num_seqs, int max_seqlen, int total_tokens, int Hq, int Hkv,
+                               long long ldq, long long ldk, long long ldv, long long ldo, long long lddo,
+                               long long lddq, long long lddk, long long lddv, float scale, int causal, int* status,
+                               cudaStream_t s) {
+  if (num_seqs <= 0 || total_tokens <= 0) return 0;
+  if (Hq % Hkv) return -1;
+  if ((ldq | ldk | ldv | ldo | lddo | lddq | lddk | lddv) & 7) return -2;
+  CUtensorMap mq, mk, mv, mdo;
+  if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq) || !attn_map(&mk, k, total_tokens, Hkv * kHd, ldk) ||
+      !attn_map(&mv, v, total_tokens, Hkv * kHd, ldv) || !attn_map(&mdo, dout, total_tokens, Hq * kHd, lddo))
+    return -3;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  const long long nwarps = (long long)total_tokens * Hq;
+  attn_delta_kernel<<<(unsigned)((nwarps * 32 + 255) / 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, total_tokens, Hq, ldo, lddo);
+  const long long acc_elems = (long long)total_tokens * Hq * kHd;
+  // dq_acc holds [dq | dk_part | dv_part] contiguously (3 * acc_elems floats); only dq needs zeros.
+  cudaMemsetAsync(dq_acc, 0, acc_elems * sizeof(float), s);
+  AttnBwdParams p;
+  p.lse = lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dk_part = dq_acc + acc_elems;
+  p.dv_part = dq_acc + 2 * acc_elems;
+  p.cu = cu_seqlens;
+  p.max_tiles = (max_seqlen + kTile - 1) / kTile;
+  p.T = total_tokens;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = scale;
+  p.scale_log2 = scale * kLog2e;
+  p.causal = causal;
+  p.status = status;
+  dim3 grid(p.max_tiles * Hq, num_seqs);
+  attn_bwd_kernel<<<grid, 192, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
+  const long long n4 = acc_elems / 4;
+  attn_bwd_finalize_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(
+      dq_acc, p.dk_part, p.dv_part, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, total_tokens, Hq, Hkv,
+      lddq, lddk, lddv);
+  return (int)cudaGetLastError();
+}

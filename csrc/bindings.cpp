@@ -1,0 +1,353 @@
+// Python bindings of the sm_100a kernels. Kernels live in .cu files without torch headers and
+// expose extern "C" launchers; this file validates tensors and forwards raw pointers together with
+// the current CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+extern "C" {
+int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn, void* C,
+                     long long ldc, int c_f32, int M, int N, int K, float alpha, float beta, const void* bias,
+                     const void* residual, long long ldr, int* status, int block_n, int max_ctas, cudaStream_t stream);
+int accerl_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int H, long long ldx,
+                       long long ldy, float eps, cudaStream_t s);
+int accerl_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, const void* dx_accum, void* dx,
+                       float* dw, float* workspace, int rows, int H, long long ld, int dw_accumulate, cudaStream_t s);
+int accerl_bias_grad(const void* dy, float* db, float* workspace, int rows, int N, long long ld, int accumulate,
+                     cudaStream_t s);
+int accerl_rope(void* qkv, const long long* pos, int T, int n_rot_heads, int D, long long ld, float theta, int inverse,
+                cudaStream_t s);
+int accerl_swiglu_fwd(const void* gu, void* h, int T, int I, cudaStream_t s);
+int accerl_swiglu_bwd(const void* dh, const void* gu, void* dgu, int T, int I, cudaStream_t s);
+int accerl_embedding_fwd(const long long* ids, const void* table, void* out, int T, int H, cudaStream_t s);
+int accerl_embedding_bwd(const long long* ids, const void* dout, float* grad, int T, int H, cudaStream_t s);
+int accerl_logsoftmax_label_fwd(const void* logits, long long ld, const long long* labels, float* logprob, float* lse,
+                                float* entropy, int rows, int V, cudaStream_t s);
+int accerl_logsoftmax_label_bwd(void* logits, long long ld, const long long* labels, const float* lse,
+                                const float* grad, int rows, int V, cudaStream_t s);
+int accerl_policy_loss(const float* lp, const float* old_lp, const float* adv, float* dlp, double* stats, int n,
+                       int mode, float clip_eps, float gipo_sigma, float tau_pos, float tau_neg, float kl_coef,
+                       float loss_scale, cudaStream_t s);
+int accerl_sumsq(const float* g, long long n, double* out, cudaStream_t s);
+int accerl_adamw(float* master, float* m, float* v, float* grad, void* param, long long n, const double* sumsq,
+                 float lr, float beta1, float beta2, float eps, float weight_decay, float max_norm, float bc1,
+                 float bc2_sqrt, cudaStream_t s);
+int accerl_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_seqlens,
+                    int num_seqs, int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq, long long ldk,
+                    long long ldv, long long ldo, float scale, int causal, int* status, cudaStream_t s);
+int accerl_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
+                    float* delta, float* dq_acc, void* dq, void* dk, void* dv, const int* cu_seqlens, int num_seqs,
+                    int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq, long long ldk, long long ldv,
+                    long long ldo, long long lddo, long long lddq, long long lddk, long long lddv, float scale,
+                    int causal, int* status, cudaStream_t s);
+int accerl_paged_decode(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
+                        const int* seq_lens, void* out, float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv,
+                        int max_blocks_per_seq, int block_size, int num_splits, float scale, long long ldq,
+                        long long ldo, cudaStream_t s);
+int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping, int T,
+                          int Hkv, long long ldk, long long ldv, cudaStream_t s);
+int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
+                         const unsigned long long* seeds, const long long* offsets, long long* out_tokens,
+                         float* out_logprobs, float* part, int num_chunks, cudaStream_t s);
+}
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Launch status of the most recent call on this thread; Python reads it through last_error() and
+// raises there, so no C++ exception ever crosses the kernel-launch path.
+thread_local int g_last_rc = 0;
+thread_local const char* g_last_what = "";
+
+void check(int rc, const char* what) {
+  g_last_rc = rc;
+  g_last_what = what;
+}
+
+std::tuple<int64_t, std::string> last_error() {
+  const int rc = g_last_rc;
+  std::string msg = g_last_what;
+  if (rc > 0) msg += std::string(": ") + cudaGetErrorString(static_cast<cudaError_t>(rc));
+  g_last_rc = 0;
+  g_last_what = "";
+  return {rc, msg};
+}
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_F32(x) TORCH_CHECK((x).scalar_type() == at::kFloat, #x " must be float32")
+#define CHECK_I64(x) TORCH_CHECK((x).scalar_type() == at::kLong, #x " must be int64")
+#define CHECK_I32(x) TORCH_CHECK((x).scalar_type() == at::kInt, #x " must be int32")
+
+const void* opt_ptr(const c10::optional<at::Tensor>& t) { return t.has_value() ? t->data_ptr() : nullptr; }
+
+int* status_ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? t->data_ptr<int>() : nullptr;
+}
+
+// Row-major 2-D view helpers: leading dimension = stride(0), last dim contiguous.
+long long ld_of(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 2, "expected a 2-D tensor");
+  TORCH_CHECK(t.stride(1) == 1, "last dimension must be contiguous");
+  return t.stride(0);
+}
+
+// out = alpha * op(a) op(b) + beta*out (+bias)(+residual)
+// a: [M,K] (a_mn=false) or [K,M] (a_mn=true); b: [N,K] (b_mn=false) or [K,N] (b_mn=true)
+void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, double alpha, double beta,
+          const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
+          const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  CHECK_CUDA(out);
+  CHECK_BF16(a);
+  CHECK_BF16(b);
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "out must be bf16 or f32");
+  const int M = a_mn ? a.size(1) : a.size(0);
+  const int K = a_mn ? a.size(0) : a.size(1);
+  const int N = b_mn ? b.size(1) : b.size(0);
+  const int Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm: inner dimensions differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm: output shape mismatch");
+  long long ldr = 0;
+  if (residual.has_value()) {
+    CHECK_BF16(*residual);
+    TORCH_CHECK(residual->size(0) == M && residual->size(1) == N, "gemm: residual shape mismatch");
+    ldr = ld_of(*residual);
+  }
+  if (bias.has_value()) {
+    CHECK_BF16(*bias);
+    TORCH_CHECK(bias->numel() == N && bias->is_contiguous(), "gemm: bias must be contiguous [N]");
+  }
+  const c10::cuda::CUDAGuard guard(a.device());
+  check(accerl_gemm_bf16(a.data_ptr(), ld_of(a), a_mn, b.data_ptr(), ld_of(b), b_mn, out.data_ptr(), ld_of(out),
+                         out.scalar_type() == at::kFloat, M, N, K, static_cast<float>(alpha), static_cast<float>(beta),
+                         opt_ptr(bias), opt_ptr(residual), ldr, status_ptr(status), static_cast<int>(block_n),
+                         static_cast<int>(max_ctas), cur_stream()),
+        "gemm");
+}
+
+at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& rstd,
+                       double eps) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(y);
+  const int rows = x.size(0), H = x.size(1);
+  float* r = rstd.has_value() ? rstd->data_ptr<float>() : nullptr;
+  check(accerl_rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), r, rows, H, ld_of(x), ld_of(y),
+                           static_cast<float>(eps), cur_stream()),
+        "rmsnorm_fwd");
+  return y;
+}
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                 const c10::optional<at::Tensor>& dx_accum, at::Tensor& dx, const c10::optional<at::Tensor>& dw,
+                 const c10::optional<at::Tensor>& workspace, bool dw_accumulate) {
+  CHECK_BF16(dy);
+  CHECK_BF16(x);
+  CHECK_F32(rstd);
+  const int rows = x.size(0), H = x.size(1);
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous(), "rmsnorm_bwd: contiguous inputs");
+  float* dwp = nullptr;
+  float* ws = nullptr;
+  if (dw.has_value()) {
+    CHECK_F32(*dw);
+    TORCH_CHECK(workspace.has_value() && workspace->numel() >= ((rows + 63) / 64) * (long long)H,
+                "rmsnorm_bwd: workspace too small");
+    dwp = dw->data_ptr<float>();
+    ws = workspace->data_ptr<float>();
+  }
+  check(accerl_rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), opt_ptr(dx_accum),
+                           dx.data_ptr(), dwp, ws, rows, H, H, dw_accumulate, cur_stream()),
+        "rmsnorm_bwd");
+}
+
+void bias_grad(const at::Tensor& dy, at::Tensor& db, at::Tensor& workspace, bool accumulate) {
+  CHECK_BF16(dy);
+  CHECK_F32(db);
+  const int rows = dy.size(0), N = dy.size(1);
+  TORCH_CHECK(workspace.numel() >= ((rows + 63) / 64) * (long long)N, "bias_grad: workspace too small");
+  check(accerl_bias_grad(dy.data_ptr(), db.data_ptr<float>(), workspace.data_ptr<float>(), rows, N, ld_of(dy),
+                         accumulate, cur_stream()),
+        "bias_grad");
+}
+
+void rope(at::Tensor& qkv, const at::Tensor& pos, int64_t n_rot_heads, int64_t head_dim, double theta, bool inverse) {
+  CHECK_BF16(qkv);
+  CHECK_I64(pos);
+  TORCH_CHECK(pos.is_contiguous() && pos.numel() == qkv.size(0), "rope: positions must be [T]");
+  check(accerl_rope(qkv.data_ptr(), reinterpret_cast<long long*>(pos.data_ptr<int64_t>()), qkv.size(0), n_rot_heads, head_dim, ld_of(qkv),
+                    static_cast<float>(theta), inverse, cur_stream()),
+        "rope");
+}
+
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& h) {
+  CHECK_BF16(gu);
+  TORCH_CHECK(gu.is_contiguous() && h.is_contiguous(), "swiglu: contiguous");
+  check(accerl_swiglu_fwd(gu.data_ptr(), h.data_ptr(), gu.size(0), h.size(1), cur_stream()), "swiglu_fwd");
+}
+
+void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, at::Tensor& dgu) {
+  TORCH_CHECK(dh.is_contiguous() && gu.is_contiguous() && dgu.is_contiguous(), "swiglu_bwd: contiguous");
+  check(accerl_swiglu_bwd(dh.data_ptr(), gu.data_ptr(), dgu.data_ptr(), gu.size(0), dh.size(1), cur_stream()),
+        "swiglu_bwd");
+}
+
+void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
+  CHECK_I64(ids);
+  CHECK_BF16(table);
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embedding: contiguous");
+  check(accerl_embedding_fwd(reinterpret_cast<long long*>(ids.data_ptr<int64_t>()), table.data_ptr(), out.data_ptr(), ids.numel(), table.size(1),
+                             cur_stream()),
+        "embedding_fwd");
+}
+
+void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& grad) {
+  CHECK_I64(ids);
+  CHECK_F32(grad);
+  check(accerl_embedding_bwd(reinterpret_cast<long long*>(ids.data_ptr<int64_t>()), dout.data_ptr(), grad.data_ptr<float>(), ids.numel(),
+                             grad.size(1), cur_stream()),
+        "embedding_bwd");
+}
+
+void logsoftmax_label_fwd(const at::Tensor& logits, const at::Tensor& labels, at::Tensor& logprob, at::Tensor& lse,
+                          const c10::optional<at::Tensor>& entropy) {
+  CHECK_BF16(logits);
+  CHECK_I64(labels);
+  float* ent = entropy.has_value() ? entropy->data_ptr<float>() : nullptr;
+  check(accerl_logsoftmax_label_fwd(logits.data_ptr(), ld_of(logits), reinterpret_cast<long long*>(labels.data_ptr<int64_t>()),
+                                    logprob.data_ptr<float>(), lse.data_ptr<float>(), ent, logits.size(0),
+                                    logits.size(1), cur_stream()),
+        "logsoftmax_label_fwd");
+}
+
+void logsoftmax_label_bwd(at::Tensor& logits, const at::Tensor& labels, const at::Tensor& lse, const at::Tensor& grad) {
+  check(accerl_logsoftmax_label_bwd(logits.data_ptr(), ld_of(logits), reinterpret_cast<long long*>(labels.data_ptr<int64_t>()), lse.data_ptr<float>(),
+                                    grad.data_ptr<float>(), logits.size(0), logits.size(1), cur_stream()),
+        "logsoftmax_label_bwd");
+}
+
+void policy_loss(const at::Tensor& lp, const at::Tensor& old_lp, const at::Tensor& adv, at::Tensor& dlp,
+                 at::Tensor& stats, int64_t mode, double clip_eps, double gipo_sigma, double tau_pos, double tau_neg,
+                 double kl_coef, double loss_scale) {
+  CHECK_F32(lp);
+  CHECK_F32(old_lp);
+  CHECK_F32(adv);
+  TORCH_CHECK(stats.scalar_type() == at::kDouble && stats.numel() >= 3, "stats must be float64[3]");
+  check(accerl_policy_loss(lp.data_ptr<float>(), old_lp.data_ptr<float>(), adv.data_ptr<float>(),
+                           dlp.data_ptr<float>(), stats.data_ptr<double>(), lp.numel(), mode, clip_eps, gipo_sigma,
+                           tau_pos, tau_neg, kl_coef, loss_scale, cur_stream()),
+        "policy_loss");
+}
+
+void sumsq(const at::Tensor& g, at::Tensor& out) {
+  CHECK_F32(g);
+  TORCH_CHECK(out.scalar_type() == at::kDouble, "sumsq: out must be float64");
+  check(accerl_sumsq(g.data_ptr<float>(), g.numel(), out.data_ptr<double>(), cur_stream()), "sumsq");
+}
+
+void adamw(at::Tensor& master, at::Tensor& m, at::Tensor& v, at::Tensor& grad, at::Tensor& param,
+           const at::Tensor& sumsq_t, double lr, double beta1, double beta2, double eps, double weight_decay,
+           double max_norm, double bc1, double bc2_sqrt) {
+  CHECK_F32(master);
+  CHECK_BF16(param);
+  TORCH_CHECK(master.numel() == param.numel() && grad.numel() == param.numel(), "adamw: size mismatch");
+  check(accerl_adamw(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(),
+                     param.data_ptr(), master.numel(), sumsq_t.data_ptr<double>(), lr, beta1, beta2, eps, weight_decay,
+                     max_norm, bc1, bc2_sqrt, cur_stream()),
+        "adamw");
+}
+
+// q: [T, Hq*D] view (row stride ldq), k/v: [T, Hkv*D], o: [T, Hq*D]; lse: [Hq, T] fp32
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+              const at::Tensor& cu_seqlens, int64_t max_seqlen, int64_t Hq, int64_t Hkv, double scale, bool causal,
+              const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(q);
+  CHECK_BF16(k);
+  CHECK_BF16(v);
+  CHECK_BF16(o);
+  CHECK_F32(lse);
+  CHECK_I32(cu_seqlens);
+  check(accerl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
+                        cu_seqlens.data_ptr<int>(), cu_seqlens.numel() - 1, max_seqlen, q.size(0), Hq, Hkv, ld_of(q),
+                        ld_of(k), ld_of(v), ld_of(o), static_cast<float>(scale), causal, status_ptr(status),
+                        cur_stream()),
+        "attn_fwd");
+}
+
+void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+              const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dq,
+              at::Tensor& dk, at::Tensor& dv, const at::Tensor& cu_seqlens, int64_t max_seqlen, int64_t Hq, int64_t Hkv,
+              double scale, bool causal, const c10::optional<at::Tensor>& status) {
+  CHECK_F32(delta);
+  CHECK_F32(dq_acc);
+  check(accerl_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(), lse.data_ptr<float>(),
+                        delta.data_ptr<float>(), dq_acc.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                        cu_seqlens.data_ptr<int>(), cu_seqlens.numel() - 1, max_seqlen, q.size(0), Hq, Hkv, ld_of(q),
+                        ld_of(k), ld_of(v), ld_of(o), ld_of(dout), ld_of(dq), ld_of(dk), ld_of(dv),
+                        static_cast<float>(scale), causal, status_ptr(status), cur_stream()),
+        "attn_bwd");
+}
+
+void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                  const at::Tensor& block_table, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& part_o,
+                  at::Tensor& part_ml, int64_t Hq, int64_t Hkv, int64_t num_splits, double scale) {
+  CHECK_BF16(q);
+  CHECK_I32(block_table);
+  CHECK_I32(seq_lens);
+  check(accerl_paged_decode(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr<int>(),
+                            seq_lens.data_ptr<int>(), out.data_ptr(), part_o.data_ptr<float>(),
+                            part_ml.data_ptr<float>(), q.size(0), Hq, Hkv, block_table.size(1), k_cache.size(1),
+                            num_splits, static_cast<float>(scale), ld_of(q), ld_of(out), cur_stream()),
+        "paged_decode");
+}
+
+void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache, at::Tensor& v_cache,
+                    const at::Tensor& slot_mapping, int64_t Hkv) {
+  CHECK_I32(slot_mapping);
+  check(accerl_kv_cache_write(k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                              slot_mapping.data_ptr<int>(), k.size(0), Hkv, ld_of(k), ld_of(v), cur_stream()),
+        "kv_cache_write");
+}
+
+void sample_logits(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& seeds,
+                   const at::Tensor& offsets, at::Tensor& out_tokens, at::Tensor& out_logprobs, at::Tensor& part,
+                   int64_t num_chunks) {
+  CHECK_BF16(logits);
+  CHECK_F32(temperature);
+  check(accerl_sample_logits(logits.data_ptr(), ld_of(logits), logits.size(0), logits.size(1),
+                             temperature.data_ptr<float>(),
+                             reinterpret_cast<const unsigned long long*>(reinterpret_cast<long long*>(seeds.data_ptr<int64_t>())),
+                             reinterpret_cast<long long*>(offsets.data_ptr<int64_t>()), reinterpret_cast<long long*>(out_tokens.data_ptr<int64_t>()),
+                             out_logprobs.data_ptr<float>(), part.data_ptr<float>(), num_chunks, cur_stream()),
+        "sample_logits");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "accerl_agent_b200 sm_100a kernels";
+  m.def("last_error", &last_error, "(code, message) of the most recent launch; resets it");
+  m.def("gemm", &gemm, "tcgen05 bf16 GEMM");
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("bias_grad", &bias_grad);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("logsoftmax_label_fwd", &logsoftmax_label_fwd);
+  m.def("logsoftmax_label_bwd", &logsoftmax_label_bwd);
+  m.def("policy_loss", &policy_loss);
+  m.def("sumsq", &sumsq);
+  m.def("adamw", &adamw);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("paged_decode", &paged_decode);
+  m.def("kv_cache_write", &kv_cache_write);
+  m.def("sample_logits", &sample_logits);
+}

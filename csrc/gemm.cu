@@ -1,0 +1,434 @@
+// Persistent warp-specialised bf16 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+//   C[M,N] = alpha * sum_k A(m,k) * B(n,k)  (+ beta * C_old) (+ bias[n]) (+ residual[m,n])
+//
+// Operand storage is flexible so the three GEMMs of a linear layer run without transposes:
+//   A(m,k): K-major  -> A[m*lda + k]   ([M,K] row-major)      MN-major -> A[k*lda + m] ([K,M])
+//   B(n,k): K-major  -> B[n*ldb + k]   ([N,K], weight layout) MN-major -> B[k*ldb + n] ([K,N])
+//   forward  Y = X W^T : A=X (K-major),  B=W (K-major)
+//   dgrad   dX = dY W  : A=dY (K-major), B=W (MN-major)
+//   wgrad   dW = dY^T X: A=dY (MN-major), B=X (MN-major)
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0    : TMA producer. 128B-swizzled tiles of A and B land in a STAGES-deep smem ring;
+//               each stage completes an mbarrier by transaction bytes.
+//   warp 1    : allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16) from one elected lane;
+//               tcgen05.commit frees smem stages and publishes finished accumulators.
+//   warps 2-5 : epilogue. tcgen05.ld the fp32 accumulator (one TMEM lane = one output row per
+//               thread), apply alpha/beta/bias/residual, convert and store.
+// Accumulators are double-buffered in TMEM (2 x BN columns) so the epilogue of tile i overlaps the
+// main loop of tile i+1. Tiles are visited in grouped-M order for L2 reuse of B.
+// No cluster multicast is used: every CTA loads its own tiles.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace accerl {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+struct GemmParams {
+  int M, N, K;
+  void* C;
+  long long ldc;
+  int c_f32;
+  float alpha, beta;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  long long ldr;
+  int* status;
+  int tiles_m, tiles_n, num_tiles, group_m;
+};
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_blk, int& n_blk) {
+  const int per_group = p.group_m * p.tiles_n;
+  const int group = t / per_group;
+  const int first_m = group * p.group_m;
+  const int gsize = min(p.tiles_m - first_m, p.group_m);
+  const int r = t % per_group;
+  m_blk = first_m + r % gsize;
+  n_blk = r / gsize;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmParams p) {
+  using S = GemmSmem<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * S::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  constexpr uint32_t kTmemCols = 2 * BN;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0;
+      uint32_t last_parity = 0;  // bit s = parity of the last load issued into stage s
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int m_blk, n_blk;
+        tile_coords(p, t, m_blk, n_blk);
+        const int m0 = m_blk * kBM, n0 = n_blk * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          const int k0 = kb * kBK;
+          uint8_t* a_dst = smA + stage * S::kABytes;
+          uint8_t* b_dst = smB + stage * S::kBBytes;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) tma_load_2d(a_dst + j * 64 * kBK * 2, &tmA, &full[stage], m0 + 64 * j, k0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 64 * kBK * 2, &tmB, &full[stage], n0 + 64 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+          }
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: never leave a bulk copy in flight into shared memory of a finished CTA.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued_mask & (1u << s)) mbar_wait(&full[s], (last_parity >> s) & 1u, nullptr, 0, 20000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tbase + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + stage * S::kABytes);
+          const uint32_t b_addr = smem_u32(smB + stage * S::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            uint64_t adesc, bdesc;
+            if constexpr (A_MN) adesc = make_sw128_desc(a_addr + kk * 16 * 128, 64 * kBK * 2, 1024);
+            else adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            if constexpr (B_MN) bdesc = make_sw128_desc(b_addr + kk * 16 * 128, 64 * kBK * 2, 1024);
+            else bdesc = make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+      int m_blk, n_blk;
+      tile_coords(p, t, m_blk, n_blk);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = m_blk * kBM + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tbase + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + c0, v);
+        tmem_wait_ld();
+        const int col0 = n_blk * BN + c0;
+        if (!row_ok) continue;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int col = col0 + g * 8;
+          if (col >= p.N) break;
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(v[g * 8 + i]) * p.alpha;
+          if (p.bias) {
+            const uint4 b = *reinterpret_cast<const uint4*>(p.bias + col);
+            const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 bb = unpack_bf16x2(bw[i]);
+              f[2 * i] += bb.x;
+              f[2 * i + 1] += bb.y;
+            }
+          }
+          if (p.residual) {
+            const uint4 r = *reinterpret_cast<const uint4*>(p.residual + static_cast<long long>(row) * p.ldr + col);
+            const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 rr = unpack_bf16x2(rw[i]);
+              f[2 * i] += rr.x;
+              f[2 * i + 1] += rr.y;
+            }
+          }
+          if (p.c_f32) {
+            float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            if (p.beta != 0.f) {
+              const float4 o0 = *reinterpret_cast<const float4*>(c);
+              const float4 o1 = *reinterpret_cast<const float4*>(c + 4);
+              f[0] += p.beta * o0.x; f[1] += p.beta * o0.y; f[2] += p.beta * o0.z; f[3] += p.beta * o0.w;
+              f[4] += p.beta * o1.x; f[5] += p.beta * o1.y; f[6] += p.beta * o1.z; f[7] += p.beta * o1.w;
+            }
+            *reinterpret_cast<float4*>(c) = make_float4(f[0], f[1], f[2], f[3]);
+            *reinterpret_cast<float4*>(c + 4) = make_float4(f[4], f[5], f[6], f[7]);
+          } else {
+            __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            if (p.beta != 0.f) {
+              const uint4 o = *reinterpret_cast<const uint4*>(c);
+              const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 oo = unpack_bf16x2(ow[i]);
+                f[2 * i] += p.beta * oo.x;
+                f[2 * i + 1] += p.beta * oo.y;
+              }
+            }
+            uint4 o;
+            o.x = pack_bf16x2(f[0], f[1]);
+            o.y = pack_bf16x2(f[2], f[3]);
+            o.z = pack_bf16x2(f[4], f[5]);
+            o.w = pack_bf16x2(f[6], f[7]);
+            *reinterpret_cast<uint4*>(c) = o;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+struct MapKey {
+  uintptr_t ptr;
+  uint64_t d0, d1, stride;
+  uint32_t b0, b1;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && stride == o.stride && b0 == o.b0 && b1 == o.b1;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<uintptr_t>()(k.ptr);
+    h ^= std::hash<uint64_t>()(k.d0 * 1315423911ull + k.d1) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+    h ^= std::hash<uint64_t>()(k.stride * 2654435761ull + (uint64_t(k.b0) << 32 | k.b1)) + (h << 6) + (h >> 2);
+    return h;
+  }
+};
+
+std::mutex g_map_mutex;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
+
+// 2-D bf16 tensor map: inner dimension d0 (contiguous), outer d1 with a row stride in elements.
+bool make_map_2d(CUtensorMap* out, const void* ptr, uint64_t d0, uint64_t d1, uint64_t stride_elems, uint32_t b0,
+                 uint32_t b1) {
+  MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_elems, b0, b1};
+  {
+    std::lock_guard<std::mutex> g(g_map_mutex);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {d0, d1};
+  cuuint64_t strides[1] = {stride_elems * 2};
+  cuuint32_t box[2] = {b0, b1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> g(g_map_mutex);
+  if (g_map_cache.size() > 8192) g_map_cache.clear();
+  g_map_cache.emplace(key, *out);
+  return true;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p, cudaStream_t stream, int max_ctas) {
+  auto kern = gemm_bf16_tcgen05<BN, STAGES, A_MN, B_MN>;
+  constexpr int smem_bytes = STAGES * GemmSmem<BN>::kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set = true;
+  }
+  int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
+  kern<<<grid, kThreads, smem_bytes, stream>>>(ma, mb, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int STAGES>
+int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
+                   cudaStream_t s, int max_ctas) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, false, false>(ma, mb, p, s, max_ctas);
+  if (!a_mn && b_mn) return launch_gemm<BN, STAGES, false, true>(ma, mb, p, s, max_ctas);
+  if (a_mn && !b_mn) return launch_gemm<BN, STAGES, true, false>(ma, mb, p, s, max_ctas);
+  return launch_gemm<BN, STAGES, true, true>(ma, mb, p, s, max_ctas);
+}
+
+}  // namespace
+}  // namespace accerl
+
+// Returns 0 on success, a cudaError_t value on launch failure, or -1..-9 for argument errors.
+extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                                void* C, long long ldc, int c_f32, int M, int N, int K, float alpha, float beta,
+                                const void* bias, const void* residual, long long ldr, int* status, int block_n,
+                                int max_ctas, cudaStream_t stream) {
+  using namespace accerl;
+  if (M <= 0 || N <= 0) return 0;
+  if (K <= 0) return -1;
+  // TMA needs 16-byte row strides; the vectorised epilogue needs N % 8 == 0. K and M are free.
+  if ((N % 8) != 0 || (ldc % 8) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -2;
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15) return -3;
+  if (residual && ((ldr % 8) != 0 || (reinterpret_cast<uintptr_t>(residual) & 15))) return -4;
+  if (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) return -5;
+  int bn = block_n;
+  if (bn != 128 && bn != 256) {
+    const long long tiles256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
+    bn = (N <= 128 || tiles256 < num_sms() / 2) ? 128 : 256;
+  }
+  CUtensorMap ma, mb;
+  bool ok;
+  if (a_mn) ok = make_map_2d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64);
+  else ok = make_map_2d(&ma, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, 128);
+  if (!ok) return -7;
+  if (b_mn) ok = make_map_2d(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64);
+  else ok = make_map_2d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, (uint32_t)bn);
+  if (!ok) return -8;
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = C;
+  p.ldc = ldc;
+  p.c_f32 = c_f32;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
+  p.ldr = ldr;
+  p.status = status;
+  p.tiles_m = (M + kBM - 1) / kBM;
+  p.tiles_n = (N + bn - 1) / bn;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.group_m = 8;
+  if (bn == 256) return dispatch_major<256, 4>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
+  return dispatch_major<128, 6>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
+}

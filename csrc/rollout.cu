@@ -1,0 +1,338 @@
+// Rollout-engine kernels (sm_100a):
+//  * paged-KV decode attention, split over the sequence ("flash decoding") and packed over the q
+//    heads of one GQA group so each K/V row is read once per group; partial (o, m, l) per split are
+//    merged by a second kernel.
+//  * KV-cache write of freshly projected K/V rows into their paged slots.
+//  * sampler: one pass over each bf16 logits row computes the log-sum-exp, and the Gumbel-max sample
+//    argmax(logit/T + G) (greedy argmax when T == 0) with a counter-based SplitMix64 noise stream;
+//    the sampled token's log-probability is reported under the untempered distribution.
+// Cache layout: k_cache/v_cache [num_blocks, block_size, Hkv, 128] bf16.
+#include "common.cuh"
+
+namespace accerl {
+
+constexpr int kDHead = 128;
+constexpr int kMaxGroup = 16;
+
+// out[s, h, :] = softmax(q . K^T * scale) V over the first seq_lens[s] cached tokens.
+// grid (num_seqs, Hkv, num_splits), 4 warps; lanes map to tokens for Q.K and to head dims for P.V.
+template <int G>
+__global__ void __launch_bounds__(128) paged_decode_kernel(const __nv_bfloat16* __restrict__ q, long long ldq,
+                                                          const __nv_bfloat16* __restrict__ k_cache,
+                                                          const __nv_bfloat16* __restrict__ v_cache,
+                                                          const int* __restrict__ block_table, int max_blocks,
+                                                          const int* __restrict__ seq_lens, int block_size, int Hkv,
+                                                          int num_splits, float scale, float* __restrict__ part_o,
+                                                          float* __restrict__ part_ml) {
+  const int s = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int len = seq_lens[s];
+  const int per_split = (((len + num_splits - 1) / num_splits) + 31) & ~31;
+  const int t0 = split * per_split;
+  const int t1 = min(len, t0 + per_split);
+  __shared__ float q_s[G][kDHead];
+  __shared__ float p_s[4][G][32];
+  __shared__ float red_m[4][G], red_l[4][G];
+  __shared__ float red_o[4][G][kDHead];
+  const int Hq = Hkv * G;
+  for (int i = threadIdx.x; i < G * kDHead; i += blockDim.x) {
+    const int h = i / kDHead, d = i % kDHead;
+    q_s[h][d] = __bfloat162float(q[static_cast<long long>(s) * ldq + (kvh * G + h) * kDHead + d]) * scale;
+  }
+  __syncthreads();
+  float m[G], l[G], acc[G][4];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[h][i] = 0.f;
+  }
+  const long long row_stride = static_cast<long long>(Hkv) * kDHead;
+  for (int base = t0 + warp * 32; base < t1; base += 4 * 32) {
+    const int tok = base + lane;
+    const bool valid = tok < t1;
+    long long off = 0;
+    if (valid) {
+      const int blk = block_table[static_cast<long long>(s) * max_blocks + tok / block_size];
+      off = (static_cast<long long>(blk) * block_size + tok % block_size) * row_stride + kvh * kDHead;
+    }
+    float sc[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) sc[h] = 0.f;
+    if (valid) {
+      const uint4* kr = reinterpret_cast<const uint4*>(k_cache + off);
+#pragma unroll 4
+      for (int c = 0; c < kDHead / 8; ++c) {
+        const uint4 kv = kr[c];
+        const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = unpack_bf16x2(kw[i]);
+#pragma unroll
+          for (int h = 0; h < G; ++h) sc[h] += f.x * q_s[h][c * 8 + 2 * i] + f.y * q_s[h][c * 8 + 2 * i + 1];
+        }
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float x = valid ? sc[h] : -INFINITY;
+      const float cm = warp_max(x);
+      const float mn = fmaxf(m[h], cm);
+      const float a = (m[h] == -INFINITY) ? 0.f : __expf(m[h] - mn);
+      const float pv = valid ? __expf(x - mn) : 0.f;
+      l[h] = l[h] * a + warp_sum(pv);
+      m[h] = mn;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[h][i] *= a;
+      p_s[warp][h][lane] = pv;
+    }
+    __syncwarp();
+    const int nvalid = min(32, t1 - base);
+    for (int t = 0; t < nvalid; ++t) {
+      const long long o = __shfl_sync(0xffffffffu, off, t);
+      const uint2 vv = *reinterpret_cast<const uint2*>(v_cache + o + lane * 4);
+      const float2 v0 = unpack_bf16x2(vv.x), v1 = unpack_bf16x2(vv.y);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float pv = p_s[warp][h][t];
+        acc[h][0] += pv * v0.x;
+        acc[h][1] += pv * v0.y;
+        acc[h][2] += pv * v1.x;
+        acc[h][3] += pv * v1.y;
+      }
+    }
+    __syncwarp();
+  }
+  // merge the 4 warps
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    if (lane == 0) {
+      red_m[warp][h] = m[h];
+      red_l[warp][h] = l[h];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red_o[warp][h][lane * 4 + i] = acc[h][i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * kDHead; i += blockDim.x) {
+    const int h = i / kDHead, d = i % kDHead;
+    float mm = -INFINITY;
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, red_m[w][h]);
+    float ll = 0.f, oo = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float a = (red_m[w][h] == -INFINITY) ? 0.f : __expf(red_m[w][h] - mm);
+      ll += red_l[w][h] * a;
+      oo += red_o[w][h][d] * a;
+    }
+    const int hq = kvh * G + h;
+    const long long pidx = (static_cast<long long>(s) * Hq + hq) * num_splits + split;
+    part_o[pidx * kDHead + d] = oo;
+    if (d == 0) {
+      part_ml[pidx * 2] = mm;
+      part_ml[pidx * 2 + 1] = ll;
+    }
+  }
+}
+
+__global__ void paged_decode_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                          __nv_bfloat16* __restrict__ out, long long ldo, int Hq, int num_splits) {
+  const int s = blockIdx.x, hq = blockIdx.y, d = threadIdx.x;
+  const long long base = (static_cast<long long>(s) * Hq + hq) * num_splits;
+  float mm = -INFINITY;
+  for (int k = 0; k < num_splits; ++k) mm = fmaxf(mm, part_ml[(base + k) * 2]);
+  float ll = 0.f, oo = 0.f;
+  for (int k = 0; k < num_splits; ++k) {
+    const float m = part_ml[(base + k) * 2];
+    const float a = (m == -INFINITY) ? 0.f : __expf(m - mm);
+    ll += part_ml[(base + k) * 2 + 1] * a;
+    oo += part_o[(base + k) * kDHead + d] * a;
+  }
+  out[static_cast<long long>(s) * ldo + hq * kDHead + d] = __float2bfloat16(ll > 0.f ? oo / ll : 0.f);
+}
+
+__global__ void kv_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+                                      __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
+                                      const int* __restrict__ slots, int T, int Hkv, long long ldk, long long ldv) {
+  const int t = blockIdx.x;
+  const int slot = slots[t];
+  if (slot < 0) return;
+  const int n16 = Hkv * kDHead / 8;
+  const long long dst = static_cast<long long>(slot) * Hkv * kDHead;
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+    reinterpret_cast<uint4*>(k_cache + dst)[i] = reinterpret_cast<const uint4*>(k + t * ldk)[i];
+    reinterpret_cast<uint4*>(v_cache + dst)[i] = reinterpret_cast<const uint4*>(v + t * ldv)[i];
+  }
+}
+
+// SplitMix64 (Steele, Lea, Flood 2014) as a counter-based generator.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9e3779b97f4a7c15ull;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float gumbel_noise(uint64_t seed, uint64_t offset, uint32_t idx) {
+  const uint64_t h = splitmix64(seed ^ splitmix64(offset * 0x100000001b3ull + idx));
+  // 24-bit uniform in (0, 1)
+  const float u = (static_cast<float>(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  return -__logf(-__logf(u));
+}
+
+// part layout per (row, chunk): [max, sumexp, best_score, best_idx]
+__global__ void sample_partial_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V,
+                                      const float* __restrict__ temperature, const unsigned long long* __restrict__ seeds,
+                                      const long long* __restrict__ offsets, float* __restrict__ part, int num_chunks) {
+  const int row = blockIdx.x, chunk = blockIdx.y;
+  const int per = (((V + num_chunks - 1) / num_chunks) + 7) & ~7;
+  const int c0 = chunk * per, c1 = min(V, c0 + per);
+  const float T = temperature[row];
+  const bool greedy = T <= 0.f;
+  const float invT = greedy ? 1.f : 1.f / T;
+  const uint64_t seed = seeds[row];
+  const uint64_t offset = static_cast<uint64_t>(offsets[row]);
+  const __nv_bfloat16* l = logits + row * ld;
+  float m = -INFINITY, s = 0.f, best = -INFINITY;
+  int best_i = c0;
+  for (int c = c0 + threadIdx.x * 8; c < c1; c += blockDim.x * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(l + c);
+    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(vw[i]);
+      const float xs[2] = {f.x, f.y};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int idx = c + 2 * i + h;
+        const float x = xs[h];
+        const float mn = fmaxf(m, x);
+        s = s * ((m == -INFINITY) ? 0.f : __expf(m - mn)) + __expf(x - mn);
+        m = mn;
+        const float sc = greedy ? x : x * invT + gumbel_noise(seed, offset, static_cast<uint32_t>(idx));
+        if (sc > best) {
+          best = sc;
+          best_i = idx;
+        }
+      }
+    }
+  }
+  // block reduction
+  __shared__ float sm_m[32], sm_s[32], sm_b[32];
+  __shared__ int sm_i[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, best_i, o);
+    const float mn = fmaxf(m, m2);
+    s = s * ((m == -INFINITY) ? 0.f : __expf(m - mn)) + s2 * ((m2 == -INFINITY) ? 0.f : __expf(m2 - mn));
+    m = mn;
+    if (b2 > best || (b2 == best && i2 < best_i)) {
+      best = b2;
+      best_i = i2;
+    }
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sm_m[w] = m;
+    sm_s[w] = s;
+    sm_b[w] = best;
+    sm_i[w] = best_i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = -INFINITY, S = 0.f, B = -INFINITY;
+    int I = c0;
+    for (int k = 0; k < (blockDim.x >> 5); ++k) {
+      const float mn = fmaxf(M, sm_m[k]);
+      S = S * ((M == -INFINITY) ? 0.f : __expf(M - mn)) + sm_s[k] * ((sm_m[k] == -INFINITY) ? 0.f : __expf(sm_m[k] - mn));
+      M = mn;
+      if (sm_b[k] > B || (sm_b[k] == B && sm_i[k] < I)) {
+        B = sm_b[k];
+        I = sm_i[k];
+      }
+    }
+    float* dst = part + (static_cast<long long>(row) * num_chunks + chunk) * 4;
+    dst[0] = M;
+    dst[1] = S;
+    dst[2] = B;
+    dst[3] = __int_as_float(I);
+  }
+}
+
+__global__ void sample_final_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, const float* __restrict__ part,
+                                    int rows, int num_chunks, long long* __restrict__ out_tokens,
+                                    float* __restrict__ out_logprobs) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  float M = -INFINITY, S = 0.f, B = -INFINITY;
+  int I = 0;
+  for (int k = 0; k < num_chunks; ++k) {
+    const float* p = part + (static_cast<long long>(row) * num_chunks + k) * 4;
+    const float mn = fmaxf(M, p[0]);
+    S = S * ((M == -INFINITY) ? 0.f : __expf(M - mn)) + p[1] * ((p[0] == -INFINITY) ? 0.f : __expf(p[0] - mn));
+    M = mn;
+    const int pi = __float_as_int(p[3]);
+    if (p[2] > B || (p[2] == B && pi < I)) {
+      B = p[2];
+      I = pi;
+    }
+  }
+  out_tokens[row] = I;
+  out_logprobs[row] = __bfloat162float(logits[row * ld + I]) - (M + __logf(S));
+}
+
+}  // namespace accerl
+
+using namespace accerl;
+
+extern "C" int accerl_paged_decode(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
+                                   const int* seq_lens, void* out, float* part_o, float* part_ml, int num_seqs, int Hq,
+                                   int Hkv, int max_blocks_per_seq, int block_size, int num_splits, float scale,
+                                   long long ldq, long long ldo, cudaStream_t s) {
+  if (num_seqs == 0) return 0;
+  if (Hq % Hkv) return -1;
+  const int G = Hq / Hkv;
+  dim3 grid(num_seqs, Hkv, num_splits);
+#define LAUNCH_G(GV)                                                                                              \
+  case GV:                                                                                                        \
+    paged_decode_kernel<GV><<<grid, 128, 0, s>>>((const __nv_bfloat16*)q, ldq, (const __nv_bfloat16*)k_cache,   \
+                                                 (const __nv_bfloat16*)v_cache, block_table, max_blocks_per_seq, \
+                                                 seq_lens, block_size, Hkv, num_splits, scale, part_o, part_ml);  \
+    break;
+  switch (G) {
+    LAUNCH_G(1)
+    LAUNCH_G(2)
+    LAUNCH_G(4)
+    LAUNCH_G(6)
+    LAUNCH_G(8)
+    default:
+      return -2;
+  }
+#undef LAUNCH_G
+  paged_decode_merge_kernel<<<dim3(num_seqs, Hq), kDHead, 0, s>>>(part_o, part_ml, (__nv_bfloat16*)out, ldo, Hq,
+                                                                  num_splits);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping,
+                                     int T, int Hkv, long long ldk, long long ldv, cudaStream_t s) {
+  if (T == 0) return 0;
+  if ((ldk | ldv) & 7) return -1;
+  kv_cache_write_kernel<<<T, 128, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (__nv_bfloat16*)k_cache,
+                                          (__nv_bfloat16*)v_cache, slot_mapping, T, Hkv, ldk, ldv);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
+                                    const unsigned long long* seeds, const long long* offsets, long long* out_tokens,
+                                    float* out_logprobs, float* part, int num_chunks, cudaStream_t s) {
+  if (rows == 0) return 0;
+  if (V % 8 || ld % 8) return -1;
+  sample_partial_kernel<<<dim3(rows, num_chunks), 256, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, seeds,
+                                                               offsets, part, num_chunks);
+  sample_final_kernel<<<(rows + 127) / 128, 128, 0, s>>>((const __nv_bfloat16*)logits, ld, part, rows, num_chunks,
+                                                         out_tokens, out_logprobs);
+  return (int)cudaGetLastError();
+}

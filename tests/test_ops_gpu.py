@@ -1,0 +1,279 @@
+"""Numerics of every sm_100a kernel against an fp32 PyTorch reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from accerl_agent_b200 import ops
+from accerl_agent_b200.algo.objectives import ObjectiveConfig, varlen_token_sum_loss
+from accerl_agent_b200.ops import reference as ref
+
+DEV = "cuda"
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(0)
+    yield
+    ops.check_status(torch.device(DEV))
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 264, 136), (1024, 768, 1536)])
+def test_gemm_layouts(a_mn, b_mn, M, N, K):
+    if a_mn and M % 8:
+        # an MN-major A is stored [K, M]; TMA needs its row stride to be a multiple of 16 bytes
+        a_in = torch.zeros(K, M, device=DEV).bfloat16()
+        with pytest.raises(RuntimeError):
+            ops.gemm(a_in, torch.zeros(N, K, device=DEV).bfloat16(), a_mn=True)
+        return
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    a_in = A.t().contiguous() if a_mn else A
+    b_in = B.t().contiguous() if b_mn else B
+    out = ops.gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn, out_dtype=torch.float32)
+    want = A.float() @ B.float().t()
+    assert _rel(out, want) < 1e-5
+    out_bf = ops.gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn)
+    assert _rel(out_bf, want) < 1e-2
+
+
+@pytest.mark.parametrize("block_n", [128, 256])
+def test_gemm_epilogue_bias_residual_beta(block_n):
+    M, N, K = 520, 1024, 320
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    bias = torch.randn(N, device=DEV).bfloat16()
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    out = ops.gemm(A, B, bias=bias, residual=res, block_n=block_n)
+    want = A.float() @ B.float().t() + bias.float() + res.float()
+    assert _rel(out, want) < 1e-2
+    acc = torch.randn(M, N, device=DEV)
+    base = acc.clone()
+    ops.gemm(A, B, acc, beta=1.0, alpha=0.5, out_dtype=torch.float32, block_n=block_n)
+    assert _rel(acc, base + 0.5 * (A.float() @ B.float().t())) < 1e-5
+
+
+def test_gemm_strided_views():
+    # q/k/v style column slices of a fused buffer as operands and outputs
+    T, H = 384, 256
+    qkv = torch.randn(T, 3 * H, device=DEV).bfloat16()
+    W = torch.randn(H, H, device=DEV).bfloat16()
+    q = qkv[:, H : 2 * H]
+    out = torch.empty(T, 2 * H, device=DEV, dtype=torch.bfloat16)
+    ops.gemm(q, W, out[:, H:])
+    assert _rel(out[:, H:], q.float() @ W.float().t()) < 1e-2
+
+
+def test_linear_grads_match_autograd():
+    T, IN, OUT = 640, 512, 384
+    x = torch.randn(T, IN, device=DEV).bfloat16()
+    w = (torch.randn(OUT, IN, device=DEV) * 0.05).bfloat16()
+    dy = torch.randn(T, OUT, device=DEV).bfloat16()
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    (xf @ wf.t()).backward(dy.float())
+    dx = ops.linear_dgrad(dy, w)
+    gw = torch.zeros(OUT, IN, device=DEV)
+    ops.linear_wgrad(dy, x, gw, accumulate=True)
+    ops.linear_wgrad(dy, x, gw, accumulate=True)
+    assert _rel(dx, xf.grad) < 1e-2
+    assert _rel(gw, 2 * wf.grad) < 1e-5
+    db = torch.zeros(OUT, device=DEV)
+    ops.bias_grad(dy, db)
+    assert _rel(db, dy.float().sum(0)) < 1e-5
+
+
+def test_rmsnorm_fwd_bwd():
+    T, H = 777, 1536
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).bfloat16()
+    y, rstd = ops.rmsnorm(x, w, 1e-6)
+    y_ref, rstd_ref = ref.rmsnorm(x, w, 1e-6)
+    assert _rel(y, y_ref) < 1e-2
+    assert _rel(rstd, rstd_ref) < 1e-5
+    dy = torch.randn(T, H, device=DEV).bfloat16()
+    acc = torch.randn(T, H, device=DEV).bfloat16()
+    dw = torch.zeros(H, device=DEV)
+    dx = ops.rmsnorm_backward(dy, x, w, rstd, dx_accum=acc, dw_grad=dw)
+    dx_ref, dw_ref = ref.rmsnorm_backward(dy, x, w, rstd_ref)
+    assert _rel(dx, dx_ref + acc.float()) < 1e-2
+    assert _rel(dw, dw_ref) < 1e-2
+
+
+def test_rope_roundtrip_and_reference():
+    T, Hq, Hkv, D = 300, 12, 2, 128
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).bfloat16()
+    pos = torch.randint(0, 8192, (T,), device=DEV)
+    orig = qkv.clone()
+    ops.rope_(qkv, pos, Hq + Hkv, D, 1e6)
+    want = ref.apply_rope(orig[:, : (Hq + Hkv) * D].reshape(T, Hq + Hkv, D), pos, 1e6)
+    assert _rel(qkv[:, : (Hq + Hkv) * D].reshape(T, Hq + Hkv, D), want) < 1e-2
+    assert torch.equal(qkv[:, (Hq + Hkv) * D :], orig[:, (Hq + Hkv) * D :])
+    ops.rope_(qkv, pos, Hq + Hkv, D, 1e6, inverse=True)
+    assert _rel(qkv, orig) < 2e-2
+
+
+def test_swiglu_fwd_bwd():
+    T, I = 513, 8960
+    gu = torch.randn(T, 2 * I, device=DEV).bfloat16()
+    h = ops.swiglu(gu)
+    assert _rel(h, ref.swiglu(gu)) < 1e-2
+    dh = torch.randn(T, I, device=DEV).bfloat16()
+    assert _rel(ops.swiglu_backward(dh, gu), ref.swiglu_backward(dh, gu)) < 1e-2
+
+
+def test_embedding_fwd_bwd():
+    V, H, T = 5000, 1536, 1000
+    table = torch.randn(V, H, device=DEV).bfloat16()
+    ids = torch.randint(0, V, (T,), device=DEV)
+    out = ops.embedding(ids, table)
+    assert torch.equal(out, table[ids])
+    d = torch.randn(T, H, device=DEV).bfloat16()
+    g = torch.zeros(V, H, device=DEV)
+    ops.embedding_backward(ids, d, g)
+    want = torch.zeros(V, H, device=DEV).index_add_(0, ids, d.float())
+    assert _rel(g, want) < 1e-5
+
+
+def test_logsoftmax_label_fwd_bwd():
+    n, V = 37, 151936
+    logits = (torch.randn(n, V, device=DEV) * 3).bfloat16()
+    labels = torch.randint(0, V, (n,), device=DEV)
+    lp, lse, ent = ops.logsoftmax_label(logits, labels, with_entropy=True)
+    lp_r, lse_r, ent_r = ref.logsoftmax_label(logits, labels)
+    assert torch.allclose(lp, lp_r, atol=2e-3, rtol=0)
+    assert torch.allclose(lse, lse_r, atol=2e-3, rtol=0)
+    assert torch.allclose(ent, ent_r, atol=2e-2, rtol=1e-3)
+    g = torch.randn(n, device=DEV)
+    lf = logits.float().requires_grad_(True)
+    (torch.log_softmax(lf, -1).gather(1, labels.view(-1, 1)).squeeze(1) * g).sum().backward()
+    d = logits.clone()
+    ops.logsoftmax_label_backward(d, labels, lse, g)
+    assert _rel(d, lf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("mode", ["ppo", "gipo", "sapo"])
+def test_policy_loss_matches_autograd(mode):
+    n = 5000
+    lp = -torch.rand(n, device=DEV) * 5
+    old = lp + 0.3 * torch.randn(n, device=DEV)
+    adv = torch.randn(n, device=DEV)
+    cfg = ObjectiveConfig(clip_mode=mode, clip_eps=0.2, kl_coef=0.05)
+    dlp, stats = ops.policy_loss(lp, old, adv, cfg, loss_scale=0.25)
+    x = lp.clone().requires_grad_(True)
+    loss, stats_ref = varlen_token_sum_loss(x, old, adv, cfg)
+    (loss * 0.25).backward()
+    assert torch.allclose(dlp, x.grad, atol=1e-5, rtol=1e-4)
+    assert torch.allclose(stats, stats_ref.to(stats.device), rtol=1e-4, atol=1e-2)
+
+
+def test_adamw_matches_torch():
+    n = 10007
+    p0 = torch.randn(n, device=DEV)
+    grads = [torch.randn(n, device=DEV) * 3 for _ in range(3)]
+    ref_p = p0.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([ref_p], lr=1e-3, weight_decay=0.01)
+    master, m, v = p0.clone(), torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    bf = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    for step, g in enumerate(grads, start=1):
+        ref_p.grad = g.clone()
+        torch.nn.utils.clip_grad_norm_([ref_p], 1.0)
+        opt.step()
+        gg = g.clone()
+        ss = ops.grad_sumsq(gg)
+        ops.adamw_step(master, m, v, gg, bf, ss, 1e-3, 0.9, 0.999, 1e-8, 0.01, 1.0, step)
+        assert float(gg.abs().max()) == 0.0
+    assert torch.allclose(master, ref_p.detach(), atol=1e-6, rtol=1e-5)
+    assert torch.equal(bf, master.bfloat16())
+
+
+def _varlen_case(lengths, Hq, Hkv, D=128):
+    T = sum(lengths)
+    cu = torch.tensor([0] + list(torch.tensor(lengths).cumsum(0)), dtype=torch.int32, device=DEV)
+    qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV)).bfloat16()
+    q = qkv[:, : Hq * D]
+    k = qkv[:, Hq * D : (Hq + Hkv) * D]
+    v = qkv[:, (Hq + Hkv) * D :]
+    return T, cu, qkv, q, k, v
+
+
+@pytest.mark.parametrize("lengths,Hq,Hkv", [([1, 130, 257, 64], 4, 2), ([512], 2, 2), ([300, 700], 6, 1)])
+def test_attention_forward(lengths, Hq, Hkv):
+    T, cu, qkv, q, k, v = _varlen_case(lengths, Hq, Hkv)
+    o, lse = ops.attention_varlen(q, k, v, cu, max(lengths), Hq, Hkv, 128)
+    o_r, lse_r = ref.attention_varlen(q.reshape(T, Hq, 128), k.reshape(T, Hkv, 128), v.reshape(T, Hkv, 128), cu,
+                                      1 / math.sqrt(128))
+    assert _rel(o, o_r.reshape(T, -1)) < 2e-2
+    assert torch.allclose(lse, lse_r, atol=1e-2)
+
+
+@pytest.mark.parametrize("lengths,Hq,Hkv", [([1, 130, 257, 64], 4, 2), ([384], 2, 2), ([300, 700], 6, 1)])
+def test_attention_backward(lengths, Hq, Hkv):
+    T, cu, qkv, q, k, v = _varlen_case(lengths, Hq, Hkv)
+    o, lse = ops.attention_varlen(q, k, v, cu, max(lengths), Hq, Hkv, 128)
+    do = torch.randn(T, Hq * 128, device=DEV).bfloat16()
+    dq, dk, dv = ops.attention_varlen_backward(do, q, k, v, o, lse, cu, max(lengths), Hq, Hkv, 128)
+    qf = q.float().reshape(T, Hq, 128).requires_grad_(True)
+    kf = k.float().reshape(T, Hkv, 128).requires_grad_(True)
+    vf = v.float().reshape(T, Hkv, 128).requires_grad_(True)
+    of, _ = ref.attention_varlen(qf, kf, vf, cu, 1 / math.sqrt(128))
+    of.backward(do.float().reshape(T, Hq, 128))
+    assert _rel(dq, qf.grad.reshape(T, -1)) < 3e-2
+    assert _rel(dk, kf.grad.reshape(T, -1)) < 3e-2
+    assert _rel(dv, vf.grad.reshape(T, -1)) < 3e-2
+
+
+@pytest.mark.parametrize("Hq,Hkv,splits", [(12, 2, 1), (32, 4, 4), (8, 8, 2)])
+def test_paged_decode_and_cache_write(Hq, Hkv, splits):
+    S, bs, D = 5, 16, 128
+    lens = torch.tensor([1, 17, 64, 100, 33], dtype=torch.int32, device=DEV)
+    max_blocks = 8
+    nb = S * max_blocks
+    kc = torch.zeros(nb, bs, Hkv, D, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    perm = torch.randperm(nb, device=DEV).to(torch.int32)
+    table = perm.view(S, max_blocks)
+    # write each sequence's K/V through the cache-write kernel
+    for s in range(S):
+        n = int(lens[s])
+        kk = torch.randn(n, Hkv * D, device=DEV).bfloat16()
+        vv = torch.randn(n, Hkv * D, device=DEV).bfloat16()
+        t = torch.arange(n, device=DEV)
+        slots = (table[s, t // bs].long() * bs + t % bs).to(torch.int32)
+        ops.kv_cache_write(kk, vv, kc, vc, slots, Hkv)
+        blocks = table[s, t // bs].long()
+        assert torch.equal(kc[blocks, t % bs].reshape(n, -1), kk)
+    q = torch.randn(S, Hq * D, device=DEV).bfloat16()
+    out = ops.paged_decode(q, kc, vc, table, lens, Hq, Hkv, 1 / math.sqrt(D), num_splits=splits)
+    want = ref.paged_decode(q.reshape(S, Hq, D), kc, vc, table, lens, 1 / math.sqrt(D))
+    assert _rel(out, want.reshape(S, -1)) < 2e-2
+
+
+def test_sampler_greedy_and_distribution():
+    rows, V = 6, 151936
+    logits = (torch.randn(rows, V, device=DEV) * 2).bfloat16()
+    temp = torch.zeros(rows, device=DEV)
+    seeds = torch.arange(rows, device=DEV, dtype=torch.int64)
+    offs = torch.zeros(rows, device=DEV, dtype=torch.int64)
+    tok, lp = ops.sample(logits, temp, seeds, offs)
+    assert torch.equal(tok, logits.float().argmax(-1))
+    want = torch.log_softmax(logits.float(), -1).gather(1, tok.view(-1, 1)).squeeze(1)
+    assert torch.allclose(lp, want, atol=2e-3)
+    # temperature 1 on a 4-token support: empirical frequencies follow softmax
+    small = torch.full((1, 64), -1e4, device=DEV)
+    small[0, :4] = torch.tensor([0.0, 1.0, 2.0, 0.5], device=DEV)
+    small = small.bfloat16().repeat(4000, 1)
+    tok, lp = ops.sample(small, torch.ones(4000, device=DEV), torch.arange(4000, device=DEV), offs.new_zeros(4000),
+                         num_chunks=1)
+    freq = torch.bincount(tok, minlength=64)[:4].float() / 4000
+    probs = torch.softmax(small[0, :4].float(), -1)
+    assert torch.allclose(freq, probs, atol=0.03)
