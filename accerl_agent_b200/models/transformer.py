@@ -200,7 +200,8 @@ class CausalLM:
 
     def init_weights(self, seed: int = 0, std: float = 0.02) -> None:
         """Random init (normal(0, std) matrices, unit norms, zero biases), deterministic per seed."""
-        gen = torch.Generator(device="cpu")
+        dev = self.params.device
+        gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
         with torch.no_grad():
             for name in self.layout.order:
@@ -210,7 +211,7 @@ class CausalLM:
                 elif name.endswith(".bias"):
                     v.zero_()
                 else:
-                    chunk = torch.randn(v.shape, generator=gen, dtype=torch.float32) * std
+                    chunk = torch.randn(v.shape, generator=gen, dtype=torch.float32, device=dev) * std
                     v.copy_(chunk.to(v.dtype))
 
     # ---------------------------------------------------------------- forward
@@ -281,7 +282,7 @@ class CausalLM:
         pos = batch["position_ids"].reshape(-1)
         cu = batch["cu_seqlens"]
         pred_idx = batch["prediction_indices"]
-        labels = batch["labels"][batch["target_indices"]]
+        labels = batch["target_labels"] if "target_labels" in batch else batch["labels"][batch["target_indices"]]
         x, caches = self.forward_hidden(ids, pos, cu, max_seqlen, save)
         hN, rstdN = ops.rmsnorm(x, self.w("model.norm.weight"), self.cfg.rms_norm_eps)
         rows = hN.index_select(0, pred_idx)

@@ -16,6 +16,13 @@ from . import reference
 from ._ext import available, check_status, native as _native_module, status_tensor
 
 
+# Kernels launched by one call of each binding (the benchmark reports launches per timed step).
+KERNELS_PER_CALL = {
+    "rmsnorm_bwd": 3, "bias_grad": 2, "attn_bwd": 4, "paged_decode": 2, "sample_logits": 2,
+}
+LAUNCHES = [0]
+
+
 class _Checked:
     """Proxy over the extension: every kernel launch is followed by a check of its launch code
     (argument validation or cudaError) so failures raise here with the op name."""
@@ -25,9 +32,11 @@ class _Checked:
 
     def __getattr__(self, name):
         fn = getattr(self._ext, name)
+        per_call = KERNELS_PER_CALL.get(name, 1)
 
         def call(*args):
             fn(*args)
+            LAUNCHES[0] += per_call
             rc, msg = self._ext.last_error()
             if rc != 0:
                 raise RuntimeError(f"native op {name} failed (code {rc}): {msg}")

@@ -1,0 +1,124 @@
+"""FSDP-style sharded optimizer state over flat parameter buffers.
+
+The reference shards every decoder layer with FSDP2 ``fully_shard`` and re-gathers parameters before
+each forward and backward, reduce-scattering bf16 gradients after every micro-batch
+(agent_textworld.py:474-496). On B200 (180 GB per GPU) the compute copy of the parameters of every
+benchmarked model fits on each rank, so this runtime keeps it resident and shards only what is big and
+fp32: master weights, Adam moments and the reduced gradient. Per optimizer step:
+
+1. gradients accumulate locally in one flat fp32 buffer over all micro-batches (wgrad GEMMs add in
+   their epilogue);
+2. one reduce-scatter (SUM) gives every rank the gradient of its shard;
+3. the global gradient norm is one 8-byte all-reduce of per-shard sums of squares;
+4. the fused clip + AdamW kernel updates the fp32 shard and writes the bf16 compute shard;
+5. one in-place all-gather refreshes the full bf16 copy on every rank.
+
+Micro-batches therefore run with no parameter traffic at all. The loss is scaled by
+``1 / global_valid_tokens`` and gradients are summed over ranks, which equals the reference's
+``world / global_tokens`` pre-scale followed by FSDP's ``1 / world`` gradient divide.
+
+On a single rank the shard is the whole trainable segment and no collective is issued. CPU ranks use
+gloo (reduce-scatter is emulated with an all-reduce there).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+def dist_ready() -> bool:
+    return dist.is_available() and dist.is_initialized()
+
+
+class ShardedAdamW:
+    def __init__(self, model, lr: float, weight_decay: float = 0.0, betas=(0.9, 0.999), eps: float = 1e-8,
+                 max_grad_norm: float = 1.0, group=None):
+        self.model = model
+        self.group = group
+        self.world = dist.get_world_size(group) if dist_ready() else 1
+        self.rank = dist.get_rank(group) if dist_ready() else 0
+        n = model.layout.trainable_numel
+        if n % max(self.world, 1):
+            raise ValueError("trainable segment must be padded to a multiple of the world size")
+        self.shard_numel = n // self.world
+        self.lr = lr
+        self.weight_decay = weight_decay
+        self.betas = betas
+        self.eps = eps
+        self.max_grad_norm = max_grad_norm
+        self.step_count = 0
+        lo = self.rank * self.shard_numel
+        self.param_shard = model.params[lo : lo + self.shard_numel]
+        self.master = self.param_shard.detach().float().clone()
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        if self.world == 1:
+            self.grad_shard = model.grads
+        else:
+            self.grad_shard = torch.zeros(self.shard_numel, dtype=torch.float32, device=model.params.device)
+        self._sumsq = torch.zeros(1, dtype=torch.float64, device=model.params.device)
+        self.backend = dist.get_backend(group) if dist_ready() else "none"
+
+    def refresh_master_from_params(self) -> None:
+        """Re-seed fp32 master weights after parameters were overwritten (e.g. checkpoint load)."""
+        self.master.copy_(self.param_shard.float())
+
+    def reduce_gradients(self) -> None:
+        if self.world == 1:
+            return
+        full = self.model.grads
+        if self.backend == "nccl":
+            dist.reduce_scatter_tensor(self.grad_shard, full, op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            dist.all_reduce(full, op=dist.ReduceOp.SUM, group=self.group)
+            lo = self.rank * self.shard_numel
+            self.grad_shard.copy_(full[lo : lo + self.shard_numel])
+        full.zero_()
+
+    def global_grad_sumsq(self) -> torch.Tensor:
+        self._sumsq.zero_()
+        ops.grad_sumsq(self.grad_shard, self._sumsq)
+        if self.world > 1:
+            dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
+        return self._sumsq
+
+    def step(self, lr: Optional[float] = None) -> torch.Tensor:
+        """Reduce, clip (global norm ``max_grad_norm``), update and re-gather. Returns the float64
+        sum of squared gradients (a device tensor; no host sync)."""
+        if lr is not None:
+            self.lr = lr
+        self.reduce_gradients()
+        sumsq = self.global_grad_sumsq()
+        self.step_count += 1
+        ops.adamw_step(self.master, self.exp_avg, self.exp_avg_sq, self.grad_shard, self.param_shard, sumsq,
+                       self.lr, self.betas[0], self.betas[1], self.eps, self.weight_decay, self.max_grad_norm,
+                       self.step_count)
+        self.all_gather_params()
+        return sumsq
+
+    def all_gather_params(self) -> None:
+        if self.world == 1:
+            return
+        full = self.model.params[: self.model.layout.trainable_numel]
+        if self.backend == "nccl":
+            dist.all_gather_into_tensor(full, self.param_shard, group=self.group)
+        else:
+            parts = list(full.chunk(self.world))
+            local = self.param_shard.clone()
+            dist.all_gather(parts, local, group=self.group)
+
+    def state_dict(self):
+        return {"step": self.step_count, "master": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq}
+
+    def load_state_dict(self, state):
+        self.step_count = int(state["step"])
+        self.master.copy_(state["master"])
+        self.exp_avg.copy_(state["exp_avg"])
+        self.exp_avg_sq.copy_(state["exp_avg_sq"])
+        self.param_shard.copy_(self.master.to(self.param_shard.dtype))
+        self.all_gather_params()
