@@ -111,15 +111,20 @@ def gemm(
     out_dtype: torch.dtype = torch.bfloat16,
     block_n: int = 0,
     max_ctas: int = 0,
+    splits: int = 0,
 ) -> torch.Tensor:
     """``out = alpha * A @ B^T + beta*out (+bias) (+residual)`` with A given as [M,K] (or [K,M] if
-    ``a_mn``) and B as [N,K] (or [K,N] if ``b_mn``)."""
+    ``a_mn``) and B as [N,K] (or [K,N] if ``b_mn``).
+
+    ``splits`` > 1 splits K across CTAs (fp32 output accumulated with ``beta=1`` only); 0 lets the
+    launcher choose for fp32 accumulation, 1 disables it."""
     M = a.shape[1] if a_mn else a.shape[0]
     N = b.shape[1] if b_mn else b.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype, device=a.device)
     if a.is_cuda:
-        native().gemm(a, a_mn, b, b_mn, out, alpha, beta, bias, residual, status_tensor(a.device), block_n, max_ctas)
+        native().gemm(a, a_mn, b, b_mn, out, alpha, beta, bias, residual, status_tensor(a.device), block_n, max_ctas,
+                      splits)
         return out
     af = a.float().t() if a_mn else a.float()
     bf = b.float() if b_mn else b.float().t()
@@ -135,7 +140,21 @@ def gemm(
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, out=None) -> torch.Tensor:
-    """``y = x w^T (+b) (+residual)``; x [T, in], w [out, in]."""
+    """``y = x w^T (+b) (+residual)``; x [T, in], w [out, in]. Skinny products (few rows, e.g. decode
+    steps) run split-K into an fp32 scratch and a finishing pass, so the whole GPU streams weights."""
+    if x.is_cuda and x.shape[0] <= 256 and x.dtype == torch.bfloat16:
+        M, N, K = x.shape[0], w.shape[0], w.shape[1]
+        tiles = (N + 127) // 128
+        splits = 1
+        while tiles * splits * 2 <= 148 and (K // 64) // (splits * 2) >= 2:
+            splits *= 2
+        if splits > 1:
+            acc = workspace(x.device, "splitk_acc", M * N).view(M, N)
+            acc.zero_()
+            gemm(x, w, acc, beta=1.0, out_dtype=torch.float32, block_n=128, splits=splits)
+            out = out if out is not None else torch.empty(M, N, dtype=x.dtype, device=x.device)
+            native().splitk_finish(acc, bias, residual, out)
+            return out
     return gemm(x, w, out, bias=bias, residual=residual, out_dtype=x.dtype)
 
 
@@ -145,8 +164,10 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out=None, accumulate: bool =
 
 
 def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, grad: torch.Tensor, accumulate: bool = True) -> torch.Tensor:
-    """``grad (+)= dy^T x`` in fp32; dy [T, out], x [T, in], grad [out, in] fp32."""
-    return gemm(dy, x, grad, a_mn=True, b_mn=True, beta=1.0 if accumulate else 0.0, out_dtype=torch.float32)
+    """``grad (+)= dy^T x`` in fp32; dy [T, out], x [T, in], grad [out, in] fp32. Accumulating calls
+    split the token dimension across CTAs when the weight alone would not fill the GPU."""
+    return gemm(dy, x, grad, a_mn=True, b_mn=True, beta=1.0 if accumulate else 0.0, out_dtype=torch.float32,
+                splits=0 if accumulate else 1)
 
 
 def bias_grad(dy: torch.Tensor, grad: torch.Tensor, accumulate: bool = True) -> torch.Tensor:
@@ -252,8 +273,12 @@ def attention_varlen(
     scale: Optional[float] = None,
     causal: bool = True,
     out: Optional[torch.Tensor] = None,
+    cu_seqlens_k: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
-    """q: [T, Hq*D] (may be a strided view), k/v: [T, Hkv*D]. Returns (o [T, Hq*D], lse [Hq, T])."""
+    """q: [T, Hq*D] (may be a strided view), k/v: [Tk, Hkv*D]. Returns (o [T, Hq*D], lse [Hq, T]).
+
+    ``cu_seqlens_k`` (default: ``cu_seqlens``) lets every sequence have more keys than queries; the
+    queries are then the last ones of the sequence (causal mask aligned to the end of the keys)."""
     scale = reference.default_scale(head_dim) if scale is None else scale
     T = q.shape[0]
     if q.is_cuda:
@@ -261,9 +286,15 @@ def attention_varlen(
             raise ValueError("the native attention kernel supports head_dim 128")
         o = out if out is not None else torch.empty(T, n_heads * head_dim, dtype=q.dtype, device=q.device)
         lse = torch.empty(n_heads, T, dtype=torch.float32, device=q.device)
-        native().attn_fwd(q, k, v, o, lse, cu_seqlens, max_seqlen, n_heads, n_kv_heads, scale, causal,
+        native().attn_fwd(q, k, v, o, lse, cu_seqlens, cu_seqlens_k, max_seqlen, n_heads, n_kv_heads, scale, causal,
                           status_tensor(q.device))
         return o, lse
+    if cu_seqlens_k is not None:
+        o, lse = reference.attention_varlen_qk(
+            q.reshape(T, n_heads, head_dim), k.reshape(-1, n_kv_heads, head_dim), v.reshape(-1, n_kv_heads, head_dim),
+            cu_seqlens, cu_seqlens_k, scale, causal,
+        )
+        return o.reshape(T, n_heads * head_dim), lse
     o, lse = reference.attention_varlen(
         q.reshape(T, n_heads, head_dim), k.reshape(T, n_kv_heads, head_dim), v.reshape(T, n_kv_heads, head_dim),
         cu_seqlens, scale, causal,

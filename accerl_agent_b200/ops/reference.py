@@ -99,6 +99,34 @@ def attention_varlen(
     return out.to(q.dtype), lse
 
 
+def attention_varlen_qk(q, k, v, cu_q, cu_k, scale: float, causal: bool = True):
+    """Queries ``q[cu_q[b]:cu_q[b+1]]`` are the last ones of sequence b whose keys are
+    ``k[cu_k[b]:cu_k[b+1]]`` (causal mask aligned to the end)."""
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    group = Hq // Hkv
+    out = torch.zeros(T, Hq, D, dtype=torch.float32, device=q.device)
+    lse = torch.zeros(Hq, T, dtype=torch.float32, device=q.device)
+    cq, ck = cu_q.tolist(), cu_k.tolist()
+    for b in range(len(cq) - 1):
+        qs, qe, ks, ke = cq[b], cq[b + 1], ck[b], ck[b + 1]
+        Lq, Lk = qe - qs, ke - ks
+        if Lq <= 0:
+            continue
+        qb = q[qs:qe].float().transpose(0, 1)
+        kb = k[ks:ke].float().transpose(0, 1).repeat_interleave(group, 0)
+        vb = v[ks:ke].float().transpose(0, 1).repeat_interleave(group, 0)
+        scores = torch.matmul(qb, kb.transpose(1, 2)) * scale
+        if causal:
+            qpos = torch.arange(Lq, device=q.device).unsqueeze(1) + (Lk - Lq)
+            kpos = torch.arange(Lk, device=q.device).unsqueeze(0)
+            scores = scores.masked_fill(kpos > qpos, float("-inf"))
+        lse_b = torch.logsumexp(scores, dim=-1)
+        out[qs:qe] = torch.matmul(torch.exp(scores - lse_b.unsqueeze(-1)), vb).transpose(0, 1)
+        lse[:, qs:qe] = lse_b
+    return out.to(q.dtype), lse
+
+
 def logsoftmax_label(logits: torch.Tensor, labels: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     lf = logits.float()
     lse = torch.logsumexp(lf, dim=-1)

@@ -47,6 +47,7 @@ struct AttnFwdParams {
   __nv_bfloat16* o;
   float* lse;
   const int* cu;
+  const int* cu_k;  // key boundaries; equal to cu for self-attention over packed sequences
   int max_tiles, T, Hq, Hkv;
   long long ldo;
   float scale_log2;
@@ -63,8 +64,15 @@ __global__ void __launch_bounds__(192, 1)
   const int seq_start = p.cu[b];
   const int len = p.cu[b + 1] - seq_start;
   if (q_tile * kTile >= len) return;
-  const int n_kv = p.causal ? q_tile + 1 : (len + kTile - 1) / kTile;
+  // Keys may outnumber queries (a chunk of new queries over a cached prefix): query i sits at key
+  // position i + k_off, and causal masking is aligned to the end of the key range.
+  const int k_start = p.cu_k[b];
+  const int len_k = p.cu_k[b + 1] - k_start;
+  const int k_off = len_k - len;
+  const int kv_tiles = (len_k + kTile - 1) / kTile;
+  const int n_kv = p.causal ? min(kv_tiles, (q_tile * kTile + kTile - 1 + k_off) / kTile + 1) : kv_tiles;
   const int kvh = head / (p.Hq / p.Hkv);
+  if (n_kv <= 0) return;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -119,7 +127,7 @@ __global__ void __launch_bounds__(192, 1)
           ok = false;
           break;
         }
-        const int ky = seq_start + j * kTile;
+        const int ky = k_start + j * kTile;
         mbar_arrive_expect_tx(&k_full[s], kTileBytes);
         tma_load_2d(sK + s * kTileBytes, &tmK, &k_full[s], kvh * kHd, ky);
         tma_load_2d(sK + s * kTileBytes + kChunk, &tmK, &k_full[s], kvh * kHd + 64, ky);
@@ -191,12 +199,13 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive(&s_free[bsel]);
-      if (j == n_kv - 1) {
-        const int kbase = j * kTile;
+      const int kbase = j * kTile;
+      if ((p.causal && kbase + kTile - 1 > q_tile * kTile + k_off) || kbase + kTile > len_k) {
+        const int lim = q_pos + k_off;
 #pragma unroll
         for (int e = 0; e < 128; ++e) {
           const int kp = kbase + e;
-          if ((p.causal && kp > q_pos) || kp >= len) x[e] = -INFINITY;
+          if ((p.causal && kp > lim) || kp >= len_k) x[e] = -INFINITY;
         }
       }
       float mx = x[0];
@@ -609,15 +618,15 @@ constexpr int kBwdSmem = 6 * kTileBytes + 1024 + 1024 + 256;
 using namespace accerl;
 
 extern "C" int accerl_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_seqlens,
-                               int num_seqs, int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq,
-                               long long ldk, long long ldv, long long ldo, float scale, int causal, int* status,
-                               cudaStream_t s) {
+                               const int* cu_seqlens_k, int num_seqs, int max_seqlen, int total_tokens, int total_k,
+                               int Hq, int Hkv, long long ldq, long long ldk, long long ldv, long long ldo, float scale,
+                               int causal, int* status, cudaStream_t s) {
   if (num_seqs <= 0 || total_tokens <= 0) return 0;
   if (Hq % Hkv) return -1;
   if ((ldq | ldk | ldv | ldo) & 7) return -2;
   CUtensorMap mq, mk, mv;
-  if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq) || !attn_map(&mk, k, total_tokens, Hkv * kHd, ldk) ||
-      !attn_map(&mv, v, total_tokens, Hkv * kHd, ldv))
+  if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq) || !attn_map(&mk, k, total_k, Hkv * kHd, ldk) ||
+      !attn_map(&mv, v, total_k, Hkv * kHd, ldv))
     return -3;
   static bool attr = false;
   if (!attr) {
@@ -629,6 +638,7 @@ extern "C" int accerl_attn_fwd(const void* q, const void* k, const void* v, void
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.lse = lse;
   p.cu = cu_seqlens;
+  p.cu_k = cu_seqlens_k ? cu_seqlens_k : cu_seqlens;
   p.max_tiles = (max_seqlen + kTile - 1) / kTile;
   p.T = total_tokens;
   p.Hq = Hq;

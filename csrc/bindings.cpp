@@ -9,7 +9,10 @@
 extern "C" {
 int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn, void* C,
                      long long ldc, int c_f32, int M, int N, int K, float alpha, float beta, const void* bias,
-                     const void* residual, long long ldr, int* status, int block_n, int max_ctas, cudaStream_t stream);
+                     const void* residual, long long ldr, int* status, int block_n, int max_ctas, int splits,
+                     cudaStream_t stream);
+int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
+                         void* out, long long ldo, int M, int N, cudaStream_t stream);
 int accerl_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int H, long long ldx,
                        long long ldy, float eps, cudaStream_t s);
 int accerl_rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, const void* dx_accum, void* dx,
@@ -34,8 +37,9 @@ int accerl_adamw(float* master, float* m, float* v, float* grad, void* param, lo
                  float lr, float beta1, float beta2, float eps, float weight_decay, float max_norm, float bc1,
                  float bc2_sqrt, cudaStream_t s);
 int accerl_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_seqlens,
-                    int num_seqs, int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq, long long ldk,
-                    long long ldv, long long ldo, float scale, int causal, int* status, cudaStream_t s);
+                    const int* cu_seqlens_k, int num_seqs, int max_seqlen, int total_tokens, int total_k, int Hq,
+                    int Hkv, long long ldq, long long ldk, long long ldv, long long ldo, float scale, int causal,
+                    int* status, cudaStream_t s);
 int accerl_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
                     float* delta, float* dq_acc, void* dq, void* dk, void* dv, const int* cu_seqlens, int num_seqs,
                     int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq, long long ldk, long long ldv,
@@ -98,7 +102,7 @@ long long ld_of(const at::Tensor& t) {
 // a: [M,K] (a_mn=false) or [K,M] (a_mn=true); b: [N,K] (b_mn=false) or [K,N] (b_mn=true)
 void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, double alpha, double beta,
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& residual,
-          const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas) {
+          const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas, int64_t splits) {
   CHECK_CUDA(a);
   CHECK_CUDA(b);
   CHECK_CUDA(out);
@@ -125,8 +129,18 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
   check(accerl_gemm_bf16(a.data_ptr(), ld_of(a), a_mn, b.data_ptr(), ld_of(b), b_mn, out.data_ptr(), ld_of(out),
                          out.scalar_type() == at::kFloat, M, N, K, static_cast<float>(alpha), static_cast<float>(beta),
                          opt_ptr(bias), opt_ptr(residual), ldr, status_ptr(status), static_cast<int>(block_n),
-                         static_cast<int>(max_ctas), cur_stream()),
+                         static_cast<int>(max_ctas), static_cast<int>(splits), cur_stream()),
         "gemm");
+}
+
+void splitk_finish(const at::Tensor& acc, const c10::optional<at::Tensor>& bias,
+                   const c10::optional<at::Tensor>& residual, at::Tensor& out) {
+  CHECK_F32(acc);
+  CHECK_BF16(out);
+  check(accerl_splitk_finish(acc.data_ptr<float>(), ld_of(acc), opt_ptr(bias), opt_ptr(residual),
+                             residual.has_value() ? ld_of(*residual) : 0, out.data_ptr(), ld_of(out), out.size(0),
+                             out.size(1), cur_stream()),
+        "splitk_finish");
 }
 
 at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& rstd,
@@ -263,18 +277,19 @@ void adamw(at::Tensor& master, at::Tensor& m, at::Tensor& v, at::Tensor& grad, a
 
 // q: [T, Hq*D] view (row stride ldq), k/v: [T, Hkv*D], o: [T, Hq*D]; lse: [Hq, T] fp32
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
-              const at::Tensor& cu_seqlens, int64_t max_seqlen, int64_t Hq, int64_t Hkv, double scale, bool causal,
-              const c10::optional<at::Tensor>& status) {
+              const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& cu_seqlens_k, int64_t max_seqlen,
+              int64_t Hq, int64_t Hkv, double scale, bool causal, const c10::optional<at::Tensor>& status) {
   CHECK_BF16(q);
   CHECK_BF16(k);
   CHECK_BF16(v);
   CHECK_BF16(o);
   CHECK_F32(lse);
   CHECK_I32(cu_seqlens);
+  const int* cuk = cu_seqlens_k.has_value() ? cu_seqlens_k->data_ptr<int>() : nullptr;
   check(accerl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
-                        cu_seqlens.data_ptr<int>(), cu_seqlens.numel() - 1, max_seqlen, q.size(0), Hq, Hkv, ld_of(q),
-                        ld_of(k), ld_of(v), ld_of(o), static_cast<float>(scale), causal, status_ptr(status),
-                        cur_stream()),
+                        cu_seqlens.data_ptr<int>(), cuk, cu_seqlens.numel() - 1, max_seqlen, q.size(0), k.size(0), Hq,
+                        Hkv, ld_of(q), ld_of(k), ld_of(v), ld_of(o), static_cast<float>(scale), causal,
+                        status_ptr(status), cur_stream()),
         "attn_fwd");
 }
 
@@ -332,6 +347,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "accerl_agent_b200 sm_100a kernels";
   m.def("last_error", &last_error, "(code, message) of the most recent launch; resets it");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM");
+  m.def("splitk_finish", &splitk_finish);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("bias_grad", &bias_grad);

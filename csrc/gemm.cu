@@ -43,6 +43,7 @@ struct GemmParams {
   long long ldr;
   int* status;
   int tiles_m, tiles_n, num_tiles, group_m;
+  int splits, kb_per_split;  // split-K: work item = (tile, split); splits > 1 adds fp32 partials atomically
 };
 
 template <int BN>
@@ -53,6 +54,7 @@ struct GemmSmem {
 };
 
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_blk, int& n_blk) {
+  t /= p.splits;
   const int per_group = p.group_m * p.tiles_n;
   const int group = t / per_group;
   const int first_m = group * p.group_m;
@@ -115,7 +117,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int m_blk, n_blk;
         tile_coords(p, t, m_blk, n_blk);
         const int m0 = m_blk * kBM, n0 = n_blk * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        const int kb0 = (t % p.splits) * p.kb_per_split;
+        const int kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer)) {
             ok = false;
             break;
@@ -164,7 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tbase + acc * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        const int kb0 = (t % p.splits) * p.kb_per_split;
+        const int kb1 = min(k_blocks, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             else adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
             if constexpr (B_MN) bdesc = make_sw128_desc(b_addr + kk * 16 * 128, 64 * kBK * 2, 1024);
             else bdesc = make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb != kb0) || (kk != 0));
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -239,7 +245,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               f[2 * i + 1] += rr.y;
             }
           }
-          if (p.c_f32) {
+          if (p.splits > 1) {
+            // split-K partial: add into the fp32 output (pre-initialised by the caller)
+            float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            atomicAdd(reinterpret_cast<float4*>(c), make_float4(f[0], f[1], f[2], f[3]));
+            atomicAdd(reinterpret_cast<float4*>(c + 4), make_float4(f[4], f[5], f[6], f[7]));
+          } else if (p.c_f32) {
             float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
             if (p.beta != 0.f) {
               const float4 o0 = *reinterpret_cast<const float4*>(c);
@@ -390,7 +401,7 @@ int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMa
 extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                                 void* C, long long ldc, int c_f32, int M, int N, int K, float alpha, float beta,
                                 const void* bias, const void* residual, long long ldr, int* status, int block_n,
-                                int max_ctas, cudaStream_t stream) {
+                                int max_ctas, int splits, cudaStream_t stream) {
   using namespace accerl;
   if (M <= 0 || N <= 0) return 0;
   if (K <= 0) return -1;
@@ -402,7 +413,7 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   int bn = block_n;
   if (bn != 128 && bn != 256) {
     const long long tiles256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
-    bn = (N <= 128 || tiles256 < num_sms() / 2) ? 128 : 256;
+    bn = (N <= 128 || tiles256 < num_sms()) ? 128 : 256;
   }
   CUtensorMap ma, mb;
   bool ok;
@@ -427,8 +438,54 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   p.status = status;
   p.tiles_m = (M + kBM - 1) / kBM;
   p.tiles_n = (N + bn - 1) / bn;
-  p.num_tiles = p.tiles_m * p.tiles_n;
+  const int k_blocks = (K + kBK - 1) / kBK;
+  if (splits <= 0) {
+    // automatic: split K when the tile grid would leave most SMs idle and K is long
+    const int tiles = p.tiles_m * p.tiles_n;
+    splits = 1;
+    if (c_f32 && beta == 1.f && !bias && !residual) {
+      while (tiles * splits * 2 <= num_sms() && k_blocks / (splits * 2) >= 4) splits *= 2;
+    }
+  }
+  if (splits > 1 && (!c_f32 || bias || residual || beta != 1.f)) return -9;
+  p.kb_per_split = (k_blocks + splits - 1) / splits;
+  p.splits = (k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  p.num_tiles = p.tiles_m * p.tiles_n * p.splits;
   p.group_m = 8;
   if (bn == 256) return dispatch_major<256, 4>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
   return dispatch_major<128, 6>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
+}
+
+// out_bf16[m, n] = bf16(acc[m, n] + bias[n] + residual[m, n]) : finishing pass of a split-K GEMM.
+__global__ void splitk_finish_kernel(const float* __restrict__ acc, long long lda, const __nv_bfloat16* __restrict__ bias,
+                                     const __nv_bfloat16* __restrict__ residual, long long ldr,
+                                     __nv_bfloat16* __restrict__ out, long long ldo, int M, int N) {
+  const long long idx = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (idx >= static_cast<long long>(M) * N) return;
+  const int m = static_cast<int>(idx / N), n = static_cast<int>(idx % N);
+  const float4 a0 = *reinterpret_cast<const float4*>(acc + m * lda + n);
+  const float4 a1 = *reinterpret_cast<const float4*>(acc + m * lda + n + 4);
+  float f[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  if (bias) {
+    for (int i = 0; i < 8; ++i) f[i] += __bfloat162float(bias[n + i]);
+  }
+  if (residual) {
+    for (int i = 0; i < 8; ++i) f[i] += __bfloat162float(residual[m * ldr + n + i]);
+  }
+  uint4 o;
+  o.x = accerl::pack_bf16x2(f[0], f[1]);
+  o.y = accerl::pack_bf16x2(f[2], f[3]);
+  o.z = accerl::pack_bf16x2(f[4], f[5]);
+  o.w = accerl::pack_bf16x2(f[6], f[7]);
+  *reinterpret_cast<uint4*>(out + m * ldo + n) = o;
+}
+
+extern "C" int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual,
+                                    long long ldr, void* out, long long ldo, int M, int N, cudaStream_t stream) {
+  if (N % 8) return -1;
+  const long long n8 = (long long)M * N / 8;
+  if (n8 == 0) return 0;
+  splitk_finish_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>(
+      acc, lda, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)residual, ldr, (__nv_bfloat16*)out, ldo, M, N);
+  return (int)cudaGetLastError();
 }

@@ -277,3 +277,41 @@ def test_sampler_greedy_and_distribution():
     freq = torch.bincount(tok, minlength=64)[:4].float() / 4000
     probs = torch.softmax(small[0, :4].float(), -1)
     assert torch.allclose(freq, probs, atol=0.03)
+
+
+@pytest.mark.parametrize("splits", [2, 4, 0])
+def test_gemm_split_k_accumulate(splits):
+    M, N, K = 256, 512, 4096
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    acc = torch.randn(M, N, device=DEV)
+    base = acc.clone()
+    ops.gemm(A.t().contiguous(), B.t().contiguous(), acc, a_mn=True, b_mn=True, beta=1.0, out_dtype=torch.float32,
+             splits=splits)
+    assert _rel(acc, base + A.float() @ B.float().t()) < 1e-5
+
+
+@pytest.mark.parametrize("M", [1, 7, 64, 256])
+def test_skinny_linear_split_k_with_bias_residual(M):
+    N, K = 2048, 1536
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    b = torch.randn(N, device=DEV).bfloat16()
+    r = torch.randn(M, N, device=DEV).bfloat16()
+    y = ops.linear(x, w, bias=b, residual=r)
+    assert _rel(y, x.float() @ w.float().t() + b.float() + r.float()) < 1e-2
+
+
+@pytest.mark.parametrize("q_lens,k_lens", [([5, 130, 1], [300, 130, 77]), ([200], [1000])])
+def test_attention_forward_queries_over_longer_keys(q_lens, k_lens):
+    Hq, Hkv, D = 4, 2, 128
+    cu_q = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    cu_k = torch.tensor([0] + list(torch.tensor(k_lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    q = torch.randn(sum(q_lens), Hq * D, device=DEV).bfloat16()
+    k = torch.randn(sum(k_lens), Hkv * D, device=DEV).bfloat16()
+    v = torch.randn(sum(k_lens), Hkv * D, device=DEV).bfloat16()
+    o, lse = ops.attention_varlen(q, k, v, cu_q, max(q_lens), Hq, Hkv, D, cu_seqlens_k=cu_k)
+    o_r, lse_r = ref.attention_varlen_qk(q.reshape(-1, Hq, D), k.reshape(-1, Hkv, D), v.reshape(-1, Hkv, D), cu_q,
+                                         cu_k, 1 / math.sqrt(D))
+    assert _rel(o, o_r.reshape(o.shape)) < 2e-2
+    assert torch.allclose(lse, lse_r, atol=1e-2)
