@@ -294,12 +294,16 @@ def attention_varlen(
             q.reshape(T, n_heads, head_dim), k.reshape(-1, n_kv_heads, head_dim), v.reshape(-1, n_kv_heads, head_dim),
             cu_seqlens, cu_seqlens_k, scale, causal,
         )
-        return o.reshape(T, n_heads * head_dim), lse
-    o, lse = reference.attention_varlen(
-        q.reshape(T, n_heads, head_dim), k.reshape(T, n_kv_heads, head_dim), v.reshape(T, n_kv_heads, head_dim),
-        cu_seqlens, scale, causal,
-    )
-    return o.reshape(T, n_heads * head_dim), lse
+    else:
+        o, lse = reference.attention_varlen(
+            q.reshape(T, n_heads, head_dim), k.reshape(T, n_kv_heads, head_dim), v.reshape(T, n_kv_heads, head_dim),
+            cu_seqlens, scale, causal,
+        )
+    o = o.reshape(T, n_heads * head_dim)
+    if out is not None:
+        out.copy_(o)
+        o = out
+    return o, lse
 
 
 def attention_varlen_backward(
@@ -427,7 +431,11 @@ def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads
                               num_splits, scale)
         return o
     res = reference.paged_decode(q.reshape(S, n_heads, D), k_cache, v_cache, block_table, seq_lens, scale)
-    return res.reshape(S, n_heads * D)
+    res = res.reshape(S, n_heads * D)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
 
 
 def kv_cache_write(k, v, k_cache, v_cache, slot_mapping, n_kv_heads):

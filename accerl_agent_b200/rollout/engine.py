@@ -1,0 +1,570 @@
+"""Native paged-KV generation engine (continuous batching, chunked prefill, prefix caching,
+temperature sampling, abort/pause/resume, in-place weight updates).
+
+It is the rollout-side replacement of the vLLM ``AsyncLLMEngine`` that the reference drives
+(agent_textworld.py:1916-2060) and exposes the same asynchronous surface:
+
+* ``async for out in engine.generate({"prompt_token_ids": ids}, sampling_params, request_id=...)``
+  yields cumulative ``RequestOutput`` objects (``.finished``, ``.outputs[0].token_ids``,
+  ``.outputs[0].finish_reason``, ``.outputs[0].logprobs`` as ``[{token: logprob}]``);
+* ``pause_generation(mode="abort", clear_cache=True)`` finishes every in-flight request with reason
+  ``"abort"`` and frees (and optionally forgets) the KV cache; ``resume_generation()``;
+* ``collective_rpc("reload_weights", kwargs={"weights_path": ...})`` and ``load_flat_weights`` for
+  in-place weight updates (the trainer and engine share the fused flat parameter layout).
+
+One background thread runs the step loop. A step schedules decode tokens of running sequences first
+and then prefill chunks of waiting ones under ``max_num_batched_tokens`` / ``max_num_seqs``, runs one
+forward over the mixed batch (new K/V written straight into their paged slots, prefill queries over
+their cached prefix with the varlen attention kernel, decode queries with the paged decode kernel),
+applies the LM head only to rows that sample, and samples with the fused Gumbel-max kernel, which
+also returns each sampled token's log-probability. Sampled ids come back to the host once per step.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import itertools
+import math
+import threading
+import time
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Any, Deque, Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.config import ModelConfig
+from ..models.transformer import CausalLM, ParamLayout
+from .generation import SamplingParams
+from .kv_cache import BlockAllocator, block_hash
+
+
+@dataclass
+class CompletionOutput:
+    index: int
+    token_ids: List[int]
+    finish_reason: Optional[str]
+    logprobs: Optional[List[Dict[int, float]]]
+    text: str = ""
+
+
+@dataclass
+class RequestOutput:
+    request_id: str
+    prompt_token_ids: List[int]
+    outputs: List[CompletionOutput]
+    finished: bool
+
+
+@dataclass
+class _Seq:
+    rid: str
+    prompt: List[int]
+    params: SamplingParams
+    seed: int
+    loop: Any
+    queue: Any
+    out: List[int] = field(default_factory=list)
+    lps: List[float] = field(default_factory=list)
+    blocks: List[int] = field(default_factory=list)
+    hashes: List[int] = field(default_factory=list)
+    num_computed: int = 0
+    finish_reason: Optional[str] = None
+    arrival: float = 0.0
+
+    @property
+    def tokens(self) -> List[int]:
+        return self.prompt + self.out
+
+    @property
+    def length(self) -> int:
+        return len(self.prompt) + len(self.out)
+
+
+class GenerationEngine:
+    def __init__(
+        self,
+        cfg: ModelConfig,
+        device: torch.device,
+        dtype: torch.dtype = torch.bfloat16,
+        max_num_seqs: int = 128,
+        max_num_batched_tokens: int = 8192,
+        max_model_len: Optional[int] = None,
+        block_size: int = 16,
+        num_blocks: Optional[int] = None,
+        kv_cache_gb: Optional[float] = None,
+        enable_prefix_caching: bool = True,
+        tokenizer=None,
+        params: Optional[torch.Tensor] = None,
+        seed: int = 0,
+        decode_splits: Optional[int] = None,
+    ):
+        self.cfg = cfg
+        self.device = device
+        self.dtype = dtype
+        self.max_num_seqs = max_num_seqs
+        self.max_num_batched_tokens = max_num_batched_tokens
+        self.max_model_len = max_model_len or cfg.max_position_embeddings
+        self.block_size = block_size
+        self.tokenizer = tokenizer
+        self.layout = ParamLayout.build(cfg, "full")
+        if params is None:
+            params = torch.zeros(self.layout.total_numel, dtype=dtype, device=device)
+        self.model = CausalLM(cfg, self.layout, params, None)
+        L, Hkv, D = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+        per_block = 2 * L * block_size * Hkv * D * torch.tensor([], dtype=dtype).element_size()
+        if num_blocks is None:
+            if kv_cache_gb is None:
+                if device.type == "cuda":
+                    free, _ = torch.cuda.mem_get_info(device)
+                    kv_cache_gb = 0.6 * free / 1024**3
+                else:
+                    kv_cache_gb = 0.25
+            num_blocks = max(16, int(kv_cache_gb * 1024**3 // per_block))
+        self.num_blocks = num_blocks
+        self.k_cache = torch.zeros(L, num_blocks, block_size, Hkv, D, dtype=dtype, device=device)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.allocator = BlockAllocator(num_blocks, block_size, enable_prefix_caching)
+        self.waiting: Deque[_Seq] = deque()
+        self.running: List[_Seq] = []
+        self.by_id: Dict[str, _Seq] = {}
+        self.paused = False
+        self._lock = threading.RLock()  # protects queues and sequence state
+        self._step_lock = threading.Lock()  # held for the duration of one engine step
+        self._wake = threading.Condition(self._lock)
+        self._stop = False
+        self._seed_counter = itertools.count(seed * 1_000_003 + 1)
+        self.decode_splits = decode_splits
+        self.stats = {"generated_tokens": 0, "prompt_tokens_computed": 0, "steps": 0, "preemptions": 0,
+                      "aborted": 0, "finished": 0}
+        self._thread: Optional[threading.Thread] = None
+        self.eos_ids = {cfg.eos_token_id}
+        if tokenizer is not None and getattr(tokenizer, "eos_token_id", None) is not None:
+            self.eos_ids.add(int(tokenizer.eos_token_id))
+
+    # ------------------------------------------------------------------ lifecycle
+    def start(self) -> None:
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._run_loop, name="generation-engine", daemon=True)
+            self._thread.start()
+
+    async def shutdown(self) -> None:
+        with self._lock:
+            self._stop = True
+            self._wake.notify_all()
+        if self._thread is not None:
+            await asyncio.to_thread(self._thread.join, 30)
+            self._thread = None
+        self._abort_all("abort")
+
+    def _run_loop(self) -> None:
+        while True:
+            with self._lock:
+                while not self._stop and (self.paused or (not self.waiting and not self.running)):
+                    self._wake.wait(timeout=0.5)
+                if self._stop:
+                    return
+            try:
+                self.step()
+            except Exception as exc:  # fail every request loudly instead of hanging callers
+                import traceback
+
+                traceback.print_exc()
+                self._abort_all("abort", error=exc)
+
+    # ------------------------------------------------------------------ public async API
+    async def generate(self, prompt: Dict[str, List[int]], sampling_params: SamplingParams, request_id: str):
+        if self._thread is None:
+            self.start()
+        loop = asyncio.get_running_loop()
+        queue: asyncio.Queue = asyncio.Queue()
+        ids = list(prompt["prompt_token_ids"])
+        seed = sampling_params.seed if sampling_params.seed is not None else next(self._seed_counter)
+        seq = _Seq(request_id, ids, sampling_params, int(seed) & ((1 << 62) - 1), loop, queue, arrival=time.time())
+        with self._lock:
+            if request_id in self.by_id:
+                raise ValueError(f"duplicate request id {request_id}")
+            self.by_id[request_id] = seq
+            self.waiting.append(seq)
+            self._wake.notify_all()
+        finished = False
+        try:
+            while True:
+                item = await queue.get()
+                if isinstance(item, BaseException):
+                    raise item
+                yield item
+                if item.finished:
+                    finished = True
+                    break
+        finally:
+            if not finished:
+                self.abort(request_id)
+
+    def abort(self, request_id: str) -> None:
+        with self._step_lock, self._lock:
+            seq = self.by_id.get(request_id)
+            if seq is not None:
+                self._finish(seq, "abort")
+
+    async def pause_generation(self, mode: str = "abort", clear_cache: bool = True) -> None:
+        """Stop scheduling; with ``mode='abort'`` every in-flight request ends with reason 'abort'."""
+        def _pause():
+            with self._step_lock, self._lock:
+                self.paused = True
+                if mode == "abort":
+                    self._abort_all("abort")
+                if clear_cache:
+                    self.allocator.clear_cache()
+
+        await asyncio.to_thread(_pause)
+
+    async def resume_generation(self) -> None:
+        with self._lock:
+            self.paused = False
+            self._wake.notify_all()
+
+    async def collective_rpc(self, method: str, kwargs: Optional[Dict[str, Any]] = None, args=()):
+        kwargs = kwargs or {}
+        if method == "reload_weights":
+            path = kwargs.get("weights_path") or (args[0] if args else None)
+            await asyncio.to_thread(self.reload_weights, path)
+            return [None]
+        fn = getattr(self, method)
+        res = fn(*args, **kwargs)
+        if asyncio.iscoroutine(res):
+            res = await res
+        return [res]
+
+    def reload_weights(self, path: str) -> None:
+        from ..models.hf_io import load_hf_checkpoint
+
+        with self._step_lock:
+            load_hf_checkpoint(self.model, path)
+            self.allocator.clear_cache()
+
+    def load_flat_weights(self, src: torch.Tensor, start: int = 0, stream=None) -> None:
+        """Copy a fused-layout flat weight range (from a trainer, possibly a peer GPU's memory)."""
+        with self._step_lock:
+            dst = self.model.params[start : start + src.numel()]
+            if stream is not None:
+                with torch.cuda.stream(stream):
+                    dst.copy_(src, non_blocking=True)
+            else:
+                dst.copy_(src, non_blocking=True)
+
+    def get_stats(self) -> Dict[str, Any]:
+        with self._lock:
+            s = dict(self.stats)
+            s.update(waiting=len(self.waiting), running=len(self.running), free_blocks=self.allocator.num_free,
+                     prefix_cache_hit_rate=self.allocator.hits / max(self.allocator.queries, 1))
+            return s
+
+    # ------------------------------------------------------------------ request bookkeeping
+    def _deliver(self, seq: _Seq, finished: bool, error: Optional[BaseException] = None) -> None:
+        if error is not None:
+            item: Any = error
+        else:
+            want_lp = seq.params.logprobs is not None
+            comp = CompletionOutput(
+                0, list(seq.out), seq.finish_reason if finished else None,
+                [{t: lp} for t, lp in zip(seq.out, seq.lps)] if want_lp else None,
+            )
+            item = RequestOutput(seq.rid, seq.prompt, [comp], finished)
+        try:
+            seq.loop.call_soon_threadsafe(seq.queue.put_nowait, item)
+        except RuntimeError:
+            pass  # the caller's event loop is gone
+
+    def _finish(self, seq: _Seq, reason: str, error: Optional[BaseException] = None) -> None:
+        seq.finish_reason = reason
+        if seq in self.running:
+            self.running.remove(seq)
+        try:
+            self.waiting.remove(seq)
+        except ValueError:
+            pass
+        self.allocator.free(seq.blocks)
+        seq.blocks = []
+        self.by_id.pop(seq.rid, None)
+        self.stats["aborted" if reason == "abort" else "finished"] += 1
+        self._deliver(seq, True, error)
+
+    def _abort_all(self, reason: str, error: Optional[BaseException] = None) -> None:
+        with self._lock:
+            for seq in list(self.running) + list(self.waiting):
+                self._finish(seq, reason, error)
+
+    # ------------------------------------------------------------------ scheduling
+    def _ensure_blocks(self, seq: _Seq, upto: int) -> bool:
+        need = (upto + self.block_size - 1) // self.block_size
+        while len(seq.blocks) < need:
+            b = self.allocator.allocate()
+            if b is None:
+                return False
+            seq.blocks.append(b)
+        return True
+
+    def _preempt(self, seq: _Seq) -> None:
+        """Recompute-style preemption: drop the sequence's KV and requeue it first."""
+        self.running.remove(seq)
+        self.allocator.free(seq.blocks)
+        seq.blocks, seq.hashes, seq.num_computed = [], [], 0
+        self.waiting.appendleft(seq)
+        self.stats["preemptions"] += 1
+
+    def _admit(self, seq: _Seq) -> None:
+        toks = seq.tokens
+        blocks, hashes = self.allocator.match_prefix(toks)
+        # always compute at least the last token so there is a row to sample from
+        usable = min(len(blocks) * self.block_size, seq.length - 1)
+        keep = usable // self.block_size
+        self.allocator.free(blocks[keep:])
+        seq.blocks = blocks[:keep]
+        seq.hashes = hashes[:keep]
+        seq.num_computed = keep * self.block_size
+
+    def _schedule(self):
+        budget = self.max_num_batched_tokens
+        plan = []  # (seq, start, n_tokens, samples)
+        with self._lock:
+            if self.paused:
+                return None
+            for seq in list(self.running):
+                if budget <= 0:
+                    break
+                n = min(seq.length - seq.num_computed, budget)
+                if n <= 0:
+                    continue
+                while not self._ensure_blocks(seq, seq.num_computed + n):
+                    victim = self.running[-1]
+                    if victim is seq:
+                        break
+                    self._preempt(victim)
+                    plan = [p for p in plan if p[0] is not victim]
+                if len(seq.blocks) * self.block_size < seq.num_computed + n:
+                    self._preempt(seq)
+                    continue
+                plan.append((seq, seq.num_computed, n, seq.num_computed + n == seq.length))
+                budget -= n
+            while self.waiting and budget > 0 and len(self.running) < self.max_num_seqs:
+                seq = self.waiting[0]
+                if seq.num_computed == 0 and not seq.blocks:
+                    self._admit(seq)
+                n = min(seq.length - seq.num_computed, budget)
+                if not self._ensure_blocks(seq, seq.num_computed + n):
+                    self.allocator.free(seq.blocks)
+                    seq.blocks, seq.hashes, seq.num_computed = [], [], 0
+                    break
+                self.waiting.popleft()
+                self.running.append(seq)
+                plan.append((seq, seq.num_computed, n, seq.num_computed + n == seq.length))
+                budget -= n
+        return plan or None
+
+    # ------------------------------------------------------------------ execution
+    def step(self) -> bool:
+        with self._step_lock:
+            plan = self._schedule()
+            if not plan:
+                return False
+            # multi-token chunks use the varlen kernel over their cached prefix; single tokens (decode
+            # steps, or a one-token tail of a prompt chunk) use the paged decode kernel
+            prefill = [p for p in plan if p[2] > 1]
+            decode = [p for p in plan if p[2] == 1]
+            order = prefill + decode
+            toks, logps = self._execute(order, len(prefill))
+            self._postprocess(order, toks, logps)
+            self.stats["steps"] += 1
+            return True
+
+    def _execute(self, order, n_prefill: int):
+        cfg = self.cfg
+        bs = self.block_size
+        dev = self.device
+        ids: List[int] = []
+        pos: List[int] = []
+        slots: List[int] = []
+        sample_rows: List[int] = []
+        cu_q = [0]
+        cu_k = [0]
+        k_slots: List[int] = []
+        max_q = 1
+        for i, (seq, start, n, samples) in enumerate(order):
+            toks = seq.tokens
+            blocks = np.asarray(seq.blocks, dtype=np.int64)
+            p = np.arange(start, start + n)
+            ids.extend(toks[start : start + n])
+            pos.extend(p.tolist())
+            slots.extend((blocks[p // bs] * bs + p % bs).tolist())
+            if samples:
+                sample_rows.append(len(ids) - 1)
+            if i < n_prefill:
+                cu_q.append(cu_q[-1] + n)
+                ctx = start + n
+                cu_k.append(cu_k[-1] + ctx)
+                pk = np.arange(ctx)
+                k_slots.extend((blocks[pk // bs] * bs + pk % bs).tolist())
+                max_q = max(max_q, n)
+        Tp = cu_q[-1]
+        decode = order[n_prefill:]
+        nd = len(decode)
+        # one host->device transfer for all index data
+        header = [len(ids), len(pos), len(slots), len(sample_rows), len(cu_q), len(cu_k), len(k_slots)]
+        flat = np.concatenate([
+            np.asarray(ids, np.int64), np.asarray(pos, np.int64), np.asarray(slots, np.int64),
+            np.asarray(sample_rows, np.int64), np.asarray(cu_q, np.int64), np.asarray(cu_k, np.int64),
+            np.asarray(k_slots, np.int64),
+        ])
+        host = torch.from_numpy(flat)
+        if dev.type == "cuda":
+            host = host.pin_memory()
+        d = host.to(dev, non_blocking=True)
+        off = np.cumsum([0] + header)
+        ids_d = d[off[0] : off[1]]
+        pos_d = d[off[1] : off[2]]
+        slots_d = d[off[2] : off[3]].to(torch.int32)
+        rows_d = d[off[3] : off[4]]
+        cu_q_d = d[off[4] : off[5]].to(torch.int32)
+        cu_k_d = d[off[5] : off[6]].to(torch.int32)
+        kslots_d = d[off[6] : off[7]]
+        if nd:
+            max_blocks = max(len(s.blocks) for s, *_ in decode)
+            table = np.zeros((nd, max_blocks), np.int32)
+            lens = np.zeros(nd, np.int32)
+            for j, (s, start, n, _) in enumerate(decode):
+                table[j, : len(s.blocks)] = s.blocks
+                lens[j] = start + n
+            dt = torch.from_numpy(np.concatenate([table.reshape(-1), lens]))
+            if dev.type == "cuda":
+                dt = dt.pin_memory()
+            dt = dt.to(dev, non_blocking=True)
+            table_d = dt[: nd * max_blocks].view(nd, max_blocks)
+            lens_d = dt[nd * max_blocks :]
+            max_len = int(lens.max())
+        m = self.model
+        D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        scale = 1.0 / math.sqrt(D)
+        splits = self.decode_splits or max(1, min(16, (148 * 2) // max(nd * Hkv, 1)))
+        with torch.no_grad():
+            x = ops.embedding(ids_d, m.w("model.embed_tokens.weight"))
+            for layer in range(cfg.num_hidden_layers):
+                p = f"model.layers.{layer}."
+                h1, _ = ops.rmsnorm(x, m.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
+                bias = m.w(p + "self_attn.qkv_proj.bias") if cfg.qkv_bias else None
+                qkv = ops.linear(h1, m.w(p + "self_attn.qkv_proj.weight"), bias=bias)
+                if cfg.qk_norm:
+                    m._qk_norm_forward(layer, qkv)
+                ops.rope_(qkv, pos_d, Hq + Hkv, D, cfg.rope_theta)
+                q = qkv[:, : cfg.q_dim]
+                k = qkv[:, cfg.q_dim : cfg.q_dim + cfg.kv_dim]
+                v = qkv[:, cfg.q_dim + cfg.kv_dim :]
+                kc, vc = self.k_cache[layer], self.v_cache[layer]
+                ops.kv_cache_write(k, v, kc, vc, slots_d, Hkv)
+                attn = torch.empty(x.shape[0], cfg.q_dim, dtype=x.dtype, device=dev)
+                if Tp:
+                    kctx = kc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
+                    vctx = vc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
+                    ops.attention_varlen(q[:Tp], kctx, vctx, cu_q_d, max_q, Hq, Hkv, D, scale=scale,
+                                         out=attn[:Tp], cu_seqlens_k=cu_k_d)
+                if nd:
+                    ops.paged_decode(q[Tp:], kc, vc, table_d, lens_d, Hq, Hkv, scale, num_splits=splits,
+                                     out=attn[Tp:])
+                x = ops.linear(attn, m.w(p + "self_attn.o_proj.weight"), residual=x)
+                h2, _ = ops.rmsnorm(x, m.w(p + "post_attention_layernorm.weight"), cfg.rms_norm_eps)
+                if cfg.layer_is_moe(layer):
+                    from ..models.moe import moe_forward
+
+                    x, _ = moe_forward(m, layer, h2, x, save=False)
+                else:
+                    gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
+                    x = ops.linear(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), residual=x)
+            if not sample_rows:
+                return [], []
+            xs = x.index_select(0, rows_d)
+            hN, _ = ops.rmsnorm(xs, m.w("model.norm.weight"), cfg.rms_norm_eps)
+            logits = ops.linear(hN, m.w(m.lm_head_name))
+            sampled = [e for e in order if e[3]]
+            temps = torch.tensor([float(s.params.temperature) for s, *_ in sampled], dtype=torch.float32)
+            seeds = torch.tensor([s.seed for s, *_ in sampled], dtype=torch.int64)
+            offs = torch.tensor([len(s.out) for s, *_ in sampled], dtype=torch.int64)
+            if any(s.params.top_p < 1.0 or (s.params.top_k or -1) > 0 for s, *_ in sampled):
+                tokens, lps = _sample_filtered(logits, [s.params for s, *_ in sampled], seeds)
+            else:
+                tokens, lps = ops.sample(logits, temps.to(dev), seeds.to(dev), offs.to(dev))
+            res = torch.stack([tokens.double(), lps.double()]).cpu()  # the one device->host read per step
+        return res[0].long().tolist(), res[1].tolist()
+
+    def _postprocess(self, order, tokens: List[int], logps: List[float]) -> None:
+        bs = self.block_size
+        it = iter(zip(tokens, logps))
+        with self._lock:
+            for seq, start, n, samples in order:
+                if seq.finish_reason is not None:
+                    if samples:
+                        next(it)
+                    continue
+                seq.num_computed = start + n
+                self.stats["prompt_tokens_computed"] += n
+                # register newly completed full blocks for prefix reuse
+                toks = seq.tokens
+                while len(seq.hashes) < seq.num_computed // bs:
+                    i = len(seq.hashes)
+                    parent = seq.hashes[-1] if seq.hashes else None
+                    h = block_hash(parent, toks[i * bs : (i + 1) * bs])
+                    seq.hashes.append(h)
+                    self.allocator.register(seq.blocks[i], h)
+                if not samples:
+                    continue
+                tok, lp = next(it)
+                seq.out.append(int(tok))
+                seq.lps.append(float(lp))
+                self.stats["generated_tokens"] += 1
+                reason = self._stop_reason(seq, int(tok))
+                if reason is not None:
+                    self._finish(seq, reason)
+                else:
+                    self._deliver(seq, False)
+
+    def _stop_reason(self, seq: _Seq, tok: int) -> Optional[str]:
+        p = seq.params
+        if not p.ignore_eos and tok in self.eos_ids:
+            return "stop"
+        if p.stop_token_ids and tok in p.stop_token_ids:
+            return "stop"
+        if p.stop and self.tokenizer is not None:
+            tail = self.tokenizer.decode(seq.out[-8:], skip_special_tokens=p.skip_special_tokens)
+            if any(s in tail for s in p.stop):
+                return "stop"
+        if len(seq.out) >= p.max_tokens or seq.length >= self.max_model_len:
+            return "length"
+        return None
+
+
+def _sample_filtered(logits: torch.Tensor, params: List[SamplingParams], seeds: torch.Tensor):
+    """top-p / top-k sampling (sort based). Returns tokens and untempered log-probabilities."""
+    lf = logits.float()
+    logp = torch.log_softmax(lf, dim=-1)
+    out = torch.empty(lf.shape[0], dtype=torch.long, device=lf.device)
+    for i, p in enumerate(params):
+        row = lf[i]
+        if p.temperature <= 0:
+            out[i] = torch.argmax(row)
+            continue
+        row = row / p.temperature
+        if p.top_k and p.top_k > 0:
+            kth = torch.topk(row, min(p.top_k, row.numel())).values[-1]
+            row = row.masked_fill(row < kth, float("-inf"))
+        probs = torch.softmax(row, dim=-1)
+        if p.top_p < 1.0:
+            sp, si = torch.sort(probs, descending=True)
+            keep = torch.cumsum(sp, 0) - sp < p.top_p
+            sp = sp * keep
+            probs = torch.zeros_like(probs).scatter_(0, si, sp)
+            probs = probs / probs.sum()
+        g = torch.Generator(device=lf.device)
+        g.manual_seed(int(seeds[i]))
+        out[i] = torch.multinomial(probs, 1, generator=g)
+    return out, logp.gather(1, out.view(-1, 1)).squeeze(1)
