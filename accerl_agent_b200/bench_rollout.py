@@ -1,0 +1,81 @@
+"""Rollout throughput of the native engine: synthetic text-game GRPO groups played against one engine
+(one GPU), the way rollout workers drive it (every request carries the whole growing transcript,
+16-token actions at temperature 1.0, prefix caching on).
+
+    python -m accerl_agent_b200.bench_rollout [--model qwen2.5-1.5b] [--groups 32] [--seconds 30]
+
+Reports generated tokens/s (``Infer/TokensPerSec``), prefix-cache hit rate and engine step counts.
+"""
+
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import time
+
+import torch
+
+from .core.config import make_args
+from .models.config import get_preset
+from .rollout.inference import InferenceService
+from .rollout.worker import RolloutWorker
+
+
+async def _drive(service, args, groups: int, seconds: float):
+    sink_samples = []
+    worker_list = [RolloutWorker(args, service, i, sink_samples.extend, lambda *a: None) for i in range(groups)]
+    tasks = [asyncio.create_task(w.run()) for w in worker_list]
+    await asyncio.sleep(3.0)  # warm-up: prefill of the first observations, kernel caches
+    tok0 = service.total_tokens
+    t0 = time.perf_counter()
+    await asyncio.sleep(seconds)
+    tok1 = service.total_tokens
+    el = time.perf_counter() - t0
+    for w in worker_list:
+        await w.stop()
+    await asyncio.wait(tasks, timeout=60)
+    return (tok1 - tok0) / el, el, len(sink_samples)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="qwen2.5-1.5b")
+    ap.add_argument("--groups", type=int, default=32, help="concurrent GRPO groups (x8 trajectories)")
+    ap.add_argument("--seconds", type=float, default=30.0)
+    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
+    ap.add_argument("--window", type=int, default=8192)
+    ap.add_argument("--json", default=None)
+    a = ap.parse_args()
+    args = make_args(model_path=a.model, env="synthetic", rl_algorithm="grpo", rollout_batch_size=8,
+                     tw_max_episode_steps=50, tw_history_token_window=a.window, max_length=a.window,
+                     infer_max_tokens=16, infer_temperature=1.0, vllm_max_num_seqs=a.max_num_seqs,
+                     vllm_max_num_batched_tokens=a.max_num_batched_tokens, kv_cache_gb=60.0)
+    dev = torch.device("cuda", 0)
+    service = InferenceService(args, dev)
+    service.engine.model.init_weights(seed=0)
+    rate, el, samples = asyncio.run(_drive(service, args, a.groups, a.seconds))
+    st = service.get_stats()
+    out = {
+        "metric": "rollout tok/s",
+        "value": round(rate, 1),
+        "unit": "generated tokens/s (Infer/TokensPerSec), one engine GPU",
+        "model": a.model,
+        "concurrent_trajectories": a.groups * 8,
+        "max_num_seqs": a.max_num_seqs,
+        "seconds": round(el, 2),
+        "samples_produced": samples,
+        "prefix_cache_hit_rate": round(st["prefix_cache_hit_rate"], 4),
+        "engine_steps": st["steps"],
+        "preemptions": st["preemptions"],
+    }
+    print(json.dumps(out))
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump(out, f, indent=1)
+    asyncio.run(service.shutdown())
+
+
+if __name__ == "__main__":
+    main()

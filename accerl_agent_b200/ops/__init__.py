@@ -201,7 +201,8 @@ def rmsnorm_backward(dy, x, w, rstd, dx_accum=None, dw_grad=None, dw_accumulate:
         dx = torch.empty_like(x)
         ws = None
         if dw_grad is not None:
-            ws = workspace(x.device, "rmsnorm_dw", ((x.shape[0] + 63) // 64) * x.shape[1])
+            rows, H = x.shape
+            ws = workspace(x.device, "rmsnorm_dw", max((rows + 63) // 64, 8 * ((min((rows + 3) // 4, 148 * 16) + 7) // 8)) * H)
         native().rmsnorm_bwd(dy, x, w, rstd, dx_accum, dx, dw_grad, ws, dw_accumulate)
         return dx
     dx, dw = reference.rmsnorm_backward(dy, x, w, rstd)

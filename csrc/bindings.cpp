@@ -169,7 +169,9 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   float* ws = nullptr;
   if (dw.has_value()) {
     CHECK_F32(*dw);
-    TORCH_CHECK(workspace.has_value() && workspace->numel() >= ((rows + 63) / 64) * (long long)H,
+    const long long fused_warps = 8LL * ((std::min((rows + 3) / 4, 148 * 16) + 7) / 8);
+    TORCH_CHECK(workspace.has_value() &&
+                    workspace->numel() >= std::max<long long>((rows + 63) / 64, fused_warps) * (long long)H,
                 "rmsnorm_bwd: workspace too small");
     dwp = dw->data_ptr<float>();
     ws = workspace->data_ptr<float>();

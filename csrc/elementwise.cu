@@ -1,6 +1,8 @@
 // Memory-bound fused ops of the decoder layer (sm_100a): RMSNorm fwd/bwd, rotary embedding,
 // SwiGLU fwd/bwd, token embedding gather / scatter-add, bias-gradient column sums.
 // All vector accesses are 16 bytes (8 bf16); the hidden sizes used here are multiples of 8.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace accerl {
@@ -100,6 +102,82 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
   }
 }
 
+// Fused backward: dx as above plus the weight-gradient partial of the rows this warp visits, kept in
+// registers (NC = H / 256 chunks of 8 columns per lane) and written once per warp.
+template <int NC>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                                const __nv_bfloat16* __restrict__ x,
+                                                                const __nv_bfloat16* __restrict__ w,
+                                                                const float* __restrict__ rstd,
+                                                                const __nv_bfloat16* dx_accum, __nv_bfloat16* dx,
+                                                                float* __restrict__ part, int rows, long long ld) {
+  constexpr int H = NC * 256;
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  float wf[NC][8];
+  float acc[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const uint4 g = *reinterpret_cast<const uint4*>(w + c * 256 + lane * 8);
+    const uint32_t gw4[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(gw4[i]);
+      wf[c][2 * i] = f.x;
+      wf[c][2 * i + 1] = f.y;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
+  }
+  for (int row = gw; row < rows; row += nw) {
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const uint4 av = *reinterpret_cast<const uint4*>(dy + row * ld + c * 256 + lane * 8);
+      const uint4 bv = *reinterpret_cast<const uint4*>(x + row * ld + c * 256 + lane * 8);
+      const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 fa = unpack_bf16x2(aw[i]), fb = unpack_bf16x2(bw[i]);
+        dot += fa.x * wf[c][2 * i] * fb.x * r + fa.y * wf[c][2 * i + 1] * fb.y * r;
+        // the module rounds x*rstd to bf16 before scaling by w; the weight gradient uses that value
+        const float2 n = unpack_bf16x2(pack_bf16x2(fb.x * r, fb.y * r));
+        acc[c][2 * i] += fa.x * n.x;
+        acc[c][2 * i + 1] += fa.y * n.y;
+      }
+    }
+    dot = warp_sum(dot) / static_cast<float>(H);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      // second touch of the row hits L1
+      const uint4 av = *reinterpret_cast<const uint4*>(dy + row * ld + c * 256 + lane * 8);
+      const uint4 bv = *reinterpret_cast<const uint4*>(x + row * ld + c * 256 + lane * 8);
+      const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+      uint32_t qw[4] = {0, 0, 0, 0};
+      if (dx_accum) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(dx_accum + row * ld + c * 256 + lane * 8);
+        qw[0] = qv.x; qw[1] = qv.y; qw[2] = qv.z; qw[3] = qv.w;
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 fa = unpack_bf16x2(aw[i]), fb = unpack_bf16x2(bw[i]), q = unpack_bf16x2(qw[i]);
+        const float d0 = r * (fa.x * wf[c][2 * i] - fb.x * r * dot) + q.x;
+        const float d1 = r * (fa.y * wf[c][2 * i + 1] - fb.y * r * dot) + q.y;
+        o[i] = pack_bf16x2(d0, d1);
+      }
+      *reinterpret_cast<uint4*>(dx + row * ld + c * 256 + lane * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  float* dst = part + static_cast<long long>(gw) * H;
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[c * 256 + lane * 8 + i] = acc[c][i];
+}
+
 // Partial column sums for the RMSNorm weight gradient: part[b, h] = sum over this block's rows of
 // dy * x * rstd. Each thread owns 8 consecutive columns.
 __global__ void rmsnorm_dw_partial_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
@@ -169,25 +247,32 @@ __global__ void colsum_partial_kernel(const __nv_bfloat16* __restrict__ dy, floa
 // ------------------------------------------------------------------------------------------------
 __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const long long* __restrict__ pos, int T, int n_rot_heads,
                             int D, long long ld, float log2_theta, float sign) {
+  // one block per token; cos/sin of the D/2 frequencies computed once and shared by all heads
+  extern __shared__ float cs[];  // [D/2] cos, [D/2] sin
+  const int t = blockIdx.x;
   const int half = D >> 1;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(T) * n_rot_heads * half;
-  if (idx >= total) return;
-  const int i = static_cast<int>(idx % half);
-  const long long th = idx / half;
-  const int head = static_cast<int>(th % n_rot_heads);
-  const int t = static_cast<int>(th / n_rot_heads);
-  const float inv_freq = exp2f(-log2_theta * (2.0f * i) / static_cast<float>(D));
-  const float ang = static_cast<float>(pos[t]) * inv_freq;
-  float s, c;
-  sincosf(ang, &s, &c);
-  c = __bfloat162float(__float2bfloat16(c));
-  s = __bfloat162float(__float2bfloat16(s)) * sign;
-  __nv_bfloat16* base = qkv + t * ld + static_cast<long long>(head) * D;
-  const float x1 = __bfloat162float(base[i]);
-  const float x2 = __bfloat162float(base[i + half]);
-  base[i] = __float2bfloat16(x1 * c - x2 * s);
-  base[i + half] = __float2bfloat16(x2 * c + x1 * s);
+  const float p = static_cast<float>(pos[t]);
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float inv_freq = exp2f(-log2_theta * (2.0f * i) / static_cast<float>(D));
+    float s, c;
+    sincosf(p * inv_freq, &s, &c);
+    cs[i] = __bfloat162float(__float2bfloat16(c));
+    cs[half + i] = __bfloat162float(__float2bfloat16(s)) * sign;
+  }
+  __syncthreads();
+  __nv_bfloat16* row = qkv + t * ld;
+  const int pairs = half >> 1;  // bf16x2 pairs per half
+  for (int idx = threadIdx.x; idx < n_rot_heads * pairs; idx += blockDim.x) {
+    const int h = idx / pairs;
+    const int i = (idx % pairs) * 2;
+    __nv_bfloat162* a = reinterpret_cast<__nv_bfloat162*>(row + h * D + i);
+    __nv_bfloat162* b = reinterpret_cast<__nv_bfloat162*>(row + h * D + i + half);
+    const float2 x1 = __bfloat1622float2(*a);
+    const float2 x2 = __bfloat1622float2(*b);
+    const float c0 = cs[i], c1 = cs[i + 1], s0 = cs[half + i], s1 = cs[half + i + 1];
+    *a = __floats2bfloat162_rn(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+    *b = __floats2bfloat162_rn(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -293,6 +378,27 @@ extern "C" int accerl_rmsnorm_bwd(const void* dy, const void* x, const void* w, 
                                   void* dx, float* dw, float* workspace, int rows, int H, long long ld, int dw_accumulate,
                                   cudaStream_t s) {
   if (H % 8) return -1;
+  if (dw && H % 256 == 0 && H <= 2048 && rows > 0) {
+    // fused single pass: 8 warps per block, grid sized so every warp visits several rows
+    const int nwarps_total = std::min((rows + 3) / 4, 148 * 16);
+    const int blocks = (nwarps_total + 7) / 8;
+    const int nw = blocks * 8;
+#define RMS_BWD_CASE(NCV)                                                                                        \
+  case NCV:                                                                                                      \
+    rmsnorm_bwd_fused_kernel<NCV><<<blocks, 256, 0, s>>>(                                                        \
+        (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rstd,                        \
+        (const __nv_bfloat16*)dx_accum, (__nv_bfloat16*)dx, workspace, rows, ld);                                \
+    break;
+    switch (H / 256) {
+      RMS_BWD_CASE(1) RMS_BWD_CASE(2) RMS_BWD_CASE(4) RMS_BWD_CASE(6) RMS_BWD_CASE(8)
+      default:
+        goto generic;
+    }
+#undef RMS_BWD_CASE
+    column_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(workspace, dw, nw, H, dw_accumulate);
+    return (int)cudaGetLastError();
+  }
+generic:
   const int warps = 8;
   rmsnorm_bwd_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, s>>>(
       (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rstd, (const __nv_bfloat16*)dx_accum,
@@ -321,10 +427,10 @@ extern "C" int accerl_bias_grad(const void* dy, float* db, float* workspace, int
 
 extern "C" int accerl_rope(void* qkv, const long long* pos, int T, int n_rot_heads, int D, long long ld, float theta,
                            int inverse, cudaStream_t s) {
-  const long long total = (long long)T * n_rot_heads * (D / 2);
-  if (total == 0) return 0;
-  rope_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>((__nv_bfloat16*)qkv, pos, T, n_rot_heads, D, ld,
-                                                               log2f(theta), inverse ? -1.f : 1.f);
+  if (T == 0) return 0;
+  if (D % 4) return -1;
+  rope_kernel<<<T, 256, D * sizeof(float), s>>>((__nv_bfloat16*)qkv, pos, T, n_rot_heads, D, ld, log2f(theta),
+                                                inverse ? -1.f : 1.f);
   return (int)cudaGetLastError();
 }
 
