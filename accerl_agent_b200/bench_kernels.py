@@ -121,6 +121,30 @@ def bench_memory_bound(results):
     results["adamw_375M"] = {"ms": t, "gbs": b / t / 1e6, "frac_hbm": b / t / 1e6 / hbm}
 
 
+def profile_case(kind: str):
+    """One small launch of a kernel family (for ncu captures): attention fwd+bwd on 1 x 4096 tokens,
+    12 q / 2 kv heads; or the layer GEMMs of 4096 tokens of the 1.5B shape."""
+    if kind == "attnprof":
+        Hq, Hkv, D, T = 12, 2, 128, 4096
+        cu = torch.tensor([0, T], dtype=torch.int32, device="cuda")
+        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+        q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D : (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D :]
+        for _ in range(2):
+            o, lse = ops.attention_varlen(q, k, v, cu, T, Hq, Hkv, D)
+            ops.attention_varlen_backward(torch.randn_like(o), q, k, v, o, lse, cu, T, Hq, Hkv, D)
+    elif kind == "gemmprof":
+        T, H, I = 4096, 1536, 8960
+        x = torch.randn(T, H, device="cuda").bfloat16()
+        w = torch.randn(2 * I, H, device="cuda").bfloat16()
+        gw = torch.zeros(2 * I, H, device="cuda")
+        for _ in range(2):
+            y = ops.gemm(x, w)
+            ops.linear_dgrad(y, w)
+            ops.linear_wgrad(y, x, gw)
+    torch.cuda.synchronize()
+    ops.check_status(torch.device("cuda"))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -129,6 +153,11 @@ def main():
     peak_tf, _ = _peaks()
     results = {"peak_bf16_tflops_measured": peak_tf}
     sel = set(args.only.split(","))
+    if sel & {"attnprof", "gemmprof"}:
+        for kind in sel & {"attnprof", "gemmprof"}:
+            profile_case(kind)
+        print("profile case done")
+        return
     if "gemm" in sel:
         bench_gemm(results)
     if "attn" in sel:

@@ -1,0 +1,132 @@
+"""Distributed behaviour on CPU ranks (gloo): the local SFT smoke run with world size 2, sharded
+optimizer steps that equal the single-rank step on the union of the packs (global valid-token
+normalisation), and the all-reduce(MIN) failure propagation of varlen window preparation."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from accerl_agent_b200.algo.objectives import ObjectiveConfig
+from accerl_agent_b200.algo.packing import make_varlen_batch
+from accerl_agent_b200.core.sample import RLSample
+from accerl_agent_b200.models.config import get_preset
+from accerl_agent_b200.models.transformer import build_model
+from accerl_agent_b200.parallel.fsdp import ShardedAdamW
+from accerl_agent_b200 import ops
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _pack(seed):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for L in (20, 13):
+        ids = torch.randint(0, 4096, (L,), generator=g).tolist()
+        labels = [-100] * (L - 5) + ids[L - 5:]
+        out.append(RLSample("grpo", ids, [1] * L, labels, [-8.0] * L, 0.7 if seed % 2 else -0.4, [0.0] * L,
+                            [-1] * (L - 5) + [0] * 5, [0]))
+    return make_varlen_batch(out)
+
+
+def _step(model, opt, packs, global_tokens):
+    cfg = ObjectiveConfig()
+    for b in packs:
+        lp, ctx = model.forward_logprobs(b, 20)
+        tgt = b["target_indices"]
+        adv = b["sample_advantages"][b["sequence_ids"][tgt]]
+        dlp, _ = ops.policy_loss(lp, b["old_logprobs"][tgt], adv, cfg, loss_scale=1.0 / global_tokens)
+        model.backward_from_logprobs(dlp, ctx)
+    opt.step(1e-3)
+
+
+def _sharded_worker(rank, port, out):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    cfg = get_preset("tiny-qwen2")
+    model = build_model(cfg, "full", torch.device("cpu"), torch.float32, pad_to=2)
+    model.init_weights(seed=1)
+    opt = ShardedAdamW(model, lr=1e-3)
+    packs = [_pack(10 + rank)]
+    total = sum(int(p["target_indices"].numel()) for p in (_pack(10), _pack(11)))
+    _step(model, opt, packs, total)
+    if rank == 0:
+        out.put(model.params.clone())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_step_equals_single_rank_step():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    sharded = q.get(timeout=120)
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    cfg = get_preset("tiny-qwen2")
+    model = build_model(cfg, "full", torch.device("cpu"), torch.float32, pad_to=2)
+    model.init_weights(seed=1)
+    opt = ShardedAdamW(model, lr=1e-3)
+    packs = [_pack(10), _pack(11)]
+    total = sum(int(p["target_indices"].numel()) for p in packs)
+    _step(model, opt, packs, total)
+    assert torch.allclose(sharded, model.params, atol=1e-6, rtol=1e-5)
+
+
+def test_local_trainer_fsdp_world2_cpu():
+    from accerl_agent_b200.local_trainer import main
+
+    res = main(["--model-path", "tiny-qwen2", "--device", "cpu", "--use-fsdp", "--fsdp-world-size", "2",
+                "--batch-size", "1", "--max-length", "128", "--response-length", "32", "--learning-rate", "1e-5",
+                "--max-steps", "5", "--grad-accum-steps", "1", "--train-mode", "full", "--dataset", "random",
+                "--dtype", "float32"])
+    assert sorted(res) == [0, 1]
+    for r in res.values():
+        assert r["steps"] == 5 and torch.isfinite(torch.tensor(r["last_loss"]))
+
+
+def _fail_worker(rank, port, out):
+    from accerl_agent_b200.core.config import make_args
+    from accerl_agent_b200.replay import ReplayBuffer
+    from accerl_agent_b200.trainer.worker import TrainWorker
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    args = make_args(model_path="tiny-qwen2", train_packing="varlen", train_token_budget=64, max_length=64,
+                     tw_history_token_window=64, batch_size=1, grad_accum_steps=1, device="cpu",
+                     min_replay_size_per_rank=1, replay_sample_timeout_seconds=0.5, replay_wait_sleep_seconds=0.05)
+    rb = ReplayBuffer(8)
+    if rank == 0:  # rank 1 never receives samples and times out preparing its window
+        rb.add_samples([RLSample("grpo", list(range(10)), [1] * 10, [-100] * 5 + list(range(5, 10)), [-1.0] * 10,
+                                 1.0, [0.0] * 10, [-1] * 5 + [0] * 5, [0])])
+    w = TrainWorker(args, rank=rank, fsdp_world_size=2, replay_buffer=rb, device=torch.device("cpu"))
+    try:
+        w.train_until_next_sync(1)
+        out.put((rank, "ok"))
+    except Exception as exc:
+        out.put((rank, type(exc).__name__ + ": " + str(exc)[:80]))
+    dist.destroy_process_group()
+
+
+def test_window_preparation_failure_fails_every_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_fail_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(60)
+    assert all("At least one FSDP rank failed" in v for v in res.values()), res
