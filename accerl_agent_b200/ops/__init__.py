@@ -82,6 +82,7 @@ __all__ = [
 ]
 
 _WORKSPACE: Dict[Tuple[int, str], torch.Tensor] = {}
+_RETIRED: list = []  # outgrown workspaces stay alive: captured CUDA graphs may still point at them
 
 
 def workspace(device: torch.device, name: str, numel: int, dtype=torch.float32) -> torch.Tensor:
@@ -89,6 +90,8 @@ def workspace(device: torch.device, name: str, numel: int, dtype=torch.float32) 
     key = (device.index if device.index is not None else -1, name)
     buf = _WORKSPACE.get(key)
     if buf is None or buf.numel() < numel or buf.dtype != dtype:
+        if buf is not None:
+            _RETIRED.append(buf)
         buf = torch.empty(max(numel, 1), dtype=dtype, device=device)
         _WORKSPACE[key] = buf
     return buf[:numel]

@@ -100,6 +100,7 @@ class GenerationEngine:
         params: Optional[torch.Tensor] = None,
         seed: int = 0,
         decode_splits: Optional[int] = None,
+        use_cuda_graphs: bool = True,
     ):
         self.cfg = cfg
         self.device = device
@@ -127,6 +128,11 @@ class GenerationEngine:
         self.k_cache = torch.zeros(L, num_blocks, block_size, Hkv, D, dtype=dtype, device=device)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.allocator = BlockAllocator(num_blocks, block_size, enable_prefix_caching)
+        # block 0 is never handed to a sequence: padded rows of captured decode graphs point at it
+        self.scratch_block = self.allocator.allocate()
+        self.use_cuda_graphs = use_cuda_graphs and device.type == "cuda" and not cfg.is_moe
+        self._graphs: Dict[Any, Any] = {}
+        self._graph_pool = None
         self.waiting: Deque[_Seq] = deque()
         self.running: List[_Seq] = []
         self.by_id: Dict[str, _Seq] = {}
@@ -370,15 +376,131 @@ class GenerationEngine:
             plan = self._schedule()
             if not plan:
                 return False
-            # multi-token chunks use the varlen kernel over their cached prefix; single tokens (decode
-            # steps, or a one-token tail of a prompt chunk) use the paged decode kernel
+            # prefill-first: multi-token chunks run in their own (eager) step with the varlen kernel over
+            # their cached prefix; steps where every scheduled sequence advances by one token run the
+            # paged decode path, replayed from a captured CUDA graph when possible
             prefill = [p for p in plan if p[2] > 1]
             decode = [p for p in plan if p[2] == 1]
-            order = prefill + decode
-            toks, logps = self._execute(order, len(prefill))
+            if prefill:
+                order = prefill
+                toks, logps = self._execute(order, len(prefill))
+            else:
+                order = decode
+                if self.use_cuda_graphs and all(p[3] for p in decode):
+                    toks, logps = self._execute_decode_graph(order)
+                else:
+                    toks, logps = self._execute(order, 0)
             self._postprocess(order, toks, logps)
             self.stats["steps"] += 1
             return True
+
+    # ------------------------------------------------------------------ CUDA-graph decode
+    _BUCKETS = (8, 16, 32, 64, 128, 256, 512)
+
+    def _decode_core(self, ids_d, pos_d, slots_d, table_d, lens_d, temps_d, seeds_d, offs_d, splits: int):
+        """Forward of single-token rows (every row samples): returns (tokens, logprobs) on device."""
+        cfg, m, dev = self.cfg, self.model, self.device
+        D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        scale = 1.0 / math.sqrt(D)
+        x = ops.embedding(ids_d, m.w("model.embed_tokens.weight"))
+        for layer in range(cfg.num_hidden_layers):
+            p = f"model.layers.{layer}."
+            h1, _ = ops.rmsnorm(x, m.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
+            bias = m.w(p + "self_attn.qkv_proj.bias") if cfg.qkv_bias else None
+            qkv = ops.linear(h1, m.w(p + "self_attn.qkv_proj.weight"), bias=bias)
+            if cfg.qk_norm:
+                m._qk_norm_forward(layer, qkv)
+            ops.rope_(qkv, pos_d, Hq + Hkv, D, cfg.rope_theta)
+            q = qkv[:, : cfg.q_dim]
+            k = qkv[:, cfg.q_dim : cfg.q_dim + cfg.kv_dim]
+            v = qkv[:, cfg.q_dim + cfg.kv_dim :]
+            kc, vc = self.k_cache[layer], self.v_cache[layer]
+            ops.kv_cache_write(k, v, kc, vc, slots_d, Hkv)
+            attn = ops.paged_decode(q, kc, vc, table_d, lens_d, Hq, Hkv, scale, num_splits=splits)
+            x = ops.linear(attn, m.w(p + "self_attn.o_proj.weight"), residual=x)
+            h2, _ = ops.rmsnorm(x, m.w(p + "post_attention_layernorm.weight"), cfg.rms_norm_eps)
+            gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
+            x = ops.linear(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), residual=x)
+        hN, _ = ops.rmsnorm(x, m.w("model.norm.weight"), cfg.rms_norm_eps)
+        logits = ops.linear(hN, m.w(m.lm_head_name))
+        return ops.sample(logits, temps_d, seeds_d, offs_d)
+
+    def _graph_for(self, bucket: int, width: int):
+        key = (bucket, width)
+        g = self._graphs.get(key)
+        if g is not None:
+            return g
+        dev = self.device
+        meta = torch.zeros(bucket * (5 + width), dtype=torch.int64, device=dev)
+        temps = torch.zeros(bucket, dtype=torch.float32, device=dev)
+
+        def views():
+            ids = meta[:bucket]
+            pos = meta[bucket : 2 * bucket]
+            slots = meta[2 * bucket : 3 * bucket].to(torch.int32)
+            lens = meta[3 * bucket : 4 * bucket].to(torch.int32)
+            seeds = meta[4 * bucket : 5 * bucket]
+            table = meta[5 * bucket :].view(bucket, width).to(torch.int32)
+            return ids, pos, slots, table, lens, seeds
+
+        # a valid dummy batch: every row reads one token of the scratch block and writes nothing
+        meta[2 * bucket : 3 * bucket] = -1
+        meta[3 * bucket : 4 * bucket] = 1
+        meta[5 * bucket :] = self.scratch_block
+        splits = self.decode_splits or max(1, min(16, (148 * 2) // max(bucket * self.cfg.num_key_value_heads, 1)))
+        offs = torch.zeros(bucket, dtype=torch.int64, device=dev)
+
+        def run():
+            ids, pos, slots, table, lens, seeds = views()
+            return self._decode_core(ids, pos, slots, table, lens, temps, seeds, offs, splits)
+
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                run()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, pool=self._graph_pool):
+            out_tok, out_lp = run()
+        g = {"graph": graph, "meta": meta, "temps": temps, "offs": offs, "tok": out_tok, "lp": out_lp}
+        self._graphs[key] = g
+        return g
+
+    def _execute_decode_graph(self, order):
+        bs = self.block_size
+        B = len(order)
+        bucket = next((b for b in self._BUCKETS if b >= B), None)
+        if bucket is None:
+            return self._execute(order, 0)
+        width = max(len(s.blocks) for s, *_ in order)
+        width = (width + 63) // 64 * 64
+        g = self._graph_for(bucket, width)
+        host = np.zeros(bucket * (5 + width), dtype=np.int64)
+        host[2 * bucket : 3 * bucket] = -1
+        host[3 * bucket : 4 * bucket] = 1
+        table = host[5 * bucket :].reshape(bucket, width)
+        table[:] = self.scratch_block
+        temps = np.zeros(bucket, dtype=np.float32)
+        offs = np.zeros(bucket, dtype=np.int64)
+        for j, (seq, start, n, _) in enumerate(order):
+            blk = seq.blocks
+            host[j] = seq.tokens[start]
+            host[bucket + j] = start
+            host[2 * bucket + j] = blk[start // bs] * bs + start % bs
+            host[3 * bucket + j] = start + 1
+            host[4 * bucket + j] = seq.seed
+            table[j, : len(blk)] = blk
+            temps[j] = float(seq.params.temperature)
+            offs[j] = len(seq.out)
+        g["meta"].copy_(torch.from_numpy(host), non_blocking=False)
+        g["temps"].copy_(torch.from_numpy(temps))
+        g["offs"].copy_(torch.from_numpy(offs))
+        g["graph"].replay()
+        res = torch.stack([g["tok"][:B].double(), g["lp"][:B].double()]).cpu()
+        return res[0].long().tolist(), res[1].tolist()
 
     def _execute(self, order, n_prefill: int):
         cfg = self.cfg

@@ -189,13 +189,15 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       float x[128];
+      {
+        uint32_t v[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS + bsel * 128 + c * 32 + lane_off, v);
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + bsel * 128 + c * 32 + lane_off, v[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[e]) * p.scale_log2;
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[c][e]) * p.scale_log2;
       }
       tc_fence_before();
       mbar_arrive(&s_free[bsel]);
@@ -424,19 +426,27 @@ __global__ void __launch_bounds__(192, 1)
     const bool key_valid = k_pos < len;
     const int ldacc = p.Hq * kHd;
     bool ok = true;
-    for (int i = 0; i < nq; ++i) {
-      const int qt = q_first + i;
+    // lse / delta of the query tile, loaded one iteration ahead so the load latency hides behind MMAs
+    auto load_stats = [&](int qt, float& l2, float& dl) {
       const int q_pos_t = qt * kTile + r;
-      named_bar_sync(1, 128);
       if (q_pos_t < len) {
         const long long idx = static_cast<long long>(head) * p.T + seq_start + q_pos_t;
-        s_lse[r] = p.lse[idx] * kLog2e;
-        s_delta[r] = p.delta[idx];
+        l2 = p.lse[idx] * kLog2e;
+        dl = p.delta[idx];
       } else {
-        s_lse[r] = INFINITY;
-        s_delta[r] = 0.f;
+        l2 = INFINITY;
+        dl = 0.f;
       }
+    };
+    float nxt_lse, nxt_delta;
+    load_stats(q_first, nxt_lse, nxt_delta);
+    for (int i = 0; i < nq; ++i) {
+      const int qt = q_first + i;
       named_bar_sync(1, 128);
+      s_lse[r] = nxt_lse;
+      s_delta[r] = nxt_delta;
+      named_bar_sync(1, 128);
+      if (i + 1 < nq) load_stats(qt + 1, nxt_lse, nxt_delta);
       if (!mbar_wait(s_full, i & 1, p.status, kStatusTimeoutEpilogue)) {
         ok = false;
         break;
@@ -447,7 +457,7 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c * 32 + lane_off, sv);
         tmem_ld32(tDP + c * 32 + lane_off, dv);
-        tmem_wait_ld();
+        tmem_wait_ld();  // both loads in flight together
         uint32_t pw[16], dw[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
@@ -482,16 +492,22 @@ __global__ void __launch_bounds__(192, 1)
       const int q_pos = qt * kTile + r;
       float* dqrow = p.dq_acc + static_cast<long long>(seq_start + q_pos) * ldacc + head * kHd;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
+      for (int c = 0; c < 4; c += 2) {
+        uint32_t v[32], v2[32];
         tmem_ld32(tS + c * 32 + lane_off, v);
+        tmem_ld32(tS + (c + 1) * 32 + lane_off, v2);
         tmem_wait_ld();
         if (q_pos < len) {
 #pragma unroll
+          for (int g = 0; g < 8; ++g)
+            red_add_v4(dqrow + (c + 1) * 32 + g * 4, __uint_as_float(v2[g * 4]), __uint_as_float(v2[g * 4 + 1]),
+                       __uint_as_float(v2[g * 4 + 2]), __uint_as_float(v2[g * 4 + 3]));
+        }
+        if (q_pos < len) {
+#pragma unroll
           for (int g = 0; g < 8; ++g) {
-            float4 val = make_float4(__uint_as_float(v[g * 4]), __uint_as_float(v[g * 4 + 1]),
-                                     __uint_as_float(v[g * 4 + 2]), __uint_as_float(v[g * 4 + 3]));
-            atomicAdd(reinterpret_cast<float4*>(dqrow + c * 32 + g * 4), val);
+            red_add_v4(dqrow + c * 32 + g * 4, __uint_as_float(v[g * 4]), __uint_as_float(v[g * 4 + 1]),
+                       __uint_as_float(v[g * 4 + 2]), __uint_as_float(v[g * 4 + 3]));
           }
         }
       }

@@ -222,6 +222,13 @@ ACCERL_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
 ACCERL_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 ACCERL_DEVINL void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Fire-and-forget vector reduction into global fp32 memory (no return value, so the issuing warp does
+// not wait for the round trip the way a value-returning atomic does).
+ACCERL_DEVINL void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma operand reads).
 ACCERL_DEVINL void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

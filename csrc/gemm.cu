@@ -248,8 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.splits > 1) {
             // split-K partial: add into the fp32 output (pre-initialised by the caller)
             float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
-            atomicAdd(reinterpret_cast<float4*>(c), make_float4(f[0], f[1], f[2], f[3]));
-            atomicAdd(reinterpret_cast<float4*>(c + 4), make_float4(f[4], f[5], f[6], f[7]));
+            red_add_v4(c, f[0], f[1], f[2], f[3]);
+            red_add_v4(c + 4, f[4], f[5], f[6], f[7]);
           } else if (p.c_f32) {
             float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
             if (p.beta != 0.f) {
@@ -410,11 +410,42 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15) return -3;
   if (residual && ((ldr % 8) != 0 || (reinterpret_cast<uintptr_t>(residual) & 15))) return -4;
   if (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) return -5;
+  // Tile width and split-K are chosen to minimise wave quantisation: estimated time ~
+  // ceil(work_items / SMs) * (k_blocks / splits) * tile_cost, with a 256-wide tile costing ~2x a
+  // 128-wide one. Split-K is only possible for fp32 outputs accumulated with beta = 1.
+  const int sms = num_sms();
+  const int k_blocks_all = (K + kBK - 1) / kBK;
+  const bool can_split = c_f32 && beta == 1.f && !bias && !residual;
   int bn = block_n;
-  if (bn != 128 && bn != 256) {
-    const long long tiles256 = (long long)((M + 127) / 128) * ((N + 255) / 256);
-    bn = (N <= 128 || tiles256 < num_sms()) ? 128 : 256;
+  int best_split = 1;
+  {
+    double best = 1e30;
+    const int bn_opts[2] = {256, 128};
+    for (int oi = 0; oi < 2; ++oi) {
+      const int cand = bn_opts[oi];
+      if (block_n == 128 || block_n == 256) {
+        if (cand != block_n) continue;
+      } else if (cand == 256 && N <= 128) {
+        continue;
+      }
+      const long long tiles = (long long)((M + 127) / 128) * ((N + cand - 1) / cand);
+      // splitting only pays while the tile grid leaves SMs idle (partials cost extra fp32 traffic)
+      const int max_split = (splits > 0) ? splits : ((can_split && tiles < sms) ? 8 : 1);
+      for (int sp = (splits > 0 ? splits : 1); sp <= max_split; ++sp) {
+        if (sp > 1 && k_blocks_all / sp < 4) break;
+        const long long items = tiles * sp;
+        const double waves = (double)((items + sms - 1) / sms);
+        const double t = waves * ((double)((k_blocks_all + sp - 1) / sp)) * (cand == 256 ? 2.0 : 1.0) *
+                         (cand == 256 ? 1.0 : 1.08);  // 128-wide tiles re-read A twice as often
+        if (t < best * 0.97) {
+          best = t;
+          bn = cand;
+          best_split = sp;
+        }
+      }
+    }
   }
+  if (splits <= 0) splits = best_split;
   CUtensorMap ma, mb;
   bool ok;
   if (a_mn) ok = make_map_2d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64);
@@ -438,15 +469,7 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   p.status = status;
   p.tiles_m = (M + kBM - 1) / kBM;
   p.tiles_n = (N + bn - 1) / bn;
-  const int k_blocks = (K + kBK - 1) / kBK;
-  if (splits <= 0) {
-    // automatic: split K when the tile grid would leave most SMs idle and K is long
-    const int tiles = p.tiles_m * p.tiles_n;
-    splits = 1;
-    if (c_f32 && beta == 1.f && !bias && !residual) {
-      while (tiles * splits * 2 <= num_sms() && k_blocks / (splits * 2) >= 4) splits *= 2;
-    }
-  }
+  const int k_blocks = k_blocks_all;
   if (splits > 1 && (!c_f32 || bias || residual || beta != 1.f)) return -9;
   p.kb_per_split = (k_blocks + splits - 1) / splits;
   p.splits = (k_blocks + p.kb_per_split - 1) / p.kb_per_split;
