@@ -19,10 +19,18 @@ Micro-batches therefore run with no parameter traffic at all. The loss is scaled
 
 On a single rank the shard is the whole trainable segment and no collective is issued. CPU ranks use
 gloo (reduce-scatter is emulated with an all-reduce there).
+
+With NCCL ranks on one node (``fused_collectives``, the default when every GPU pair has peer access)
+steps 2-5 run as two kernels over NVLink peer memory instead (``csrc/collectives.cu``): a
+reduce-scatter that reads the shard range of every peer's fp32 gradient buffer and accumulates the
+squared norm in the same pass, then clip + AdamW whose epilogue stores the new bf16 shard into every
+peer's parameter buffer (the all-gather). Only the 8-byte norm all-reduce and a 4-byte barrier stay
+on NCCL.
 """
 
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -63,6 +71,15 @@ class ShardedAdamW:
             self.grad_shard = torch.zeros(self.shard_numel, dtype=torch.float32, device=model.params.device)
         self._sumsq = torch.zeros(1, dtype=torch.float64, device=model.params.device)
         self.backend = dist.get_backend(group) if dist_ready() else "none"
+        self.fused = False
+        if self.world > 1 and self.backend == "nccl" and os.environ.get("ACCERL_FUSED_COLLECTIVES", "1") != "0":
+            from .symmetric import PeerBuffers, peer_access_available
+
+            if peer_access_available(group):
+                self._grad_peers = PeerBuffers(model.grads, group)
+                self._param_peers = PeerBuffers(model.params, group)
+                self._barrier_flag = torch.zeros(1, dtype=torch.int32, device=model.params.device)
+                self.fused = True
 
     def refresh_master_from_params(self) -> None:
         """Re-seed fp32 master weights after parameters were overwritten (e.g. checkpoint load)."""
@@ -92,6 +109,8 @@ class ShardedAdamW:
         sum of squared gradients (a device tensor; no host sync)."""
         if lr is not None:
             self.lr = lr
+        if self.fused:
+            return self._fused_step()
         self.reduce_gradients()
         sumsq = self.global_grad_sumsq()
         self.step_count += 1
@@ -100,6 +119,26 @@ class ShardedAdamW:
                        self.step_count)
         self.all_gather_params()
         return sumsq
+
+    def _fused_step(self) -> torch.Tensor:
+        import math
+
+        native = ops.native()
+        self._sumsq.zero_()
+        # every peer has finished accumulating its gradients before anyone reads them
+        dist.all_reduce(self._barrier_flag, group=self.group)
+        native.rs_sumsq(self._grad_peers.ptrs, self.rank, self.shard_numel, self.grad_shard, self._sumsq)
+        # the norm all-reduce also guarantees every peer has finished reading this rank's gradients
+        dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
+        self.model.grads.zero_()
+        self.step_count += 1
+        b1, b2 = self.betas
+        native.adamw_push(self.master, self.exp_avg, self.exp_avg_sq, self.grad_shard, self._param_peers.ptrs,
+                          self.rank, self._sumsq, self.lr, b1, b2, self.eps, self.weight_decay, self.max_grad_norm,
+                          1.0 - b1 ** self.step_count, math.sqrt(1.0 - b2 ** self.step_count))
+        # every peer's parameter pushes into this rank's buffer land before the next forward
+        dist.all_reduce(self._barrier_flag, group=self.group)
+        return self._sumsq
 
     def all_gather_params(self) -> None:
         if self.world == 1:

@@ -381,15 +381,15 @@ class GenerationEngine:
             # paged decode path, replayed from a captured CUDA graph when possible
             prefill = [p for p in plan if p[2] > 1]
             decode = [p for p in plan if p[2] == 1]
-            if prefill:
-                order = prefill
-                toks, logps = self._execute(order, len(prefill))
+            if self.use_cuda_graphs and decode and all(p[3] for p in decode):
+                # two passes per step: prefill chunks eagerly, then all decode rows from one graph replay
+                toks, logps = self._execute(prefill, len(prefill)) if prefill else ([], [])
+                dt, dl = self._execute_decode_graph(decode)
+                order = prefill + decode
+                toks, logps = toks + dt, logps + dl
             else:
-                order = decode
-                if self.use_cuda_graphs and all(p[3] for p in decode):
-                    toks, logps = self._execute_decode_graph(order)
-                else:
-                    toks, logps = self._execute(order, 0)
+                order = prefill + decode
+                toks, logps = self._execute(order, len(prefill))
             self._postprocess(order, toks, logps)
             self.stats["steps"] += 1
             return True

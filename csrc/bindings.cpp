@@ -49,6 +49,12 @@ int accerl_paged_decode(const void* q, const void* k_cache, const void* v_cache,
                         const int* seq_lens, void* out, float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv,
                         int max_blocks_per_seq, int block_size, int num_splits, float scale, long long ldq,
                         long long ldo, cudaStream_t s);
+int accerl_enable_peer_access(int peer);
+int accerl_rs_sumsq(const float* const* peers, int world, int rank, long long shard, float* out, double* sumsq,
+                    cudaStream_t s);
+int accerl_adamw_push(float* master, float* m, float* v, const float* grad, void* const* peer_params, int world,
+                      int rank, long long shard, const double* sumsq, float lr, float beta1, float beta2, float eps,
+                      float weight_decay, float max_norm, float bc1, float bc2_sqrt, cudaStream_t s);
 int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping, int T,
                           int Hkv, long long ldk, long long ldv, cudaStream_t s);
 int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
@@ -330,6 +336,28 @@ void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cach
         "kv_cache_write");
 }
 
+void enable_peer_access(int64_t peer) { check(accerl_enable_peer_access(static_cast<int>(peer)), "enable_peer_access"); }
+
+// peer_ptrs: int64 device tensor [world] of base addresses (fp32 full gradient buffers)
+void rs_sumsq(const at::Tensor& peer_ptrs, int64_t rank, int64_t shard, at::Tensor& out, at::Tensor& sumsq) {
+  CHECK_F32(out);
+  TORCH_CHECK(peer_ptrs.scalar_type() == at::kLong && peer_ptrs.is_cuda(), "peer_ptrs: int64 cuda tensor");
+  check(accerl_rs_sumsq(reinterpret_cast<const float* const*>(peer_ptrs.data_ptr<int64_t>()), peer_ptrs.numel(),
+                        rank, shard, out.data_ptr<float>(), sumsq.data_ptr<double>(), cur_stream()),
+        "rs_sumsq");
+}
+
+void adamw_push(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tensor& grad, const at::Tensor& peer_ptrs,
+                int64_t rank, const at::Tensor& sumsq_t, double lr, double beta1, double beta2, double eps,
+                double weight_decay, double max_norm, double bc1, double bc2_sqrt) {
+  CHECK_F32(master);
+  check(accerl_adamw_push(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(),
+                          reinterpret_cast<void* const*>(peer_ptrs.data_ptr<int64_t>()), peer_ptrs.numel(), rank,
+                          master.numel(), sumsq_t.data_ptr<double>(), lr, beta1, beta2, eps, weight_decay, max_norm,
+                          bc1, bc2_sqrt, cur_stream()),
+        "adamw_push");
+}
+
 void sample_logits(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& seeds,
                    const at::Tensor& offsets, at::Tensor& out_tokens, at::Tensor& out_logprobs, at::Tensor& part,
                    int64_t num_chunks) {
@@ -368,4 +396,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode", &paged_decode);
   m.def("kv_cache_write", &kv_cache_write);
   m.def("sample_logits", &sample_logits);
+  m.def("enable_peer_access", &enable_peer_access);
+  m.def("rs_sumsq", &rs_sumsq);
+  m.def("adamw_push", &adamw_push);
 }

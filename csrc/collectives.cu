@@ -1,0 +1,143 @@
+// Optimizer-step collectives over NVLink peer memory, fused with their compute (sm_100a).
+//
+//  rs_sumsq     reduce-scatter fused with the global-norm partial: rank r reads its shard range
+//               [r*S, (r+1)*S) of every peer's full fp32 gradient buffer with vectorised P2P loads,
+//               writes the fp32 sum to its gradient shard and accumulates sum(g^2) into one double.
+//  adamw_push   clip (by the all-reduced norm) + AdamW on the fp32 shard, then the all-gather half:
+//               the updated bf16 parameter shard is stored into the same range of every peer's full
+//               bf16 parameter buffer (P2P stores), so no separate all-gather runs.
+// Peer buffers are mapped once (CUDA IPC) and passed as device arrays of base pointers. Plain loads
+// and stores only: no TMA, no multicast.
+#include "common.cuh"
+
+namespace accerl {
+
+__global__ void rs_sumsq_kernel(const float* const* __restrict__ peers, int world, int rank, long long shard,
+                                float* __restrict__ out, double* __restrict__ sumsq) {
+  const long long base = static_cast<long long>(rank) * shard;
+  const long long n4 = shard / 4;
+  float acc2 = 0.f;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < world; ++r) {
+      const int peer = (rank + r) % world;  // stagger the start so ranks hit different peers first
+      const float4 v = reinterpret_cast<const float4*>(peers[peer] + base)[i];
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    reinterpret_cast<float4*>(out)[i] = s;
+    acc2 += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+  }
+  for (long long i = n4 * 4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < shard;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < world; ++r) s += peers[r][base + i];
+    out[i] = s;
+    acc2 += s * s;
+  }
+  acc2 = warp_sum(acc2);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc2;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) atomicAdd(sumsq, static_cast<double>(v));
+  }
+}
+
+struct PushCfg {
+  float lr, beta1, beta2, eps, weight_decay, max_norm, bc1, bc2_sqrt;
+};
+
+__global__ void adamw_push_kernel(float* __restrict__ master, float* __restrict__ m, float* __restrict__ v,
+                                  const float* __restrict__ grad, __nv_bfloat16* const* __restrict__ peer_params,
+                                  int world, int rank, long long shard, const double* __restrict__ sumsq, PushCfg c) {
+  float coef = 1.f;
+  if (c.max_norm > 0.f) coef = fminf(1.f, c.max_norm / (static_cast<float>(sqrt(*sumsq)) + 1e-6f));
+  const float step = c.lr / c.bc1;
+  const long long base = static_cast<long long>(rank) * shard;
+  const long long n2 = shard / 2;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n2;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float out[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const long long j = 2 * i + h;
+      const float g = grad[j] * coef;
+      float p = master[j];
+      p -= c.lr * c.weight_decay * p;
+      const float mi = c.beta1 * m[j] + (1.f - c.beta1) * g;
+      const float vi = c.beta2 * v[j] + (1.f - c.beta2) * g * g;
+      m[j] = mi;
+      v[j] = vi;
+      p -= step * mi / (sqrtf(vi) / c.bc2_sqrt + c.eps);
+      master[j] = p;
+      out[h] = p;
+    }
+    const __nv_bfloat162 b = __floats2bfloat162_rn(out[0], out[1]);
+    for (int r = 0; r < world; ++r) {
+      const int peer = (rank + r) % world;
+      reinterpret_cast<__nv_bfloat162*>(peer_params[peer] + base)[i] = b;
+    }
+  }
+  if ((shard & 1) && blockIdx.x == 0 && threadIdx.x == 0) {
+    const long long j = shard - 1;
+    const float g = grad[j] * coef;
+    float p = master[j] * (1.f - c.lr * c.weight_decay);
+    const float mi = c.beta1 * m[j] + (1.f - c.beta1) * g;
+    const float vi = c.beta2 * v[j] + (1.f - c.beta2) * g * g;
+    m[j] = mi;
+    v[j] = vi;
+    p -= step * mi / (sqrtf(vi) / c.bc2_sqrt + c.eps);
+    master[j] = p;
+    for (int r = 0; r < world; ++r) peer_params[r][base + j] = __float2bfloat16(p);
+  }
+  __threadfence_system();
+}
+
+}  // namespace accerl
+
+using namespace accerl;
+
+extern "C" int accerl_enable_peer_access(int peer) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (peer == dev) return 0;
+  int can = 0;
+  cudaDeviceCanAccessPeer(&can, dev, peer);
+  if (!can) return -1;
+  cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return 0;
+  }
+  return (int)e;
+}
+
+extern "C" int accerl_rs_sumsq(const float* const* peers, int world, int rank, long long shard, float* out,
+                               double* sumsq, cudaStream_t s) {
+  if (shard <= 0) return 0;
+  long long blocks = (shard / 4 + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  rs_sumsq_kernel<<<(unsigned)blocks, 256, 0, s>>>(peers, world, rank, shard, out, sumsq);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_adamw_push(float* master, float* m, float* v, const float* grad, void* const* peer_params,
+                                 int world, int rank, long long shard, const double* sumsq, float lr, float beta1,
+                                 float beta2, float eps, float weight_decay, float max_norm, float bc1, float bc2_sqrt,
+                                 cudaStream_t s) {
+  if (shard <= 0) return 0;
+  PushCfg c{lr, beta1, beta2, eps, weight_decay, max_norm, bc1, bc2_sqrt};
+  long long blocks = (shard / 2 + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  adamw_push_kernel<<<(unsigned)blocks, 256, 0, s>>>(master, m, v, grad, (__nv_bfloat16* const*)peer_params, world,
+                                                     rank, shard, sumsq, c);
+  return (int)cudaGetLastError();
+}

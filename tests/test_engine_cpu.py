@@ -60,7 +60,15 @@ def test_greedy_matches_full_recompute_with_chunking_and_prefix_cache():
 
 def test_pause_aborts_and_runner_resumes_with_new_version():
     cfg, m, eng = make_engine(max_num_batched_tokens=64)
-    N = 120
+    N = 400
+    _, _, eng_ref = make_engine(max_num_batched_tokens=64)
+
+    async def reference():
+        o = await collect(eng_ref, [3, 4, 5, 6], SamplingParams(temperature=0.0, max_tokens=N, ignore_eos=True), "ref")
+        await eng_ref.shutdown()
+        return o.outputs[0].token_ids
+
+    uninterrupted = asyncio.run(reference())
 
     async def run():
         runner = InterruptibleGenerationRunner(eng, temperature=0.0, top_p=1.0, stop_sequences=None,
@@ -87,4 +95,4 @@ def test_pause_aborts_and_runner_resumes_with_new_version():
     assert state.output_versions[: len(partial)] == [0] * len(partial)
     assert set(state.output_versions[len(partial):]) <= {1}
     # greedy continuation after the abort equals an uninterrupted greedy run
-    assert state.output_tokens == greedy_reference(m, [3, 4, 5, 6], N)
+    assert state.output_tokens == uninterrupted
