@@ -58,7 +58,7 @@ def _proc(rank: int, a, port: int, q):
             torch.cuda.synchronize()
             if i >= a.warmup:
                 ts.append(s.elapsed_time(e))
-        assert torch.equal(buf[:1024], src[:1024])
+        assert torch.equal(buf[:1024].cpu(), src[:1024].cpu())
         results["ipc_pull_ms"] = sorted(ts)[len(ts) // 2]
     dist.barrier()
     # ---- NCCL broadcast in packed 1 GiB buffers

@@ -98,6 +98,8 @@ def build_parser() -> argparse.ArgumentParser:
     a("--device", default="auto", help="auto | cpu | cuda")
     a("--kv-cache-gb", type=float, default=None, help="KV cache size per rollout GPU (default: 60%% of free memory).")
     a("--kv-block-size", type=int, default=16)
+    a("--expert-parallel", action="store_true",
+      help="MoE models: partition the experts over the trainer ranks (token dispatch/combine over NVLink).")
     a("--weight-sync", default="ipc", choices=("ipc", "nccl"), help="Trainer->rollout weight transfer path.")
     return p
 

@@ -39,13 +39,10 @@ def _expert_segments(topi: torch.Tensor, num_experts: int):
     return order, counts, bounds
 
 
-def experts_forward(model, layer: int, xs: torch.Tensor, bounds, expert_ids=None):
-    """Run each expert's SwiGLU MLP on its contiguous row segment of ``xs``."""
-    cfg = model.cfg
-    p = f"model.layers.{layer}.mlp.experts."
-    Wgu = model.w(p + "gate_up_proj")
-    Wd = model.w(p + "down_proj")
-    Im = cfg.moe_intermediate_size
+def experts_forward_local(Wgu: torch.Tensor, Wd: torch.Tensor, xs: torch.Tensor, bounds, expert_ids=None):
+    """Each expert's SwiGLU MLP on its contiguous row segment ``xs[bounds[i]:bounds[i+1]]``;
+    ``Wgu [E, 2I, H]`` and ``Wd [E, H, I]`` are indexed by ``expert_ids`` (default ``0..``)."""
+    Im = Wd.shape[-1]
     n = xs.shape[0]
     gu = torch.empty(n, 2 * Im, dtype=xs.dtype, device=xs.device)
     ids = range(len(bounds) - 1) if expert_ids is None else expert_ids
@@ -54,18 +51,20 @@ def experts_forward(model, layer: int, xs: torch.Tensor, bounds, expert_ids=None
         if t > s:
             ops.linear(xs[s:t], Wgu[e], out=gu[s:t])
     act = ops.swiglu(gu)
-    ys = torch.empty(n, cfg.hidden_size, dtype=xs.dtype, device=xs.device)
+    ys = torch.empty(n, Wd.shape[1], dtype=xs.dtype, device=xs.device)
     for e, s, t in segs:
         if t > s:
             ops.linear(act[s:t], Wd[e], out=ys[s:t])
     return ys, gu, act
 
 
-def experts_backward(model, layer: int, dys: torch.Tensor, xs, gu, act, bounds, expert_ids=None):
-    cfg = model.cfg
+def experts_forward(model, layer: int, xs: torch.Tensor, bounds, expert_ids=None):
+    """Run each expert's SwiGLU MLP on its contiguous row segment of ``xs``."""
     p = f"model.layers.{layer}.mlp.experts."
-    Wgu, Wd = model.w(p + "gate_up_proj"), model.w(p + "down_proj")
-    gWgu, gWd = model.g(p + "gate_up_proj"), model.g(p + "down_proj")
+    return experts_forward_local(model.w(p + "gate_up_proj"), model.w(p + "down_proj"), xs, bounds, expert_ids)
+
+
+def experts_backward_local(Wgu, Wd, gWgu, gWd, dys: torch.Tensor, xs, gu, act, bounds, expert_ids=None):
     ids = range(len(bounds) - 1) if expert_ids is None else expert_ids
     segs = list(zip(ids, bounds[:-1], bounds[1:]))
     dact = torch.empty_like(act)
@@ -84,6 +83,83 @@ def experts_backward(model, layer: int, dys: torch.Tensor, xs, gu, act, bounds, 
     return dxs
 
 
+def experts_backward(model, layer: int, dys: torch.Tensor, xs, gu, act, bounds, expert_ids=None):
+    p = f"model.layers.{layer}.mlp.experts."
+    return experts_backward_local(model.w(p + "gate_up_proj"), model.w(p + "down_proj"), model.g(p + "gate_up_proj"),
+                                  model.g(p + "down_proj"), dys, xs, gu, act, bounds, expert_ids)
+
+
+# ------------------------------------------------------------------------------------------------
+# CUDA path: padded expert segments + one grouped tcgen05 GEMM launch per projection
+# ------------------------------------------------------------------------------------------------
+SEG = 128  # expert segments are padded to whole 128-row GEMM tiles
+
+
+def padded_layout(counts, device):
+    """Row layout of the dispatched tokens with every expert segment padded to SEG rows."""
+    return padded_layout_from_pads([((c + SEG - 1) // SEG) * SEG for c in counts], device)
+
+
+def padded_layout_from_pads(pads, device):
+    """Grouped-GEMM metadata for expert segments of ``pads`` rows each (multiples of SEG)."""
+    starts = [0]
+    for pdd in pads[:-1]:
+        starts.append(starts[-1] + pdd)
+    tile_expert = [e for e, pdd in enumerate(pads) for _ in range(pdd // SEG)]
+    meta = torch.tensor(tile_expert + starts + pads, dtype=torch.int32).to(device, non_blocking=True)
+    nt = len(tile_expert)
+    E = len(pads)
+    return {
+        "total": sum(pads),
+        "starts": starts,
+        "tile_expert": meta[:nt],
+        "row_start": meta[nt : nt + E],
+        "rows": meta[nt + E :],
+    }
+
+
+def _grouped(a, a_mn, b, b_mn, out, M, N, K, mode, lay, b_stride, c_stride=0, beta=0.0, row_dst=None):
+    ops.native().grouped_gemm(a, a_mn, b, b_mn, out, M, N, K, beta, mode, lay["tile_expert"], lay["row_start"],
+                              lay["rows"], len(lay["starts"]), b_stride, c_stride, ops.status_tensor(a.device),
+                              row_dst)
+
+
+def experts_forward_grouped(model, layer: int, xs_pad: torch.Tensor, lay):
+    cfg = model.cfg
+    p = f"model.layers.{layer}.mlp.experts."
+    E, Im, H = cfg.num_experts, cfg.moe_intermediate_size, cfg.hidden_size
+    Wgu = model.w(p + "gate_up_proj").reshape(E * 2 * Im, H)
+    Wd = model.w(p + "down_proj").reshape(E * H, Im)
+    R = lay["total"]
+    gu = torch.empty(R, 2 * Im, dtype=xs_pad.dtype, device=xs_pad.device)
+    _grouped(xs_pad, False, Wgu, False, gu, R, 2 * Im, H, 1, lay, 2 * Im)
+    act = ops.swiglu(gu)
+    ys = torch.empty(R, H, dtype=xs_pad.dtype, device=xs_pad.device)
+    _grouped(act, False, Wd, False, ys, R, H, Im, 1, lay, H)
+    return ys, gu, act
+
+
+def experts_backward_grouped(model, layer: int, dys_pad, xs_pad, gu, act, lay):
+    cfg = model.cfg
+    p = f"model.layers.{layer}.mlp.experts."
+    E, Im, H = cfg.num_experts, cfg.moe_intermediate_size, cfg.hidden_size
+    Wgu = model.w(p + "gate_up_proj").reshape(E * 2 * Im, H)
+    Wd = model.w(p + "down_proj").reshape(E * H, Im)
+    gWgu, gWd = model.g(p + "gate_up_proj"), model.g(p + "down_proj")
+    R = lay["total"]
+    dact = torch.empty(R, Im, dtype=dys_pad.dtype, device=dys_pad.device)
+    _grouped(dys_pad, False, Wd, True, dact, R, Im, H, 1, lay, H)
+    if gWd is not None:
+        _grouped(dys_pad, True, act, True, gWd.view(E * H, Im), H, Im, R, 2, lay, 0, H, beta=1.0)
+    dgu = ops.swiglu_backward(dact, gu)
+    del dact
+    dxs = torch.empty(R, H, dtype=dys_pad.dtype, device=dys_pad.device)
+    _grouped(dgu, False, Wgu, True, dxs, R, H, 2 * Im, 1, lay, 2 * Im)
+    if gWgu is not None:
+        _grouped(dgu, True, xs_pad, True, gWgu.view(E * 2 * Im, H), 2 * Im, H, R, 2, lay, 0, 2 * Im, beta=1.0)
+    return dxs
+
+
 def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save: bool):
     cfg = model.cfg
     k = cfg.num_experts_per_tok
@@ -91,13 +167,25 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
     tok = torch.div(order, k, rounding_mode="floor")
-    xs = h.index_select(0, tok)
     ep = getattr(model, "expert_parallel", None)
+    lay = None
+    ep_state = None
     if ep is not None:
-        ys, gu, act, ep_state = ep.forward(model, layer, xs, counts)
+        e_sorted = topi.reshape(-1).index_select(0, order)
+        ys, ep_state = ep.forward(model, layer, h, tok, e_sorted, counts, bounds)
+        xs = gu = act = None
+    elif h.is_cuda and h.dtype == torch.bfloat16:
+        lay = padded_layout(counts.tolist(), h.device)
+        # row of every (token, slot) pair inside its expert's padded segment
+        seg = torch.tensor([lay["starts"][e] - bounds[e] for e in range(cfg.num_experts)], device=h.device)
+        pos = torch.arange(order.numel(), device=h.device) + seg.repeat_interleave(counts)
+        xs = torch.zeros(lay["total"], h.shape[1], dtype=h.dtype, device=h.device)
+        xs.index_copy_(0, pos, h.index_select(0, tok))
+        ys_pad, gu, act = experts_forward_grouped(model, layer, xs, lay)
+        ys = ys_pad.index_select(0, pos)
     else:
+        xs = h.index_select(0, tok)
         ys, gu, act = experts_forward(model, layer, xs, bounds)
-        ep_state = None
     w_sorted = w_act.reshape(-1).index_select(0, order)
     y = torch.zeros(h.shape[0], cfg.hidden_size, dtype=torch.float32, device=h.device)
     y.index_add_(0, tok, ys.float() * w_sorted.float().unsqueeze(1))
@@ -118,6 +206,9 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
         cache["bounds"] = torch.tensor(bounds)
         if ep_state is not None:
             cache["ep_state"] = ep_state  # type: ignore[assignment]
+        if lay is not None:
+            cache["layout"] = lay  # type: ignore[assignment]
+            cache["pos"] = pos
     return out, cache
 
 
@@ -134,7 +225,12 @@ def moe_backward(model, layer: int, dx3: torch.Tensor, c) -> torch.Tensor:
     bounds = m["bounds"].tolist()
     ep = getattr(model, "expert_parallel", None)
     if ep is not None:
-        dxs = ep.backward(model, layer, dys, m)
+        dxs = ep.backward(model, layer, dys, m["ep_state"])
+    elif "layout" in m:
+        lay, pos = m["layout"], m["pos"]
+        dys_pad = torch.zeros(lay["total"], cfg.hidden_size, dtype=dys.dtype, device=dys.device)
+        dys_pad.index_copy_(0, pos, dys)
+        dxs = experts_backward_grouped(model, layer, dys_pad, m["xs"], m["gu"], m["act"], lay).index_select(0, pos)
     else:
         dxs = experts_backward(model, layer, dys, m["xs"], m["gu"], m["act"], bounds)
     dh = torch.zeros(h.shape[0], cfg.hidden_size, dtype=torch.float32, device=h.device)

@@ -164,6 +164,15 @@ class TrainWorker:
         if self.model.layout.trainable_numel == 0:
             raise RuntimeError(f"No trainable parameters found for mode: {args.train_mode}")
         self.optimizer = ShardedAdamW(self.model, lr=args.learning_rate, weight_decay=args.weight_decay)
+        if getattr(args, "expert_parallel", False) and self.cfg.num_experts > 0 and fsdp_world_size > 1:
+            from ..parallel.expert_parallel import ExpertParallel
+
+            if getattr(args, "train_packing", "padded") == "varlen" and args.train_token_budget:
+                max_tokens = int(args.train_token_budget)
+            else:
+                max_tokens = int(args.batch_size) * int(args.max_length)
+            self.model.expert_parallel = ExpertParallel(self.cfg, max_tokens=max_tokens, device=self.device,
+                                                        dtype=self.dtype)
         self.tokenizer = tokenizer
         self.pad_token_id = self._pad_token_id(tokenizer)
         self.collate_fn = make_padded_collate(self.pad_token_id)

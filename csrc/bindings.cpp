@@ -2,8 +2,11 @@
 // expose extern "C" launchers; this file validates tensors and forwards raw pointers together with
 // the current CUDA stream.
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_runtime.h>
+
+#include <cstring>
 #include <torch/extension.h>
 
 extern "C" {
@@ -11,6 +14,13 @@ int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long
                      long long ldc, int c_f32, int M, int N, int K, float alpha, float beta, const void* bias,
                      const void* residual, long long ldr, int* status, int block_n, int max_ctas, int splits,
                      cudaStream_t stream);
+int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn, void* C,
+                             long long ldc, int c_f32, int M, int N, int K, long long b_rows_total, float beta, int mode,
+                             const int* tile_expert, const int* group_row_start, const int* group_rows, int num_groups,
+                             int b_group_stride, long long c_group_stride, const long long* row_dst, int* status,
+                             cudaStream_t stream);
+int accerl_row_scatter(const void* src, long long ld, const long long* src_row, const long long* dst_addr, long long n,
+                       int H, cudaStream_t s);
 int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
                          void* out, long long ldo, int M, int N, cudaStream_t stream);
 int accerl_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int H, long long ldx,
@@ -137,6 +147,38 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
                          opt_ptr(bias), opt_ptr(residual), ldr, status_ptr(status), static_cast<int>(block_n),
                          static_cast<int>(max_ctas), static_cast<int>(splits), cur_stream()),
         "gemm");
+}
+
+// Grouped expert GEMM. mode 1: a [M, K] (or [K, M] if a_mn), b stacked [E*Nb, K] K-major / [E*Kb, N]
+// MN-major, out [M, N]. mode 2: a [R, M], b [R, N] (MN-major), out stacked [E*c_stride, N] fp32.
+void grouped_gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Tensor& out, int64_t M,
+                  int64_t N, int64_t K, double beta, int64_t mode, const c10::optional<at::Tensor>& tile_expert,
+                  const c10::optional<at::Tensor>& row_start, const c10::optional<at::Tensor>& rows,
+                  int64_t num_groups, int64_t b_group_stride, int64_t c_group_stride,
+                  const c10::optional<at::Tensor>& status, const c10::optional<at::Tensor>& row_dst) {
+  CHECK_BF16(a);
+  CHECK_BF16(b);
+  auto iptr = [](const c10::optional<at::Tensor>& t) -> const int* {
+    return t.has_value() ? t->data_ptr<int>() : nullptr;
+  };
+  check(accerl_grouped_gemm_bf16(a.data_ptr(), ld_of(a), a_mn, b.data_ptr(), ld_of(b), b_mn, out.data_ptr(), ld_of(out),
+                                 out.scalar_type() == at::kFloat, M, N, K, b.size(0), static_cast<float>(beta), mode,
+                                 iptr(tile_expert), iptr(row_start), iptr(rows), num_groups, b_group_stride,
+                                 c_group_stride,
+                                 row_dst.has_value() ? reinterpret_cast<const long long*>(row_dst->data_ptr<int64_t>())
+                                                     : nullptr,
+                                 status_ptr(status), cur_stream()),
+        "grouped_gemm");
+}
+
+void row_scatter(const at::Tensor& src, const c10::optional<at::Tensor>& src_row, const at::Tensor& dst_addr) {
+  CHECK_BF16(src);
+  check(accerl_row_scatter(src.data_ptr(), ld_of(src),
+                           src_row.has_value() ? reinterpret_cast<const long long*>(src_row->data_ptr<int64_t>())
+                                               : nullptr,
+                           reinterpret_cast<const long long*>(dst_addr.data_ptr<int64_t>()), dst_addr.numel(),
+                           src.size(1), cur_stream()),
+        "row_scatter");
 }
 
 void splitk_finish(const at::Tensor& acc, const c10::optional<at::Tensor>& bias,
@@ -336,6 +378,46 @@ void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cach
         "kv_cache_write");
 }
 
+// CUDA IPC of a tensor's allocation. The handle covers the caching-allocator segment that holds the
+// tensor; the tensor's byte offset inside it travels with the handle. Peers open it on THEIR current
+// device with lazy peer access, so the mapping lives in the context their kernels run in. Errors are
+// returned as codes (no exceptions across the binding).
+std::tuple<int64_t, py::bytes, int64_t> ipc_export(const at::Tensor& t) {
+  TORCH_CHECK(t.is_cuda(), "ipc_export: cuda tensor");
+  size_t seg = 0;
+  void* base = c10::cuda::CUDACachingAllocator::getBaseAllocation(t.data_ptr(), &seg);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, base);
+  const int64_t off = static_cast<const char*>(t.data_ptr()) - static_cast<const char*>(base);
+  return {static_cast<int64_t>(e), py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)), off};
+}
+
+std::tuple<int64_t, int64_t> ipc_open(const py::bytes& handle) {
+  const std::string raw = handle;
+  if (raw.size() != sizeof(cudaIpcMemHandle_t)) return {-1, 0};
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, raw.data(), sizeof(h));
+  void* base = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) cudaGetLastError();
+  return {static_cast<int64_t>(e), reinterpret_cast<int64_t>(base)};
+}
+
+int64_t ipc_close(int64_t base) {
+  const cudaError_t e = cudaIpcCloseMemHandle(reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) cudaGetLastError();
+  return static_cast<int64_t>(e);
+}
+
+// Synchronous copy of n bytes from a (peer) device address into host memory: a host-side check that
+// a mapping is readable and holds what its owner reports, before any kernel dereferences it.
+std::tuple<int64_t, py::bytes> peer_read(int64_t addr, int64_t n) {
+  std::string out(static_cast<size_t>(n), '\0');
+  const cudaError_t e = cudaMemcpy(out.data(), reinterpret_cast<const void*>(addr), n, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) cudaGetLastError();
+  return {static_cast<int64_t>(e), py::bytes(out)};
+}
+
 void enable_peer_access(int64_t peer) { check(accerl_enable_peer_access(static_cast<int>(peer)), "enable_peer_access"); }
 
 // peer_ptrs: int64 device tensor [world] of base addresses (fp32 full gradient buffers)
@@ -378,6 +460,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("last_error", &last_error, "(code, message) of the most recent launch; resets it");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM");
   m.def("splitk_finish", &splitk_finish);
+  m.def("grouped_gemm", &grouped_gemm);
+  m.def("row_scatter", &row_scatter);
+  m.def("ipc_export", &ipc_export);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_read", &peer_read);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("bias_grad", &bias_grad);

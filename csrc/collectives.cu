@@ -99,9 +99,35 @@ __global__ void adamw_push_kernel(float* __restrict__ master, float* __restrict_
   __threadfence_system();
 }
 
+// Row copy to arbitrary (local or peer) addresses: row i of the source (src_row[i], or i when null) is
+// stored at dst_addr[i] (0 = skip). One warp per row, 16-byte P2P stores. Used for the expert-parallel
+// dispatch of tokens (and of their gradients) into the owning rank's receive buffer.
+__global__ void row_scatter_kernel(const __nv_bfloat16* __restrict__ src, long long ld, const long long* __restrict__ src_row,
+                                   const long long* __restrict__ dst_addr, long long n, int H) {
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const long long dst = dst_addr[w];
+  if (dst == 0) return;
+  const long long r = src_row ? src_row[w] : w;
+  const uint4* s = reinterpret_cast<const uint4*>(src + r * ld);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  for (int c = lane; c < H / 8; c += 32) d[c] = s[c];
+}
+
 }  // namespace accerl
 
 using namespace accerl;
+
+extern "C" int accerl_row_scatter(const void* src, long long ld, const long long* src_row, const long long* dst_addr,
+                                  long long n, int H, cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (H % 8 || ld % 8) return -1;
+  const long long threads = n * 32;
+  row_scatter_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)src, ld, src_row, dst_addr,
+                                                                        n, H);
+  return (int)cudaGetLastError();
+}
 
 extern "C" int accerl_enable_peer_access(int peer) {
   int dev = 0;

@@ -44,6 +44,26 @@ struct GemmParams {
   int* status;
   int tiles_m, tiles_n, num_tiles, group_m;
   int splits, kb_per_split;  // split-K: work item = (tile, split); splits > 1 adds fp32 partials atomically
+  // grouped (mixture-of-experts) problems; expert row segments are padded to multiples of 128 rows
+  //  mode 1: A rows are grouped by expert; tile_expert[m_blk] names the expert whose B slice is used
+  //          (K-major B: rows e*b_group_stride.., MN-major B: reduction rows e*b_group_stride..)
+  //  mode 2: per-expert weight gradient; work item = (expert, m_blk, n_blk), reduction over the expert's
+  //          rows [group_row_start[e], +group_rows[e]), output rows offset by e*c_group_stride
+  int group_mode;
+  const int* tile_expert;
+  const int* group_row_start;
+  const int* group_rows;
+  int b_group_stride;
+  long long c_group_stride;
+  int num_groups;
+  // scatter epilogue: bf16 output row r is stored at address row_dst[r] (0 = drop the row); used to
+  // write expert outputs straight into the source rank's buffer over NVLink
+  const long long* row_dst;
+};
+
+struct WorkItem {
+  int m_blk, n_blk, kb0, kb1, b_n_off, b_k_off;
+  long long c_row_off;
 };
 
 template <int BN>
@@ -62,6 +82,34 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& m_b
   const int r = t % per_group;
   m_blk = first_m + r % gsize;
   n_blk = r / gsize;
+}
+
+template <bool B_MN>
+__device__ __forceinline__ WorkItem work_item(const GemmParams& p, int t, int k_blocks) {
+  WorkItem w;
+  w.b_n_off = 0;
+  w.b_k_off = 0;
+  w.c_row_off = 0;
+  if (p.group_mode == 2) {
+    const int per_e = p.tiles_m * p.tiles_n;
+    const int e = t / per_e;
+    const int local = t % per_e;
+    w.m_blk = local % p.tiles_m;
+    w.n_blk = local / p.tiles_m;
+    w.kb0 = p.group_row_start[e] / kBK;
+    w.kb1 = w.kb0 + p.group_rows[e] / kBK;
+    w.c_row_off = static_cast<long long>(e) * p.c_group_stride;
+    return w;
+  }
+  tile_coords(p, t, w.m_blk, w.n_blk);
+  w.kb0 = (t % p.splits) * p.kb_per_split;
+  w.kb1 = min(k_blocks, w.kb0 + p.kb_per_split);
+  if (p.group_mode == 1) {
+    const int e = p.tile_expert[w.m_blk];
+    if (B_MN) w.b_k_off = e * p.b_group_stride;
+    else w.b_n_off = e * p.b_group_stride;
+  }
+  return w;
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
@@ -114,12 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t last_parity = 0;  // bit s = parity of the last load issued into stage s
       bool ok = true;
       for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-        int m_blk, n_blk;
-        tile_coords(p, t, m_blk, n_blk);
-        const int m0 = m_blk * kBM, n0 = n_blk * BN;
-        const int kb0 = (t % p.splits) * p.kb_per_split;
-        const int kb1 = min(k_blocks, kb0 + p.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        const WorkItem w = work_item<B_MN>(p, t, k_blocks);
+        if (w.kb1 <= w.kb0) continue;
+        const int m0 = w.m_blk * kBM, n0 = w.n_blk * BN;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kStatusTimeoutProducer)) {
             ok = false;
             break;
@@ -136,9 +182,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if constexpr (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 64 * kBK * 2, &tmB, &full[stage], n0 + 64 * j, k0);
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 64 * kBK * 2, &tmB, &full[stage], n0 + 64 * j, k0 + w.b_k_off);
           } else {
-            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0 + w.b_n_off);
           }
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -162,14 +209,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        const WorkItem w = work_item<B_MN>(p, t, k_blocks);
+        if (w.kb1 <= w.kb0) continue;
+        const int kb0 = w.kb0, kb1 = w.kb1;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tbase + acc * BN;
-        const int kb0 = (t % p.splits) * p.kb_per_split;
-        const int kb1 = min(k_blocks, kb0 + p.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
             ok = false;
@@ -202,15 +251,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
-      int m_blk, n_blk;
-      tile_coords(p, t, m_blk, n_blk);
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      const WorkItem w = work_item<B_MN>(p, t, k_blocks);
+      if (w.kb1 <= w.kb0) continue;
+      const int m_blk = w.m_blk, n_blk = w.n_blk;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row = m_blk * kBM + row_in_tile;
-      const bool row_ok = row < p.M;
+      const bool row_ok = m_blk * kBM + row_in_tile < p.M;
+      const long long row = w.c_row_off + m_blk * kBM + row_in_tile;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
@@ -236,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (p.residual) {
-            const uint4 r = *reinterpret_cast<const uint4*>(p.residual + static_cast<long long>(row) * p.ldr + col);
+            const uint4 r = *reinterpret_cast<const uint4*>(p.residual + row * p.ldr + col);
             const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -247,11 +298,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (p.splits > 1) {
             // split-K partial: add into the fp32 output (pre-initialised by the caller)
-            float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            float* c = reinterpret_cast<float*>(p.C) + row * p.ldc + col;
             red_add_v4(c, f[0], f[1], f[2], f[3]);
             red_add_v4(c + 4, f[4], f[5], f[6], f[7]);
           } else if (p.c_f32) {
-            float* c = reinterpret_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            float* c = reinterpret_cast<float*>(p.C) + row * p.ldc + col;
             if (p.beta != 0.f) {
               const float4 o0 = *reinterpret_cast<const float4*>(c);
               const float4 o1 = *reinterpret_cast<const float4*>(c + 4);
@@ -261,7 +312,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<float4*>(c) = make_float4(f[0], f[1], f[2], f[3]);
             *reinterpret_cast<float4*>(c + 4) = make_float4(f[4], f[5], f[6], f[7]);
           } else {
-            __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + col;
+            __nv_bfloat16* c;
+            if (p.row_dst) {
+              const long long dst = p.row_dst[row];
+              if (dst == 0) continue;
+              c = reinterpret_cast<__nv_bfloat16*>(dst) + col;
+            } else {
+              c = reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
+            }
             if (p.beta != 0.f) {
               const uint4 o = *reinterpret_cast<const uint4*>(c);
               const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
@@ -475,6 +533,14 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   p.splits = (k_blocks + p.kb_per_split - 1) / p.kb_per_split;
   p.num_tiles = p.tiles_m * p.tiles_n * p.splits;
   p.group_m = 8;
+  p.group_mode = 0;
+  p.tile_expert = nullptr;
+  p.group_row_start = nullptr;
+  p.group_rows = nullptr;
+  p.b_group_stride = 0;
+  p.c_group_stride = 0;
+  p.num_groups = 0;
+  p.row_dst = nullptr;
   if (bn == 256) return dispatch_major<256, 4>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
   return dispatch_major<128, 6>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
 }
@@ -511,4 +577,61 @@ extern "C" int accerl_splitk_finish(const float* acc, long long lda, const void*
   splitk_finish_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, stream>>>(
       acc, lda, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)residual, ldr, (__nv_bfloat16*)out, ldo, M, N);
   return (int)cudaGetLastError();
+}
+
+// Grouped GEMM for expert MLPs (see GemmParams group_mode). Dimensions:
+//  mode 1: A [M_total, K] (K-major) or the dgrad/fwd convention of accerl_gemm_bf16 with stacked B
+//          of b_rows_total rows; C [M_total, N].
+//  mode 2: A [rows_total, M] and B [rows_total, N] (both MN-major, K = rows_total); C is the stacked
+//          [num_groups * c_group_stride, N] weight gradient (fp32, accumulated with beta = 1).
+extern "C" int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                                        void* C, long long ldc, int c_f32, int M, int N, int K, long long b_rows_total,
+                                        float beta, int mode, const int* tile_expert, const int* group_row_start,
+                                        const int* group_rows, int num_groups, int b_group_stride,
+                                        long long c_group_stride, const long long* row_dst, int* status,
+                                        cudaStream_t stream) {
+  using namespace accerl;
+  if (M <= 0 || N <= 0 || K <= 0 || num_groups <= 0) return 0;
+  if ((N % 8) != 0 || (ldc % 8) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -2;
+  if (mode != 1 && mode != 2) return -10;
+  if (mode == 2 && !(a_mn && b_mn && c_f32)) return -11;
+  const int bn = N >= 256 ? 256 : 128;
+  CUtensorMap ma, mb;
+  bool ok;
+  if (a_mn) ok = make_map_2d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, 64);
+  else ok = make_map_2d(&ma, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, 128);
+  if (!ok) return -7;
+  if (b_mn) ok = make_map_2d(&mb, B, (uint64_t)N, (uint64_t)b_rows_total, (uint64_t)ldb, 64, 64);
+  else ok = make_map_2d(&mb, B, (uint64_t)K, (uint64_t)b_rows_total, (uint64_t)ldb, 64, (uint32_t)bn);
+  if (!ok) return -8;
+  GemmParams p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = C;
+  p.ldc = ldc;
+  p.c_f32 = c_f32;
+  p.alpha = 1.f;
+  p.beta = beta;
+  p.bias = nullptr;
+  p.residual = nullptr;
+  p.ldr = 0;
+  p.status = status;
+  p.tiles_m = (M + kBM - 1) / kBM;
+  p.tiles_n = (N + bn - 1) / bn;
+  p.splits = 1;
+  p.kb_per_split = (K + kBK - 1) / kBK;
+  p.group_m = 8;
+  p.group_mode = mode;
+  p.tile_expert = tile_expert;
+  p.group_row_start = group_row_start;
+  p.group_rows = group_rows;
+  p.b_group_stride = b_group_stride;
+  p.c_group_stride = c_group_stride;
+  p.num_groups = num_groups;
+  p.row_dst = row_dst;
+  if (row_dst && (c_f32 || beta != 0.f)) return -12;
+  p.num_tiles = p.tiles_m * p.tiles_n * (mode == 2 ? num_groups : 1);
+  if (bn == 256) return dispatch_major<256, 4>(a_mn, b_mn, ma, mb, p, stream, 0);
+  return dispatch_major<128, 6>(a_mn, b_mn, ma, mb, p, stream, 0);
 }

@@ -1,0 +1,122 @@
+"""Expert parallelism on CPU ranks (gloo): the dispatch/combine plan of ``ExpertParallel`` gives the
+same log-probabilities and, summed over ranks, the same gradients as every rank running all experts
+on its own tokens. The row exchange is the gloo emulation; the GPU path shares the plan."""
+
+import os
+import socket
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from accerl_agent_b200.algo.packing import make_varlen_batch
+from accerl_agent_b200.core.sample import RLSample
+from accerl_agent_b200.models.config import get_preset
+from accerl_agent_b200.models.transformer import build_model
+from accerl_agent_b200.parallel.expert_parallel import ExpertParallel
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cfg(model_type, num_experts=6):
+    cfg = get_preset("tiny-qwen2")
+    cfg.vocab_size = 512
+    cfg.model_type = model_type
+    cfg.num_experts = num_experts
+    cfg.num_experts_per_tok = 2
+    cfg.moe_intermediate_size = 64
+    cfg.norm_topk_prob = model_type == "qwen3_moe"
+    if model_type == "qwen2_moe":
+        cfg.shared_expert_intermediate_size = 96
+    else:
+        cfg.qkv_bias = False
+        cfg.qk_norm = True
+    return cfg
+
+
+def _pack(seed, vocab):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for L in (23, 11 + seed % 5):
+        ids = torch.randint(0, vocab, (L,), generator=g).tolist()
+        labels = [-100] * (L // 2) + ids[L // 2:]
+        out.append(RLSample("grpo", ids, [1] * L, labels, [-8.0] * L, 0.5, [0.0] * L,
+                            [-1] * (L // 2) + [0] * (L - L // 2), [0]))
+    return make_varlen_batch(out)
+
+
+def _run(model, batch):
+    lp, ctx = model.forward_logprobs(batch, 32)
+    dlp = torch.linspace(-1.0, 1.0, lp.numel(), dtype=lp.dtype) * 0.01
+    model.backward_from_logprobs(dlp, ctx)
+    return lp.detach().clone()
+
+
+def _worker(rank, port, model_type, num_experts, transport, out):
+    try:
+        _work(rank, port, model_type, num_experts, transport, out)
+    except BaseException as exc:  # report instead of leaving the parent waiting on the queue
+        out.put((rank, repr(exc), None))
+        raise
+
+
+def _work(rank, port, model_type, num_experts, transport, out):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    cfg = _cfg(model_type, num_experts)
+    model = build_model(cfg, "full", torch.device("cpu"), torch.float32, pad_to=2)
+    model.init_weights(seed=3)
+    model.expert_parallel = ExpertParallel(cfg, max_tokens=64, device=torch.device("cpu"), dtype=torch.float32,
+                                           transport=transport)
+    lp = _run(model, _pack(40 + rank, cfg.vocab_size))
+    grads = model.grads.clone()
+    dist.all_reduce(grads)
+    out.put((rank, lp, grads if rank == 0 else None))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _check(model_type, num_experts=6, transport="emulated"):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, port, model_type, num_experts, transport, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        rank, lp, g = q.get(timeout=180)
+        assert not isinstance(lp, str), f"rank {rank} failed: {lp}"
+        res[rank] = (lp, g)
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    cfg = _cfg(model_type, num_experts)
+    model = build_model(cfg, "full", torch.device("cpu"), torch.float32, pad_to=2)
+    model.init_weights(seed=3)
+    lps = [_run(model, _pack(40 + r, cfg.vocab_size)) for r in range(2)]
+    for r in range(2):
+        torch.testing.assert_close(res[r][0], lps[r], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(res[0][1], model.grads, rtol=1e-4, atol=1e-6)
+
+
+def test_expert_parallel_matches_local_experts_qwen2_moe():
+    _check("qwen2_moe")
+
+
+def test_expert_parallel_matches_local_experts_qwen3_moe():
+    _check("qwen3_moe")
+
+
+def test_expert_parallel_uneven_expert_partition():
+    # 5 experts on 2 ranks: rank 0 owns 3, rank 1 owns 2
+    _check("qwen3_moe", num_experts=5)
+
+
+def test_expert_parallel_all_to_all_transport():
+    # the all_to_all_single transport (NCCL on GPUs) runs on gloo ranks too
+    _check("qwen2_moe", num_experts=5, transport="all_to_all")

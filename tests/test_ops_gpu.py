@@ -315,3 +315,32 @@ def test_attention_forward_queries_over_longer_keys(q_lens, k_lens):
                                          cu_k, 1 / math.sqrt(D))
     assert _rel(o, o_r.reshape(o.shape)) < 2e-2
     assert torch.allclose(lse, lse_r, atol=1e-2)
+
+
+def test_grouped_expert_gemms_match_per_expert_products():
+    from accerl_agent_b200.models.moe import _grouped, padded_layout
+
+    E, H, N = 5, 256, 384
+    counts = [0, 130, 7, 256, 1]
+    lay = padded_layout(counts, torch.device(DEV))
+    R = lay["total"]
+    x = torch.zeros(R, H, device=DEV).bfloat16()
+    dy = torch.zeros(R, N, device=DEV).bfloat16()
+    for e, c in enumerate(counts):
+        s = lay["starts"][e]
+        x[s : s + c] = torch.randn(c, H, device=DEV).bfloat16()
+        dy[s : s + c] = torch.randn(c, N, device=DEV).bfloat16()
+    W = (torch.randn(E, N, H, device=DEV) * 0.05).bfloat16()
+    y = torch.empty(R, N, device=DEV).bfloat16()
+    _grouped(x, False, W.view(E * N, H), False, y, R, N, H, 1, lay, N)  # forward  y_e = x_e W_e^T
+    dx = torch.empty(R, H, device=DEV).bfloat16()
+    _grouped(dy, False, W.view(E * N, H), True, dx, R, H, N, 1, lay, N)  # dgrad    dx_e = dy_e W_e
+    gW = torch.ones(E * N, H, device=DEV)
+    _grouped(dy, True, x, True, gW, N, H, R, 2, lay, 0, N, beta=1.0)  # wgrad  gW_e += dy_e^T x_e
+    for e, c in enumerate(counts):
+        s = lay["starts"][e]
+        xe, dye, We = x[s : s + c].float(), dy[s : s + c].float(), W[e].float()
+        if c:
+            assert _rel(y[s : s + c], xe @ We.t()) < 1e-2
+            assert _rel(dx[s : s + c], dye @ We) < 1e-2
+        assert _rel(gW[e * N : (e + 1) * N], 1.0 + dye.t() @ xe) < 1e-5
