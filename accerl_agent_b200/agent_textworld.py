@@ -126,7 +126,7 @@ def run_train(args) -> Dict[str, float]:
             infer_end = sum(s["total_tokens"] for s in get([e.get_stats.remote() for e in engines]))
             while True:
                 try:
-                    stats.add_textworld_episode(*stats_queue.get_nowait())
+                    stats.add_record(*stats_queue.get_nowait())
                 except pyqueue.Empty:
                     break
             r0 = next(s for s in summaries if s["rank"] == 0)
@@ -139,11 +139,24 @@ def run_train(args) -> Dict[str, float]:
             n = len(summaries)
             tokens = (float(r0["segment_valid_tokens"]) if args.train_packing == "varlen"
                       else sum(float(s["segment_valid_tokens"]) for s in summaries))
+            if args.env == "gsm8k":
+                env_scal = {
+                    "Rollout/GlobalRewardSumMean": rs["global_reward_sum_mean"],
+                    "Rollout/ResponseLengthMean": rs["response_length_mean"],
+                    "Rollout/AbortRate": rs["abort_rate"],
+                }
+                score = rs["global_reward_sum_mean"]
+            else:
+                env_scal = {
+                    "TextWorld/NormalizedScore": rs["tw_normalized_score"],
+                    "TextWorld/WinRate": rs["tw_win_rate"],
+                    "TextWorld/InvalidActionRate": rs["tw_invalid_action_rate"],
+                    "TextWorld/EnvStepsMean": rs["tw_env_steps_mean"],
+                }
+                score = rs["tw_normalized_score"]
             scal = {
-                "TextWorld/NormalizedScore": rs["tw_normalized_score"],
-                "TextWorld/WinRate": rs["tw_win_rate"],
-                "TextWorld/InvalidActionRate": rs["tw_invalid_action_rate"],
-                "TextWorld/EnvStepsMean": rs["tw_env_steps_mean"],
+                **env_scal,
+                "Train/OptimizerStep": latest_step,
                 "Replay/FillRatio": sum(r["size"] for r in replay) / max(sum(r["capacity"] for r in replay), 1),
                 "Replay/TrainSampleTrainerVersionLagMean": sum(s["segment_version_lag_mean"] for s in summaries) / n,
                 "Rollout/ActiveWorkers": rs["active_workers"],
@@ -164,7 +177,7 @@ def run_train(args) -> Dict[str, float]:
             writer.add_scalars(scal, latest_step)
             print(f"[metrics] step={latest_step} loss={scal['Train/Loss']:.6f} kl={scal['KL/OldNewK3TokenMean']:.6f} "
                   f"train_tokens_per_sec={scal['Train/TokensPerSec']:.2f} "
-                  f"infer_tokens_per_sec={scal['Infer/TokensPerSec']:.2f} score={rs['tw_normalized_score']:.4f}")
+                  f"infer_tokens_per_sec={scal['Infer/TokensPerSec']:.2f} score={score:.4f}")
             writer.flush()
             final = dict(scal)
             if args.save_checkpoint and args.checkpoint_every_sync_rounds > 0 and \

@@ -32,7 +32,7 @@ class ObjectiveConfig:
 
     @property
     def mode_id(self) -> int:
-        return {"ppo": 0, "gipo": 1, "sapo": 2}[self.clip_mode]
+        return {"ppo": 0, "gipo": 1, "sapo": 2, "none": 3}[self.clip_mode]
 
 
 def token_objective(
@@ -60,6 +60,9 @@ def token_objective(
             torch.full_like(adv, cfg.sapo_tau_neg),
         )
         obj = torch.sigmoid(tau * (r - 1.0)) * (4.0 / tau) * adv
+    elif cfg.clip_mode == "none":
+        # REINFORCE-style objective without importance ratio (vllm_fsdp.py:628-638)
+        obj = adv * lp
     else:
         raise ValueError(f"Unsupported clip_mode: {cfg.clip_mode}")
     k3 = ratio - 1.0 - log_ratio

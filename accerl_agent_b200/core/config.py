@@ -48,7 +48,7 @@ def build_parser() -> argparse.ArgumentParser:
     a("--weight-decay", type=float, default=0.0)
     a("--grad-accum-steps", type=int, default=8)
     a("--train-logprob-mode", type=str, default="full_logits_ce", choices=["full_logits_ce", "response_only_lm_head"])
-    a("--clip-mode", type=str, default="ppo", choices=["ppo", "gipo", "sapo"])
+    a("--clip-mode", type=str, default="ppo", choices=["ppo", "gipo", "sapo", "none"])
     a("--ppo-normalize-advantages", action="store_true")
     a("--ppo-adv-norm-eps", type=float, default=1e-8)
     a("--clip-eps", type=float, default=0.2)
@@ -90,7 +90,11 @@ def build_parser() -> argparse.ArgumentParser:
     a("--disable-vllm-prefix-caching", action="store_true")
     a("--max-sync-rounds", type=int, default=None)
     # ---- additions of this framework
-    a("--env", default="textworld", choices=("textworld", "synthetic"))
+    a("--env", default="textworld", choices=("textworld", "synthetic", "gsm8k"))
+    a("--lr-schedule", default="warmup_cosine", choices=("warmup_cosine", "constant"))
+    a("--gsm8k-train-path", default="synthetic",
+      help="GSM8K train jsonl for --env gsm8k; 'synthetic' uses seeded arithmetic word problems.")
+    a("--gsm8k-limit", type=int, default=None)
     a("--synthetic-obs-min", type=int, default=64)
     a("--synthetic-obs-max", type=int, default=256)
     a("--synthetic-reward-prob", type=float, default=0.1)

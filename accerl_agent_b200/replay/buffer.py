@@ -77,6 +77,11 @@ class RolloutStats:
         self.wins: deque = deque(maxlen=window_size)
         self.steps: deque = deque(maxlen=window_size)
         self.invalid_actions: deque = deque(maxlen=window_size)
+        # math variant (per generated answer)
+        self.rewards: deque = deque(maxlen=window_size)
+        self.response_lengths: deque = deque(maxlen=window_size)
+        self.abort_flags: deque = deque(maxlen=window_size)
+        self.total_answers = 0
         self._lock = threading.Lock()
 
     def add_textworld_episode(
@@ -92,6 +97,25 @@ class RolloutStats:
 
     add_episode = add_textworld_episode
 
+    def add_rollout_batch(self, worker_id: int, rewards, response_lengths, abort_flags) -> None:
+        """One group of answers of the math variant (``vllm_fsdp.py:1013-1030``)."""
+        if not (len(rewards) == len(response_lengths) == len(abort_flags)):
+            raise ValueError(f"Rollout metric batch lengths must match: rewards={len(rewards)} "
+                             f"response_lengths={len(response_lengths)} abort_flags={len(abort_flags)}")
+        with self._lock:
+            self.rewards.extend(float(r) for r in rewards)
+            self.response_lengths.extend(int(n) for n in response_lengths)
+            self.abort_flags.extend(bool(f) for f in abort_flags)
+            self.total_answers += len(rewards)
+            self.worker_last_active[int(worker_id)] = self.clock()
+
+    def add_record(self, *rec) -> None:
+        """Dispatch a statistics record from a rollout worker: ``("math", ...)`` or a TextWorld episode."""
+        if rec and rec[0] == "math":
+            self.add_rollout_batch(*rec[1:])
+        else:
+            self.add_textworld_episode(*rec)
+
     def get_stats(self) -> Dict[str, float]:
         with self._lock:
             cutoff = self.clock() - self.active_timeout_seconds
@@ -106,4 +130,9 @@ class RolloutStats:
                 "tw_invalid_action_rate": (sum(self.invalid_actions) / total_steps) if total_steps else 0.0,
                 "tw_env_steps_mean": (total_steps / n) if n else 0.0,
                 "episodes": n,
+                "global_reward_sum_mean": (sum(self.rewards) / len(self.rewards)) if self.rewards else 0.0,
+                "response_length_mean": (sum(self.response_lengths) / len(self.response_lengths))
+                if self.response_lengths else 0.0,
+                "abort_rate": (sum(1 for f in self.abort_flags if f) / len(self.abort_flags)) if self.abort_flags else 0.0,
+                "total_episodes": self.total_answers,
             }

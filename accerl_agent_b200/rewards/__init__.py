@@ -1,0 +1,5 @@
+"""Reward functions for the math (GSM8K) variant of the RL loop."""
+
+from .math_grader import extract_boxed, grade_answer, normalize_answer, r1_zero_reward_fn
+
+__all__ = ["extract_boxed", "grade_answer", "normalize_answer", "r1_zero_reward_fn"]

@@ -26,7 +26,16 @@ class InferenceActor:
         else:
             device = torch.device("cpu")
         self.args = args
-        tokenizer = _load_tokenizer(args) if args.env == "textworld" else None
+        if args.env == "textworld":
+            tokenizer = _load_tokenizer(args)
+        elif args.env == "gsm8k":
+            from ..core.tokenizer import load_tokenizer
+            from ..models.config import resolve_model_config
+
+            tokenizer = load_tokenizer(args.model_path, args.trust_remote_code,
+                                       vocab_size=resolve_model_config(args.model_path).vocab_size, fallback=True)
+        else:
+            tokenizer = None
         self.service = InferenceService(args, device, tokenizer=tokenizer)
         world = len(replay_queues)
 
@@ -37,8 +46,15 @@ class InferenceActor:
         def stats_sink(*rec):
             stats_queue.put(rec)
 
-        self.workers = [RolloutWorker(args, self.service, wid, sink_for(wid), stats_sink, tokenizer=tokenizer)
-                        for wid in worker_ids]
+        if args.env == "gsm8k":
+            from .math_worker import MathRolloutWorker, load_math_examples
+
+            examples = load_math_examples(args)
+            self.workers = [MathRolloutWorker(args, self.service, wid, sink_for(wid), stats_sink, tokenizer=tokenizer,
+                                              examples=examples) for wid in worker_ids]
+        else:
+            self.workers = [RolloutWorker(args, self.service, wid, sink_for(wid), stats_sink, tokenizer=tokenizer)
+                            for wid in worker_ids]
         self.tasks: List[asyncio.Task] = []
 
     async def start_workers(self) -> int:

@@ -657,7 +657,8 @@ class GenerationEngine:
         if p.stop_token_ids and tok in p.stop_token_ids:
             return "stop"
         if p.stop and self.tokenizer is not None:
-            tail = self.tokenizer.decode(seq.out[-8:], skip_special_tokens=p.skip_special_tokens)
+            window = max(8, max(len(x) for x in p.stop) + 2)
+            tail = self.tokenizer.decode(seq.out[-window:], skip_special_tokens=p.skip_special_tokens)
             if any(s in tail for s in p.stop):
                 return "stop"
         if len(seq.out) >= p.max_tokens or seq.length >= self.max_model_len:

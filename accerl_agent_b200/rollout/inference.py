@@ -47,7 +47,12 @@ class InferenceService:
             enable_prefix_caching=not args.disable_vllm_prefix_caching,
             tokenizer=tokenizer,
         )
-        stop = ["\n"] if tokenizer is not None else None
+        if tokenizer is None:
+            stop = None
+        elif getattr(args, "env", "textworld") == "gsm8k":
+            stop = ["</answer>"]  # R1-zero answers end at the closing tag (vllm_fsdp.py:1212-1217)
+        else:
+            stop = ["\n"]
         self.runner = InterruptibleGenerationRunner(
             self.engine, temperature=args.infer_temperature, top_p=args.infer_top_p, stop_sequences=stop,
             collect_logprobs=True,
@@ -55,6 +60,8 @@ class InferenceService:
         if stop is None:
             self.runner.stop_sequences = None
         self.total_tokens = 0
+        # bound on in-flight generation requests (the reference's actor max-concurrency knob)
+        self._slots = asyncio.Semaphore(int(getattr(args, "infer_actor_max_concurrency", 1 << 20)))
         self.next_request_index = 0
         self.stopped = False
         self.active_generation_tasks = set()
@@ -64,6 +71,10 @@ class InferenceService:
 
     # ------------------------------------------------------------------ generation
     async def request_batch(self, input_ids: List[int], infer_max_tokens: int) -> InferenceResult:
+        async with self._slots:
+            return await self._request(input_ids, infer_max_tokens)
+
+    async def _request(self, input_ids: List[int], infer_max_tokens: int) -> InferenceResult:
         if self.stopped:
             raise RuntimeError("InferenceService is stopped.")
         index = self.next_request_index

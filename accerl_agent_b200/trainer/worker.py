@@ -212,6 +212,8 @@ class TrainWorker:
         return self.replay_buffer.get_stats()
 
     def current_lr(self) -> float:
+        if getattr(self.args, "lr_schedule", "warmup_cosine") == "constant":
+            return float(self.args.learning_rate)
         return warmup_cosine_lr(self.optimizer_step, self.args.learning_rate, self.args.lr_warmup_steps,
                                 self.args.max_steps)
 

@@ -134,7 +134,7 @@ __global__ void logsoftmax_label_bwd_kernel(__nv_bfloat16* __restrict__ logits, 
 // Fused policy objective
 // ------------------------------------------------------------------------------------------------
 struct PolicyCfg {
-  int mode;  // 0 ppo, 1 gipo, 2 sapo
+  int mode;  // 0 ppo, 1 gipo, 2 sapo, 3 none (advantage x logprob, no ratio)
   float clip_eps, gipo_sigma, tau_pos, tau_neg, kl_coef, loss_scale;
 };
 
@@ -169,6 +169,9 @@ __global__ void policy_loss_kernel(const float* __restrict__ lp, const float* __
       const float coeff = expf(-0.5f * z * z);
       obj = r * A * coeff;
       dobj = A * coeff * r;
+    } else if (cfg.mode == 3) {
+      obj = A * lp[i];
+      dobj = A;
     } else {
       const float rc = fminf(fmaxf(r, 1e-6f), 1e6f);
       const float tau = A > 0.f ? cfg.tau_pos : cfg.tau_neg;

@@ -161,7 +161,7 @@ def test_logsoftmax_label_fwd_bwd():
     assert _rel(d, lf.grad) < 1e-2
 
 
-@pytest.mark.parametrize("mode", ["ppo", "gipo", "sapo"])
+@pytest.mark.parametrize("mode", ["ppo", "gipo", "sapo", "none"])
 def test_policy_loss_matches_autograd(mode):
     n = 5000
     lp = -torch.rand(n, device=DEV) * 5
