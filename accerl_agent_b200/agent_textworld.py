@@ -46,15 +46,14 @@ def device_plan(args):
     use_cuda = args.device != "cpu" and torch.cuda.is_available()
     world = args.fsdp_world_size
     n_engines = args.infer_size
-    if args.infer_tp_size != 1:
-        raise NotImplementedError("--infer-tp-size > 1 is not supported by this engine build; use --infer-size")
+    tp = args.infer_tp_size
     if not use_cuda:
-        return [None] * world, [None] * n_engines
-    need = world + n_engines * args.infer_tp_size
+        return [None] * world, [[None] * tp for _ in range(n_engines)]
+    need = world + n_engines * tp
     have = torch.cuda.device_count()
     if have < need:
         raise RuntimeError(f"need {need} GPUs (fsdp_world_size + infer_tp_size * infer_size), found {have}")
-    return list(range(world)), [world + i for i in range(n_engines)]
+    return list(range(world)), [[world + i * tp + j for j in range(tp)] for i in range(n_engines)]
 
 
 def sync_weights(engines, trainers, scope: str) -> Dict[str, float]:
@@ -62,7 +61,7 @@ def sync_weights(engines, trainers, scope: str) -> Dict[str, float]:
     for t in trainers:
         t.synchronize()
     t0 = time.perf_counter()
-    results = get([e.pull_weights.remote(numel) for e in engines])
+    results = get([e.pull_weights.remote(scope) for e in engines])
     elapsed = time.perf_counter() - t0
     nbytes = sum(r["bytes"] for r in results)
     dev_ms = max(r["device_ms"] for r in results)
@@ -85,6 +84,7 @@ def run_train(args) -> Dict[str, float]:
     addr = args.fsdp_master_addr or "127.0.0.1"
     port = args.fsdp_master_port or find_open_port()
     trainers, engines = [], []
+    followers: List[List] = []
     final: Dict[str, float] = {}
     try:
         trainers = [spawn_actor("accerl_agent_b200.trainer.actor:TrainerActor", args, r, world, addr, port,
@@ -96,13 +96,20 @@ def run_train(args) -> Dict[str, float]:
         assignment: List[List[int]] = [[] for _ in engine_devs]
         for wid in range(args.num_rollout_workers):
             assignment[wid % len(engine_devs)].append(wid)
-        engines = [spawn_actor("accerl_agent_b200.rollout.actor:InferenceActor", args, engine_devs[i], assignment[i],
-                               replay_queues, stats_queue, name=f"engine{i}", ready_timeout=None)
+        tp_ports = [find_open_port() for _ in engine_devs]
+        engines = [spawn_actor("accerl_agent_b200.rollout.actor:InferenceActor", args, engine_devs[i][0], assignment[i],
+                               replay_queues, stats_queue, tp_ports[i], name=f"engine{i}", ready_timeout=None)
                    for i in range(len(engine_devs))]
-        for e in engines:
+        followers = [[spawn_actor("accerl_agent_b200.rollout.actor:InferenceFollower", args, engine_devs[i][j], j,
+                                  tp_ports[i], name=f"engine{i}-tp{j}", ready_timeout=None)
+                      for j in range(1, args.infer_tp_size)] for i in range(len(engine_devs))]
+        for e in engines + [f for fs in followers for f in fs]:
             e.wait_ready(1800)
         for i, e in enumerate(engines):
-            e.attach_trainer_weights(get(trainers[i % world].export_weights_handle.remote()))
+            handle = get(trainers[i % world].export_weights_handle.remote())
+            e.attach_trainer_weights(handle)
+            for f in followers[i]:
+                f.attach_trainer_weights(handle)
         print("[sync] Initial full sync from trainers to engines...")
         get([e.pause_and_wait_idle.remote() for e in engines])
         sync_weights(engines, trainers, "all")
@@ -119,6 +126,11 @@ def run_train(args) -> Dict[str, float]:
                 err = get(e.check_workers.remote())
                 if err:
                     raise RuntimeError(f"A rollout worker exited unexpectedly: {err}")
+            for fs in followers:
+                for f in fs:
+                    err = f.check()
+                    if err:
+                        raise RuntimeError(f"A tensor-parallel engine rank failed: {err}")
             infer_start = sum(s["total_tokens"] for s in get([e.get_stats.remote() for e in engines]))
             t0 = time.perf_counter()
             summaries = get([t.train_until_next_sync.remote(args.sync_every_optimizer_steps) for t in trainers])
@@ -208,6 +220,13 @@ def run_train(args) -> Dict[str, float]:
             except Exception as exc:
                 print(f"[cleanup] Ignoring engine shutdown error: {exc!r}")
             e.stop_process()
+        for fs in followers:
+            for f in fs:
+                try:
+                    get(f.shutdown.remote(30), timeout=60)
+                except Exception as exc:
+                    print(f"[cleanup] Ignoring engine follower shutdown error: {exc!r}")
+                f.stop_process()
         for t in trainers:
             try:
                 get(t.close.remote(), timeout=60)

@@ -122,27 +122,111 @@ def bench_memory_bound(results):
 
 
 def profile_case(kind: str):
-    """One small launch of a kernel family (for ncu captures): attention fwd+bwd on 1 x 4096 tokens,
-    12 q / 2 kv heads; or the layer GEMMs of 4096 tokens of the 1.5B shape."""
+    """Small launches of one kernel family for ncu captures (each a few hundred MB at most, inputs
+    still larger than L2 where the kernel streams memory):
+
+    * ``attnprof``: attention fwd+bwd on 1 x 4096 tokens, 12 q / 2 kv heads (the 1.5B shape);
+    * ``gemmprof``: the gate_up GEMMs of 4096 tokens of the 1.5B shape (fwd, dgrad, wgrad);
+    * ``moeprof``: grouped expert GEMMs of 4096 tokens x top-4 over 60 experts (Qwen1.5-MoE shape);
+    * ``opsprof``: RMSNorm fwd/bwd, RoPE, SwiGLU fwd/bwd, embedding fwd/bwd, log-softmax/label
+      fwd/bwd on 4096 response rows of a 151936 vocabulary, policy loss, AdamW on 64 M parameters;
+    * ``decodeprof``: paged decode attention for 256 sequences of 1024 cached tokens, KV-cache write
+      and sampling of 256 rows of a 151936 vocabulary.
+    """
+    dev = "cuda"
     if kind == "attnprof":
         Hq, Hkv, D, T = 12, 2, 128, 4096
-        cu = torch.tensor([0, T], dtype=torch.int32, device="cuda")
-        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+        cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev).bfloat16()
         q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D : (Hq + Hkv) * D], qkv[:, (Hq + Hkv) * D :]
         for _ in range(2):
             o, lse = ops.attention_varlen(q, k, v, cu, T, Hq, Hkv, D)
             ops.attention_varlen_backward(torch.randn_like(o), q, k, v, o, lse, cu, T, Hq, Hkv, D)
     elif kind == "gemmprof":
         T, H, I = 4096, 1536, 8960
-        x = torch.randn(T, H, device="cuda").bfloat16()
-        w = torch.randn(2 * I, H, device="cuda").bfloat16()
-        gw = torch.zeros(2 * I, H, device="cuda")
+        x = torch.randn(T, H, device=dev).bfloat16()
+        w = torch.randn(2 * I, H, device=dev).bfloat16()
+        gw = torch.zeros(2 * I, H, device=dev)
         for _ in range(2):
             y = ops.gemm(x, w)
             ops.linear_dgrad(y, w)
             ops.linear_wgrad(y, x, gw)
+    elif kind == "moeprof":
+        from .models import moe
+
+        E, k, H, Im, T = 60, 4, 2048, 1408, 4096
+        g = torch.Generator().manual_seed(0)
+        counts = torch.bincount(torch.randint(0, E, (T * k,), generator=g), minlength=E).tolist()
+        lay = moe.padded_layout(counts, torch.device(dev))
+        R = lay["total"]
+        xs = torch.randn(R, H, device=dev).bfloat16()
+        wgu = (torch.randn(E * 2 * Im, H, device=dev) * 0.02).bfloat16()
+        wd = (torch.randn(E * H, Im, device=dev) * 0.02).bfloat16()
+        gu = torch.empty(R, 2 * Im, device=dev, dtype=torch.bfloat16)
+        ys = torch.empty(R, H, device=dev, dtype=torch.bfloat16)
+        gwd = torch.zeros(E * H, Im, device=dev)
+        for _ in range(2):
+            moe._grouped(xs, False, wgu, False, gu, R, 2 * Im, H, 1, lay, 2 * Im)
+            act = ops.swiglu(gu)
+            moe._grouped(act, False, wd, False, ys, R, H, Im, 1, lay, H)
+            moe._grouped(ys, True, act, True, gwd, H, Im, R, 2, lay, 0, H, beta=1.0)
+    elif kind == "opsprof":
+        from .algo.objectives import ObjectiveConfig
+
+        T, H, I, V = 16384, 1536, 8960, 151936
+        x = torch.randn(T, H, device=dev).bfloat16()
+        w = torch.ones(H, device=dev).bfloat16()
+        y, rstd = ops.rmsnorm(x, w, 1e-6)
+        dw = torch.zeros(H, device=dev)
+        ops.rmsnorm_backward(torch.randn_like(y), x, w, rstd, dw_grad=dw)
+        qkv = torch.randn(T, 16 * 128, device=dev).bfloat16()
+        pos = torch.arange(T, device=dev)
+        ops.rope_(qkv, pos, 14, 128, 1e6)
+        gu = torch.randn(T, 2 * I, device=dev).bfloat16()
+        a = ops.swiglu(gu)
+        ops.swiglu_backward(torch.randn_like(a), gu)
+        emb = torch.randn(V, H, device=dev).bfloat16()
+        ids = torch.randint(0, V, (T,), device=dev)
+        ops.embedding(ids, emb)
+        gemb = torch.zeros(V, H, device=dev)
+        ops.embedding_backward(ids, x, gemb)
+        n = 4096
+        logits = torch.randn(n, V, device=dev).bfloat16()
+        labels = torch.randint(0, V, (n,), device=dev)
+        lp, lse, ent = ops.logsoftmax_label(logits, labels, with_entropy=True)
+        ops.logsoftmax_label_backward(logits, labels, lse, torch.randn(n, device=dev))
+        adv = torch.randn(n, device=dev)
+        ops.policy_loss(lp, lp + 0.1 * torch.randn_like(lp), adv, ObjectiveConfig(), loss_scale=1e-4)
+        N = 64 << 20
+        master = torch.randn(N, device=dev)
+        m, v, gr = torch.zeros_like(master), torch.zeros_like(master), torch.randn_like(master)
+        pb = torch.empty(N, dtype=torch.bfloat16, device=dev)
+        ss = torch.zeros(1, dtype=torch.float64, device=dev)
+        ops.grad_sumsq(gr, ss)
+        ops.adamw_step(master, m, v, gr, pb, ss, 1e-6, 0.9, 0.999, 1e-8, 0.0, 1.0, 1)
+    elif kind == "decodeprof":
+        B, L, Hq, Hkv, D, bs, V = 256, 1024, 12, 2, 128, 16, 151936
+        nb = B * L // bs
+        kc = torch.randn(nb, bs, Hkv, D, device=dev).bfloat16()
+        vc = torch.randn(nb, bs, Hkv, D, device=dev).bfloat16()
+        tables = torch.arange(nb, device=dev, dtype=torch.int32).view(B, L // bs)
+        lens = torch.full((B,), L, device=dev, dtype=torch.int32)
+        q = torch.randn(B, Hq * D, device=dev).bfloat16()
+        for _ in range(2):
+            ops.paged_decode(q, kc, vc, tables, lens, Hq, Hkv, 1.0 / D ** 0.5, num_splits=4)
+        knew = torch.randn(B, Hkv * D, device=dev).bfloat16()
+        slots = (torch.arange(B, device=dev, dtype=torch.int32) * (L // bs)) * bs
+        ops.kv_cache_write(knew, knew, kc, vc, slots, Hkv)
+        logits = torch.randn(B, V, device=dev).bfloat16()
+        temp = torch.ones(B, device=dev)
+        seeds = torch.arange(B, device=dev, dtype=torch.int64)
+        offs = torch.zeros(B, device=dev, dtype=torch.int64)
+        ops.sample(logits, temp, seeds, offs)
     torch.cuda.synchronize()
     ops.check_status(torch.device("cuda"))
+
+
+PROFILE_CASES = ("attnprof", "gemmprof", "moeprof", "opsprof", "decodeprof")
 
 
 def main():
@@ -153,9 +237,12 @@ def main():
     peak_tf, _ = _peaks()
     results = {"peak_bf16_tflops_measured": peak_tf}
     sel = set(args.only.split(","))
-    if sel & {"attnprof", "gemmprof"}:
-        for kind in sel & {"attnprof", "gemmprof"}:
+    if "profall" in sel:
+        sel |= set(PROFILE_CASES)
+    if sel & set(PROFILE_CASES):
+        for kind in [c for c in PROFILE_CASES if c in sel]:
             profile_case(kind)
+            torch.cuda.empty_cache()  # keep the footprint (and ncu's save/restore) small
         print("profile case done")
         return
     if "gemm" in sel:

@@ -2,9 +2,11 @@
 (one GPU), the way rollout workers drive it (every request carries the whole growing transcript,
 16-token actions at temperature 1.0, prefix caching on).
 
-    python -m accerl_agent_b200.bench_rollout [--model qwen2.5-1.5b] [--groups 32] [--seconds 30]
+    python -m accerl_agent_b200.bench_rollout [--model qwen2.5-1.5b] [--groups 32] [--seconds 30] [--tp 2]
 
 Reports generated tokens/s (``Infer/TokensPerSec``), prefix-cache hit rate and engine step counts.
+``--tp N`` runs one tensor-parallel engine over GPUs 0..N-1 (rank 0 in this process, the others in
+spawned follower processes); every rank pulls its weight shard from a seeded full copy on its GPU.
 """
 
 from __future__ import annotations
@@ -38,6 +40,27 @@ async def _drive(service, args, groups: int, seconds: float):
     return (tok1 - tok0) / el, el, len(sink_samples)
 
 
+def _seed_weights(engine, dev):
+    """Every rank builds the same seeded full model on its GPU and pulls its shard from it."""
+    from .models.transformer import build_model
+
+    full = build_model(engine.full_cfg, "full", dev, torch.bfloat16)
+    full.init_weights(seed=0)
+    engine.set_weight_source(full.layout, addr=full.params.data_ptr())
+    return full
+
+
+def _follower(rank: int, tp: int, port: int, args):
+    from .rollout.inference import build_engine, init_tp_groups
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    engine = build_engine(args, dev, tp_groups=init_tp_groups(rank, tp, port, dev))
+    full = _seed_weights(engine, dev)
+    engine.serve_follower()
+    del full
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen2.5-1.5b")
@@ -46,6 +69,7 @@ def main():
     ap.add_argument("--max-num-seqs", type=int, default=256)
     ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
     ap.add_argument("--window", type=int, default=8192)
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks of the engine (GPUs 0..tp-1)")
     ap.add_argument("--json", default=None)
     a = ap.parse_args()
     args = make_args(model_path=a.model, env="synthetic", rl_algorithm="grpo", rollout_batch_size=8,
@@ -53,14 +77,37 @@ def main():
                      infer_max_tokens=16, infer_temperature=1.0, vllm_max_num_seqs=a.max_num_seqs,
                      vllm_max_num_batched_tokens=a.max_num_batched_tokens, kv_cache_gb=60.0)
     dev = torch.device("cuda", 0)
-    service = InferenceService(args, dev)
-    service.engine.model.init_weights(seed=0)
+    procs, full = [], None
+    if a.tp > 1:
+        import socket
+
+        import torch.multiprocessing as mp
+
+        from .rollout.inference import init_tp_groups
+
+        args.infer_tp_size = a.tp
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_follower, args=(r, a.tp, port, args)) for r in range(1, a.tp)]
+        for p in procs:
+            p.start()
+        service = InferenceService(args, dev, tp_groups=init_tp_groups(0, a.tp, port, dev))
+        full = _seed_weights(service.engine, dev)
+        service.engine.pull_weights("all")
+        del full
+        torch.cuda.empty_cache()
+    else:
+        service = InferenceService(args, dev)
+        service.engine.model.init_weights(seed=0)
     rate, el, samples = asyncio.run(_drive(service, args, a.groups, a.seconds))
     st = service.get_stats()
     out = {
         "metric": "rollout tok/s",
         "value": round(rate, 1),
-        "unit": "generated tokens/s (Infer/TokensPerSec), one engine GPU",
+        "unit": f"generated tokens/s (Infer/TokensPerSec), one engine on {a.tp} GPU(s)",
+        "tp": a.tp,
         "model": a.model,
         "concurrent_trajectories": a.groups * 8,
         "max_num_seqs": a.max_num_seqs,
@@ -75,6 +122,8 @@ def main():
         with open(a.json, "w") as f:
             json.dump(out, f, indent=1)
     asyncio.run(service.shutdown())
+    for p in procs:
+        p.join(120)
 
 
 if __name__ == "__main__":

@@ -37,6 +37,10 @@ class ModelConfig:
     norm_topk_prob: bool = False
     decoder_sparse_step: int = 1
     mlp_only_layers: List[int] = field(default_factory=list)
+    # tensor-parallel engine shards: routed experts stored on this rank and the global index of the
+    # first one (None: all experts)
+    local_experts: Optional[int] = None
+    expert_offset: int = 0
     torch_dtype: str = "bfloat16"
     bos_token_id: int = 151643
     eos_token_id: int = 151645

@@ -127,7 +127,7 @@ def _grouped(a, a_mn, b, b_mn, out, M, N, K, mode, lay, b_stride, c_stride=0, be
 def experts_forward_grouped(model, layer: int, xs_pad: torch.Tensor, lay):
     cfg = model.cfg
     p = f"model.layers.{layer}.mlp.experts."
-    E, Im, H = cfg.num_experts, cfg.moe_intermediate_size, cfg.hidden_size
+    E, Im, H = model.w(p + "gate_up_proj").shape[0], cfg.moe_intermediate_size, cfg.hidden_size
     Wgu = model.w(p + "gate_up_proj").reshape(E * 2 * Im, H)
     Wd = model.w(p + "down_proj").reshape(E * H, Im)
     R = lay["total"]
@@ -166,6 +166,14 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     probs, topw, topi = route(model, layer, h)
     w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
+    El = cfg.local_experts
+    if El is not None and El != cfg.num_experts:
+        # tensor-parallel engine shard: only the (token, slot) pairs routed to this rank's experts;
+        # the caller all-reduces the partial outputs of the ranks
+        lo = cfg.expert_offset
+        a, b = bounds[lo], bounds[lo + El]
+        order, counts = order[a:b], counts[lo : lo + El]
+        bounds = [x - a for x in bounds[lo : lo + El + 1]]
     tok = torch.div(order, k, rounding_mode="floor")
     ep = getattr(model, "expert_parallel", None)
     lay = None
@@ -177,7 +185,7 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     elif h.is_cuda and h.dtype == torch.bfloat16:
         lay = padded_layout(counts.tolist(), h.device)
         # row of every (token, slot) pair inside its expert's padded segment
-        seg = torch.tensor([lay["starts"][e] - bounds[e] for e in range(cfg.num_experts)], device=h.device)
+        seg = torch.tensor([lay["starts"][e] - bounds[e] for e in range(len(counts))], device=h.device)
         pos = torch.arange(order.numel(), device=h.device) + seg.repeat_interleave(counts)
         xs = torch.zeros(lay["total"], h.shape[1], dtype=h.dtype, device=h.device)
         xs.index_copy_(0, pos, h.index_select(0, tok))

@@ -40,9 +40,10 @@ def parameter_specs(cfg: ModelConfig) -> List[Tuple[str, Tuple[int, ...]]]:
         specs.append((p + "post_attention_layernorm.weight", (H,)))
         if cfg.layer_is_moe(layer):
             E, Im = cfg.num_experts, cfg.moe_intermediate_size
+            El = cfg.local_experts or E
             specs.append((p + "mlp.gate.weight", (E, H)))
-            specs.append((p + "mlp.experts.gate_up_proj", (E, 2 * Im, H)))
-            specs.append((p + "mlp.experts.down_proj", (E, H, Im)))
+            specs.append((p + "mlp.experts.gate_up_proj", (El, 2 * Im, H)))
+            specs.append((p + "mlp.experts.down_proj", (El, H, Im)))
             if cfg.shared_expert_intermediate_size > 0:
                 Is = cfg.shared_expert_intermediate_size
                 specs.append((p + "mlp.shared_expert.gate_up_proj.weight", (2 * Is, H)))

@@ -388,6 +388,13 @@ def policy_loss(lp, old_lp, adv, cfg, loss_scale: float):
     return g, stats
 
 
+def weight_pull(plan, src_addr: int, dst: torch.Tensor) -> None:
+    """Run a copy plan (``weight_map.descs_tensor``) from the device address ``src_addr`` (a peer
+    GPU's buffer mapped by CUDA IPC, or a local one) into ``dst``."""
+    desc, unit_start, n_units = plan
+    native().weight_pull(desc, unit_start, n_units, int(src_addr), dst)
+
+
 def grad_sumsq(flat_grad: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:
         out = torch.zeros(1, dtype=torch.float64, device=flat_grad.device)

@@ -15,7 +15,10 @@ import torch
 
 
 class InferenceActor:
-    def __init__(self, args, device_index: Optional[int], worker_ids: List[int], replay_queues, stats_queue):
+    def __init__(self, args, device_index: Optional[int], worker_ids: List[int], replay_queues, stats_queue,
+                 tp_port: Optional[int] = None):
+        """Rank 0 of an engine. With ``--infer-tp-size`` > 1 the other ranks are ``InferenceFollower``
+        actors joined through ``tp_port``; this rank schedules and broadcasts every step."""
         from ..trainer.actor import _load_tokenizer
         from .inference import InferenceService
         from .worker import RolloutWorker
@@ -36,7 +39,12 @@ class InferenceActor:
                                        vocab_size=resolve_model_config(args.model_path).vocab_size, fallback=True)
         else:
             tokenizer = None
-        self.service = InferenceService(args, device, tokenizer=tokenizer)
+        tp_groups = None
+        if getattr(args, "infer_tp_size", 1) > 1:
+            from .inference import init_tp_groups
+
+            tp_groups = init_tp_groups(0, args.infer_tp_size, tp_port, device)
+        self.service = InferenceService(args, device, tokenizer=tokenizer, tp_groups=tp_groups)
         world = len(replay_queues)
 
         def sink_for(wid):
@@ -86,8 +94,8 @@ class InferenceActor:
     def attach_trainer_weights(self, handle) -> int:
         return self.service.attach_trainer_weights(handle)
 
-    def pull_weights(self, numel: Optional[int] = None) -> Dict[str, float]:
-        return self.service.pull_weights(numel)
+    def pull_weights(self, scope: Any = "all") -> Dict[str, float]:
+        return self.service.pull_weights(scope)
 
     def get_stats(self) -> Dict[str, Any]:
         return self.service.get_stats()
@@ -99,3 +107,48 @@ class InferenceActor:
             if not t.done():
                 t.cancel()
         return await self.service.shutdown()
+
+
+class InferenceFollower:
+    """Rank > 0 of a tensor-parallel engine: holds its weight and KV-cache shards and replays the
+    steps, weight pulls and cache commands broadcast by rank 0 on a background thread."""
+
+    def __init__(self, args, device_index: Optional[int], tp_rank: int, tp_port: int):
+        import threading
+
+        from .inference import build_engine, init_tp_groups
+
+        if device_index is not None and torch.cuda.is_available():
+            device = torch.device("cuda", device_index)
+            torch.cuda.set_device(device)
+        else:
+            device = torch.device("cpu")
+        self.args = args
+        self.device = device
+        groups = init_tp_groups(tp_rank, args.infer_tp_size, tp_port, device)
+        self.engine = build_engine(args, device, tp_groups=groups)
+        self._ipc_bases: List[int] = []
+        self.error: Optional[str] = None
+        self._thread = threading.Thread(target=self._serve, name="tp-follower", daemon=True)
+        self._thread.start()
+
+    def _serve(self) -> None:
+        try:
+            self.engine.serve_follower()
+        except BaseException as exc:  # reported through check()
+            self.error = repr(exc)
+
+    def attach_trainer_weights(self, handle) -> int:
+        from .inference import attach_weight_source
+
+        return attach_weight_source(self.engine, self.args, self.device, handle, self._ipc_bases)
+
+    def check(self) -> Optional[str]:
+        if self.error:
+            return self.error
+        return None if self._thread.is_alive() else "follower loop exited"
+
+    def shutdown(self, timeout: float = 60.0) -> bool:
+        """Wait for the loop to end (rank 0 sends the stop command when it shuts down)."""
+        self._thread.join(timeout)
+        return not self._thread.is_alive()

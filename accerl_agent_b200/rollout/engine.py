@@ -101,7 +101,34 @@ class GenerationEngine:
         seed: int = 0,
         decode_splits: Optional[int] = None,
         use_cuda_graphs: bool = True,
+        layout: Optional[ParamLayout] = None,
+        tp_group=None,
+        cmd_group=None,
     ):
+        """``layout``: flat parameter layout of the engine (default: the full-model layout); pass the
+        trainer's layout to make weight syncs plain range copies. ``tp_group``/``cmd_group``: process
+        groups of a tensor-parallel engine (NCCL for the activations' all-reduce, gloo for the step
+        commands the leader, group rank 0, broadcasts); rank r then holds the r-th shard of every
+        tensor-parallel weight and ranks > 0 run ``serve_follower``."""
+        self.full_cfg = cfg
+        self.tp_group = tp_group
+        self.cmd_group = cmd_group
+        if tp_group is not None:
+            import torch.distributed as dist
+
+            self.tp = dist.get_world_size(tp_group)
+            self.tp_rank = dist.get_rank(tp_group)
+            self._cmd_src = dist.get_global_rank(cmd_group, 0)
+        else:
+            self.tp, self.tp_rank, self._cmd_src = 1, 0, 0
+        self._followers_stopped = False
+        if self.tp > 1:
+            from .weight_map import tp_shard_config
+
+            cfg = tp_shard_config(cfg, self.tp)
+            if cfg.local_experts:
+                cfg.expert_offset = self.tp_rank * cfg.local_experts
+            layout = None
         self.cfg = cfg
         self.device = device
         self.dtype = dtype
@@ -110,7 +137,9 @@ class GenerationEngine:
         self.max_model_len = max_model_len or cfg.max_position_embeddings
         self.block_size = block_size
         self.tokenizer = tokenizer
-        self.layout = ParamLayout.build(cfg, "full")
+        self.layout = layout or ParamLayout.build(cfg, "full")
+        self._weight_src = None
+        self._weight_maps: Dict[str, Any] = {}
         if params is None:
             params = torch.zeros(self.layout.total_numel, dtype=dtype, device=device)
         self.model = CausalLM(cfg, self.layout, params, None)
@@ -130,7 +159,9 @@ class GenerationEngine:
         self.allocator = BlockAllocator(num_blocks, block_size, enable_prefix_caching)
         # block 0 is never handed to a sequence: padded rows of captured decode graphs point at it
         self.scratch_block = self.allocator.allocate()
-        self.use_cuda_graphs = use_cuda_graphs and device.type == "cuda" and not cfg.is_moe
+        # MoE steps synchronise with the host (routing counts); tensor-parallel steps all-reduce through
+        # NCCL, which stays outside graph capture here: both run eagerly
+        self.use_cuda_graphs = use_cuda_graphs and device.type == "cuda" and not cfg.is_moe and self.tp == 1
         self._graphs: Dict[Any, Any] = {}
         self._graph_pool = None
         self.waiting: Deque[_Seq] = deque()
@@ -260,6 +291,48 @@ class GenerationEngine:
                     dst.copy_(src, non_blocking=True)
             else:
                 dst.copy_(src, non_blocking=True)
+
+    def set_weight_source(self, src_layout: ParamLayout, tensor: Optional[torch.Tensor] = None,
+                          addr: Optional[int] = None) -> None:
+        """Register the trainer's flat bf16 buffer (a tensor, or a device address mapped by CUDA IPC)
+        and precompute this rank's copy plans for the ``all`` and ``trainable`` scopes."""
+        from .weight_map import build_weight_map, descs_tensor
+
+        maps = {}
+        for scope in ("all", "trainable"):
+            descs = build_weight_map(self.full_cfg, src_layout, self.layout, self.tp_rank, self.tp, scope)
+            maps[scope] = (descs, descs_tensor(descs, self.device) if self.device.type == "cuda" else None)
+        self._weight_maps = maps
+        self._weight_src = (tensor, addr)
+
+    def pull_weights(self, scope: str = "all") -> int:
+        """Copy this engine's slice of the registered trainer buffer into its weights (every TP rank
+        pulls its own shard). Returns the bytes this rank copied."""
+        with self._step_lock:
+            if self.tp > 1 and self.tp_rank == 0:
+                import torch.distributed as dist
+
+                self._cmd(("pull", scope))
+                n = self._pull_local(scope)
+                dist.barrier(group=self.cmd_group)
+                return n
+            return self._pull_local(scope)
+
+    def _pull_local(self, scope: str) -> int:
+        from .weight_map import apply_map_torch, map_bytes
+
+        if self._weight_src is None:
+            raise RuntimeError("set_weight_source() was not called")
+        descs, descs_d = self._weight_maps[scope]
+        tensor, addr = self._weight_src
+        dst = self.model.params
+        if addr is not None:
+            with torch.cuda.device(self.device):
+                ops.weight_pull(descs_d, addr, dst)
+                torch.cuda.synchronize(self.device)
+        else:
+            apply_map_torch(tensor, dst, descs)
+        return map_bytes(descs, dst.element_size())
 
     def get_stats(self) -> Dict[str, Any]:
         with self._lock:
@@ -397,12 +470,25 @@ class GenerationEngine:
     # ------------------------------------------------------------------ CUDA-graph decode
     _BUCKETS = (8, 16, 32, 64, 128, 256, 512)
 
-    def _decode_core(self, ids_d, pos_d, slots_d, table_d, lens_d, temps_d, seeds_d, offs_d, splits: int):
-        """Forward of single-token rows (every row samples): returns (tokens, logprobs) on device."""
-        cfg, m, dev = self.cfg, self.model, self.device
+    # ------------------------------------------------------------------ model forward
+    def _all_reduce(self, y: torch.Tensor) -> torch.Tensor:
+        if self.tp > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(y, group=self.tp_group)
+        return y
+
+    def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """``residual + a @ w^T`` for a row-parallel weight: every rank multiplies its column slice,
+        rank 0 adds the residual in the GEMM epilogue, and the partial sums are all-reduced."""
+        y = ops.linear(a, w, residual=residual if self.tp_rank == 0 else None)
+        return self._all_reduce(y)
+
+    def _forward_layers(self, x, pos_d, slots_d, attn_fn):
+        """Decoder layers over rows ``x``; ``attn_fn(layer, q, k_cache, v_cache)`` returns the
+        attention output rows. Returns the final hidden rows (before the last norm)."""
+        cfg, m = self.cfg, self.model
         D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
-        scale = 1.0 / math.sqrt(D)
-        x = ops.embedding(ids_d, m.w("model.embed_tokens.weight"))
         for layer in range(cfg.num_hidden_layers):
             p = f"model.layers.{layer}."
             h1, _ = ops.rmsnorm(x, m.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
@@ -416,11 +502,34 @@ class GenerationEngine:
             v = qkv[:, cfg.q_dim + cfg.kv_dim :]
             kc, vc = self.k_cache[layer], self.v_cache[layer]
             ops.kv_cache_write(k, v, kc, vc, slots_d, Hkv)
-            attn = ops.paged_decode(q, kc, vc, table_d, lens_d, Hq, Hkv, scale, num_splits=splits)
-            x = ops.linear(attn, m.w(p + "self_attn.o_proj.weight"), residual=x)
+            attn = attn_fn(layer, q, kc, vc)
+            x = self._row_parallel(attn, m.w(p + "self_attn.o_proj.weight"), x)
             h2, _ = ops.rmsnorm(x, m.w(p + "post_attention_layernorm.weight"), cfg.rms_norm_eps)
-            gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
-            x = ops.linear(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), residual=x)
+            if cfg.layer_is_moe(layer):
+                from ..models.moe import moe_forward
+
+                res = x if self.tp_rank == 0 else torch.zeros_like(x)
+                x, _ = moe_forward(m, layer, h2, res, save=False)
+                x = self._all_reduce(x)
+            else:
+                gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
+                x = self._row_parallel(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), x)
+        return x
+
+    # ------------------------------------------------------------------ CUDA-graph decode
+    _BUCKETS = (8, 16, 32, 64, 128, 256, 512)
+
+    def _decode_core(self, ids_d, pos_d, slots_d, table_d, lens_d, temps_d, seeds_d, offs_d, splits: int):
+        """Forward of single-token rows (every row samples): returns (tokens, logprobs) on device."""
+        cfg, m = self.cfg, self.model
+        scale = 1.0 / math.sqrt(cfg.head_dim)
+        Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+
+        def attn_fn(layer, q, kc, vc):
+            return ops.paged_decode(q, kc, vc, table_d, lens_d, Hq, Hkv, scale, num_splits=splits)
+
+        x = ops.embedding(ids_d, m.w("model.embed_tokens.weight"))
+        x = self._forward_layers(x, pos_d, slots_d, attn_fn)
         hN, _ = ops.rmsnorm(x, m.w("model.norm.weight"), cfg.rms_norm_eps)
         logits = ops.linear(hN, m.w(m.lm_head_name))
         return ops.sample(logits, temps_d, seeds_d, offs_d)
@@ -469,15 +578,15 @@ class GenerationEngine:
         self._graphs[key] = g
         return g
 
-    def _execute_decode_graph(self, order):
+    def _graph_meta(self, order) -> Optional[Dict[str, Any]]:
+        """Host inputs of one decode-graph replay (None when the batch exceeds every bucket)."""
         bs = self.block_size
         B = len(order)
         bucket = next((b for b in self._BUCKETS if b >= B), None)
         if bucket is None:
-            return self._execute(order, 0)
+            return None
         width = max(len(s.blocks) for s, *_ in order)
         width = (width + 63) // 64 * 64
-        g = self._graph_for(bucket, width)
         host = np.zeros(bucket * (5 + width), dtype=np.int64)
         host[2 * bucket : 3 * bucket] = -1
         host[3 * bucket : 4 * bucket] = 1
@@ -495,17 +604,28 @@ class GenerationEngine:
             table[j, : len(blk)] = blk
             temps[j] = float(seq.params.temperature)
             offs[j] = len(seq.out)
-        g["meta"].copy_(torch.from_numpy(host), non_blocking=False)
-        g["temps"].copy_(torch.from_numpy(temps))
-        g["offs"].copy_(torch.from_numpy(offs))
+        return {"kind": "graph", "B": B, "bucket": bucket, "width": width, "host": host, "temps": temps, "offs": offs}
+
+    def _run_graph(self, meta):
+        g = self._graph_for(meta["bucket"], meta["width"])
+        g["meta"].copy_(torch.from_numpy(meta["host"]), non_blocking=False)
+        g["temps"].copy_(torch.from_numpy(meta["temps"]))
+        g["offs"].copy_(torch.from_numpy(meta["offs"]))
         g["graph"].replay()
+        B = meta["B"]
         res = torch.stack([g["tok"][:B].double(), g["lp"][:B].double()]).cpu()
         return res[0].long().tolist(), res[1].tolist()
 
-    def _execute(self, order, n_prefill: int):
-        cfg = self.cfg
+    def _execute_decode_graph(self, order):
+        meta = self._graph_meta(order)
+        if meta is None:
+            return self._execute(order, 0)
+        self._send_step(meta)
+        return self._run_graph(meta)
+
+    def _exec_meta(self, order, n_prefill: int) -> Dict[str, Any]:
+        """Host inputs of one eager step over ``order`` (first ``n_prefill`` entries are prefill chunks)."""
         bs = self.block_size
-        dev = self.device
         ids: List[int] = []
         pos: List[int] = []
         slots: List[int] = []
@@ -530,17 +650,42 @@ class GenerationEngine:
                 pk = np.arange(ctx)
                 k_slots.extend((blocks[pk // bs] * bs + pk % bs).tolist())
                 max_q = max(max_q, n)
-        Tp = cu_q[-1]
         decode = order[n_prefill:]
         nd = len(decode)
-        # one host->device transfer for all index data
         header = [len(ids), len(pos), len(slots), len(sample_rows), len(cu_q), len(cu_k), len(k_slots)]
         flat = np.concatenate([
             np.asarray(ids, np.int64), np.asarray(pos, np.int64), np.asarray(slots, np.int64),
             np.asarray(sample_rows, np.int64), np.asarray(cu_q, np.int64), np.asarray(cu_k, np.int64),
             np.asarray(k_slots, np.int64),
         ])
-        host = torch.from_numpy(flat)
+        meta: Dict[str, Any] = {"kind": "exec", "header": header, "flat": flat, "Tp": cu_q[-1], "max_q": max_q,
+                                "nd": nd}
+        if nd:
+            max_blocks = max(len(s.blocks) for s, *_ in decode)
+            table = np.zeros((nd, max_blocks), np.int32)
+            lens = np.zeros(nd, np.int32)
+            for j, (sq, start, n, _) in enumerate(decode):
+                table[j, : len(sq.blocks)] = sq.blocks
+                lens[j] = start + n
+            meta["table"], meta["lens"] = table, lens
+        sampled = [e for e in order if e[3]]
+        meta["temps"] = np.asarray([float(sq.params.temperature) for sq, *_ in sampled], np.float32)
+        meta["seeds"] = np.asarray([sq.seed for sq, *_ in sampled], np.int64)
+        meta["offs"] = np.asarray([len(sq.out) for sq, *_ in sampled], np.int64)
+        if any(sq.params.top_p < 1.0 or (sq.params.top_k or -1) > 0 for sq, *_ in sampled):
+            meta["filter_params"] = [sq.params for sq, *_ in sampled]
+        return meta
+
+    def _execute(self, order, n_prefill: int):
+        meta = self._exec_meta(order, n_prefill)
+        self._send_step(meta)
+        return self._run_exec(meta)
+
+    def _run_exec(self, meta):
+        cfg = self.cfg
+        dev = self.device
+        header, Tp, max_q, nd = meta["header"], meta["Tp"], meta["max_q"], meta["nd"]
+        host = torch.from_numpy(meta["flat"])
         if dev.type == "cuda":
             host = host.pin_memory()
         d = host.to(dev, non_blocking=True)
@@ -553,71 +698,89 @@ class GenerationEngine:
         cu_k_d = d[off[5] : off[6]].to(torch.int32)
         kslots_d = d[off[6] : off[7]]
         if nd:
-            max_blocks = max(len(s.blocks) for s, *_ in decode)
-            table = np.zeros((nd, max_blocks), np.int32)
-            lens = np.zeros(nd, np.int32)
-            for j, (s, start, n, _) in enumerate(decode):
-                table[j, : len(s.blocks)] = s.blocks
-                lens[j] = start + n
+            table, lens = meta["table"], meta["lens"]
+            max_blocks = table.shape[1]
             dt = torch.from_numpy(np.concatenate([table.reshape(-1), lens]))
             if dev.type == "cuda":
                 dt = dt.pin_memory()
             dt = dt.to(dev, non_blocking=True)
             table_d = dt[: nd * max_blocks].view(nd, max_blocks)
             lens_d = dt[nd * max_blocks :]
-            max_len = int(lens.max())
         m = self.model
         D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         scale = 1.0 / math.sqrt(D)
         splits = self.decode_splits or max(1, min(16, (148 * 2) // max(nd * Hkv, 1)))
+
+        def attn_fn(layer, q, kc, vc):
+            attn = torch.empty(q.shape[0], cfg.q_dim, dtype=q.dtype, device=dev)
+            if Tp:
+                kctx = kc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
+                vctx = vc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
+                ops.attention_varlen(q[:Tp], kctx, vctx, cu_q_d, max_q, Hq, Hkv, D, scale=scale,
+                                     out=attn[:Tp], cu_seqlens_k=cu_k_d)
+            if nd:
+                ops.paged_decode(q[Tp:], kc, vc, table_d, lens_d, Hq, Hkv, scale, num_splits=splits,
+                                 out=attn[Tp:])
+            return attn
+
         with torch.no_grad():
             x = ops.embedding(ids_d, m.w("model.embed_tokens.weight"))
-            for layer in range(cfg.num_hidden_layers):
-                p = f"model.layers.{layer}."
-                h1, _ = ops.rmsnorm(x, m.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
-                bias = m.w(p + "self_attn.qkv_proj.bias") if cfg.qkv_bias else None
-                qkv = ops.linear(h1, m.w(p + "self_attn.qkv_proj.weight"), bias=bias)
-                if cfg.qk_norm:
-                    m._qk_norm_forward(layer, qkv)
-                ops.rope_(qkv, pos_d, Hq + Hkv, D, cfg.rope_theta)
-                q = qkv[:, : cfg.q_dim]
-                k = qkv[:, cfg.q_dim : cfg.q_dim + cfg.kv_dim]
-                v = qkv[:, cfg.q_dim + cfg.kv_dim :]
-                kc, vc = self.k_cache[layer], self.v_cache[layer]
-                ops.kv_cache_write(k, v, kc, vc, slots_d, Hkv)
-                attn = torch.empty(x.shape[0], cfg.q_dim, dtype=x.dtype, device=dev)
-                if Tp:
-                    kctx = kc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
-                    vctx = vc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
-                    ops.attention_varlen(q[:Tp], kctx, vctx, cu_q_d, max_q, Hq, Hkv, D, scale=scale,
-                                         out=attn[:Tp], cu_seqlens_k=cu_k_d)
-                if nd:
-                    ops.paged_decode(q[Tp:], kc, vc, table_d, lens_d, Hq, Hkv, scale, num_splits=splits,
-                                     out=attn[Tp:])
-                x = ops.linear(attn, m.w(p + "self_attn.o_proj.weight"), residual=x)
-                h2, _ = ops.rmsnorm(x, m.w(p + "post_attention_layernorm.weight"), cfg.rms_norm_eps)
-                if cfg.layer_is_moe(layer):
-                    from ..models.moe import moe_forward
-
-                    x, _ = moe_forward(m, layer, h2, x, save=False)
-                else:
-                    gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
-                    x = ops.linear(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), residual=x)
-            if not sample_rows:
+            x = self._forward_layers(x, pos_d, slots_d, attn_fn)
+            if header[3] == 0:
                 return [], []
             xs = x.index_select(0, rows_d)
             hN, _ = ops.rmsnorm(xs, m.w("model.norm.weight"), cfg.rms_norm_eps)
             logits = ops.linear(hN, m.w(m.lm_head_name))
-            sampled = [e for e in order if e[3]]
-            temps = torch.tensor([float(s.params.temperature) for s, *_ in sampled], dtype=torch.float32)
-            seeds = torch.tensor([s.seed for s, *_ in sampled], dtype=torch.int64)
-            offs = torch.tensor([len(s.out) for s, *_ in sampled], dtype=torch.int64)
-            if any(s.params.top_p < 1.0 or (s.params.top_k or -1) > 0 for s, *_ in sampled):
-                tokens, lps = _sample_filtered(logits, [s.params for s, *_ in sampled], seeds)
+            seeds = torch.from_numpy(meta["seeds"])
+            if "filter_params" in meta:
+                tokens, lps = _sample_filtered(logits, meta["filter_params"], seeds)
             else:
-                tokens, lps = ops.sample(logits, temps.to(dev), seeds.to(dev), offs.to(dev))
+                tokens, lps = ops.sample(logits, torch.from_numpy(meta["temps"]).to(dev), seeds.to(dev),
+                                         torch.from_numpy(meta["offs"]).to(dev))
             res = torch.stack([tokens.double(), lps.double()]).cpu()  # the one device->host read per step
         return res[0].long().tolist(), res[1].tolist()
+
+    # ------------------------------------------------------------------ tensor-parallel followers
+    def _send_step(self, meta) -> None:
+        """Leader: hand the step's host inputs to the follower ranks before running it."""
+        if self.tp > 1 and self.tp_rank == 0:
+            self._cmd(("step", meta))
+
+    def _cmd(self, msg) -> None:
+        import torch.distributed as dist
+
+        obj = [msg]
+        dist.broadcast_object_list(obj, src=self._cmd_src, group=self.cmd_group)
+
+    def serve_follower(self) -> None:
+        """Follower ranks: run every step, weight pull and cache command the leader broadcasts, until
+        ``stop``. Sampled tokens are computed (the math is replicated) and discarded."""
+        import torch.distributed as dist
+
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        while True:
+            obj = [None]
+            dist.broadcast_object_list(obj, src=self._cmd_src, group=self.cmd_group)
+            kind, payload = obj[0]
+            if kind == "stop":
+                return
+            if kind == "step":
+                if payload["kind"] == "graph":
+                    self._run_graph(payload)
+                else:
+                    self._run_exec(payload)
+            elif kind == "pull":
+                self._pull_local(payload)
+                dist.barrier(group=self.cmd_group)
+            elif kind == "clear_graphs":
+                self._graphs.clear()
+
+    def stop_followers(self) -> None:
+        with self._step_lock:
+            if self.tp > 1 and self.tp_rank == 0 and not self._followers_stopped:
+                self._followers_stopped = True
+                self._cmd(("stop", None))
 
     def _postprocess(self, order, tokens: List[int], logps: List[float]) -> None:
         bs = self.block_size

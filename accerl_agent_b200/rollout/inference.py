@@ -7,10 +7,11 @@ the runner, aborts the engine's in-flight requests with their KV cache cleared a
 attempt has drained; ``resume_generation(increment_version)`` bumps the policy version.
 
 Weight sync: a trainer rank exports its flat bf16 parameter buffer once (a CUDA IPC handle, or a
-shared-memory handle on CPU); ``attach_trainer_weights`` maps it into this process and
-``pull_weights(scope_numel)`` copies the requested prefix (all parameters, or only the contiguous
-trainable segment) straight from trainer memory into the engine's identical fused layout over NVLink,
-timed with CUDA events.
+shared-memory handle on CPU); ``attach_trainer_weights`` maps it into this process (opened on this
+engine's device) together with the trainer's parameter layout, and ``pull_weights(scope)`` copies
+the engine's slice of every parameter (``all``, or only the ``trainable`` ones) straight from trainer
+memory into the engine's fused layout with one copy-plan kernel over NVLink, timed with CUDA events.
+Tensor-parallel engines pull on every rank, each its own shard.
 """
 
 from __future__ import annotations
@@ -26,27 +27,50 @@ from .engine import GenerationEngine
 from .generation import InferenceResult, InterruptibleGenerationRunner, OnlineGenerationState
 
 
+def init_tp_groups(tp_rank: int, tp_size: int, port: int, device: torch.device):
+    """Process groups of one tensor-parallel engine (its ranks only): the default group carries the
+    activations' all-reduces (NCCL on GPUs), a gloo group carries the leader's step commands."""
+    import datetime
+
+    import torch.distributed as dist
+
+    backend = "nccl" if device.type == "cuda" else "gloo"
+    kw = {"device_id": device} if device.type == "cuda" else {}
+    dist.init_process_group(backend, init_method=f"tcp://127.0.0.1:{port}", rank=tp_rank, world_size=tp_size,
+                            timeout=datetime.timedelta(seconds=600), **kw)
+    return dist.group.WORLD, dist.new_group(backend="gloo")
+
+
+def build_engine(args, device: torch.device, tokenizer=None, dtype: Optional[torch.dtype] = None,
+                 tp_groups=None) -> GenerationEngine:
+    cfg = resolve_model_config(args.model_path)
+    dtype = dtype or (torch.bfloat16 if device.type == "cuda" else torch.float32)
+    tp_group, cmd_group = tp_groups if tp_groups else (None, None)
+    return GenerationEngine(
+        cfg,
+        device,
+        dtype,
+        max_num_seqs=args.vllm_max_num_seqs,
+        max_num_batched_tokens=args.vllm_max_num_batched_tokens,
+        max_model_len=args.vllm_max_model_len,
+        block_size=getattr(args, "kv_block_size", 16),
+        kv_cache_gb=getattr(args, "kv_cache_gb", None),
+        enable_prefix_caching=not args.disable_vllm_prefix_caching,
+        tokenizer=tokenizer,
+        tp_group=tp_group,
+        cmd_group=cmd_group,
+    )
+
+
 class InferenceService:
-    def __init__(self, args, device: torch.device, tokenizer=None, dtype: Optional[torch.dtype] = None):
+    def __init__(self, args, device: torch.device, tokenizer=None, dtype: Optional[torch.dtype] = None,
+                 tp_groups=None):
         self.args = args
         self.device = device
         if device.type == "cuda":
             torch.cuda.set_device(device)
-        cfg = resolve_model_config(args.model_path)
-        self.cfg = cfg
-        dtype = dtype or (torch.bfloat16 if device.type == "cuda" else torch.float32)
-        self.engine = GenerationEngine(
-            cfg,
-            device,
-            dtype,
-            max_num_seqs=args.vllm_max_num_seqs,
-            max_num_batched_tokens=args.vllm_max_num_batched_tokens,
-            max_model_len=args.vllm_max_model_len,
-            block_size=getattr(args, "kv_block_size", 16),
-            kv_cache_gb=getattr(args, "kv_cache_gb", None),
-            enable_prefix_caching=not args.disable_vllm_prefix_caching,
-            tokenizer=tokenizer,
-        )
+        self.engine = build_engine(args, device, tokenizer, dtype, tp_groups)
+        self.cfg = self.engine.full_cfg
         if tokenizer is None:
             stop = None
         elif getattr(args, "env", "textworld") == "gsm8k":
@@ -65,7 +89,7 @@ class InferenceService:
         self.next_request_index = 0
         self.stopped = False
         self.active_generation_tasks = set()
-        self._trainer_params: Optional[torch.Tensor] = None
+        self._ipc_bases: List[int] = []
         self.last_sync: Dict[str, float] = {}
         self.engine.start()
 
@@ -113,33 +137,28 @@ class InferenceService:
 
     # ------------------------------------------------------------------ weights
     def attach_trainer_weights(self, handle) -> int:
-        """Map a trainer's exported flat parameter buffer into this process."""
-        fn, fargs = handle
-        self._trainer_params = fn(*fargs)
-        if self._trainer_params.numel() < self.engine.layout.total_numel:
-            raise ValueError("trainer parameter buffer is smaller than the engine layout")
-        return int(self._trainer_params.numel())
+        """Map a trainer's exported flat parameter buffer into this process and register it (with the
+        trainer's layout) as the engine's weight source. Returns the buffer's element count."""
+        return attach_weight_source(self.engine, self.args, self.device, handle, self._ipc_bases)
 
-    def pull_weights(self, numel: Optional[int] = None) -> Dict[str, float]:
-        """Copy the first ``numel`` elements (default: everything) of the trainer's flat buffer into
-        the engine. The engine must be paused. Returns timing and throughput."""
-        if self._trainer_params is None:
-            raise RuntimeError("attach_trainer_weights() was not called")
-        n = self.engine.layout.total_numel if numel is None else int(numel)
-        src = self._trainer_params[:n]
+    def pull_weights(self, scope: Any = "all") -> Dict[str, float]:
+        """Copy this engine's slice of the trainer's parameters (``scope`` ``"all"`` or
+        ``"trainable"``) into its weights. The engine must be paused. Returns timing and bytes."""
+        if not isinstance(scope, str):
+            scope = "all"
         t0 = time.perf_counter()
         if self.device.type == "cuda":
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record()
-            self.engine.load_flat_weights(src)
-            end.record()
-            torch.cuda.synchronize(self.device)
-            dev_ms = start.elapsed_time(end)
+            with torch.cuda.device(self.device):
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+                nbytes = self.engine.pull_weights(scope)
+                end.record()
+                torch.cuda.synchronize(self.device)
+                dev_ms = start.elapsed_time(end)
         else:
-            self.engine.load_flat_weights(src)
+            nbytes = self.engine.pull_weights(scope)
             dev_ms = (time.perf_counter() - t0) * 1e3
         wall = time.perf_counter() - t0
-        nbytes = n * src.element_size()
         self.last_sync = {"device_ms": dev_ms, "wall_s": wall, "bytes": float(nbytes),
                           "gbs": nbytes / max(dev_ms, 1e-6) / 1e6}
         return self.last_sync
@@ -162,4 +181,41 @@ class InferenceService:
         if self.active_generation_tasks:
             await asyncio.gather(*self.active_generation_tasks, return_exceptions=True)
         await self.engine.shutdown()
+        await asyncio.to_thread(self.engine.stop_followers)
         return self.get_stats()
+
+
+def attach_weight_source(engine: GenerationEngine, args, device: torch.device, handle, opened: List[int]) -> int:
+    """Open a trainer's exported parameter handle on ``device`` and register it with ``engine``."""
+    from ..models.transformer import ParamLayout
+
+    src_layout = ParamLayout.build(engine.full_cfg, args.train_mode, pad_to=args.fsdp_world_size)
+    if isinstance(handle, dict) and handle.get("kind") == "cuda-ipc":
+        from .. import ops
+        from ..ops._ext import native
+
+        ext = native()
+        with torch.cuda.device(device):
+            if handle["device"] != device.index:
+                ops.native().enable_peer_access(handle["device"])
+            rc, base = ext.ipc_open(handle["handle"])
+            if rc != 0:
+                raise RuntimeError(f"cudaIpcOpenMemHandle of the trainer's parameters failed with code {rc}")
+            opened.append(base)
+            addr = base + handle["offset"]
+            probe = handle.get("probe") or b""
+            if probe:
+                rc, got = ext.peer_read(addr, len(probe))
+                if rc != 0 or bytes(got) != probe:
+                    raise RuntimeError("the trainer's parameter mapping is not readable or holds other data")
+        numel = int(handle["numel"])
+        if numel < src_layout.total_numel:
+            raise ValueError("trainer parameter buffer is smaller than the trainer layout")
+        engine.set_weight_source(src_layout, addr=addr)
+        return numel
+    fn, fargs = handle["reduce"] if isinstance(handle, dict) else handle
+    tensor = fn(*fargs)
+    if tensor.numel() < src_layout.total_numel:
+        raise ValueError("trainer parameter buffer is smaller than the trainer layout")
+    engine.set_weight_source(src_layout, tensor=tensor)
+    return int(tensor.numel())

@@ -77,13 +77,23 @@ class TrainerActor:
         return int(self.worker.flat_weights(scope).numel())
 
     def export_weights_handle(self):
-        """Handle that lets another process map this rank's flat bf16 parameters (CUDA IPC on GPU,
-        shared memory on CPU). Every rank holds the full compute copy after each optimizer step."""
+        """Handle that lets another process map this rank's flat bf16 parameters (a CUDA IPC handle of
+        the allocation plus the buffer's offset on GPU, a shared-memory handle on CPU). Every rank
+        holds the full compute copy after each optimizer step."""
         from torch.multiprocessing.reductions import reduce_tensor
 
-        if self.worker.device.type == "cuda":
-            torch.cuda.synchronize(self.worker.device)
-        return reduce_tensor(self.worker.model.params)
+        params = self.worker.model.params
+        if params.is_cuda:
+            from ..ops._ext import native
+
+            torch.cuda.synchronize(params.device)
+            rc, handle, offset = native().ipc_export(params)
+            if rc != 0:
+                raise RuntimeError(f"cudaIpcGetMemHandle failed with code {rc}")
+            probe = bytes(params[:8].view(torch.uint8).cpu().numpy().tobytes())
+            return {"kind": "cuda-ipc", "handle": bytes(handle), "offset": int(offset), "numel": params.numel(),
+                    "device": params.device.index, "probe": probe}
+        return {"kind": "torch", "reduce": reduce_tensor(params), "numel": params.numel()}
 
     def synchronize(self) -> None:
         if self.worker.device.type == "cuda":

@@ -21,6 +21,8 @@ int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, const void*
                              cudaStream_t stream);
 int accerl_row_scatter(const void* src, long long ld, const long long* src_row, const long long* dst_addr, long long n,
                        int H, cudaStream_t s);
+int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
+                       const void* src, void* dst, cudaStream_t s);
 int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
                          void* out, long long ldo, int M, int N, cudaStream_t stream);
 int accerl_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int H, long long ldx,
@@ -169,6 +171,17 @@ void grouped_gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn
                                                      : nullptr,
                                  status_ptr(status), cur_stream()),
         "grouped_gemm");
+}
+
+void weight_pull(const at::Tensor& desc, const at::Tensor& unit_start, int64_t n_units, int64_t src_addr,
+                 at::Tensor& dst) {
+  CHECK_BF16(dst);
+  TORCH_CHECK(desc.scalar_type() == at::kLong && unit_start.scalar_type() == at::kLong, "weight_pull: int64 plans");
+  check(accerl_weight_pull(reinterpret_cast<const long long*>(desc.data_ptr<int64_t>()),
+                           reinterpret_cast<const long long*>(unit_start.data_ptr<int64_t>()),
+                           static_cast<int>(desc.size(0)), n_units, reinterpret_cast<const void*>(src_addr),
+                           dst.data_ptr(), cur_stream()),
+        "weight_pull");
 }
 
 void row_scatter(const at::Tensor& src, const c10::optional<at::Tensor>& src_row, const at::Tensor& dst_addr) {
@@ -462,6 +475,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("splitk_finish", &splitk_finish);
   m.def("grouped_gemm", &grouped_gemm);
   m.def("row_scatter", &row_scatter);
+  m.def("weight_pull", &weight_pull);
   m.def("ipc_export", &ipc_export);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

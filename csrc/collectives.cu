@@ -115,9 +115,60 @@ __global__ void row_scatter_kernel(const __nv_bfloat16* __restrict__ src, long l
   for (int c = lane; c < H / 8; c += 32) d[c] = s[c];
 }
 
+// Trainer -> engine weight pull: a list of 2-D copies desc[i] = {src_off, src_ld, dst_off, dst_ld,
+// rows, cols} (elements) from a source buffer (the trainer's flat parameters, normally another GPU's
+// memory mapped by CUDA IPC) into the local flat parameter buffer. Work is split into units of one
+// row chunk of at most kPullChunk elements; unit_start[i] is the first unit of descriptor i. One warp
+// per unit, 16-byte loads and stores where both addresses allow, element copies otherwise.
+constexpr int kPullChunk = 4096;
+
+__global__ void weight_pull_kernel(const long long* __restrict__ desc, const long long* __restrict__ unit_start,
+                                   int n_desc, const __nv_bfloat16* __restrict__ src, __nv_bfloat16* __restrict__ dst) {
+  const long long n_units = unit_start[n_desc];
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const int lane = threadIdx.x & 31;
+  for (long long u = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; u < n_units; u += warps) {
+    int lo = 0, hi = n_desc;  // unit_start[lo] <= u < unit_start[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (unit_start[mid] <= u) lo = mid;
+      else hi = mid;
+    }
+    const long long* d = desc + 6 * lo;
+    const long long cols = d[5];
+    const long long per_row = (cols + kPullChunk - 1) / kPullChunk;
+    const long long local = u - unit_start[lo];
+    const long long row = local / per_row;
+    const long long c0 = (local % per_row) * kPullChunk;
+    const long long c1 = min(cols, c0 + kPullChunk);
+    const __nv_bfloat16* s = src + d[0] + row * d[1];
+    __nv_bfloat16* t = dst + d[2] + row * d[3];
+    const bool vec = (((reinterpret_cast<uintptr_t>(s + c0) | reinterpret_cast<uintptr_t>(t + c0)) & 15) == 0);
+    long long c = c0;
+    if (vec) {
+      const long long nv = (c1 - c0) / 8;
+      const uint4* sv = reinterpret_cast<const uint4*>(s + c0);
+      uint4* tv = reinterpret_cast<uint4*>(t + c0);
+      for (long long i = lane; i < nv; i += 32) tv[i] = sv[i];
+      c = c0 + nv * 8;
+    }
+    for (long long i = c + lane; i < c1; i += 32) t[i] = s[i];
+  }
+}
+
 }  // namespace accerl
 
 using namespace accerl;
+
+extern "C" int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
+                                  const void* src, void* dst, cudaStream_t s) {
+  if (n_desc <= 0 || n_units <= 0) return 0;
+  long long blocks = (n_units + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  weight_pull_kernel<<<(unsigned)blocks, 256, 0, s>>>(desc, unit_start, n_desc, (const __nv_bfloat16*)src,
+                                                      (__nv_bfloat16*)dst);
+  return (int)cudaGetLastError();
+}
 
 extern "C" int accerl_row_scatter(const void* src, long long ld, const long long* src_row, const long long* dst_addr,
                                   long long n, int H, cudaStream_t s) {
