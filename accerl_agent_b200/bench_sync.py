@@ -1,15 +1,19 @@
-"""Trainer -> rollout weight-sync benchmark on two GPUs of one node.
+"""Trainer -> rollout weight-sync benchmark on one node.
 
-    python -m accerl_agent_b200.bench_sync [--model qwen3-8b] [--iters 5]
+    python -m accerl_agent_b200.bench_sync [--model qwen3-8b] [--trainers 1] [--tp 1] [--iters 5]
 
-GPU 0 plays a trainer rank holding the full bf16 compute copy of the model in the fused layout;
-GPU 1 plays a rollout engine. Two transfer paths are timed with CUDA events (device time of the
-receiving GPU, max over the two processes where both take part):
+``--trainers T`` processes play trainer ranks on GPUs 0..T-1, each holding the full bf16 compute copy
+in the trainer's flat layout (the resident-parameter design); ``--tp P`` processes on GPUs T..T+P-1
+play one tensor-parallel rollout engine. Two transfer paths are timed with CUDA events, max over the
+receiving ranks:
 
-* ``ipc_pull``: the engine maps the trainer buffer once (CUDA IPC) and copies it into its own weights
-  in place (one peer-to-peer copy over NVLink, no staging, no rank-0 funnel);
-* ``nccl_broadcast``: the baseline transfer of the reference (NCCL broadcast of the weights packed into
-  1 GiB buffers, double-buffered), between the same two GPUs.
+* ``kernel_pull``: every engine rank maps trainer ``r % T``'s buffer once (CUDA IPC, opened on the
+  engine's GPU) and runs its copy plan: one kernel that reads exactly its TP shard of every parameter
+  over NVLink and writes it into the engine's fused layout in place (no gather, no rank-0 funnel);
+* ``nccl_broadcast``: the reference's transfer (trainer rank 0 broadcasts the whole model packed into
+  1 GiB buffers, double-buffered; every engine rank receives all of it and would slice afterwards).
+
+The weight-sync configuration of Qwen3-8B is ``--trainers 6 --tp 2`` on 8 GPUs.
 """
 
 from __future__ import annotations
@@ -23,72 +27,112 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 
-def _proc(rank: int, a, port: int, q):
-    torch.cuda.set_device(rank)
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("nccl", rank=rank, world_size=2, device_id=torch.device("cuda", rank))
-    from .models.config import get_preset
-    from .models.transformer import ParamLayout
-
-    cfg = get_preset(a.model)
-    n = ParamLayout.build(cfg, "full").total_numel
-    buf = torch.empty(n, dtype=torch.bfloat16, device="cuda")
-    if rank == 0:
-        buf.normal_()
-    results = {}
-    # ---- IPC pull
-    if rank == 0:
-        from torch.multiprocessing.reductions import reduce_tensor
-
-        obj = [reduce_tensor(buf)]
-    else:
-        obj = [None]
-    dist.broadcast_object_list(obj, src=0)
-    if rank == 1:
-        fn, fargs = obj[0]
-        src = fn(*fargs)
-        ts = []
-        for i in range(a.warmup + a.iters):
-            torch.cuda.synchronize()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            buf.copy_(src, non_blocking=True)
-            e.record()
-            torch.cuda.synchronize()
-            if i >= a.warmup:
-                ts.append(s.elapsed_time(e))
-        assert torch.equal(buf[:1024].cpu(), src[:1024].cpu())
-        results["ipc_pull_ms"] = sorted(ts)[len(ts) // 2]
-    dist.barrier()
-    # ---- NCCL broadcast in packed 1 GiB buffers
-    bucket = (1 << 30) // 2
+def _time(fn, warmup: int, iters: int, sync_group=None):
     ts = []
-    for i in range(a.warmup + a.iters):
+    for i in range(warmup + iters):
         torch.cuda.synchronize()
-        dist.barrier()
+        if sync_group is not None:
+            dist.barrier(group=sync_group)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for off in range(0, n, bucket):
-            dist.broadcast(buf[off : off + bucket], src=0)
+        fn()
         e.record()
         torch.cuda.synchronize()
-        if i >= a.warmup:
+        if i >= warmup:
             ts.append(s.elapsed_time(e))
-    t = torch.tensor([sorted(ts)[len(ts) // 2]], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    results["nccl_broadcast_ms"] = float(t.item())
-    if rank == 1:
-        gb = n * 2 / 1e9
+    return sorted(ts)[len(ts) // 2]
+
+
+def _proc(rank: int, world: int, a, port: int, q):
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    from .models.config import get_preset
+    from .models.transformer import ParamLayout
+    from .ops._ext import native
+    from .rollout.weight_map import build_weight_map, descs_tensor, map_bytes, tp_shard_config
+    from . import ops
+
+    T, P = a.trainers, a.tp
+    cfg = get_preset(a.model)
+    src_layout = ParamLayout.build(cfg, "full", pad_to=T)
+    is_trainer = rank < T
+    results = {}
+    if is_trainer:
+        buf = torch.empty(src_layout.total_numel, dtype=torch.bfloat16, device=dev)
+        gen = torch.Generator(device=dev).manual_seed(0)
+        buf.normal_(generator=gen)
+        rc, handle, off = native().ipc_export(buf)
+        assert rc == 0
+        info = (rank, handle, off)
+    else:
+        info = None
+    infos = [None] * world
+    dist.all_gather_object(infos, info)
+    engine_ranks = list(range(T, T + P))
+    engine_group = dist.new_group(engine_ranks)
+    bcast_group = dist.new_group([0] + engine_ranks)
+    # ---- kernel pull of this rank's shard
+    if not is_trainer:
+        r = rank - T
+        scfg = tp_shard_config(cfg, P)
+        if scfg.local_experts:
+            scfg.expert_offset = r * scfg.local_experts
+        dst_layout = ParamLayout.build(scfg, "full")
+        dst = torch.empty(dst_layout.total_numel, dtype=torch.bfloat16, device=dev)
+        tr, handle, off = infos[r % T]
+        native().enable_peer_access(tr)
+        rc, base = native().ipc_open(handle)
+        assert rc == 0
+        descs = build_weight_map(cfg, src_layout, dst_layout, r, P, "all")
+        plan = descs_tensor(descs, dev)
+        ms = _time(lambda: ops.weight_pull(plan, base + off, dst), a.warmup, a.iters, engine_group)
+        results["kernel_pull_ms"] = ms
+        results["kernel_pull_bytes"] = map_bytes(descs)
+        # spot check against a host copy of one parameter slice
+        name = "model.layers.0.self_attn.o_proj.weight"
+        s_slot, d_slot = src_layout.slots[name], dst_layout.slots[name]
+        ql = cfg.q_dim // P
+        got = dst[d_slot.offset : d_slot.offset + d_slot.numel].view(cfg.hidden_size, ql)
+        rc, raw = native().peer_read(base + off + 2 * s_slot.offset, 2 * s_slot.numel)
+        assert rc == 0
+        full = torch.frombuffer(bytearray(raw), dtype=torch.bfloat16).view(cfg.hidden_size, cfg.q_dim)
+        assert torch.equal(got.cpu(), full[:, r * ql : (r + 1) * ql]), "pulled shard differs from the trainer's"
+    dist.barrier()
+    # ---- NCCL broadcast of the packed full model from trainer 0 to every engine rank
+    if rank == 0 or not is_trainer:
+        n = src_layout.total_numel
+        payload = buf if rank == 0 else torch.empty(n, dtype=torch.bfloat16, device=dev)
+        bucket = (1 << 30) // 2
+
+        def bcast():
+            for o in range(0, n, bucket):
+                dist.broadcast(payload[o : o + bucket], src=0, group=bcast_group)
+
+        results["nccl_broadcast_ms"] = _time(bcast, a.warmup, a.iters, bcast_group)
+    dist.barrier()
+    gathered = [None] * world
+    dist.all_gather_object(gathered, results)
+    if rank == T:
+        pulls = [g["kernel_pull_ms"] for g in gathered if "kernel_pull_ms" in g]
+        bytes_max = max(g["kernel_pull_bytes"] for g in gathered if "kernel_pull_bytes" in g)
+        bc = max(g["nccl_broadcast_ms"] for g in gathered if "nccl_broadcast_ms" in g)
+        full_bytes = src_layout.total_numel * 2
         q.put({
             "metric": "weight-sync ms",
             "model": a.model,
-            "bytes": n * 2,
-            "ipc_pull_ms": round(results["ipc_pull_ms"], 3),
-            "ipc_pull_gbs": round(gb / (results["ipc_pull_ms"] / 1e3), 1),
-            "nccl_broadcast_ms": round(results["nccl_broadcast_ms"], 3),
-            "nccl_broadcast_gbs": round(gb / (results["nccl_broadcast_ms"] / 1e3), 1),
-            "link_roofline_ms_at_770GBs": round(gb / 770 * 1e3, 3),
+            "trainers": T,
+            "engine_tp": P,
+            "model_bytes": full_bytes,
+            "kernel_pull_ms": round(max(pulls), 3),
+            "kernel_pull_bytes_per_engine_rank": bytes_max,
+            "kernel_pull_gbs_per_rank": round(bytes_max / 1e9 / (max(pulls) / 1e3), 1),
+            "nccl_broadcast_ms": round(bc, 3),
+            "speedup_vs_broadcast": round(bc / max(pulls), 2),
+            "link_roofline_ms_at_770GBs": round(bytes_max / 770e9 * 1e3, 3),
+            "frac_of_link_roofline": round(bytes_max / 770e9 * 1e3 / max(pulls), 3),
         })
     dist.barrier()
     dist.destroy_process_group()
@@ -97,18 +141,23 @@ def _proc(rank: int, a, port: int, q):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--trainers", type=int, default=1)
+    ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--json", default=None)
     a = ap.parse_args()
     import socket
 
+    world = a.trainers + a.tp
+    if torch.cuda.device_count() < world:
+        raise SystemExit(f"needs {world} GPUs, found {torch.cuda.device_count()}")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_proc, args=(r, a, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_proc, args=(r, world, a, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -73,14 +73,23 @@ class _Seq:
     num_computed: int = 0
     finish_reason: Optional[str] = None
     arrival: float = 0.0
+    toks: List[int] = field(default_factory=list)  # prompt + out, kept in step (no per-access concat)
+
+    def __post_init__(self) -> None:
+        self.toks = list(self.prompt)
+
+    def append(self, tok: int, lp: float) -> None:
+        self.out.append(tok)
+        self.lps.append(lp)
+        self.toks.append(tok)
 
     @property
     def tokens(self) -> List[int]:
-        return self.prompt + self.out
+        return self.toks
 
     @property
     def length(self) -> int:
-        return len(self.prompt) + len(self.out)
+        return len(self.toks)
 
 
 class GenerationEngine:
@@ -157,11 +166,22 @@ class GenerationEngine:
         self.k_cache = torch.zeros(L, num_blocks, block_size, Hkv, D, dtype=dtype, device=device)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.allocator = BlockAllocator(num_blocks, block_size, enable_prefix_caching)
+        self._tp_ar = None
+        self._ar_calls = 0
+        if self.tp > 1 and device.type == "cuda":
+            from ..parallel.symmetric import peer_access_available
+
+            if peer_access_available(tp_group):
+                from ..parallel.tp_allreduce import TPAllReduce
+
+                rows = max(max_num_batched_tokens, max(self._BUCKETS))
+                self._tp_ar = TPAllReduce(tp_group, device, rows * cfg.hidden_size, dtype)
         # block 0 is never handed to a sequence: padded rows of captured decode graphs point at it
         self.scratch_block = self.allocator.allocate()
-        # MoE steps synchronise with the host (routing counts); tensor-parallel steps all-reduce through
-        # NCCL, which stays outside graph capture here: both run eagerly
-        self.use_cuda_graphs = use_cuda_graphs and device.type == "cuda" and not cfg.is_moe and self.tp == 1
+        # MoE steps synchronise with the host (routing counts) and run eagerly; tensor-parallel steps
+        # are captured only with the peer-memory all-reduce (no NCCL inside graphs)
+        self.use_cuda_graphs = (use_cuda_graphs and device.type == "cuda" and not cfg.is_moe
+                                and (self.tp == 1 or self._tp_ar is not None))
         self._graphs: Dict[Any, Any] = {}
         self._graph_pool = None
         self.waiting: Deque[_Seq] = deque()
@@ -175,7 +195,9 @@ class GenerationEngine:
         self._seed_counter = itertools.count(seed * 1_000_003 + 1)
         self.decode_splits = decode_splits
         self.stats = {"generated_tokens": 0, "prompt_tokens_computed": 0, "steps": 0, "preemptions": 0,
-                      "aborted": 0, "finished": 0}
+                      "aborted": 0, "finished": 0, "prefill_rows": 0, "decode_rows": 0,
+                      # host wall time per step phase (the prefill and decode phases include their GPU work)
+                      "t_schedule_s": 0.0, "t_prefill_s": 0.0, "t_decode_s": 0.0, "t_post_s": 0.0}
         self._thread: Optional[threading.Thread] = None
         self.eos_ids = {cfg.eos_token_id}
         if tokenizer is not None and getattr(tokenizer, "eos_token_id", None) is not None:
@@ -446,9 +468,11 @@ class GenerationEngine:
     # ------------------------------------------------------------------ execution
     def step(self) -> bool:
         with self._step_lock:
+            t0 = time.perf_counter()
             plan = self._schedule()
             if not plan:
                 return False
+            t1 = time.perf_counter()
             # prefill-first: multi-token chunks run in their own (eager) step with the varlen kernel over
             # their cached prefix; steps where every scheduled sequence advances by one token run the
             # paged decode path, replayed from a captured CUDA graph when possible
@@ -457,14 +481,25 @@ class GenerationEngine:
             if self.use_cuda_graphs and decode and all(p[3] for p in decode):
                 # two passes per step: prefill chunks eagerly, then all decode rows from one graph replay
                 toks, logps = self._execute(prefill, len(prefill)) if prefill else ([], [])
+                t2 = time.perf_counter()
                 dt, dl = self._execute_decode_graph(decode)
                 order = prefill + decode
                 toks, logps = toks + dt, logps + dl
             else:
                 order = prefill + decode
                 toks, logps = self._execute(order, len(prefill))
+                t2 = time.perf_counter()
+            t3 = time.perf_counter()
             self._postprocess(order, toks, logps)
-            self.stats["steps"] += 1
+            t4 = time.perf_counter()
+            st = self.stats
+            st["steps"] += 1
+            st["prefill_rows"] += sum(p[2] for p in prefill)
+            st["decode_rows"] += len(decode)
+            st["t_schedule_s"] += t1 - t0
+            st["t_prefill_s"] += t2 - t1
+            st["t_decode_s"] += t3 - t2
+            st["t_post_s"] += t4 - t3
             return True
 
     # ------------------------------------------------------------------ CUDA-graph decode
@@ -479,9 +514,29 @@ class GenerationEngine:
         return y
 
     def _row_parallel(self, a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
-        """``residual + a @ w^T`` for a row-parallel weight: every rank multiplies its column slice,
-        rank 0 adds the residual in the GEMM epilogue, and the partial sums are all-reduced."""
+        """``residual + a @ w^T`` for a row-parallel weight: every rank multiplies its column slice
+        and the partial sums are all-reduced. With peer access the GEMM writes its partial into the
+        symmetric buffer and one P2P kernel sums the ranks and adds the residual; otherwise rank 0
+        adds the residual in the GEMM epilogue and NCCL (gloo on CPU) all-reduces."""
+        if self._tp_ar is not None:
+            k = self._ar_calls
+            self._ar_calls += 1
+            part = self._tp_ar.slot(k, a.shape[0], w.shape[0])
+            ops.linear(a, w, out=part)
+            return self._tp_ar.reduce(k, part, residual)
         y = ops.linear(a, w, residual=residual if self.tp_rank == 0 else None)
+        return self._all_reduce(y)
+
+    def _reduce_partial(self, y: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """``residual + sum over ranks of y`` (``y`` a partial computed outside the symmetric buffer)."""
+        if self._tp_ar is not None:
+            k = self._ar_calls
+            self._ar_calls += 1
+            part = self._tp_ar.slot(k, y.shape[0], y.shape[1])
+            part.copy_(y)
+            return self._tp_ar.reduce(k, part, residual)
+        if self.tp_rank == 0:
+            y = y + residual
         return self._all_reduce(y)
 
     def _forward_layers(self, x, pos_d, slots_d, attn_fn):
@@ -489,6 +544,7 @@ class GenerationEngine:
         attention output rows. Returns the final hidden rows (before the last norm)."""
         cfg, m = self.cfg, self.model
         D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        self._ar_calls = 0
         for layer in range(cfg.num_hidden_layers):
             p = f"model.layers.{layer}."
             h1, _ = ops.rmsnorm(x, m.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
@@ -508,9 +564,8 @@ class GenerationEngine:
             if cfg.layer_is_moe(layer):
                 from ..models.moe import moe_forward
 
-                res = x if self.tp_rank == 0 else torch.zeros_like(x)
-                x, _ = moe_forward(m, layer, h2, res, save=False)
-                x = self._all_reduce(x)
+                y, _ = moe_forward(m, layer, h2, torch.zeros_like(x), save=False)
+                x = self._reduce_partial(y, x)
             else:
                 gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
                 x = self._row_parallel(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), x)
@@ -614,6 +669,8 @@ class GenerationEngine:
         g["graph"].replay()
         B = meta["B"]
         res = torch.stack([g["tok"][:B].double(), g["lp"][:B].double()]).cpu()
+        if self._tp_ar is not None:
+            self._tp_ar.check()
         return res[0].long().tolist(), res[1].tolist()
 
     def _execute_decode_graph(self, order):
@@ -626,38 +683,38 @@ class GenerationEngine:
     def _exec_meta(self, order, n_prefill: int) -> Dict[str, Any]:
         """Host inputs of one eager step over ``order`` (first ``n_prefill`` entries are prefill chunks)."""
         bs = self.block_size
-        ids: List[int] = []
-        pos: List[int] = []
-        slots: List[int] = []
+        ids_l, pos_l, slots_l, ks_l = [], [], [], []
         sample_rows: List[int] = []
         cu_q = [0]
         cu_k = [0]
-        k_slots: List[int] = []
         max_q = 1
+        rows = 0
         for i, (seq, start, n, samples) in enumerate(order):
-            toks = seq.tokens
             blocks = np.asarray(seq.blocks, dtype=np.int64)
-            p = np.arange(start, start + n)
-            ids.extend(toks[start : start + n])
-            pos.extend(p.tolist())
-            slots.extend((blocks[p // bs] * bs + p % bs).tolist())
+            p = np.arange(start, start + n, dtype=np.int64)
+            ids_l.append(np.asarray(seq.toks[start : start + n], dtype=np.int64))
+            pos_l.append(p)
+            slots_l.append(blocks[p // bs] * bs + p % bs)
+            rows += n
             if samples:
-                sample_rows.append(len(ids) - 1)
+                sample_rows.append(rows - 1)
             if i < n_prefill:
                 cu_q.append(cu_q[-1] + n)
                 ctx = start + n
                 cu_k.append(cu_k[-1] + ctx)
-                pk = np.arange(ctx)
-                k_slots.extend((blocks[pk // bs] * bs + pk % bs).tolist())
+                pk = np.arange(ctx, dtype=np.int64)
+                ks_l.append(blocks[pk // bs] * bs + pk % bs)
                 max_q = max(max_q, n)
+        empty = np.zeros(0, np.int64)
+        ids = np.concatenate(ids_l) if ids_l else empty
+        pos = np.concatenate(pos_l) if pos_l else empty
+        slots = np.concatenate(slots_l) if slots_l else empty
+        k_slots = np.concatenate(ks_l) if ks_l else empty
         decode = order[n_prefill:]
         nd = len(decode)
         header = [len(ids), len(pos), len(slots), len(sample_rows), len(cu_q), len(cu_k), len(k_slots)]
-        flat = np.concatenate([
-            np.asarray(ids, np.int64), np.asarray(pos, np.int64), np.asarray(slots, np.int64),
-            np.asarray(sample_rows, np.int64), np.asarray(cu_q, np.int64), np.asarray(cu_k, np.int64),
-            np.asarray(k_slots, np.int64),
-        ])
+        flat = np.concatenate([ids, pos, slots, np.asarray(sample_rows, np.int64), np.asarray(cu_q, np.int64),
+                               np.asarray(cu_k, np.int64), k_slots])
         meta: Dict[str, Any] = {"kind": "exec", "header": header, "flat": flat, "Tp": cu_q[-1], "max_q": max_q,
                                 "nd": nd}
         if nd:
@@ -738,6 +795,8 @@ class GenerationEngine:
                 tokens, lps = ops.sample(logits, torch.from_numpy(meta["temps"]).to(dev), seeds.to(dev),
                                          torch.from_numpy(meta["offs"]).to(dev))
             res = torch.stack([tokens.double(), lps.double()]).cpu()  # the one device->host read per step
+        if self._tp_ar is not None:
+            self._tp_ar.check()
         return res[0].long().tolist(), res[1].tolist()
 
     # ------------------------------------------------------------------ tensor-parallel followers
@@ -804,8 +863,7 @@ class GenerationEngine:
                 if not samples:
                     continue
                 tok, lp = next(it)
-                seq.out.append(int(tok))
-                seq.lps.append(float(lp))
+                seq.append(int(tok), float(lp))
                 self.stats["generated_tokens"] += 1
                 reason = self._stop_reason(seq, int(tok))
                 if reason is not None:

@@ -21,6 +21,9 @@ int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, const void*
                              cudaStream_t stream);
 int accerl_row_scatter(const void* src, long long ld, const long long* src_row, const long long* dst_addr, long long n,
                        int H, cudaStream_t s);
+int accerl_tp_allreduce(const long long* peer_data, const long long* peer_flags, int world, int rank, int slot,
+                        long long slot_elems, long long n, const void* residual, void* out, int* ctr, int* status,
+                        cudaStream_t s);
 int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
                        const void* src, void* dst, cudaStream_t s);
 int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
@@ -182,6 +185,20 @@ void weight_pull(const at::Tensor& desc, const at::Tensor& unit_start, int64_t n
                            static_cast<int>(desc.size(0)), n_units, reinterpret_cast<const void*>(src_addr),
                            dst.data_ptr(), cur_stream()),
         "weight_pull");
+}
+
+void tp_allreduce(const at::Tensor& peer_data, const at::Tensor& peer_flags, int64_t rank, int64_t slot,
+                  int64_t slot_elems, int64_t n, const c10::optional<at::Tensor>& residual, at::Tensor& out,
+                  at::Tensor& ctr, at::Tensor& status) {
+  CHECK_BF16(out);
+  TORCH_CHECK(ctr.scalar_type() == at::kInt && ctr.numel() >= 2, "tp_allreduce: int32 counter pair");
+  if (residual.has_value()) CHECK_BF16(*residual);
+  check(accerl_tp_allreduce(reinterpret_cast<const long long*>(peer_data.data_ptr<int64_t>()),
+                            reinterpret_cast<const long long*>(peer_flags.data_ptr<int64_t>()),
+                            static_cast<int>(peer_data.numel()), static_cast<int>(rank), static_cast<int>(slot),
+                            slot_elems, n, residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(),
+                            ctr.data_ptr<int>(), status.data_ptr<int>(), cur_stream()),
+        "tp_allreduce");
 }
 
 void row_scatter(const at::Tensor& src, const c10::optional<at::Tensor>& src_row, const at::Tensor& dst_addr) {
@@ -476,6 +493,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &grouped_gemm);
   m.def("row_scatter", &row_scatter);
   m.def("weight_pull", &weight_pull);
+  m.def("tp_allreduce", &tp_allreduce);
   m.def("ipc_export", &ipc_export);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -156,9 +156,117 @@ __global__ void weight_pull_kernel(const long long* __restrict__ desc, const lon
   }
 }
 
+// One-shot all-reduce of bf16 partial sums for tensor-parallel (row-parallel) layers, over NVLink
+// peer memory. Every rank's partial for this call sits in slot `slot` of its symmetric buffer
+// (element offset slot * slot_elems). Block 0 publishes `epoch` into flags_r[slot][rank] of every
+// rank r (system-scope release); every block then waits (bounded) until this rank's flags[slot][src]
+// equal `epoch` for all src, sums all ranks' partials in rank order (identical result on every rank)
+// plus the optional residual, and writes `out`. epoch = *ctr + 1; the last block to finish stores it
+// back into *ctr, so the count lives on the device and CUDA-graph replays advance it. Ranks issue the
+// same calls in the same order, alternating slots, so a rank can be at most one call ahead and a
+// slot is never overwritten while a peer still reads it. On timeout the status word is set and the
+// kernel returns without writing.
+__global__ void tp_allreduce_kernel(const long long* __restrict__ peer_data, const long long* __restrict__ peer_flags,
+                                    int world, int rank, int slot, long long slot_elems, long long n,
+                                    const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out,
+                                    int* ctr, int* done, int* status) {
+  __shared__ int epoch_s, ok_s;
+  if (threadIdx.x == 0) {
+    const int epoch = *reinterpret_cast<volatile int*>(ctr) + 1;
+    epoch_s = epoch;
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int r = 0; r < world; ++r)
+        st_release_sys(reinterpret_cast<int*>(peer_flags[r]) + slot * world + rank, epoch);
+    }
+    const int* mine = reinterpret_cast<const int*>(peer_flags[rank]) + slot * world;
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int r = 0; r < world && ok; ++r) {
+      while (ld_acquire_sys(mine + r) != epoch) {
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicExch(status, kStatusTimeoutPeer);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    ok_s = ok;
+  }
+  __syncthreads();
+  if (ok_s) {
+    const long long base = static_cast<long long>(slot) * slot_elems;
+    const long long n8 = n / 8;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      float acc[8];
+      if (residual) {
+        const uint4 r = *reinterpret_cast<const uint4*>(residual + 8 * i);
+        const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(rw[j]);
+          acc[2 * j] = f.x;
+          acc[2 * j + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      }
+      for (int r = 0; r < world; ++r) {
+        const uint4 v = ld_cg_v4(reinterpret_cast<const __nv_bfloat16*>(peer_data[r]) + base + 8 * i);
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack_bf16x2(vw[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(acc[0], acc[1]);
+      o.y = pack_bf16x2(acc[2], acc[3]);
+      o.z = pack_bf16x2(acc[4], acc[5]);
+      o.w = pack_bf16x2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(out + 8 * i) = o;
+    }
+    if (blockIdx.x == 0) {
+      for (long long i = n8 * 8 + threadIdx.x; i < n; i += blockDim.x) {
+        float a = residual ? __bfloat162float(residual[i]) : 0.f;
+        for (int r = 0; r < world; ++r)
+          a += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(peer_data[r])[base + i]);
+        out[i] = __float2bfloat16(a);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1) {
+      *done = 0;
+      *ctr = epoch_s;
+      __threadfence();
+    }
+  }
+}
+
 }  // namespace accerl
 
 using namespace accerl;
+
+extern "C" int accerl_tp_allreduce(const long long* peer_data, const long long* peer_flags, int world, int rank, int slot,
+                                   long long slot_elems, long long n, const void* residual, void* out, int* ctr,
+                                   int* status, cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (world < 1 || world > 8 || slot < 0 || slot > 1 || n > slot_elems) return -1;
+  long long blocks = (n / 8 + 255) / 256;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks < 1) blocks = 1;
+  tp_allreduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(peer_data, peer_flags, world, rank, slot, slot_elems, n,
+                                                       (const __nv_bfloat16*)residual, (__nv_bfloat16*)out, ctr,
+                                                       ctr + 1, status);
+  return (int)cudaGetLastError();
+}
 
 extern "C" int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
                                   const void* src, void* dst, cudaStream_t s) {

@@ -230,6 +230,22 @@ ACCERL_DEVINL void red_add_v4(float* addr, float a, float b, float c, float d) {
 }
 
 // Make generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma operand reads).
+// System-scope release store / acquire load of a 32-bit flag (cross-GPU signalling over NVLink).
+ACCERL_DEVINL void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+ACCERL_DEVINL int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// 16-byte load cached in L2 only (no L1): peer data that changes between kernel launches.
+ACCERL_DEVINL uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
 ACCERL_DEVINL void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Named barrier among a subset of warps (id 1..15; id 0 is __syncthreads).

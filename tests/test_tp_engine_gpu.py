@@ -57,7 +57,7 @@ async def _generate(engine, n=12):
 
     outs = []
     for i, ids in enumerate(PROMPTS):
-        sp = SamplingParams(temperature=0.0, max_tokens=n, ignore_eos=True)
+        sp = SamplingParams(temperature=0.0, max_tokens=n, ignore_eos=True, logprobs=1)
         last = None
         async for o in engine.generate({"prompt_token_ids": ids}, sp, request_id=f"r{i}"):
             last = o
@@ -124,3 +124,83 @@ def test_tp2_engine_matches_single_gpu(moe):
         assert abs(lp[0] - lp_w[0]) < 0.05
         agree = sum(a == b for a, b in zip(tok, tok_w)) / len(tok)
         assert agree >= 0.5, (tok, tok_w)
+
+
+def _ar_worker(rank, port, q):
+    try:
+        from accerl_agent_b200.parallel.tp_allreduce import TPAllReduce
+
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev)
+        ar = TPAllReduce(dist.group.WORLD, dev, 300 * 1536)
+        errs = []
+        g = torch.Generator(device=dev).manual_seed(rank)
+        # eager calls of varying sizes (odd tail included), alternating slots
+        for k, rows in enumerate([7, 300, 1, 64, 33]):
+            cols = 1536 if rows != 33 else 1530
+            part = ar.slot(k, rows, cols)
+            part.copy_(torch.randn(rows, cols, device=dev, generator=g).bfloat16())
+            res = torch.randn(rows, cols, device=dev, generator=g).bfloat16()
+            out = ar.reduce(k, part, res)
+            want = part.float().clone()
+            dist.all_reduce(want)
+            errs.append(float((out.float() - (want + res.float())).abs().max()))
+        # the same calls captured in a CUDA graph and replayed with new inputs
+        src = torch.zeros(64, 1536, device=dev, dtype=torch.bfloat16)
+        res = torch.zeros_like(src)
+
+        def body():
+            p0 = ar.slot(0, 64, 1536)
+            p0.copy_(src)
+            o0 = ar.reduce(0, p0, res)
+            p1 = ar.slot(1, 64, 1536)
+            p1.copy_(o0)
+            return ar.reduce(1, p1, None)
+
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            body()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = body()
+        for _ in range(3):
+            src.copy_(torch.randn(64, 1536, device=dev, generator=g).bfloat16())
+            res.copy_(torch.randn(64, 1536, device=dev, generator=g).bfloat16())
+            graph.replay()
+            s_all = src.float().clone()
+            dist.all_reduce(s_all)
+            o0 = (s_all + res.float()).bfloat16().float()
+            want = o0.clone()
+            dist.all_reduce(want)
+            errs.append(float((out.float() - want).abs().max()))
+        ar.check()
+        torch.cuda.synchronize()
+        del graph
+        q.put((rank, errs))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:
+        q.put((rank, repr(exc)))
+        raise
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_allreduce_kernel_eager_and_graph():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_ar_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(60)
+    for r in (0, 1):
+        assert not isinstance(res[r], str), res[r]
+        assert max(res[r]) < 0.07, res[r]
