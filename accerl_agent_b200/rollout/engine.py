@@ -297,6 +297,15 @@ class GenerationEngine:
             res = await res
         return [res]
 
+    def report_cuda_memory(self, label: str, empty_cache: bool = False) -> Dict[str, Any]:
+        """Memory of this engine's process (``collective_rpc("report_cuda_memory", args=(label,))``)."""
+        from ..utils.memory import cuda_memory_report
+
+        if self.device.type != "cuda":
+            return {"label": label, "device": "cpu"}
+        with torch.cuda.device(self.device):
+            return cuda_memory_report(label, empty_cache)
+
     def reload_weights(self, path: str) -> None:
         from ..models.hf_io import load_hf_checkpoint
 

@@ -296,3 +296,26 @@ def test_synthetic_game_is_seeded():
         steps += 1
         assert r in (0.0, 1.0)
     assert steps == 5 and info["moves"] == 5
+
+
+def test_eval_script_synthetic_cpu():
+    """The TextWorld evaluation entry point end to end on the synthetic game (CPU engine)."""
+    from accerl_agent_b200.eval_textworld import main
+
+    summary = main(["--model-path", "tiny-qwen2", "--env", "synthetic", "--device", "cpu", "--episodes", "3",
+                    "--max-episode-steps", "2", "--num-samples", "2", "--max-action-tokens", "4", "--game-limit", "2"])
+    assert summary["episodes"] == 3 and summary["avg_steps"] == 2.0
+
+
+def test_history_prompt_keeps_last_turns():
+    from accerl_agent_b200.eval_textworld import history_prompt
+
+    infos = {"objective": "win", "admissible_commands": ["go north", "look"], "inventory": "nothing"}
+    turns = [{"kind": "env", "action": f"a{i}", "pre_obs": f"pre{i}", "pre_infos": infos, "obs": f"obs{i}",
+              "infos": infos} for i in range(5)]
+    turns.append({"kind": "illegal", "action": "dance", "pre_obs": "obs4", "pre_infos": infos, "obs": "obs4",
+                  "infos": infos})
+    p = history_prompt("start", infos, turns, None, history_steps=2)
+    assert "pre4" in p and "a4" in p and "dance" in p and "a3" not in p and "start" not in p
+    p0 = history_prompt("start", infos, [], None, history_steps=0)
+    assert "start" in p0
