@@ -24,11 +24,20 @@ from .rollout.inference import InferenceService
 from .rollout.worker import RolloutWorker
 
 
-async def _drive(service, args, groups: int, seconds: float):
+async def _drive(service, args, groups: int, seconds: float, profile: float = 0.0):
     sink_samples = []
     worker_list = [RolloutWorker(args, service, i, sink_samples.extend, lambda *a: None) for i in range(groups)]
     tasks = [asyncio.create_task(w.run()) for w in worker_list]
     await asyncio.sleep(3.0)  # warm-up: prefill of the first observations, kernel caches
+    if profile > 0:
+        # kernel-time breakdown of a window of engine steps (not a throughput measurement)
+        from torch.profiler import ProfilerActivity, profile as tprof
+
+        with tprof(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            await asyncio.sleep(profile)
+        steps = service.engine.stats["steps"]
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=25, max_name_column_width=60))
+        print(f"[profile] engine steps so far: {steps}")
     tok0 = service.total_tokens
     t0 = time.perf_counter()
     await asyncio.sleep(seconds)
@@ -70,6 +79,8 @@ def main():
     ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
     ap.add_argument("--window", type=int, default=8192)
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks of the engine (GPUs 0..tp-1)")
+    ap.add_argument("--profile-seconds", type=float, default=0.0,
+                    help="print a torch.profiler kernel table of this many seconds before timing")
     ap.add_argument("--json", default=None)
     a = ap.parse_args()
     args = make_args(model_path=a.model, env="synthetic", rl_algorithm="grpo", rollout_batch_size=8,
@@ -101,7 +112,7 @@ def main():
     else:
         service = InferenceService(args, dev)
         service.engine.model.init_weights(seed=0)
-    rate, el, samples = asyncio.run(_drive(service, args, a.groups, a.seconds))
+    rate, el, samples = asyncio.run(_drive(service, args, a.groups, a.seconds, a.profile_seconds))
     st = service.get_stats()
     out = {
         "metric": "rollout tok/s",

@@ -181,42 +181,49 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     if ep is not None:
         e_sorted = topi.reshape(-1).index_select(0, order)
         ys, ep_state = ep.forward(model, layer, h, tok, e_sorted, counts, bounds)
+        rows = torch.arange(order.numel(), device=h.device)
         xs = gu = act = None
     elif h.is_cuda and h.dtype == torch.bfloat16:
         lay = padded_layout(counts.tolist(), h.device)
         # row of every (token, slot) pair inside its expert's padded segment
         seg = torch.tensor([lay["starts"][e] - bounds[e] for e in range(len(counts))], device=h.device)
-        pos = torch.arange(order.numel(), device=h.device) + seg.repeat_interleave(counts)
+        rows = torch.arange(order.numel(), device=h.device) + seg.repeat_interleave(counts)
         xs = torch.zeros(lay["total"], h.shape[1], dtype=h.dtype, device=h.device)
-        xs.index_copy_(0, pos, h.index_select(0, tok))
-        ys_pad, gu, act = experts_forward_grouped(model, layer, xs, lay)
-        ys = ys_pad.index_select(0, pos)
+        xs.index_copy_(0, rows, h.index_select(0, tok))
+        ys, gu, act = experts_forward_grouped(model, layer, xs, lay)
     else:
         xs = h.index_select(0, tok)
         ys, gu, act = experts_forward(model, layer, xs, bounds)
-    w_sorted = w_act.reshape(-1).index_select(0, order)
-    y = torch.zeros(h.shape[0], cfg.hidden_size, dtype=torch.float32, device=h.device)
-    y.index_add_(0, tok, ys.float() * w_sorted.float().unsqueeze(1))
+        rows = torch.arange(order.numel(), device=h.device)
+    # per (token, slot) pair in token-major order: its row in ``ys`` and its weight (pairs this rank
+    # does not run keep weight 0)
+    n_pairs = topi.numel()
+    pos_pairs = torch.zeros(n_pairs, dtype=torch.long, device=h.device)
+    pos_pairs[order] = rows
+    w_pairs = torch.zeros(n_pairs, dtype=torch.float32, device=h.device)
+    w_pairs[order] = w_act.reshape(-1).float().index_select(0, order)
+    if ys.shape[0] == 0:
+        # no pair runs here (a tensor-parallel shard whose experts got no tokens): row 0 must exist
+        ys = torch.zeros(1, cfg.hidden_size, dtype=h.dtype, device=h.device)
     cache: Dict[str, torch.Tensor] = {}
+    sy = sg = None
     if cfg.shared_expert_intermediate_size > 0:
         p = f"model.layers.{layer}.mlp."
         sgu = ops.linear(h, model.w(p + "shared_expert.gate_up_proj.weight"))
         sact = ops.swiglu(sgu)
         sy = ops.linear(sact, model.w(p + "shared_expert.down_proj.weight"))
         sg = torch.sigmoid((h @ model.w(p + "shared_expert_gate.weight").t()).float())
-        y += sg * sy.float()
         if save:
             cache.update(sgu=sgu, sact=sact, sy=sy, sg=sg)
-    out = (residual.float() + y).to(h.dtype)
+    out = ops.moe_combine(ys, pos_pairs, w_pairs, k, residual=residual, shared=sy, sg=sg)
     if save:
         cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=xs, gu=gu, act=act, ys=ys,
-                     w_sorted=w_sorted)
+                     pos_pairs=pos_pairs, w_pairs=w_pairs)
         cache["bounds"] = torch.tensor(bounds)
         if ep_state is not None:
             cache["ep_state"] = ep_state  # type: ignore[assignment]
         if lay is not None:
             cache["layout"] = lay  # type: ignore[assignment]
-            cache["pos"] = pos
     return out, cache
 
 
@@ -226,27 +233,26 @@ def moe_backward(model, layer: int, dx3: torch.Tensor, c) -> torch.Tensor:
     h = c.h2
     k = cfg.num_experts_per_tok
     p = f"model.layers.{layer}.mlp."
-    tok, order = m["tok"], m["order"]
-    dxg = dx3.index_select(0, tok)
-    dys = (dxg.float() * m["w_sorted"].float().unsqueeze(1)).to(dx3.dtype)
-    dw_sorted = (dxg.float() * m["ys"].float()).sum(-1)
+    pos_pairs, w_pairs, ys = m["pos_pairs"], m["w_pairs"], m["ys"]
     bounds = m["bounds"].tolist()
     ep = getattr(model, "expert_parallel", None)
+    dx3c = dx3.contiguous()
+    if "layout" in m:
+        lay = m["layout"]
+        dys = torch.zeros(lay["total"], cfg.hidden_size, dtype=dx3.dtype, device=dx3.device)  # pad rows stay 0
+    else:
+        dys = torch.empty(ys.shape[0], cfg.hidden_size, dtype=dx3.dtype, device=dx3.device)
+    dw = ops.moe_combine_backward(dx3c, ys, pos_pairs, w_pairs, k, dys)
     if ep is not None:
         dxs = ep.backward(model, layer, dys, m["ep_state"])
     elif "layout" in m:
-        lay, pos = m["layout"], m["pos"]
-        dys_pad = torch.zeros(lay["total"], cfg.hidden_size, dtype=dys.dtype, device=dys.device)
-        dys_pad.index_copy_(0, pos, dys)
-        dxs = experts_backward_grouped(model, layer, dys_pad, m["xs"], m["gu"], m["act"], lay).index_select(0, pos)
+        dxs = experts_backward_grouped(model, layer, dys, m["xs"], m["gu"], m["act"], m["layout"])
     else:
         dxs = experts_backward(model, layer, dys, m["xs"], m["gu"], m["act"], bounds)
-    dh = torch.zeros(h.shape[0], cfg.hidden_size, dtype=torch.float32, device=h.device)
-    dh.index_add_(0, tok, dxs.float())
+    # every pair's input-gradient row back to its token (unit weights)
+    dh = ops.moe_combine(dxs, pos_pairs, torch.ones_like(w_pairs), k).float()
     # router
-    dtopw = torch.zeros(order.numel(), dtype=torch.float32, device=h.device)
-    dtopw[order] = dw_sorted
-    dtopw = dtopw.view(-1, k)
+    dtopw = dw.view(-1, k)
     topw = m["topw"]
     if cfg.norm_topk_prob:
         probs_k = m["probs"].gather(1, m["topi"])

@@ -388,6 +388,37 @@ def policy_loss(lp, old_lp, adv, cfg, loss_scale: float):
     return g, stats
 
 
+def moe_combine(ys, pos, w, k: int, residual=None, shared=None, sg=None, out=None) -> torch.Tensor:
+    """MoE combine per token t: ``residual[t] + sum_j w[t,j] * ys[pos[t,j]] + sg[t] * shared[t]``
+    (fp32 accumulation). ``pos``/``w``: int64 / fp32 per (token, slot) pair in token-major order."""
+    T, H = pos.numel() // k, ys.shape[1]
+    if ys.is_cuda:
+        out = out if out is not None else torch.empty(T, H, dtype=ys.dtype, device=ys.device)
+        native().moe_combine_fwd(ys, pos, w, k, residual, shared, None if sg is None else sg.reshape(-1), out)
+        return out
+    y = residual.float() if residual is not None else torch.zeros(T, H, dtype=torch.float32, device=ys.device)
+    y = y + (ys.float().index_select(0, pos) * w.float().unsqueeze(1)).view(T, k, H).sum(1)
+    if shared is not None:
+        y = y + sg.reshape(-1, 1).float() * shared.float()
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y.to(ys.dtype)
+
+
+def moe_combine_backward(dout, ys, pos, w, k: int, dys_out) -> torch.Tensor:
+    """Backward of ``moe_combine`` w.r.t. the expert rows and the weights: writes
+    ``dys_out[pos[t,j]] = w[t,j] * dout[t]`` and returns ``dw[t,j] = <dout[t], ys[pos[t,j]]>`` (fp32)."""
+    if dout.is_cuda:
+        dw = torch.empty(pos.numel(), dtype=torch.float32, device=dout.device)
+        native().moe_combine_bwd(dout.contiguous(), ys, pos, w, k, dys_out, dw)
+        return dw
+    g = dout.float().repeat_interleave(k, 0)
+    dw = (g * ys.float().index_select(0, pos)).sum(-1)
+    dys_out.index_copy_(0, pos, (g * w.float().unsqueeze(1)).to(dys_out.dtype))
+    return dw
+
+
 def weight_pull(plan, src_addr: int, dst: torch.Tensor) -> None:
     """Run a copy plan (``weight_map.descs_tensor``) from the device address ``src_addr`` (a peer
     GPU's buffer mapped by CUDA IPC, or a local one) into ``dst``."""

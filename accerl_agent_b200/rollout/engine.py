@@ -620,7 +620,7 @@ class GenerationEngine:
         meta[2 * bucket : 3 * bucket] = -1
         meta[3 * bucket : 4 * bucket] = 1
         meta[5 * bucket :] = self.scratch_block
-        splits = self.decode_splits or max(1, min(16, (148 * 2) // max(bucket * self.cfg.num_key_value_heads, 1)))
+        splits = self.decode_splits or _decode_splits(bucket * self.cfg.num_key_value_heads)
         offs = torch.zeros(bucket, dtype=torch.int64, device=dev)
 
         def run():
@@ -775,7 +775,7 @@ class GenerationEngine:
         m = self.model
         D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         scale = 1.0 / math.sqrt(D)
-        splits = self.decode_splits or max(1, min(16, (148 * 2) // max(nd * Hkv, 1)))
+        splits = self.decode_splits or _decode_splits(nd * Hkv)
 
         def attn_fn(layer, q, kc, vc):
             attn = torch.empty(q.shape[0], cfg.q_dim, dtype=q.dtype, device=dev)
@@ -877,7 +877,7 @@ class GenerationEngine:
                 reason = self._stop_reason(seq, int(tok))
                 if reason is not None:
                     self._finish(seq, reason)
-                else:
+                elif seq.params.output_kind != "final_only":
                     self._deliver(seq, False)
 
     def _stop_reason(self, seq: _Seq, tok: int) -> Optional[str]:
@@ -894,6 +894,11 @@ class GenerationEngine:
         if len(seq.out) >= p.max_tokens or seq.length >= self.max_model_len:
             return "length"
         return None
+
+
+def _decode_splits(ctas_per_split: int) -> int:
+    """Sequence splits of the paged decode kernel: about 4 CTAs per SM (148 SMs), at most 16."""
+    return max(1, min(16, -(-4 * 148 // max(ctas_per_split, 1))))
 
 
 def _sample_filtered(logits: torch.Tensor, params: List[SamplingParams], seeds: torch.Tensor):

@@ -37,12 +37,15 @@ class SamplingParams:
     skip_special_tokens: bool = True
     frequency_penalty: float = 0.0
     seed: Optional[int] = None
+    # "cumulative": a RequestOutput after every step (streaming); "final_only": only the finished
+    # (or aborted) output, which saves the per-step hand-off for callers that use only the last one
+    output_kind: str = "cumulative"
 
     def __init__(self, **kwargs: Any):
         for name, default in (
             ("temperature", 1.0), ("top_p", 1.0), ("top_k", -1), ("max_tokens", 16), ("stop", None),
             ("stop_token_ids", None), ("ignore_eos", False), ("logprobs", None), ("skip_special_tokens", True),
-            ("frequency_penalty", 0.0), ("seed", None),
+            ("frequency_penalty", 0.0), ("seed", None), ("output_kind", "cumulative"),
         ):
             setattr(self, name, kwargs.pop(name, default))
         kwargs.pop("use_beam_search", None)
@@ -180,6 +183,8 @@ class InterruptibleGenerationRunner:
             }
             if self.collect_logprobs:
                 kwargs["logprobs"] = 1
+            if self.sampling_params_cls is SamplingParams:
+                kwargs["output_kind"] = "final_only"  # only the last output of an attempt is used
             params = self.sampling_params_cls(**kwargs)
             request_id = f"online-sync-{state.index}-v{attempt_version}-try{attempt}-{uuid.uuid4()}"
             final_output = None

@@ -24,6 +24,10 @@ int accerl_row_scatter(const void* src, long long ld, const long long* src_row, 
 int accerl_tp_allreduce(const long long* peer_data, const long long* peer_flags, int world, int rank, int slot,
                         long long slot_elems, long long n, const void* residual, void* out, int* ctr, int* status,
                         cudaStream_t s);
+int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w, long long T, int k, int H,
+                           const void* residual, const void* shared, const float* sg, void* out, cudaStream_t s);
+int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* pos, const float* w, long long T, int k,
+                           int H, void* dys, float* dw, cudaStream_t s);
 int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
                        const void* src, void* dst, cudaStream_t s);
 int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
@@ -199,6 +203,39 @@ void tp_allreduce(const at::Tensor& peer_data, const at::Tensor& peer_flags, int
                             slot_elems, n, residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(),
                             ctr.data_ptr<int>(), status.data_ptr<int>(), cur_stream()),
         "tp_allreduce");
+}
+
+void moe_combine_fwd(const at::Tensor& ys, const at::Tensor& pos, const at::Tensor& w, int64_t k,
+                     const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& shared,
+                     const c10::optional<at::Tensor>& sg, at::Tensor& out) {
+  CHECK_BF16(ys);
+  CHECK_BF16(out);
+  CHECK_F32(w);
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.is_contiguous() && w.is_contiguous(), "moe_combine: pos/w");
+  TORCH_CHECK(ys.is_contiguous() && out.is_contiguous(), "moe_combine: contiguous rows");
+  if (residual.has_value()) TORCH_CHECK(residual->is_contiguous() && residual->scalar_type() == at::kBFloat16);
+  if (shared.has_value()) TORCH_CHECK(shared->is_contiguous() && shared->scalar_type() == at::kBFloat16);
+  check(accerl_moe_combine_fwd(ys.data_ptr(), reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()),
+                               w.data_ptr<float>(), pos.numel() / k, static_cast<int>(k), static_cast<int>(ys.size(1)),
+                               residual.has_value() ? residual->data_ptr() : nullptr,
+                               shared.has_value() ? shared->data_ptr() : nullptr,
+                               sg.has_value() ? sg->data_ptr<float>() : nullptr, out.data_ptr(), cur_stream()),
+        "moe_combine_fwd");
+}
+
+void moe_combine_bwd(const at::Tensor& dout, const at::Tensor& ys, const at::Tensor& pos, const at::Tensor& w,
+                     int64_t k, at::Tensor& dys, at::Tensor& dw) {
+  CHECK_BF16(dout);
+  CHECK_BF16(ys);
+  CHECK_BF16(dys);
+  CHECK_F32(w);
+  CHECK_F32(dw);
+  TORCH_CHECK(pos.scalar_type() == at::kLong && dout.is_contiguous() && ys.is_contiguous() && dys.is_contiguous(),
+              "moe_combine_bwd: layouts");
+  check(accerl_moe_combine_bwd(dout.data_ptr(), ys.data_ptr(), reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()),
+                               w.data_ptr<float>(), pos.numel() / k, static_cast<int>(k), static_cast<int>(ys.size(1)),
+                               dys.data_ptr(), dw.data_ptr<float>(), cur_stream()),
+        "moe_combine_bwd");
 }
 
 void row_scatter(const at::Tensor& src, const c10::optional<at::Tensor>& src_row, const at::Tensor& dst_addr) {
@@ -493,6 +530,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &grouped_gemm);
   m.def("row_scatter", &row_scatter);
   m.def("weight_pull", &weight_pull);
+  m.def("moe_combine_fwd", &moe_combine_fwd);
+  m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("tp_allreduce", &tp_allreduce);
   m.def("ipc_export", &ipc_export);
   m.def("ipc_open", &ipc_open);

@@ -1,0 +1,161 @@
+// MoE combine kernels (sm_100a), one block per token row:
+//  combine_fwd  out[t] = residual[t] + sum_j w[t,j] * ys[pos[t,j]] + sg[t] * shared[t]
+//               (fp32 accumulation, bf16 out; residual / shared expert optional)
+//  combine_bwd  dys[pos[t,j]] = w[t,j] * dout[t]  (bf16 rows of the expert-output gradient)
+//               dw[t,j] = <dout[t], ys[pos[t,j]]> (fp32 gradient of the routing weight)
+// pos maps a (token, slot) pair to its row in the expert-ordered buffer (padded segments or the
+// sorted order of an expert-parallel exchange). H must be a multiple of 8 and k <= 8.
+#include "common.cuh"
+
+namespace accerl {
+
+constexpr int kMoeMaxK = 8;
+
+__global__ void moe_combine_fwd_kernel(const __nv_bfloat16* __restrict__ ys, const long long* __restrict__ pos,
+                                       const float* __restrict__ w, int k, int H,
+                                       const __nv_bfloat16* __restrict__ residual,
+                                       const __nv_bfloat16* __restrict__ shared, const float* __restrict__ sg,
+                                       __nv_bfloat16* __restrict__ out) {
+  const long long t = blockIdx.x;
+  const int nv = H / 8;
+  __shared__ long long rows[kMoeMaxK];
+  __shared__ float ws[kMoeMaxK];
+  if (threadIdx.x < k) {
+    rows[threadIdx.x] = pos[t * k + threadIdx.x];
+    ws[threadIdx.x] = w[t * k + threadIdx.x];
+  }
+  __syncthreads();
+  const float g = sg ? sg[t] : 0.f;
+  for (int c = threadIdx.x; c < nv; c += blockDim.x) {
+    float acc[8];
+    if (residual) {
+      const uint4 r = reinterpret_cast<const uint4*>(residual + t * H)[c];
+      const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(rw[i]);
+        acc[2 * i] = f.x;
+        acc[2 * i + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    }
+    for (int j = 0; j < k; ++j) {
+      const uint4 v = reinterpret_cast<const uint4*>(ys + rows[j] * H)[c];
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+      const float wj = ws[j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(vw[i]);
+        acc[2 * i] += wj * f.x;
+        acc[2 * i + 1] += wj * f.y;
+      }
+    }
+    if (shared) {
+      const uint4 v = reinterpret_cast<const uint4*>(shared + t * H)[c];
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(vw[i]);
+        acc[2 * i] += g * f.x;
+        acc[2 * i + 1] += g * f.y;
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + t * H)[c] = o;
+  }
+}
+
+__global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ ys,
+                                       const long long* __restrict__ pos, const float* __restrict__ w, int k, int H,
+                                       __nv_bfloat16* __restrict__ dys, float* __restrict__ dw) {
+  const long long t = blockIdx.x;
+  const int nv = H / 8;
+  __shared__ long long rows[kMoeMaxK];
+  __shared__ float ws[kMoeMaxK];
+  __shared__ float red[kMoeMaxK][8];
+  if (threadIdx.x < k) {
+    rows[threadIdx.x] = pos[t * k + threadIdx.x];
+    ws[threadIdx.x] = w[t * k + threadIdx.x];
+  }
+  __syncthreads();
+  float dot[kMoeMaxK];
+#pragma unroll
+  for (int j = 0; j < kMoeMaxK; ++j) dot[j] = 0.f;
+  for (int c = threadIdx.x; c < nv; c += blockDim.x) {
+    const uint4 d = reinterpret_cast<const uint4*>(dout + t * H)[c];
+    const uint32_t dwd[4] = {d.x, d.y, d.z, d.w};
+    float g[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(dwd[i]);
+      g[2 * i] = f.x;
+      g[2 * i + 1] = f.y;
+    }
+#pragma unroll
+    for (int j = 0; j < kMoeMaxK; ++j) {
+      if (j >= k) break;
+      const uint4 v = reinterpret_cast<const uint4*>(ys + rows[j] * H)[c];
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(vw[i]);
+        s += g[2 * i] * f.x + g[2 * i + 1] * f.y;
+      }
+      dot[j] += s;
+      const float wj = ws[j];
+      uint4 o;
+      o.x = pack_bf16x2(wj * g[0], wj * g[1]);
+      o.y = pack_bf16x2(wj * g[2], wj * g[3]);
+      o.z = pack_bf16x2(wj * g[4], wj * g[5]);
+      o.w = pack_bf16x2(wj * g[6], wj * g[7]);
+      reinterpret_cast<uint4*>(dys + rows[j] * H)[c] = o;
+    }
+  }
+  // block reduction of the k dot products (blockDim.x <= 256: 8 warps)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kMoeMaxK; ++j) {
+    if (j >= k) break;
+    const float v = warp_sum(dot[j]);
+    if (lane == 0) red[j][warp] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < k) {
+    float s = 0.f;
+    for (int i = 0; i < (blockDim.x >> 5); ++i) s += red[threadIdx.x][i];
+    dw[t * k + threadIdx.x] = s;
+  }
+}
+
+}  // namespace accerl
+
+using namespace accerl;
+
+extern "C" int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w, long long T, int k, int H,
+                                      const void* residual, const void* shared, const float* sg, void* out,
+                                      cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 || k < 1 || k > kMoeMaxK) return -1;
+  const int threads = min(256, max(32, ((H / 8 + 31) / 32) * 32));
+  moe_combine_fwd_kernel<<<(unsigned)T, threads, 0, s>>>((const __nv_bfloat16*)ys, pos, w, k, H,
+                                                         (const __nv_bfloat16*)residual, (const __nv_bfloat16*)shared,
+                                                         sg, (__nv_bfloat16*)out);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* pos, const float* w, long long T,
+                                      int k, int H, void* dys, float* dw, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (H % 8 || k < 1 || k > kMoeMaxK) return -1;
+  const int threads = min(256, max(32, ((H / 8 + 31) / 32) * 32));
+  moe_combine_bwd_kernel<<<(unsigned)T, threads, 0, s>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)ys, pos, w,
+                                                         k, H, (__nv_bfloat16*)dys, dw);
+  return (int)cudaGetLastError();
+}

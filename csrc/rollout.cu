@@ -62,9 +62,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __nv_bfloat16* 
     for (int h = 0; h < G; ++h) sc[h] = 0.f;
     if (valid) {
       const uint4* kr = reinterpret_cast<const uint4*>(k_cache + off);
-#pragma unroll 4
+      uint4 krow[kDHead / 8];  // the whole 256-byte K row in flight at once
+#pragma unroll
+      for (int c = 0; c < kDHead / 8; ++c) krow[c] = kr[c];
+#pragma unroll
       for (int c = 0; c < kDHead / 8; ++c) {
-        const uint4 kv = kr[c];
+        const uint4 kv = krow[c];
         const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -88,18 +91,29 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __nv_bfloat16* 
       p_s[warp][h][lane] = pv;
     }
     __syncwarp();
+    // P.V: lanes own 4 head dims; 8 V rows are loaded before their FMAs so the loads overlap.
+    // Invalid tokens have p = 0 and offset 0 (a valid row of the cache), so no guards are needed.
     const int nvalid = min(32, t1 - base);
-    for (int t = 0; t < nvalid; ++t) {
-      const long long o = __shfl_sync(0xffffffffu, off, t);
-      const uint2 vv = *reinterpret_cast<const uint2*>(v_cache + o + lane * 4);
-      const float2 v0 = unpack_bf16x2(vv.x), v1 = unpack_bf16x2(vv.y);
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float pv = p_s[warp][h][t];
-        acc[h][0] += pv * v0.x;
-        acc[h][1] += pv * v0.y;
-        acc[h][2] += pv * v1.x;
-        acc[h][3] += pv * v1.y;
+    for (int tb = 0; tb < 32; tb += 8) {
+      if (tb >= nvalid) break;
+      uint2 vv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const long long o = __shfl_sync(0xffffffffu, off, tb + j);
+        vv[j] = *reinterpret_cast<const uint2*>(v_cache + o + lane * 4);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 v0 = unpack_bf16x2(vv[j].x), v1 = unpack_bf16x2(vv[j].y);
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          const float pv = p_s[warp][h][tb + j];
+          acc[h][0] += pv * v0.x;
+          acc[h][1] += pv * v0.y;
+          acc[h][2] += pv * v1.x;
+          acc[h][3] += pv * v1.y;
+        }
       }
     }
     __syncwarp();

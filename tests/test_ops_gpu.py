@@ -344,3 +344,25 @@ def test_grouped_expert_gemms_match_per_expert_products():
             assert _rel(y[s : s + c], xe @ We.t()) < 1e-2
             assert _rel(dx[s : s + c], dye @ We) < 1e-2
         assert _rel(gW[e * N : (e + 1) * N], 1.0 + dye.t() @ xe) < 1e-5
+
+
+def test_moe_combine_fwd_bwd():
+    T, k, H, R = 300, 4, 2048, 1600
+    ys = torch.randn(R, H, device=DEV).bfloat16()
+    pos = torch.randperm(R, device=DEV)[: T * k]
+    w = torch.rand(T * k, device=DEV)
+    res = torch.randn(T, H, device=DEV).bfloat16()
+    sh = torch.randn(T, H, device=DEV).bfloat16()
+    sg = torch.rand(T, 1, device=DEV)
+    out = ops.moe_combine(ys, pos, w, k, residual=res, shared=sh, sg=sg)
+    ref = res.float() + (ys.float()[pos] * w[:, None]).view(T, k, H).sum(1) + sg * sh.float()
+    assert _rel(out, ref) < 1e-2
+    dout = torch.randn(T, H, device=DEV).bfloat16()
+    dys = torch.zeros(R, H, device=DEV, dtype=torch.bfloat16)
+    dw = ops.moe_combine_backward(dout, ys, pos, w, k, dys)
+    g = dout.float().repeat_interleave(k, 0)
+    assert _rel(dw, (g * ys.float()[pos]).sum(-1)) < 1e-3
+    assert _rel(dys[pos], g * w[:, None]) < 1e-2
+    untouched = torch.ones(R, dtype=torch.bool, device=DEV)
+    untouched[pos] = False
+    assert bool((dys[untouched] == 0).all())
