@@ -3,11 +3,12 @@
 // Forward, one CTA per (128-query tile, q head, sequence), 6 warps:
 //   warp 4     TMA producer: the Q tile once, then K/V tiles of 128 keys into a 2-stage ring.
 //   warp 5     MMA issuer: S_j = Q K_j^T into one of two TMEM score buffers, then O += P_{j-1} V_{j-1}
-//              (P from shared memory, V as an MN-major operand) into a TMEM output accumulator.
+//              with P read from TMEM (V as an MN-major smem operand) into a TMEM output accumulator.
 //   warps 0-3  softmax, one query row per thread (= one TMEM lane): tcgen05.ld the score row, mask,
-//              online max/sum in the log2 domain, write P (bf16, 128B-swizzled K-major) to smem.
-//              O is rescaled in TMEM only when the running max grows by more than 2^8, so most
-//              blocks need no correction pass; the final normalisation uses the same stale max.
+//              online max/sum in the log2 domain, write P as bf16 back into the first 64 columns of
+//              the same score buffer. O is rescaled in TMEM only when the running max grows by more
+//              than 2^8, and only then does the tile wait for the previous PV MMA, so the softmax of
+//              tile j+1 overlaps the PV MMA of tile j; the final normalisation uses the same stale max.
 // Backward, one CTA per (128-key tile, q head, sequence): S^T = K Q^T and dP^T = V dO^T land in TMEM,
 // the softmax warps (one key row per thread) rebuild P^T and dS^T into smem, then dV += P^T dO,
 // dK += dS^T Q (accumulated in TMEM over all query tiles) and dQ_i = dS_i K (TMEM, drained with fp32
@@ -79,17 +80,16 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + kTileBytes;
   uint8_t* sV = sK + 2 * kTileBytes;
-  uint8_t* sP = sV + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + 2 * kTileBytes);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;     // [2]
   uint64_t* v_full = bars + 3;     // [2]
   uint64_t* kv_empty = bars + 5;   // [2]
   uint64_t* s_full = bars + 7;     // [2]
-  uint64_t* s_free = bars + 9;     // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;   // after every PV (waited only before a rescale: at most one behind)
+  uint64_t* o_final = bars + 11;  // once, after the last PV
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -100,10 +100,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 128);
     }
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
     fence_mbar_init();
   }
   if (warp == 5) tmem_alloc(tmem_slot, 512);
@@ -144,13 +144,12 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
       bool ok = mbar_wait(q_full, 0, p.status, kStatusTimeoutMma);
       for (int j = 0; j <= n_kv && ok; ++j) {
         if (j < n_kv) {
           const int s = j & 1;
           if (!mbar_wait(&k_full[s], (j >> 1) & 1, p.status, kStatusTimeoutMma)) break;
-          if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1u, p.status, kStatusTimeoutMma)) break;
+          // buffer s held P_{j-2}; PV_{j-2} was issued before this MMA, and tcgen05.mma executes in issue order
           tc_fence_after();
           const uint32_t k_addr = smem_u32(sK + s * kTileBytes);
 #pragma unroll
@@ -167,11 +166,12 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t v_addr = smem_u32(sV + s2 * kTileBytes);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_bf16(tO, desc_kmajor(p_addr, kk), desc_mnmajor(v_addr, kk), idesc_o, (jj > 0) || (kk > 0));
+            umma_bf16_ts(tO, tS + s2 * 128 + kk * 8, desc_mnmajor(v_addr, kk), idesc_o, (jj > 0) || (kk > 0));
           umma_commit(o_done);
           umma_commit(&kv_empty[s2]);
         }
       }
+      umma_commit(o_final);
     }
   } else {
     // ---------------- softmax warps 0..3: thread = query row ----------------
@@ -199,8 +199,6 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[c][e]) * p.scale_log2;
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[bsel]);
       const int kbase = j * kTile;
       if ((p.causal && kbase + kTile - 1 > q_tile * kTile + k_off) || kbase + kTile > len_k) {
         const int lim = q_pos + k_off;
@@ -213,13 +211,6 @@ __global__ void __launch_bounds__(192, 1)
       float mx = x[0];
 #pragma unroll
       for (int e = 1; e < 128; ++e) mx = fmaxf(mx, x[e]);
-      if (j > 0) {
-        if (!mbar_wait(o_done, (j - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
       const float m_new = fmaxf(m_used, mx);
       const bool need = m_new > m_used + 8.0f;
       float alpha = 1.f;
@@ -229,6 +220,13 @@ __global__ void __launch_bounds__(192, 1)
         l *= alpha;
       }
       if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O may only be rescaled once PV_{j-1} has landed. s_full(j) covered every MMA issued before
+        // S_j (PV_{j-2} included), so o_done is at most one completion behind and its parity is exact.
+        if (!mbar_wait(o_done, (j - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
@@ -241,23 +239,25 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_st();
       }
       const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+      // P (bf16, two per 32-bit column) back into the first 64 columns of this tile's S buffer: the
+      // PV MMA reads it as its TMEM A operand
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        uint32_t w[4];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t w[32];
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float p0 = exp2f(x[u * 8 + 2 * h] - m_eff);
-          const float p1 = exp2f(x[u * 8 + 2 * h + 1] - m_eff);
+        for (int u = 0; u < 32; ++u) {
+          const float p0 = exp2f(x[half * 64 + 2 * u] - m_eff);
+          const float p1 = exp2f(x[half * 64 + 2 * u + 1] - m_eff);
           l += p0 + p1;
-          w[h] = pack_bf16x2(p0, p1);
+          w[u] = pack_bf16x2(p0, p1);
         }
-        *reinterpret_cast<uint4*>(sP + swz_offset(r, u)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st32(tS + bsel * 128 + half * 32 + lane_off, w);
       }
-      fence_async_shared();
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    if (ok && mbar_wait(o_done, (n_kv - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+    if (ok && mbar_wait(o_final, 0, p.status, kStatusTimeoutEpilogue)) {
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = q_pos < len;
@@ -625,7 +625,7 @@ bool attn_map(CUtensorMap* m, const void* ptr, int T, int width, long long ld) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr int kFwdSmem = 6 * kTileBytes + 1024 + 256;
+constexpr int kFwdSmem = 5 * kTileBytes + 1024 + 256;
 constexpr int kBwdSmem = 6 * kTileBytes + 1024 + 1024 + 256;
 
 }  // namespace

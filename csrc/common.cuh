@@ -173,6 +173,20 @@ ACCERL_DEVINL void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, ui
       : "memory");
 }
 
+// D (+)= A * B with A read from tensor memory (M rows = TMEM lanes, K packed two bf16 per 32-bit
+// column, so a K step of 16 advances 8 columns) and B from shared memory.
+ACCERL_DEVINL void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "setp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Signal `bar` once every previously issued tcgen05.mma of this thread has completed.
 ACCERL_DEVINL void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -229,7 +243,6 @@ ACCERL_DEVINL void red_add_v4(float* addr, float a, float b, float c, float d) {
                : "memory");
 }
 
-// Make generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma operand reads).
 // System-scope release store / acquire load of a 32-bit flag (cross-GPU signalling over NVLink).
 ACCERL_DEVINL void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -246,6 +259,7 @@ ACCERL_DEVINL uint4 ld_cg_v4(const void* p) {
   return v;
 }
 
+// Make generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma operand reads).
 ACCERL_DEVINL void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Named barrier among a subset of warps (id 1..15; id 0 is __syncthreads).
