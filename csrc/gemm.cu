@@ -469,8 +469,8 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   if (residual && ((ldr % 8) != 0 || (reinterpret_cast<uintptr_t>(residual) & 15))) return -4;
   if (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) return -5;
   // Tile width and split-K are chosen to minimise wave quantisation: estimated time ~
-  // ceil(work_items / SMs) * (k_blocks / splits) * tile_cost, with a 256-wide tile costing ~2x a
-  // 128-wide one. Split-K is only possible for fp32 outputs accumulated with beta = 1.
+  // ceil(work_items / SMs) * (k_blocks / splits) * tile_cost, with a 128-wide tile costing ~0.68x a
+  // 256-wide one. Split-K is only possible for fp32 outputs accumulated with beta = 1.
   const int sms = num_sms();
   const int k_blocks_all = (K + kBK - 1) / kBK;
   const bool can_split = c_f32 && beta == 1.f && !bias && !residual;
@@ -493,8 +493,10 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
         if (sp > 1 && k_blocks_all / sp < 4) break;
         const long long items = tiles * sp;
         const double waves = (double)((items + sms - 1) / sms);
+        // A 128-wide tile moves as many A bytes per MMA as B bytes and sits at the shared-memory operand
+        // bandwidth limit: measured tensor-pipe utilisation 0.47 vs 0.66 for 256-wide tiles (ncu)
         const double t = waves * ((double)((k_blocks_all + sp - 1) / sp)) * (cand == 256 ? 2.0 : 1.0) *
-                         (cand == 256 ? 1.0 : 1.08);  // 128-wide tiles re-read A twice as often
+                         (cand == 256 ? 1.0 : 1.35);
         if (t < best * 0.97) {
           best = t;
           bn = cand;
