@@ -128,7 +128,7 @@ def main():
         "engine_steps": st["steps"],
         "preemptions": st["preemptions"],
         "step_phase_ms": {k[2:-2]: round(1e3 * st[k] / max(st["steps"], 1), 3)
-                          for k in ("t_schedule_s", "t_prefill_s", "t_decode_s", "t_post_s")},
+                          for k in ("t_schedule_s", "t_launch_s", "t_complete_s")},
         "rows_per_step": {"prefill": round(st["prefill_rows"] / max(st["steps"], 1), 1),
                           "decode": round(st["decode_rows"] / max(st["steps"], 1), 1)},
     }

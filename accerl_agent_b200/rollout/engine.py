@@ -74,6 +74,8 @@ class _Seq:
     finish_reason: Optional[str] = None
     arrival: float = 0.0
     toks: List[int] = field(default_factory=list)  # prompt + out, kept in step (no per-access concat)
+    slot: int = -1     # row of the engine's device-side last-token table
+    pending: int = 0   # 1 while a sampled token is on the device but not yet on the host
 
     def __post_init__(self) -> None:
         self.toks = list(self.prompt)
@@ -89,7 +91,8 @@ class _Seq:
 
     @property
     def length(self) -> int:
-        return len(self.toks)
+        """Logical length: known tokens plus the one still on the device."""
+        return len(self.toks) + self.pending
 
 
 class GenerationEngine:
@@ -113,6 +116,7 @@ class GenerationEngine:
         layout: Optional[ParamLayout] = None,
         tp_group=None,
         cmd_group=None,
+        async_steps: bool = True,
     ):
         """``layout``: flat parameter layout of the engine (default: the full-model layout); pass the
         trainer's layout to make weight syncs plain range copies. ``tp_group``/``cmd_group``: process
@@ -184,6 +188,21 @@ class GenerationEngine:
                                 and (self.tp == 1 or self._tp_ar is not None))
         self._graphs: Dict[Any, Any] = {}
         self._graph_pool = None
+        # Asynchronous steps: step N+1 is launched before the tokens of step N reach the host. A decode
+        # row reads its input token from a device table indexed by the sequence's slot (written by the
+        # sampler), stop conditions are applied one step late, and a row launched for a sequence that
+        # turned out to be finished is discarded.
+        self.async_steps = async_steps
+        n_slots = 2 * max_num_seqs + 1
+        self._slot_tok = torch.zeros(n_slots, dtype=torch.long, device=device)
+        self._dummy_slot = n_slots - 1
+        self._free_slots = list(range(n_slots - 1))
+        self._inflight = None
+        self._pin_ring: List[torch.Tensor] = []
+        self._pin_next = 0
+        self._in_ring: List[List[Any]] = []
+        self._in_next = 0
+        self._res_rows = max(max_num_seqs, max(self._BUCKETS))
         self.waiting: Deque[_Seq] = deque()
         self.running: List[_Seq] = []
         self.by_id: Dict[str, _Seq] = {}
@@ -196,8 +215,9 @@ class GenerationEngine:
         self.decode_splits = decode_splits
         self.stats = {"generated_tokens": 0, "prompt_tokens_computed": 0, "steps": 0, "preemptions": 0,
                       "aborted": 0, "finished": 0, "prefill_rows": 0, "decode_rows": 0,
-                      # host wall time per step phase (the prefill and decode phases include their GPU work)
-                      "t_schedule_s": 0.0, "t_prefill_s": 0.0, "t_decode_s": 0.0, "t_post_s": 0.0}
+                      # host wall time per step phase: scheduling, building and launching the step, and
+                      # completing the previous one (waiting for its samples, appending, stop checks)
+                      "t_schedule_s": 0.0, "t_launch_s": 0.0, "t_complete_s": 0.0}
         self._thread: Optional[threading.Thread] = None
         self.eos_ids = {cfg.eos_token_id}
         if tokenizer is not None and getattr(tokenizer, "eos_token_id", None) is not None:
@@ -221,7 +241,8 @@ class GenerationEngine:
     def _run_loop(self) -> None:
         while True:
             with self._lock:
-                while not self._stop and (self.paused or (not self.waiting and not self.running)):
+                while not self._stop and self._inflight is None and (
+                        self.paused or (not self.waiting and not self.running)):
                     self._wake.wait(timeout=0.5)
                 if self._stop:
                     return
@@ -271,6 +292,8 @@ class GenerationEngine:
     async def pause_generation(self, mode: str = "abort", clear_cache: bool = True) -> None:
         """Stop scheduling; with ``mode='abort'`` every in-flight request ends with reason 'abort'."""
         def _pause():
+            with self._step_lock:
+                self._flush()
             with self._step_lock, self._lock:
                 self.paused = True
                 if mode == "abort":
@@ -310,12 +333,14 @@ class GenerationEngine:
         from ..models.hf_io import load_hf_checkpoint
 
         with self._step_lock:
+            self._flush()
             load_hf_checkpoint(self.model, path)
             self.allocator.clear_cache()
 
     def load_flat_weights(self, src: torch.Tensor, start: int = 0, stream=None) -> None:
         """Copy a fused-layout flat weight range (from a trainer, possibly a peer GPU's memory)."""
         with self._step_lock:
+            self._flush()
             dst = self.model.params[start : start + src.numel()]
             if stream is not None:
                 with torch.cuda.stream(stream):
@@ -340,6 +365,7 @@ class GenerationEngine:
         """Copy this engine's slice of the registered trainer buffer into its weights (every TP rank
         pulls its own shard). Returns the bytes this rank copied."""
         with self._step_lock:
+            self._flush()
             if self.tp > 1 and self.tp_rank == 0:
                 import torch.distributed as dist
 
@@ -390,6 +416,10 @@ class GenerationEngine:
 
     def _finish(self, seq: _Seq, reason: str, error: Optional[BaseException] = None) -> None:
         seq.finish_reason = reason
+        if seq.slot >= 0:
+            # a row still in flight may write this slot; the next owner writes it later in stream order
+            self._free_slots.append(seq.slot)
+            seq.slot = -1
         if seq in self.running:
             self.running.remove(seq)
         try:
@@ -461,6 +491,12 @@ class GenerationEngine:
                 budget -= n
             while self.waiting and budget > 0 and len(self.running) < self.max_num_seqs:
                 seq = self.waiting[0]
+                if seq.pending:
+                    break  # preempted with a token in flight: re-admit once it is on the host
+                if seq.slot < 0:
+                    if not self._free_slots:
+                        break
+                    seq.slot = self._free_slots.pop()
                 if seq.num_computed == 0 and not seq.blocks:
                     self._admit(seq)
                 n = min(seq.length - seq.num_computed, budget)
@@ -479,40 +515,101 @@ class GenerationEngine:
         with self._step_lock:
             t0 = time.perf_counter()
             plan = self._schedule()
-            if not plan:
-                return False
             t1 = time.perf_counter()
-            # prefill-first: multi-token chunks run in their own (eager) step with the varlen kernel over
-            # their cached prefix; steps where every scheduled sequence advances by one token run the
-            # paged decode path, replayed from a captured CUDA graph when possible
-            prefill = [p for p in plan if p[2] > 1]
-            decode = [p for p in plan if p[2] == 1]
-            if self.use_cuda_graphs and decode and all(p[3] for p in decode):
-                # two passes per step: prefill chunks eagerly, then all decode rows from one graph replay
-                toks, logps = self._execute(prefill, len(prefill)) if prefill else ([], [])
-                t2 = time.perf_counter()
-                dt, dl = self._execute_decode_graph(decode)
-                order = prefill + decode
-                toks, logps = toks + dt, logps + dl
-            else:
-                order = prefill + decode
-                toks, logps = self._execute(order, len(prefill))
-                t2 = time.perf_counter()
+            launched = self._launch(plan) if plan else None
+            t2 = time.perf_counter()
+            prev, self._inflight = self._inflight, launched
+            if prev is not None:
+                self._complete(prev)
+            if not self.async_steps and self._inflight is not None:
+                cur, self._inflight = self._inflight, None
+                self._complete(cur)
             t3 = time.perf_counter()
-            self._postprocess(order, toks, logps)
-            t4 = time.perf_counter()
+            if plan is None and prev is None:
+                return False
             st = self.stats
-            st["steps"] += 1
-            st["prefill_rows"] += sum(p[2] for p in prefill)
-            st["decode_rows"] += len(decode)
+            if plan:
+                st["steps"] += 1
+                st["prefill_rows"] += sum(p[2] for p in plan if p[2] > 1)
+                st["decode_rows"] += sum(1 for p in plan if p[2] == 1)
             st["t_schedule_s"] += t1 - t0
-            st["t_prefill_s"] += t2 - t1
-            st["t_decode_s"] += t3 - t2
-            st["t_post_s"] += t4 - t3
+            st["t_launch_s"] += t2 - t1
+            st["t_complete_s"] += t3 - t2
             return True
 
-    # ------------------------------------------------------------------ CUDA-graph decode
-    _BUCKETS = (8, 16, 32, 64, 128, 256, 512)
+    def _launch(self, plan) -> Dict[str, Any]:
+        """Launch one step (prefill chunks eagerly, single-token rows from a decode graph when all of
+        them sample) and commit its optimistic bookkeeping. Returns the handle ``_complete`` reads."""
+        prefill = [p for p in plan if p[2] > 1]
+        decode = [p for p in plan if p[2] == 1]
+        parts = []
+        if self.use_cuda_graphs and decode and all(p[3] for p in decode):
+            if prefill:
+                parts.append((prefill, self._execute(prefill, len(prefill))))
+            parts.append((decode, self._execute_decode_graph(decode)))
+        else:
+            order = prefill + decode
+            parts.append((order, self._execute(order, len(prefill))))
+        for seq, start, n, samples in plan:
+            seq.num_computed = start + n
+            self.stats["prompt_tokens_computed"] += n
+            if samples:
+                seq.pending += 1
+        return {"parts": parts}
+
+    def _flush(self) -> None:
+        """Complete the step in flight (callers hold the step lock)."""
+        if self._inflight is not None:
+            cur, self._inflight = self._inflight, None
+            self._complete(cur)
+
+    def _h2d(self, host: np.ndarray) -> torch.Tensor:
+        """Copy an int64 host array to a fresh device tensor without blocking the host: it is staged in
+        a pinned buffer from a ring whose entries are reused only after their previous copy has run."""
+        n = host.size
+        if self.device.type != "cuda":
+            return torch.from_numpy(np.array(host, dtype=np.int64, copy=True))
+        if not self._in_ring:
+            self._in_ring = [[None, None] for _ in range(8)]
+        entry = self._in_ring[self._in_next]
+        self._in_next = (self._in_next + 1) % len(self._in_ring)
+        if entry[1] is not None:
+            entry[1].synchronize()
+        if entry[0] is None or entry[0].numel() < n:
+            entry[0] = torch.empty(max(n, 1 << 16), dtype=torch.int64).pin_memory()
+        entry[0].numpy()[:n] = host
+        out = torch.empty(n, dtype=torch.int64, device=self.device)
+        out.copy_(entry[0][:n], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        entry[1] = ev
+        return out
+
+    def _result_buffer(self) -> torch.Tensor:
+        """Pinned [2, rows] float64 buffer for one step part's tokens and log-probs (a small ring: at
+        most two steps, of at most two parts each, are alive)."""
+        if not self._pin_ring:
+            pin = self.device.type == "cuda"
+            self._pin_ring = [torch.empty(2, self._res_rows, dtype=torch.float64, pin_memory=pin) for _ in range(6)]
+        buf = self._pin_ring[self._pin_next]
+        self._pin_next = (self._pin_next + 1) % len(self._pin_ring)
+        return buf
+
+    def _stage_results(self, tokens: torch.Tensor, lps: torch.Tensor):
+        """Start the device->host copy of a step part's samples; returns (buffer, n, event)."""
+        n = tokens.shape[0]
+        buf = self._result_buffer()
+        if n > buf.shape[1]:
+            buf = torch.empty(2, n, dtype=torch.float64, pin_memory=self.device.type == "cuda")
+        res = torch.stack([tokens.double(), lps.double()])
+        ev = None
+        if self.device.type == "cuda":
+            buf[:, :n].copy_(res, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+        else:
+            buf[:, :n].copy_(res)
+        return buf, n, ev
 
     # ------------------------------------------------------------------ model forward
     def _all_reduce(self, y: torch.Tensor) -> torch.Tensor:
@@ -583,9 +680,14 @@ class GenerationEngine:
     # ------------------------------------------------------------------ CUDA-graph decode
     _BUCKETS = (8, 16, 32, 64, 128, 256, 512)
 
-    def _decode_core(self, ids_d, pos_d, slots_d, table_d, lens_d, temps_d, seeds_d, offs_d, splits: int):
-        """Forward of single-token rows (every row samples): returns (tokens, logprobs) on device."""
+    def _decode_core(self, ids_d, pos_d, slots_d, table_d, lens_d, temps_d, seeds_d, offs_d, splits: int,
+                     rowslot_d=None):
+        """Forward of single-token rows (every row samples): returns (tokens, logprobs) on device.
+        Rows whose id is negative read their input token from the slot table (``rowslot_d``), and the
+        sampled tokens are written back into it."""
         cfg, m = self.cfg, self.model
+        if rowslot_d is not None:
+            ids_d = torch.where(ids_d >= 0, ids_d, self._slot_tok.index_select(0, rowslot_d))
         scale = 1.0 / math.sqrt(cfg.head_dim)
         Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
 
@@ -596,7 +698,10 @@ class GenerationEngine:
         x = self._forward_layers(x, pos_d, slots_d, attn_fn)
         hN, _ = ops.rmsnorm(x, m.w("model.norm.weight"), cfg.rms_norm_eps)
         logits = ops.linear(hN, m.w(m.lm_head_name))
-        return ops.sample(logits, temps_d, seeds_d, offs_d)
+        tok, lp = ops.sample(logits, temps_d, seeds_d, offs_d)
+        if rowslot_d is not None:
+            self._slot_tok.index_copy_(0, rowslot_d, tok)
+        return tok, lp
 
     def _graph_for(self, bucket: int, width: int):
         key = (bucket, width)
@@ -604,7 +709,7 @@ class GenerationEngine:
         if g is not None:
             return g
         dev = self.device
-        meta = torch.zeros(bucket * (5 + width), dtype=torch.int64, device=dev)
+        meta = torch.zeros(bucket * (6 + width), dtype=torch.int64, device=dev)
         temps = torch.zeros(bucket, dtype=torch.float32, device=dev)
 
         def views():
@@ -613,19 +718,21 @@ class GenerationEngine:
             slots = meta[2 * bucket : 3 * bucket].to(torch.int32)
             lens = meta[3 * bucket : 4 * bucket].to(torch.int32)
             seeds = meta[4 * bucket : 5 * bucket]
-            table = meta[5 * bucket :].view(bucket, width).to(torch.int32)
-            return ids, pos, slots, table, lens, seeds
+            rowslot = meta[5 * bucket : 6 * bucket]
+            table = meta[6 * bucket :].view(bucket, width).to(torch.int32)
+            return ids, pos, slots, table, lens, seeds, rowslot
 
         # a valid dummy batch: every row reads one token of the scratch block and writes nothing
         meta[2 * bucket : 3 * bucket] = -1
         meta[3 * bucket : 4 * bucket] = 1
-        meta[5 * bucket :] = self.scratch_block
+        meta[5 * bucket : 6 * bucket] = self._dummy_slot
+        meta[6 * bucket :] = self.scratch_block
         splits = self.decode_splits or _decode_splits(bucket * self.cfg.num_key_value_heads)
         offs = torch.zeros(bucket, dtype=torch.int64, device=dev)
 
         def run():
-            ids, pos, slots, table, lens, seeds = views()
-            return self._decode_core(ids, pos, slots, table, lens, temps, seeds, offs, splits)
+            ids, pos, slots, table, lens, seeds, rowslot = views()
+            return self._decode_core(ids, pos, slots, table, lens, temps, seeds, offs, splits, rowslot)
 
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
@@ -651,36 +758,50 @@ class GenerationEngine:
             return None
         width = max(len(s.blocks) for s, *_ in order)
         width = (width + 63) // 64 * 64
-        host = np.zeros(bucket * (5 + width), dtype=np.int64)
-        host[2 * bucket : 3 * bucket] = -1
-        host[3 * bucket : 4 * bucket] = 1
-        table = host[5 * bucket :].reshape(bucket, width)
+        host = np.empty(bucket * (6 + width), dtype=np.int64)
+        n = B
+        starts = np.fromiter((st for _, st, _, _ in order), dtype=np.int64, count=n)
+        # input token: known on the host, or -1 = the sequence's pending token in the slot table
+        host[:n] = np.fromiter((s.toks[st] if st < len(s.toks) else -1 for s, st, _, _ in order), dtype=np.int64,
+                               count=n)
+        host[n:bucket] = 0
+        host[bucket : bucket + n] = starts
+        host[bucket + n : 2 * bucket] = 0
+        last_blk = np.fromiter((s.blocks[st // bs] for s, st, _, _ in order), dtype=np.int64, count=n)
+        host[2 * bucket : 2 * bucket + n] = last_blk * bs + starts % bs
+        host[2 * bucket + n : 3 * bucket] = -1
+        host[3 * bucket : 3 * bucket + n] = starts + 1
+        host[3 * bucket + n : 4 * bucket] = 1
+        host[4 * bucket : 4 * bucket + n] = np.fromiter((s.seed for s, *_ in order), dtype=np.int64, count=n)
+        host[4 * bucket + n : 5 * bucket] = 0
+        host[5 * bucket : 5 * bucket + n] = np.fromiter((s.slot for s, *_ in order), dtype=np.int64, count=n)
+        host[5 * bucket + n : 6 * bucket] = self._dummy_slot
+        table = host[6 * bucket :].reshape(bucket, width)
         table[:] = self.scratch_block
-        temps = np.zeros(bucket, dtype=np.float32)
-        offs = np.zeros(bucket, dtype=np.int64)
-        for j, (seq, start, n, _) in enumerate(order):
+        for j, (seq, _, _, _) in enumerate(order):
             blk = seq.blocks
-            host[j] = seq.tokens[start]
-            host[bucket + j] = start
-            host[2 * bucket + j] = blk[start // bs] * bs + start % bs
-            host[3 * bucket + j] = start + 1
-            host[4 * bucket + j] = seq.seed
             table[j, : len(blk)] = blk
-            temps[j] = float(seq.params.temperature)
-            offs[j] = len(seq.out)
+        temps = np.zeros(bucket, dtype=np.float32)
+        temps[:n] = np.fromiter((float(s.params.temperature) for s, *_ in order), dtype=np.float32, count=n)
+        offs = np.zeros(bucket, dtype=np.int64)
+        offs[:n] = np.fromiter((len(s.out) + s.pending for s, *_ in order), dtype=np.int64, count=n)
         return {"kind": "graph", "B": B, "bucket": bucket, "width": width, "host": host, "temps": temps, "offs": offs}
 
     def _run_graph(self, meta):
         g = self._graph_for(meta["bucket"], meta["width"])
-        g["meta"].copy_(torch.from_numpy(meta["host"]), non_blocking=False)
-        g["temps"].copy_(torch.from_numpy(meta["temps"]))
-        g["offs"].copy_(torch.from_numpy(meta["offs"]))
+        n_meta = g["meta"].numel()
+        bk = meta["bucket"]
+        host = np.empty(n_meta + 2 * bk, dtype=np.int64)
+        host[:n_meta] = meta["host"]
+        host[n_meta : n_meta + bk] = meta["offs"]
+        host[n_meta + bk :].view(np.float32)[:bk] = meta["temps"]
+        d = self._h2d(host)
+        g["meta"].copy_(d[:n_meta])
+        g["offs"].copy_(d[n_meta : n_meta + bk])
+        g["temps"].copy_(d[n_meta + bk :].view(torch.float32)[:bk])
         g["graph"].replay()
         B = meta["B"]
-        res = torch.stack([g["tok"][:B].double(), g["lp"][:B].double()]).cpu()
-        if self._tp_ar is not None:
-            self._tp_ar.check()
-        return res[0].long().tolist(), res[1].tolist()
+        return self._stage_results(g["tok"][:B], g["lp"][:B])
 
     def _execute_decode_graph(self, order):
         meta = self._graph_meta(order)
@@ -698,10 +819,15 @@ class GenerationEngine:
         cu_k = [0]
         max_q = 1
         rows = 0
+        rs_l = []
         for i, (seq, start, n, samples) in enumerate(order):
             blocks = np.asarray(seq.blocks, dtype=np.int64)
             p = np.arange(start, start + n, dtype=np.int64)
-            ids_l.append(np.asarray(seq.toks[start : start + n], dtype=np.int64))
+            known = seq.toks[start : start + n]
+            if len(known) < n:  # the pending token (decode rows only): read from the slot table
+                known = known + [-1] * (n - len(known))
+            ids_l.append(np.asarray(known, dtype=np.int64))
+            rs_l.append(np.full(n, seq.slot if seq.slot >= 0 else self._dummy_slot, dtype=np.int64))
             pos_l.append(p)
             slots_l.append(blocks[p // bs] * bs + p % bs)
             rows += n
@@ -719,11 +845,12 @@ class GenerationEngine:
         pos = np.concatenate(pos_l) if pos_l else empty
         slots = np.concatenate(slots_l) if slots_l else empty
         k_slots = np.concatenate(ks_l) if ks_l else empty
+        row_slots = np.concatenate(rs_l) if rs_l else empty
         decode = order[n_prefill:]
         nd = len(decode)
-        header = [len(ids), len(pos), len(slots), len(sample_rows), len(cu_q), len(cu_k), len(k_slots)]
+        header = [len(ids), len(pos), len(slots), len(sample_rows), len(cu_q), len(cu_k), len(k_slots), len(row_slots)]
         flat = np.concatenate([ids, pos, slots, np.asarray(sample_rows, np.int64), np.asarray(cu_q, np.int64),
-                               np.asarray(cu_k, np.int64), k_slots])
+                               np.asarray(cu_k, np.int64), k_slots, row_slots])
         meta: Dict[str, Any] = {"kind": "exec", "header": header, "flat": flat, "Tp": cu_q[-1], "max_q": max_q,
                                 "nd": nd}
         if nd:
@@ -737,7 +864,7 @@ class GenerationEngine:
         sampled = [e for e in order if e[3]]
         meta["temps"] = np.asarray([float(sq.params.temperature) for sq, *_ in sampled], np.float32)
         meta["seeds"] = np.asarray([sq.seed for sq, *_ in sampled], np.int64)
-        meta["offs"] = np.asarray([len(sq.out) for sq, *_ in sampled], np.int64)
+        meta["offs"] = np.asarray([len(sq.out) + sq.pending for sq, *_ in sampled], np.int64)
         if any(sq.params.top_p < 1.0 or (sq.params.top_k or -1) > 0 for sq, *_ in sampled):
             meta["filter_params"] = [sq.params for sq, *_ in sampled]
         return meta
@@ -751,10 +878,19 @@ class GenerationEngine:
         cfg = self.cfg
         dev = self.device
         header, Tp, max_q, nd = meta["header"], meta["Tp"], meta["max_q"], meta["nd"]
-        host = torch.from_numpy(meta["flat"])
-        if dev.type == "cuda":
-            host = host.pin_memory()
-        d = host.to(dev, non_blocking=True)
+        ns = len(meta["seeds"])
+        parts = [meta["flat"]]
+        if nd:
+            parts += [meta["table"].reshape(-1).astype(np.int64), meta["lens"].astype(np.int64)]
+        tail = np.empty(3 * ns, dtype=np.int64)
+        tail[:ns] = meta["seeds"]
+        tail[ns : 2 * ns] = meta["offs"]
+        tail[2 * ns :].view(np.float32)[:ns] = meta["temps"]
+        parts.append(tail)
+        big = self._h2d(np.concatenate(parts))
+        nflat = meta["flat"].size
+        d = big[:nflat]
+        rest = big[nflat:]
         off = np.cumsum([0] + header)
         ids_d = d[off[0] : off[1]]
         pos_d = d[off[1] : off[2]]
@@ -763,15 +899,16 @@ class GenerationEngine:
         cu_q_d = d[off[4] : off[5]].to(torch.int32)
         cu_k_d = d[off[5] : off[6]].to(torch.int32)
         kslots_d = d[off[6] : off[7]]
+        rowslot_d = d[off[7] : off[8]]
+        ids_d = torch.where(ids_d >= 0, ids_d, self._slot_tok.index_select(0, rowslot_d))
         if nd:
-            table, lens = meta["table"], meta["lens"]
-            max_blocks = table.shape[1]
-            dt = torch.from_numpy(np.concatenate([table.reshape(-1), lens]))
-            if dev.type == "cuda":
-                dt = dt.pin_memory()
-            dt = dt.to(dev, non_blocking=True)
-            table_d = dt[: nd * max_blocks].view(nd, max_blocks)
-            lens_d = dt[nd * max_blocks :]
+            max_blocks = meta["table"].shape[1]
+            table_d = rest[: nd * max_blocks].view(nd, max_blocks).to(torch.int32)
+            lens_d = rest[nd * max_blocks : nd * max_blocks + nd].to(torch.int32)
+            rest = rest[nd * max_blocks + nd :]
+        seeds_d = rest[:ns]
+        offs_d = rest[ns : 2 * ns]
+        temps_d = rest[2 * ns :].view(torch.float32)[:ns]
         m = self.model
         D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         scale = 1.0 / math.sqrt(D)
@@ -793,20 +930,17 @@ class GenerationEngine:
             x = ops.embedding(ids_d, m.w("model.embed_tokens.weight"))
             x = self._forward_layers(x, pos_d, slots_d, attn_fn)
             if header[3] == 0:
-                return [], []
+                return self._stage_results(torch.zeros(0, dtype=torch.long, device=dev),
+                                           torch.zeros(0, dtype=torch.float32, device=dev))
             xs = x.index_select(0, rows_d)
             hN, _ = ops.rmsnorm(xs, m.w("model.norm.weight"), cfg.rms_norm_eps)
             logits = ops.linear(hN, m.w(m.lm_head_name))
-            seeds = torch.from_numpy(meta["seeds"])
             if "filter_params" in meta:
-                tokens, lps = _sample_filtered(logits, meta["filter_params"], seeds)
+                tokens, lps = _sample_filtered(logits, meta["filter_params"], torch.from_numpy(meta["seeds"]))
             else:
-                tokens, lps = ops.sample(logits, torch.from_numpy(meta["temps"]).to(dev), seeds.to(dev),
-                                         torch.from_numpy(meta["offs"]).to(dev))
-            res = torch.stack([tokens.double(), lps.double()]).cpu()  # the one device->host read per step
-        if self._tp_ar is not None:
-            self._tp_ar.check()
-        return res[0].long().tolist(), res[1].tolist()
+                tokens, lps = ops.sample(logits, temps_d, seeds_d, offs_d)
+            self._slot_tok.index_copy_(0, rowslot_d.index_select(0, rows_d), tokens.to(torch.long))
+            return self._stage_results(tokens, lps)  # the one device->host copy of the step
 
     # ------------------------------------------------------------------ tensor-parallel followers
     def _send_step(self, meta) -> None:
@@ -835,9 +969,13 @@ class GenerationEngine:
                 return
             if kind == "step":
                 if payload["kind"] == "graph":
-                    self._run_graph(payload)
+                    _, _, ev = self._run_graph(payload)
                 else:
-                    self._run_exec(payload)
+                    _, _, ev = self._run_exec(payload)
+                if ev is not None:
+                    ev.synchronize()  # the result buffers are reused a few steps later
+                if self._tp_ar is not None:
+                    self._tp_ar.check()
             elif kind == "pull":
                 self._pull_local(payload)
                 dist.barrier(group=self.cmd_group)
@@ -850,35 +988,41 @@ class GenerationEngine:
                 self._followers_stopped = True
                 self._cmd(("stop", None))
 
-    def _postprocess(self, order, tokens: List[int], logps: List[float]) -> None:
+    def _complete(self, launched) -> None:
+        """Apply the samples of a launched step: append tokens, register full prefix blocks, finish
+        sequences that stop (rows of already-finished sequences are discarded)."""
         bs = self.block_size
-        it = iter(zip(tokens, logps))
-        with self._lock:
-            for seq, start, n, samples in order:
-                if seq.finish_reason is not None:
+        for order, (buf, n, ev) in launched["parts"]:
+            if ev is not None:
+                ev.synchronize()
+            vals = buf[:, :n].tolist()
+            it = iter(zip(vals[0], vals[1]))
+            with self._lock:
+                for seq, start, nn, samples in order:
                     if samples:
-                        next(it)
-                    continue
-                seq.num_computed = start + n
-                self.stats["prompt_tokens_computed"] += n
-                # register newly completed full blocks for prefix reuse
-                toks = seq.tokens
-                while len(seq.hashes) < seq.num_computed // bs:
-                    i = len(seq.hashes)
-                    parent = seq.hashes[-1] if seq.hashes else None
-                    h = block_hash(parent, toks[i * bs : (i + 1) * bs])
-                    seq.hashes.append(h)
-                    self.allocator.register(seq.blocks[i], h)
-                if not samples:
-                    continue
-                tok, lp = next(it)
-                seq.append(int(tok), float(lp))
-                self.stats["generated_tokens"] += 1
-                reason = self._stop_reason(seq, int(tok))
-                if reason is not None:
-                    self._finish(seq, reason)
-                elif seq.params.output_kind != "final_only":
-                    self._deliver(seq, False)
+                        tok, lp = next(it)
+                    if seq.finish_reason is not None:
+                        continue
+                    # register newly completed full blocks (known tokens only) for prefix reuse
+                    toks = seq.toks
+                    while len(seq.hashes) < min(seq.num_computed, len(toks)) // bs and len(seq.hashes) < len(seq.blocks):
+                        i = len(seq.hashes)
+                        parent = seq.hashes[-1] if seq.hashes else None
+                        h = block_hash(parent, toks[i * bs : (i + 1) * bs])
+                        seq.hashes.append(h)
+                        self.allocator.register(seq.blocks[i], h)
+                    if not samples:
+                        continue
+                    seq.pending -= 1
+                    seq.append(int(tok), float(lp))
+                    self.stats["generated_tokens"] += 1
+                    reason = self._stop_reason(seq, int(tok))
+                    if reason is not None:
+                        self._finish(seq, reason)
+                    elif seq.params.output_kind != "final_only":
+                        self._deliver(seq, False)
+        if self._tp_ar is not None:
+            self._tp_ar.check()
 
     def _stop_reason(self, seq: _Seq, tok: int) -> Optional[str]:
         p = seq.params

@@ -103,7 +103,8 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
 }
 
 // Fused backward: dx as above plus the weight-gradient partial of the rows this warp visits, kept in
-// registers (NC = H / 256 chunks of 8 columns per lane) and written once per warp.
+// registers (NC = H / 256 chunks of 8 columns per lane); the block's warps sum theirs in shared
+// memory and each block writes one partial row.
 template <int NC>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const __nv_bfloat16* __restrict__ dy,
                                                                 const __nv_bfloat16* __restrict__ x,
@@ -171,11 +172,23 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const __nv_bfloa
       *reinterpret_cast<uint4*>(dx + row * ld + c * 256 + lane * 8) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
-  float* dst = part + static_cast<long long>(gw) * H;
+  // the block's 8 warps add their partials in fixed warp order (deterministic), one row per block
+  __shared__ float red[H];
+  const int warp = threadIdx.x >> 5;
+  for (int wv = 0; wv < 8; ++wv) {
+    if (warp == wv) {
 #pragma unroll
-  for (int c = 0; c < NC; ++c)
+      for (int c = 0; c < NC; ++c)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dst[c * 256 + lane * 8 + i] = acc[c][i];
+        for (int i = 0; i < 8; ++i) {
+          float* slot = red + c * 256 + lane * 8 + i;
+          *slot = (wv == 0 ? 0.f : *slot) + acc[c][i];
+        }
+    }
+    __syncthreads();
+  }
+  float* dst = part + static_cast<long long>(blockIdx.x) * H;
+  for (int h = threadIdx.x; h < H; h += blockDim.x) dst[h] = red[h];
 }
 
 // Partial column sums for the RMSNorm weight gradient: part[b, h] = sum over this block's rows of
@@ -207,14 +220,24 @@ __global__ void rmsnorm_dw_partial_kernel(const __nv_bfloat16* __restrict__ dy, 
   for (int i = 0; i < 8; ++i) dst[i] = acc[i];
 }
 
-// out[h] (+)= sum_b part[b, h]   (fixed order -> deterministic)
+// out[h] (+)= sum_b part[b, h]: block (32 columns x 8 row groups); row group g sums rows g, g+8, ...
+// and the 8 group sums are added in fixed order (deterministic).
 __global__ void column_reduce_kernel(const float* __restrict__ part, float* __restrict__ out, int nblk, int H,
                                      int accumulate) {
-  const int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h >= H) return;
+  const int tx = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int h = blockIdx.x * 32 + tx;
+  __shared__ float red[8][33];
   float s = 0.f;
-  for (int b = 0; b < nblk; ++b) s += part[static_cast<long long>(b) * H + h];
-  out[h] = accumulate ? out[h] + s : s;
+  if (h < H)
+    for (int b = g; b < nblk; b += 8) s += part[static_cast<long long>(b) * H + h];
+  red[g][tx] = s;
+  __syncthreads();
+  if (g == 0 && h < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i][tx];
+    out[h] = accumulate ? out[h] + t : t;
+  }
 }
 
 // Bias gradient partials: part[b, n] = sum of dy[r, n] over this block's rows.
@@ -382,7 +405,6 @@ extern "C" int accerl_rmsnorm_bwd(const void* dy, const void* x, const void* w, 
     // fused single pass: 8 warps per block, grid sized so every warp visits several rows
     const int nwarps_total = std::min((rows + 3) / 4, 148 * 16);
     const int blocks = (nwarps_total + 7) / 8;
-    const int nw = blocks * 8;
 #define RMS_BWD_CASE(NCV)                                                                                        \
   case NCV:                                                                                                      \
     rmsnorm_bwd_fused_kernel<NCV><<<blocks, 256, 0, s>>>(                                                        \
@@ -395,7 +417,7 @@ extern "C" int accerl_rmsnorm_bwd(const void* dy, const void* x, const void* w, 
         goto generic;
     }
 #undef RMS_BWD_CASE
-    column_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(workspace, dw, nw, H, dw_accumulate);
+    column_reduce_kernel<<<(H + 31) / 32, 256, 0, s>>>(workspace, dw, blocks, H, dw_accumulate);
     return (int)cudaGetLastError();
   }
 generic:
@@ -409,7 +431,7 @@ generic:
     dim3 grid(nblk, (H / 8 + 127) / 128);
     rmsnorm_dw_partial_kernel<<<grid, 128, 0, s>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, rstd, workspace,
                                                    rows, H, ld, rpb);
-    column_reduce_kernel<<<(H + 255) / 256, 256, 0, s>>>(workspace, dw, nblk, H, dw_accumulate);
+    column_reduce_kernel<<<(H + 31) / 32, 256, 0, s>>>(workspace, dw, nblk, H, dw_accumulate);
   }
   return (int)cudaGetLastError();
 }
@@ -421,7 +443,7 @@ extern "C" int accerl_bias_grad(const void* dy, float* db, float* workspace, int
   const int nblk = (rows + rpb - 1) / rpb;
   dim3 grid(nblk, (N / 8 + 127) / 128);
   colsum_partial_kernel<<<grid, 128, 0, s>>>((const __nv_bfloat16*)dy, workspace, rows, N, ld, rpb);
-  column_reduce_kernel<<<(N + 255) / 256, 256, 0, s>>>(workspace, db, nblk, N, accumulate);
+  column_reduce_kernel<<<(N + 31) / 32, 256, 0, s>>>(workspace, db, nblk, N, accumulate);
   return (int)cudaGetLastError();
 }
 
