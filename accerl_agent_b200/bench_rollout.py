@@ -37,6 +37,7 @@ async def _drive(service, args, groups: int, seconds: float, profile: float = 0.
             await asyncio.sleep(profile)
         steps = service.engine.stats["steps"]
         print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=25, max_name_column_width=60))
+        print(prof.key_averages().table(sort_by="self_cpu_time_total", row_limit=25, max_name_column_width=60))
         print(f"[profile] engine steps so far: {steps}")
     tok0 = service.total_tokens
     t0 = time.perf_counter()

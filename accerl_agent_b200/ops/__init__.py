@@ -90,9 +90,12 @@ def workspace(device: torch.device, name: str, numel: int, dtype=torch.float32) 
     key = (device.index if device.index is not None else -1, name)
     buf = _WORKSPACE.get(key)
     if buf is None or buf.numel() < numel or buf.dtype != dtype:
+        size = numel
         if buf is not None:
             _RETIRED.append(buf)
-        buf = torch.empty(max(numel, 1), dtype=dtype, device=device)
+            if buf.dtype == dtype:
+                size = max(numel, int(buf.numel() * 1.5))  # grow geometrically: few reallocations
+        buf = torch.empty(max(size, 1), dtype=dtype, device=device)
         _WORKSPACE[key] = buf
     return buf[:numel]
 

@@ -586,30 +586,32 @@ class GenerationEngine:
         return out
 
     def _result_buffer(self) -> torch.Tensor:
-        """Pinned [2, rows] float64 buffer for one step part's tokens and log-probs (a small ring: at
-        most two steps, of at most two parts each, are alive)."""
+        """Flat pinned float64 buffer for one step part's tokens and log-probs (a small ring: at most
+        two steps, of at most two parts each, are alive)."""
         if not self._pin_ring:
             pin = self.device.type == "cuda"
-            self._pin_ring = [torch.empty(2, self._res_rows, dtype=torch.float64, pin_memory=pin) for _ in range(6)]
+            self._pin_ring = [torch.empty(2 * self._res_rows, dtype=torch.float64, pin_memory=pin) for _ in range(6)]
         buf = self._pin_ring[self._pin_next]
         self._pin_next = (self._pin_next + 1) % len(self._pin_ring)
         return buf
 
     def _stage_results(self, tokens: torch.Tensor, lps: torch.Tensor):
-        """Start the device->host copy of a step part's samples; returns (buffer, n, event)."""
+        """Start the device->host copy of a step part's samples; returns (view [2, n], n, event). The
+        destination is a contiguous prefix of a pinned buffer, so the copy never blocks the host."""
         n = tokens.shape[0]
         buf = self._result_buffer()
-        if n > buf.shape[1]:
-            buf = torch.empty(2, n, dtype=torch.float64, pin_memory=self.device.type == "cuda")
+        if 2 * n > buf.numel():
+            buf = torch.empty(2 * n, dtype=torch.float64, pin_memory=self.device.type == "cuda")
+        dst = buf[: 2 * n].view(2, n)
         res = torch.stack([tokens.double(), lps.double()])
         ev = None
         if self.device.type == "cuda":
-            buf[:, :n].copy_(res, non_blocking=True)
+            dst.copy_(res, non_blocking=True)
             ev = torch.cuda.Event()
             ev.record()
         else:
-            buf[:, :n].copy_(res)
-        return buf, n, ev
+            dst.copy_(res)
+        return dst, n, ev
 
     # ------------------------------------------------------------------ model forward
     def _all_reduce(self, y: torch.Tensor) -> torch.Tensor:
@@ -995,7 +997,7 @@ class GenerationEngine:
         for order, (buf, n, ev) in launched["parts"]:
             if ev is not None:
                 ev.synchronize()
-            vals = buf[:, :n].tolist()
+            vals = buf.tolist()
             it = iter(zip(vals[0], vals[1]))
             with self._lock:
                 for seq, start, nn, samples in order:
