@@ -56,6 +56,18 @@ def device_plan(args):
     return list(range(world)), [[world + i * tp + j for j in range(tp)] for i in range(n_engines)]
 
 
+def exchange_weight_handles(trainers, engines, followers, timeout: float = 600.0) -> None:
+    """Hand every engine rank (leader and tensor-parallel followers) the weight-buffer handle of
+    trainer ``i % world``, once at start-up; later syncs pull through the mapped buffers. A trainer
+    or engine process that died before or during the exchange raises ``ActorDied`` here (the
+    reference builds its NCCL weight-transfer group at this point, ``agent_textworld.py:3035-3057``)."""
+    for i, e in enumerate(engines):
+        handle = get(trainers[i % len(trainers)].export_weights_handle.remote(), timeout=timeout)
+        e.attach_trainer_weights(handle)
+        for f in followers[i] if followers else ():
+            f.attach_trainer_weights(handle)
+
+
 def sync_weights(engines, trainers, scope: str) -> Dict[str, float]:
     numel = get(trainers[0].weight_numel.remote(scope))
     for t in trainers:
@@ -105,11 +117,7 @@ def run_train(args) -> Dict[str, float]:
                       for j in range(1, args.infer_tp_size)] for i in range(len(engine_devs))]
         for e in engines + [f for fs in followers for f in fs]:
             e.wait_ready(1800)
-        for i, e in enumerate(engines):
-            handle = get(trainers[i % world].export_weights_handle.remote())
-            e.attach_trainer_weights(handle)
-            for f in followers[i]:
-                f.attach_trainer_weights(handle)
+        exchange_weight_handles(trainers, engines, followers)
         print("[sync] Initial full sync from trainers to engines...")
         get([e.pause_and_wait_idle.remote() for e in engines])
         sync_weights(engines, trainers, "all")

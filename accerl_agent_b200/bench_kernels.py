@@ -16,16 +16,13 @@ import math
 import torch
 
 from . import ops
+from .utils.roofline import load_peaks
 from .utils.timing import median_ms
 
 
 def _peaks():
-    try:
-        with open("MEASURED_PEAKS.json") as f:
-            p = json.load(f)
-        return float(p["bf16_tflops"]), float(p["hbm_gbs"])
-    except Exception:
-        return 1590.0, 6650.0
+    p = load_peaks()
+    return p.bf16_tflops, p.hbm_gbs
 
 
 def bench_gemm(results):

@@ -68,6 +68,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--checkpoint-dir", default=None)
     a("--checkpoint-name", default="latest")
     a("--checkpoint-every-sync-rounds", type=int, default=0)
+    a("--save-optimizer-state", action="store_true",
+      help="Also save each rank's optimizer shard (fp32 master, Adam moments) and step counters.")
+    a("--resume-from", default=None, help="Checkpoint directory to resume the trainer from.")
     a("--seed", type=int, default=42)
     a("--trust-remote-code", action="store_true")
     a("--gradient-checkpointing", action="store_true")

@@ -35,6 +35,7 @@ import numpy as np
 import torch
 
 from .. import ops
+from ..utils import nvtx
 from ..models.config import ModelConfig
 from ..models.transformer import CausalLM, ParamLayout
 from .generation import SamplingParams
@@ -364,7 +365,7 @@ class GenerationEngine:
     def pull_weights(self, scope: str = "all") -> int:
         """Copy this engine's slice of the registered trainer buffer into its weights (every TP rank
         pulls its own shard). Returns the bytes this rank copied."""
-        with self._step_lock:
+        with self._step_lock, nvtx.range("engine/pull_weights"):
             self._flush()
             if self.tp > 1 and self.tp_rank == 0:
                 import torch.distributed as dist
@@ -514,16 +515,19 @@ class GenerationEngine:
     def step(self) -> bool:
         with self._step_lock:
             t0 = time.perf_counter()
-            plan = self._schedule()
+            with nvtx.range("engine/schedule"):
+                plan = self._schedule()
             t1 = time.perf_counter()
-            launched = self._launch(plan) if plan else None
+            with nvtx.range("engine/launch"):
+                launched = self._launch(plan) if plan else None
             t2 = time.perf_counter()
             prev, self._inflight = self._inflight, launched
-            if prev is not None:
-                self._complete(prev)
-            if not self.async_steps and self._inflight is not None:
-                cur, self._inflight = self._inflight, None
-                self._complete(cur)
+            with nvtx.range("engine/complete"):
+                if prev is not None:
+                    self._complete(prev)
+                if not self.async_steps and self._inflight is not None:
+                    cur, self._inflight = self._inflight, None
+                    self._complete(cur)
             t3 = time.perf_counter()
             if plan is None and prev is None:
                 return False

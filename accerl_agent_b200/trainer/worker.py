@@ -30,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from ..utils import nvtx
 from ..algo.objectives import ObjectiveConfig, normalize_advantages, padded_loss
 from ..algo.packing import (
     make_padded_collate,
@@ -190,6 +191,8 @@ class TrainWorker:
         self.stager = PinnedStager(self.device)
         self.last_h2d_bytes = 0
         self.last_pack_stats: Dict[str, float] = {}
+        if getattr(args, "resume_from", None):
+            self.load_checkpoint(args.resume_from)
         if rank == 0:
             total = sum(s.numel for s in self.model.layout.slots.values())
             trainable = sum(s.numel for s in self.model.layout.slots.values() if s.trainable)
@@ -393,7 +396,8 @@ class TrainWorker:
         return stats
 
     def _run_varlen_optimizer_step(self, trainer_version: float) -> Dict[str, float]:
-        window = self._prepare_varlen_optimizer_window(trainer_version)
+        with nvtx.range("train/prepare_window"):
+            window = self._prepare_varlen_optimizer_window(trainer_version)
         local_tokens = sum(p.valid_token_count for p in window)
         tok = torch.tensor([local_tokens], dtype=torch.int64, device=self._comm_device())
         global_tokens = int(self._all_reduce(tok).item())
@@ -403,11 +407,15 @@ class TrainWorker:
         h2d = 0
         scale = 1.0 / float(global_tokens)
         for pack in window:
-            dp = self.pack_to_device(pack)
+            with nvtx.range("train/h2d"):
+                dp = self.pack_to_device(pack)
             h2d += dp.h2d_bytes
-            lp, ctx = self.model.forward_logprobs(dp.batch, dp.max_seqlen)
-            dlp, st = ops.policy_loss(lp, dp.old_lp, dp.adv, self.obj_cfg, loss_scale=scale)
-            self.model.backward_from_logprobs(dlp, ctx)
+            with nvtx.range("train/forward"):
+                lp, ctx = self.model.forward_logprobs(dp.batch, dp.max_seqlen)
+            with nvtx.range("train/loss"):
+                dlp, st = ops.policy_loss(lp, dp.old_lp, dp.adv, self.obj_cfg, loss_scale=scale)
+            with nvtx.range("train/backward"):
+                self.model.backward_from_logprobs(dlp, ctx)
             stats += st.to(stats.device)
             self.train_micro_step += 1
             del ctx, lp, dlp, dp
@@ -415,12 +423,14 @@ class TrainWorker:
         version = torch.tensor([sum(p.version_lag_sum for p in window), sum(p.sample_count for p in window)],
                                dtype=torch.float64, device=self._comm_device())
         if self.fsdp_world_size > 1:
-            st_comm = stats.to(self._comm_device())
-            self._all_reduce(st_comm)
-            stats = st_comm
-            self._all_reduce(version)
+            with nvtx.range("train/stats_allreduce"):
+                st_comm = stats.to(self._comm_device())
+                self._all_reduce(st_comm)
+                stats = st_comm
+                self._all_reduce(version)
         lr = self.current_lr()
-        self.optimizer.step(lr)
+        with nvtx.range("train/optimizer"):
+            self.optimizer.step(lr)
         self.optimizer_step += 1
         policy_sum, kl_sum, clip_count = stats.tolist()
         lag_sum, sample_count = version.tolist()
@@ -603,7 +613,12 @@ class TrainWorker:
             return self.model.params
         raise ValueError(f"Unsupported weight scope: {scope!r}")
 
-    def save_checkpoint(self, checkpoint_dir: str, tag: str, save_optimizer: bool = False) -> Dict[str, Any]:
+    def save_checkpoint(self, checkpoint_dir: str, tag: str, save_optimizer: Optional[bool] = None) -> Dict[str, Any]:
+        """HF-format weights (as ``agent_textworld.py:1502`` of the reference saves them) plus, with
+        ``save_optimizer`` (default ``--save-optimizer-state``), this rank's fp32 master / Adam moment
+        shards and the step counters, so ``--resume-from`` continues the same optimisation."""
+        if save_optimizer is None:
+            save_optimizer = bool(getattr(self.args, "save_optimizer_state", False))
         if not checkpoint_dir:
             raise ValueError("checkpoint_dir must be non-empty")
         if not tag:

@@ -60,3 +60,58 @@ def test_actor_errors_and_death_are_reported():
     with pytest.raises(ActorDied):
         h.ping()
     h.stop_process()
+
+
+class FakeTrainer:
+    def __init__(self, rank, die=False):
+        self.rank, self.die = rank, die
+
+    def export_weights_handle(self):
+        if self.die:
+            os._exit(5)
+        return {"kind": "test", "rank": self.rank}
+
+
+class FakeEngine:
+    def __init__(self):
+        self.handle = None
+
+    def attach_trainer_weights(self, handle):
+        self.handle = handle
+
+    def attached(self):
+        return self.handle
+
+    def die(self):
+        os._exit(4)
+
+
+def test_weight_handle_exchange_and_peer_drop():
+    """Every engine rank gets trainer ``i % world``'s handle; a trainer that dies during the
+    exchange, or an engine that died before it, fails the exchange with ``ActorDied``."""
+    import time
+
+    from accerl_agent_b200.agent_textworld import exchange_weight_handles
+
+    trainers = [spawn_actor(FakeTrainer, r, name=f"t{r}") for r in range(2)]
+    engines = [spawn_actor(FakeEngine, name=f"e{i}") for i in range(3)]
+    follower = spawn_actor(FakeEngine, name="f0")
+    try:
+        exchange_weight_handles(trainers, engines, [[follower], [], []])
+        assert [e.attached()["rank"] for e in engines] == [0, 1, 0]
+        assert follower.attached()["rank"] == 0
+
+        dead_trainer = spawn_actor(FakeTrainer, 0, True, name="tdead")
+        t0 = time.monotonic()
+        with pytest.raises(ActorDied):
+            exchange_weight_handles([dead_trainer], engines[:1], [[]])
+        assert time.monotonic() - t0 < 30
+        dead_trainer.stop_process()
+
+        with pytest.raises(ActorDied):
+            get(engines[2].die.remote(), timeout=30)
+        with pytest.raises(ActorDied):
+            exchange_weight_handles(trainers, engines, [[], [], []])
+    finally:
+        for h in trainers + engines + [follower]:
+            h.stop_process()

@@ -130,3 +130,54 @@ def test_window_preparation_failure_fails_every_rank():
     for p in procs:
         p.join(60)
     assert all("At least one FSDP rank failed" in v for v in res.values()), res
+
+
+def _drop_worker(rank, port, out):
+    from accerl_agent_b200.core.config import make_args
+    from accerl_agent_b200.replay import ReplayBuffer
+    from accerl_agent_b200.trainer.worker import TrainWorker
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ["ACCERL_PG_TIMEOUT"] = "10"
+    args = make_args(model_path="tiny-qwen2", train_packing="varlen", train_token_budget=64, max_length=64,
+                     tw_history_token_window=64, batch_size=1, grad_accum_steps=1, device="cpu",
+                     min_replay_size_per_rank=1, replay_sample_timeout_seconds=5.0, replay_wait_sleep_seconds=0.01)
+    rb = ReplayBuffer(8)
+    rb.add_samples([RLSample("grpo", list(range(10)), [1] * 10, [-100] * 5 + list(range(5, 10)), [-1.0] * 10,
+                             1.0, [0.0] * 10, [-1] * 5 + [0] * 5, [0])])
+    w = TrainWorker(args, rank=rank, fsdp_world_size=2, fsdp_master_addr="127.0.0.1", fsdp_master_port=port,
+                    replay_buffer=rb, device=torch.device("cpu"))
+    w.train_until_next_sync(1)
+    if rank == 1:  # leaves between steps, with nothing in flight
+        out.put((rank, "left"))
+        out.close()
+        out.join_thread()
+        os._exit(0)
+    import time
+
+    t0 = time.monotonic()
+    try:
+        w.train_until_next_sync(1)
+        out.put((rank, "no error"))
+    except Exception as exc:
+        out.put((rank, f"error after {time.monotonic() - t0:.1f}s: {type(exc).__name__}"))
+    out.close()
+    out.join_thread()
+    os._exit(0)
+
+
+def test_rank_that_leaves_fails_the_next_collective_of_the_others():
+    """A trainer rank that exits between optimizer steps makes the next step of the remaining rank
+    raise (the lost peer or the short process-group timeout ends its collective) instead of hanging."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_drop_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(60)
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res
+    assert float(res[0].split()[2].rstrip("s:")) < 60.0, res
