@@ -42,12 +42,23 @@ def bench_gemm(results):
         t_cublas = median_ms(lambda: torch.matmul(a, w.t(), out=out))
         results[f"gemm/{name}"] = {"M": M, "N": N, "K": K, "ms": t_ours, "tflops": flops / t_ours / 1e9,
                                    "cublas_ms": t_cublas, "cublas_tflops": flops / t_cublas / 1e9}
+        # tile variants: one CTA per 128 x 256 tile vs a CTA pair per 256 x 256 tile (cta_group::2)
+        for tag, bn in (("single256", 256), ("pair256", -256)):
+            t = median_ms(lambda: ops.gemm(a, w, out, block_n=bn))
+            results[f"gemm/{name}"][f"{tag}_tflops"] = flops / t / 1e9
         # dgrad and wgrad of the same layer
         dy = torch.randn(M, N, device="cuda").bfloat16()
         dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
         gw = torch.zeros(N, K, device="cuda", dtype=torch.float32)
         t_d = median_ms(lambda: ops.linear_dgrad(dy, w, out=dx))
         t_w = median_ms(lambda: ops.linear_wgrad(dy, a, gw))
+        variants = {}
+        for tag, bn in (("single256", 256), ("single128", 128), ("pair256", -256)):
+            td = median_ms(lambda: ops.gemm(dy, w, dx, b_mn=True, block_n=bn))
+            tw = median_ms(lambda: ops.gemm(dy, a, gw, a_mn=True, b_mn=True, beta=1.0, out_dtype=torch.float32,
+                                            block_n=bn, splits=1))
+            variants[f"dgrad_{tag}_tflops"] = flops / td / 1e9
+            variants[f"wgrad_{tag}_tflops"] = flops / tw / 1e9
         t_dc = median_ms(lambda: torch.matmul(dy, w, out=dx))
         gwb = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
         t_wc = median_ms(lambda: torch.matmul(dy.t(), a, out=gwb))
@@ -55,6 +66,7 @@ def bench_gemm(results):
                                                               "cublas_ms": t_dc, "cublas_tflops": flops / t_dc / 1e9}
         results[f"gemm/{name.replace('_fwd', '')}_wgrad"] = {"ms": t_w, "tflops": flops / t_w / 1e9,
                                                               "cublas_ms": t_wc, "cublas_tflops": flops / t_wc / 1e9}
+        results[f"gemm/{name.replace('_fwd', '')}_variants"] = variants
         del a, w, out, dy, dx, gw, gwb
 
 

@@ -3,6 +3,7 @@
 16-token actions at temperature 1.0, prefix caching on).
 
     python -m accerl_agent_b200.bench_rollout [--model qwen2.5-1.5b] [--groups 32] [--seconds 30] [--tp 2]
+    python -m accerl_agent_b200.bench_rollout --impl reference   # the reference's vLLM inference actor
 
 Reports generated tokens/s (``Infer/TokensPerSec``), prefix-cache hit rate and engine step counts.
 ``--tp N`` runs one tensor-parallel engine over GPUs 0..N-1 (rank 0 in this process, the others in
@@ -24,11 +25,11 @@ from .rollout.inference import InferenceService
 from .rollout.worker import RolloutWorker
 
 
-async def _drive(service, args, groups: int, seconds: float, profile: float = 0.0):
+async def _drive(service, args, groups: int, seconds: float, profile: float = 0.0, warmup: float = 3.0):
     sink_samples = []
     worker_list = [RolloutWorker(args, service, i, sink_samples.extend, lambda *a: None) for i in range(groups)]
     tasks = [asyncio.create_task(w.run()) for w in worker_list]
-    await asyncio.sleep(3.0)  # warm-up: prefill of the first observations, kernel caches
+    await asyncio.sleep(warmup)  # warm-up: prefill of the first observations, kernel caches
     if profile > 0:
         # kernel-time breakdown of a window of engine steps (not a throughput measurement)
         from torch.profiler import ProfilerActivity, profile as tprof
@@ -82,12 +83,27 @@ def main():
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks of the engine (GPUs 0..tp-1)")
     ap.add_argument("--profile-seconds", type=float, default=0.0,
                     help="print a torch.profiler kernel table of this many seconds before timing")
+    ap.add_argument("--warmup-seconds", type=float, default=3.0)
+    ap.add_argument("--gpu-memory-utilization", type=float, default=0.8,
+                    help="share of the device the engine may hold (weights + KV cache), as the reference passes to vLLM")
+    ap.add_argument("--impl", default="native", choices=("native", "reference"),
+                    help="reference: the reference's own vLLM inference actor, driven by the same rollout loop")
     ap.add_argument("--json", default=None)
     a = ap.parse_args()
+    if a.impl == "reference":
+        import os
+        import sys
+
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        from baseline.reference_rollout import run_reference_rollout
+
+        run_reference_rollout(a)
+        return
     args = make_args(model_path=a.model, env="synthetic", rl_algorithm="grpo", rollout_batch_size=8,
                      tw_max_episode_steps=50, tw_history_token_window=a.window, max_length=a.window,
                      infer_max_tokens=16, infer_temperature=1.0, vllm_max_num_seqs=a.max_num_seqs,
-                     vllm_max_num_batched_tokens=a.max_num_batched_tokens, kv_cache_gb=60.0)
+                     vllm_max_num_batched_tokens=a.max_num_batched_tokens)
+    args.gpu_memory_utilization = a.gpu_memory_utilization
     dev = torch.device("cuda", 0)
     procs, full = [], None
     if a.tp > 1:
@@ -113,11 +129,13 @@ def main():
     else:
         service = InferenceService(args, dev)
         service.engine.model.init_weights(seed=0)
-    rate, el, samples = asyncio.run(_drive(service, args, a.groups, a.seconds, a.profile_seconds))
+    rate, el, samples = asyncio.run(_drive(service, args, a.groups, a.seconds, a.profile_seconds,
+                                                a.warmup_seconds))
     st = service.get_stats()
     out = {
         "metric": "rollout tok/s",
         "value": round(rate, 1),
+        "kv_cache_tokens": service.engine.num_blocks * service.engine.block_size,
         "unit": f"generated tokens/s (Infer/TokensPerSec), one engine on {a.tp} GPU(s)",
         "tp": a.tp,
         "model": a.model,

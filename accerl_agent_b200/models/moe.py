@@ -11,7 +11,7 @@ exchanged between ranks before and after the expert GEMMs.
 
 from __future__ import annotations
 
-from typing import Dict, Tuple
+from typing import Dict, Optional, Tuple
 
 import torch
 
@@ -111,6 +111,7 @@ def padded_layout_from_pads(pads, device):
     E = len(pads)
     return {
         "total": sum(pads),
+        "num_groups": E,
         "starts": starts,
         "tile_expert": meta[:nt],
         "row_start": meta[nt : nt + E],
@@ -118,13 +119,49 @@ def padded_layout_from_pads(pads, device):
     }
 
 
+def device_padded_layout(topi: torch.Tensor, num_experts: int, lo: int = 0, El: Optional[int] = None):
+    """Grouped-GEMM layout computed on the device, with no host synchronisation.
+
+    The pairs ``(token, slot)`` of ``topi`` are sorted by expert; experts ``[lo, lo + El)`` get row
+    segments padded to SEG rows, laid out back to back. Sizes are bounded on the host without reading
+    the counts: ``total = round_up(n + El * (SEG - 1), SEG)`` rows always hold every segment, and the
+    128-row tiles past the real end carry ``tile_expert = -1`` (the GEMM skips them). Pairs routed to
+    experts outside the range (tensor-parallel engine shards) are sent to the extra row ``total``.
+    Returns ``(order, rows_sorted, valid_sorted, layout)``: the sorting permutation, every sorted
+    pair's row and whether it runs here."""
+    flat = topi.reshape(-1)
+    n = flat.numel()
+    El = num_experts if El is None else El
+    dev = flat.device
+    order = torch.argsort(flat, stable=True)
+    e_sorted = flat.index_select(0, order)
+    counts = torch.bincount(flat, minlength=num_experts)
+    cstart = torch.cumsum(counts, 0) - counts
+    cl = counts[lo : lo + El]
+    pads = torch.div(cl + (SEG - 1), SEG, rounding_mode="floor") * SEG
+    ends = torch.cumsum(pads, 0)
+    starts = ends - pads
+    total = ((n + El * (SEG - 1) + SEG - 1) // SEG) * SEG
+    tiles = total // SEG
+    te = torch.searchsorted(ends, torch.arange(tiles, device=dev, dtype=ends.dtype) * SEG, right=True)
+    tile_expert = torch.where(te < El, te, torch.full_like(te, -1)).to(torch.int32)
+    e_loc = e_sorted - lo
+    valid = (e_loc >= 0) & (e_loc < El)
+    e_idx = e_loc.clamp(0, El - 1)
+    rows = starts.index_select(0, e_idx) + torch.arange(n, device=dev) - cstart.index_select(0, e_sorted)
+    rows = torch.where(valid, rows, torch.full_like(rows, total))
+    lay = {"total": total, "num_groups": El, "tile_expert": tile_expert, "row_start": starts.to(torch.int32),
+           "rows": pads.to(torch.int32), "counts": counts}
+    return order, rows, valid, lay
+
+
 def _grouped(a, a_mn, b, b_mn, out, M, N, K, mode, lay, b_stride, c_stride=0, beta=0.0, row_dst=None):
     ops.native().grouped_gemm(a, a_mn, b, b_mn, out, M, N, K, beta, mode, lay["tile_expert"], lay["row_start"],
-                              lay["rows"], len(lay["starts"]), b_stride, c_stride, ops.status_tensor(a.device),
+                              lay["rows"], lay["num_groups"], b_stride, c_stride, ops.status_tensor(a.device),
                               row_dst)
 
 
-def experts_forward_grouped(model, layer: int, xs_pad: torch.Tensor, lay):
+def experts_forward_grouped(model, layer: int, xs_pad: torch.Tensor, lay, out=None):
     cfg = model.cfg
     p = f"model.layers.{layer}.mlp.experts."
     E, Im, H = model.w(p + "gate_up_proj").shape[0], cfg.moe_intermediate_size, cfg.hidden_size
@@ -134,7 +171,7 @@ def experts_forward_grouped(model, layer: int, xs_pad: torch.Tensor, lay):
     gu = torch.empty(R, 2 * Im, dtype=xs_pad.dtype, device=xs_pad.device)
     _grouped(xs_pad, False, Wgu, False, gu, R, 2 * Im, H, 1, lay, 2 * Im)
     act = ops.swiglu(gu)
-    ys = torch.empty(R, H, dtype=xs_pad.dtype, device=xs_pad.device)
+    ys = out if out is not None else torch.empty(R, H, dtype=xs_pad.dtype, device=xs_pad.device)
     _grouped(act, False, Wd, False, ys, R, H, Im, 1, lay, H)
     return ys, gu, act
 
@@ -165,6 +202,9 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     k = cfg.num_experts_per_tok
     probs, topw, topi = route(model, layer, h)
     w_act = topw.to(h.dtype)
+    ep = getattr(model, "expert_parallel", None)
+    if ep is None and h.is_cuda and h.dtype == torch.bfloat16:
+        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
     El = cfg.local_experts
     if El is not None and El != cfg.num_experts:
@@ -175,7 +215,6 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
         order, counts = order[a:b], counts[lo : lo + El]
         bounds = [x - a for x in bounds[lo : lo + El + 1]]
     tok = torch.div(order, k, rounding_mode="floor")
-    ep = getattr(model, "expert_parallel", None)
     lay = None
     ep_state = None
     if ep is not None:
@@ -206,15 +245,7 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
         # no pair runs here (a tensor-parallel shard whose experts got no tokens): row 0 must exist
         ys = torch.zeros(1, cfg.hidden_size, dtype=h.dtype, device=h.device)
     cache: Dict[str, torch.Tensor] = {}
-    sy = sg = None
-    if cfg.shared_expert_intermediate_size > 0:
-        p = f"model.layers.{layer}.mlp."
-        sgu = ops.linear(h, model.w(p + "shared_expert.gate_up_proj.weight"))
-        sact = ops.swiglu(sgu)
-        sy = ops.linear(sact, model.w(p + "shared_expert.down_proj.weight"))
-        sg = torch.sigmoid((h @ model.w(p + "shared_expert_gate.weight").t()).float())
-        if save:
-            cache.update(sgu=sgu, sact=sact, sy=sy, sg=sg)
+    sy, sg = _shared_expert(model, layer, h, cache if save else None)
     out = ops.moe_combine(ys, pos_pairs, w_pairs, k, residual=residual, shared=sy, sg=sg)
     if save:
         cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=xs, gu=gu, act=act, ys=ys,
@@ -227,6 +258,54 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     return out, cache
 
 
+def _shared_expert(model, layer: int, h: torch.Tensor, cache):
+    cfg = model.cfg
+    if cfg.shared_expert_intermediate_size <= 0:
+        return None, None
+    p = f"model.layers.{layer}.mlp."
+    sgu = ops.linear(h, model.w(p + "shared_expert.gate_up_proj.weight"))
+    sact = ops.swiglu(sgu)
+    sy = ops.linear(sact, model.w(p + "shared_expert.down_proj.weight"))
+    sg = torch.sigmoid((h @ model.w(p + "shared_expert_gate.weight").t()).float())
+    if cache is not None:
+        cache.update(sgu=sgu, sact=sact, sy=sy, sg=sg)
+    return sy, sg
+
+
+def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi):
+    """CUDA path without host synchronisation: device-side padded layout, grouped GEMMs over the
+    bounded tile count, fused combine. Training (``save``) zeroes the padded input rows because the
+    weight-gradient contraction runs over them; inference leaves them uninitialised (their output
+    rows are never read)."""
+    cfg = model.cfg
+    k = cfg.num_experts_per_tok
+    El = cfg.local_experts if cfg.local_experts is not None else cfg.num_experts
+    lo = cfg.expert_offset if El != cfg.num_experts else 0
+    order, rows, valid, lay = device_padded_layout(topi, cfg.num_experts, lo, El)
+    R = lay["total"]
+    tok = torch.div(order, k, rounding_mode="floor")
+    alloc = torch.zeros if save else torch.empty
+    xs = alloc(R + 1, h.shape[1], dtype=h.dtype, device=h.device)
+    xs.index_copy_(0, rows, h.index_select(0, tok))
+    ys_full = torch.empty(R + 1, cfg.hidden_size, dtype=h.dtype, device=h.device)
+    ys_full[R].zero_()  # the row of pairs that do not run here (weight 0)
+    ys, gu, act = experts_forward_grouped(model, layer, xs[:R], lay, out=ys_full[:R])
+    n_pairs = topi.numel()
+    pos_pairs = torch.empty(n_pairs, dtype=torch.long, device=h.device)
+    pos_pairs[order] = rows
+    w_sorted = topw.to(h.dtype).reshape(-1).float().index_select(0, order)
+    w_pairs = torch.empty(n_pairs, dtype=torch.float32, device=h.device)
+    w_pairs[order] = torch.where(valid, w_sorted, torch.zeros_like(w_sorted))
+    cache: Dict[str, torch.Tensor] = {}
+    sy, sg = _shared_expert(model, layer, h, cache if save else None)
+    out = ops.moe_combine(ys_full, pos_pairs, w_pairs, k, residual=residual, shared=sy, sg=sg)
+    if save:
+        cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=xs[:R], gu=gu, act=act,
+                     ys=ys_full, pos_pairs=pos_pairs, w_pairs=w_pairs)
+        cache["layout"] = lay  # type: ignore[assignment]
+    return out, cache
+
+
 def moe_backward(model, layer: int, dx3: torch.Tensor, c) -> torch.Tensor:
     cfg = model.cfg
     m = c.mlp
@@ -234,19 +313,21 @@ def moe_backward(model, layer: int, dx3: torch.Tensor, c) -> torch.Tensor:
     k = cfg.num_experts_per_tok
     p = f"model.layers.{layer}.mlp."
     pos_pairs, w_pairs, ys = m["pos_pairs"], m["w_pairs"], m["ys"]
-    bounds = m["bounds"].tolist()
+    bounds = m["bounds"].tolist() if "bounds" in m else None
     ep = getattr(model, "expert_parallel", None)
     dx3c = dx3.contiguous()
     if "layout" in m:
         lay = m["layout"]
-        dys = torch.zeros(lay["total"], cfg.hidden_size, dtype=dx3.dtype, device=dx3.device)  # pad rows stay 0
+        # pad rows stay 0; one spare row for the device layout's row of pairs that do not run here
+        dys = torch.zeros(lay["total"] + 1, cfg.hidden_size, dtype=dx3.dtype, device=dx3.device)
     else:
         dys = torch.empty(ys.shape[0], cfg.hidden_size, dtype=dx3.dtype, device=dx3.device)
     dw = ops.moe_combine_backward(dx3c, ys, pos_pairs, w_pairs, k, dys)
     if ep is not None:
         dxs = ep.backward(model, layer, dys, m["ep_state"])
     elif "layout" in m:
-        dxs = experts_backward_grouped(model, layer, dys, m["xs"], m["gu"], m["act"], m["layout"])
+        R = m["layout"]["total"]
+        dxs = experts_backward_grouped(model, layer, dys[:R], m["xs"], m["gu"], m["act"], m["layout"])
     else:
         dxs = experts_backward(model, layer, dys, m["xs"], m["gu"], m["act"], bounds)
     # every pair's input-gradient row back to its token (unit weights)

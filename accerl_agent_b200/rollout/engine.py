@@ -111,6 +111,7 @@ class GenerationEngine:
         enable_prefix_caching: bool = True,
         tokenizer=None,
         params: Optional[torch.Tensor] = None,
+        gpu_memory_utilization: Optional[float] = None,
         seed: int = 0,
         decode_splits: Optional[int] = None,
         use_cuda_graphs: bool = True,
@@ -162,8 +163,14 @@ class GenerationEngine:
         if num_blocks is None:
             if kv_cache_gb is None:
                 if device.type == "cuda":
-                    free, _ = torch.cuda.mem_get_info(device)
-                    kv_cache_gb = 0.6 * free / 1024**3
+                    free, total = torch.cuda.mem_get_info(device)
+                    if gpu_memory_utilization:
+                        # vLLM's rule: this process may hold `utilization` of the device; what the
+                        # weights leave, minus a reserve for step workspaces, becomes KV cache
+                        reserve = 10 * 1024**3
+                        kv_cache_gb = max(1.0, (gpu_memory_utilization * total - (total - free) - reserve) / 1024**3)
+                    else:
+                        kv_cache_gb = 0.6 * free / 1024**3
                 else:
                     kv_cache_gb = 0.25
             num_blocks = max(16, int(kv_cache_gb * 1024**3 // per_block))

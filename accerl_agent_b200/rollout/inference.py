@@ -55,6 +55,7 @@ def build_engine(args, device: torch.device, tokenizer=None, dtype: Optional[tor
         max_model_len=args.vllm_max_model_len,
         block_size=getattr(args, "kv_block_size", 16),
         kv_cache_gb=getattr(args, "kv_cache_gb", None),
+        gpu_memory_utilization=getattr(args, "gpu_memory_utilization", None),
         enable_prefix_caching=not args.disable_vllm_prefix_caching,
         tokenizer=tokenizer,
         tp_group=tp_group,

@@ -79,8 +79,9 @@ def _install_ray_stand_in():
     sys.modules["textworld.gym"] = tw_gym
 
 
-def _write_model_dir(path: str, model: str):
-    """Random-init HF checkpoint + word-level tokenizer of the benchmark shape (rank 0 writes)."""
+def _write_model_dir(path: str, model: str, weights: bool = True):
+    """Random-init HF checkpoint + word-level tokenizer of the benchmark shape (rank 0 writes).
+    ``weights=False`` writes only the config and tokenizer (enough for vLLM's dummy weights)."""
     import torch
     import transformers
     from tokenizers import Tokenizer, models, pre_tokenizers
@@ -89,11 +90,15 @@ def _write_model_dir(path: str, model: str):
 
     cfg = get_preset(model)
     hf_cfg = transformers.AutoConfig.for_model(**cfg.to_hf_dict())
-    torch.manual_seed(42)
-    m = transformers.AutoModelForCausalLM.from_config(hf_cfg, torch_dtype=torch.bfloat16)
-    m.save_pretrained(path, safe_serialization=True)
+    if weights:
+        torch.manual_seed(42)
+        m = transformers.AutoModelForCausalLM.from_config(hf_cfg, dtype=torch.bfloat16)
+        m.save_pretrained(path, safe_serialization=True)
+    else:
+        hf_cfg.save_pretrained(path)
+    # word-level vocabulary over every model id (no newline token), so any sampled id decodes
     vocab = {"<|endoftext|>": 0, "<|im_start|>": 1, "<|im_end|>": 2}
-    for i in range(3, 1024):
+    for i in range(3, cfg.vocab_size):
         vocab[f"w{i}"] = i
     tok = Tokenizer(models.WordLevel(vocab=vocab, unk_token="<|endoftext|>"))
     tok.pre_tokenizer = pre_tokenizers.Whitespace()

@@ -295,6 +295,9 @@ __global__ void __launch_bounds__(192, 1)
 // ------------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------------
+// 8 elementwise warps (two warpgroups over the column halves), 1 TMA warp, 1 MMA warp
+constexpr int kBwdThreads = 320;
+
 struct AttnBwdParams {
   const float* lse;    // [Hq, T]
   const float* delta;  // [Hq, T]
@@ -308,7 +311,7 @@ struct AttnBwdParams {
   int* status;
 };
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const AttnBwdParams p) {
@@ -351,13 +354,13 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(ps_full, 128);
+    mbar_init(ps_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 256);
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  if (warp == 9) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -367,7 +370,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tDV = tbase + 256;
   const uint32_t tDK = tbase + 384;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       const int ky = seq_start + kt * kTile;
       mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
@@ -386,7 +389,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       mbar_wait(kv_full, 0, nullptr, 0, 20000000ull);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       constexpr uint32_t idesc_kk = make_idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_kmn = make_idesc_bf16_f32(128, 128, false, true);
@@ -420,8 +423,12 @@ __global__ void __launch_bounds__(192, 1)
       umma_commit(acc_done);
     }
   } else {
-    const int r = threadIdx.x;  // key row for S^T/dP^T/dK/dV; query row for dQ
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    // Two warpgroups share every 128 x 128 tile: warp w reads TMEM lanes 32*(w%4).. (its rows) and
+    // handles the column half w/4, so each thread does 64 columns of the elementwise work.
+    const int quad = warp & 3;
+    const int half = warp >> 2;
+    const int r = quad * 32 + lane;  // key row for S^T/dP^T/dK/dV; query row for dQ
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const int k_pos = kt * kTile + r;
     const bool key_valid = k_pos < len;
     const int ldacc = p.Hq * kHd;
@@ -438,22 +445,24 @@ __global__ void __launch_bounds__(192, 1)
         dl = 0.f;
       }
     };
-    float nxt_lse, nxt_delta;
-    load_stats(q_first, nxt_lse, nxt_delta);
+    float nxt_lse = 0.f, nxt_delta = 0.f;
+    if (half == 0) load_stats(q_first, nxt_lse, nxt_delta);
     for (int i = 0; i < nq; ++i) {
       const int qt = q_first + i;
-      named_bar_sync(1, 128);
-      s_lse[r] = nxt_lse;
-      s_delta[r] = nxt_delta;
-      named_bar_sync(1, 128);
-      if (i + 1 < nq) load_stats(qt + 1, nxt_lse, nxt_delta);
+      named_bar_sync(1, 256);
+      if (half == 0) {
+        s_lse[r] = nxt_lse;
+        s_delta[r] = nxt_delta;
+      }
+      named_bar_sync(1, 256);
+      if (half == 0 && i + 1 < nq) load_stats(qt + 1, nxt_lse, nxt_delta);
       if (!mbar_wait(s_full, i & 1, p.status, kStatusTimeoutEpilogue)) {
         ok = false;
         break;
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c * 32 + lane_off, sv);
         tmem_ld32(tDP + c * 32 + lane_off, dv);
@@ -491,8 +500,8 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int q_pos = qt * kTile + r;
       float* dqrow = p.dq_acc + static_cast<long long>(seq_start + q_pos) * ldacc + head * kHd;
-#pragma unroll 1
-      for (int c = 0; c < 4; c += 2) {
+      {
+        const int c = 2 * half;
         uint32_t v[32], v2[32];
         tmem_ld32(tS + c * 32 + lane_off, v);
         tmem_ld32(tS + (c + 1) * 32 + lane_off, v2);
@@ -518,7 +527,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const long long rowoff = static_cast<long long>(seq_start + k_pos) * ldacc + head * kHd;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t v[32], w[32];
         tmem_ld32(tDV + c * 32 + lane_off, v);
         tmem_ld32(tDK + c * 32 + lane_off, w);
@@ -538,7 +547,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);
   }
@@ -709,7 +718,7 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
   p.causal = causal;
   p.status = status;
   dim3 grid(p.max_tiles * Hq, num_seqs);
-  attn_bwd_kernel<<<grid, 192, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
+  attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
   const long long n4 = acc_elems / 4;
   attn_bwd_finalize_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(
       dq_acc, p.dk_part, p.dv_part, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, total_tokens, Hq, Hkv,

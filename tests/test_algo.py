@@ -171,3 +171,34 @@ def test_lr_schedule():
     assert math.isclose(warmup_cosine_lr(55, 1.0, 10, 100), 0.5, rel_tol=1e-9)
     assert math.isclose(warmup_cosine_lr(100, 1.0, 10, 100), 0.0, abs_tol=1e-12)
     assert warmup_cosine_lr(3, 2.0, 0, 0) == 2.0
+
+
+def test_device_padded_layout_matches_host_layout():
+    """The sync-free expert layout (computed with device ops, here on CPU) places every (token, slot)
+    pair in the same padded segment row as the host layout, marks tiles past the end with -1 and sends
+    pairs of experts outside a tensor-parallel shard's range to the spare row."""
+    import torch
+
+    from accerl_agent_b200.models.moe import SEG, _expert_segments, device_padded_layout, padded_layout
+
+    g = torch.Generator().manual_seed(3)
+    E, k, T = 12, 4, 300
+    topi = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    for lo, El in ((0, E), (4, 5)):
+        order, rows, valid, lay = device_padded_layout(topi, E, lo, El)
+        o_ref, counts, bounds = _expert_segments(topi, E)
+        assert torch.equal(order, o_ref)
+        ref = padded_layout(counts[lo : lo + El].tolist(), torch.device("cpu"))
+        n_tiles_ref = ref["tile_expert"].numel()
+        assert torch.equal(lay["tile_expert"][:n_tiles_ref], ref["tile_expert"])
+        assert bool((lay["tile_expert"][n_tiles_ref:] == -1).all())
+        assert lay["total"] % SEG == 0 and lay["total"] >= ref["total"]
+        assert torch.equal(lay["row_start"], ref["row_start"]) and torch.equal(lay["rows"], ref["rows"])
+        e_sorted = topi.reshape(-1)[order]
+        for j in range(order.numel()):
+            e = int(e_sorted[j])
+            if lo <= e < lo + El:
+                assert bool(valid[j])
+                assert int(rows[j]) == ref["starts"][e - lo] + j - bounds[e]
+            else:
+                assert not bool(valid[j]) and int(rows[j]) == lay["total"]

@@ -62,6 +62,44 @@ def test_gemm_epilogue_bias_residual_beta(block_n):
     assert _rel(acc, base + 0.5 * (A.float() @ B.float().t())) < 1e-5
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("M,N,K", [(1024, 1536, 512), (520, 776, 328)])
+def test_gemm_cta_pair_layouts(a_mn, b_mn, M, N, K):
+    """The CTA-pair kernel (two SMs per 256 x 256 tile, tcgen05 cta_group::2) for every operand
+    major, with row / column / K tails, against the fp32 product."""
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    a_in = A.t().contiguous() if a_mn else A
+    b_in = B.t().contiguous() if b_mn else B
+    want = A.float() @ B.float().t()
+    out = ops.gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn, out_dtype=torch.float32, block_n=-256)
+    assert _rel(out, want) < 1e-5
+    out_bf = ops.gemm(a_in, b_in, a_mn=a_mn, b_mn=b_mn, block_n=-256)
+    assert _rel(out_bf, want) < 1e-2
+    st = ops.status_tensor(torch.device(DEV))
+    assert int(st[0]) == 0
+
+
+def test_gemm_cta_pair_epilogues_and_split():
+    M, N, K = 777, 1280, 1024
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    bias = torch.randn(N, device=DEV).bfloat16()
+    res = torch.randn(M, N, device=DEV).bfloat16()
+    out = ops.gemm(A, B, bias=bias, residual=res, block_n=-256)
+    assert _rel(out, A.float() @ B.float().t() + bias.float() + res.float()) < 1e-2
+    acc = torch.randn(M, N, device=DEV)
+    base = acc.clone()
+    ops.gemm(A, B, acc, beta=1.0, alpha=0.5, out_dtype=torch.float32, block_n=-256)
+    assert _rel(acc, base + 0.5 * (A.float() @ B.float().t())) < 1e-5
+    acc2 = torch.zeros(M, N, device=DEV)
+    ops.gemm(A, B, acc2, beta=1.0, out_dtype=torch.float32, block_n=-256, splits=4)
+    assert _rel(acc2, A.float() @ B.float().t()) < 1e-5
+    # a grid smaller than the tile count: clusters loop over several work items
+    out3 = ops.gemm(A, B, block_n=-256, max_ctas=4)
+    assert _rel(out3, A.float() @ B.float().t()) < 1e-2
+
+
 def test_gemm_strided_views():
     # q/k/v style column slices of a fused buffer as operands and outputs
     T, H = 384, 256
