@@ -263,8 +263,11 @@ def _shared_expert(model, layer: int, h: torch.Tensor, cache):
     if cfg.shared_expert_intermediate_size <= 0:
         return None, None
     p = f"model.layers.{layer}.mlp."
-    sgu = ops.linear(h, model.w(p + "shared_expert.gate_up_proj.weight"))
-    sact = ops.swiglu(sgu)
+    if cache is not None:
+        sgu = ops.linear(h, model.w(p + "shared_expert.gate_up_proj.weight"))
+        sact = ops.swiglu(sgu)
+    else:
+        sact, sgu = ops.linear_swiglu(h, model.w(p + "shared_expert.gate_up_proj.weight"))
     sy = ops.linear(sact, model.w(p + "shared_expert.down_proj.weight"))
     sg = torch.sigmoid((h @ model.w(p + "shared_expert_gate.weight").t()).float())
     if cache is not None:

@@ -239,8 +239,13 @@ class CausalLM:
 
             x3, mlp_cache = moe_forward(self, layer, h2, x2, save)
         else:
-            gu = ops.linear(h2, self.w(p + "mlp.gate_up_proj.weight"))
-            act = ops.swiglu(gu)
+            if save:
+                # training keeps g|u for the backward; the separate SwiGLU kernel is cheaper here than
+                # the fused epilogue, whose three row-strided outputs slow the short-K GEMM
+                gu = ops.linear(h2, self.w(p + "mlp.gate_up_proj.weight"))
+                act = ops.swiglu(gu)
+            else:
+                act, gu = ops.linear_swiglu(h2, self.w(p + "mlp.gate_up_proj.weight"))
             x3 = ops.linear(act, self.w(p + "mlp.down_proj.weight"), residual=x2)
             mlp_cache = {"gu": gu, "act": act} if save else {}
         cache = LayerCache(x, h1, rstd1, qkv, attn, lse, x2, h2, rstd2, mlp_cache, qk) if save else None
@@ -348,12 +353,15 @@ class CausalLM:
         k = c.qkv[:, cfg.q_dim : cfg.q_dim + cfg.kv_dim]
         v = c.qkv[:, cfg.q_dim + cfg.kv_dim :]
         dqkv = torch.empty_like(c.qkv)
+        fuse_rope = dattn.is_cuda and D == 128
         ops.attention_varlen_backward(
             dattn, q, k, v, c.attn, c.lse, ctx.cu, ctx.max_seqlen, Hq, Hkv, D,
             dq=dqkv[:, : cfg.q_dim], dk=dqkv[:, cfg.q_dim : cfg.q_dim + cfg.kv_dim], dv=dqkv[:, cfg.q_dim + cfg.kv_dim :],
+            rope_pos=ctx.pos.view(-1) if fuse_rope else None, rope_theta=cfg.rope_theta,
         )
         del dattn
-        ops.rope_(dqkv, ctx.pos, Hq + Hkv, D, cfg.rope_theta, inverse=True)
+        if not fuse_rope:
+            ops.rope_(dqkv, ctx.pos, Hq + Hkv, D, cfg.rope_theta, inverse=True)
         if cfg.qk_norm:
             self._qk_norm_backward(layer, dqkv, c)
         if cfg.qkv_bias:

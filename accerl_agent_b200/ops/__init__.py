@@ -66,6 +66,8 @@ __all__ = [
     "rope_",
     "swiglu",
     "swiglu_backward",
+    "linear_swiglu",
+    "linear_dgrad_swiglu",
     "embedding",
     "embedding_backward",
     "attention_varlen",
@@ -233,6 +235,31 @@ def rope_(qkv: torch.Tensor, pos: torch.Tensor, n_rot_heads: int, head_dim: int,
     return qkv
 
 
+def linear_swiglu(x: torch.Tensor, w: torch.Tensor, keep_gu: bool = False):
+    """``h = silu(x Wg^T) * (x Wu^T)`` for ``w = [Wg; Wu]`` ([2I, in]). Returns ``(h, gu)`` where
+    ``gu = x w^T`` is materialised only when ``keep_gu`` (the backward needs it). On the GPU the
+    SwiGLU runs in the GEMM epilogue (one kernel; I a multiple of 128); skinny products (decode
+    steps) keep the split-K GEMM and the separate SwiGLU kernel."""
+    inter = w.shape[0] // 2
+    if x.is_cuda and x.dtype == torch.bfloat16 and inter % 128 == 0 and x.shape[0] > 256:
+        h = torch.empty(x.shape[0], inter, dtype=x.dtype, device=x.device)
+        gu = torch.empty(x.shape[0], 2 * inter, dtype=x.dtype, device=x.device) if keep_gu else None
+        native().gemm_glu(x, w, gu, h, status_tensor(x.device), 0, 0)
+        return h, gu
+    gu = linear(x, w)
+    return swiglu(gu), (gu if keep_gu else None)
+
+
+def linear_dgrad_swiglu(dy: torch.Tensor, wd: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
+    """``d(gate|up)`` of a SwiGLU MLP from the down projection's output gradient: the SwiGLU backward
+    of ``dy wd`` (wd [out, I]) given the saved ``gu``, fused into the dgrad GEMM's epilogue on the GPU."""
+    if dy.is_cuda and dy.dtype == torch.bfloat16:
+        dgu = torch.empty_like(gu)
+        native().gemm_dglu(dy, wd, gu, dgu, status_tensor(dy.device), 0, 0)
+        return dgu
+    return swiglu_backward(linear_dgrad(dy, wd), gu)
+
+
 def swiglu(gu: torch.Tensor) -> torch.Tensor:
     if gu.is_cuda:
         h = torch.empty(gu.shape[0], gu.shape[1] // 2, dtype=gu.dtype, device=gu.device)
@@ -315,9 +342,11 @@ def attention_varlen(
 
 def attention_varlen_backward(
     dout, q, k, v, o, lse, cu_seqlens, max_seqlen, n_heads, n_kv_heads, head_dim, scale=None, causal=True,
-    dq=None, dk=None, dv=None,
+    dq=None, dk=None, dv=None, rope_pos=None, rope_theta: float = 0.0,
 ):
-    """Gradients w.r.t. q, k, v. ``dq/dk/dv`` may be strided views into a fused d(qkv) buffer."""
+    """Gradients w.r.t. q, k, v. ``dq/dk/dv`` may be strided views into a fused d(qkv) buffer.
+    With ``rope_pos`` (int64 [T]) the inverse rotary rotation (``rope_theta``) is applied to dq and dk,
+    i.e. the gradients are returned w.r.t. q and k before RoPE (fused into the finishing kernel)."""
     scale = reference.default_scale(head_dim) if scale is None else scale
     T = q.shape[0]
     if q.is_cuda:
@@ -326,8 +355,10 @@ def attention_varlen_backward(
         dv = dv if dv is not None else torch.empty(T, n_kv_heads * head_dim, dtype=q.dtype, device=q.device)
         acc = workspace(q.device, "attn_acc", 3 * T * n_heads * head_dim)
         delta = workspace(q.device, "attn_delta", n_heads * T)
+        if rope_pos is not None and head_dim != 128:
+            raise ValueError("fused inverse RoPE needs head_dim 128")
         native().attn_bwd(q, k, v, o, dout, lse, delta, acc, dq, dk, dv, cu_seqlens, max_seqlen, n_heads,
-                          n_kv_heads, scale, causal, status_tensor(q.device))
+                          n_kv_heads, scale, causal, status_tensor(q.device), rope_pos, float(rope_theta))
         return dq, dk, dv
     with torch.enable_grad():
         qf = q.detach().float().reshape(T, n_heads, head_dim).requires_grad_(True)
@@ -343,6 +374,10 @@ def attention_varlen_backward(
             res.append(dst)
         else:
             res.append(g)
+    if rope_pos is not None:
+        for g, heads in ((res[0], n_heads), (res[1], n_kv_heads)):
+            view = g.reshape(T, heads, head_dim)
+            view.copy_(reference.apply_rope(view, rope_pos.view(-1), rope_theta, True))
     return tuple(res)
 
 

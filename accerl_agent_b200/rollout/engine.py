@@ -686,8 +686,8 @@ class GenerationEngine:
                 y, _ = moe_forward(m, layer, h2, torch.zeros_like(x), save=False)
                 x = self._reduce_partial(y, x)
             else:
-                gu = ops.linear(h2, m.w(p + "mlp.gate_up_proj.weight"))
-                x = self._row_parallel(ops.swiglu(gu), m.w(p + "mlp.down_proj.weight"), x)
+                act, _ = ops.linear_swiglu(h2, m.w(p + "mlp.gate_up_proj.weight"))
+                x = self._row_parallel(act, m.w(p + "mlp.down_proj.weight"), x)
         return x
 
     # ------------------------------------------------------------------ CUDA-graph decode

@@ -570,40 +570,75 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 }
 
 // dq (bf16, strided) from the fp32 accumulator; dk/dv from per-q-head partials summed over the GQA group.
+// dq / dk / dv to bf16 (dk, dv summed over the query heads of each KV group), optionally with the
+// inverse rotary rotation of dq and dk fused in (pos != nullptr). One thread per (token, head, 4 of
+// the first 64 head dims): it also handles the 4 matching dims of the second half (d + 64), the
+// pair that the rotate-half convention mixes.
 __global__ void attn_bwd_finalize_kernel(const float* __restrict__ dq_acc, const float* __restrict__ dk_part,
                                          const float* __restrict__ dv_part, __nv_bfloat16* __restrict__ dq,
                                          __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int T, int Hq,
-                                         int Hkv, long long lddq, long long lddk, long long lddv) {
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // over T*Hq*128/4
-  const long long per_t = static_cast<long long>(Hq) * kHd / 4;
+                                         int Hkv, long long lddq, long long lddk, long long lddv,
+                                         const long long* __restrict__ pos, float log2_theta) {
+  constexpr int kHalf = kHd / 2;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // over T*Hq*kHalf/4
+  const long long per_t = static_cast<long long>(Hq) * kHalf / 4;
   if (idx >= static_cast<long long>(T) * per_t) return;
   const int t = static_cast<int>(idx / per_t);
-  const int c4 = static_cast<int>(idx % per_t) * 4;  // column inside the q-head space
-  const float4 q = *reinterpret_cast<const float4*>(dq_acc + static_cast<long long>(t) * Hq * kHd + c4);
-  uint2 qo;
-  qo.x = pack_bf16x2(q.x, q.y);
-  qo.y = pack_bf16x2(q.z, q.w);
-  *reinterpret_cast<uint2*>(dq + t * lddq + c4) = qo;
+  const int r = static_cast<int>(idx % per_t);
+  const int h = r / (kHalf / 4);
+  const int d = (r % (kHalf / 4)) * 4;  // 0..60
+  float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
+  if (pos) {
+    const float p = static_cast<float>(pos[t]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      rope_cos_sin(p, d + i, kHd, log2_theta, c[i], sn[i]);
+      sn[i] = -sn[i];  // inverse rotation
+    }
+  }
+  auto store_rot = [&](float4 lo, float4 hi, __nv_bfloat16* dst, bool rotate) {
+    float a[4] = {lo.x, lo.y, lo.z, lo.w}, b[4] = {hi.x, hi.y, hi.z, hi.w};
+    float x[4], y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (rotate) {
+        // bf16 inputs, as the separate RoPE kernel sees them
+        const float a16 = __bfloat162float(__float2bfloat16(a[i])), b16 = __bfloat162float(__float2bfloat16(b[i]));
+        x[i] = a16 * c[i] - b16 * sn[i];
+        y[i] = b16 * c[i] + a16 * sn[i];
+      } else {
+        x[i] = a[i];
+        y[i] = b[i];
+      }
+    }
+    uint2 o1, o2;
+    o1.x = pack_bf16x2(x[0], x[1]);
+    o1.y = pack_bf16x2(x[2], x[3]);
+    o2.x = pack_bf16x2(y[0], y[1]);
+    o2.y = pack_bf16x2(y[2], y[3]);
+    *reinterpret_cast<uint2*>(dst + d) = o1;
+    *reinterpret_cast<uint2*>(dst + d + kHalf) = o2;
+  };
+  const long long qoff = static_cast<long long>(t) * Hq * kHd + h * kHd + d;
+  store_rot(*reinterpret_cast<const float4*>(dq_acc + qoff), *reinterpret_cast<const float4*>(dq_acc + qoff + kHalf),
+            dq + t * lddq + h * kHd, pos != nullptr);
   const int group = Hq / Hkv;
-  const int h = c4 / kHd;
   if (h % group != 0) return;  // the first head of each group writes the group sum
-  const int d = c4 % kHd;
   const int kvh = h / group;
-  float4 sk = make_float4(0, 0, 0, 0), sv = make_float4(0, 0, 0, 0);
+  float4 k0 = make_float4(0, 0, 0, 0), k1 = k0, v0 = k0, v1 = k0;
   for (int g = 0; g < group; ++g) {
     const long long off = static_cast<long long>(t) * Hq * kHd + (h + g) * kHd + d;
-    const float4 a = *reinterpret_cast<const float4*>(dk_part + off);
-    const float4 b = *reinterpret_cast<const float4*>(dv_part + off);
-    sk.x += a.x; sk.y += a.y; sk.z += a.z; sk.w += a.w;
-    sv.x += b.x; sv.y += b.y; sv.z += b.z; sv.w += b.w;
+    const float4 a0 = *reinterpret_cast<const float4*>(dk_part + off);
+    const float4 a1 = *reinterpret_cast<const float4*>(dk_part + off + kHalf);
+    const float4 b0 = *reinterpret_cast<const float4*>(dv_part + off);
+    const float4 b1 = *reinterpret_cast<const float4*>(dv_part + off + kHalf);
+    k0.x += a0.x; k0.y += a0.y; k0.z += a0.z; k0.w += a0.w;
+    k1.x += a1.x; k1.y += a1.y; k1.z += a1.z; k1.w += a1.w;
+    v0.x += b0.x; v0.y += b0.y; v0.z += b0.z; v0.w += b0.w;
+    v1.x += b1.x; v1.y += b1.y; v1.z += b1.z; v1.w += b1.w;
   }
-  uint2 ko, vo;
-  ko.x = pack_bf16x2(sk.x, sk.y);
-  ko.y = pack_bf16x2(sk.z, sk.w);
-  vo.x = pack_bf16x2(sv.x, sv.y);
-  vo.y = pack_bf16x2(sv.z, sv.w);
-  *reinterpret_cast<uint2*>(dk + t * lddk + kvh * kHd + d) = ko;
-  *reinterpret_cast<uint2*>(dv + t * lddv + kvh * kHd + d) = vo;
+  store_rot(k0, k1, dk + t * lddk + kvh * kHd, pos != nullptr);
+  store_rot(v0, v1, dv + t * lddv + kvh * kHd, false);
 }
 
 namespace {
@@ -682,8 +717,9 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
                                const int* cu_seqlens, int num_seqs, int max_seqlen, int total_tokens, int Hq, int Hkv,
                                long long ldq, long long ldk, long long ldv, long long ldo, long long lddo,
                                long long lddq, long long lddk, long long lddv, float scale, int causal, int* status,
-                               cudaStream_t s) {
+                               const long long* rope_pos, float rope_theta, cudaStream_t s) {
   if (num_seqs <= 0 || total_tokens <= 0) return 0;
+  if (rope_pos && !(rope_theta > 0.f)) return -4;
   if (Hq % Hkv) return -1;
   if ((ldq | ldk | ldv | ldo | lddo | lddq | lddk | lddv) & 7) return -2;
   CUtensorMap mq, mk, mv, mdo;
@@ -719,9 +755,9 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
   p.status = status;
   dim3 grid(p.max_tiles * Hq, num_seqs);
   attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
-  const long long n4 = acc_elems / 4;
-  attn_bwd_finalize_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(
+  const long long n8 = acc_elems / 8;  // one thread per 4 dims of each head half
+  attn_bwd_finalize_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(
       dq_acc, p.dk_part, p.dv_part, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, total_tokens, Hq, Hkv,
-      lddq, lddk, lddv);
+      lddq, lddk, lddv, rope_pos, rope_theta > 0.f ? log2f(rope_theta) : 0.f);
   return (int)cudaGetLastError();
 }

@@ -14,6 +14,12 @@ int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long
                      long long ldc, int c_f32, int M, int N, int K, float alpha, float beta, const void* bias,
                      const void* residual, long long ldr, int* status, int block_n, int max_ctas, int splits,
                      cudaStream_t stream);
+int accerl_gemm_glu_bf16(const void* X, long long ldx, const void* W, long long ldw, void* gu, long long ldgu, void* h,
+                         long long ldh, int M, int I, int K, int* status, int block_n, int max_ctas,
+                         cudaStream_t stream);
+int accerl_gemm_dglu_bf16(const void* dY, long long lddy, const void* Wd, long long ldwd, const void* gu,
+                          long long ldgu, void* dgu, long long lddgu, int M, int I, int K, int* status, int block_n,
+                          int max_ctas, cudaStream_t stream);
 int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn, void* C,
                              long long ldc, int c_f32, int M, int N, int K, long long b_rows_total, float beta, int mode,
                              const int* tile_expert, const int* group_row_start, const int* group_rows, int num_groups,
@@ -63,7 +69,7 @@ int accerl_attn_bwd(const void* q, const void* k, const void* v, const void* o, 
                     float* delta, float* dq_acc, void* dq, void* dk, void* dv, const int* cu_seqlens, int num_seqs,
                     int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq, long long ldk, long long ldv,
                     long long ldo, long long lddo, long long lddq, long long lddk, long long lddv, float scale,
-                    int causal, int* status, cudaStream_t s);
+                    int causal, int* status, const long long* rope_pos, float rope_theta, cudaStream_t s);
 int accerl_paged_decode(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
                         const int* seq_lens, void* out, float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv,
                         int max_blocks_per_seq, int block_size, int num_splits, float scale, long long ldq,
@@ -156,6 +162,44 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
                          opt_ptr(bias), opt_ptr(residual), ldr, status_ptr(status), static_cast<int>(block_n),
                          static_cast<int>(max_ctas), static_cast<int>(splits), cur_stream()),
         "gemm");
+}
+
+// h = silu(x Wg^T) * (x Wu^T) for w = [Wg; Wu] ([2I, K]); gu (optional, [M, 2I]) keeps the gate|up outputs.
+void gemm_glu(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& gu, at::Tensor& h,
+              const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(h);
+  const int M = x.size(0), K = x.size(1), I = h.size(1);
+  TORCH_CHECK(w.size(0) == 2 * I && w.size(1) == K, "gemm_glu: weight must be [2I, K]");
+  TORCH_CHECK(h.size(0) == M, "gemm_glu: output rows");
+  if (gu.has_value()) {
+    CHECK_BF16(*gu);
+    TORCH_CHECK(gu->size(0) == M && gu->size(1) == 2 * I, "gemm_glu: gu must be [M, 2I]");
+  }
+  check(accerl_gemm_glu_bf16(x.data_ptr(), ld_of(x), w.data_ptr(), ld_of(w), gu.has_value() ? gu->data_ptr() : nullptr,
+                             gu.has_value() ? ld_of(*gu) : 0, h.data_ptr(), ld_of(h), M, I, K, status_ptr(status),
+                             static_cast<int>(block_n), static_cast<int>(max_ctas), cur_stream()),
+        "gemm_glu");
+}
+
+// dgu = SwiGLU backward of (dy Wd) given gu; dy [M, K], wd [K, I] (the down projection), gu/dgu [M, 2I].
+void gemm_dglu(const at::Tensor& dy, const at::Tensor& wd, const at::Tensor& gu, at::Tensor& dgu,
+               const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas) {
+  CHECK_CUDA(dy);
+  CHECK_BF16(dy);
+  CHECK_BF16(wd);
+  CHECK_BF16(gu);
+  CHECK_BF16(dgu);
+  const int M = dy.size(0), K = dy.size(1), I = wd.size(1);
+  TORCH_CHECK(wd.size(0) == K, "gemm_dglu: down weight must be [K, I]");
+  TORCH_CHECK(gu.size(0) == M && gu.size(1) == 2 * I && dgu.size(0) == M && dgu.size(1) == 2 * I,
+              "gemm_dglu: gu / dgu must be [M, 2I]");
+  check(accerl_gemm_dglu_bf16(dy.data_ptr(), ld_of(dy), wd.data_ptr(), ld_of(wd), gu.data_ptr(), ld_of(gu),
+                              dgu.data_ptr(), ld_of(dgu), M, I, K, status_ptr(status), static_cast<int>(block_n),
+                              static_cast<int>(max_ctas), cur_stream()),
+        "gemm_dglu");
 }
 
 // Grouped expert GEMM. mode 1: a [M, K] (or [K, M] if a_mn), b stacked [E*Nb, K] K-major / [E*Kb, N]
@@ -413,14 +457,19 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
               const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dq,
               at::Tensor& dk, at::Tensor& dv, const at::Tensor& cu_seqlens, int64_t max_seqlen, int64_t Hq, int64_t Hkv,
-              double scale, bool causal, const c10::optional<at::Tensor>& status) {
+              double scale, bool causal, const c10::optional<at::Tensor>& status,
+              const c10::optional<at::Tensor>& rope_pos, double rope_theta) {
   CHECK_F32(delta);
+  if (rope_pos.has_value())
+    TORCH_CHECK(rope_pos->scalar_type() == at::kLong && rope_pos->numel() == q.size(0), "attn_bwd: rope_pos int64 [T]");
   CHECK_F32(dq_acc);
   check(accerl_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(), lse.data_ptr<float>(),
                         delta.data_ptr<float>(), dq_acc.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                         cu_seqlens.data_ptr<int>(), cu_seqlens.numel() - 1, max_seqlen, q.size(0), Hq, Hkv, ld_of(q),
                         ld_of(k), ld_of(v), ld_of(o), ld_of(dout), ld_of(dq), ld_of(dk), ld_of(dv),
-                        static_cast<float>(scale), causal, status_ptr(status), cur_stream()),
+                        static_cast<float>(scale), causal, status_ptr(status),
+                        rope_pos.has_value() ? reinterpret_cast<const long long*>(rope_pos->data_ptr<int64_t>()) : nullptr,
+                        static_cast<float>(rope_theta), cur_stream()),
         "attn_bwd");
 }
 
@@ -526,6 +575,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "accerl_agent_b200 sm_100a kernels";
   m.def("last_error", &last_error, "(code, message) of the most recent launch; resets it");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM");
+  m.def("gemm_glu", &gemm_glu, "gate/up GEMM with the SwiGLU epilogue");
+  m.def("gemm_dglu", &gemm_dglu, "down-projection dgrad GEMM with the SwiGLU backward epilogue");
   m.def("splitk_finish", &splitk_finish);
   m.def("grouped_gemm", &grouped_gemm);
   m.def("row_scatter", &row_scatter);

@@ -204,6 +204,32 @@ ACCERL_DEVINL void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// ---- TMA stores (shared -> global), bulk-group completion ------------------------------------
+ACCERL_DEVINL void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+// element-wise add of the shared tile into global memory (performed at L2)
+ACCERL_DEVINL void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+ACCERL_DEVINL void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+ACCERL_DEVINL void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+ACCERL_DEVINL void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// byte offset of 16-byte chunk j of row r in a 128-byte-row tile with the TMA 128B swizzle
+ACCERL_DEVINL uint32_t swz128(uint32_t r, uint32_t j) { return r * 128u + (((j ^ (r & 7u)) & 7u) << 4); }
+
 // ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) ------------------------------------------
 // The two CTAs of a cluster share one MMA: the even CTA (rank 0) issues tcgen05.mma.cta_group::2,
 // which reads A (M/2 rows) and B (N/2 rows) from the same shared-memory offsets in both CTAs and
@@ -345,6 +371,30 @@ ACCERL_DEVINL uint32_t pack_bf16x2(float lo, float hi) {
 ACCERL_DEVINL float2 unpack_bf16x2(uint32_t v) {
   __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(b);
+}
+
+// SwiGLU on bf16 inputs g (gate) and u (up): h = bf16(silu(g)) * u, and its gradients for an output
+// gradient d (all three already rounded to bf16). Shared by the elementwise kernels and the GEMM
+// epilogues that fuse them, so fused and unfused paths give identical bits.
+ACCERL_DEVINL float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
+ACCERL_DEVINL float swiglu_h(float g, float u) { return bf16_round(g / (1.f + __expf(-g))) * u; }
+ACCERL_DEVINL void swiglu_grads(float g, float u, float d, float& dg, float& du) {
+  const float sig = 1.f / (1.f + __expf(-g));
+  const float act = bf16_round(g * sig);
+  const float dact = sig * (1.f + g * (1.f - sig));
+  dg = d * u * dact;
+  du = d * act;
+}
+
+// Rotary embedding coefficients of frequency i (0 <= i < D/2) at position p: inv_freq = theta^(-2i/D),
+// angle in fp32, cos / sin rounded to bf16 (as the reference module does). Shared by the RoPE kernel
+// and the attention backward's fused inverse rotation, so both give identical bits.
+ACCERL_DEVINL void rope_cos_sin(float p, int i, int D, float log2_theta, float& c, float& s) {
+  const float inv_freq = exp2f(-log2_theta * (2.0f * i) / static_cast<float>(D));
+  float sn, cn;
+  sincosf(p * inv_freq, &sn, &cn);
+  c = __bfloat162float(__float2bfloat16(cn));
+  s = __bfloat162float(__float2bfloat16(sn));
 }
 
 ACCERL_DEVINL float warp_sum(float v) {

@@ -276,11 +276,10 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const long long* __
   const int half = D >> 1;
   const float p = static_cast<float>(pos[t]);
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
-    const float inv_freq = exp2f(-log2_theta * (2.0f * i) / static_cast<float>(D));
-    float s, c;
-    sincosf(p * inv_freq, &s, &c);
-    cs[i] = __bfloat162float(__float2bfloat16(c));
-    cs[half + i] = __bfloat162float(__float2bfloat16(s)) * sign;
+    float c, s;
+    rope_cos_sin(p, i, D, log2_theta, c, s);
+    cs[i] = c;
+    cs[half + i] = s * sign;
   }
   __syncthreads();
   __nv_bfloat16* row = qkv + t * ld;
@@ -301,8 +300,6 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ qkv, const long long* __
 // ------------------------------------------------------------------------------------------------
 // SwiGLU on a fused gate|up row: h = silu(g) * u ; backward gives d(gate|up).
 // ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g)); }
-
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ h, int T, int I) {
   const long long idx = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   const long long total = static_cast<long long>(T) * I;
@@ -318,8 +315,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
   for (int i = 0; i < 4; ++i) {
     const float2 fg = unpack_bf16x2(gw[i]), fu = unpack_bf16x2(uw[i]);
     // act(gate) is rounded to the activation dtype before the product, as in the reference module.
-    const float2 a = unpack_bf16x2(pack_bf16x2(silu_f(fg.x), silu_f(fg.y)));
-    o[i] = pack_bf16x2(a.x * fu.x, a.y * fu.y);
+    o[i] = pack_bf16x2(swiglu_h(fg.x, fu.x), swiglu_h(fg.y, fu.y));
   }
   *reinterpret_cast<uint4*>(h + idx) = make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -343,13 +339,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const __
     float r[2], s2[2];
     const float gg[2] = {fg.x, fg.y}, uu[2] = {fu.x, fu.y}, dd[2] = {fd.x, fd.y};
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const float sig = 1.f / (1.f + __expf(-gg[j]));
-      const float act = __bfloat162float(__float2bfloat16(gg[j] * sig));
-      const float dact = sig * (1.f + gg[j] * (1.f - sig));
-      r[j] = dd[j] * uu[j] * dact;  // d gate
-      s2[j] = dd[j] * act;          // d up
-    }
+    for (int j = 0; j < 2; ++j) swiglu_grads(gg[j], uu[j], dd[j], r[j], s2[j]);  // d gate, d up
     og[i] = pack_bf16x2(r[0], r[1]);
     ou[i] = pack_bf16x2(s2[0], s2[1]);
   }

@@ -66,7 +66,26 @@ struct GemmParams {
   // scatter epilogue: bf16 output row r is stored at address row_dst[r] (0 = drop the row); used to
   // write expert outputs straight into the source rank's buffer over NVLink
   const long long* row_dst;
+  // SwiGLU forward epilogue (glu_I > 0, K-major B = [gate; up] of 2*glu_I rows, BN = 256): work item n
+  // multiplies gate rows [n*128, +128) and up rows [glu_I + n*128, +128); the epilogue stores
+  // h = silu(g) * u into glu_out (and g, u into C when C is set, for the backward)
+  int glu_I;
+  __nv_bfloat16* glu_out;
+  long long ld_glu;
+  // SwiGLU backward epilogue (dglu_gu set): the accumulator is d(h) for columns [0, N) of the SwiGLU;
+  // the epilogue reads g, u from dglu_gu (row stride ld_dglu, up at +N) and stores d(gate) at column
+  // c and d(up) at column N + c of C
+  const __nv_bfloat16* dglu_gu;
+  long long ld_dglu;
+  // epilogue output path: 0 = per-thread stores, 1 = TMA tile stores of C (bf16 or fp32, beta = 0),
+  // 2 = TMA reduce-add of fp32 tiles into C (beta = 1, split-K partials)
+  int tma_store;
 };
+
+// Epilogue staging: per epilogue warp two 32-row x 128-byte tiles (64 bf16 or 32 fp32 columns),
+// written with the 128B swizzle and drained by TMA stores while the next chunk is converted.
+constexpr int kEpiChunkBytes = 32 * 128;
+constexpr int kEpiBytes = 4 * 2 * kEpiChunkBytes;
 
 struct WorkItem {
   int m_blk, n_blk, kb0, kb1, b_n_off, b_k_off;
@@ -134,14 +153,15 @@ __device__ __forceinline__ WorkItem work_item(const GemmParams& p, int t, int k_
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using S = GemmSmem<BN, PAIR>;
   constexpr int TM = PAIR ? 2 * kBM : kBM;  // rows of C per work item
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smA = smem;
   uint8_t* smB = smem + STAGES * S::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint8_t* smEpi = smem + STAGES * S::kStageBytes;  // 1024-byte aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(smEpi + kEpiBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -216,6 +236,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < S::kBRows / 64; ++j)
                 tma_load_2d_pair(b_dst + j * 64 * kBK * 2, &tmB, bar, n0 + 64 * j, k0 + w.b_k_off);
+            } else if (p.glu_I) {
+              // the even CTA stages the gate block, the odd CTA the matching up block
+              tma_load_2d_pair(b_dst, &tmB, bar, k0, (rank ? p.glu_I : 0) + w.n_blk * 128);
             } else {
               tma_load_2d_pair(b_dst, &tmB, bar, k0, n0 + w.b_n_off);
             }
@@ -232,6 +255,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < BN / 64; ++j)
                 tma_load_2d(b_dst + j * 64 * kBK * 2, &tmB, &full[stage], n0 + 64 * j, k0 + w.b_k_off);
+            } else if (p.glu_I) {
+              tma_load_2d(b_dst, &tmB, &full[stage], k0, w.n_blk * 128);
+              tma_load_2d(b_dst + 128 * kBK * 2, &tmB, &full[stage], k0, p.glu_I + w.n_blk * 128);
             } else {
               tma_load_2d(b_dst, &tmB, &full[stage], k0, n0 + w.b_n_off);
             }
@@ -314,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
+    int epi_chunk = 0;
     const uint32_t tempty_even = PAIR ? map_shared_rank(&tempty[0], 0) : 0u;
     for (int t = first_item; t < p.num_tiles; t += item_stride) {
       const WorkItem w = work_item<B_MN>(p, t, k_blocks);
@@ -327,6 +354,120 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row_in_c = m_blk * TM + static_cast<int>(rank) * kBM + row_in_tile;
       const bool row_ok = row_in_c < p.M;
       const long long row = w.c_row_off + row_in_c;
+      const uint32_t t_row = tbase + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+      if (p.tma_store) {
+        // stage 32-row chunks in swizzled shared memory and write them with TMA (full-line, async)
+        uint8_t* wbuf = smEpi + quarter * (2 * kEpiChunkBytes);
+        const int chunk_cols = p.c_f32 ? 32 : 64;
+        const int y0 = static_cast<int>(w.c_row_off) + m_blk * TM + static_cast<int>(rank) * kBM + quarter * 32;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += chunk_cols) {
+          uint8_t* buf = wbuf + (epi_chunk & 1) * kEpiChunkBytes;
+          ++epi_chunk;
+          if (lane == 0) bulk_wait_read<1>();  // the store issued from this buffer two chunks ago
+          __syncwarp();
+          const int col0 = n_blk * BN + c0;
+          if (p.c_f32) {
+            uint32_t v[32];
+            tmem_ld32(t_row + c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float f[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int col = col0 + 4 * j + i;
+                f[i] = __uint_as_float(v[4 * j + i]) * p.alpha;
+                if (p.bias && col < p.N) f[i] += __bfloat162float(p.bias[col]);
+                if (p.residual && row_ok && col < p.N) f[i] += __bfloat162float(p.residual[row * p.ldr + col]);
+              }
+              *reinterpret_cast<float4*>(buf + swz128(lane, j)) = make_float4(f[0], f[1], f[2], f[3]);
+            }
+          } else {
+            uint32_t v[32], v2[32];
+            tmem_ld32(t_row + c0, v);
+            tmem_ld32(t_row + c0 + 32, v2);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int col = col0 + 8 * j;
+              float f[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(j < 4 ? v[8 * j + i] : v2[8 * (j - 4) + i]) * p.alpha;
+              if (col < p.N) {
+                if (p.bias) {
+                  const uint4 b = *reinterpret_cast<const uint4*>(p.bias + col);
+                  const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float2 bb = unpack_bf16x2(bw[i]);
+                    f[2 * i] += bb.x;
+                    f[2 * i + 1] += bb.y;
+                  }
+                }
+                if (p.residual && row_ok) {
+                  const uint4 r = *reinterpret_cast<const uint4*>(p.residual + row * p.ldr + col);
+                  const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float2 rr = unpack_bf16x2(rw[i]);
+                    f[2 * i] += rr.x;
+                    f[2 * i + 1] += rr.y;
+                  }
+                }
+              }
+              *reinterpret_cast<uint4*>(buf + swz128(lane, j)) =
+                  make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                             pack_bf16x2(f[6], f[7]));
+            }
+          }
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            if (p.tma_store == 2) tma_reduce_add_2d(&tmC, buf, col0, y0);
+            else tma_store_2d(&tmC, buf, col0, y0);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        if constexpr (PAIR) mbar_arrive_cluster(tempty_even + acc * 8);
+        else mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      if (BN == 256 && p.glu_I) {
+        // SwiGLU forward: accumulator columns [0,128) are gate, [128,256) the matching up columns
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t vg[32], vu[32];
+          tmem_ld32(t_row + c0, vg);
+          tmem_ld32(t_row + 128 + c0, vu);
+          tmem_wait_ld();
+          if (!row_ok) continue;
+          const int col0 = n_blk * 128 + c0;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint32_t og[4], ou[4], oh[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              og[i] = pack_bf16x2(__uint_as_float(vg[g * 8 + 2 * i]), __uint_as_float(vg[g * 8 + 2 * i + 1]));
+              ou[i] = pack_bf16x2(__uint_as_float(vu[g * 8 + 2 * i]), __uint_as_float(vu[g * 8 + 2 * i + 1]));
+              const float2 fg = unpack_bf16x2(og[i]), fu = unpack_bf16x2(ou[i]);
+              oh[i] = pack_bf16x2(swiglu_h(fg.x, fu.x), swiglu_h(fg.y, fu.y));
+            }
+            if (p.C) {
+              __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0 + g * 8;
+              *reinterpret_cast<uint4*>(c) = make_uint4(og[0], og[1], og[2], og[3]);
+              *reinterpret_cast<uint4*>(c + p.glu_I) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+            }
+            *reinterpret_cast<uint4*>(p.glu_out + row * p.ld_glu + col0 + g * 8) =
+                make_uint4(oh[0], oh[1], oh[2], oh[3]);
+          }
+        }
+        tc_fence_before();
+        if constexpr (PAIR) mbar_arrive_cluster(tempty_even + acc * 8);
+        else mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
@@ -382,6 +523,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             *reinterpret_cast<float4*>(c) = make_float4(f[0], f[1], f[2], f[3]);
             *reinterpret_cast<float4*>(c + 4) = make_float4(f[4], f[5], f[6], f[7]);
+          } else if (p.dglu_gu) {
+            // SwiGLU backward: d(h) -> d(gate) at column col, d(up) at column N + col
+            const __nv_bfloat16* gu = p.dglu_gu + row * p.ld_dglu + col;
+            const uint4 gv = *reinterpret_cast<const uint4*>(gu);
+            const uint4 uv = *reinterpret_cast<const uint4*>(gu + p.N);
+            const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+            uint32_t og[4], ou[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 fg = unpack_bf16x2(gw[i]), fu = unpack_bf16x2(uw[i]);
+              float dg0, du0, dg1, du1;
+              swiglu_grads(fg.x, fu.x, bf16_round(f[2 * i]), dg0, du0);
+              swiglu_grads(fg.y, fu.y, bf16_round(f[2 * i + 1]), dg1, du1);
+              og[i] = pack_bf16x2(dg0, dg1);
+              ou[i] = pack_bf16x2(du0, du1);
+            }
+            __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col;
+            *reinterpret_cast<uint4*>(c) = make_uint4(og[0], og[1], og[2], og[3]);
+            *reinterpret_cast<uint4*>(c + p.N) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
           } else {
             __nv_bfloat16* c;
             if (p.row_dst) {
@@ -414,6 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (PAIR) mbar_arrive_cluster(tempty_even + acc * 8);  // the even CTA's barrier
       else mbar_arrive(&tempty[acc]);
     }
+    if (lane == 0) bulk_wait<0>();  // TMA stores of this warp complete before the CTA exits
   }
 
   if constexpr (PAIR) {
@@ -453,16 +614,17 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 struct MapKey {
   uintptr_t ptr;
   uint64_t d0, d1, stride;
-  uint32_t b0, b1;
+  uint32_t b0, b1, esize;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && stride == o.stride && b0 == o.b0 && b1 == o.b1;
+    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && stride == o.stride && b0 == o.b0 && b1 == o.b1 &&
+           esize == o.esize;
   }
 };
 struct MapKeyHash {
   size_t operator()(const MapKey& k) const {
     size_t h = std::hash<uintptr_t>()(k.ptr);
     h ^= std::hash<uint64_t>()(k.d0 * 1315423911ull + k.d1) + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
-    h ^= std::hash<uint64_t>()(k.stride * 2654435761ull + (uint64_t(k.b0) << 32 | k.b1)) + (h << 6) + (h >> 2);
+    h ^= std::hash<uint64_t>()(k.stride * 2654435761ull + (uint64_t(k.b0) << 32 | k.b1) + k.esize) + (h << 6) + (h >> 2);
     return h;
   }
 };
@@ -470,10 +632,11 @@ struct MapKeyHash {
 std::mutex g_map_mutex;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
 
-// 2-D bf16 tensor map: inner dimension d0 (contiguous), outer d1 with a row stride in elements.
+// 2-D tensor map (bf16, or fp32 with esize 4), 128B swizzle: inner dimension d0 (contiguous), outer d1
+// with a row stride in elements.
 bool make_map_2d(CUtensorMap* out, const void* ptr, uint64_t d0, uint64_t d1, uint64_t stride_elems, uint32_t b0,
-                 uint32_t b1) {
-  MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_elems, b0, b1};
+                 uint32_t b1, uint32_t esize = 2) {
+  MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_elems, b0, b1, esize};
   {
     std::lock_guard<std::mutex> g(g_map_mutex);
     auto it = g_map_cache.find(key);
@@ -485,10 +648,11 @@ bool make_map_2d(CUtensorMap* out, const void* ptr, uint64_t d0, uint64_t d1, ui
   auto fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {d0, d1};
-  cuuint64_t strides[1] = {stride_elems * 2};
+  cuuint64_t strides[1] = {stride_elems * esize};
   cuuint32_t box[2] = {b0, b1};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  CUresult r = fn(out, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
@@ -510,9 +674,12 @@ int num_sms() {
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
-int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p, cudaStream_t stream, int max_ctas) {
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmParams p,
+                cudaStream_t stream, int max_ctas) {
   auto kern = gemm_bf16_tcgen05<BN, STAGES, A_MN, B_MN, PAIR>;
-  constexpr int smem_bytes = STAGES * GemmSmem<BN, PAIR>::kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  constexpr int smem_bytes =
+      STAGES * GemmSmem<BN, PAIR>::kStageBytes + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static_assert(smem_bytes <= 232448, "shared memory per CTA");
   static int max_clusters = -1;  // per instantiation: clusters of 2 that can be resident at once
   if (max_clusters < 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
@@ -540,7 +707,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p, cuda
   }
   if (!PAIR) {
     int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
-    kern<<<grid, kThreads, smem_bytes, stream>>>(ma, mb, p);
+    kern<<<grid, kThreads, smem_bytes, stream>>>(ma, mb, mc, p);
     return static_cast<int>(cudaGetLastError());
   }
   int clusters = std::min(p.num_tiles, max_clusters);
@@ -557,26 +724,48 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p, cuda
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, ma, mb, p));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p));
 }
 
 template <int BN, int STAGES, bool PAIR>
-int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
-                   cudaStream_t s, int max_ctas) {
-  if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, false, false, PAIR>(ma, mb, p, s, max_ctas);
-  if (!a_mn && b_mn) return launch_gemm<BN, STAGES, false, true, PAIR>(ma, mb, p, s, max_ctas);
-  if (a_mn && !b_mn) return launch_gemm<BN, STAGES, true, false, PAIR>(ma, mb, p, s, max_ctas);
-  return launch_gemm<BN, STAGES, true, true, PAIR>(ma, mb, p, s, max_ctas);
+int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                   const GemmParams& p, cudaStream_t s, int max_ctas) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, false, false, PAIR>(ma, mb, mc, p, s, max_ctas);
+  if (!a_mn && b_mn) return launch_gemm<BN, STAGES, false, true, PAIR>(ma, mb, mc, p, s, max_ctas);
+  if (a_mn && !b_mn) return launch_gemm<BN, STAGES, true, false, PAIR>(ma, mb, mc, p, s, max_ctas);
+  return launch_gemm<BN, STAGES, true, true, PAIR>(ma, mb, mc, p, s, max_ctas);
+}
+
+// Output tensor map for the TMA-store epilogue, or 0 when the per-thread store path must be used
+// (scatter rows, bf16 accumulation, the SwiGLU epilogues, beta other than 0 / 1, odd strides).
+int output_map(CUtensorMap* mc, const GemmParams& p, uint64_t rows_total) {
+  if (p.row_dst || p.glu_I || p.dglu_gu || !p.C) return 0;
+  const uint32_t esize = p.c_f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(p.C) & 15) || ((p.ldc * esize) & 15)) return 0;
+  int mode;
+  if (p.c_f32 && (p.beta == 1.f || p.splits > 1)) mode = 2;
+  else if (p.beta == 0.f && p.splits == 1) mode = 1;
+  else return 0;
+  if (!make_map_2d(mc, p.C, (uint64_t)p.N, rows_total, (uint64_t)p.ldc, p.c_f32 ? 32 : 64, 32, esize)) return 0;
+  return mode;
 }
 
 }  // namespace
 }  // namespace accerl
 
-// Returns 0 on success, a cudaError_t value on launch failure, or -1..-9 for argument errors.
-extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
-                                void* C, long long ldc, int c_f32, int M, int N, int K, float alpha, float beta,
-                                const void* bias, const void* residual, long long ldr, int* status, int block_n,
-                                int max_ctas, int splits, cudaStream_t stream) {
+namespace {
+struct EpilogueExtras {
+  int glu_I = 0;
+  void* glu_out = nullptr;
+  long long ld_glu = 0;
+  const void* dglu_gu = nullptr;
+  long long ld_dglu = 0;
+};
+
+int gemm_dense(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn, void* C, long long ldc,
+               int c_f32, int M, int N, int K, float alpha, float beta, const void* bias, const void* residual,
+               long long ldr, int* status, int block_n, int max_ctas, int splits, cudaStream_t stream,
+               const EpilogueExtras& ex) {
   using namespace accerl;
   if (M <= 0 || N <= 0) return 0;
   if (K <= 0) return -1;
@@ -605,6 +794,7 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
     const Opt opts[3] = {{256, false, 2.0}, {128, false, 1.35}, {256, true, 2.0 * kPairCost}};
     for (const Opt& o : opts) {
       if (block_n != 0 && (o.bn != bn || o.pair != pair)) continue;
+      if (ex.glu_I && o.bn != 256) continue;  // a SwiGLU tile is 128 gate + 128 up columns
       if (block_n == 0 && o.bn == 256 && N <= 128) continue;
       if (block_n == 0 && o.pair && !kPairAuto) continue;
       const int tm = o.pair ? 256 : 128;
@@ -633,7 +823,8 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   else ok = make_map_2d(&ma, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 64, 128);
   if (!ok) return -7;
   if (b_mn) ok = make_map_2d(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, 64);
-  else ok = make_map_2d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, (uint32_t)(pair ? bn / 2 : bn));
+  else ok = make_map_2d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64,
+                        (uint32_t)((pair || ex.glu_I) ? bn / 2 : bn));
   if (!ok) return -8;
   GemmParams p;
   p.M = M;
@@ -664,9 +855,58 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
   p.c_group_stride = 0;
   p.num_groups = 0;
   p.row_dst = nullptr;
-  if (pair) return dispatch_major<256, 6, true>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
-  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
-  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, p, stream, max_ctas);
+  p.glu_I = ex.glu_I;
+  p.glu_out = reinterpret_cast<__nv_bfloat16*>(ex.glu_out);
+  p.ld_glu = ex.ld_glu;
+  p.dglu_gu = reinterpret_cast<const __nv_bfloat16*>(ex.dglu_gu);
+  p.ld_dglu = ex.ld_dglu;
+  CUtensorMap mc = ma;
+  p.tma_store = output_map(&mc, p, (uint64_t)M);
+  if (pair) return dispatch_major<256, 6, true>(a_mn, b_mn, ma, mb, mc, p, stream, max_ctas);
+  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, mc, p, stream, max_ctas);
+  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, mc, p, stream, max_ctas);
+}
+}  // namespace
+
+// Returns 0 on success, a cudaError_t value on launch failure, or -1..-9 for argument errors.
+extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                                void* C, long long ldc, int c_f32, int M, int N, int K, float alpha, float beta,
+                                const void* bias, const void* residual, long long ldr, int* status, int block_n,
+                                int max_ctas, int splits, cudaStream_t stream) {
+  return gemm_dense(A, lda, a_mn, B, ldb, b_mn, C, ldc, c_f32, M, N, K, alpha, beta, bias, residual, ldr, status,
+                    block_n, max_ctas, splits, stream, EpilogueExtras{});
+}
+
+// Gate/up projection fused with SwiGLU: for W = [gate; up] ([2I, K], K-major) computes g, u = X W^T
+// and h = silu(g) * u ([M, I], row stride ldh); gu ([M, 2I], row stride ldgu) receives g | u when
+// non-null (training keeps it for the backward). I must be a multiple of 128. -14: bad I.
+extern "C" int accerl_gemm_glu_bf16(const void* X, long long ldx, const void* W, long long ldw, void* gu,
+                                    long long ldgu, void* h, long long ldh, int M, int I, int K, int* status,
+                                    int block_n, int max_ctas, cudaStream_t stream) {
+  if (I <= 0 || I % 128) return -14;
+  if (block_n != 0 && block_n != 256 && block_n != -256) return -14;
+  if ((ldh % 8) || (reinterpret_cast<uintptr_t>(h) & 15)) return -3;
+  EpilogueExtras ex;
+  ex.glu_I = I;
+  ex.glu_out = h;
+  ex.ld_glu = ldh;
+  // C (= gu) may be null: pass a valid dummy pointer/stride for the argument checks
+  return gemm_dense(X, ldx, 0, W, ldw, 0, gu, gu ? ldgu : 8, 0, M, 2 * I, K, 1.f, 0.f, nullptr, nullptr, 0, status,
+                    block_n, max_ctas, 1, stream, ex);
+}
+
+// Down-projection input gradient fused with the SwiGLU backward: dA = dY Wd ([M, I]; dY [M, K],
+// Wd [K, I] row-major) is turned, with g | u from gu ([M, 2I], row stride ldgu), into
+// d(gate) | d(up) in dgu ([M, 2I], row stride lddgu).
+extern "C" int accerl_gemm_dglu_bf16(const void* dY, long long lddy, const void* Wd, long long ldwd, const void* gu,
+                                     long long ldgu, void* dgu, long long lddgu, int M, int I, int K, int* status,
+                                     int block_n, int max_ctas, cudaStream_t stream) {
+  if (I <= 0 || I % 8 || (ldgu % 8) || (reinterpret_cast<uintptr_t>(gu) & 15)) return -14;
+  EpilogueExtras ex;
+  ex.dglu_gu = gu;
+  ex.ld_dglu = ldgu;
+  return gemm_dense(dY, lddy, 0, Wd, ldwd, 1, dgu, lddgu, 0, M, I, K, 1.f, 0.f, nullptr, nullptr, 0, status, block_n,
+                    max_ctas, 1, stream, ex);
 }
 
 // out_bf16[m, n] = bf16(acc[m, n] + bias[n] + residual[m, n]) : finishing pass of a split-K GEMM.
@@ -747,6 +987,11 @@ extern "C" int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, 
   p.kb_per_split = (K + kBK - 1) / kBK;
   p.group_m = 8;
   p.group_mode = mode;
+  p.glu_I = 0;
+  p.glu_out = nullptr;
+  p.ld_glu = 0;
+  p.dglu_gu = nullptr;
+  p.ld_dglu = 0;
   p.tile_expert = tile_expert;
   p.group_row_start = group_row_start;
   p.group_rows = group_rows;
@@ -756,6 +1001,12 @@ extern "C" int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, 
   p.row_dst = row_dst;
   if (row_dst && (c_f32 || beta != 0.f)) return -12;
   p.num_tiles = p.tiles_m * p.tiles_n * (mode == 2 ? num_groups : 1);
-  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, p, stream, 0);
-  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, p, stream, 0);
+  CUtensorMap mc = ma;
+  // a per-expert weight-gradient tile must not spill into the next expert's rows
+  if (mode == 1 || (p.M % kBM) == 0)
+    p.tma_store = output_map(&mc, p, mode == 2 ? (uint64_t)num_groups * (uint64_t)c_group_stride : (uint64_t)M);
+  else
+    p.tma_store = 0;
+  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, mc, p, stream, 0);
+  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, mc, p, stream, 0);
 }

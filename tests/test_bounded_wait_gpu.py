@@ -42,7 +42,7 @@ def test_tp_allreduce_completes_when_peer_flag_arrives(slot):
     flags[0][slot * world + 1] = 1  # the peer's epoch 1, already delivered
     residual = torch.randn(n, device="cuda").to(torch.bfloat16)
     out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
-    status = ops.status_tensor(torch.device("cuda", 0))
+    status = torch.zeros(16, dtype=torch.int32, device="cuda")  # private: the shared word stays clean
     ops.native().tp_allreduce(dp, fp, 0, slot, n, n, residual, out, ctr, status)
     torch.cuda.synchronize()
     assert int(status[0]) == 0
@@ -58,7 +58,7 @@ def test_tp_allreduce_peer_that_never_signals_times_out():
     n = 8192
     bufs, flags, dp, fp, ctr = _fake_group(n)
     out = torch.full((n,), 7.0, dtype=torch.bfloat16, device="cuda")
-    status = ops.status_tensor(torch.device("cuda", 0))
+    status = torch.zeros(16, dtype=torch.int32, device="cuda")  # private: the shared word stays clean
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     ops.native().tp_allreduce(dp, fp, 0, 0, n, n, None, out, ctr, status)

@@ -100,6 +100,42 @@ def test_gemm_cta_pair_epilogues_and_split():
     assert _rel(out3, A.float() @ B.float().t()) < 1e-2
 
 
+@pytest.mark.parametrize("block_n", [256, -256])
+@pytest.mark.parametrize("M,I,K", [(520, 384, 320), (1024, 256, 192)])
+def test_gemm_swiglu_epilogues(block_n, M, I, K):
+    """Gate/up GEMM with the SwiGLU epilogue (single CTA and CTA pair) and the down-projection dgrad
+    with the SwiGLU-backward epilogue, against the fp32 reference and the unfused kernels."""
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    w = (torch.randn(2 * I, K, device=DEV) * 0.1).bfloat16()
+    h = torch.empty(M, I, device=DEV, dtype=torch.bfloat16)
+    gu = torch.empty(M, 2 * I, device=DEV, dtype=torch.bfloat16)
+    st = ops.status_tensor(torch.device(DEV))
+    ops.native().gemm_glu(x, w, gu, h, st, block_n, 0)
+    want_gu = x.float() @ w.float().t()
+    assert _rel(gu, want_gu) < 1e-2
+    assert torch.equal(h, ops.swiglu(gu))  # the epilogue's SwiGLU is the kernel's, bit for bit
+    h2 = torch.empty_like(h)
+    ops.native().gemm_glu(x, w, None, h2, st, block_n, 0)
+    assert torch.equal(h2, h)
+    wd = (torch.randn(K, I, device=DEV) * 0.1).bfloat16()  # down projection [out=K, I]
+    dy = torch.randn(M, K, device=DEV).bfloat16()
+    dgu = torch.empty_like(gu)
+    ops.native().gemm_dglu(dy, wd, gu, dgu, st, block_n, 0)
+    da = ops.gemm(dy, wd, b_mn=True, block_n=block_n)
+    ref = ops.swiglu_backward(da, gu)
+    assert _rel(dgu, ref) < 1e-2
+    g, u = gu.float()[:, :I], gu.float()[:, I:]
+    sig = torch.sigmoid(g)
+    d = (dy.float() @ wd.float())
+    want = torch.cat([d * u * sig * (1 + g * (1 - sig)), d * (g * sig)], 1)
+    assert _rel(dgu, want) < 2e-2
+    assert int(st[0]) == 0
+    # the public wrappers
+    hh, gg = ops.linear_swiglu(x, w, keep_gu=True)
+    assert _rel(gg, want_gu) < 1e-2 and _rel(hh, ops.swiglu(gg)) < 1e-6
+    assert _rel(ops.linear_dgrad_swiglu(dy, wd, gu), ref) < 1e-2
+
+
 def test_gemm_strided_views():
     # q/k/v style column slices of a fused buffer as operands and outputs
     T, H = 384, 256
@@ -268,6 +304,23 @@ def test_attention_backward(lengths, Hq, Hkv):
     assert _rel(dq, qf.grad.reshape(T, -1)) < 3e-2
     assert _rel(dk, kf.grad.reshape(T, -1)) < 3e-2
     assert _rel(dv, vf.grad.reshape(T, -1)) < 3e-2
+
+
+def test_attention_backward_fused_inverse_rope():
+    """The finishing kernel's fused inverse rotation equals the separate RoPE kernel run afterwards."""
+    lengths, Hq, Hkv = [200, 333], 6, 2
+    T, cu, qkv, q, k, v = _varlen_case(lengths, Hq, Hkv)
+    o, lse = ops.attention_varlen(q, k, v, cu, max(lengths), Hq, Hkv, 128)
+    do = torch.randn(T, Hq * 128, device=DEV).bfloat16()
+    pos = torch.cat([torch.arange(n, device=DEV) for n in lengths]).long()
+    dq, dk, dv = ops.attention_varlen_backward(do, q, k, v, o, lse, cu, max(lengths), Hq, Hkv, 128)
+    d = torch.cat([dq, dk, dv], 1)
+    ops.rope_(d, pos, Hq + Hkv, 128, 1e6, inverse=True)
+    fq, fk, fv = ops.attention_varlen_backward(do, q, k, v, o, lse, cu, max(lengths), Hq, Hkv, 128,
+                                               rope_pos=pos, rope_theta=1e6)
+    assert torch.equal(fv, dv)
+    assert _rel(fq, d[:, : Hq * 128]) < 1e-2 and _rel(fk, d[:, Hq * 128 : (Hq + Hkv) * 128]) < 1e-2
+    assert (fq.float() - d[:, : Hq * 128].float()).abs().max() <= 2e-2 * d.float().abs().max()
 
 
 @pytest.mark.parametrize("Hq,Hkv,splits", [(12, 2, 1), (32, 4, 4), (8, 8, 2)])
