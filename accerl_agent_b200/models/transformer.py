@@ -240,8 +240,8 @@ class CausalLM:
             x3, mlp_cache = moe_forward(self, layer, h2, x2, save)
         else:
             if save:
-                # training keeps g|u for the backward; the separate SwiGLU kernel is cheaper here than
-                # the fused epilogue, whose three row-strided outputs slow the short-K GEMM
+                # training keeps g|u for the backward: measured faster as the plain GEMM plus the
+                # SwiGLU kernel (which reads g|u back from L2) than as the three-output fused epilogue
                 gu = ops.linear(h2, self.w(p + "mlp.gate_up_proj.weight"))
                 act = ops.swiglu(gu)
             else:

@@ -229,6 +229,8 @@ ACCERL_DEVINL void bulk_wait() {
 }
 // byte offset of 16-byte chunk j of row r in a 128-byte-row tile with the TMA 128B swizzle
 ACCERL_DEVINL uint32_t swz128(uint32_t r, uint32_t j) { return r * 128u + (((j ^ (r & 7u)) & 7u) << 4); }
+// the same for 64-byte rows and the 64B swizzle (address bits [4,5] ^= bits [7,8])
+ACCERL_DEVINL uint32_t swz64(uint32_t r, uint32_t j) { return r * 64u + (((j ^ (r >> 1)) & 3u) << 4); }
 
 // ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) ------------------------------------------
 // The two CTAs of a cluster share one MMA: the even CTA (rank 0) issues tcgen05.mma.cta_group::2,

@@ -153,7 +153,8 @@ __device__ __forceinline__ WorkItem work_item(const GemmParams& p, int t, int k_
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH,
+                      const GemmParams p) {
   using S = GemmSmem<BN, PAIR>;
   constexpr int TM = PAIR ? 2 * kBM : kBM;  // rows of C per work item
   extern __shared__ uint8_t smem_raw[];
@@ -435,32 +436,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if (BN == 256 && p.glu_I) {
-        // SwiGLU forward: accumulator columns [0,128) are gate, [128,256) the matching up columns
+        // SwiGLU forward: accumulator columns [0,128) are gate, [128,256) the matching up columns.
+        // Per 32-column chunk the warp writes h (and g, u when C is set) as 32 x 32 bf16 tiles through
+        // four 2 KB staging slots (64B swizzle) and TMA stores.
+        uint8_t* wbuf = smEpi + quarter * (2 * kEpiChunkBytes);
+        const int y0 = m_blk * TM + static_cast<int>(rank) * kBM + quarter * 32;
+        const int nout = p.C ? 3 : 1;
 #pragma unroll 1
         for (int c0 = 0; c0 < 128; c0 += 32) {
           uint32_t vg[32], vu[32];
           tmem_ld32(t_row + c0, vg);
           tmem_ld32(t_row + 128 + c0, vu);
           tmem_wait_ld();
-          if (!row_ok) continue;
-          const int col0 = n_blk * 128 + c0;
+          const int x = n_blk * 128 + c0;
+#pragma unroll 1
+          for (int o = 0; o < nout; ++o) {
+            uint8_t* buf = wbuf + (epi_chunk & 3) * 2048;
+            ++epi_chunk;
+            if (lane == 0) bulk_wait_read<3>();  // the store issued from this slot four stores ago
+            __syncwarp();
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint32_t og[4], ou[4], oh[4];
+            for (int j = 0; j < 4; ++j) {
+              uint32_t w4[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              og[i] = pack_bf16x2(__uint_as_float(vg[g * 8 + 2 * i]), __uint_as_float(vg[g * 8 + 2 * i + 1]));
-              ou[i] = pack_bf16x2(__uint_as_float(vu[g * 8 + 2 * i]), __uint_as_float(vu[g * 8 + 2 * i + 1]));
-              const float2 fg = unpack_bf16x2(og[i]), fu = unpack_bf16x2(ou[i]);
-              oh[i] = pack_bf16x2(swiglu_h(fg.x, fu.x), swiglu_h(fg.y, fu.y));
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t g2 = pack_bf16x2(__uint_as_float(vg[8 * j + 2 * i]), __uint_as_float(vg[8 * j + 2 * i + 1]));
+                const uint32_t u2 = pack_bf16x2(__uint_as_float(vu[8 * j + 2 * i]), __uint_as_float(vu[8 * j + 2 * i + 1]));
+                if (o == 0) {
+                  const float2 fg = unpack_bf16x2(g2), fu = unpack_bf16x2(u2);
+                  w4[i] = pack_bf16x2(swiglu_h(fg.x, fu.x), swiglu_h(fg.y, fu.y));
+                } else {
+                  w4[i] = o == 1 ? g2 : u2;
+                }
+              }
+              *reinterpret_cast<uint4*>(buf + swz64(lane, j)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
             }
-            if (p.C) {
-              __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0 + g * 8;
-              *reinterpret_cast<uint4*>(c) = make_uint4(og[0], og[1], og[2], og[3]);
-              *reinterpret_cast<uint4*>(c + p.glu_I) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+              if (o == 0) tma_store_2d(&tmH, buf, x, y0);
+              else tma_store_2d(&tmC, buf, (o == 2 ? p.glu_I : 0) + x, y0);
+              bulk_commit();
             }
-            *reinterpret_cast<uint4*>(p.glu_out + row * p.ld_glu + col0 + g * 8) =
-                make_uint4(oh[0], oh[1], oh[2], oh[3]);
           }
         }
         tc_fence_before();
@@ -635,8 +652,8 @@ std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
 // 2-D tensor map (bf16, or fp32 with esize 4), 128B swizzle: inner dimension d0 (contiguous), outer d1
 // with a row stride in elements.
 bool make_map_2d(CUtensorMap* out, const void* ptr, uint64_t d0, uint64_t d1, uint64_t stride_elems, uint32_t b0,
-                 uint32_t b1, uint32_t esize = 2) {
-  MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_elems, b0, b1, esize};
+                 uint32_t b1, uint32_t esize = 2, bool swizzle64 = false) {
+  MapKey key{reinterpret_cast<uintptr_t>(ptr), d0, d1, stride_elems, b0, b1, esize + (swizzle64 ? 16u : 0u)};
   {
     std::lock_guard<std::mutex> g(g_map_mutex);
     auto it = g_map_cache.find(key);
@@ -653,7 +670,8 @@ bool make_map_2d(CUtensorMap* out, const void* ptr, uint64_t d0, uint64_t d1, ui
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(out, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                   const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   std::lock_guard<std::mutex> g(g_map_mutex);
@@ -674,8 +692,8 @@ int num_sms() {
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
-int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, GemmParams p,
-                cudaStream_t stream, int max_ctas) {
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mh,
+                GemmParams p, cudaStream_t stream, int max_ctas) {
   auto kern = gemm_bf16_tcgen05<BN, STAGES, A_MN, B_MN, PAIR>;
   constexpr int smem_bytes =
       STAGES * GemmSmem<BN, PAIR>::kStageBytes + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
@@ -707,7 +725,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   }
   if (!PAIR) {
     int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());
-    kern<<<grid, kThreads, smem_bytes, stream>>>(ma, mb, mc, p);
+    kern<<<grid, kThreads, smem_bytes, stream>>>(ma, mb, mc, mh, p);
     return static_cast<int>(cudaGetLastError());
   }
   int clusters = std::min(p.num_tiles, max_clusters);
@@ -724,16 +742,16 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mh, p));
 }
 
 template <int BN, int STAGES, bool PAIR>
 int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                   const GemmParams& p, cudaStream_t s, int max_ctas) {
-  if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, false, false, PAIR>(ma, mb, mc, p, s, max_ctas);
-  if (!a_mn && b_mn) return launch_gemm<BN, STAGES, false, true, PAIR>(ma, mb, mc, p, s, max_ctas);
-  if (a_mn && !b_mn) return launch_gemm<BN, STAGES, true, false, PAIR>(ma, mb, mc, p, s, max_ctas);
-  return launch_gemm<BN, STAGES, true, true, PAIR>(ma, mb, mc, p, s, max_ctas);
+                   const CUtensorMap& mh, const GemmParams& p, cudaStream_t s, int max_ctas) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, STAGES, false, false, PAIR>(ma, mb, mc, mh, p, s, max_ctas);
+  if (!a_mn && b_mn) return launch_gemm<BN, STAGES, false, true, PAIR>(ma, mb, mc, mh, p, s, max_ctas);
+  if (a_mn && !b_mn) return launch_gemm<BN, STAGES, true, false, PAIR>(ma, mb, mc, mh, p, s, max_ctas);
+  return launch_gemm<BN, STAGES, true, true, PAIR>(ma, mb, mc, mh, p, s, max_ctas);
 }
 
 // Output tensor map for the TMA-store epilogue, or 0 when the per-thread store path must be used
@@ -860,11 +878,16 @@ int gemm_dense(const void* A, long long lda, int a_mn, const void* B, long long 
   p.ld_glu = ex.ld_glu;
   p.dglu_gu = reinterpret_cast<const __nv_bfloat16*>(ex.dglu_gu);
   p.ld_dglu = ex.ld_dglu;
-  CUtensorMap mc = ma;
+  CUtensorMap mc = ma, mh = ma;
   p.tma_store = output_map(&mc, p, (uint64_t)M);
-  if (pair) return dispatch_major<256, 6, true>(a_mn, b_mn, ma, mb, mc, p, stream, max_ctas);
-  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, mc, p, stream, max_ctas);
-  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, mc, p, stream, max_ctas);
+  if (ex.glu_I) {
+    // the SwiGLU epilogue writes 32 x 32 tiles of h (and of g | u when kept) with TMA
+    if (!make_map_2d(&mh, ex.glu_out, (uint64_t)ex.glu_I, (uint64_t)M, (uint64_t)ex.ld_glu, 32, 32, 2, true)) return -7;
+    if (C && !make_map_2d(&mc, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 32, 32, 2, true)) return -7;
+  }
+  if (pair) return dispatch_major<256, 6, true>(a_mn, b_mn, ma, mb, mc, mh, p, stream, max_ctas);
+  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, mc, mh, p, stream, max_ctas);
+  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, mc, mh, p, stream, max_ctas);
 }
 }  // namespace
 
@@ -1007,6 +1030,6 @@ extern "C" int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, 
     p.tma_store = output_map(&mc, p, mode == 2 ? (uint64_t)num_groups * (uint64_t)c_group_stride : (uint64_t)M);
   else
     p.tma_store = 0;
-  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, mc, p, stream, 0);
-  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, mc, p, stream, 0);
+  if (bn == 256) return dispatch_major<256, 4, false>(a_mn, b_mn, ma, mb, mc, ma, p, stream, 0);
+  return dispatch_major<128, 6, false>(a_mn, b_mn, ma, mb, mc, ma, p, stream, 0);
 }
