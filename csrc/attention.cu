@@ -314,7 +314,7 @@ struct AttnBwdParams {
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const AttnBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const AttnBwdParams p) {
   const int head = blockIdx.x % p.Hq;
   const int kt = static_cast<int>(blockIdx.x / p.Hq);
   const int b = blockIdx.y;
@@ -332,8 +332,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = sK + kTileBytes;
   uint8_t* sQ = sV + kTileBytes;
   uint8_t* sDO = sQ + kTileBytes;
-  uint8_t* sP = sDO + kTileBytes;
-  uint8_t* sDS = sP + kTileBytes;
+  uint8_t* sDQ = sDO + kTileBytes;  // dQ staging: one 32 x 32 fp32 tile (4 KB) per elementwise warp
+  uint8_t* sDS = sDQ + kTileBytes;
   float* s_lse = reinterpret_cast<float*>(sDS + kTileBytes);
   float* s_delta = s_lse + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_delta + 128);
@@ -365,8 +365,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tS = tbase;          // S^T, then dQ
-  const uint32_t tDP = tbase + 128;   // dP^T
+  const uint32_t tS = tbase;          // S^T, then P^T (bf16 pairs: queries 0-63 in cols 0-31, 64-127 in 64-95)
+  const uint32_t tDP = tbase + 128;   // dP^T, then dQ
   const uint32_t tDV = tbase + 256;
   const uint32_t tDK = tbase + 384;
 
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       constexpr uint32_t idesc_kmn = make_idesc_bf16_f32(128, 128, false, true);
       constexpr uint32_t idesc_mnmn = make_idesc_bf16_f32(128, 128, true, true);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ), do_addr = smem_u32(sDO);
-      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      const uint32_t ds_addr = smem_u32(sDS);
       bool ok = mbar_wait(kv_full, 0, p.status, kStatusTimeoutMma);
       for (int i = 0; i < nq && ok; ++i) {
         if (!mbar_wait(q_full, i & 1, p.status, kStatusTimeoutMma)) break;
@@ -408,15 +408,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(s_full);
         if (!mbar_wait(ps_full, i & 1, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
+        // dV += P^T dO with P^T read from TMEM (the elementwise warps wrote it over S^T)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tDV, desc_kmajor(p_addr, kk), desc_mnmajor(do_addr, kk), idesc_kmn, (i > 0) || (kk > 0));
+          umma_bf16_ts(tDV, tS + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8), desc_mnmajor(do_addr, kk), idesc_kmn,
+                       (i > 0) || (kk > 0));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_bf16(tDK, desc_kmajor(ds_addr, kk), desc_mnmajor(q_addr, kk), idesc_kmn, (i > 0) || (kk > 0));
+        // dQ = dS K into the dP^T columns (read out by the elementwise warps before the next dP^T)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_bf16(tS, desc_mnmajor(ds_addr, kk), desc_mnmajor(k_addr, kk), idesc_mnmn, kk > 0);
+          umma_bf16(tDP, desc_mnmajor(ds_addr, kk), desc_mnmajor(k_addr, kk), idesc_mnmn, kk > 0);
         umma_commit(dq_full);
         umma_commit(q_empty);
       }
@@ -462,7 +465,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int c = 2 * half; c < 2 * half + 2; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * half + cc;
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c * 32 + lane_off, sv);
         tmem_ld32(tDP + c * 32 + lane_off, dv);
@@ -486,10 +490,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const uint32_t off = swz_offset(r, c * 4 + u);
-          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pw[4 * u], pw[4 * u + 1], pw[4 * u + 2], pw[4 * u + 3]);
           *reinterpret_cast<uint4*>(sDS + off) = make_uint4(dw[4 * u], dw[4 * u + 1], dw[4 * u + 2], dw[4 * u + 3]);
         }
+        // P^T as bf16 pairs into columns [64*half + 16*cc, +16): S^T of this warp's first chunk, already read
+        tmem_st16(tS + half * 64 + cc * 16 + lane_off, pw);
       }
+      tmem_wait_st();
       fence_async_shared();
       tc_fence_before();
       mbar_arrive(ps_full);
@@ -498,31 +504,38 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         break;
       }
       tc_fence_after();
-      const int q_pos = qt * kTile + r;
-      float* dqrow = p.dq_acc + static_cast<long long>(seq_start + q_pos) * ldacc + head * kHd;
       {
-        const int c = 2 * half;
+        // dQ rows of this warp (32 queries) x its 64 columns, added into dq_acc by two TMA reduce-adds
+        // of 32 x 32 fp32 tiles staged in shared memory. Rows past the sequence carry zeros (their P and
+        // dS are zero), so the tile may overlap the next sequence; rows past T are clipped by TMA.
+        uint8_t* buf = sDQ + warp * 4096;
+        const int y = seq_start + qt * kTile + quad * 32;
         uint32_t v[32], v2[32];
-        tmem_ld32(tS + c * 32 + lane_off, v);
-        tmem_ld32(tS + (c + 1) * 32 + lane_off, v2);
+        tmem_ld32(tDP + half * 64 + lane_off, v);
+        tmem_ld32(tDP + half * 64 + 32 + lane_off, v2);
         tmem_wait_ld();
-        if (q_pos < len) {
+        tc_fence_before();
+        mbar_arrive(dq_free);  // the accumulator is in registers: the next dP^T may overwrite it
 #pragma unroll
-          for (int g = 0; g < 8; ++g)
-            red_add_v4(dqrow + (c + 1) * 32 + g * 4, __uint_as_float(v2[g * 4]), __uint_as_float(v2[g * 4 + 1]),
-                       __uint_as_float(v2[g * 4 + 2]), __uint_as_float(v2[g * 4 + 3]));
-        }
-        if (q_pos < len) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const uint32_t* src = cc ? v2 : v;
+          if (lane == 0) bulk_wait_read<0>();  // this warp's previous tile has left the buffer
+          __syncwarp();
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            red_add_v4(dqrow + c * 32 + g * 4, __uint_as_float(v[g * 4]), __uint_as_float(v[g * 4 + 1]),
-                       __uint_as_float(v[g * 4 + 2]), __uint_as_float(v[g * 4 + 3]));
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(buf + swz128(lane, j)) =
+                make_float4(__uint_as_float(src[4 * j]), __uint_as_float(src[4 * j + 1]),
+                            __uint_as_float(src[4 * j + 2]), __uint_as_float(src[4 * j + 3]));
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(&tmDQ, buf, head * kHd + half * 64 + cc * 32, y);
+            bulk_commit();
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(dq_free);
     }
+    if (lane == 0) bulk_wait<0>();  // dQ reductions complete before the CTA exits
     if (ok && mbar_wait(acc_done, 0, p.status, kStatusTimeoutEpilogue)) {
       tc_fence_after();
       const long long rowoff = static_cast<long long>(seq_start + k_pos) * ldacc + head * kHd;
@@ -669,6 +682,19 @@ bool attn_map(CUtensorMap* m, const void* ptr, int T, int width, long long ld) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 [T, width] map with 32 x 32 boxes (128-byte rows, 128B swizzle) for the dQ reduce-adds
+bool attn_map_f32(CUtensorMap* m, const float* ptr, int T, int width) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(width) * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 constexpr int kFwdSmem = 5 * kTileBytes + 1024 + 256;
 constexpr int kBwdSmem = 6 * kTileBytes + 1024 + 1024 + 256;
 
@@ -738,6 +764,8 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
   const long long acc_elems = (long long)total_tokens * Hq * kHd;
   // dq_acc holds [dq | dk_part | dv_part] contiguously (3 * acc_elems floats); only dq needs zeros.
   cudaMemsetAsync(dq_acc, 0, acc_elems * sizeof(float), s);
+  CUtensorMap mdq;
+  if (!attn_map_f32(&mdq, dq_acc, total_tokens, Hq * kHd)) return -3;
   AttnBwdParams p;
   p.lse = lse;
   p.delta = delta;
@@ -754,7 +782,7 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
   p.causal = causal;
   p.status = status;
   dim3 grid(p.max_tiles * Hq, num_seqs);
-  attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, p);
+  attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mdq, p);
   const long long n8 = acc_elems / 8;  // one thread per 4 dims of each head half
   attn_bwd_finalize_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(
       dq_acc, p.dk_part, p.dv_part, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, total_tokens, Hq, Hkv,
