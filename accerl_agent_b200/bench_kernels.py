@@ -221,8 +221,8 @@ def profile_case(kind: str):
         tables = torch.arange(nb, device=dev, dtype=torch.int32).view(B, L // bs)
         lens = torch.full((B,), L, device=dev, dtype=torch.int32)
         q = torch.randn(B, Hq * D, device=dev).bfloat16()
-        for _ in range(2):
-            ops.paged_decode(q, kc, vc, tables, lens, Hq, Hkv, 1.0 / D ** 0.5, num_splits=4)
+        for impl in (1, 2):  # the CUDA-core and the tensor-core kernels
+            ops.paged_decode(q, kc, vc, tables, lens, Hq, Hkv, 1.0 / D ** 0.5, num_splits=4, impl=impl)
         knew = torch.randn(B, Hkv * D, device=dev).bfloat16()
         slots = (torch.arange(B, device=dev, dtype=torch.int32) * (L // bs)) * bs
         ops.kv_cache_write(knew, knew, kc, vc, slots, Hkv)
@@ -233,6 +233,34 @@ def profile_case(kind: str):
         ops.sample(logits, temp, seeds, offs)
     torch.cuda.synchronize()
     ops.check_status(torch.device("cuda"))
+
+
+def bench_decode(results):
+    """Paged decode attention of the 1.5B shape (12 q / 2 kv heads): 256 sequences of 1024 and 4096
+    cached tokens; achieved GB/s over the K/V bytes read, for the CUDA-core and tensor-core kernels."""
+    D, bs = 128, 16
+    _, peak_gbs = _peaks()
+    # (12, 2): the 1.5B shape, KV heads interleaved in each cached token row; (8, 1): one KV head, so
+    # every page of a head is one contiguous 4 KB run
+    for B, L, Hq, Hkv in ((256, 1024, 12, 2), (256, 4096, 12, 2), (256, 4096, 8, 1)):
+        nb = B * L // bs
+        kc = torch.randn(nb, bs, Hkv, D, device="cuda").bfloat16()
+        vc = torch.randn(nb, bs, Hkv, D, device="cuda").bfloat16()
+        tables = torch.randperm(nb, device="cuda").to(torch.int32).view(B, L // bs)
+        lens = torch.full((B,), L, device="cuda", dtype=torch.int32)
+        q = torch.randn(B, Hq * D, device="cuda").bfloat16()
+        nbytes = 2 * B * L * Hkv * D * 2
+        entry = {"bytes": nbytes}
+        for tag, impl in (("cuda_core", 1), ("tensor_core", 2)):
+            for splits in (1, 4):
+                t = median_ms(lambda: ops.paged_decode(q, kc, vc, tables, lens, Hq, Hkv, 1.0 / D ** 0.5,
+                                                       num_splits=splits, impl=impl))
+                entry[f"{tag}_s{splits}_ms"] = t
+                entry[f"{tag}_s{splits}_gbs"] = nbytes / t / 1e6
+                entry[f"{tag}_s{splits}_frac"] = nbytes / t / 1e6 / peak_gbs
+        results[f"decode/{B}x{L}/hq{Hq}_hkv{Hkv}"] = entry
+        del kc, vc
+        torch.cuda.empty_cache()
 
 
 PROFILE_CASES = ("attnprof", "gemmprof", "moeprof", "opsprof", "decodeprof")
@@ -260,6 +288,8 @@ def main():
         bench_attention(results)
     if "mem" in sel:
         bench_memory_bound(results)
+    if "decode" in sel:
+        bench_decode(results)
     for k, v in results.items():
         if isinstance(v, dict) and "tflops" in v:
             v["frac_of_measured_peak"] = v["tflops"] / peak_tf

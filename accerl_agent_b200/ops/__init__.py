@@ -499,8 +499,11 @@ def adamw_step(master, m, v, grad, param_bf16, sumsq, lr, beta1, beta2, eps, wei
 # ------------------------------------------------------------------------------------------------
 # rollout
 # ------------------------------------------------------------------------------------------------
-def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads, scale, num_splits=1, out=None):
-    """q: [S, Hq*D] -> [S, Hq*D]."""
+def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads, scale, num_splits=1, out=None,
+                 impl: int = 0):
+    """q: [S, Hq*D] -> [S, Hq*D]. ``impl``: 0 = the tensor-core kernel where the shape allows it (head dim
+    128, at most 32 query heads per KV head, pages dividing 128 tokens), 1 = the CUDA-core kernel,
+    2 = the tensor-core kernel only."""
     S = q.shape[0]
     D = k_cache.shape[-1]
     if q.is_cuda:
@@ -508,7 +511,7 @@ def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads
         part_o = workspace(q.device, "decode_o", S * n_heads * num_splits * D)
         part_ml = workspace(q.device, "decode_ml", S * n_heads * num_splits * 2)
         native().paged_decode(q, k_cache, v_cache, block_table, seq_lens, o, part_o, part_ml, n_heads, n_kv_heads,
-                              num_splits, scale)
+                              num_splits, scale, impl, status_tensor(q.device))
         return o
     res = reference.paged_decode(q.reshape(S, n_heads, D), k_cache, v_cache, block_table, seq_lens, scale)
     res = res.reshape(S, n_heads * D)

@@ -44,6 +44,16 @@ ACCERL_DEVINL uint32_t swz_offset(int r, int u) {
   return (u >> 3) * kChunk + r * 128 + (((u & 7) ^ (r & 7)) << 4);
 }
 
+// Max of a 128-value row with eight independent comparison chains.
+ACCERL_DEVINL float row_max128(const float (&x)[128]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = x[i];
+#pragma unroll
+  for (int e = 8; e < 128; ++e) m[e & 7] = fmaxf(m[e & 7], x[e]);
+  return fmaxf(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])), fmaxf(fmaxf(m[4], m[5]), fmaxf(m[6], m[7])));
+}
+
 struct AttnFwdParams {
   __nv_bfloat16* o;
   float* lse;
@@ -208,9 +218,7 @@ __global__ void __launch_bounds__(192, 1)
           if ((p.causal && kp > lim) || kp >= len_k) x[e] = -INFINITY;
         }
       }
-      float mx = x[0];
-#pragma unroll
-      for (int e = 1; e < 128; ++e) mx = fmaxf(mx, x[e]);
+      const float mx = row_max128(x);
       const float m_new = fmaxf(m_used, mx);
       const bool need = m_new > m_used + 8.0f;
       float alpha = 1.f;
@@ -241,6 +249,7 @@ __global__ void __launch_bounds__(192, 1)
       const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
       // P (bf16, two per 32-bit column) back into the first 64 columns of this tile's S buffer: the
       // PV MMA reads it as its TMEM A operand
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums (no 128-long add chain)
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t w[32];
@@ -248,11 +257,12 @@ __global__ void __launch_bounds__(192, 1)
         for (int u = 0; u < 32; ++u) {
           const float p0 = exp2f(x[half * 64 + 2 * u] - m_eff);
           const float p1 = exp2f(x[half * 64 + 2 * u + 1] - m_eff);
-          l += p0 + p1;
+          ls[u & 3] += p0 + p1;
           w[u] = pack_bf16x2(p0, p1);
         }
         tmem_st32(tS + bsel * 128 + half * 32 + lane_off, w);
       }
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -283,6 +293,346 @@ __global__ void __launch_bounds__(192, 1)
         const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
         p.lse[static_cast<long long>(head) * p.T + seq_start + q_pos] = (m_eff + log2f(l)) * kLn2;
       }
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// paged decode on the tensor cores
+// ------------------------------------------------------------------------------------------------
+// One work item = (sequence, KV head, key split). The G query heads that share the KV head are the
+// M rows of the MMAs (rows G..127 of Q are zero), so S = Q K^T and O += P V run as 128 x 128 x 128
+// tcgen05 MMAs over 128-token key tiles whose pages TMA gathers from the paged cache (one box per
+// page). The kernel is persistent: each CTA walks work items with a continuous 2-stage K/V ring, and
+// writes the unnormalised partial output, the running max (natural log units) and the sum of each
+// item for the split-merge kernel. Warp 0 builds Q and runs the softmax of the G rows; warp 4 loads;
+// warp 5 issues the MMAs and owns TMEM.
+constexpr int kDecStages = 3;  // K/V ring depth of the decode kernel (Q + 3 x (K, V) = 224 KB)
+
+struct DecodeTcParams {
+  const __nv_bfloat16* q;
+  long long ldq;
+  const int* block_table;
+  int max_blocks;
+  const int* seq_lens;
+  int num_seqs, Hq, Hkv, G, block_size, num_splits;
+  float scale_log2;
+  float* part_o;
+  float* part_ml;
+  int* status;
+};
+
+struct DecodeItem {
+  int s, kvh, split, t0, t1, ntiles;
+};
+
+ACCERL_DEVINL DecodeItem decode_item(const DecodeTcParams& p, int it) {
+  DecodeItem d;
+  d.split = it % p.num_splits;
+  d.kvh = (it / p.num_splits) % p.Hkv;
+  d.s = it / (p.num_splits * p.Hkv);
+  const int len = p.seq_lens[d.s];
+  // splits are whole 128-token tiles so every tile starts on a page boundary
+  const int per = ((((len + p.num_splits - 1) / p.num_splits) + kTile - 1) / kTile) * kTile;
+  d.t0 = d.split * per;
+  d.t1 = min(len, d.t0 + per);
+  d.ntiles = d.t1 > d.t0 ? (d.t1 - d.t0 + kTile - 1) / kTile : 0;
+  return d;
+}
+
+__global__ void __launch_bounds__(192, 1)
+    paged_decode_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                           const DecodeTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + kDecStages * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kDecStages * kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;                    // [kDecStages]
+  uint64_t* v_full = k_full + kDecStages;         // [kDecStages]
+  uint64_t* kv_empty = v_full + kDecStages;       // [kDecStages]
+  uint64_t* s_full = kv_empty + kDecStages;       // [2] (TMEM score buffers)
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 1;  // after every PV
+  uint64_t* o_item = p_full + 2;  // after the last PV of an item
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_full + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_items = p.num_seqs * p.Hkv * p.num_splits;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 32);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);
+    mbar_init(p_full, 32);
+    mbar_init(o_done, 1);
+    mbar_init(o_item, 1);
+    fence_mbar_init();
+  }
+  // rows G..127 of Q stay zero for the whole kernel
+  if (warp < 4)
+    for (int i = threadIdx.x; i < kTileBytes / 16; i += 128) reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
+  fence_async_shared();
+  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t tS = tbase;        // two score buffers: columns [0,128) and [128,256)
+  const uint32_t tO = tbase + 256;  // output accumulator: columns [256,384)
+
+  if (warp == 4) {
+    // ---------------- TMA producer: one box per page of the tile ----------------
+    // Lane i looks up page i's block id (independent loads, issued before the stage wait so their
+    // latency overlaps it); lane 0 then issues the page boxes from a shared-memory copy of the ids.
+    __shared__ int s_blk[kTile / 8];
+    const int bs = p.block_size;
+    const int pages = kTile / bs;
+    int g = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < num_items && ok; it += gridDim.x) {
+      const DecodeItem d = decode_item(p, it);
+      const int* table = p.block_table + static_cast<long long>(d.s) * p.max_blocks;
+      for (int j = 0; j < d.ntiles; ++j, ++g) {
+        int blk = 0;
+        if (lane < pages) {
+          const int tok = d.t0 + j * kTile + lane * bs;
+          blk = tok < d.t1 ? table[tok / bs] : 0;  // pages past the end: any valid block, masked
+        }
+        const int st = g % kDecStages;
+        int good = 1;
+        if (lane == 0)
+          good = mbar_wait(&kv_empty[st], ((g / kDecStages) & 1) ^ 1u, p.status, kStatusTimeoutProducer) ? 1 : 0;
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
+        if (lane < pages) s_blk[lane] = blk;
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+          for (int pg = 0; pg < pages; ++pg) {
+            const int b = s_blk[pg] * bs;
+            uint8_t* dst = sK + st * kTileBytes + pg * bs * 128;
+            tma_load_2d(dst, &tmK, &k_full[st], d.kvh * kHd, b);
+            tma_load_2d(dst + kChunk, &tmK, &k_full[st], d.kvh * kHd + 64, b);
+          }
+          mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+          for (int pg = 0; pg < pages; ++pg) {
+            const int b = s_blk[pg] * bs;
+            uint8_t* dst = sV + st * kTileBytes + pg * bs * 128;
+            tma_load_2d(dst, &tmV, &v_full[st], d.kvh * kHd, b);
+            tma_load_2d(dst + kChunk, &tmV, &v_full[st], d.kvh * kHd + 64, b);
+          }
+        }
+        __syncwarp();  // s_blk is rewritten next tile
+      }
+    }
+    if (lane == 0) {
+      // never leave a bulk copy in flight into shared memory of a finished CTA
+      for (int t = max(0, g - kDecStages); t < g; ++t)
+        mbar_wait(&v_full[t % kDecStages], (t / kDecStages) & 1, nullptr, 0, 20000000ull);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, 128, false, true);
+      const uint32_t q_addr = smem_u32(sQ);
+      int g = 0, itn = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < num_items && ok; it += gridDim.x) {
+        const DecodeItem d = decode_item(p, it);
+        if (d.ntiles == 0) continue;
+        if (!mbar_wait(q_full, itn & 1, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        for (int j = 0; j <= d.ntiles; ++j) {
+          if (j < d.ntiles) {
+            const int gg = g + j;
+            const int st = gg % kDecStages;
+            const int sb = gg & 1;  // TMEM score buffer
+            if (!mbar_wait(&k_full[st], (gg / kDecStages) & 1, p.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            // score buffer sb held P of tile gg-2, whose PV was issued before this MMA (issue order)
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16(tS + sb * 128, desc_kmajor(q_addr, kk), desc_kmajor(k_addr, kk), idesc_s, kk > 0);
+            umma_commit(&s_full[sb]);
+            if (j == d.ntiles - 1) umma_commit(q_empty);
+          }
+          if (j >= 1) {
+            const int gg = g + j - 1;
+            const int st2 = gg % kDecStages;
+            const int sb2 = gg & 1;
+            if (!mbar_wait(p_full, gg & 1, p.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(&v_full[st2], (gg / kDecStages) & 1, p.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sV + st2 * kTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16_ts(tO, tS + sb2 * 128 + kk * 8, desc_mnmajor(v_addr, kk), idesc_o, (j > 1) || (kk > 0));
+            umma_commit(o_done);
+            umma_commit(&kv_empty[st2]);
+          }
+        }
+        if (!ok) break;
+        umma_commit(o_item);
+        g += d.ntiles;
+        ++itn;
+      }
+    }
+  } else if (warp == 0) {
+    // ---------------- Q rows and the softmax of the G real rows: thread = query head ----------------
+    const int r = lane;
+    int g = 0, itn = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < num_items && ok; it += gridDim.x) {
+      const DecodeItem d = decode_item(p, it);
+      const int hq = d.kvh * p.G + r;
+      const long long pidx = (static_cast<long long>(d.s) * p.Hq + hq) * p.num_splits + d.split;
+      if (d.ntiles == 0) {
+        if (r < p.G) {
+          for (int c = 0; c < kHd; c += 4)
+            *reinterpret_cast<float4*>(p.part_o + pidx * kHd + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+          p.part_ml[pidx * 2] = -INFINITY;
+          p.part_ml[pidx * 2 + 1] = 0.f;
+        }
+        continue;
+      }
+      if (itn > 0 && !mbar_wait(q_empty, (itn - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      if (r < p.G) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.q + static_cast<long long>(d.s) * p.ldq + hq * kHd);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) *reinterpret_cast<uint4*>(sQ + swz_offset(r, u)) = src[u];
+      }
+      fence_async_shared();
+      mbar_arrive(q_full);
+      const uint32_t lane_off = 0;  // warp 0 reads TMEM lanes 0..31
+      float m_used = -INFINITY, l = 0.f;
+      for (int j = 0; j < d.ntiles; ++j) {
+        const int gg = g + j;
+        const int bsel = gg & 1;
+        if (!mbar_wait(&s_full[bsel], (gg >> 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float x[128];
+        {
+          uint32_t v[4][32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld32(tS + bsel * 128 + c * 32 + lane_off, v[c]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) x[c * 32 + e] = __uint_as_float(v[c][e]) * p.scale_log2;
+        }
+        const int kbase = d.t0 + j * kTile;
+        if (kbase + kTile > d.t1) {
+#pragma unroll
+          for (int e = 0; e < 128; ++e)
+            if (kbase + e >= d.t1) x[e] = -INFINITY;
+        }
+        const float mx = row_max128(x);
+        const float m_new = fmaxf(m_used, mx);
+        const bool need = m_new > m_used + 8.0f;
+        float alpha = 1.f;
+        if (need) {
+          alpha = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
+          m_used = m_new;
+          l *= alpha;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // rescale O once the previous PV has landed (o_done is at most one completion behind)
+          if (!mbar_wait(o_done, (gg - 1) & 1, p.status, kStatusTimeoutEpilogue)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t v[32];
+            tmem_ld32(tO + c * 32 + lane_off, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * alpha);
+            tmem_st32(tO + c * 32 + lane_off, v);
+          }
+          tmem_wait_st();
+        }
+        const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t w[32];
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            const float p0 = exp2f(x[half * 64 + 2 * u] - m_eff);
+            const float p1 = exp2f(x[half * 64 + 2 * u + 1] - m_eff);
+            ls[u & 3] += p0 + p1;
+            w[u] = pack_bf16x2(p0, p1);
+          }
+          tmem_st32(tS + bsel * 128 + half * 32 + lane_off, w);
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      if (!mbar_wait(o_item, itn & 1, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tO + c * 32 + lane_off, v);
+        tmem_wait_ld();
+        if (r < p.G) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(p.part_o + pidx * kHd + c * 32 + e) =
+                make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
+                            __uint_as_float(v[e + 3]));
+        }
+      }
+      if (r < p.G) {
+        p.part_ml[pidx * 2] = m_used == -INFINITY ? -INFINITY : m_used * kLn2;
+        p.part_ml[pidx * 2 + 1] = l;
+      }
+      tc_fence_before();
+      g += d.ntiles;
+      ++itn;
     }
   }
   __syncthreads();
@@ -583,25 +933,49 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 }
 
 // dq (bf16, strided) from the fp32 accumulator; dk/dv from per-q-head partials summed over the GQA group.
+// Store 4 dims of each half of a head (d and d + 64) as bf16, rotated by the inverse RoPE when asked
+// (inputs rounded to bf16 first, as the separate RoPE kernel sees them).
+ACCERL_DEVINL void store_rotated(float4 lo, float4 hi, const float (&c)[4], const float (&sn)[4], bool rotate,
+                                 __nv_bfloat16* dst) {
+  const float a[4] = {lo.x, lo.y, lo.z, lo.w}, b[4] = {hi.x, hi.y, hi.z, hi.w};
+  float x[4], y[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (rotate) {
+      const float a16 = __bfloat162float(__float2bfloat16(a[i])), b16 = __bfloat162float(__float2bfloat16(b[i]));
+      x[i] = a16 * c[i] - b16 * sn[i];
+      y[i] = b16 * c[i] + a16 * sn[i];
+    } else {
+      x[i] = a[i];
+      y[i] = b[i];
+    }
+  }
+  uint2 o1, o2;
+  o1.x = pack_bf16x2(x[0], x[1]);
+  o1.y = pack_bf16x2(x[2], x[3]);
+  o2.x = pack_bf16x2(y[0], y[1]);
+  o2.y = pack_bf16x2(y[2], y[3]);
+  *reinterpret_cast<uint2*>(dst) = o1;
+  *reinterpret_cast<uint2*>(dst + kHd / 2) = o2;
+}
+
 // dq / dk / dv to bf16 (dk, dv summed over the query heads of each KV group), optionally with the
-// inverse rotary rotation of dq and dk fused in (pos != nullptr). One thread per (token, head, 4 of
-// the first 64 head dims): it also handles the 4 matching dims of the second half (d + 64), the
-// pair that the rotate-half convention mixes.
+// inverse rotary rotation of dq and dk fused in (pos != nullptr). One thread per (token, 4 of the
+// first 64 head dims): it computes the rotation coefficients once and walks every head, handling
+// the 4 matching dims of the second half (d + 64), the pair that the rotate-half convention mixes.
 __global__ void attn_bwd_finalize_kernel(const float* __restrict__ dq_acc, const float* __restrict__ dk_part,
                                          const float* __restrict__ dv_part, __nv_bfloat16* __restrict__ dq,
                                          __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int T, int Hq,
                                          int Hkv, long long lddq, long long lddk, long long lddv,
                                          const long long* __restrict__ pos, float log2_theta) {
   constexpr int kHalf = kHd / 2;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // over T*Hq*kHalf/4
-  const long long per_t = static_cast<long long>(Hq) * kHalf / 4;
-  if (idx >= static_cast<long long>(T) * per_t) return;
-  const int t = static_cast<int>(idx / per_t);
-  const int r = static_cast<int>(idx % per_t);
-  const int h = r / (kHalf / 4);
-  const int d = (r % (kHalf / 4)) * 4;  // 0..60
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // over T * kHalf/4
+  if (idx >= static_cast<long long>(T) * (kHalf / 4)) return;
+  const int t = static_cast<int>(idx / (kHalf / 4));
+  const int d = static_cast<int>(idx % (kHalf / 4)) * 4;  // 0..60
   float c[4] = {1.f, 1.f, 1.f, 1.f}, sn[4] = {0.f, 0.f, 0.f, 0.f};
-  if (pos) {
+  const bool rot = pos != nullptr;
+  if (rot) {
     const float p = static_cast<float>(pos[t]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -609,49 +983,29 @@ __global__ void attn_bwd_finalize_kernel(const float* __restrict__ dq_acc, const
       sn[i] = -sn[i];  // inverse rotation
     }
   }
-  auto store_rot = [&](float4 lo, float4 hi, __nv_bfloat16* dst, bool rotate) {
-    float a[4] = {lo.x, lo.y, lo.z, lo.w}, b[4] = {hi.x, hi.y, hi.z, hi.w};
-    float x[4], y[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (rotate) {
-        // bf16 inputs, as the separate RoPE kernel sees them
-        const float a16 = __bfloat162float(__float2bfloat16(a[i])), b16 = __bfloat162float(__float2bfloat16(b[i]));
-        x[i] = a16 * c[i] - b16 * sn[i];
-        y[i] = b16 * c[i] + a16 * sn[i];
-      } else {
-        x[i] = a[i];
-        y[i] = b[i];
-      }
-    }
-    uint2 o1, o2;
-    o1.x = pack_bf16x2(x[0], x[1]);
-    o1.y = pack_bf16x2(x[2], x[3]);
-    o2.x = pack_bf16x2(y[0], y[1]);
-    o2.y = pack_bf16x2(y[2], y[3]);
-    *reinterpret_cast<uint2*>(dst + d) = o1;
-    *reinterpret_cast<uint2*>(dst + d + kHalf) = o2;
-  };
-  const long long qoff = static_cast<long long>(t) * Hq * kHd + h * kHd + d;
-  store_rot(*reinterpret_cast<const float4*>(dq_acc + qoff), *reinterpret_cast<const float4*>(dq_acc + qoff + kHalf),
-            dq + t * lddq + h * kHd, pos != nullptr);
+  const long long row = static_cast<long long>(t) * Hq * kHd;
   const int group = Hq / Hkv;
-  if (h % group != 0) return;  // the first head of each group writes the group sum
-  const int kvh = h / group;
-  float4 k0 = make_float4(0, 0, 0, 0), k1 = k0, v0 = k0, v1 = k0;
-  for (int g = 0; g < group; ++g) {
-    const long long off = static_cast<long long>(t) * Hq * kHd + (h + g) * kHd + d;
-    const float4 a0 = *reinterpret_cast<const float4*>(dk_part + off);
-    const float4 a1 = *reinterpret_cast<const float4*>(dk_part + off + kHalf);
-    const float4 b0 = *reinterpret_cast<const float4*>(dv_part + off);
-    const float4 b1 = *reinterpret_cast<const float4*>(dv_part + off + kHalf);
-    k0.x += a0.x; k0.y += a0.y; k0.z += a0.z; k0.w += a0.w;
-    k1.x += a1.x; k1.y += a1.y; k1.z += a1.z; k1.w += a1.w;
-    v0.x += b0.x; v0.y += b0.y; v0.z += b0.z; v0.w += b0.w;
-    v1.x += b1.x; v1.y += b1.y; v1.z += b1.z; v1.w += b1.w;
+  for (int h = 0; h < Hq; ++h) {
+    const float4 lo = *reinterpret_cast<const float4*>(dq_acc + row + h * kHd + d);
+    const float4 hi = *reinterpret_cast<const float4*>(dq_acc + row + h * kHd + d + kHalf);
+    store_rotated(lo, hi, c, sn, rot, dq + t * lddq + h * kHd + d);
   }
-  store_rot(k0, k1, dk + t * lddk + kvh * kHd, pos != nullptr);
-  store_rot(v0, v1, dv + t * lddv + kvh * kHd, false);
+  for (int kvh = 0; kvh < Hkv; ++kvh) {
+    float4 k0 = make_float4(0, 0, 0, 0), k1 = k0, v0 = k0, v1 = k0;
+    for (int g = 0; g < group; ++g) {
+      const long long off = row + (kvh * group + g) * kHd + d;
+      const float4 a0 = *reinterpret_cast<const float4*>(dk_part + off);
+      const float4 a1 = *reinterpret_cast<const float4*>(dk_part + off + kHalf);
+      const float4 b0 = *reinterpret_cast<const float4*>(dv_part + off);
+      const float4 b1 = *reinterpret_cast<const float4*>(dv_part + off + kHalf);
+      k0.x += a0.x; k0.y += a0.y; k0.z += a0.z; k0.w += a0.w;
+      k1.x += a1.x; k1.y += a1.y; k1.z += a1.z; k1.w += a1.w;
+      v0.x += b0.x; v0.y += b0.y; v0.z += b0.z; v0.w += b0.w;
+      v1.x += b1.x; v1.y += b1.y; v1.z += b1.z; v1.w += b1.w;
+    }
+    store_rotated(k0, k1, c, sn, rot, dk + t * lddk + kvh * kHd + d);
+    store_rotated(v0, v1, c, sn, false, dv + t * lddv + kvh * kHd + d);
+  }
 }
 
 namespace {
@@ -783,9 +1137,66 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
   p.status = status;
   dim3 grid(p.max_tiles * Hq, num_seqs);
   attn_bwd_kernel<<<grid, kBwdThreads, kBwdSmem, s>>>(mq, mk, mv, mdo, mdq, p);
-  const long long n8 = acc_elems / 8;  // one thread per 4 dims of each head half
-  attn_bwd_finalize_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(
+  const long long nthr = (long long)total_tokens * (kHd / 8);  // one thread per (token, 4 dims of a half)
+  attn_bwd_finalize_kernel<<<(unsigned)((nthr + 255) / 256), 256, 0, s>>>(
       dq_acc, p.dk_part, p.dv_part, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, total_tokens, Hq, Hkv,
       lddq, lddk, lddv, rope_pos, rope_theta > 0.f ? log2f(rope_theta) : 0.f);
+  return (int)cudaGetLastError();
+}
+
+// Tensor-core paged decode (see paged_decode_tc_kernel). k_cache / v_cache: [num_blocks, block_size,
+// Hkv, 128] bf16 of one layer. Writes the per-split partials that accerl_paged_decode_merge combines.
+// Returns -2 when the shape is not supported by this kernel (the caller uses the CUDA-core kernel).
+extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* k_cache, const void* v_cache,
+                                      int num_blocks, const int* block_table, int max_blocks, const int* seq_lens,
+                                      float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv, int block_size,
+                                      int num_splits, float scale, int* status, cudaStream_t s) {
+  if (num_seqs == 0) return 0;
+  if (Hq % Hkv) return -1;
+  const int G = Hq / Hkv;
+  if (G > 32 || block_size < 8 || block_size > kTile || kTile % block_size || (ldq & 7)) return -2;
+  auto fn = encode_fn();
+  if (!fn) return -3;
+  CUtensorMap mk, mv;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(Hkv) * kHd, static_cast<cuuint64_t>(num_blocks) * block_size};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(Hkv) * kHd * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(block_size)};
+  cuuint32_t es[2] = {1, 1};
+  if (fn(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(k_cache), dims, strides, box, es,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+      fn(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(v_cache), dims, strides, box, es,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return -3;
+  constexpr int smem = (1 + 2 * kDecStages) * kTileBytes + 1024 + 256;
+  static_assert(smem <= 232448, "shared memory per CTA");
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  DecodeTcParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p.ldq = ldq;
+  p.block_table = block_table;
+  p.max_blocks = max_blocks;
+  p.seq_lens = seq_lens;
+  p.num_seqs = num_seqs;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.G = G;
+  p.block_size = block_size;
+  p.num_splits = num_splits;
+  p.scale_log2 = scale * kLog2e;
+  p.part_o = part_o;
+  p.part_ml = part_ml;
+  p.status = status;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int items = num_seqs * Hkv * num_splits;
+  paged_decode_tc_kernel<<<std::min(items, sms), 192, smem, s>>>(mk, mv, p);
   return (int)cudaGetLastError();
 }

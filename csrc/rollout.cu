@@ -330,6 +330,15 @@ extern "C" int accerl_paged_decode(const void* q, const void* k_cache, const voi
   return (int)cudaGetLastError();
 }
 
+// Combine the per-split partials of a paged decode into out ([num_seqs, Hq*128] bf16, row stride ldo).
+extern "C" int accerl_paged_decode_merge(const float* part_o, const float* part_ml, void* out, long long ldo,
+                                         int num_seqs, int Hq, int num_splits, cudaStream_t s) {
+  if (num_seqs == 0) return 0;
+  paged_decode_merge_kernel<<<dim3(num_seqs, Hq), kDHead, 0, s>>>(part_o, part_ml, (__nv_bfloat16*)out, ldo, Hq,
+                                                                  num_splits);
+  return (int)cudaGetLastError();
+}
+
 extern "C" int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping,
                                      int T, int Hkv, long long ldk, long long ldv, cudaStream_t s) {
   if (T == 0) return 0;

@@ -323,11 +323,14 @@ def test_attention_backward_fused_inverse_rope():
     assert (fq.float() - d[:, : Hq * 128].float()).abs().max() <= 2e-2 * d.float().abs().max()
 
 
-@pytest.mark.parametrize("Hq,Hkv,splits", [(12, 2, 1), (32, 4, 4), (8, 8, 2)])
-def test_paged_decode_and_cache_write(Hq, Hkv, splits):
+@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("Hq,Hkv,splits", [(12, 2, 1), (32, 4, 4), (8, 8, 2), (16, 2, 3)])
+def test_paged_decode_and_cache_write(Hq, Hkv, splits, impl):
+    """Both decode kernels (CUDA cores, and tensor cores with TMA page gathers) against the fp32
+    reference, with lengths that leave empty splits and partial 128-token tiles."""
     S, bs, D = 5, 16, 128
-    lens = torch.tensor([1, 17, 64, 100, 33], dtype=torch.int32, device=DEV)
-    max_blocks = 8
+    lens = torch.tensor([1, 17, 300, 100, 129], dtype=torch.int32, device=DEV)
+    max_blocks = 20
     nb = S * max_blocks
     kc = torch.zeros(nb, bs, Hkv, D, device=DEV, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)
@@ -344,9 +347,10 @@ def test_paged_decode_and_cache_write(Hq, Hkv, splits):
         blocks = table[s, t // bs].long()
         assert torch.equal(kc[blocks, t % bs].reshape(n, -1), kk)
     q = torch.randn(S, Hq * D, device=DEV).bfloat16()
-    out = ops.paged_decode(q, kc, vc, table, lens, Hq, Hkv, 1 / math.sqrt(D), num_splits=splits)
+    out = ops.paged_decode(q, kc, vc, table, lens, Hq, Hkv, 1 / math.sqrt(D), num_splits=splits, impl=impl)
     want = ref.paged_decode(q.reshape(S, Hq, D), kc, vc, table, lens, 1 / math.sqrt(D))
     assert _rel(out, want.reshape(S, -1)) < 2e-2
+    assert int(ops.status_tensor(torch.device(DEV))[0]) == 0
 
 
 def test_sampler_greedy_and_distribution():
