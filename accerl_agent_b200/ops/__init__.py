@@ -308,21 +308,38 @@ def attention_varlen(
     causal: bool = True,
     out: Optional[torch.Tensor] = None,
     cu_seqlens_k: Optional[torch.Tensor] = None,
+    block_table: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """q: [T, Hq*D] (may be a strided view), k/v: [Tk, Hkv*D]. Returns (o [T, Hq*D], lse [Hq, T]).
 
     ``cu_seqlens_k`` (default: ``cu_seqlens``) lets every sequence have more keys than queries; the
-    queries are then the last ones of the sequence (causal mask aligned to the end of the keys)."""
+    queries are then the last ones of the sequence (causal mask aligned to the end of the keys).
+    With ``block_table`` ([num_seqs, max_blocks] int32) k and v are a layer's paged caches
+    ([num_blocks, block_size, Hkv, D]) and sequence b's keys are the first ``len_k`` positions of
+    its pages (read in place, no gather)."""
     scale = reference.default_scale(head_dim) if scale is None else scale
     T = q.shape[0]
     if q.is_cuda:
         if head_dim != 128:
             raise ValueError("the native attention kernel supports head_dim 128")
+        if block_table is not None and cu_seqlens_k is None:
+            raise ValueError("paged keys need cu_seqlens_k")
         o = out if out is not None else torch.empty(T, n_heads * head_dim, dtype=q.dtype, device=q.device)
         lse = torch.empty(n_heads, T, dtype=torch.float32, device=q.device)
         native().attn_fwd(q, k, v, o, lse, cu_seqlens, cu_seqlens_k, max_seqlen, n_heads, n_kv_heads, scale, causal,
-                          status_tensor(q.device))
+                          status_tensor(q.device), block_table)
         return o, lse
+    if block_table is not None:
+        # gather the pages into contiguous keys for the reference path
+        bs = k.shape[1]
+        lens = (cu_seqlens_k[1:] - cu_seqlens_k[:-1]).tolist()
+        rows = []
+        for b, n in enumerate(lens):
+            pk = torch.arange(n, device=k.device)
+            rows.append(block_table[b, pk // bs].long() * bs + pk % bs)
+        idx = torch.cat(rows) if rows else torch.zeros(0, dtype=torch.long, device=k.device)
+        k = k.reshape(-1, n_kv_heads * head_dim).index_select(0, idx)
+        v = v.reshape(-1, n_kv_heads * head_dim).index_select(0, idx)
     if cu_seqlens_k is not None:
         o, lse = reference.attention_varlen_qk(
             q.reshape(T, n_heads, head_dim), k.reshape(-1, n_kv_heads, head_dim), v.reshape(-1, n_kv_heads, head_dim),

@@ -151,6 +151,10 @@ class GenerationEngine:
         self.max_num_batched_tokens = max_num_batched_tokens
         self.max_model_len = max_model_len or cfg.max_position_embeddings
         self.block_size = block_size
+        # prefill attention reads keys from the paged cache in place (tensor-core kernel, head dim 128,
+        # pages that divide its 128-token tiles); otherwise the context keys are gathered by slot
+        self._paged_prefill = (device.type == "cuda" and cfg.head_dim == 128 and 8 <= block_size <= 128
+                               and 128 % block_size == 0)
         self.tokenizer = tokenizer
         self.layout = layout or ParamLayout.build(cfg, "full")
         self._weight_src = None
@@ -850,8 +854,9 @@ class GenerationEngine:
                 cu_q.append(cu_q[-1] + n)
                 ctx = start + n
                 cu_k.append(cu_k[-1] + ctx)
-                pk = np.arange(ctx, dtype=np.int64)
-                ks_l.append(blocks[pk // bs] * bs + pk % bs)
+                if not self._paged_prefill:  # the CPU path gathers the context keys by slot
+                    pk = np.arange(ctx, dtype=np.int64)
+                    ks_l.append(blocks[pk // bs] * bs + pk % bs)
                 max_q = max(max_q, n)
         empty = np.zeros(0, np.int64)
         ids = np.concatenate(ids_l) if ids_l else empty
@@ -874,6 +879,13 @@ class GenerationEngine:
                 table[j, : len(sq.blocks)] = sq.blocks
                 lens[j] = start + n
             meta["table"], meta["lens"] = table, lens
+        if n_prefill and self._paged_prefill:
+            # prefill attention reads its keys from the pages in place: one block-table row per chunk
+            pre = order[:n_prefill]
+            ptable = np.zeros((n_prefill, max(len(s.blocks) for s, *_ in pre)), np.int32)
+            for j, (sq, *_rest) in enumerate(pre):
+                ptable[j, : len(sq.blocks)] = sq.blocks
+            meta["ptable"] = ptable
         sampled = [e for e in order if e[3]]
         meta["temps"] = np.asarray([float(sq.params.temperature) for sq, *_ in sampled], np.float32)
         meta["seeds"] = np.asarray([sq.seed for sq, *_ in sampled], np.int64)
@@ -895,6 +907,9 @@ class GenerationEngine:
         parts = [meta["flat"]]
         if nd:
             parts += [meta["table"].reshape(-1).astype(np.int64), meta["lens"].astype(np.int64)]
+        ptable = meta.get("ptable")
+        if ptable is not None:
+            parts.append(ptable.reshape(-1).astype(np.int64))
         tail = np.empty(3 * ns, dtype=np.int64)
         tail[:ns] = meta["seeds"]
         tail[ns : 2 * ns] = meta["offs"]
@@ -919,6 +934,10 @@ class GenerationEngine:
             table_d = rest[: nd * max_blocks].view(nd, max_blocks).to(torch.int32)
             lens_d = rest[nd * max_blocks : nd * max_blocks + nd].to(torch.int32)
             rest = rest[nd * max_blocks + nd :]
+        ptable_d = None
+        if ptable is not None:
+            ptable_d = rest[: ptable.size].view(ptable.shape).to(torch.int32)
+            rest = rest[ptable.size :]
         seeds_d = rest[:ns]
         offs_d = rest[ns : 2 * ns]
         temps_d = rest[2 * ns :].view(torch.float32)[:ns]
@@ -929,7 +948,10 @@ class GenerationEngine:
 
         def attn_fn(layer, q, kc, vc):
             attn = torch.empty(q.shape[0], cfg.q_dim, dtype=q.dtype, device=dev)
-            if Tp:
+            if Tp and ptable_d is not None:
+                ops.attention_varlen(q[:Tp], kc, vc, cu_q_d, max_q, Hq, Hkv, D, scale=scale, out=attn[:Tp],
+                                     cu_seqlens_k=cu_k_d, block_table=ptable_d)
+            elif Tp:
                 kctx = kc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
                 vctx = vc.view(-1, cfg.kv_dim).index_select(0, kslots_d)
                 ops.attention_varlen(q[:Tp], kctx, vctx, cu_q_d, max_q, Hq, Hkv, D, scale=scale,

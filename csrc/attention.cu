@@ -64,6 +64,10 @@ struct AttnFwdParams {
   float scale_log2;
   int causal;
   int* status;
+  // paged keys (prefill over a paged KV cache): key position kp of sequence b lives in cache row
+  // block_table[b * max_blocks + kp / block_size] * block_size + kp % block_size; null = contiguous
+  const int* block_table;
+  int max_blocks, block_size;
 };
 
 __global__ void __launch_bounds__(192, 1)
@@ -124,7 +128,53 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tS = tbase;         // two score buffers: columns [0,128) and [128,256)
   const uint32_t tO = tbase + 256;   // output accumulator: columns [256,384)
 
-  if (warp == 4) {
+  if (warp == 4 && p.block_table) {
+    // ---- paged keys: one TMA box per page; lane i looks up page i's block id in parallel ----
+    __shared__ int s_blk[kTile / 8];
+    const int bs = p.block_size;
+    const int pages = kTile / bs;
+    const int* table = p.block_table + static_cast<long long>(b) * p.max_blocks;
+    if (lane == 0) {
+      const int qy = seq_start + q_tile * kTile;
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_2d(sQ, &tmQ, q_full, head * kHd, qy);
+      tma_load_2d(sQ + kChunk, &tmQ, q_full, head * kHd + 64, qy);
+    }
+    bool ok = true;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int s = j & 1;
+      int blk = 0;
+      if (lane < pages) {
+        const int kp = j * kTile + lane * bs;
+        blk = kp < len_k ? table[kp / bs] : 0;  // pages past the keys: any valid block, masked
+      }
+      int good = 1;
+      if (lane == 0) good = mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1u, p.status, kStatusTimeoutProducer) ? 1 : 0;
+      good = __shfl_sync(0xffffffffu, good, 0);
+      if (!good) {
+        ok = false;
+        break;
+      }
+      if (lane < pages) s_blk[lane] = blk;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        for (int pg = 0; pg < pages; ++pg) {
+          uint8_t* dst = sK + s * kTileBytes + pg * bs * 128;
+          tma_load_2d(dst, &tmK, &k_full[s], kvh * kHd, s_blk[pg] * bs);
+          tma_load_2d(dst + kChunk, &tmK, &k_full[s], kvh * kHd + 64, s_blk[pg] * bs);
+        }
+        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        for (int pg = 0; pg < pages; ++pg) {
+          uint8_t* dst = sV + s * kTileBytes + pg * bs * 128;
+          tma_load_2d(dst, &tmV, &v_full[s], kvh * kHd, s_blk[pg] * bs);
+          tma_load_2d(dst + kChunk, &tmV, &v_full[s], kvh * kHd + 64, s_blk[pg] * bs);
+        }
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0) mbar_wait(q_full, 0, nullptr, 0, 20000000ull);
+  } else if (warp == 4) {
     if (lane == 0) {
       const int qy = seq_start + q_tile * kTile;
       mbar_arrive_expect_tx(q_full, kTileBytes);
@@ -1024,6 +1074,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Tile map over a [T, width] bf16 matrix with a 64-column x 128-row box, 128B swizzle.
+// bf16 [T, width] map whose boxes are `rows` high (one page of a paged KV cache)
+bool attn_map_rows(CUtensorMap* m, const void* ptr, int T, int width, long long ld, int rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(T)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(rows)};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool attn_map(CUtensorMap* m, const void* ptr, int T, int width, long long ld) {
   auto fn = encode_fn();
   if (!fn) return false;
@@ -1057,17 +1120,27 @@ constexpr int kBwdSmem = 6 * kTileBytes + 1024 + 1024 + 256;
 
 using namespace accerl;
 
+// Paged keys: pass block_table ([num_seqs, max_blocks] int32) with k / v the layer's caches
+// ([num_blocks, block_size, Hkv, 128], total_k = num_blocks * block_size rows); cu_seqlens_k then gives
+// each sequence's key count (its keys are positions 0..len_k-1 of its pages).
 extern "C" int accerl_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_seqlens,
                                const int* cu_seqlens_k, int num_seqs, int max_seqlen, int total_tokens, int total_k,
                                int Hq, int Hkv, long long ldq, long long ldk, long long ldv, long long ldo, float scale,
-                               int causal, int* status, cudaStream_t s) {
+                               int causal, int* status, const int* block_table, int max_blocks, int block_size,
+                               cudaStream_t s) {
   if (num_seqs <= 0 || total_tokens <= 0) return 0;
   if (Hq % Hkv) return -1;
   if ((ldq | ldk | ldv | ldo) & 7) return -2;
+  if (block_table && (block_size < 8 || block_size > kTile || kTile % block_size || !cu_seqlens_k)) return -4;
   CUtensorMap mq, mk, mv;
-  if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq) || !attn_map(&mk, k, total_k, Hkv * kHd, ldk) ||
-      !attn_map(&mv, v, total_k, Hkv * kHd, ldv))
+  if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq)) return -3;
+  if (block_table) {
+    if (!attn_map_rows(&mk, k, total_k, Hkv * kHd, ldk, block_size) ||
+        !attn_map_rows(&mv, v, total_k, Hkv * kHd, ldv, block_size))
+      return -3;
+  } else if (!attn_map(&mk, k, total_k, Hkv * kHd, ldk) || !attn_map(&mv, v, total_k, Hkv * kHd, ldv)) {
     return -3;
+  }
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
@@ -1087,6 +1160,9 @@ extern "C" int accerl_attn_fwd(const void* q, const void* k, const void* v, void
   p.scale_log2 = scale * kLog2e;
   p.causal = causal;
   p.status = status;
+  p.block_table = block_table;
+  p.max_blocks = max_blocks;
+  p.block_size = block_size;
   dim3 grid(p.max_tiles * Hq, num_seqs);
   attn_fwd_kernel<<<grid, 192, kFwdSmem, s>>>(mq, mk, mv, p);
   return (int)cudaGetLastError();

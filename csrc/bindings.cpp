@@ -64,7 +64,7 @@ int accerl_adamw(float* master, float* m, float* v, float* grad, void* param, lo
 int accerl_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, const int* cu_seqlens,
                     const int* cu_seqlens_k, int num_seqs, int max_seqlen, int total_tokens, int total_k, int Hq,
                     int Hkv, long long ldq, long long ldk, long long ldv, long long ldo, float scale, int causal,
-                    int* status, cudaStream_t s);
+                    int* status, const int* block_table, int max_blocks, int block_size, cudaStream_t s);
 int accerl_attn_bwd(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
                     float* delta, float* dq_acc, void* dq, void* dk, void* dv, const int* cu_seqlens, int num_seqs,
                     int max_seqlen, int total_tokens, int Hq, int Hkv, long long ldq, long long ldk, long long ldv,
@@ -445,7 +445,8 @@ void adamw(at::Tensor& master, at::Tensor& m, at::Tensor& v, at::Tensor& grad, a
 // q: [T, Hq*D] view (row stride ldq), k/v: [T, Hkv*D], o: [T, Hq*D]; lse: [Hq, T] fp32
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
               const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& cu_seqlens_k, int64_t max_seqlen,
-              int64_t Hq, int64_t Hkv, double scale, bool causal, const c10::optional<at::Tensor>& status) {
+              int64_t Hq, int64_t Hkv, double scale, bool causal, const c10::optional<at::Tensor>& status,
+              const c10::optional<at::Tensor>& block_table) {
   CHECK_BF16(q);
   CHECK_BF16(k);
   CHECK_BF16(v);
@@ -453,10 +454,22 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   CHECK_F32(lse);
   CHECK_I32(cu_seqlens);
   const int* cuk = cu_seqlens_k.has_value() ? cu_seqlens_k->data_ptr<int>() : nullptr;
+  if (block_table.has_value()) {
+    // k / v: the layer's paged caches [num_blocks, block_size, Hkv, 128]
+    CHECK_I32(*block_table);
+    TORCH_CHECK(k.dim() == 4 && k.is_contiguous() && v.is_contiguous(), "attn_fwd: paged caches must be contiguous");
+    check(accerl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
+                          cu_seqlens.data_ptr<int>(), cuk, cu_seqlens.numel() - 1, max_seqlen, q.size(0),
+                          k.size(0) * k.size(1), Hq, Hkv, ld_of(q), Hkv * 128, Hkv * 128, ld_of(o),
+                          static_cast<float>(scale), causal, status_ptr(status), block_table->data_ptr<int>(),
+                          block_table->size(1), k.size(1), cur_stream()),
+          "attn_fwd");
+    return;
+  }
   check(accerl_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
                         cu_seqlens.data_ptr<int>(), cuk, cu_seqlens.numel() - 1, max_seqlen, q.size(0), k.size(0), Hq,
                         Hkv, ld_of(q), ld_of(k), ld_of(v), ld_of(o), static_cast<float>(scale), causal,
-                        status_ptr(status), cur_stream()),
+                        status_ptr(status), nullptr, 0, 0, cur_stream()),
         "attn_fwd");
 }
 

@@ -306,6 +306,37 @@ def test_attention_backward(lengths, Hq, Hkv):
     assert _rel(dv, vf.grad.reshape(T, -1)) < 3e-2
 
 
+def test_attention_forward_paged_keys():
+    """Prefill queries over keys read in place from a paged cache (one TMA box per page) equal the
+    same attention over the keys gathered into contiguous rows."""
+    Hq, Hkv, D, bs = 6, 2, 128, 16
+    q_lens, k_lens = [37, 130, 1], [300, 130, 515]
+    nb = 96
+    kc = torch.randn(nb, bs, Hkv, D, device=DEV).bfloat16()
+    vc = torch.randn(nb, bs, Hkv, D, device=DEV).bfloat16()
+    perm = torch.randperm(nb, device=DEV).to(torch.int32)
+    max_blocks = max((n + bs - 1) // bs for n in k_lens)
+    table = torch.zeros(len(k_lens), max_blocks, dtype=torch.int32, device=DEV)
+    used = 0
+    rows = []
+    for b, n in enumerate(k_lens):
+        nblk = (n + bs - 1) // bs
+        table[b, :nblk] = perm[used : used + nblk]
+        used += nblk
+        pk = torch.arange(n, device=DEV)
+        rows.append(table[b, pk // bs].long() * bs + pk % bs)
+    idx = torch.cat(rows)
+    kctx = kc.view(-1, Hkv * D).index_select(0, idx)
+    vctx = vc.view(-1, Hkv * D).index_select(0, idx)
+    cu_q = torch.tensor([0] + list(torch.tensor(q_lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    cu_k = torch.tensor([0] + list(torch.tensor(k_lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    q = torch.randn(sum(q_lens), Hq * D, device=DEV).bfloat16()
+    want, lse_w = ops.attention_varlen(q, kctx, vctx, cu_q, max(q_lens), Hq, Hkv, D, cu_seqlens_k=cu_k)
+    got, lse_g = ops.attention_varlen(q, kc, vc, cu_q, max(q_lens), Hq, Hkv, D, cu_seqlens_k=cu_k, block_table=table)
+    assert torch.equal(got, want)
+    assert torch.allclose(lse_g, lse_w)
+
+
 def test_attention_backward_fused_inverse_rope():
     """The finishing kernel's fused inverse rotation equals the separate RoPE kernel run afterwards."""
     lengths, Hq, Hkv = [200, 333], 6, 2
