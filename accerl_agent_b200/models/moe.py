@@ -18,14 +18,34 @@ import torch
 from .. import ops
 
 
-def route(model, layer: int, h: torch.Tensor):
+def route(model, layer: int, h: torch.Tensor, counts: bool = False):
+    """Router probabilities, top-k weights and expert ids (and, with ``counts``, rows per expert).
+
+    On the GPU the logits come from the tcgen05 GEMM (fp32 out, rounded to bf16 as the reference's
+    bf16 linear gives them) and one fused kernel does softmax, top-k, renormalisation and the
+    per-expert counts (``moe_router_kernel``, HF ``Qwen2MoeTopKRouter``)."""
     cfg = model.cfg
     p = f"model.layers.{layer}.mlp."
-    logits = (h @ model.w(p + "gate.weight").t()).float()
+    Wg = model.w(p + "gate.weight")
+    E, k = cfg.num_experts, cfg.num_experts_per_tok
+    if h.is_cuda and h.dtype == torch.bfloat16 and E <= 128 and k <= 8 and h.shape[0] > 0:
+        T = h.shape[0]
+        ld = (E + 3) // 4 * 4
+        logits = ops.workspace(h.device, "router_logits", T * ld).view(T, ld)[:, :E]
+        ops.gemm(h, Wg, logits, out_dtype=torch.float32)
+        probs = torch.empty(T, E, dtype=torch.float32, device=h.device)
+        topw = torch.empty(T, k, dtype=torch.float32, device=h.device)
+        topi = torch.empty(T, k, dtype=torch.long, device=h.device)
+        cnt = torch.zeros(E, dtype=torch.int32, device=h.device)
+        ops.native().moe_router(logits, E, k, bool(cfg.norm_topk_prob), probs, topw, topi, cnt)
+        return (probs, topw, topi, cnt) if counts else (probs, topw, topi)
+    logits = (h @ Wg.t()).float()
     probs = torch.softmax(logits, dim=-1)
-    topw, topi = probs.topk(cfg.num_experts_per_tok, dim=-1)
+    topw, topi = probs.topk(k, dim=-1)
     if cfg.norm_topk_prob:
         topw = topw / topw.sum(-1, keepdim=True)
+    if counts:
+        return probs, topw, topi, torch.bincount(topi.reshape(-1), minlength=E).to(torch.int32)
     return probs, topw, topi
 
 

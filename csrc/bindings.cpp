@@ -34,6 +34,8 @@ int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w,
                            const void* residual, const void* shared, const float* sg, void* out, cudaStream_t s);
 int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* pos, const float* w, long long T, int k,
                            int H, void* dys, float* dw, cudaStream_t s);
+int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs,
+                      float* topw, long long* topi, int* counts, cudaStream_t s);
 int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
                        const void* src, void* dst, cudaStream_t s);
 int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
@@ -253,6 +255,19 @@ void tp_allreduce(const at::Tensor& peer_data, const at::Tensor& peer_flags, int
                             slot_elems, n, residual.has_value() ? residual->data_ptr() : nullptr, out.data_ptr(),
                             ctr.data_ptr<int>(), status.data_ptr<int>(), cur_stream()),
         "tp_allreduce");
+}
+
+// Router: logits fp32 [T, >=E] -> probs [T, E], topw [T, k], topi int64 [T, k]; counts int32 [E] += rows.
+void moe_router(const at::Tensor& logits, int64_t E, int64_t k, bool norm_topk, at::Tensor& probs, at::Tensor& topw,
+                at::Tensor& topi, at::Tensor& counts) {
+  CHECK_F32(logits);
+  CHECK_F32(probs);
+  CHECK_F32(topw);
+  TORCH_CHECK(topi.scalar_type() == at::kLong && counts.scalar_type() == at::kInt, "moe_router: topi int64, counts int32");
+  check(accerl_moe_router(logits.data_ptr<float>(), ld_of(logits), logits.size(0), E, k, norm_topk,
+                          probs.data_ptr<float>(), topw.data_ptr<float>(),
+                          reinterpret_cast<long long*>(topi.data_ptr<int64_t>()), counts.data_ptr<int>(), cur_stream()),
+        "moe_router");
 }
 
 void moe_combine_fwd(const at::Tensor& ys, const at::Tensor& pos, const at::Tensor& w, int64_t k,
@@ -617,6 +632,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &grouped_gemm);
   m.def("row_scatter", &row_scatter);
   m.def("weight_pull", &weight_pull);
+  m.def("moe_router", &moe_router);
   m.def("moe_combine_fwd", &moe_combine_fwd);
   m.def("moe_combine_bwd", &moe_combine_bwd);
   m.def("tp_allreduce", &tp_allreduce);

@@ -787,8 +787,12 @@ int gemm_dense(const void* A, long long lda, int a_mn, const void* B, long long 
   using namespace accerl;
   if (M <= 0 || N <= 0) return 0;
   if (K <= 0) return -1;
-  // TMA needs 16-byte row strides; the vectorised epilogue needs N % 8 == 0. K and M are free.
-  if ((N % 8) != 0 || (ldc % 8) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -2;
+  // TMA needs 16-byte row strides; the per-thread epilogue needs N % 8 == 0 (the TMA-store epilogue
+  // clips columns, so an fp32 output without bias / residual / accumulation may have any N). K and M
+  // are free.
+  const bool ragged_n_ok = c_f32 && !bias && !residual && beta == 0.f && splits <= 1 && (ldc % 4) == 0;
+  if (((N % 8) != 0 && !ragged_n_ok) || ((N % 8) == 0 && (ldc % 8) != 0) || (lda % 8) != 0 || (ldb % 8) != 0)
+    return -2;
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) & 15) return -3;
   if (residual && ((ldr % 8) != 0 || (reinterpret_cast<uintptr_t>(residual) & 15))) return -4;
   if (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) return -5;
@@ -880,6 +884,7 @@ int gemm_dense(const void* A, long long lda, int a_mn, const void* B, long long 
   p.ld_dglu = ex.ld_dglu;
   CUtensorMap mc = ma, mh = ma;
   p.tma_store = output_map(&mc, p, (uint64_t)M);
+  if ((N % 8) != 0 && p.tma_store == 0) return -2;
   if (ex.glu_I) {
     // the SwiGLU epilogue writes 32 x 32 tiles of h (and of g | u when kept) with TMA
     if (!make_map_2d(&mh, ex.glu_out, (uint64_t)ex.glu_I, (uint64_t)M, (uint64_t)ex.ld_glu, 32, 32, 2, true)) return -7;

@@ -134,6 +134,80 @@ __global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, c
   }
 }
 
+// Router of a mixture-of-experts layer, one warp per token: logits (fp32 GEMM output, rounded to
+// bf16 as the reference's bf16 linear produces them) -> softmax over E experts -> top-k (largest
+// first, lower expert id on ties) -> optional renormalisation of the k weights; per-expert routed
+// row counts accumulate into `counts` (zeroed by the caller). E <= 128, k <= 8.
+__global__ void moe_router_kernel(const float* __restrict__ logits, long long ldl, int T, int E, int k, int norm_topk,
+                                  float* __restrict__ probs, float* __restrict__ topw, long long* __restrict__ topi,
+                                  int* __restrict__ counts) {
+  const int t = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float v[4];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? __bfloat162float(__float2bfloat16(logits[static_cast<long long>(t) * ldl + e])) : -INFINITY;
+    mx = fmaxf(mx, v[j]);
+  }
+  mx = warp_max(mx);
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[j] = lane + 32 * j < E ? expf(v[j] - mx) : 0.f;
+    sum += v[j];
+  }
+  sum = warp_sum(sum);
+  const float inv = 1.f / sum;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane + 32 * j;
+    v[j] *= inv;
+    if (e < E) probs[static_cast<long long>(t) * E + e] = v[j];
+  }
+  // top-k by repeated warp arg-max; a chosen value is set to -1 (probabilities are >= 0)
+  float w_sel[kMoeMaxK];
+  int i_sel[kMoeMaxK];
+  float wsum = 0.f;
+  for (int r = 0; r < k; ++r) {
+    float best = -2.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && v[j] > best) {
+        best = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    w_sel[r] = best;
+    i_sel[r] = bi;
+    wsum += best;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (lane + 32 * j == bi) v[j] = -1.f;
+  }
+  if (lane == 0) {
+    const float scale = norm_topk ? 1.f / wsum : 1.f;
+    for (int r = 0; r < k; ++r) {
+      topw[static_cast<long long>(t) * k + r] = w_sel[r] * scale;
+      topi[static_cast<long long>(t) * k + r] = i_sel[r];
+      atomicAdd(counts + i_sel[r], 1);
+    }
+  }
+}
+
 }  // namespace accerl
 
 using namespace accerl;
@@ -157,5 +231,15 @@ extern "C" int accerl_moe_combine_bwd(const void* dout, const void* ys, const lo
   const int threads = min(256, max(32, ((H / 8 + 31) / 32) * 32));
   moe_combine_bwd_kernel<<<(unsigned)T, threads, 0, s>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)ys, pos, w,
                                                          k, H, (__nv_bfloat16*)dys, dw);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs,
+                                 float* topw, long long* topi, int* counts, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (E < 1 || E > 128 || k < 1 || k > kMoeMaxK || k > E) return -1;
+  const long long threads = static_cast<long long>(T) * 32;
+  moe_router_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(logits, ldl, T, E, k, norm_topk, probs, topw,
+                                                                       topi, counts);
   return (int)cudaGetLastError();
 }

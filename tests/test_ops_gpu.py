@@ -492,3 +492,39 @@ def test_moe_combine_fwd_bwd():
     untouched = torch.ones(R, dtype=torch.bool, device=DEV)
     untouched[pos] = False
     assert bool((dys[untouched] == 0).all())
+
+
+@pytest.mark.parametrize("E,k,norm", [(60, 4, False), (128, 8, True), (8, 2, False)])
+def test_moe_router_kernel(E, k, norm):
+    """Fused router (tcgen05 logits GEMM with a ragged expert count + softmax / top-k / renorm / counts
+    kernel) against the PyTorch router on the same bf16 logits."""
+    from types import SimpleNamespace
+
+    from accerl_agent_b200.models import moe
+
+    T, H = 1000, 512
+    h = torch.randn(T, H, device=DEV).bfloat16()
+    W = (torch.randn(E, H, device=DEV) * 0.05).bfloat16()
+    cfg = SimpleNamespace(num_experts=E, num_experts_per_tok=k, norm_topk_prob=norm)
+    model = SimpleNamespace(cfg=cfg, w=lambda name: W)
+    probs, topw, topi, cnt = moe.route(model, 0, h, counts=True)
+    # logits rounded to bf16 from fp32 sums in a different order can differ by one bf16 step
+    logits = (h.float() @ W.float().t()).bfloat16().float()
+    want_p = torch.softmax(logits, -1)
+    assert torch.allclose(probs, want_p, atol=1e-4, rtol=2e-2)
+    assert torch.allclose(probs.sum(-1), torch.ones(T, device=DEV), atol=1e-5)
+    # bf16 logits tie often; compare the chosen weights as sorted multisets and require every chosen
+    # expert to be within the top k of the kernel's own probabilities
+    want_w, _ = want_p.topk(k, -1)
+    if norm:
+        want_w = want_w / want_w.sum(-1, keepdim=True)
+    assert torch.allclose(topw.sort(-1).values, want_w.sort(-1).values, atol=1e-4, rtol=2e-2)
+    kth = probs.topk(k, -1).values[:, -1:]
+    assert bool((probs.gather(1, topi) >= kth).all())
+    assert bool((topi.sort(-1).values[:, 1:] != topi.sort(-1).values[:, :-1]).all())  # distinct experts
+    # the kernel's own weights are consistent with its probabilities
+    sel = probs.gather(1, topi)
+    if norm:
+        sel = sel / sel.sum(-1, keepdim=True)
+    assert torch.allclose(topw, sel, atol=1e-6, rtol=1e-5)
+    assert torch.equal(cnt.long(), torch.bincount(topi.reshape(-1), minlength=E))
