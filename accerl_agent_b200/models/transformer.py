@@ -223,8 +223,10 @@ class CausalLM:
         Hq, Hkv = cfg.num_attention_heads, cfg.num_key_value_heads
         h1, rstd1 = ops.rmsnorm(x, self.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
         bias = self.w(p + "self_attn.qkv_proj.bias") if cfg.qkv_bias else None
-        qkv = ops.linear(h1, self.w(p + "self_attn.qkv_proj.weight"), bias=bias)
         qk: Dict[str, torch.Tensor] = {}
+        # the RoPE kernel computes each token's cos/sin once for all heads; the projection's fused RoPE
+        # epilogue (ops.linear_rope) recomputes them per tile and measured slower in this step
+        qkv = ops.linear(h1, self.w(p + "self_attn.qkv_proj.weight"), bias=bias)
         if cfg.qk_norm:
             qk = self._qk_norm_forward(layer, qkv)
         ops.rope_(qkv, pos, Hq + Hkv, D, cfg.rope_theta)

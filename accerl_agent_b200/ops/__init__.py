@@ -67,6 +67,7 @@ __all__ = [
     "swiglu",
     "swiglu_backward",
     "linear_swiglu",
+    "linear_rope",
     "linear_dgrad_swiglu",
     "embedding",
     "embedding_backward",
@@ -233,6 +234,22 @@ def rope_(qkv: torch.Tensor, pos: torch.Tensor, n_rot_heads: int, head_dim: int,
     view = qkv[:, : n_rot_heads * head_dim].reshape(T, n_rot_heads, head_dim)
     view.copy_(reference.apply_rope(view, pos.view(-1), theta, inverse))
     return qkv
+
+
+def linear_rope(x: torch.Tensor, w: torch.Tensor, bias, pos: torch.Tensor, n_rot_heads: int, head_dim: int,
+                theta: float) -> torch.Tensor:
+    """``qkv = x w^T (+bias)`` with the rotary embedding applied to its first ``n_rot_heads`` heads at
+    positions ``pos``. On the GPU the rotation runs in the GEMM's epilogue (head dim 128, more than 256
+    rows); otherwise the projection is followed by the RoPE kernel."""
+    if (x.is_cuda and x.dtype == torch.bfloat16 and head_dim == 128 and x.shape[0] > 256
+            and (n_rot_heads * head_dim) % 128 == 0):
+        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+        native().gemm_rope(x, w, out, bias, pos.reshape(-1), n_rot_heads * head_dim, float(theta),
+                           status_tensor(x.device), 0, 0)
+        return out
+    out = linear(x, w, bias=bias)
+    rope_(out, pos, n_rot_heads, head_dim, theta)
+    return out
 
 
 def linear_swiglu(x: torch.Tensor, w: torch.Tensor, keep_gu: bool = False):

@@ -14,6 +14,9 @@ int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long
                      long long ldc, int c_f32, int M, int N, int K, float alpha, float beta, const void* bias,
                      const void* residual, long long ldr, int* status, int block_n, int max_ctas, int splits,
                      cudaStream_t stream);
+int accerl_gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M,
+                          int N, int K, const void* bias, const long long* pos, int rope_cols, float theta, int* status,
+                          int block_n, int max_ctas, cudaStream_t stream);
 int accerl_gemm_glu_bf16(const void* X, long long ldx, const void* W, long long ldw, void* gu, long long ldgu, void* h,
                          long long ldh, int M, int I, int K, int* status, int block_n, int max_ctas,
                          cudaStream_t stream);
@@ -170,6 +173,25 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
                          opt_ptr(bias), opt_ptr(residual), ldr, status_ptr(status), static_cast<int>(block_n),
                          static_cast<int>(max_ctas), static_cast<int>(splits), cur_stream()),
         "gemm");
+}
+
+// out = x w^T (+ bias) with the rotary embedding applied to the first rope_cols columns (heads of 128)
+// at positions pos (int64 [M]) in the epilogue.
+void gemm_rope(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+               const at::Tensor& pos, int64_t rope_cols, double theta, const c10::optional<at::Tensor>& status,
+               int64_t block_n, int64_t max_ctas) {
+  CHECK_CUDA(x);
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(out);
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.numel() == x.size(0), "gemm_rope: pos int64 [M]");
+  TORCH_CHECK(w.size(1) == x.size(1) && out.size(0) == x.size(0) && out.size(1) == w.size(0), "gemm_rope: shapes");
+  if (bias.has_value()) CHECK_BF16(*bias);
+  check(accerl_gemm_rope_bf16(x.data_ptr(), ld_of(x), w.data_ptr(), ld_of(w), out.data_ptr(), ld_of(out), x.size(0),
+                              w.size(0), x.size(1), opt_ptr(bias), reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()),
+                              static_cast<int>(rope_cols), static_cast<float>(theta), status_ptr(status),
+                              static_cast<int>(block_n), static_cast<int>(max_ctas), cur_stream()),
+        "gemm_rope");
 }
 
 // h = silu(x Wg^T) * (x Wu^T) for w = [Wg; Wu] ([2I, K]); gu (optional, [M, 2I]) keeps the gate|up outputs.
@@ -627,6 +649,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("last_error", &last_error, "(code, message) of the most recent launch; resets it");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM");
   m.def("gemm_glu", &gemm_glu, "gate/up GEMM with the SwiGLU epilogue");
+  m.def("gemm_rope", &gemm_rope, "projection GEMM with the rotary-embedding epilogue");
   m.def("gemm_dglu", &gemm_dglu, "down-projection dgrad GEMM with the SwiGLU backward epilogue");
   m.def("splitk_finish", &splitk_finish);
   m.def("grouped_gemm", &grouped_gemm);

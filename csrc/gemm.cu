@@ -80,6 +80,11 @@ struct GemmParams {
   // epilogue output path: 0 = per-thread stores, 1 = TMA tile stores of C (bf16 or fp32, beta = 0),
   // 2 = TMA reduce-add of fp32 tiles into C (beta = 1, split-K partials)
   int tma_store;
+  // rotary embedding in the bf16 TMA-store epilogue: output columns [0, rope_cols) form heads of 128
+  // that are rotated (rotate-half) at position rope_pos[row], inv_freq = theta^(-2i/128)
+  const long long* rope_pos;
+  int rope_cols;
+  float rope_log2_theta;
 };
 
 // Epilogue staging: per epilogue warp two 32-row x 128-byte tiles (64 bf16 or 32 fp32 columns),
@@ -150,7 +155,7 @@ __device__ __forceinline__ WorkItem work_item(const GemmParams& p, int t, int k_
 // barriers live in the even CTA (both CTAs' loads complete there), stage-empty and accumulator-full
 // barriers are signalled in both CTAs by multicast commits, and both CTAs' epilogues release an
 // accumulator on the even CTA's barrier. Loads are plain per-CTA TMA loads (no multicast).
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR, bool ROPE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH,
@@ -361,8 +366,62 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* wbuf = smEpi + quarter * (2 * kEpiChunkBytes);
         const int chunk_cols = p.c_f32 ? 32 : 64;
         const int y0 = static_cast<int>(w.c_row_off) + m_blk * TM + static_cast<int>(rank) * kBM + quarter * 32;
+        // rotary heads of this tile: both halves of a head (columns d and d + 64) in registers, rotated,
+        // then written as two 64-column chunks
+        int c_start = 0;
+        if (ROPE && p.rope_pos && !p.c_f32) {
+          const float pos = static_cast<float>(row_ok ? p.rope_pos[row] : 0);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += chunk_cols) {
+          for (int hd = 0; hd < BN && n_blk * BN + hd < p.rope_cols; hd += 128) {
+            uint32_t a[64], b[64];
+            tmem_ld32(t_row + hd, *reinterpret_cast<uint32_t(*)[32]>(a));
+            tmem_ld32(t_row + hd + 32, *reinterpret_cast<uint32_t(*)[32]>(a + 32));
+            tmem_ld32(t_row + hd + 64, *reinterpret_cast<uint32_t(*)[32]>(b));
+            tmem_ld32(t_row + hd + 96, *reinterpret_cast<uint32_t(*)[32]>(b + 32));
+            tmem_wait_ld();
+            const int colh = n_blk * BN + hd;
+#pragma unroll 1
+            for (int part = 0; part < 2; ++part) {
+              uint8_t* buf = wbuf + (epi_chunk & 1) * kEpiChunkBytes;
+              ++epi_chunk;
+              if (lane == 0) bulk_wait_read<1>();
+              __syncwarp();
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                uint32_t o[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  float r2[2];
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const int d = 8 * j + 2 * i + e;  // frequency index 0..63
+                    float x1 = __uint_as_float(a[d]) * p.alpha, x2 = __uint_as_float(b[d]) * p.alpha;
+                    if (p.bias) {
+                      x1 += __bfloat162float(p.bias[colh + d]);
+                      x2 += __bfloat162float(p.bias[colh + 64 + d]);
+                    }
+                    x1 = bf16_round(x1);  // the rotation sees the bf16 projection, as the separate kernel does
+                    x2 = bf16_round(x2);
+                    float cs, sn;
+                    rope_cos_sin(pos, d, 128, p.rope_log2_theta, cs, sn);
+                    r2[e] = part == 0 ? x1 * cs - x2 * sn : x2 * cs + x1 * sn;
+                  }
+                  o[i] = pack_bf16x2(r2[0], r2[1]);
+                }
+                *reinterpret_cast<uint4*>(buf + swz128(lane, j)) = make_uint4(o[0], o[1], o[2], o[3]);
+              }
+              fence_async_shared();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmC, buf, colh + part * 64, y0);
+                bulk_commit();
+              }
+            }
+            c_start = hd + 128;
+          }
+        }
+#pragma unroll 1
+        for (int c0 = c_start; c0 < BN; c0 += chunk_cols) {
           uint8_t* buf = wbuf + (epi_chunk & 1) * kEpiChunkBytes;
           ++epi_chunk;
           if (lane == 0) bulk_wait_read<1>();  // the store issued from this buffer two chunks ago
@@ -691,10 +750,10 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR, bool ROPE = false>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mh,
                 GemmParams p, cudaStream_t stream, int max_ctas) {
-  auto kern = gemm_bf16_tcgen05<BN, STAGES, A_MN, B_MN, PAIR>;
+  auto kern = gemm_bf16_tcgen05<BN, STAGES, A_MN, B_MN, PAIR, ROPE>;
   constexpr int smem_bytes =
       STAGES * GemmSmem<BN, PAIR>::kStageBytes + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(smem_bytes <= 232448, "shared memory per CTA");
@@ -773,6 +832,9 @@ int output_map(CUtensorMap* mc, const GemmParams& p, uint64_t rows_total) {
 
 namespace {
 struct EpilogueExtras {
+  const long long* rope_pos = nullptr;
+  int rope_cols = 0;
+  float rope_log2_theta = 0.f;
   int glu_I = 0;
   void* glu_out = nullptr;
   long long ld_glu = 0;
@@ -885,6 +947,15 @@ int gemm_dense(const void* A, long long lda, int a_mn, const void* B, long long 
   CUtensorMap mc = ma, mh = ma;
   p.tma_store = output_map(&mc, p, (uint64_t)M);
   if ((N % 8) != 0 && p.tma_store == 0) return -2;
+  p.rope_pos = reinterpret_cast<const long long*>(ex.rope_pos);
+  p.rope_cols = ex.rope_cols;
+  p.rope_log2_theta = ex.rope_log2_theta;
+  if (ex.rope_pos && (p.tma_store != 1 || c_f32 || (ex.rope_cols % 128) != 0 || a_mn || b_mn)) return -15;
+  if (ex.rope_pos) {
+    if (pair) return launch_gemm<256, 6, false, false, true, true>(ma, mb, mc, mh, p, stream, max_ctas);
+    if (bn == 256) return launch_gemm<256, 4, false, false, false, true>(ma, mb, mc, mh, p, stream, max_ctas);
+    return launch_gemm<128, 6, false, false, false, true>(ma, mb, mc, mh, p, stream, max_ctas);
+  }
   if (ex.glu_I) {
     // the SwiGLU epilogue writes 32 x 32 tiles of h (and of g | u when kept) with TMA
     if (!make_map_2d(&mh, ex.glu_out, (uint64_t)ex.glu_I, (uint64_t)M, (uint64_t)ex.ld_glu, 32, 32, 2, true)) return -7;
@@ -903,6 +974,20 @@ extern "C" int accerl_gemm_bf16(const void* A, long long lda, int a_mn, const vo
                                 int max_ctas, int splits, cudaStream_t stream) {
   return gemm_dense(A, lda, a_mn, B, ldb, b_mn, C, ldc, c_f32, M, N, K, alpha, beta, bias, residual, ldr, status,
                     block_n, max_ctas, splits, stream, EpilogueExtras{});
+}
+
+// Projection whose first rope_cols output columns (heads of 128) get the rotary embedding at position
+// pos[row] in the epilogue (the qkv projection: q and k heads rotated, v untouched). bf16 output.
+extern "C" int accerl_gemm_rope_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc,
+                                     int M, int N, int K, const void* bias, const long long* pos, int rope_cols,
+                                     float theta, int* status, int block_n, int max_ctas, cudaStream_t stream) {
+  if (!pos || rope_cols <= 0 || rope_cols > N || !(theta > 0.f)) return -15;
+  EpilogueExtras ex;
+  ex.rope_pos = pos;
+  ex.rope_cols = rope_cols;
+  ex.rope_log2_theta = log2f(theta);
+  return gemm_dense(A, lda, 0, B, ldb, 0, C, ldc, 0, M, N, K, 1.f, 0.f, bias, nullptr, 0, status, block_n, max_ctas, 1,
+                    stream, ex);
 }
 
 // Gate/up projection fused with SwiGLU: for W = [gate; up] ([2I, K], K-major) computes g, u = X W^T
@@ -1015,6 +1100,9 @@ extern "C" int accerl_grouped_gemm_bf16(const void* A, long long lda, int a_mn, 
   p.kb_per_split = (K + kBK - 1) / kBK;
   p.group_m = 8;
   p.group_mode = mode;
+  p.rope_pos = nullptr;
+  p.rope_cols = 0;
+  p.rope_log2_theta = 0.f;
   p.glu_I = 0;
   p.glu_out = nullptr;
   p.ld_glu = 0;

@@ -528,3 +528,23 @@ def test_moe_router_kernel(E, k, norm):
         sel = sel / sel.sum(-1, keepdim=True)
     assert torch.allclose(topw, sel, atol=1e-6, rtol=1e-5)
     assert torch.equal(cnt.long(), torch.bincount(topi.reshape(-1), minlength=E))
+
+
+@pytest.mark.parametrize("block_n", [0, 256, 128, -256])
+def test_gemm_rope_epilogue(block_n):
+    """qkv projection with the rotary embedding in the epilogue equals the projection followed by the
+    RoPE kernel (q and k heads rotated, v heads untouched), with bias and a row tail."""
+    T, H, Hq, Hkv, D = 777, 384, 6, 2, 128
+    x = torch.randn(T, H, device=DEV).bfloat16()
+    w = (torch.randn((Hq + 2 * Hkv) * D, H, device=DEV) * 0.05).bfloat16()
+    bias = torch.randn((Hq + 2 * Hkv) * D, device=DEV).bfloat16()
+    pos = torch.randint(0, 8192, (T,), device=DEV)
+    want = ops.gemm(x, w, bias=bias)
+    ops.rope_(want, pos, Hq + Hkv, D, 1e6)
+    got = torch.empty_like(want)
+    ops.native().gemm_rope(x, w, got, bias, pos, (Hq + Hkv) * D, 1e6, ops.status_tensor(torch.device(DEV)), block_n, 0)
+    # identical up to fp32 contraction differences in the rotation
+    assert (got.float() - want.float()).abs().max() <= 1e-2 * want.float().abs().max()
+    assert torch.equal(got[:, (Hq + Hkv) * D :], want[:, (Hq + Hkv) * D :])  # v
+    got2 = ops.linear_rope(x, w, bias, pos, Hq + Hkv, D, 1e6)
+    assert torch.equal(got2, got) or block_n != 0
