@@ -139,7 +139,8 @@ def padded_layout_from_pads(pads, device):
     }
 
 
-def device_padded_layout(topi: torch.Tensor, num_experts: int, lo: int = 0, El: Optional[int] = None):
+def device_padded_layout(topi: torch.Tensor, num_experts: int, lo: int = 0, El: Optional[int] = None,
+                         counts: Optional[torch.Tensor] = None):
     """Grouped-GEMM layout computed on the device, with no host synchronisation.
 
     The pairs ``(token, slot)`` of ``topi`` are sorted by expert; experts ``[lo, lo + El)`` get row
@@ -155,7 +156,11 @@ def device_padded_layout(topi: torch.Tensor, num_experts: int, lo: int = 0, El: 
     dev = flat.device
     order = torch.argsort(flat, stable=True)
     e_sorted = flat.index_select(0, order)
-    counts = torch.bincount(flat, minlength=num_experts)
+    if counts is None:
+        # scatter-add, not bincount: bincount sizes its output from the data (a device->host sync)
+        counts = torch.zeros(num_experts, dtype=torch.long, device=dev).scatter_add_(0, flat, torch.ones_like(flat))
+    else:
+        counts = counts.to(torch.long)
     cstart = torch.cumsum(counts, 0) - counts
     cl = counts[lo : lo + El]
     pads = torch.div(cl + (SEG - 1), SEG, rounding_mode="floor") * SEG
@@ -220,11 +225,12 @@ def experts_backward_grouped(model, layer: int, dys_pad, xs_pad, gu, act, lay):
 def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save: bool):
     cfg = model.cfg
     k = cfg.num_experts_per_tok
-    probs, topw, topi = route(model, layer, h)
-    w_act = topw.to(h.dtype)
     ep = getattr(model, "expert_parallel", None)
     if ep is None and h.is_cuda and h.dtype == torch.bfloat16:
-        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi)
+        probs, topw, topi, counts = route(model, layer, h, counts=True)
+        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi, counts)
+    probs, topw, topi = route(model, layer, h)
+    w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
     El = cfg.local_experts
     if El is not None and El != cfg.num_experts:
@@ -295,7 +301,7 @@ def _shared_expert(model, layer: int, h: torch.Tensor, cache):
     return sy, sg
 
 
-def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi):
+def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi, counts=None):
     """CUDA path without host synchronisation: device-side padded layout, grouped GEMMs over the
     bounded tile count, fused combine. Training (``save``) zeroes the padded input rows because the
     weight-gradient contraction runs over them; inference leaves them uninitialised (their output
@@ -304,7 +310,7 @@ def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw,
     k = cfg.num_experts_per_tok
     El = cfg.local_experts if cfg.local_experts is not None else cfg.num_experts
     lo = cfg.expert_offset if El != cfg.num_experts else 0
-    order, rows, valid, lay = device_padded_layout(topi, cfg.num_experts, lo, El)
+    order, rows, valid, lay = device_padded_layout(topi, cfg.num_experts, lo, El, counts)
     R = lay["total"]
     tok = torch.div(order, k, rounding_mode="floor")
     alloc = torch.zeros if save else torch.empty
