@@ -233,9 +233,10 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
     El = cfg.local_experts
-    if El is not None and El != cfg.num_experts:
+    if ep is None and El is not None and El != cfg.num_experts:
         # tensor-parallel engine shard: only the (token, slot) pairs routed to this rank's experts;
-        # the caller all-reduces the partial outputs of the ranks
+        # the caller all-reduces the partial outputs of the ranks (with expert parallelism every pair
+        # is dispatched to its owner instead)
         lo = cfg.expert_offset
         a, b = bounds[lo], bounds[lo + El]
         order, counts = order[a:b], counts[lo : lo + El]

@@ -70,6 +70,11 @@ def is_trainable(name: str, train_mode: str, num_layers: int) -> bool:
     raise ValueError(f"Unsupported train mode: {train_mode}")
 
 
+def is_expert_param(name: str) -> bool:
+    """Routed-expert tensors (stacked over experts); the router and shared expert are not."""
+    return name.endswith("mlp.experts.gate_up_proj") or name.endswith("mlp.experts.down_proj")
+
+
 @dataclass
 class ParamSlot:
     name: str
@@ -82,15 +87,26 @@ class ParamSlot:
 
 @dataclass
 class ParamLayout:
-    """Offsets of every parameter in two flat segments: trainable first, then frozen."""
+    """Offsets of every parameter in two flat segments: trainable first, then frozen.
+
+    ``experts_last`` (expert-partitioned training: each rank holds only its routed experts) orders
+    the trainable segment as [replicated parameters | this rank's expert tensors]: the first
+    ``replicated_numel`` elements are laid out identically on every rank (sharded and reduced by the
+    optimizer), the rest is rank-local."""
 
     slots: Dict[str, ParamSlot]
     order: List[str]
     trainable_numel: int
     total_numel: int
+    replicated_numel: int = -1
+
+    def __post_init__(self):
+        if self.replicated_numel < 0:
+            self.replicated_numel = self.trainable_numel
 
     @classmethod
-    def build(cls, cfg: ModelConfig, train_mode: str = "full", pad_to: int = 1) -> "ParamLayout":
+    def build(cls, cfg: ModelConfig, train_mode: str = "full", pad_to: int = 1,
+              experts_last: bool = False) -> "ParamLayout":
         specs = parameter_specs(cfg)
         tied = cfg.tie_word_embeddings
 
@@ -101,9 +117,14 @@ class ParamLayout:
 
         slots: Dict[str, ParamSlot] = {}
         off = 0
-        for group in (True, False):
+        q = ALIGN * max(pad_to, 1)
+        replicated_numel = -1
+        passes = ((True, False), (True, True), (False, None)) if experts_last else ((True, None), (False, None))
+        for group, experts in passes:
             for name, shape in specs:
                 if trainable(name) != group:
+                    continue
+                if experts is not None and is_expert_param(name) != experts:
                     continue
                 n = 1
                 for s in shape:
@@ -111,15 +132,16 @@ class ParamLayout:
                 slots[name] = ParamSlot(name, tuple(shape), off, n, group)
                 off += (n + ALIGN - 1) // ALIGN * ALIGN
             if group:
-                q = ALIGN * max(pad_to, 1)
                 off = (off + q - 1) // q * q
-                trainable_numel = off
-        q = ALIGN * max(pad_to, 1)
+                if experts is False:
+                    replicated_numel = off
+                else:
+                    trainable_numel = off
         total = (off + q - 1) // q * q
         for s in slots.values():
             if s.trainable:
                 s.grad_offset = s.offset
-        return cls(slots, [n for n, _ in specs], trainable_numel, total)
+        return cls(slots, [n for n, _ in specs], trainable_numel, total, replicated_numel)
 
 
 @dataclass
@@ -204,6 +226,8 @@ class CausalLM:
         dev = self.params.device
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
+        cfg = self.cfg
+        partial = cfg.local_experts is not None and cfg.local_experts != cfg.num_experts
         with torch.no_grad():
             for name in self.layout.order:
                 v = self._views[name]
@@ -211,6 +235,12 @@ class CausalLM:
                     v.fill_(1.0)
                 elif name.endswith(".bias"):
                     v.zero_()
+                elif partial and is_expert_param(name):
+                    # draw the whole expert stack and keep this rank's experts: every partition of the
+                    # experts holds exactly the values of the unpartitioned model
+                    full = torch.randn((cfg.num_experts,) + tuple(v.shape[1:]), generator=gen, dtype=torch.float32,
+                                       device=dev) * std
+                    v.copy_(full[cfg.expert_offset : cfg.expert_offset + v.shape[0]].to(v.dtype))
                 else:
                     chunk = torch.randn(v.shape, generator=gen, dtype=torch.float32, device=dev) * std
                     v.copy_(chunk.to(v.dtype))
@@ -398,8 +428,8 @@ class CausalLM:
 
 
 def build_model(cfg: ModelConfig, train_mode: str, device, dtype: torch.dtype, with_grads: bool = True,
-                pad_to: int = 1) -> CausalLM:
-    layout = ParamLayout.build(cfg, train_mode, pad_to=pad_to)
+                pad_to: int = 1, experts_last: bool = False) -> CausalLM:
+    layout = ParamLayout.build(cfg, train_mode, pad_to=pad_to, experts_last=experts_last)
     params = torch.zeros(layout.total_numel, dtype=dtype, device=device)
     grads = torch.zeros(layout.trainable_numel, dtype=torch.float32, device=device) if with_grads else None
     return CausalLM(cfg, layout, params, grads)

@@ -22,8 +22,11 @@ runs dgrad/wgrad of its experts (expert weight gradients therefore only land on 
 optimizer's reduce-scatter sums ranks, so the total is exact), and the gate/up dgrad GEMM scatters
 the input-gradient rows back to their sources.
 
-Every rank keeps the full bf16 parameter copy (the resident-parameter design of ``fsdp.py``); only
-the compute is partitioned. Receive buffers are capacity-free: sized for the worst case in which
+By default every rank keeps the full bf16 parameter copy (the resident-parameter design of
+``fsdp.py``) and only the compute is partitioned. With expert-partitioned storage
+(``expert_partition(cfg, rank, world)`` + ``build_model(..., experts_last=True)``) a rank holds only
+its own experts' weights, gradients and optimizer state, which is what lets models whose experts
+dominate the parameter count (30 B-class MoE) fit. Receive buffers are capacity-free: sized for the worst case in which
 every source routes all of its rows to one owner (``W * max_tokens * top_k`` rows plus padding).
 Pad rows of the receive buffer must read as zero (they enter the weight-gradient contraction), so
 the owner clears the rows it used after copying them out; the buffer is zero between uses.
@@ -48,6 +51,24 @@ from ..models import moe as moe_mod
 SEG = moe_mod.SEG
 
 
+def expert_ranges(num_experts: int, world: int):
+    """Contiguous expert ranges of the ranks: the first ``E % W`` ranks own one extra expert."""
+    base_n, extra = divmod(num_experts, world)
+    nloc = [base_n + (1 if r < extra else 0) for r in range(world)]
+    return nloc, [sum(nloc[:r]) for r in range(world)]
+
+
+def expert_partition(cfg, rank: int, world: int):
+    """Model config of one rank's expert-partitioned storage (its routed experts only)."""
+    import copy
+
+    nloc, lo = expert_ranges(cfg.num_experts, world)
+    c = copy.deepcopy(cfg)
+    c.local_experts = nloc[rank]
+    c.expert_offset = lo[rank]
+    return c
+
+
 class ExpertParallel:
     def __init__(self, cfg, group=None, max_tokens: int = 16384, device: Optional[torch.device] = None,
                  dtype: torch.dtype = torch.bfloat16, transport: Optional[str] = None):
@@ -63,9 +84,7 @@ class ExpertParallel:
         self.Im = cfg.moe_intermediate_size
         # contiguous expert ranges; the first E % W ranks own one extra expert (60 experts on 8 ranks:
         # 8,8,8,8,7,7,7,7)
-        base_n, extra = divmod(self.E, self.world)
-        self.nloc = [base_n + (1 if r < extra else 0) for r in range(self.world)]
-        self.lo_of = [sum(self.nloc[:r]) for r in range(self.world)]
+        self.nloc, self.lo_of = expert_ranges(self.E, self.world)
         self.owner = [r for r in range(self.world) for _ in range(self.nloc[r])]
         self.E_loc = self.nloc[self.rank]
         self.lo = self.lo_of[self.rank]
@@ -256,7 +275,16 @@ class ExpertParallel:
     # ---------------------------------------------------------------- expert compute
     def _weights(self, model, layer):
         p = f"model.layers.{layer}.mlp.experts."
-        sl = slice(self.lo, self.lo + self.E_loc)
+        W = model.w(p + "gate_up_proj")
+        if W.shape[0] == self.E:
+            sl = slice(self.lo, self.lo + self.E_loc)  # every rank keeps the whole expert stack
+        else:
+            # expert-partitioned storage: the model holds exactly this rank's experts
+            cfg = model.cfg
+            if W.shape[0] != self.E_loc or cfg.expert_offset != self.lo:
+                raise ValueError(f"model holds experts [{cfg.expert_offset}, +{W.shape[0]}) but this rank owns "
+                                 f"[{self.lo}, +{self.E_loc})")
+            sl = slice(0, self.E_loc)
         Wgu = model.w(p + "gate_up_proj")[sl]
         Wd = model.w(p + "down_proj")[sl]
         gWgu, gWd = model.g(p + "gate_up_proj"), model.g(p + "down_proj")

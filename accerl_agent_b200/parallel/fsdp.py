@@ -20,6 +20,11 @@ Micro-batches therefore run with no parameter traffic at all. The loss is scaled
 On a single rank the shard is the whole trainable segment and no collective is issued. CPU ranks use
 gloo (reduce-scatter is emulated with an all-reduce there).
 
+With expert-partitioned storage (``ParamLayout.build(..., experts_last=True)``) only the replicated
+prefix of the trainable segment is sharded and reduced; each rank's own routed experts (the rest of the
+segment) keep their full fp32 state on that rank and are updated locally (their gradients only ever
+land on the owner). The global gradient norm sums both parts before its all-reduce.
+
 With NCCL ranks on one node (``fused_collectives``, the default when every GPU pair has peer access)
 steps 2-5 run as two kernels over NVLink peer memory instead (``csrc/collectives.cu``): a
 reduce-scatter that reads the shard range of every peer's fp32 gradient buffer and accumulates the
@@ -50,10 +55,11 @@ class ShardedAdamW:
         self.group = group
         self.world = dist.get_world_size(group) if dist_ready() else 1
         self.rank = dist.get_rank(group) if dist_ready() else 0
-        n = model.layout.trainable_numel
+        n = model.layout.replicated_numel
         if n % max(self.world, 1):
             raise ValueError("trainable segment must be padded to a multiple of the world size")
         self.shard_numel = n // self.world
+        self.local_lo, self.local_hi = n, model.layout.trainable_numel  # rank-local experts (may be empty)
         self.lr = lr
         self.weight_decay = weight_decay
         self.betas = betas
@@ -65,8 +71,15 @@ class ShardedAdamW:
         self.master = self.param_shard.detach().float().clone()
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
+        self.has_local = self.local_hi > self.local_lo
+        if self.has_local:
+            self.local_params = model.params[self.local_lo : self.local_hi]
+            self.local_master = self.local_params.detach().float().clone()
+            self.local_m = torch.zeros_like(self.local_master)
+            self.local_v = torch.zeros_like(self.local_master)
+            self.local_grads = model.grads[self.local_lo : self.local_hi]
         if self.world == 1:
-            self.grad_shard = model.grads
+            self.grad_shard = model.grads[: self.shard_numel]
         else:
             self.grad_shard = torch.zeros(self.shard_numel, dtype=torch.float32, device=model.params.device)
         self._sumsq = torch.zeros(1, dtype=torch.float64, device=model.params.device)
@@ -84,11 +97,13 @@ class ShardedAdamW:
     def refresh_master_from_params(self) -> None:
         """Re-seed fp32 master weights after parameters were overwritten (e.g. checkpoint load)."""
         self.master.copy_(self.param_shard.float())
+        if self.has_local:
+            self.local_master.copy_(self.local_params.float())
 
     def reduce_gradients(self) -> None:
         if self.world == 1:
             return
-        full = self.model.grads
+        full = self.model.grads[: self.local_lo]
         if self.backend == "nccl":
             dist.reduce_scatter_tensor(self.grad_shard, full, op=dist.ReduceOp.SUM, group=self.group)
         else:
@@ -100,6 +115,8 @@ class ShardedAdamW:
     def global_grad_sumsq(self) -> torch.Tensor:
         self._sumsq.zero_()
         ops.grad_sumsq(self.grad_shard, self._sumsq)
+        if self.has_local:
+            ops.grad_sumsq(self.local_grads, self._sumsq)
         if self.world > 1:
             dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
         return self._sumsq
@@ -117,8 +134,17 @@ class ShardedAdamW:
         ops.adamw_step(self.master, self.exp_avg, self.exp_avg_sq, self.grad_shard, self.param_shard, sumsq,
                        self.lr, self.betas[0], self.betas[1], self.eps, self.weight_decay, self.max_grad_norm,
                        self.step_count)
+        self._local_step(sumsq)
         self.all_gather_params()
         return sumsq
+
+    def _local_step(self, sumsq: torch.Tensor) -> None:
+        """Clip + AdamW of this rank's own experts (full state here, no collective)."""
+        if not self.has_local:
+            return
+        ops.adamw_step(self.local_master, self.local_m, self.local_v, self.local_grads, self.local_params, sumsq,
+                       self.lr, self.betas[0], self.betas[1], self.eps, self.weight_decay, self.max_grad_norm,
+                       self.step_count)  # (the kernel zeroes the gradients it consumed)
 
     def _fused_step(self) -> torch.Tensor:
         import math
@@ -128,10 +154,13 @@ class ShardedAdamW:
         # every peer has finished accumulating its gradients before anyone reads them
         dist.all_reduce(self._barrier_flag, group=self.group)
         native.rs_sumsq(self._grad_peers.ptrs, self.rank, self.shard_numel, self.grad_shard, self._sumsq)
+        if self.has_local:
+            ops.grad_sumsq(self.local_grads, self._sumsq)
         # the norm all-reduce also guarantees every peer has finished reading this rank's gradients
         dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
-        self.model.grads.zero_()
         self.step_count += 1
+        self._local_step(self._sumsq)
+        self.model.grads.zero_()
         b1, b2 = self.betas
         native.adamw_push(self.master, self.exp_avg, self.exp_avg_sq, self.grad_shard, self._param_peers.ptrs,
                           self.rank, self._sumsq, self.lr, b1, b2, self.eps, self.weight_decay, self.max_grad_norm,
@@ -143,7 +172,7 @@ class ShardedAdamW:
     def all_gather_params(self) -> None:
         if self.world == 1:
             return
-        full = self.model.params[: self.model.layout.trainable_numel]
+        full = self.model.params[: self.local_lo]
         if self.backend == "nccl":
             dist.all_gather_into_tensor(full, self.param_shard, group=self.group)
         else:
@@ -152,7 +181,10 @@ class ShardedAdamW:
             dist.all_gather(parts, local, group=self.group)
 
     def state_dict(self):
-        return {"step": self.step_count, "master": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq}
+        st = {"step": self.step_count, "master": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq}
+        if self.has_local:
+            st.update(local_master=self.local_master, local_exp_avg=self.local_m, local_exp_avg_sq=self.local_v)
+        return st
 
     def load_state_dict(self, state):
         self.step_count = int(state["step"])
@@ -160,4 +192,9 @@ class ShardedAdamW:
         self.exp_avg.copy_(state["exp_avg"])
         self.exp_avg_sq.copy_(state["exp_avg_sq"])
         self.param_shard.copy_(self.master.to(self.param_shard.dtype))
+        if self.has_local:
+            self.local_master.copy_(state["local_master"])
+            self.local_m.copy_(state["local_exp_avg"])
+            self.local_v.copy_(state["local_exp_avg_sq"])
+            self.local_params.copy_(self.local_master.to(self.local_params.dtype))
         self.all_gather_params()

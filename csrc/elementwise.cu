@@ -132,13 +132,40 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const __nv_bfloa
     for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
   }
   for (int row = gw; row < rows; row += nw) {
+    // every load of the row is issued up front (dy, x and the incoming dx): one DRAM round trip per row.
+    // Rows wider than 1536 keep only the incoming dx in registers and re-read dy, x from L1.
+    constexpr bool kHold = NC <= 6;
+    constexpr int NH = kHold ? NC : 1;
+    uint4 av[NH], bv[NH], qv[NH];
+    if constexpr (kHold) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        av[c] = *reinterpret_cast<const uint4*>(dy + row * ld + c * 256 + lane * 8);
+        bv[c] = *reinterpret_cast<const uint4*>(x + row * ld + c * 256 + lane * 8);
+        qv[c] = dx_accum ? *reinterpret_cast<const uint4*>(dx_accum + row * ld + c * 256 + lane * 8)
+                         : make_uint4(0, 0, 0, 0);
+      }
+    }
+    auto ld_q = [&](int c) -> uint4 {
+      if constexpr (kHold) return qv[c];
+      else
+        return dx_accum ? *reinterpret_cast<const uint4*>(dx_accum + row * ld + c * 256 + lane * 8)
+                        : make_uint4(0, 0, 0, 0);
+    };
+    auto ld_dy = [&](int c) -> uint4 {
+      if constexpr (kHold) return av[c];
+      else return *reinterpret_cast<const uint4*>(dy + row * ld + c * 256 + lane * 8);
+    };
+    auto ld_x = [&](int c) -> uint4 {
+      if constexpr (kHold) return bv[c];
+      else return *reinterpret_cast<const uint4*>(x + row * ld + c * 256 + lane * 8);
+    };
     const float r = rstd[row];
     float dot = 0.f;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      const uint4 av = *reinterpret_cast<const uint4*>(dy + row * ld + c * 256 + lane * 8);
-      const uint4 bv = *reinterpret_cast<const uint4*>(x + row * ld + c * 256 + lane * 8);
-      const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+      const uint4 a4 = ld_dy(c), b4 = ld_x(c);
+      const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w}, bw[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 fa = unpack_bf16x2(aw[i]), fb = unpack_bf16x2(bw[i]);
@@ -152,15 +179,10 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(const __nv_bfloa
     dot = warp_sum(dot) / static_cast<float>(H);
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      // second touch of the row hits L1
-      const uint4 av = *reinterpret_cast<const uint4*>(dy + row * ld + c * 256 + lane * 8);
-      const uint4 bv = *reinterpret_cast<const uint4*>(x + row * ld + c * 256 + lane * 8);
-      const uint32_t aw[4] = {av.x, av.y, av.z, av.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-      uint32_t qw[4] = {0, 0, 0, 0};
-      if (dx_accum) {
-        const uint4 qv = *reinterpret_cast<const uint4*>(dx_accum + row * ld + c * 256 + lane * 8);
-        qw[0] = qv.x; qw[1] = qv.y; qw[2] = qv.z; qw[3] = qv.w;
-      }
+      const uint4 a4 = ld_dy(c), b4 = ld_x(c);  // the second touch hits L1 when not held
+      const uint32_t aw[4] = {a4.x, a4.y, a4.z, a4.w}, bw[4] = {b4.x, b4.y, b4.z, b4.w};
+      const uint4 q4 = ld_q(c);
+      const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
       uint32_t o[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {

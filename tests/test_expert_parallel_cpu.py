@@ -120,3 +120,72 @@ def test_expert_parallel_uneven_expert_partition():
 def test_expert_parallel_all_to_all_transport():
     # the all_to_all_single transport (NCCL on GPUs) runs on gloo ranks too
     _check("qwen2_moe", num_experts=5, transport="all_to_all")
+
+
+def _partition_worker(rank, port, out):
+    try:
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        from accerl_agent_b200.parallel.expert_parallel import expert_partition
+        from accerl_agent_b200.parallel.fsdp import ShardedAdamW
+
+        cfg = _cfg("qwen2_moe", 5)  # uneven: rank 0 owns 3 experts, rank 1 owns 2
+        pcfg = expert_partition(cfg, rank, 2)
+        model = build_model(pcfg, "full", torch.device("cpu"), torch.float32, pad_to=2, experts_last=True)
+        model.init_weights(seed=3)
+        model.expert_parallel = ExpertParallel(cfg, max_tokens=64, device=torch.device("cpu"), dtype=torch.float32,
+                                               transport="emulated")
+        opt = ShardedAdamW(model, lr=1e-3)
+        lp = _run(model, _pack(40 + rank, cfg.vocab_size))
+        names = [n for n in model.layout.order if n.endswith("experts.gate_up_proj")]
+        local_grads = {n: model.g(n).clone() for n in names}
+        opt.step(1e-3)
+        after = {n: model.w(n).clone() for n in model.layout.order}
+        # numpy copies travel by value (tensors would be shared with a process that is about to exit)
+        out.put((rank, (lp.numpy(), {n: g.numpy() for n, g in local_grads.items()},
+                        {n: w.numpy() for n, w in after.items()}, pcfg.expert_offset, pcfg.local_experts,
+                        model.layout.replicated_numel, model.layout.trainable_numel), None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:
+        out.put((rank, repr(exc), None))
+        raise
+
+
+def test_expert_partitioned_storage_matches_full_model():
+    """Each rank holding only its experts (weights, gradients, optimizer state) computes the same
+    log-probabilities, expert gradients and post-step parameters as one rank holding every expert and
+    training on both ranks' packs; the optimizer shards only the replicated prefix."""
+    from accerl_agent_b200.parallel.fsdp import ShardedAdamW
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_partition_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, payload, _ = q.get(timeout=180)
+        assert not isinstance(payload, str), payload
+        res[r] = payload
+    for p in procs:
+        p.join(60)
+    cfg = _cfg("qwen2_moe", 5)
+    ref = build_model(cfg, "full", torch.device("cpu"), torch.float32)
+    ref.init_weights(seed=3)
+    opt = ShardedAdamW(ref, lr=1e-3)
+    lps = [_run(ref, _pack(40 + r, cfg.vocab_size)) for r in range(2)]
+    ref_grads = {n: ref.g(n).clone() for n in ref.layout.order if n.endswith("experts.gate_up_proj")}
+    opt.step(1e-3)
+    for r in range(2):
+        lp, local_grads, after, lo, nloc, repl, trainable = res[r]
+        assert repl < trainable  # a rank-local expert region exists
+        assert torch.allclose(torch.from_numpy(lp), lps[r], atol=1e-5, rtol=1e-4)
+        for n, g in local_grads.items():
+            assert torch.allclose(torch.from_numpy(g), ref_grads[n][lo : lo + nloc], atol=1e-6, rtol=1e-4), n
+        for n, w in after.items():
+            want = ref.w(n)
+            if n.endswith("experts.gate_up_proj") or n.endswith("experts.down_proj"):
+                want = want[lo : lo + nloc]
+            assert torch.allclose(torch.from_numpy(w), want, atol=1e-6, rtol=1e-5), n
