@@ -61,8 +61,14 @@ def exchange_weight_handles(trainers, engines, followers, timeout: float = 600.0
     trainer ``i % world``, once at start-up; later syncs pull through the mapped buffers. A trainer
     or engine process that died before or during the exchange raises ``ActorDied`` here (the
     reference builds its NCCL weight-transfer group at this point, ``agent_textworld.py:3035-3057``)."""
+    handles = None
     for i, e in enumerate(engines):
         handle = get(trainers[i % len(trainers)].export_weights_handle.remote(), timeout=timeout)
+        if isinstance(handle, dict) and handle.get("partition"):
+            # expert-partitioned trainers: every engine rank maps every trainer (experts come from owners)
+            if handles is None:
+                handles = get([t.export_weights_handle.remote() for t in trainers], timeout=timeout)
+            handle = handles
         e.attach_trainer_weights(handle)
         for f in followers[i] if followers else ():
             f.attach_trainer_weights(handle)

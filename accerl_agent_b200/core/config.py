@@ -107,6 +107,9 @@ def build_parser() -> argparse.ArgumentParser:
     a("--kv-block-size", type=int, default=16)
     a("--expert-parallel", action="store_true",
       help="MoE models: partition the experts over the trainer ranks (token dispatch/combine over NVLink).")
+    a("--expert-storage", default="partitioned", choices=("partitioned", "replicated"),
+      help="With --expert-parallel: each rank stores only its routed experts (weights, gradients, optimizer "
+           "state), or every rank keeps the whole expert stack.")
     a("--weight-sync", default="ipc", choices=("ipc", "nccl"), help="Trainer->rollout weight transfer path.")
     return p
 

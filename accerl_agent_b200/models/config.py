@@ -173,6 +173,13 @@ PRESETS: Dict[str, ModelConfig] = {
         num_key_value_heads=2, head_dim=32, intermediate_size=384, rope_theta=1e6, tie_word_embeddings=False,
         torch_dtype="float32", bos_token_id=1, eos_token_id=2,
     ),
+    # Tiny Qwen2-MoE-style smoke model: 6 routed experts top-2 plus a gated shared expert.
+    "tiny-qwen2-moe": ModelConfig(
+        model_type="qwen2_moe", vocab_size=4096, hidden_size=128, num_hidden_layers=2, num_attention_heads=4,
+        num_key_value_heads=2, head_dim=32, intermediate_size=384, rope_theta=1e6, tie_word_embeddings=False,
+        torch_dtype="float32", bos_token_id=1, eos_token_id=2, num_experts=6, num_experts_per_tok=2,
+        moe_intermediate_size=64, shared_expert_intermediate_size=96,
+    ),
     # Qwen2.5-1.5B shape (tied embeddings).
     "qwen2.5-1.5b": ModelConfig(),
     # Qwen1.5-MoE-A2.7B shape: 60 routed experts top-4 + 4 shared experts worth (5632) intermediate.

@@ -369,9 +369,24 @@ class GenerationEngine:
         maps = {}
         for scope in ("all", "trainable"):
             descs = build_weight_map(self.full_cfg, src_layout, self.layout, self.tp_rank, self.tp, scope)
-            maps[scope] = (descs, descs_tensor(descs, self.device) if self.device.type == "cuda" else None)
+            maps[scope] = [(descs, descs_tensor(descs, self.device) if self.device.type == "cuda" else None)]
         self._weight_maps = maps
-        self._weight_src = (tensor, addr)
+        self._weight_src = [(tensor, addr)]
+
+    def set_weight_sources(self, sources, primary: int = 0) -> None:
+        """Several trainer buffers, e.g. expert-partitioned trainers: ``sources`` lists dicts with
+        ``layout``, ``expert_lo``, ``expert_count`` and ``tensor`` or ``addr``. Routed experts are pulled
+        from their owner, everything else from ``sources[primary]``."""
+        from .weight_map import build_weight_map_multi, descs_tensor
+
+        srcs = [(src["layout"], int(src["expert_lo"]), int(src["expert_count"])) for src in sources]
+        maps = {}
+        for scope in ("all", "trainable"):
+            plans = build_weight_map_multi(self.full_cfg, srcs, self.layout, self.tp_rank, self.tp, scope, primary)
+            maps[scope] = [(pl, descs_tensor(pl, self.device) if self.device.type == "cuda" and pl else None)
+                           for pl in plans]
+        self._weight_maps = maps
+        self._weight_src = [(src.get("tensor"), src.get("addr")) for src in sources]
 
     def pull_weights(self, scope: str = "all") -> int:
         """Copy this engine's slice of the registered trainer buffer into its weights (every TP rank
@@ -392,16 +407,20 @@ class GenerationEngine:
 
         if self._weight_src is None:
             raise RuntimeError("set_weight_source() was not called")
-        descs, descs_d = self._weight_maps[scope]
-        tensor, addr = self._weight_src
         dst = self.model.params
-        if addr is not None:
-            with torch.cuda.device(self.device):
-                ops.weight_pull(descs_d, addr, dst)
-                torch.cuda.synchronize(self.device)
-        else:
-            apply_map_torch(tensor, dst, descs)
-        return map_bytes(descs, dst.element_size())
+        nbytes = 0
+        for (descs, descs_d), (tensor, addr) in zip(self._weight_maps[scope], self._weight_src):
+            if not descs:
+                continue
+            if addr is not None:
+                with torch.cuda.device(self.device):
+                    ops.weight_pull(descs_d, addr, dst)
+            else:
+                apply_map_torch(tensor, dst, descs)
+            nbytes += map_bytes(descs, dst.element_size())
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        return nbytes
 
     def get_stats(self) -> Dict[str, Any]:
         with self._lock:

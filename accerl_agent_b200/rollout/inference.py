@@ -186,11 +186,8 @@ class InferenceService:
         return self.get_stats()
 
 
-def attach_weight_source(engine: GenerationEngine, args, device: torch.device, handle, opened: List[int]) -> int:
-    """Open a trainer's exported parameter handle on ``device`` and register it with ``engine``."""
-    from ..models.transformer import ParamLayout
-
-    src_layout = ParamLayout.build(engine.full_cfg, args.train_mode, pad_to=args.fsdp_world_size)
+def _open_handle(handle, device: torch.device, opened: List[int]):
+    """Map one exported trainer buffer on ``device``: returns ``(tensor, addr, numel)``."""
     if isinstance(handle, dict) and handle.get("kind") == "cuda-ipc":
         from .. import ops
         from ..ops._ext import native
@@ -209,14 +206,39 @@ def attach_weight_source(engine: GenerationEngine, args, device: torch.device, h
                 rc, got = ext.peer_read(addr, len(probe))
                 if rc != 0 or bytes(got) != probe:
                     raise RuntimeError("the trainer's parameter mapping is not readable or holds other data")
-        numel = int(handle["numel"])
-        if numel < src_layout.total_numel:
-            raise ValueError("trainer parameter buffer is smaller than the trainer layout")
-        engine.set_weight_source(src_layout, addr=addr)
-        return numel
+        return None, addr, int(handle["numel"])
     fn, fargs = handle["reduce"] if isinstance(handle, dict) else handle
     tensor = fn(*fargs)
-    if tensor.numel() < src_layout.total_numel:
-        raise ValueError("trainer parameter buffer is smaller than the trainer layout")
-    engine.set_weight_source(src_layout, tensor=tensor)
-    return int(tensor.numel())
+    return tensor, None, int(tensor.numel())
+
+
+def attach_weight_source(engine: GenerationEngine, args, device: torch.device, handle, opened: List[int]) -> int:
+    """Open a trainer's exported parameter handle on ``device`` and register it with ``engine``. A list
+    of handles (one per trainer rank, from expert-partitioned trainers) registers every buffer: routed
+    experts are pulled from their owner, the rest from trainer ``tp_rank % len(handles)``."""
+    from ..models.transformer import ParamLayout
+
+    handles = handle if isinstance(handle, list) else [handle]
+    cfg = engine.full_cfg
+    srcs, total = [], 0
+    for h in handles:
+        part = bool(isinstance(h, dict) and h.get("partition"))
+        if part:
+            from ..parallel.expert_parallel import expert_partition
+
+            cfg_t = expert_partition(cfg, int(h["trainer_rank"]), int(h["world"]))
+        else:
+            cfg_t = cfg
+        layout = ParamLayout.build(cfg_t, args.train_mode, pad_to=args.fsdp_world_size, experts_last=part)
+        tensor, addr, numel = _open_handle(h, device, opened)
+        if numel < layout.total_numel:
+            raise ValueError("trainer parameter buffer is smaller than the trainer layout")
+        srcs.append({"layout": layout, "tensor": tensor, "addr": addr,
+                     "expert_lo": cfg_t.expert_offset if part else 0,
+                     "expert_count": cfg_t.local_experts if part else cfg.num_experts})
+        total += numel
+    if len(srcs) == 1 and srcs[0]["expert_count"] == cfg.num_experts:
+        engine.set_weight_source(srcs[0]["layout"], tensor=srcs[0]["tensor"], addr=srcs[0]["addr"])
+    else:
+        engine.set_weight_sources(srcs, primary=engine.tp_rank % len(srcs))
+    return total

@@ -124,6 +124,46 @@ def build_weight_map(cfg: ModelConfig, src_layout, dst_layout, tp_rank: int = 0,
     return coalesce(out)
 
 
+def build_weight_map_multi(cfg: ModelConfig, sources, dst_layout, tp_rank: int = 0, tp_size: int = 1,
+                           scope: str = "all", primary: int = 0) -> List[List[CopyDesc]]:
+    """Copy plans from several trainer buffers: ``sources`` lists ``(src_layout, expert_lo,
+    expert_count)`` per trainer (expert-partitioned trainers hold experts [lo, lo + count) only;
+    ``count = num_experts`` for a full copy). Routed experts come from whichever trainer owns them;
+    everything else from ``sources[primary]``. Returns one plan per source (possibly empty)."""
+    from ..models.transformer import is_expert_param
+
+    plans: List[List[CopyDesc]] = [[] for _ in sources]
+    p_layout = sources[primary][0]
+    for name, s in p_layout.slots.items():
+        if scope == "trainable" and not s.trainable:
+            continue
+        if is_expert_param(name):
+            continue
+        d = dst_layout.slots.get(name)
+        if d is None:
+            raise KeyError(f"engine layout has no parameter {name}")
+        for so, sl, do, dl, rows, cols in _slot_copies(name, s.shape, cfg, tp_rank, tp_size):
+            plans[primary].append(CopyDesc(s.offset + so, sl, d.offset + do, dl, rows, cols))
+    E = cfg.num_experts
+    if E:
+        el = E // tp_size if tp_size > 1 else E
+        want_lo, want_hi = tp_rank * el if tp_size > 1 else 0, (tp_rank + 1) * el if tp_size > 1 else E
+        for t, (layout, lo, cnt) in enumerate(sources):
+            a, b = max(want_lo, lo), min(want_hi, lo + cnt)
+            if a >= b:
+                continue
+            for name, s in layout.slots.items():
+                if not is_expert_param(name) or (scope == "trainable" and not s.trainable):
+                    continue
+                d = dst_layout.slots.get(name)
+                if d is None:
+                    raise KeyError(f"engine layout has no parameter {name}")
+                per = s.numel // s.shape[0]
+                n = (b - a) * per
+                plans[t].append(CopyDesc(s.offset + (a - lo) * per, n, d.offset + (a - want_lo) * per, n, 1, n))
+    return [coalesce(pl) for pl in plans]
+
+
 def coalesce(descs: List[CopyDesc]) -> List[CopyDesc]:
     """Merge copies that are contiguous in both buffers into single 1-D copies (identical layouts
     collapse to one copy per contiguous run)."""

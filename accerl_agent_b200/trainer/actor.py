@@ -79,10 +79,16 @@ class TrainerActor:
     def export_weights_handle(self):
         """Handle that lets another process map this rank's flat bf16 parameters (a CUDA IPC handle of
         the allocation plus the buffer's offset on GPU, a shared-memory handle on CPU). Every rank
-        holds the full compute copy after each optimizer step."""
+        holds the full compute copy after each optimizer step, except for routed experts under
+        expert-partitioned storage (the handle then says which rank of how many it is)."""
         from torch.multiprocessing.reductions import reduce_tensor
 
         params = self.worker.model.params
+        mcfg = self.worker.model.cfg
+        part = {}
+        if mcfg.local_experts is not None and mcfg.local_experts != mcfg.num_experts:
+            # expert-partitioned storage: the engine needs every rank's buffer and where its experts sit
+            part = {"partition": True, "trainer_rank": self.worker.rank, "world": self.worker.fsdp_world_size}
         if params.is_cuda:
             from ..ops._ext import native
 
@@ -92,8 +98,8 @@ class TrainerActor:
                 raise RuntimeError(f"cudaIpcGetMemHandle failed with code {rc}")
             probe = bytes(params[:8].view(torch.uint8).cpu().numpy().tobytes())
             return {"kind": "cuda-ipc", "handle": bytes(handle), "offset": int(offset), "numel": params.numel(),
-                    "device": params.device.index, "probe": probe}
-        return {"kind": "torch", "reduce": reduce_tensor(params), "numel": params.numel()}
+                    "device": params.device.index, "probe": probe, **part}
+        return {"kind": "torch", "reduce": reduce_tensor(params), "numel": params.numel(), **part}
 
     def synchronize(self) -> None:
         if self.worker.device.type == "cuda":

@@ -46,6 +46,7 @@ from ..models.config import resolve_model_config
 from ..models.hf_io import load_hf_checkpoint, save_hf_checkpoint, vllm_weight_metadata
 from ..models.transformer import build_model
 from ..parallel.fsdp import ShardedAdamW, dist_ready
+from ..parallel.expert_parallel import ExpertParallel, expert_partition
 
 
 def set_seed(seed: int) -> None:
@@ -154,7 +155,13 @@ class TrainWorker:
         set_seed(args.seed + rank)
         self.cfg = resolve_model_config(args.model_path)
         self.dtype = pick_dtype(args.dtype, self.device)
-        self.model = build_model(self.cfg, args.train_mode, self.device, self.dtype, pad_to=fsdp_world_size)
+        use_ep = bool(getattr(args, "expert_parallel", False)) and self.cfg.num_experts > 0 and fsdp_world_size > 1
+        # expert-partitioned storage: this rank's parameter buffer, gradients and optimizer state hold
+        # only its routed experts; the replicated part is laid out first and sharded by the optimizer
+        self.expert_partitioned = use_ep and getattr(args, "expert_storage", "partitioned") == "partitioned"
+        model_cfg = expert_partition(self.cfg, rank, fsdp_world_size) if self.expert_partitioned else self.cfg
+        self.model = build_model(model_cfg, args.train_mode, self.device, self.dtype, pad_to=fsdp_world_size,
+                                 experts_last=self.expert_partitioned)
         self.model.gradient_checkpointing = bool(args.gradient_checkpointing)
         if os.path.isdir(args.model_path) and any(
             f.endswith(".safetensors") for f in os.listdir(args.model_path)
@@ -165,9 +172,7 @@ class TrainWorker:
         if self.model.layout.trainable_numel == 0:
             raise RuntimeError(f"No trainable parameters found for mode: {args.train_mode}")
         self.optimizer = ShardedAdamW(self.model, lr=args.learning_rate, weight_decay=args.weight_decay)
-        if getattr(args, "expert_parallel", False) and self.cfg.num_experts > 0 and fsdp_world_size > 1:
-            from ..parallel.expert_parallel import ExpertParallel
-
+        if use_ep:
             if getattr(args, "train_packing", "padded") == "varlen" and args.train_token_budget:
                 max_tokens = int(args.train_token_budget)
             else:

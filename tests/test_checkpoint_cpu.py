@@ -7,6 +7,7 @@ import torch
 from accerl_agent_b200.core.config import make_args
 from accerl_agent_b200.core.sample import RLSample
 from accerl_agent_b200.replay import ReplayBuffer
+from accerl_agent_b200.models.hf_io import load_hf_checkpoint, save_hf_checkpoint
 from accerl_agent_b200.trainer.worker import TrainWorker
 
 
@@ -50,3 +51,39 @@ def test_weights_only_checkpoint_restores_parameters(tmp_path):
     b.load_checkpoint(str(tmp_path / "w"))
     assert b.optimizer_step == 1
     torch.testing.assert_close(b.model.params, a.model.params)
+
+
+def test_expert_partitioned_checkpoint_round_trip(tmp_path):
+    """Two ranks holding disjoint expert ranges write one HF checkpoint (replicated shards + one expert
+    file per rank + an index naming every expert); it loads into the unpartitioned model and back into
+    each partition."""
+    from accerl_agent_b200.models.config import get_preset
+    from accerl_agent_b200.models.transformer import build_model
+    from accerl_agent_b200.parallel.expert_parallel import expert_partition
+
+    cfg = get_preset("tiny-qwen2")
+    cfg.vocab_size, cfg.model_type, cfg.num_experts, cfg.num_experts_per_tok = 512, "qwen2_moe", 5, 2
+    cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size = 64, 96
+    full = build_model(cfg, "full", torch.device("cpu"), torch.float32)
+    full.init_weights(seed=7)
+    parts = []
+    for r in range(2):
+        m = build_model(expert_partition(cfg, r, 2), "full", torch.device("cpu"), torch.float32, pad_to=2,
+                        experts_last=True)
+        m.init_weights(seed=7)
+        parts.append(m)
+    for r, m in enumerate(parts):
+        written = save_hf_checkpoint(m, str(tmp_path), rank=r, world=2)
+        assert f"model-experts-{r + 1:05d}-of-00002.safetensors" in written
+    back = build_model(cfg, "full", torch.device("cpu"), torch.float32)
+    load_hf_checkpoint(back, str(tmp_path))
+    torch.testing.assert_close(back.params, full.params)
+    for r in range(2):
+        pcfg = expert_partition(cfg, r, 2)
+        m = build_model(pcfg, "full", torch.device("cpu"), torch.float32, pad_to=2, experts_last=True)
+        load_hf_checkpoint(m, str(tmp_path))
+        for name in m.layout.order:
+            want = full.w(name)
+            if name.endswith("experts.gate_up_proj") or name.endswith("experts.down_proj"):
+                want = want[pcfg.expert_offset : pcfg.expert_offset + pcfg.local_experts]
+            torch.testing.assert_close(m.w(name), want)

@@ -181,3 +181,67 @@ def test_rank_that_leaves_fails_the_next_collective_of_the_others():
     assert res[1] == "left"
     assert res[0].startswith("error after"), res
     assert float(res[0].split()[2].rstrip("s:")) < 60.0, res
+
+
+def _ep_worker(rank, port, storage, out):
+    from accerl_agent_b200.core.config import make_args
+    from accerl_agent_b200.replay import ReplayBuffer
+    from accerl_agent_b200.trainer.worker import TrainWorker
+
+    try:
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        args = make_args(model_path="tiny-qwen2-moe", train_packing="varlen", train_token_budget=64, max_length=64,
+                         tw_history_token_window=64, batch_size=1, grad_accum_steps=1, device="cpu",
+                         expert_parallel=True, expert_storage=storage, min_replay_size_per_rank=1,
+                         replay_sample_timeout_seconds=5.0, replay_wait_sleep_seconds=0.05, dtype="float32")
+        rb = ReplayBuffer(8)
+        g = torch.Generator().manual_seed(5 + rank)
+        ids = torch.randint(3, 4096, (24,), generator=g).tolist()
+        rb.add_samples([RLSample("grpo", ids, [1] * 24, [-100] * 12 + ids[12:], [-6.0] * 24, 0.5 - rank,
+                                 [0.0] * 24, [-1] * 12 + [0] * 12, [0])])
+        w = TrainWorker(args, rank=rank, fsdp_world_size=2, replay_buffer=rb, device=torch.device("cpu"))
+        w.train_until_next_sync(1)
+        names = [n for n in w.model.layout.order if n.endswith("experts.gate_up_proj")]
+        out.put((rank, (w.expert_partitioned, w.model.cfg.local_experts, w.model.cfg.expert_offset,
+                        int(w.model.params.numel()), w.optimizer_step,
+                        {n: w.model.w(n).detach().numpy().copy() for n in names})))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:
+        out.put((rank, repr(exc)))
+        raise
+
+
+def _run_ep(storage):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, port, storage, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, payload = q.get(timeout=240)
+        assert not isinstance(payload, str), payload
+        res[r] = payload
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    return res
+
+
+def test_trainer_expert_partitioned_storage_matches_replicated():
+    """A trainer run with ``--expert-parallel`` stores only its 3 of 6 experts per rank by default
+    (smaller parameter buffer) and, after one optimizer step, holds exactly the slice of the expert
+    weights that the replicated-storage run holds for the same experts."""
+    part, repl = _run_ep("partitioned"), _run_ep("replicated")
+    for r in range(2):
+        is_part, nloc, lo, numel, steps, experts = part[r]
+        r_part, r_nloc, _, r_numel, r_steps, r_experts = repl[r]
+        assert is_part and not r_part and nloc == 3 and lo == 3 * r and r_nloc is None
+        assert numel < r_numel and steps == r_steps == 1
+        for n, w in experts.items():
+            assert w.shape[0] == 3
+            assert torch.allclose(torch.from_numpy(w), torch.from_numpy(r_experts[n][lo:lo + nloc]),
+                                  atol=1e-6, rtol=1e-5), n

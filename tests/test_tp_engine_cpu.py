@@ -185,3 +185,41 @@ def test_async_loop_with_tp2_engine_cpu(tmp_path):
     assert [r["step"] for r in steps] == [1, 2]
     # the sharded engine samples from the same weights the trainer scores with
     assert all(abs(r["KL/OldNewK3TokenMean"]) < 1e-2 for r in steps)
+
+
+def test_weight_map_from_expert_partitioned_trainers():
+    """An engine rank (TP 1 or 2) filled from trainers that each hold only their experts gets the same
+    weights as from one trainer holding the whole model."""
+    import torch
+
+    from accerl_agent_b200.models.config import get_preset
+    from accerl_agent_b200.models.transformer import ParamLayout, build_model
+    from accerl_agent_b200.parallel.expert_parallel import expert_partition
+    from accerl_agent_b200.rollout.weight_map import (apply_map_torch, build_weight_map, build_weight_map_multi,
+                                                      tp_shard_config)
+
+    cfg = get_preset("tiny-qwen2")
+    cfg.vocab_size, cfg.model_type, cfg.num_experts, cfg.num_experts_per_tok = 512, "qwen2_moe", 6, 2
+    cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size = 64, 96
+    full = build_model(cfg, "full", torch.device("cpu"), torch.float32, pad_to=3)
+    full.init_weights(seed=5)
+    trainers = []
+    for t in range(3):
+        pc = expert_partition(cfg, t, 3)
+        m = build_model(pc, "full", torch.device("cpu"), torch.float32, pad_to=3, experts_last=True)
+        m.init_weights(seed=5)
+        trainers.append((m, pc))
+    for tp in (1, 2):
+        for r in range(tp):
+            scfg = tp_shard_config(cfg, tp)
+            if scfg.local_experts:
+                scfg.expert_offset = r * scfg.local_experts
+            dst_layout = ParamLayout.build(scfg, "full")
+            want = torch.zeros(dst_layout.total_numel)
+            apply_map_torch(full.params, want, build_weight_map(cfg, full.layout, dst_layout, r, tp, "all"))
+            got = torch.zeros(dst_layout.total_numel)
+            srcs = [(m.layout, pc.expert_offset, pc.local_experts) for m, pc in trainers]
+            plans = build_weight_map_multi(cfg, srcs, dst_layout, r, tp, "all", primary=r % 3)
+            for (m, _), plan in zip(trainers, plans):
+                apply_map_torch(m.params, got, plan)
+            assert torch.equal(got, want), (tp, r)
