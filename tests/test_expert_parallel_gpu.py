@@ -46,8 +46,32 @@ def _work(rank, port, model_type, q):
         g = m.grads.clone()
         dist.all_reduce(g)
         out.append((lp.float().cpu(), g.cpu()))
+    # expert-partitioned storage: this rank's buffer holds only its experts
+    from accerl_agent_b200.parallel.expert_parallel import expert_partition
+
+    pcfg = expert_partition(cfg, rank, 2)
+    m = build_model(pcfg, "full", dev, torch.bfloat16, pad_to=2, experts_last=True)
+    m.init_weights(seed=5, std=0.05)
+    m.expert_parallel = ExpertParallel(cfg, max_tokens=1024, device=dev)
+    lp, ctx = m.forward_logprobs(batch, 513)
+    m.backward_from_logprobs(torch.linspace(-1, 1, lp.numel(), device=dev), ctx)
+    rep = m.layout.replicated_numel
+    dist.all_reduce(m.grads[:rep])
+    full = build_model(cfg, "full", dev, torch.bfloat16, pad_to=2)  # layout of the replicated run's grads
+    full.grads.copy_(out[1][1].to(dev))
+    lo, nloc = pcfg.expert_offset, pcfg.local_experts
+    gerr, gmax = 0.0, 0.0
+    for n in m.layout.order:
+        if not m.layout.slots[n].trainable:
+            continue
+        want = full.g(n).float()
+        if ".mlp.experts." in n:
+            want = want[lo:lo + nloc]
+        gerr = max(gerr, float((m.g(n).float() - want).abs().max()))
+        gmax = max(gmax, float(want.abs().max()))
     torch.cuda.synchronize()
-    q.put((rank, out[0][0], out[1][0], (out[0][1], out[1][1]) if rank == 0 else None))
+    q.put((rank, out[0][0], out[1][0], ((out[0][1], out[1][1]) if rank == 0 else None,
+                                        float((lp.float().cpu() - out[1][0]).abs().max()), gerr, gmax)))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -76,6 +100,11 @@ def test_expert_parallel_p2p_matches_local(model_type):
     for r in (0, 1):
         # each expert row sees the same inputs and weights in both paths
         assert (res[r][0] - res[r][1]).abs().max() < 1e-3
-    g_local, g_ep = res[0][2]
+        # partitioned storage: same log-probabilities, and its gradients (replicated part summed over
+        # ranks, local experts as computed) equal the replicated-storage run's for the same tensors
+        _, lp_diff, gerr, gmax = res[r][2]
+        assert lp_diff < 1e-3, lp_diff
+        assert gerr <= 2e-2 * gmax + 1e-4, (gerr, gmax)
+    g_local, g_ep = res[0][2][0]
     err = (g_local - g_ep).abs().max()
     assert err <= 2e-2 * g_local.abs().max() + 1e-4, err
