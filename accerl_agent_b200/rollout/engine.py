@@ -194,9 +194,11 @@ class GenerationEngine:
                 self._tp_ar = TPAllReduce(tp_group, device, rows * cfg.hidden_size, dtype)
         # block 0 is never handed to a sequence: padded rows of captured decode graphs point at it
         self.scratch_block = self.allocator.allocate()
-        # MoE steps synchronise with the host (routing counts) and run eagerly; tensor-parallel steps
-        # are captured only with the peer-memory all-reduce (no NCCL inside graphs)
-        self.use_cuda_graphs = (use_cuda_graphs and device.type == "cuda" and not cfg.is_moe
+        # MoE layers run the device-side routing layout (no host synchronisation), so single-GPU MoE
+        # decode steps are captured like dense ones (tensor-parallel MoE engines stay eager);
+        # tensor-parallel steps are captured only with the peer-memory all-reduce (no NCCL inside graphs)
+        self.use_cuda_graphs = (use_cuda_graphs and device.type == "cuda"
+                                and (not cfg.is_moe or (dtype == torch.bfloat16 and self.tp == 1))
                                 and (self.tp == 1 or self._tp_ar is not None))
         self._graphs: Dict[Any, Any] = {}
         self._graph_pool = None

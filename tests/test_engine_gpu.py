@@ -56,3 +56,38 @@ def test_engine_greedy_and_logprobs_match_recompute():
             assert row[t] >= row.max() - 0.05
             assert abs(o.outputs[0].logprobs[j][t] - row[t].item()) < 0.05
     assert eng.allocator.hits > 0
+
+
+def test_moe_engine_decode_graphs_match_eager():
+    """MoE decode steps captured in CUDA graphs (device-side routing layout, grouped expert GEMMs,
+    router kernel) give the tokens and log-probabilities of the eager engine."""
+    cfg = small()
+    cfg.model_type = "qwen2_moe"
+    cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size = 8, 2, 256
+    cfg.shared_expert_intermediate_size = 384
+    m = build_model(cfg, "full", torch.device("cuda"), torch.bfloat16, with_grads=False)
+    m.init_weights(seed=4, std=0.05)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (20 + 13 * i,), generator=g).tolist() for i in range(11)]
+    greedy = SamplingParams(temperature=0.0, max_tokens=10, logprobs=1, ignore_eos=True)
+    res = []
+    for graphs in (True, False):
+        eng = GenerationEngine(cfg, torch.device("cuda"), params=m.params, num_blocks=512, block_size=16,
+                               max_num_batched_tokens=256, use_cuda_graphs=graphs)
+        assert eng.use_cuda_graphs == graphs
+
+        async def run():
+            outs = await asyncio.gather(*[collect(eng, p, greedy, f"m{i}") for i, p in enumerate(prompts)])
+            await eng.shutdown()
+            return outs
+
+        outs = asyncio.run(run())
+        if graphs:
+            assert len(eng._graphs) > 0
+        res.append([(list(o.outputs[0].token_ids), [list(d.values())[0] for d in o.outputs[0].logprobs])
+                    for o in outs])
+    for (tok, lp), (tok_e, lp_e) in zip(*res):
+        assert len(tok) == 10
+        assert tok[0] == tok_e[0] and abs(lp[0] - lp_e[0]) < 0.02
+        agree = sum(a == b for a, b in zip(tok, tok_e)) / len(tok)
+        assert agree >= 0.8, (tok, tok_e)
