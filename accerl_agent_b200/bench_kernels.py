@@ -221,7 +221,7 @@ def profile_case(kind: str):
         tables = torch.arange(nb, device=dev, dtype=torch.int32).view(B, L // bs)
         lens = torch.full((B,), L, device=dev, dtype=torch.int32)
         q = torch.randn(B, Hq * D, device=dev).bfloat16()
-        for impl in (1, 2):  # the CUDA-core and the tensor-core kernels
+        for impl in (1, 2, 3):  # the CUDA-core and both tensor-core kernels
             ops.paged_decode(q, kc, vc, tables, lens, Hq, Hkv, 1.0 / D ** 0.5, num_splits=4, impl=impl)
         knew = torch.randn(B, Hkv * D, device=dev).bfloat16()
         slots = (torch.arange(B, device=dev, dtype=torch.int32) * (L // bs)) * bs
@@ -236,13 +236,14 @@ def profile_case(kind: str):
 
 
 def bench_decode(results):
-    """Paged decode attention of the 1.5B shape (12 q / 2 kv heads): 256 sequences of 1024 and 4096
-    cached tokens; achieved GB/s over the K/V bytes read, for the CUDA-core and tensor-core kernels."""
+    """Paged decode attention: the 1.5B shape (12 q / 2 kv heads; 256 sequences of 1024 and 4096 cached
+    tokens), one KV head of 8 query heads, and the Qwen1.5-MoE shape (16 q / 16 kv heads, 128 x 4096);
+    achieved GB/s over the K/V bytes read, for the CUDA-core kernel and both tensor-core kernels."""
     D, bs = 128, 16
     _, peak_gbs = _peaks()
     # (12, 2): the 1.5B shape, KV heads interleaved in each cached token row; (8, 1): one KV head, so
     # every page of a head is one contiguous 4 KB run
-    for B, L, Hq, Hkv in ((256, 1024, 12, 2), (256, 4096, 12, 2), (256, 4096, 8, 1)):
+    for B, L, Hq, Hkv in ((256, 1024, 12, 2), (256, 4096, 12, 2), (256, 4096, 8, 1), (128, 4096, 16, 16)):
         nb = B * L // bs
         kc = torch.randn(nb, bs, Hkv, D, device="cuda").bfloat16()
         vc = torch.randn(nb, bs, Hkv, D, device="cuda").bfloat16()
@@ -251,7 +252,7 @@ def bench_decode(results):
         q = torch.randn(B, Hq * D, device="cuda").bfloat16()
         nbytes = 2 * B * L * Hkv * D * 2
         entry = {"bytes": nbytes}
-        for tag, impl in (("cuda_core", 1), ("tensor_core", 2)):
+        for tag, impl in (("cuda_core", 1), ("tensor_core", 2), ("tensor_core_keys_as_rows", 3)):
             for splits in (1, 4):
                 t = median_ms(lambda: ops.paged_decode(q, kc, vc, tables, lens, Hq, Hkv, 1.0 / D ** 0.5,
                                                        num_splits=splits, impl=impl))

@@ -535,9 +535,10 @@ def adamw_step(master, m, v, grad, param_bf16, sumsq, lr, beta1, beta2, eps, wei
 # ------------------------------------------------------------------------------------------------
 def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads, scale, num_splits=1, out=None,
                  impl: int = 0):
-    """q: [S, Hq*D] -> [S, Hq*D]. ``impl``: 0 = the tensor-core kernel where the shape allows it (head dim
+    """q: [S, Hq*D] -> [S, Hq*D]. ``impl``: 0 = a tensor-core kernel where the shape allows it (head dim
     128, at most 32 query heads per KV head, pages dividing 128 tokens), 1 = the CUDA-core kernel,
-    2 = the tensor-core kernel only."""
+    2 = the tensor-core kernel with the query heads as MMA rows, 3 = the tensor-core kernel with the
+    128 keys of a tile as MMA rows (the default of 0)."""
     S = q.shape[0]
     D = k_cache.shape[-1]
     if q.is_cuda:

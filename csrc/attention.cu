@@ -693,6 +693,362 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ------------------------------------------------------------------------------------------------
+// paged decode with the keys on the TMEM lanes
+// ------------------------------------------------------------------------------------------------
+// Same work items, K/V ring, page gathers and split outputs as paged_decode_tc_kernel, with the
+// products transposed so that the 128 keys of a tile, not the G query heads, are the MMA rows:
+//   S^T [128 keys x NQ]  = K [128 keys x 128 dims] . Q^T     (A: K tile, K-major; B: Q rows, K-major)
+//   O^T [128 dims x NQ] += V^T [128 dims x 128 keys] . P^T   (A: V tile, MN-major; B: P rows, K-major)
+// with NQ = G rounded up to 16 or 32. Thread t of the four softmax warps owns key t of every tile
+// (TMEM lane t) and head dim t of the output, so the exponentials of a tile are spread over all four
+// SM sub-partitions (G per thread instead of 128 per query head in one warp) and the MMAs are NQ wide
+// instead of 128. The per-head tile maximum is exchanged through shared memory once per tile; the
+// sums stay per thread until the item ends. Rescaling stays lazy (only when the maximum grows by more
+// than 2^8), as in the tile-per-head kernel.
+template <int NQ>
+__global__ void __launch_bounds__(192, 1)
+    paged_decode_tq_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                           const DecodeTcParams p) {
+  constexpr int kQChunk = NQ * 128;  // NQ rows x 64 bf16 (one 128-byte swizzled column chunk)
+  constexpr int kQBytes = 2 * kQChunk;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kDecStages * kTileBytes;
+  uint8_t* sQ = sV + kDecStages * kTileBytes;
+  uint8_t* sP = sQ + kQBytes;                                   // [2][NQ rows x 128 keys]
+  float* s_max = reinterpret_cast<float*>(sP + 2 * kQBytes);    // [2][4 warps][NQ]
+  float* s_sum = s_max + 2 * 4 * NQ;                            // [4 warps][NQ]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_sum + 4 * NQ);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;                // [kDecStages]
+  uint64_t* v_full = k_full + kDecStages;     // [kDecStages]
+  uint64_t* kv_empty = v_full + kDecStages;   // [kDecStages]
+  uint64_t* s_full = kv_empty + kDecStages;   // [2] S^T buffers
+  uint64_t* p_full = s_full + 2;              // [2] P buffers
+  uint64_t* o_done = p_full + 2;              // after every PV
+  uint64_t* o_item = o_done + 1;              // after the last PV of an item
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_item + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_items = p.num_seqs * p.Hkv * p.num_splits;
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 128);
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < kDecStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_item, 1);
+    fence_mbar_init();
+  }
+  // rows G..NQ-1 of Q and P stay zero for the whole kernel
+  if (warp < 4)
+    for (int i = threadIdx.x; i < 3 * kQBytes / 16; i += 128) reinterpret_cast<uint4*>(sQ)[i] = make_uint4(0, 0, 0, 0);
+  fence_async_shared();
+  if (warp == 5) tmem_alloc(tmem_slot, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t tS = tbase;           // two S^T buffers: columns [0, NQ) and [NQ, 2 NQ)
+  const uint32_t tO = tbase + 2 * NQ;  // O^T accumulator: columns [2 NQ, 3 NQ)
+
+  if (warp == 4) {
+    // ---------------- TMA producer (as in paged_decode_tc_kernel) ----------------
+    __shared__ int s_blk[kTile / 8];
+    const int bs = p.block_size;
+    const int pages = kTile / bs;
+    int g = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < num_items && ok; it += gridDim.x) {
+      const DecodeItem d = decode_item(p, it);
+      const int* table = p.block_table + static_cast<long long>(d.s) * p.max_blocks;
+      for (int j = 0; j < d.ntiles; ++j, ++g) {
+        int blk = 0;
+        if (lane < pages) {
+          const int tok = d.t0 + j * kTile + lane * bs;
+          blk = tok < d.t1 ? table[tok / bs] : 0;  // pages past the end: any valid block, masked
+        }
+        const int st = g % kDecStages;
+        int good = 1;
+        if (lane == 0)
+          good = mbar_wait(&kv_empty[st], ((g / kDecStages) & 1) ^ 1u, p.status, kStatusTimeoutProducer) ? 1 : 0;
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
+        if (lane < pages) s_blk[lane] = blk;
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+          for (int pg = 0; pg < pages; ++pg) {
+            const int b = s_blk[pg] * bs;
+            uint8_t* dst = sK + st * kTileBytes + pg * bs * 128;
+            tma_load_2d(dst, &tmK, &k_full[st], d.kvh * kHd, b);
+            tma_load_2d(dst + kChunk, &tmK, &k_full[st], d.kvh * kHd + 64, b);
+          }
+          mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+          for (int pg = 0; pg < pages; ++pg) {
+            const int b = s_blk[pg] * bs;
+            uint8_t* dst = sV + st * kTileBytes + pg * bs * 128;
+            tma_load_2d(dst, &tmV, &v_full[st], d.kvh * kHd, b);
+            tma_load_2d(dst + kChunk, &tmV, &v_full[st], d.kvh * kHd + 64, b);
+          }
+        }
+        __syncwarp();  // s_blk is rewritten next tile
+      }
+    }
+    if (lane == 0) {
+      // never leave a bulk copy in flight into shared memory of a finished CTA
+      for (int t = max(0, g - kDecStages); t < g; ++t)
+        mbar_wait(&v_full[t % kDecStages], (t / kDecStages) & 1, nullptr, 0, 20000000ull);
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, NQ, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, NQ, true, false);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      int g = 0, itn = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < num_items && ok; it += gridDim.x) {
+        const DecodeItem d = decode_item(p, it);
+        if (d.ntiles == 0) continue;
+        if (!mbar_wait(q_full, itn & 1, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        for (int j = 0; j <= d.ntiles; ++j) {
+          if (j < d.ntiles) {
+            const int gg = g + j;
+            const int st = gg % kDecStages;
+            const int sb = gg & 1;
+            if (!mbar_wait(&k_full[st], (gg / kDecStages) & 1, p.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            // S^T buffer sb was read by the softmax of tile gg-2 before it released P of that tile,
+            // whose PV this thread issued before this MMA
+            tc_fence_after();
+            const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16(tS + sb * NQ, desc_kmajor(k_addr, kk),
+                        make_sw128_desc(q_addr + (kk >> 2) * kQChunk + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0);
+            umma_commit(&s_full[sb]);
+            if (j == d.ntiles - 1) umma_commit(q_empty);
+          }
+          if (j >= 1) {
+            const int gg = g + j - 1;
+            const int st2 = gg % kDecStages;
+            const int pb = gg & 1;
+            if (!mbar_wait(&p_full[pb], (gg >> 1) & 1, p.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            if (!mbar_wait(&v_full[st2], (gg / kDecStages) & 1, p.status, kStatusTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sV + st2 * kTileBytes);
+            const uint32_t pbuf = p_addr + pb * kQBytes;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16(tO, desc_mnmajor(v_addr, kk),
+                        make_sw128_desc(pbuf + (kk >> 2) * kQChunk + (kk & 3) * 32, 16, 1024), idesc_o,
+                        (j > 1) || (kk > 0));
+            umma_commit(o_done);
+            umma_commit(&kv_empty[st2]);
+          }
+        }
+        if (!ok) break;
+        umma_commit(o_item);
+        g += d.ntiles;
+        ++itn;
+      }
+    }
+  } else {
+    // ---------------- softmax and output: thread t = key t of a tile = head dim t ----------------
+    const int t = threadIdx.x;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;  // this warp's TMEM lane quadrant
+    const int G = p.G;
+    const float sl2 = p.scale_log2;
+    int g = 0, itn = 0;
+    for (int it = blockIdx.x; it < num_items; it += gridDim.x) {
+      const DecodeItem d = decode_item(p, it);
+      // partial index of query head h of this item: ((s * Hq + kvh * G + h) * num_splits + split)
+      const long long pbase = (static_cast<long long>(d.s) * p.Hq + d.kvh * G) * p.num_splits + d.split;
+      const long long pstep = p.num_splits;
+      if (d.ntiles == 0) {
+        for (int h = 0; h < G; ++h) p.part_o[(pbase + h * pstep) * kHd + t] = 0.f;
+        if (t < G) {
+          p.part_ml[(pbase + t * pstep) * 2] = -INFINITY;
+          p.part_ml[(pbase + t * pstep) * 2 + 1] = 0.f;
+        }
+        continue;
+      }
+      if (itn > 0) {
+        const bool good = mbar_wait(q_empty, (itn - 1) & 1, p.status, kStatusTimeoutEpilogue);
+        if (!named_bar_and(1, 128, good)) break;
+      }
+      for (int i = t; i < G * 16; i += 128) {
+        const int r = i >> 4, u = i & 15;
+        const uint4 v = *reinterpret_cast<const uint4*>(p.q + static_cast<long long>(d.s) * p.ldq +
+                                                        (d.kvh * G + r) * kHd + u * 8);
+        *reinterpret_cast<uint4*>(sQ + (u >> 3) * kQChunk + r * 128 + (((u & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_async_shared();
+      mbar_arrive(q_full);
+      float m_used[NQ], lsum[NQ];
+#pragma unroll
+      for (int h = 0; h < NQ; ++h) {
+        m_used[h] = -INFINITY;
+        lsum[h] = 0.f;
+      }
+      bool ok = true;
+      for (int j = 0; j < d.ntiles; ++j) {
+        const int gg = g + j;
+        const int sb = gg & 1;
+        const bool good = mbar_wait(&s_full[sb], (gg >> 1) & 1, p.status, kStatusTimeoutEpilogue);
+        if (!named_bar_and(1, 128, good)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float x[NQ];
+        {
+          uint32_t v[NQ];
+          if constexpr (NQ == 16)
+            tmem_ld16(tS + sb * NQ + lane_off, v);
+          else
+            tmem_ld32(tS + sb * NQ + lane_off, v);
+          tmem_wait_ld();
+          const bool live = d.t0 + j * kTile + t < d.t1;
+#pragma unroll
+          for (int h = 0; h < NQ; ++h) x[h] = live ? __uint_as_float(v[h]) * sl2 : -INFINITY;
+        }
+        // per-head maximum of this tile: warp shuffle, then the four warps through shared memory
+        float* red = s_max + sb * 4 * NQ;
+#pragma unroll
+        for (int h = 0; h < NQ; ++h) {
+          if (h < G) {
+            float m = x[h];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            if (lane == 0) red[warp * NQ + h] = m;
+          }
+        }
+        named_bar_sync(2, 128);
+        bool any = false;
+        float alpha[NQ];
+#pragma unroll
+        for (int h = 0; h < NQ; ++h) {
+          alpha[h] = 1.f;
+          if (h < G) {
+            const float tm = fmaxf(fmaxf(red[h], red[NQ + h]), fmaxf(red[2 * NQ + h], red[3 * NQ + h]));
+            const float m_new = fmaxf(m_used[h], tm);
+            if (m_new > m_used[h] + 8.0f) {
+              alpha[h] = (m_used[h] == -INFINITY) ? 0.f : exp2f(m_used[h] - m_new);
+              m_used[h] = m_new;
+              lsum[h] *= alpha[h];
+              any = true;
+            }
+          }
+        }
+        // P^T rows (one per head) into P buffer sb; the PV that last read it (tile gg-2) completed
+        // before S^T of this tile did
+        uint8_t* prow = sP + sb * kQBytes + (t >> 6) * kQChunk + (t & 7) * 2;
+        const int unit = (t & 63) >> 3;
+#pragma unroll
+        for (int h = 0; h < NQ; ++h) {
+          if (h < G) {
+            const float m_eff = (m_used[h] == -INFINITY) ? 0.f : m_used[h];
+            const float pv = exp2f(x[h] - m_eff);
+            lsum[h] += pv;
+            *reinterpret_cast<__nv_bfloat16*>(prow + h * 128 + ((unit ^ (h & 7)) << 4)) = __float2bfloat16_rn(pv);
+          }
+        }
+        if (j > 0 && any) {
+          // rescale O^T once the previous PV has landed (o_done is at most one completion behind)
+          const bool good2 = mbar_wait(o_done, (gg - 1) & 1, p.status, kStatusTimeoutEpilogue);
+          if (!named_bar_and(1, 128, good2)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t v[NQ];
+          if constexpr (NQ == 16)
+            tmem_ld16(tO + lane_off, v);
+          else
+            tmem_ld32(tO + lane_off, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < NQ; ++h) v[h] = __float_as_uint(__uint_as_float(v[h]) * alpha[h]);
+          if constexpr (NQ == 16)
+            tmem_st16(tO + lane_off, v);
+          else
+            tmem_st32(tO + lane_off, v);
+          tmem_wait_st();
+        }
+        fence_async_shared();
+        tc_fence_before();
+        mbar_arrive(&p_full[sb]);
+      }
+      if (!ok) break;
+      const bool good = mbar_wait(o_item, itn & 1, p.status, kStatusTimeoutEpilogue);
+      if (!named_bar_and(1, 128, good)) break;
+      tc_fence_after();
+      {
+        uint32_t v[NQ];
+        if constexpr (NQ == 16)
+          tmem_ld16(tO + lane_off, v);
+        else
+          tmem_ld32(tO + lane_off, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < NQ; ++h)
+          if (h < G) p.part_o[(pbase + h * pstep) * kHd + t] = __uint_as_float(v[h]);
+      }
+#pragma unroll
+      for (int h = 0; h < NQ; ++h) {
+        if (h < G) {
+          float l = lsum[h];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+          if (lane == 0) s_sum[warp * NQ + h] = l;
+        }
+      }
+      named_bar_sync(2, 128);
+#pragma unroll
+      for (int h = 0; h < NQ; ++h) {
+        if (h < G && t == h) {
+          p.part_ml[(pbase + h * pstep) * 2] = m_used[h] == -INFINITY ? -INFINITY : m_used[h] * kLn2;
+          p.part_ml[(pbase + h * pstep) * 2 + 1] = (s_sum[h] + s_sum[NQ + h]) + (s_sum[2 * NQ + h] + s_sum[3 * NQ + h]);
+        }
+      }
+      tc_fence_before();
+      g += d.ntiles;
+      ++itn;
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 128);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // backward
 // ------------------------------------------------------------------------------------------------
 // 8 elementwise warps (two warpgroups over the column halves), 1 TMA warp, 1 MMA warp
@@ -1223,28 +1579,63 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
 // Tensor-core paged decode (see paged_decode_tc_kernel). k_cache / v_cache: [num_blocks, block_size,
 // Hkv, 128] bf16 of one layer. Writes the per-split partials that accerl_paged_decode_merge combines.
 // Returns -2 when the shape is not supported by this kernel (the caller uses the CUDA-core kernel).
-extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* k_cache, const void* v_cache,
-                                      int num_blocks, const int* block_table, int max_blocks, const int* seq_lens,
-                                      float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv, int block_size,
-                                      int num_splits, float scale, int* status, cudaStream_t s) {
-  if (num_seqs == 0) return 0;
+// Tensor maps and parameters shared by both tensor-core decode kernels; returns 0 or an error code
+// (-1 bad head counts, -2 shape the kernels do not cover, -3 tensor-map failure).
+static int decode_tc_setup(const void* q, long long ldq, const void* k_cache, const void* v_cache, int num_blocks,
+                           const int* block_table, int max_blocks, const int* seq_lens, float* part_o,
+                           float* part_ml, int num_seqs, int Hq, int Hkv, int block_size, int num_splits,
+                           float scale, int* status, CUtensorMap* mk, CUtensorMap* mv, DecodeTcParams* p) {
   if (Hq % Hkv) return -1;
   const int G = Hq / Hkv;
   if (G > 32 || block_size < 8 || block_size > kTile || kTile % block_size || (ldq & 7)) return -2;
   auto fn = encode_fn();
   if (!fn) return -3;
-  CUtensorMap mk, mv;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(Hkv) * kHd, static_cast<cuuint64_t>(num_blocks) * block_size};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(Hkv) * kHd * 2};
   cuuint32_t box[2] = {64, static_cast<cuuint32_t>(block_size)};
   cuuint32_t es[2] = {1, 1};
-  if (fn(&mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(k_cache), dims, strides, box, es,
+  if (fn(mk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(k_cache), dims, strides, box, es,
          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
-      fn(&mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(v_cache), dims, strides, box, es,
+      fn(mv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(v_cache), dims, strides, box, es,
          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return -3;
+  p->q = reinterpret_cast<const __nv_bfloat16*>(q);
+  p->ldq = ldq;
+  p->block_table = block_table;
+  p->max_blocks = max_blocks;
+  p->seq_lens = seq_lens;
+  p->num_seqs = num_seqs;
+  p->Hq = Hq;
+  p->Hkv = Hkv;
+  p->G = G;
+  p->block_size = block_size;
+  p->num_splits = num_splits;
+  p->scale_log2 = scale * kLog2e;
+  p->part_o = part_o;
+  p->part_ml = part_ml;
+  p->status = status;
+  return 0;
+}
+
+static int num_sms() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* k_cache, const void* v_cache,
+                                      int num_blocks, const int* block_table, int max_blocks, const int* seq_lens,
+                                      float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv, int block_size,
+                                      int num_splits, float scale, int* status, cudaStream_t s) {
+  if (num_seqs == 0) return 0;
+  CUtensorMap mk, mv;
+  DecodeTcParams p;
+  const int rc = decode_tc_setup(q, ldq, k_cache, v_cache, num_blocks, block_table, max_blocks, seq_lens, part_o,
+                                 part_ml, num_seqs, Hq, Hkv, block_size, num_splits, scale, status, &mk, &mv, &p);
+  if (rc) return rc;
   constexpr int smem = (1 + 2 * kDecStages) * kTileBytes + 1024 + 256;
   static_assert(smem <= 232448, "shared memory per CTA");
   static bool attr = false;
@@ -1253,26 +1644,38 @@ extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* 
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
-  DecodeTcParams p;
-  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
-  p.ldq = ldq;
-  p.block_table = block_table;
-  p.max_blocks = max_blocks;
-  p.seq_lens = seq_lens;
-  p.num_seqs = num_seqs;
-  p.Hq = Hq;
-  p.Hkv = Hkv;
-  p.G = G;
-  p.block_size = block_size;
-  p.num_splits = num_splits;
-  p.scale_log2 = scale * kLog2e;
-  p.part_o = part_o;
-  p.part_ml = part_ml;
-  p.status = status;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int items = num_seqs * Hkv * num_splits;
-  paged_decode_tc_kernel<<<std::min(items, sms), 192, smem, s>>>(mk, mv, p);
+  paged_decode_tc_kernel<<<std::min(items, num_sms()), 192, smem, s>>>(mk, mv, p);
   return (int)cudaGetLastError();
+}
+
+template <int NQ>
+static int launch_decode_tq(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeTcParams& p, int items,
+                            cudaStream_t s) {
+  // K/V ring + Q + two P buffers + per-warp maxima (two tiles) and sums + barriers, 1 KB alignment slack
+  constexpr int smem = 2 * kDecStages * kTileBytes + 3 * NQ * 256 + 3 * 4 * NQ * 4 + 32 * 8 + 1024;
+  static_assert(smem + 64 <= 232448, "shared memory per CTA");
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(paged_decode_tq_kernel<NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    attr = true;
+  }
+  paged_decode_tq_kernel<NQ><<<std::min(items, num_sms()), 192, smem, s>>>(mk, mv, p);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_paged_decode_tq(const void* q, long long ldq, const void* k_cache, const void* v_cache,
+                                      int num_blocks, const int* block_table, int max_blocks, const int* seq_lens,
+                                      float* part_o, float* part_ml, int num_seqs, int Hq, int Hkv, int block_size,
+                                      int num_splits, float scale, int* status, cudaStream_t s) {
+  if (num_seqs == 0) return 0;
+  CUtensorMap mk, mv;
+  DecodeTcParams p;
+  const int rc = decode_tc_setup(q, ldq, k_cache, v_cache, num_blocks, block_table, max_blocks, seq_lens, part_o,
+                                 part_ml, num_seqs, Hq, Hkv, block_size, num_splits, scale, status, &mk, &mv, &p);
+  if (rc) return rc;
+  const int items = num_seqs * Hkv * num_splits;
+  return p.G <= 16 ? launch_decode_tq<16>(mk, mv, p, items, s) : launch_decode_tq<32>(mk, mv, p, items, s);
 }

@@ -79,6 +79,10 @@ int accerl_paged_decode_tc(const void* q, long long ldq, const void* k_cache, co
                            const int* block_table, int max_blocks, const int* seq_lens, float* part_o, float* part_ml,
                            int num_seqs, int Hq, int Hkv, int block_size, int num_splits, float scale, int* status,
                            cudaStream_t s);
+int accerl_paged_decode_tq(const void* q, long long ldq, const void* k_cache, const void* v_cache, int num_blocks,
+                           const int* block_table, int max_blocks, const int* seq_lens, float* part_o, float* part_ml,
+                           int num_seqs, int Hq, int Hkv, int block_size, int num_splits, float scale, int* status,
+                           cudaStream_t s);
 int accerl_paged_decode_merge(const float* part_o, const float* part_ml, void* out, long long ldo, int num_seqs, int Hq,
                               int num_splits, cudaStream_t s);
 int accerl_paged_decode(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
@@ -529,8 +533,9 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
         "attn_bwd");
 }
 
-// impl: 0 = tensor-core kernel when the shape allows it, else the CUDA-core kernel; 1 = CUDA-core;
-// 2 = tensor-core (error if unsupported).
+// impl: 0 = the keys-on-lanes tensor-core kernel when the shape allows it, else the CUDA-core kernel;
+// 1 = CUDA-core; 2 = tensor-core with the query heads as MMA rows; 3 = tensor-core with the keys as
+// MMA rows (2 and 3: error if unsupported).
 void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                   const at::Tensor& block_table, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& part_o,
                   at::Tensor& part_ml, int64_t Hq, int64_t Hkv, int64_t num_splits, double scale, int64_t impl,
@@ -539,12 +544,12 @@ void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tens
   CHECK_I32(block_table);
   CHECK_I32(seq_lens);
   if (impl != 1 && k_cache.size(-1) == 128) {
-    const int rc = accerl_paged_decode_tc(q.data_ptr(), ld_of(q), k_cache.data_ptr(), v_cache.data_ptr(),
-                                          k_cache.size(0), block_table.data_ptr<int>(), block_table.size(1),
-                                          seq_lens.data_ptr<int>(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
-                                          q.size(0), Hq, Hkv, k_cache.size(1), num_splits, static_cast<float>(scale),
-                                          status_ptr(status), cur_stream());
-    if (rc != -2 || impl == 2) {
+    auto* launch = impl == 2 ? accerl_paged_decode_tc : accerl_paged_decode_tq;
+    const int rc = launch(q.data_ptr(), ld_of(q), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.size(0),
+                          block_table.data_ptr<int>(), block_table.size(1), seq_lens.data_ptr<int>(),
+                          part_o.data_ptr<float>(), part_ml.data_ptr<float>(), q.size(0), Hq, Hkv, k_cache.size(1),
+                          num_splits, static_cast<float>(scale), status_ptr(status), cur_stream());
+    if (rc != -2 || impl >= 2) {
       check(rc, "paged_decode_tc");
       check(accerl_paged_decode_merge(part_o.data_ptr<float>(), part_ml.data_ptr<float>(), out.data_ptr(), ld_of(out),
                                       q.size(0), Hq, num_splits, cur_stream()),
