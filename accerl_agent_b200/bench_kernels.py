@@ -239,11 +239,12 @@ def bench_decode(results):
     """Paged decode attention: the 1.5B shape (12 q / 2 kv heads; 256 sequences of 1024 and 4096 cached
     tokens), one KV head of 8 query heads, and the Qwen1.5-MoE shape (16 q / 16 kv heads, 128 x 4096);
     achieved GB/s over the K/V bytes read, for the CUDA-core kernel and both tensor-core kernels."""
-    D, bs = 128, 16
+    D = 128
     _, peak_gbs = _peaks()
     # (12, 2): the 1.5B shape, KV heads interleaved in each cached token row; (8, 1): one KV head, so
     # every page of a head is one contiguous 4 KB run
-    for B, L, Hq, Hkv in ((256, 1024, 12, 2), (256, 4096, 12, 2), (256, 4096, 8, 1), (128, 4096, 16, 16)):
+    for B, L, Hq, Hkv, bs in ((256, 1024, 12, 2, 16), (256, 4096, 12, 2, 16), (256, 4096, 12, 2, 64),
+                              (256, 4096, 8, 1, 16), (128, 4096, 16, 16, 16), (128, 4096, 16, 16, 64)):
         nb = B * L // bs
         kc = torch.randn(nb, bs, Hkv, D, device="cuda").bfloat16()
         vc = torch.randn(nb, bs, Hkv, D, device="cuda").bfloat16()
@@ -259,7 +260,7 @@ def bench_decode(results):
                 entry[f"{tag}_s{splits}_ms"] = t
                 entry[f"{tag}_s{splits}_gbs"] = nbytes / t / 1e6
                 entry[f"{tag}_s{splits}_frac"] = nbytes / t / 1e6 / peak_gbs
-        results[f"decode/{B}x{L}/hq{Hq}_hkv{Hkv}"] = entry
+        results[f"decode/{B}x{L}/hq{Hq}_hkv{Hkv}/page{bs}"] = entry
         del kc, vc
         torch.cuda.empty_cache()
 

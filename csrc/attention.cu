@@ -763,8 +763,10 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tO = tbase + 2 * NQ;  // O^T accumulator: columns [2 NQ, 3 NQ)
 
   if (warp == 4) {
-    // ---------------- TMA producer (as in paged_decode_tc_kernel) ----------------
-    __shared__ int s_blk[kTile / 8];
+    // ---------------- TMA producer: lane i gathers page i of the tile ----------------
+    // Every lane looks its block id up and issues the four boxes (K and V, two column halves) of its
+    // own page, so the up to 32 bulk copies of a tile leave the warp in parallel instead of one
+    // after another from a single thread.
     const int bs = p.block_size;
     const int pages = kTile / bs;
     int g = 0;
@@ -780,32 +782,27 @@ __global__ void __launch_bounds__(192, 1)
         }
         const int st = g % kDecStages;
         int good = 1;
-        if (lane == 0)
+        if (lane == 0) {
           good = mbar_wait(&kv_empty[st], ((g / kDecStages) & 1) ^ 1u, p.status, kStatusTimeoutProducer) ? 1 : 0;
+          if (good) {
+            mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+            mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+          }
+        }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) {
           ok = false;
           break;
         }
-        if (lane < pages) s_blk[lane] = blk;
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-          for (int pg = 0; pg < pages; ++pg) {
-            const int b = s_blk[pg] * bs;
-            uint8_t* dst = sK + st * kTileBytes + pg * bs * 128;
-            tma_load_2d(dst, &tmK, &k_full[st], d.kvh * kHd, b);
-            tma_load_2d(dst + kChunk, &tmK, &k_full[st], d.kvh * kHd + 64, b);
-          }
-          mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-          for (int pg = 0; pg < pages; ++pg) {
-            const int b = s_blk[pg] * bs;
-            uint8_t* dst = sV + st * kTileBytes + pg * bs * 128;
-            tma_load_2d(dst, &tmV, &v_full[st], d.kvh * kHd, b);
-            tma_load_2d(dst + kChunk, &tmV, &v_full[st], d.kvh * kHd + 64, b);
-          }
+        if (lane < pages) {
+          const int b = blk * bs;
+          uint8_t* dk = sK + st * kTileBytes + lane * bs * 128;
+          uint8_t* dv = sV + st * kTileBytes + lane * bs * 128;
+          tma_load_2d(dk, &tmK, &k_full[st], d.kvh * kHd, b);
+          tma_load_2d(dk + kChunk, &tmK, &k_full[st], d.kvh * kHd + 64, b);
+          tma_load_2d(dv, &tmV, &v_full[st], d.kvh * kHd, b);
+          tma_load_2d(dv + kChunk, &tmV, &v_full[st], d.kvh * kHd + 64, b);
         }
-        __syncwarp();  // s_blk is rewritten next tile
       }
     }
     if (lane == 0) {
