@@ -13,7 +13,7 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from . import reference
-from ._ext import available, check_status, native as _native_module, status_tensor
+from ._ext import available, check_status, debug_checks_enabled, debug_status, native as _native_module, status_tensor
 
 
 # Kernels launched by one call of each binding (the benchmark reports launches per timed step).

@@ -56,3 +56,22 @@ def check_status(device: torch.device) -> None:
     if value != 0:
         t.zero_()
         raise RuntimeError(f"device-side wait timed out (status code {value}); the kernel returned early")
+
+
+DEBUG_CHECK_NAMES = {1: "embedding token id", 2: "KV-cache slot", 3: "KV-cache page id", 4: "MoE row position"}
+
+
+def debug_checks_enabled() -> bool:
+    """True when the loaded extension was built with ``ACCERL_DEBUG_CHECKS=1`` (range checks on every
+    data-dependent index; a failing check is recorded and the access skipped, never trapped)."""
+    return len(native().debug_status(False)) > 0
+
+
+def debug_status(reset: bool = False):
+    """Failed range checks of a debug-checks build, as ``{kernel file: (check name, index)}`` (empty
+    when nothing failed or in a release build). ``reset`` clears the records after reading."""
+    out = {}
+    for unit, code, index in native().debug_status(bool(reset)):
+        if code:
+            out[unit] = (DEBUG_CHECK_NAMES.get(int(code), str(code)), int(index))
+    return out

@@ -371,6 +371,7 @@ struct DecodeTcParams {
   int max_blocks;
   const int* seq_lens;
   int num_seqs, Hq, Hkv, G, block_size, num_splits;
+  int num_blocks;  // pages in the cache (debug-checks build: page ids are range-checked)
   float scale_log2;
   float* part_o;
   float* part_ml;
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(192, 1)
         if (lane < pages) {
           const int tok = d.t0 + j * kTile + lane * bs;
           blk = tok < d.t1 ? table[tok / bs] : 0;  // pages past the end: any valid block, masked
+          if (!ACCERL_DBG_OK(blk >= 0 && blk < p.num_blocks, kDbgPageId, blk)) blk = 0;
         }
         const int st = g % kDecStages;
         int good = 1;
@@ -779,6 +781,7 @@ __global__ void __launch_bounds__(192, 1)
         if (lane < pages) {
           const int tok = d.t0 + j * kTile + lane * bs;
           blk = tok < d.t1 ? table[tok / bs] : 0;  // pages past the end: any valid block, masked
+          if (!ACCERL_DBG_OK(blk >= 0 && blk < p.num_blocks, kDbgPageId, blk)) blk = 0;
         }
         const int st = g % kDecStages;
         int good = 1;
@@ -1609,6 +1612,7 @@ static int decode_tc_setup(const void* q, long long ldq, const void* k_cache, co
   p->G = G;
   p->block_size = block_size;
   p->num_splits = num_splits;
+  p->num_blocks = num_blocks;
   p->scale_log2 = scale * kLog2e;
   p->part_o = part_o;
   p->part_ml = part_ml;
@@ -1676,3 +1680,5 @@ extern "C" int accerl_paged_decode_tq(const void* q, long long ldq, const void* 
   const int items = num_seqs * Hkv * num_splits;
   return p.G <= 16 ? launch_decode_tq<16>(mk, mv, p, items, s) : launch_decode_tq<32>(mk, mv, p, items, s);
 }
+
+ACCERL_DEBUG_EXPORT(attention)

@@ -7,6 +7,9 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <string>
+#include <tuple>
+#include <vector>
 #include <torch/extension.h>
 
 extern "C" {
@@ -34,9 +37,10 @@ int accerl_tp_allreduce(const long long* peer_data, const long long* peer_flags,
                         long long slot_elems, long long n, const void* residual, void* out, int* ctr, int* status,
                         cudaStream_t s);
 int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w, long long T, int k, int H,
-                           const void* residual, const void* shared, const float* sg, void* out, cudaStream_t s);
+                           const void* residual, const void* shared, const float* sg, void* out, long long R,
+                           cudaStream_t s);
 int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* pos, const float* w, long long T, int k,
-                           int H, void* dys, float* dw, cudaStream_t s);
+                           int H, void* dys, float* dw, long long R, cudaStream_t s);
 int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs,
                       float* topw, long long* topi, int* counts, cudaStream_t s);
 int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
@@ -53,8 +57,9 @@ int accerl_rope(void* qkv, const long long* pos, int T, int n_rot_heads, int D, 
                 cudaStream_t s);
 int accerl_swiglu_fwd(const void* gu, void* h, int T, int I, cudaStream_t s);
 int accerl_swiglu_bwd(const void* dh, const void* gu, void* dgu, int T, int I, cudaStream_t s);
-int accerl_embedding_fwd(const long long* ids, const void* table, void* out, int T, int H, cudaStream_t s);
-int accerl_embedding_bwd(const long long* ids, const void* dout, float* grad, int T, int H, cudaStream_t s);
+int accerl_embedding_fwd(const long long* ids, const void* table, void* out, int T, int H, long long V, cudaStream_t s);
+int accerl_embedding_bwd(const long long* ids, const void* dout, float* grad, int T, int H, long long V,
+                         cudaStream_t s);
 int accerl_logsoftmax_label_fwd(const void* logits, long long ld, const long long* labels, float* logprob, float* lse,
                                 float* entropy, int rows, int V, cudaStream_t s);
 int accerl_logsoftmax_label_bwd(void* logits, long long ld, const long long* labels, const float* lse,
@@ -90,13 +95,17 @@ int accerl_paged_decode(const void* q, const void* k_cache, const void* v_cache,
                         int max_blocks_per_seq, int block_size, int num_splits, float scale, long long ldq,
                         long long ldo, cudaStream_t s);
 int accerl_enable_peer_access(int peer);
+int accerl_debug_status_attention(long long* out, int reset);
+int accerl_debug_status_elementwise(long long* out, int reset);
+int accerl_debug_status_moe(long long* out, int reset);
+int accerl_debug_status_rollout(long long* out, int reset);
 int accerl_rs_sumsq(const float* const* peers, int world, int rank, long long shard, float* out, double* sumsq,
                     cudaStream_t s);
 int accerl_adamw_push(float* master, float* m, float* v, const float* grad, void* const* peer_params, int world,
                       int rank, long long shard, const double* sumsq, float lr, float beta1, float beta2, float eps,
                       float weight_decay, float max_norm, float bc1, float bc2_sqrt, cudaStream_t s);
 int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping, int T,
-                          int Hkv, long long ldk, long long ldv, cudaStream_t s);
+                          int Hkv, long long ldk, long long ldv, long long num_slots, cudaStream_t s);
 int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
                          const unsigned long long* seeds, const long long* offsets, long long* out_tokens,
                          float* out_logprobs, float* part, int num_chunks, cudaStream_t s);
@@ -310,7 +319,8 @@ void moe_combine_fwd(const at::Tensor& ys, const at::Tensor& pos, const at::Tens
                                w.data_ptr<float>(), pos.numel() / k, static_cast<int>(k), static_cast<int>(ys.size(1)),
                                residual.has_value() ? residual->data_ptr() : nullptr,
                                shared.has_value() ? shared->data_ptr() : nullptr,
-                               sg.has_value() ? sg->data_ptr<float>() : nullptr, out.data_ptr(), cur_stream()),
+                               sg.has_value() ? sg->data_ptr<float>() : nullptr, out.data_ptr(), ys.size(0),
+                               cur_stream()),
         "moe_combine_fwd");
 }
 
@@ -325,7 +335,7 @@ void moe_combine_bwd(const at::Tensor& dout, const at::Tensor& ys, const at::Ten
               "moe_combine_bwd: layouts");
   check(accerl_moe_combine_bwd(dout.data_ptr(), ys.data_ptr(), reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()),
                                w.data_ptr<float>(), pos.numel() / k, static_cast<int>(k), static_cast<int>(ys.size(1)),
-                               dys.data_ptr(), dw.data_ptr<float>(), cur_stream()),
+                               dys.data_ptr(), dw.data_ptr<float>(), std::min(ys.size(0), dys.size(0)), cur_stream()),
         "moe_combine_bwd");
 }
 
@@ -423,7 +433,7 @@ void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& o
   CHECK_BF16(table);
   TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embedding: contiguous");
   check(accerl_embedding_fwd(reinterpret_cast<long long*>(ids.data_ptr<int64_t>()), table.data_ptr(), out.data_ptr(), ids.numel(), table.size(1),
-                             cur_stream()),
+                             table.size(0), cur_stream()),
         "embedding_fwd");
 }
 
@@ -431,7 +441,7 @@ void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& gr
   CHECK_I64(ids);
   CHECK_F32(grad);
   check(accerl_embedding_bwd(reinterpret_cast<long long*>(ids.data_ptr<int64_t>()), dout.data_ptr(), grad.data_ptr<float>(), ids.numel(),
-                             grad.size(1), cur_stream()),
+                             grad.size(1), grad.size(0), cur_stream()),
         "embedding_bwd");
 }
 
@@ -568,7 +578,8 @@ void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cach
                     const at::Tensor& slot_mapping, int64_t Hkv) {
   CHECK_I32(slot_mapping);
   check(accerl_kv_cache_write(k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
-                              slot_mapping.data_ptr<int>(), k.size(0), Hkv, ld_of(k), ld_of(v), cur_stream()),
+                              slot_mapping.data_ptr<int>(), k.size(0), Hkv, ld_of(k), ld_of(v),
+                              k_cache.size(0) * k_cache.size(1), cur_stream()),
         "kv_cache_write");
 }
 
@@ -649,7 +660,26 @@ void sample_logits(const at::Tensor& logits, const at::Tensor& temperature, cons
 
 }  // namespace
 
+// Debug-checks build records, one (code, index) pair per kernel source file (code 0: no failed check).
+// Returns an empty list in a release build.
+std::vector<std::tuple<std::string, int64_t, int64_t>> debug_status(bool reset) {
+  using Reader = int (*)(long long*, int);
+  const std::pair<const char*, Reader> units[] = {{"attention", accerl_debug_status_attention},
+                                                  {"elementwise", accerl_debug_status_elementwise},
+                                                  {"moe", accerl_debug_status_moe},
+                                                  {"rollout", accerl_debug_status_rollout}};
+  std::vector<std::tuple<std::string, int64_t, int64_t>> out;
+  for (const auto& u : units) {
+    long long rec[2] = {0, 0};
+    const int rc = u.second(rec, reset ? 1 : 0);
+    TORCH_CHECK(rc >= 0, "debug_status: reading the record of ", u.first, " failed");
+    if (rc == 1) out.emplace_back(u.first, rec[0], rec[1]);
+  }
+  return out;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("debug_status", &debug_status, "debug-checks build: (unit, code, index) per kernel file");
   m.doc() = "accerl_agent_b200 sm_100a kernels";
   m.def("last_error", &last_error, "(code, message) of the most recent launch; resets it");
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM");

@@ -26,6 +26,54 @@ enum StatusCode : int {
   kStatusBadArgument = 5,
 };
 
+// ----------------------------------------------------------------------------------------------
+// debug-checks build
+// ----------------------------------------------------------------------------------------------
+// Built with -DACCERL_DEBUG_CHECKS (``ACCERL_DEBUG_CHECKS=1 python setup.py build_ext --inplace``),
+// every data-dependent index (token ids, KV-cache slots, page ids, MoE row positions) is range-checked
+// before it is used. A failing check records (check code, offending index) in its translation unit's
+// debug record, first failure wins, and the access is skipped, so the kernel still returns and the
+// host reads the record with accerl_debug_status_<unit>() (``ops.debug_status()``). The checks never
+// trap. Release builds compile them away (``ACCERL_DBG_OK`` is the constant true).
+enum DebugCheck : int {
+  kDbgEmbeddingId = 1,
+  kDbgKvSlot = 2,
+  kDbgPageId = 3,
+  kDbgMoeRow = 4,
+};
+
+#ifdef ACCERL_DEBUG_CHECKS
+static __device__ unsigned long long g_debug_record[2];
+ACCERL_DEVINL bool debug_fail(int code, long long index) {
+  if (atomicCAS(&g_debug_record[0], 0ull, static_cast<unsigned long long>(code)) == 0ull)
+    g_debug_record[1] = static_cast<unsigned long long>(index);
+  return false;
+}
+#define ACCERL_DBG_OK(cond, code, index) ((cond) ? true : ::accerl::debug_fail((code), (index)))
+// Host reader of this translation unit's record: out = {code, index}; returns 1 in a debug build.
+#define ACCERL_DEBUG_EXPORT(unit)                                                                    \
+  extern "C" int accerl_debug_status_##unit(long long* out, int reset) {                             \
+    unsigned long long r[2] = {0, 0};                                                                \
+    if (cudaMemcpyFromSymbol(r, ::accerl::g_debug_record, sizeof(r)) != cudaSuccess) return -1;      \
+    out[0] = static_cast<long long>(r[0]);                                                           \
+    out[1] = static_cast<long long>(r[1]);                                                           \
+    if (reset) {                                                                                     \
+      const unsigned long long z[2] = {0, 0};                                                        \
+      if (cudaMemcpyToSymbol(::accerl::g_debug_record, z, sizeof(z)) != cudaSuccess) return -1;      \
+    }                                                                                                \
+    return 1;                                                                                        \
+  }
+#else
+#define ACCERL_DBG_OK(cond, code, index) true
+#define ACCERL_DEBUG_EXPORT(unit)                                        \
+  extern "C" int accerl_debug_status_##unit(long long* out, int reset) { \
+    (void)reset;                                                         \
+    out[0] = 0;                                                          \
+    out[1] = 0;                                                          \
+    return 0;                                                            \
+  }
+#endif
+
 // Default deadline for a single barrier wait: 2 seconds of GPU time.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 

@@ -374,9 +374,10 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh, const __
 // Embedding
 // ------------------------------------------------------------------------------------------------
 __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
-                                     __nv_bfloat16* __restrict__ out, int T, int H) {
+                                     __nv_bfloat16* __restrict__ out, int T, int H, long long V) {
   const int t = blockIdx.x;
   const long long id = ids[t];
+  if (!ACCERL_DBG_OK(id >= 0 && id < V, kDbgEmbeddingId, id)) return;
   const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<long long>(t) * H);
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
@@ -384,9 +385,10 @@ __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const __
 
 // grad[ids[t], :] += dout[t, :] in fp32 (atomic; rows of a packed batch rarely collide).
 __global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const __nv_bfloat16* __restrict__ dout,
-                                     float* __restrict__ grad, int T, int H) {
+                                     float* __restrict__ grad, int T, int H, long long V) {
   const int t = blockIdx.x;
   const long long id = ids[t];
+  if (!ACCERL_DBG_OK(id >= 0 && id < V, kDbgEmbeddingId, id)) return;
   float* g = grad + id * H;
   const __nv_bfloat16* d = dout + static_cast<long long>(t) * H;
   for (int c = threadIdx.x * 2; c < H; c += blockDim.x * 2) {
@@ -485,14 +487,18 @@ extern "C" int accerl_swiglu_bwd(const void* dh, const void* gu, void* dgu, int 
   return (int)cudaGetLastError();
 }
 
-extern "C" int accerl_embedding_fwd(const long long* ids, const void* table, void* out, int T, int H, cudaStream_t s) {
+extern "C" int accerl_embedding_fwd(const long long* ids, const void* table, void* out, int T, int H, long long V,
+                                    cudaStream_t s) {
   if (H % 8 || T == 0) return T == 0 ? 0 : -1;
-  embedding_fwd_kernel<<<T, 128, 0, s>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, H);
+  embedding_fwd_kernel<<<T, 128, 0, s>>>(ids, (const __nv_bfloat16*)table, (__nv_bfloat16*)out, T, H, V);
   return (int)cudaGetLastError();
 }
 
-extern "C" int accerl_embedding_bwd(const long long* ids, const void* dout, float* grad, int T, int H, cudaStream_t s) {
+extern "C" int accerl_embedding_bwd(const long long* ids, const void* dout, float* grad, int T, int H, long long V,
+                                    cudaStream_t s) {
   if (T == 0) return 0;
-  embedding_bwd_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)dout, grad, T, H);
+  embedding_bwd_kernel<<<T, 256, 0, s>>>(ids, (const __nv_bfloat16*)dout, grad, T, H, V);
   return (int)cudaGetLastError();
 }
+
+ACCERL_DEBUG_EXPORT(elementwise)

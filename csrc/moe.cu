@@ -15,14 +15,20 @@ __global__ void moe_combine_fwd_kernel(const __nv_bfloat16* __restrict__ ys, con
                                        const float* __restrict__ w, int k, int H,
                                        const __nv_bfloat16* __restrict__ residual,
                                        const __nv_bfloat16* __restrict__ shared, const float* __restrict__ sg,
-                                       __nv_bfloat16* __restrict__ out) {
+                                       __nv_bfloat16* __restrict__ out, long long R) {
   const long long t = blockIdx.x;
   const int nv = H / 8;
   __shared__ long long rows[kMoeMaxK];
   __shared__ float ws[kMoeMaxK];
   if (threadIdx.x < k) {
-    rows[threadIdx.x] = pos[t * k + threadIdx.x];
-    ws[threadIdx.x] = w[t * k + threadIdx.x];
+    long long r = pos[t * k + threadIdx.x];
+    float wr = w[t * k + threadIdx.x];
+    if (!ACCERL_DBG_OK(r >= 0 && r < R, kDbgMoeRow, r)) {
+      r = 0;
+      wr = 0.f;
+    }
+    rows[threadIdx.x] = r;
+    ws[threadIdx.x] = wr;
   }
   __syncthreads();
   const float g = sg ? sg[t] : 0.f;
@@ -73,15 +79,21 @@ __global__ void moe_combine_fwd_kernel(const __nv_bfloat16* __restrict__ ys, con
 
 __global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ ys,
                                        const long long* __restrict__ pos, const float* __restrict__ w, int k, int H,
-                                       __nv_bfloat16* __restrict__ dys, float* __restrict__ dw) {
+                                       __nv_bfloat16* __restrict__ dys, float* __restrict__ dw, long long R) {
   const long long t = blockIdx.x;
   const int nv = H / 8;
   __shared__ long long rows[kMoeMaxK];
   __shared__ float ws[kMoeMaxK];
   __shared__ float red[kMoeMaxK][8];
   if (threadIdx.x < k) {
-    rows[threadIdx.x] = pos[t * k + threadIdx.x];
-    ws[threadIdx.x] = w[t * k + threadIdx.x];
+    long long r = pos[t * k + threadIdx.x];
+    float wr = w[t * k + threadIdx.x];
+    if (!ACCERL_DBG_OK(r >= 0 && r < R, kDbgMoeRow, r)) {
+      r = 0;
+      wr = 0.f;
+    }
+    rows[threadIdx.x] = r;
+    ws[threadIdx.x] = wr;
   }
   __syncthreads();
   float dot[kMoeMaxK];
@@ -214,23 +226,23 @@ using namespace accerl;
 
 extern "C" int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w, long long T, int k, int H,
                                       const void* residual, const void* shared, const float* sg, void* out,
-                                      cudaStream_t s) {
+                                      long long R, cudaStream_t s) {
   if (T <= 0) return 0;
   if (H % 8 || k < 1 || k > kMoeMaxK) return -1;
   const int threads = min(256, max(32, ((H / 8 + 31) / 32) * 32));
   moe_combine_fwd_kernel<<<(unsigned)T, threads, 0, s>>>((const __nv_bfloat16*)ys, pos, w, k, H,
                                                          (const __nv_bfloat16*)residual, (const __nv_bfloat16*)shared,
-                                                         sg, (__nv_bfloat16*)out);
+                                                         sg, (__nv_bfloat16*)out, R);
   return (int)cudaGetLastError();
 }
 
 extern "C" int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* pos, const float* w, long long T,
-                                      int k, int H, void* dys, float* dw, cudaStream_t s) {
+                                      int k, int H, void* dys, float* dw, long long R, cudaStream_t s) {
   if (T <= 0) return 0;
   if (H % 8 || k < 1 || k > kMoeMaxK) return -1;
   const int threads = min(256, max(32, ((H / 8 + 31) / 32) * 32));
   moe_combine_bwd_kernel<<<(unsigned)T, threads, 0, s>>>((const __nv_bfloat16*)dout, (const __nv_bfloat16*)ys, pos, w,
-                                                         k, H, (__nv_bfloat16*)dys, dw);
+                                                         k, H, (__nv_bfloat16*)dys, dw, R);
   return (int)cudaGetLastError();
 }
 
@@ -243,3 +255,5 @@ extern "C" int accerl_moe_router(const float* logits, long long ldl, int T, int 
                                                                        topi, counts);
   return (int)cudaGetLastError();
 }
+
+ACCERL_DEBUG_EXPORT(moe)

@@ -167,10 +167,11 @@ __global__ void paged_decode_merge_kernel(const float* __restrict__ part_o, cons
 
 __global__ void kv_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
                                       __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
-                                      const int* __restrict__ slots, int T, int Hkv, long long ldk, long long ldv) {
+                                      const int* __restrict__ slots, int T, int Hkv, long long ldk, long long ldv,
+                                      long long num_slots) {
   const int t = blockIdx.x;
   const int slot = slots[t];
-  if (slot < 0) return;
+  if (slot < 0 || !ACCERL_DBG_OK(slot < num_slots, kDbgKvSlot, slot)) return;
   const int n16 = Hkv * kDHead / 8;
   const long long dst = static_cast<long long>(slot) * Hkv * kDHead;
   for (int i = threadIdx.x; i < n16; i += blockDim.x) {
@@ -340,11 +341,11 @@ extern "C" int accerl_paged_decode_merge(const float* part_o, const float* part_
 }
 
 extern "C" int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping,
-                                     int T, int Hkv, long long ldk, long long ldv, cudaStream_t s) {
+                                     int T, int Hkv, long long ldk, long long ldv, long long num_slots, cudaStream_t s) {
   if (T == 0) return 0;
   if ((ldk | ldv) & 7) return -1;
   kv_cache_write_kernel<<<T, 128, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (__nv_bfloat16*)k_cache,
-                                          (__nv_bfloat16*)v_cache, slot_mapping, T, Hkv, ldk, ldv);
+                                          (__nv_bfloat16*)v_cache, slot_mapping, T, Hkv, ldk, ldv, num_slots);
   return (int)cudaGetLastError();
 }
 
@@ -359,3 +360,5 @@ extern "C" int accerl_sample_logits(const void* logits, long long ld, int rows, 
                                                          out_tokens, out_logprobs);
   return (int)cudaGetLastError();
 }
+
+ACCERL_DEBUG_EXPORT(rollout)

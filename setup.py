@@ -21,6 +21,9 @@ NVCC_FLAGS = [
     "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
     "-U__CUDA_NO_BFLOAT16_OPERATORS__", "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
 ]
+if os.environ.get("ACCERL_DEBUG_CHECKS", "0") not in ("", "0"):
+    # range checks on data-dependent indices; failures are recorded and read with ops.debug_status()
+    NVCC_FLAGS.append("-DACCERL_DEBUG_CHECKS")
 
 setup(
     name="accerl_agent_b200",
