@@ -701,13 +701,15 @@ __global__ void __launch_bounds__(192, 1)
 // products transposed so that the 128 keys of a tile, not the G query heads, are the MMA rows:
 //   S^T [128 keys x NQ]  = K [128 keys x 128 dims] . Q^T     (A: K tile, K-major; B: Q rows, K-major)
 //   O^T [128 dims x NQ] += V^T [128 dims x 128 keys] . P^T   (A: V tile, MN-major; B: P rows, K-major)
-// with NQ = G rounded up to 16 or 32. Thread t of the four softmax warps owns key t of every tile
+// with NQ = G rounded up to 16 or 32; the per-head softmax loops run over GM = G rounded up to a power
+// of two, unrolled without per-head branches so the reductions of all heads overlap (heads G..GM-1
+// have zero Q rows and their results are never written). Thread t of the four softmax warps owns key t of every tile
 // (TMEM lane t) and head dim t of the output, so the exponentials of a tile are spread over all four
 // SM sub-partitions (G per thread instead of 128 per query head in one warp) and the MMAs are NQ wide
 // instead of 128. The per-head tile maximum is exchanged through shared memory once per tile; the
 // sums stay per thread until the item ends. Rescaling stays lazy (only when the maximum grows by more
 // than 2^8), as in the tile-per-head kernel.
-template <int NQ>
+template <int NQ, int GM>
 __global__ void __launch_bounds__(192, 1)
     paged_decode_tq_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                            const DecodeTcParams p) {
@@ -909,9 +911,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_async_shared();
       mbar_arrive(q_full);
-      float m_used[NQ], lsum[NQ];
+      float m_used[GM], lsum[GM];
 #pragma unroll
-      for (int h = 0; h < NQ; ++h) {
+      for (int h = 0; h < GM; ++h) {
         m_used[h] = -INFINITY;
         lsum[h] = 0.f;
       }
@@ -940,29 +942,25 @@ __global__ void __launch_bounds__(192, 1)
         // per-head maximum of this tile: warp shuffle, then the four warps through shared memory
         float* red = s_max + sb * 4 * NQ;
 #pragma unroll
-        for (int h = 0; h < NQ; ++h) {
-          if (h < G) {
-            float m = x[h];
+        for (int h = 0; h < GM; ++h) {
+          float m = x[h];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            if (lane == 0) red[warp * NQ + h] = m;
-          }
+          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+          if (lane == 0) red[warp * NQ + h] = m;
         }
         named_bar_sync(2, 128);
         bool any = false;
-        float alpha[NQ];
+        float alpha[GM];
 #pragma unroll
-        for (int h = 0; h < NQ; ++h) {
+        for (int h = 0; h < GM; ++h) {
           alpha[h] = 1.f;
-          if (h < G) {
-            const float tm = fmaxf(fmaxf(red[h], red[NQ + h]), fmaxf(red[2 * NQ + h], red[3 * NQ + h]));
-            const float m_new = fmaxf(m_used[h], tm);
-            if (m_new > m_used[h] + 8.0f) {
-              alpha[h] = (m_used[h] == -INFINITY) ? 0.f : exp2f(m_used[h] - m_new);
-              m_used[h] = m_new;
-              lsum[h] *= alpha[h];
-              any = true;
-            }
+          const float tm = fmaxf(fmaxf(red[h], red[NQ + h]), fmaxf(red[2 * NQ + h], red[3 * NQ + h]));
+          const float m_new = fmaxf(m_used[h], tm);
+          if (m_new > m_used[h] + 8.0f) {
+            alpha[h] = (m_used[h] == -INFINITY) ? 0.f : exp2f(m_used[h] - m_new);
+            m_used[h] = m_new;
+            lsum[h] *= alpha[h];
+            any = true;
           }
         }
         // P^T rows (one per head) into P buffer sb; the PV that last read it (tile gg-2) completed
@@ -970,13 +968,11 @@ __global__ void __launch_bounds__(192, 1)
         uint8_t* prow = sP + sb * kQBytes + (t >> 6) * kQChunk + (t & 7) * 2;
         const int unit = (t & 63) >> 3;
 #pragma unroll
-        for (int h = 0; h < NQ; ++h) {
-          if (h < G) {
-            const float m_eff = (m_used[h] == -INFINITY) ? 0.f : m_used[h];
-            const float pv = exp2f(x[h] - m_eff);
-            lsum[h] += pv;
-            *reinterpret_cast<__nv_bfloat16*>(prow + h * 128 + ((unit ^ (h & 7)) << 4)) = __float2bfloat16_rn(pv);
-          }
+        for (int h = 0; h < GM; ++h) {
+          const float m_eff = (m_used[h] == -INFINITY) ? 0.f : m_used[h];
+          const float pv = exp2f(x[h] - m_eff);
+          lsum[h] += pv;
+          *reinterpret_cast<__nv_bfloat16*>(prow + h * 128 + ((unit ^ (h & 7)) << 4)) = __float2bfloat16_rn(pv);
         }
         if (j > 0 && any) {
           // rescale O^T once the previous PV has landed (o_done is at most one completion behind)
@@ -993,7 +989,7 @@ __global__ void __launch_bounds__(192, 1)
             tmem_ld32(tO + lane_off, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < NQ; ++h) v[h] = __float_as_uint(__uint_as_float(v[h]) * alpha[h]);
+          for (int h = 0; h < GM; ++h) v[h] = __float_as_uint(__uint_as_float(v[h]) * alpha[h]);
           if constexpr (NQ == 16)
             tmem_st16(tO + lane_off, v);
           else
@@ -1016,21 +1012,19 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(tO + lane_off, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < NQ; ++h)
+        for (int h = 0; h < GM; ++h)
           if (h < G) p.part_o[(pbase + h * pstep) * kHd + t] = __uint_as_float(v[h]);
       }
 #pragma unroll
-      for (int h = 0; h < NQ; ++h) {
-        if (h < G) {
-          float l = lsum[h];
+      for (int h = 0; h < GM; ++h) {
+        float l = lsum[h];
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-          if (lane == 0) s_sum[warp * NQ + h] = l;
-        }
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) s_sum[warp * NQ + h] = l;
       }
       named_bar_sync(2, 128);
 #pragma unroll
-      for (int h = 0; h < NQ; ++h) {
+      for (int h = 0; h < GM; ++h) {
         if (h < G && t == h) {
           p.part_ml[(pbase + h * pstep) * 2] = m_used[h] == -INFINITY ? -INFINITY : m_used[h] * kLn2;
           p.part_ml[(pbase + h * pstep) * 2 + 1] = (s_sum[h] + s_sum[NQ + h]) + (s_sum[2 * NQ + h] + s_sum[3 * NQ + h]);
@@ -1650,7 +1644,7 @@ extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* 
   return (int)cudaGetLastError();
 }
 
-template <int NQ>
+template <int NQ, int GM>
 static int launch_decode_tq(const CUtensorMap& mk, const CUtensorMap& mv, const DecodeTcParams& p, int items,
                             cudaStream_t s) {
   // K/V ring + Q + two P buffers + per-warp maxima (two tiles) and sums + barriers, 1 KB alignment slack
@@ -1659,11 +1653,11 @@ static int launch_decode_tq(const CUtensorMap& mk, const CUtensorMap& mv, const 
   static bool attr = false;
   if (!attr) {
     cudaError_t e =
-        cudaFuncSetAttribute(paged_decode_tq_kernel<NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(paged_decode_tq_kernel<NQ, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     attr = true;
   }
-  paged_decode_tq_kernel<NQ><<<std::min(items, num_sms()), 192, smem, s>>>(mk, mv, p);
+  paged_decode_tq_kernel<NQ, GM><<<std::min(items, num_sms()), 192, smem, s>>>(mk, mv, p);
   return (int)cudaGetLastError();
 }
 
@@ -1678,7 +1672,12 @@ extern "C" int accerl_paged_decode_tq(const void* q, long long ldq, const void* 
                                  part_ml, num_seqs, Hq, Hkv, block_size, num_splits, scale, status, &mk, &mv, &p);
   if (rc) return rc;
   const int items = num_seqs * Hkv * num_splits;
-  return p.G <= 16 ? launch_decode_tq<16>(mk, mv, p, items, s) : launch_decode_tq<32>(mk, mv, p, items, s);
+  if (p.G == 1) return launch_decode_tq<16, 1>(mk, mv, p, items, s);
+  if (p.G == 2) return launch_decode_tq<16, 2>(mk, mv, p, items, s);
+  if (p.G <= 4) return launch_decode_tq<16, 4>(mk, mv, p, items, s);
+  if (p.G <= 8) return launch_decode_tq<16, 8>(mk, mv, p, items, s);
+  if (p.G <= 16) return launch_decode_tq<16, 16>(mk, mv, p, items, s);
+  return launch_decode_tq<32, 32>(mk, mv, p, items, s);
 }
 
 ACCERL_DEBUG_EXPORT(attention)
