@@ -60,7 +60,10 @@ def test_engine_greedy_and_logprobs_match_recompute():
 
 def test_moe_engine_decode_graphs_match_eager():
     """MoE decode steps captured in CUDA graphs (device-side routing layout, grouped expert GEMMs,
-    router kernel) give the tokens and log-probabilities of the eager engine."""
+    router kernel) and the eager engine both produce greedy tokens that are the argmax of a
+    full-sequence recomputation (up to bf16 noise) with matching log-probabilities. The two paths are
+    not compared token for token: the graphs run padded batch buckets, whose GEMM tilings may round
+    differently, and a random small model has near-ties that then flip."""
     cfg = small()
     cfg.model_type = "qwen2_moe"
     cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size = 8, 2, 256
@@ -70,7 +73,6 @@ def test_moe_engine_decode_graphs_match_eager():
     g = torch.Generator().manual_seed(1)
     prompts = [torch.randint(0, cfg.vocab_size, (20 + 13 * i,), generator=g).tolist() for i in range(11)]
     greedy = SamplingParams(temperature=0.0, max_tokens=10, logprobs=1, ignore_eos=True)
-    res = []
     for graphs in (True, False):
         eng = GenerationEngine(cfg, torch.device("cuda"), params=m.params, num_blocks=512, block_size=16,
                                max_num_batched_tokens=256, use_cuda_graphs=graphs)
@@ -84,10 +86,14 @@ def test_moe_engine_decode_graphs_match_eager():
         outs = asyncio.run(run())
         if graphs:
             assert len(eng._graphs) > 0
-        res.append([(list(o.outputs[0].token_ids), [list(d.values())[0] for d in o.outputs[0].logprobs])
-                    for o in outs])
-    for (tok, lp), (tok_e, lp_e) in zip(*res):
-        assert len(tok) == 10
-        assert tok[0] == tok_e[0] and abs(lp[0] - lp_e[0]) < 0.02
-        agree = sum(a == b for a, b in zip(tok, tok_e)) / len(tok)
-        assert agree >= 0.8, (tok, tok_e)
+        for p, o in zip(prompts, outs):
+            toks = o.outputs[0].token_ids
+            assert len(toks) == 10 and o.finished
+            ids = torch.tensor(p + list(toks), device="cuda")
+            logits = m.forward_logits_full(ids, torch.arange(len(ids), device="cuda"),
+                                           torch.tensor([0, len(ids)], dtype=torch.int32, device="cuda"), len(ids))
+            logp = torch.log_softmax(logits.float(), -1)
+            for j, t in enumerate(toks):
+                row = logp[len(p) - 1 + j]
+                assert row[t] >= row.max() - 0.05, (graphs, j)
+                assert abs(o.outputs[0].logprobs[j][t] - row[t].item()) < 0.05, (graphs, j)

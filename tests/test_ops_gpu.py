@@ -355,11 +355,12 @@ def test_attention_backward_fused_inverse_rope():
 
 
 @pytest.mark.parametrize("impl", [1, 2, 3])
-@pytest.mark.parametrize("Hq,Hkv,splits", [(12, 2, 1), (32, 4, 4), (8, 8, 2), (16, 2, 3), (40, 2, 2)])
+@pytest.mark.parametrize("Hq,Hkv,splits", [(12, 2, 1), (32, 4, 4), (8, 8, 2), (16, 2, 3), (40, 2, 2), (4, 2, 1),
+                                           (16, 4, 2)])
 def test_paged_decode_and_cache_write(Hq, Hkv, splits, impl):
     """The three decode kernels (CUDA cores; tensor cores with the query heads, or the keys, as the
     MMA rows, both with TMA page gathers) against the fp32 reference, with lengths that leave empty
-    splits and partial 128-token tiles; GQA groups 1, 6, 8 and 20 (16- and 32-wide transposed MMAs)."""
+    splits and partial 128-token tiles; GQA groups 1, 2, 4, 6, 8 and 20 (16- and 32-wide transposed MMAs)."""
     if impl == 1 and Hq // Hkv not in (1, 2, 4, 6, 8):
         pytest.skip("the CUDA-core kernel is instantiated for GQA groups 1, 2, 4, 6 and 8")
     S, bs, D = 5, 16, 128
