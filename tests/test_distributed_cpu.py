@@ -245,3 +245,69 @@ def test_trainer_expert_partitioned_storage_matches_replicated():
             assert w.shape[0] == 3
             assert torch.allclose(torch.from_numpy(w), torch.from_numpy(r_experts[n][lo:lo + nloc]),
                                   atol=1e-6, rtol=1e-5), n
+
+
+def _ep_resume_worker(rank, port, ckpt, out):
+    from accerl_agent_b200.core.config import make_args
+    from accerl_agent_b200.replay import ReplayBuffer
+    from accerl_agent_b200.trainer.worker import TrainWorker
+
+    def args(**kw):
+        return make_args(model_path="tiny-qwen2-moe", train_packing="varlen", train_token_budget=64, max_length=64,
+                         tw_history_token_window=64, batch_size=1, grad_accum_steps=1, device="cpu", dtype="float32",
+                         expert_parallel=True, min_replay_size_per_rank=1, replay_sample_timeout_seconds=5.0,
+                         replay_wait_sleep_seconds=0.01, learning_rate=1e-3, max_steps=10, **kw)
+
+    def buffer():
+        rb = ReplayBuffer(8)
+        g = torch.Generator().manual_seed(11 + rank)
+        ids = torch.randint(3, 4096, (20,), generator=g).tolist()
+        rb.add_samples([RLSample("grpo", ids, [1] * 20, [-100] * 10 + ids[10:], [-6.0] * 20, 0.6 - rank,
+                                 [0.0] * 20, [-1] * 10 + [0] * 10, [0])])
+        return rb
+
+    try:
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        a = TrainWorker(args(save_optimizer_state=True), rank=rank, fsdp_world_size=2, replay_buffer=buffer(),
+                        device=torch.device("cpu"))
+        a.train_until_next_sync(2)
+        a.save_checkpoint(ckpt, "step2")
+        a.train_until_next_sync(1)
+        b = TrainWorker(args(resume_from=os.path.join(ckpt, "step2")), rank=rank, fsdp_world_size=2,
+                        replay_buffer=buffer(), device=torch.device("cpu"))
+        resumed_step = b.optimizer_step
+        b.train_until_next_sync(1)
+        diff = float((a.model.params - b.model.params).abs().max())
+        out.put((rank, (a.expert_partitioned, resumed_step, a.optimizer_step, b.optimizer_step, diff,
+                        sorted(os.listdir(os.path.join(ckpt, "step2"))))))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:
+        out.put((rank, repr(exc)))
+        raise
+
+
+def test_expert_partitioned_trainer_resumes_the_same_optimisation(tmp_path):
+    """Checkpoint and resume with expert-partitioned storage on 2 gloo ranks: each rank writes its own
+    experts file and optimizer shard (replicated-prefix shard plus its experts' full state); the
+    resumed run's next step equals the uninterrupted run's on every rank."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_ep_resume_worker, args=(r, port, str(tmp_path), q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, payload = q.get(timeout=300)
+        assert not isinstance(payload, str), payload
+        res[r] = payload
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    for r in range(2):
+        part, resumed, sa, sb, diff, files = res[r]
+        assert part and resumed == 2 and sa == sb == 3
+        assert diff < 1e-6, diff
+        assert "model-experts-00002-of-00002.safetensors" in files and "optimizer_rank00001.pt" in files
