@@ -242,7 +242,8 @@ def bench_decode(results):
     D = 128
     _, peak_gbs = _peaks()
     # (12, 2): the 1.5B shape, KV heads interleaved in each cached token row; (8, 1): one KV head, so
-    # every page of a head is one contiguous 4 KB run
+    # every page of a head is one contiguous 4 KB run; (16, 16): the Qwen1.5-MoE shape (one query head
+    # per KV head). 64-token pages show how much the page gathers (TMA boxes per tile) cost.
     for B, L, Hq, Hkv, bs in ((256, 1024, 12, 2, 16), (256, 4096, 12, 2, 16), (256, 4096, 12, 2, 64),
                               (256, 4096, 8, 1, 16), (128, 4096, 16, 16, 16), (128, 4096, 16, 16, 64)):
         nb = B * L // bs
