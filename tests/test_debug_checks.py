@@ -65,3 +65,25 @@ def test_debug_build_records_out_of_range_indices():
     torch.cuda.synchronize()
     assert ops.debug_status(reset=True) == {"rollout": ("KV-cache slot", 64)}
     assert torch.equal(kc.view(64, 256)[7], kv[0])
+
+
+def test_debug_status_decoding_with_a_fake_extension(monkeypatch):
+    """``ops.debug_status`` names the failed check per kernel file and drops files without a failure;
+    ``debug_checks_enabled`` is true only when the extension returns records (a debug build)."""
+    from accerl_agent_b200.ops import _ext
+
+    class Fake:
+        def __init__(self, recs):
+            self.recs, self.resets = recs, 0
+
+        def debug_status(self, reset):
+            self.resets += int(reset)
+            return self.recs
+
+    fake = Fake([("attention", 3, 977), ("elementwise", 0, 0), ("moe", 4, -1), ("rollout", 0, 0)])
+    monkeypatch.setattr(_ext, "native", lambda: fake)
+    assert _ext.debug_checks_enabled()
+    assert _ext.debug_status(reset=True) == {"attention": ("KV-cache page id", 977), "moe": ("MoE row position", -1)}
+    assert fake.resets == 1
+    monkeypatch.setattr(_ext, "native", lambda: Fake([]))
+    assert not _ext.debug_checks_enabled() and _ext.debug_status() == {}
