@@ -22,7 +22,7 @@ import os
 import sys
 import time
 
-BASELINE_PUBLISHED = None  # the reference publishes no numbers
+REFERENCE_PUBLISHED_VALUE = None  # the reference publishes no numbers
 
 MODEL_DESC = "Qwen2.5-1.5B-shape dense (28L, H1536, 12q/2kv heads, I8960, V151936, tied)"
 
@@ -159,7 +159,7 @@ def run_native(a):
             "ms_per_step": round(dev_ms / a.steps, 3),
             "higher_is_better": True,
             "scaling": "weak",
-            "vs_baseline": None if BASELINE_PUBLISHED is None else value / BASELINE_PUBLISHED,
+            "vs_baseline": None if REFERENCE_PUBLISHED_VALUE is None else value / REFERENCE_PUBLISHED_VALUE,
             "dtype": "bf16",
             "data": "synthetic (seeded synthetic text-game episodes, random-init weights)",
             "impl": "native",
