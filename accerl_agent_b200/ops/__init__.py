@@ -569,13 +569,23 @@ def kv_cache_write(k, v, k_cache, v_cache, slot_mapping, n_kv_heads):
     vc[slots] = v[valid].reshape(-1, n_kv_heads, D).to(vc.dtype)
 
 
-def sample(logits, temperature, seeds, offsets, num_chunks: int = 16, generator=None):
-    """Gumbel-max sampling per row; returns (tokens int64, logprob of the sampled token)."""
+def sample(logits, temperature, seeds, offsets, num_chunks: int = 16, generator=None, top_k=None, top_p=None):
+    """Sample one token per row of ``logits`` ([rows, V] bf16 on the GPU).
+
+    ``temperature`` [rows] (<= 0: argmax), optional ``top_k`` [rows] int32 (0: off) and ``top_p``
+    [rows] float32 (1: off). The random stream of row i is keyed by (``seeds[i]``, ``offsets[i]``).
+    Returns (tokens int64, log-probability of each token under the untempered softmax)."""
     if logits.is_cuda:
         rows = logits.shape[0]
         tokens = torch.empty(rows, dtype=torch.long, device=logits.device)
         lps = torch.empty(rows, dtype=torch.float32, device=logits.device)
         part = workspace(logits.device, "sample_part", rows * num_chunks * 4)
-        native().sample_logits(logits, temperature, seeds, offsets, tokens, lps, part, num_chunks)
+        if top_k is not None:
+            top_k = top_k.to(device=logits.device, dtype=torch.int32).contiguous()
+        if top_p is not None:
+            top_p = top_p.to(device=logits.device, dtype=torch.float32).contiguous()
+        native().sample_logits(logits, temperature, seeds, offsets, tokens, lps, part, num_chunks, top_k, top_p)
+        if top_k is not None or top_p is not None:
+            LAUNCHES[0] += 1
         return tokens, lps
-    return reference.gumbel_sample_reference(logits, temperature, generator)
+    return reference.sample_reference(logits, temperature, generator, top_k, top_p)

@@ -155,9 +155,14 @@ def paged_decode(q, k_cache, v_cache, block_table, seq_lens, scale):
     return out.to(q.dtype)
 
 
-def gumbel_sample_reference(logits: torch.Tensor, temperature: torch.Tensor, generator: Optional[torch.Generator] = None):
-    """Sampling with torch RNG (CPU path of the engine): returns (tokens, logprobs of sampled token
-    under the untempered distribution)."""
+def sample_reference(logits: torch.Tensor, temperature: torch.Tensor, generator: Optional[torch.Generator] = None,
+                     top_k: Optional[torch.Tensor] = None, top_p: Optional[torch.Tensor] = None):
+    """Sampling with torch RNG (CPU path of the engine, and the oracle of the device sampler).
+
+    Row i: argmax if temperature <= 0; otherwise softmax(x / T) restricted to the values >= the
+    top_k-th largest (top_k <= 0: no restriction) and then to the nucleus of the renormalised
+    distribution: the tokens, in descending probability, whose preceding cumulative mass is below
+    top_p. Returns (tokens, log-probability of each token under the untempered softmax)."""
     lf = logits.float()
     logp = torch.log_softmax(lf, dim=-1)
     tokens = torch.empty(lf.shape[0], dtype=torch.long, device=lf.device)
@@ -165,9 +170,19 @@ def gumbel_sample_reference(logits: torch.Tensor, temperature: torch.Tensor, gen
         t = float(temperature[i])
         if t <= 0:
             tokens[i] = int(torch.argmax(lf[i]))
-        else:
-            probs = torch.softmax(lf[i] / t, dim=-1)
-            tokens[i] = int(torch.multinomial(probs, 1, generator=generator))
+            continue
+        z = lf[i] / t
+        k = int(top_k[i]) if top_k is not None else 0
+        if 0 < k < z.numel():
+            z = z.masked_fill(z < torch.topk(z, k).values[-1], float("-inf"))
+        probs = torch.softmax(z, dim=-1)
+        p = float(top_p[i]) if top_p is not None else 1.0
+        if p < 1.0:
+            sorted_p, order = torch.sort(probs, descending=True)
+            before = torch.cumsum(sorted_p, 0) - sorted_p
+            kept = torch.zeros_like(probs).scatter_(0, order, sorted_p * (before < p))
+            probs = kept / kept.sum()
+        tokens[i] = int(torch.multinomial(probs, 1, generator=generator))
     return tokens, logp.gather(1, tokens.view(-1, 1)).squeeze(1)
 
 

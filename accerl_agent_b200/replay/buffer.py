@@ -1,8 +1,11 @@
 """Replay shards and rollout statistics.
 
-``ReplayBuffer`` keeps a FIFO ring of ``RLSample`` with ``capacity`` entries; ``sample(n)`` draws
-uniformly *without removal*, so samples are reused until evicted (agent_textworld.py:1689-1727).
-One shard exists per trainer rank and rollout worker ``i`` feeds shard ``i % world``.
+``ReplayBuffer`` is one trainer rank's replay shard: a fixed ring of ``capacity`` sample slots with a
+write cursor. New samples overwrite the oldest ones once the ring is full, and ``sample(n)`` returns
+``min(n, size)`` distinct samples chosen uniformly while leaving them in place, so a sample keeps
+being reused until it is overwritten (the replay semantics of accerl_agent/agent_textworld.py:1689-1727;
+its ``get_stats`` keys are kept so dashboards and logs read the same). Rollout worker ``i`` feeds
+shard ``i % world``.
 
 ``RolloutStats`` keeps sliding windows of episode outcomes and an active-worker count based on a
 last-seen timeout (agent_textworld.py:1634-1686).
@@ -23,48 +26,65 @@ class ReplayBuffer:
     def __init__(self, capacity: int, seed: Optional[int] = None):
         if capacity < 1:
             raise ValueError("capacity must be >= 1")
-        self.samples: deque = deque(maxlen=capacity)
-        self.total_samples_added = 0
-        self.total_samples_sampled = 0
-        self.total_samples_evicted = 0
+        self._ring: List[Optional[RLSample]] = [None] * capacity
+        self._cursor = 0  # slot the next sample is written to
+        self._filled = 0  # occupied slots
+        self._counts = {"added": 0, "drawn": 0, "overwritten": 0}
         self._rng = random.Random(seed)
-        self._lock = threading.Lock()
+        self._mu = threading.Lock()
+
+    @property
+    def capacity(self) -> int:
+        return len(self._ring)
 
     def add_samples(self, samples: List[RLSample]) -> Dict[str, int]:
-        with self._lock:
-            capacity = self.samples.maxlen or 0
-            if capacity > 0:
-                self.total_samples_evicted += max(0, len(self.samples) + len(samples) - capacity)
-            self.samples.extend(samples)
-            self.total_samples_added += len(samples)
-            return self._stats_locked()
+        """Append ``samples`` in order; returns the stats after the write."""
+        cap = len(self._ring)
+        with self._mu:
+            n = len(samples)
+            self._counts["added"] += n
+            self._counts["overwritten"] += max(0, self._filled + n - cap)
+            # only the newest `cap` of this call can survive it
+            for s in samples[max(0, n - cap):]:
+                self._ring[self._cursor] = s
+                self._cursor = (self._cursor + 1) % cap
+            self._filled = min(cap, self._filled + n)
+            return self._stats()
 
     def sample(self, batch_size: int) -> List[RLSample]:
-        with self._lock:
-            if batch_size < 1:
+        """Up to ``batch_size`` distinct stored samples, uniformly at random, without removing them."""
+        with self._mu:
+            k = min(max(batch_size, 0), self._filled)
+            if k == 0:
                 return []
-            count = min(batch_size, len(self.samples))
-            if count == 0:
-                return []
-            out = self._rng.sample(list(self.samples), count)
-            self.total_samples_sampled += len(out)
-            return out
+            cap = len(self._ring)
+            oldest = (self._cursor - self._filled) % cap
+            picks = self._rng.sample(range(self._filled), k)
+            self._counts["drawn"] += k
+            return [self._ring[(oldest + i) % cap] for i in picks]
 
-    def _stats_locked(self) -> Dict[str, int]:
+    def snapshot(self) -> List[RLSample]:
+        """The stored samples, oldest first."""
+        with self._mu:
+            cap = len(self._ring)
+            oldest = (self._cursor - self._filled) % cap
+            return [self._ring[(oldest + i) % cap] for i in range(self._filled)]
+
+    def _stats(self) -> Dict[str, int]:
         return {
-            "size": len(self.samples),
-            "capacity": self.samples.maxlen or 0,
-            "total_samples_added": self.total_samples_added,
-            "total_samples_sampled": self.total_samples_sampled,
-            "total_samples_evicted": self.total_samples_evicted,
+            "size": self._filled,
+            "capacity": len(self._ring),
+            "total_samples_added": self._counts["added"],
+            "total_samples_sampled": self._counts["drawn"],
+            "total_samples_evicted": self._counts["overwritten"],
         }
 
     def get_stats(self) -> Dict[str, int]:
-        with self._lock:
-            return self._stats_locked()
+        with self._mu:
+            return self._stats()
 
     def __len__(self) -> int:
-        return len(self.samples)
+        return self._filled
 
 
 class RolloutStats:

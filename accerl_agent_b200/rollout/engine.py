@@ -8,7 +8,10 @@ It is the rollout-side replacement of the vLLM ``AsyncLLMEngine`` that the refer
   yields cumulative ``RequestOutput`` objects (``.finished``, ``.outputs[0].token_ids``,
   ``.outputs[0].finish_reason``, ``.outputs[0].logprobs`` as ``[{token: logprob}]``);
 * ``pause_generation(mode="abort", clear_cache=True)`` finishes every in-flight request with reason
-  ``"abort"`` and frees (and optionally forgets) the KV cache; ``resume_generation()``;
+  ``"abort"`` and frees (and optionally forgets) the KV cache; ``mode="suspend"`` instead parks every
+  request (KV released, tokens kept) until ``resume_generation(version=v)``, after which it continues
+  under the new weights; every sampled token is tagged with the engine's version
+  (``CompletionOutput.token_versions``);
 * ``collective_rpc("reload_weights", kwargs={"weights_path": ...})`` and ``load_flat_weights`` for
   in-place weight updates (the trainer and engine share the fused flat parameter layout).
 
@@ -16,8 +19,8 @@ One background thread runs the step loop. A step schedules decode tokens of runn
 and then prefill chunks of waiting ones under ``max_num_batched_tokens`` / ``max_num_seqs``, runs one
 forward over the mixed batch (new K/V written straight into their paged slots, prefill queries over
 their cached prefix with the varlen attention kernel, decode queries with the paged decode kernel),
-applies the LM head only to rows that sample, and samples with the fused Gumbel-max kernel, which
-also returns each sampled token's log-probability. Sampled ids come back to the host once per step.
+applies the LM head only to rows that sample, and samples on the device (temperature, top-k,
+top-p; ``csrc/sampler.cu``), which also returns each sampled token's log-probability. Sampled ids come back to the host once per step.
 """
 
 from __future__ import annotations
@@ -49,6 +52,8 @@ class CompletionOutput:
     finish_reason: Optional[str]
     logprobs: Optional[List[Dict[int, float]]]
     text: str = ""
+    # policy version each token was sampled under (the engine's version at that step)
+    token_versions: Optional[List[int]] = None
 
 
 @dataclass
@@ -69,6 +74,7 @@ class _Seq:
     queue: Any
     out: List[int] = field(default_factory=list)
     lps: List[float] = field(default_factory=list)
+    versions: List[int] = field(default_factory=list)
     blocks: List[int] = field(default_factory=list)
     hashes: List[int] = field(default_factory=list)
     num_computed: int = 0
@@ -81,9 +87,10 @@ class _Seq:
     def __post_init__(self) -> None:
         self.toks = list(self.prompt)
 
-    def append(self, tok: int, lp: float) -> None:
+    def append(self, tok: int, lp: float, version: int) -> None:
         self.out.append(tok)
         self.lps.append(lp)
+        self.versions.append(version)
         self.toks.append(tok)
 
     @property
@@ -221,6 +228,7 @@ class GenerationEngine:
         self.running: List[_Seq] = []
         self.by_id: Dict[str, _Seq] = {}
         self.paused = False
+        self.version = 0  # policy version of the weights; tags every sampled token
         self._lock = threading.RLock()  # protects queues and sequence state
         self._step_lock = threading.Lock()  # held for the duration of one engine step
         self._wake = threading.Condition(self._lock)
@@ -228,7 +236,7 @@ class GenerationEngine:
         self._seed_counter = itertools.count(seed * 1_000_003 + 1)
         self.decode_splits = decode_splits
         self.stats = {"generated_tokens": 0, "prompt_tokens_computed": 0, "steps": 0, "preemptions": 0,
-                      "aborted": 0, "finished": 0, "prefill_rows": 0, "decode_rows": 0,
+                      "aborted": 0, "suspended": 0, "finished": 0, "prefill_rows": 0, "decode_rows": 0,
                       # host wall time per step phase: scheduling, building and launching the step, and
                       # completing the previous one (waiting for its samples, appending, stop checks)
                       "t_schedule_s": 0.0, "t_launch_s": 0.0, "t_complete_s": 0.0}
@@ -304,7 +312,10 @@ class GenerationEngine:
                 self._finish(seq, "abort")
 
     async def pause_generation(self, mode: str = "abort", clear_cache: bool = True) -> None:
-        """Stop scheduling; with ``mode='abort'`` every in-flight request ends with reason 'abort'."""
+        """Stop scheduling once the step in flight has completed. ``mode='abort'``: every request
+        ends with reason 'abort'. ``mode='suspend'``: every request is parked (its KV blocks are
+        released, its tokens kept) and continues after ``resume_generation``, recomputing its prompt
+        and tokens so far under whatever weights were loaded meanwhile."""
         def _pause():
             with self._step_lock:
                 self._flush()
@@ -312,13 +323,20 @@ class GenerationEngine:
                 self.paused = True
                 if mode == "abort":
                     self._abort_all("abort")
+                elif mode == "suspend":
+                    for seq in reversed(list(self.running)):
+                        self._preempt(seq)
+                    self.stats["suspended"] += len(self.waiting)
                 if clear_cache:
                     self.allocator.clear_cache()
 
         await asyncio.to_thread(_pause)
 
-    async def resume_generation(self) -> None:
+    async def resume_generation(self, version: Optional[int] = None) -> None:
+        """Resume scheduling; a given ``version`` tags the tokens sampled from now on."""
         with self._lock:
+            if version is not None:
+                self.version = int(version)
             self.paused = False
             self._wake.notify_all()
 
@@ -440,6 +458,7 @@ class GenerationEngine:
             comp = CompletionOutput(
                 0, list(seq.out), seq.finish_reason if finished else None,
                 [{t: lp} for t, lp in zip(seq.out, seq.lps)] if want_lp else None,
+                token_versions=list(seq.versions),
             )
             item = RequestOutput(seq.rid, seq.prompt, [comp], finished)
         try:
@@ -992,7 +1011,10 @@ class GenerationEngine:
             hN, _ = ops.rmsnorm(xs, m.w("model.norm.weight"), cfg.rms_norm_eps)
             logits = ops.linear(hN, m.w(m.lm_head_name))
             if "filter_params" in meta:
-                tokens, lps = _sample_filtered(logits, meta["filter_params"], torch.from_numpy(meta["seeds"]))
+                fp = meta["filter_params"]
+                top_k = torch.tensor([max(int(p.top_k or 0), 0) for p in fp], dtype=torch.int32)
+                top_p = torch.tensor([float(p.top_p) for p in fp], dtype=torch.float32)
+                tokens, lps = ops.sample(logits, temps_d, seeds_d, offs_d, top_k=top_k, top_p=top_p)
             else:
                 tokens, lps = ops.sample(logits, temps_d, seeds_d, offs_d)
             self._slot_tok.index_copy_(0, rowslot_d.index_select(0, rows_d), tokens.to(torch.long))
@@ -1070,7 +1092,7 @@ class GenerationEngine:
                     if not samples:
                         continue
                     seq.pending -= 1
-                    seq.append(int(tok), float(lp))
+                    seq.append(int(tok), float(lp), self.version)
                     self.stats["generated_tokens"] += 1
                     reason = self._stop_reason(seq, int(tok))
                     if reason is not None:
@@ -1099,30 +1121,3 @@ class GenerationEngine:
 def _decode_splits(ctas_per_split: int) -> int:
     """Sequence splits of the paged decode kernel: about 4 CTAs per SM (148 SMs), at most 16."""
     return max(1, min(16, -(-4 * 148 // max(ctas_per_split, 1))))
-
-
-def _sample_filtered(logits: torch.Tensor, params: List[SamplingParams], seeds: torch.Tensor):
-    """top-p / top-k sampling (sort based). Returns tokens and untempered log-probabilities."""
-    lf = logits.float()
-    logp = torch.log_softmax(lf, dim=-1)
-    out = torch.empty(lf.shape[0], dtype=torch.long, device=lf.device)
-    for i, p in enumerate(params):
-        row = lf[i]
-        if p.temperature <= 0:
-            out[i] = torch.argmax(row)
-            continue
-        row = row / p.temperature
-        if p.top_k and p.top_k > 0:
-            kth = torch.topk(row, min(p.top_k, row.numel())).values[-1]
-            row = row.masked_fill(row < kth, float("-inf"))
-        probs = torch.softmax(row, dim=-1)
-        if p.top_p < 1.0:
-            sp, si = torch.sort(probs, descending=True)
-            keep = torch.cumsum(sp, 0) - sp < p.top_p
-            sp = sp * keep
-            probs = torch.zeros_like(probs).scatter_(0, si, sp)
-            probs = probs / probs.sum()
-        g = torch.Generator(device=lf.device)
-        g.manual_seed(int(seeds[i]))
-        out[i] = torch.multinomial(probs, 1, generator=g)
-    return out, logp.gather(1, out.view(-1, 1)).squeeze(1)

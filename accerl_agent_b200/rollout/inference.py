@@ -2,9 +2,10 @@
 over the native engine, plus the trainer->engine weight pull.
 
 ``request_batch(input_ids, infer_max_tokens)`` runs one interruptible request (stop on ``"\\n"``,
-temperature / top-p from the flags, per-token logprobs and versions); ``pause_and_wait_idle`` pauses
-the runner, aborts the engine's in-flight requests with their KV cache cleared and waits until every
-attempt has drained; ``resume_generation(increment_version)`` bumps the policy version.
+temperature / top-p from the flags, per-token logprobs and versions); ``pause_and_wait_idle`` closes
+the runner's gate and parks the engine's in-flight requests with their KV cache cleared once its last
+step has completed; ``resume_generation(increment_version)`` bumps the policy version, which the
+engine then stamps on every token it samples.
 
 Weight sync: a trainer rank exports its flat bf16 parameter buffer once (a CUDA IPC handle, or a
 shared-memory handle on CPU); ``attach_trainer_weights`` maps it into this process (opened on this
@@ -121,14 +122,16 @@ class InferenceService:
         return result
 
     async def pause_and_wait_idle(self) -> None:
+        """Hold back new requests and park the engine's in-flight ones (their tokens are kept; they
+        continue after ``resume_generation`` under the new weights). Returns once the engine has
+        completed its last step, so the weights can be replaced."""
         self.runner.pause()
-        await self.engine.pause_generation(mode="abort", clear_cache=True)
-        await self.runner.wait_for_idle()
+        await self.engine.pause_generation(mode="suspend", clear_cache=True)
 
     async def resume_generation(self, increment_version: bool = False) -> int:
         if increment_version:
             self.runner.version += 1
-        await self.engine.resume_generation()
+        await self.engine.resume_generation(version=self.runner.version)
         self.runner.resume()
         return self.runner.version
 

@@ -1491,12 +1491,7 @@ extern "C" int accerl_attn_fwd(const void* q, const void* k, const void* v, void
   } else if (!attn_map(&mk, k, total_k, Hkv * kHd, ldk) || !attn_map(&mv, v, total_k, Hkv * kHd, ldv)) {
     return -3;
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-    if (e != cudaSuccess) return (int)e;
-    attr = true;
-  }
+  if (cudaError_t e = smem_attr_once<attn_fwd_kernel>(kFwdSmem); e != cudaSuccess) return (int)e;
   AttnFwdParams p;
   p.o = reinterpret_cast<__nv_bfloat16*>(o);
   p.lse = lse;
@@ -1532,12 +1527,7 @@ extern "C" int accerl_attn_bwd(const void* q, const void* k, const void* v, cons
   if (!attn_map(&mq, q, total_tokens, Hq * kHd, ldq) || !attn_map(&mk, k, total_tokens, Hkv * kHd, ldk) ||
       !attn_map(&mv, v, total_tokens, Hkv * kHd, ldv) || !attn_map(&mdo, dout, total_tokens, Hq * kHd, lddo))
     return -3;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem);
-    if (e != cudaSuccess) return (int)e;
-    attr = true;
-  }
+  if (cudaError_t e = smem_attr_once<attn_bwd_kernel>(kBwdSmem); e != cudaSuccess) return (int)e;
   const long long nwarps = (long long)total_tokens * Hq;
   attn_delta_kernel<<<(unsigned)((nwarps * 32 + 255) / 256), 256, 0, s>>>(
       (const __nv_bfloat16*)o, (const __nv_bfloat16*)dout, delta, total_tokens, Hq, ldo, lddo);
@@ -1614,12 +1604,7 @@ static int decode_tc_setup(const void* q, long long ldq, const void* k_cache, co
   return 0;
 }
 
-static int num_sms() {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms;
-}
+static int num_sms() { return device_sm_count(); }
 
 extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* k_cache, const void* v_cache,
                                       int num_blocks, const int* block_table, int max_blocks, const int* seq_lens,
@@ -1633,12 +1618,7 @@ extern "C" int accerl_paged_decode_tc(const void* q, long long ldq, const void* 
   if (rc) return rc;
   constexpr int smem = (1 + 2 * kDecStages) * kTileBytes + 1024 + 256;
   static_assert(smem <= 232448, "shared memory per CTA");
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return (int)e;
-    attr = true;
-  }
+  if (cudaError_t e = smem_attr_once<paged_decode_tc_kernel>(smem); e != cudaSuccess) return (int)e;
   const int items = num_seqs * Hkv * num_splits;
   paged_decode_tc_kernel<<<std::min(items, num_sms()), 192, smem, s>>>(mk, mv, p);
   return (int)cudaGetLastError();
@@ -1650,13 +1630,7 @@ static int launch_decode_tq(const CUtensorMap& mk, const CUtensorMap& mv, const 
   // K/V ring + Q + two P buffers + per-warp maxima (two tiles) and sums + barriers, 1 KB alignment slack
   constexpr int smem = 2 * kDecStages * kTileBytes + 3 * NQ * 256 + 3 * 4 * NQ * 4 + 32 * 8 + 1024;
   static_assert(smem + 64 <= 232448, "shared memory per CTA");
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(paged_decode_tq_kernel<NQ, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return (int)e;
-    attr = true;
-  }
+  if (cudaError_t e = smem_attr_once<paged_decode_tq_kernel<NQ, GM>>(smem); e != cudaSuccess) return (int)e;
   paged_decode_tq_kernel<NQ, GM><<<std::min(items, num_sms()), 192, smem, s>>>(mk, mv, p);
   return (int)cudaGetLastError();
 }

@@ -107,8 +107,9 @@ int accerl_adamw_push(float* master, float* m, float* v, const float* grad, void
 int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping, int T,
                           int Hkv, long long ldk, long long ldv, long long num_slots, cudaStream_t s);
 int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
-                         const unsigned long long* seeds, const long long* offsets, long long* out_tokens,
-                         float* out_logprobs, float* part, int num_chunks, cudaStream_t s);
+                         const int* top_k, const float* top_p, const unsigned long long* seeds,
+                         const long long* offsets, long long* out_tokens, float* out_logprobs, float* part,
+                         int num_chunks, cudaStream_t s);
 }
 
 namespace {
@@ -647,13 +648,25 @@ void adamw_push(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tens
 
 void sample_logits(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& seeds,
                    const at::Tensor& offsets, at::Tensor& out_tokens, at::Tensor& out_logprobs, at::Tensor& part,
-                   int64_t num_chunks) {
+                   int64_t num_chunks, const c10::optional<at::Tensor>& top_k,
+                   const c10::optional<at::Tensor>& top_p) {
   CHECK_BF16(logits);
   CHECK_F32(temperature);
+  const int* tk = nullptr;
+  const float* tp = nullptr;
+  if (top_k.has_value()) {
+    TORCH_CHECK(top_k->scalar_type() == at::kInt && top_k->is_contiguous(), "top_k must be contiguous int32");
+    tk = top_k->data_ptr<int>();
+  }
+  if (top_p.has_value()) {
+    CHECK_F32(*top_p);
+    tp = top_p->data_ptr<float>();
+  }
   check(accerl_sample_logits(logits.data_ptr(), ld_of(logits), logits.size(0), logits.size(1),
-                             temperature.data_ptr<float>(),
-                             reinterpret_cast<const unsigned long long*>(reinterpret_cast<long long*>(seeds.data_ptr<int64_t>())),
-                             reinterpret_cast<long long*>(offsets.data_ptr<int64_t>()), reinterpret_cast<long long*>(out_tokens.data_ptr<int64_t>()),
+                             temperature.data_ptr<float>(), tk, tp,
+                             reinterpret_cast<const unsigned long long*>(seeds.data_ptr<int64_t>()),
+                             reinterpret_cast<long long*>(offsets.data_ptr<int64_t>()),
+                             reinterpret_cast<long long*>(out_tokens.data_ptr<int64_t>()),
                              out_logprobs.data_ptr<float>(), part.data_ptr<float>(), num_chunks, cur_stream()),
         "sample_logits");
 }

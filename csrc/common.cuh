@@ -12,9 +12,51 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #define ACCERL_DEVINL __device__ __forceinline__
 
 namespace accerl {
+
+// ----------------------------------------------------------------------------------------------
+// per-device host-side set-up
+// ----------------------------------------------------------------------------------------------
+// Function attributes (the dynamic shared-memory opt-in) and occupancy answers belong to a device, so
+// a process that drives several GPUs sets them once per device. The flags are atomics: two host
+// threads that race both set the attribute, which is harmless.
+constexpr int kMaxHostDevices = 64;
+
+inline int host_current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+// Opt kernel `Kern` into `bytes` of dynamic shared memory on the current device (once per device).
+template <auto Kern>
+inline cudaError_t smem_attr_once(int bytes) {
+  static std::atomic<unsigned long long> done{0};  // bit d: set on device d
+  const int dev = host_current_device();
+  const unsigned long long bit = (dev >= 0 && dev < kMaxHostDevices) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
+// Number of SMs of the current device (cached per device).
+inline int device_sm_count() {
+  static std::atomic<int> cache[kMaxHostDevices];
+  const int dev = host_current_device();
+  if (dev >= 0 && dev < kMaxHostDevices) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev < 0 ? 0 : dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < kMaxHostDevices) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
 
 // Status codes written to the status word (first writer wins).
 enum StatusCode : int {

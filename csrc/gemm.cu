@@ -739,16 +739,7 @@ bool make_map_2d(CUtensorMap* out, const void* ptr, uint64_t d0, uint64_t d1, ui
   return true;
 }
 
-int num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+int num_sms() { return device_sm_count(); }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool PAIR, bool ROPE = false>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mh,
@@ -757,9 +748,13 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   constexpr int smem_bytes =
       STAGES * GemmSmem<BN, PAIR>::kStageBytes + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(smem_bytes <= 232448, "shared memory per CTA");
-  static int max_clusters = -1;  // per instantiation: clusters of 2 that can be resident at once
+  // per instantiation and device: clusters of 2 that can be resident at once, stored + 1 (0 = not yet known)
+  static std::atomic<int> cluster_cache[kMaxHostDevices];
+  const int dev = host_current_device();
+  if (dev < 0 || dev >= kMaxHostDevices) return -14;
+  int max_clusters = cluster_cache[dev].load(std::memory_order_acquire) - 1;
   if (max_clusters < 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    cudaError_t e = smem_attr_once<gemm_bf16_tcgen05<BN, STAGES, A_MN, B_MN, PAIR, ROPE>>(smem_bytes);
     if (e != cudaSuccess) return static_cast<int>(e);
     if (PAIR) {
       cudaLaunchConfig_t cfg = {};
@@ -781,6 +776,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     } else {
       max_clusters = 0;
     }
+    cluster_cache[dev].store(max_clusters + 1, std::memory_order_release);
   }
   if (!PAIR) {
     int grid = std::min(p.num_tiles, max_ctas > 0 ? max_ctas : num_sms());

@@ -3,9 +3,7 @@
 //    heads of one GQA group so each K/V row is read once per group; partial (o, m, l) per split are
 //    merged by a second kernel.
 //  * KV-cache write of freshly projected K/V rows into their paged slots.
-//  * sampler: one pass over each bf16 logits row computes the log-sum-exp, and the Gumbel-max sample
-//    argmax(logit/T + G) (greedy argmax when T == 0) with a counter-based SplitMix64 noise stream;
-//    the sampled token's log-probability is reported under the untempered distribution.
+// The token sampler is in sampler.cu.
 // Cache layout: k_cache/v_cache [num_blocks, block_size, Hkv, 128] bf16.
 #include "common.cuh"
 
@@ -180,124 +178,6 @@ __global__ void kv_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const
   }
 }
 
-// SplitMix64 (Steele, Lea, Flood 2014) as a counter-based generator.
-__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
-  z += 0x9e3779b97f4a7c15ull;
-  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
-  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
-  return z ^ (z >> 31);
-}
-
-__device__ __forceinline__ float gumbel_noise(uint64_t seed, uint64_t offset, uint32_t idx) {
-  const uint64_t h = splitmix64(seed ^ splitmix64(offset * 0x100000001b3ull + idx));
-  // 24-bit uniform in (0, 1)
-  const float u = (static_cast<float>(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
-  return -__logf(-__logf(u));
-}
-
-// part layout per (row, chunk): [max, sumexp, best_score, best_idx]
-__global__ void sample_partial_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V,
-                                      const float* __restrict__ temperature, const unsigned long long* __restrict__ seeds,
-                                      const long long* __restrict__ offsets, float* __restrict__ part, int num_chunks) {
-  const int row = blockIdx.x, chunk = blockIdx.y;
-  const int per = (((V + num_chunks - 1) / num_chunks) + 7) & ~7;
-  const int c0 = chunk * per, c1 = min(V, c0 + per);
-  const float T = temperature[row];
-  const bool greedy = T <= 0.f;
-  const float invT = greedy ? 1.f : 1.f / T;
-  const uint64_t seed = seeds[row];
-  const uint64_t offset = static_cast<uint64_t>(offsets[row]);
-  const __nv_bfloat16* l = logits + row * ld;
-  float m = -INFINITY, s = 0.f, best = -INFINITY;
-  int best_i = c0;
-  for (int c = c0 + threadIdx.x * 8; c < c1; c += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(l + c);
-    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack_bf16x2(vw[i]);
-      const float xs[2] = {f.x, f.y};
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int idx = c + 2 * i + h;
-        const float x = xs[h];
-        const float mn = fmaxf(m, x);
-        s = s * ((m == -INFINITY) ? 0.f : __expf(m - mn)) + __expf(x - mn);
-        m = mn;
-        const float sc = greedy ? x : x * invT + gumbel_noise(seed, offset, static_cast<uint32_t>(idx));
-        if (sc > best) {
-          best = sc;
-          best_i = idx;
-        }
-      }
-    }
-  }
-  // block reduction
-  __shared__ float sm_m[32], sm_s[32], sm_b[32];
-  __shared__ int sm_i[32];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
-    const float b2 = __shfl_xor_sync(0xffffffffu, best, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, best_i, o);
-    const float mn = fmaxf(m, m2);
-    s = s * ((m == -INFINITY) ? 0.f : __expf(m - mn)) + s2 * ((m2 == -INFINITY) ? 0.f : __expf(m2 - mn));
-    m = mn;
-    if (b2 > best || (b2 == best && i2 < best_i)) {
-      best = b2;
-      best_i = i2;
-    }
-  }
-  const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) {
-    sm_m[w] = m;
-    sm_s[w] = s;
-    sm_b[w] = best;
-    sm_i[w] = best_i;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float M = -INFINITY, S = 0.f, B = -INFINITY;
-    int I = c0;
-    for (int k = 0; k < (blockDim.x >> 5); ++k) {
-      const float mn = fmaxf(M, sm_m[k]);
-      S = S * ((M == -INFINITY) ? 0.f : __expf(M - mn)) + sm_s[k] * ((sm_m[k] == -INFINITY) ? 0.f : __expf(sm_m[k] - mn));
-      M = mn;
-      if (sm_b[k] > B || (sm_b[k] == B && sm_i[k] < I)) {
-        B = sm_b[k];
-        I = sm_i[k];
-      }
-    }
-    float* dst = part + (static_cast<long long>(row) * num_chunks + chunk) * 4;
-    dst[0] = M;
-    dst[1] = S;
-    dst[2] = B;
-    dst[3] = __int_as_float(I);
-  }
-}
-
-__global__ void sample_final_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, const float* __restrict__ part,
-                                    int rows, int num_chunks, long long* __restrict__ out_tokens,
-                                    float* __restrict__ out_logprobs) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= rows) return;
-  float M = -INFINITY, S = 0.f, B = -INFINITY;
-  int I = 0;
-  for (int k = 0; k < num_chunks; ++k) {
-    const float* p = part + (static_cast<long long>(row) * num_chunks + k) * 4;
-    const float mn = fmaxf(M, p[0]);
-    S = S * ((M == -INFINITY) ? 0.f : __expf(M - mn)) + p[1] * ((p[0] == -INFINITY) ? 0.f : __expf(p[0] - mn));
-    M = mn;
-    const int pi = __float_as_int(p[3]);
-    if (p[2] > B || (p[2] == B && pi < I)) {
-      B = p[2];
-      I = pi;
-    }
-  }
-  out_tokens[row] = I;
-  out_logprobs[row] = __bfloat162float(logits[row * ld + I]) - (M + __logf(S));
-}
-
 }  // namespace accerl
 
 using namespace accerl;
@@ -346,18 +226,6 @@ extern "C" int accerl_kv_cache_write(const void* k, const void* v, void* k_cache
   if ((ldk | ldv) & 7) return -1;
   kv_cache_write_kernel<<<T, 128, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (__nv_bfloat16*)k_cache,
                                           (__nv_bfloat16*)v_cache, slot_mapping, T, Hkv, ldk, ldv, num_slots);
-  return (int)cudaGetLastError();
-}
-
-extern "C" int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
-                                    const unsigned long long* seeds, const long long* offsets, long long* out_tokens,
-                                    float* out_logprobs, float* part, int num_chunks, cudaStream_t s) {
-  if (rows == 0) return 0;
-  if (V % 8 || ld % 8) return -1;
-  sample_partial_kernel<<<dim3(rows, num_chunks), 256, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature, seeds,
-                                                               offsets, part, num_chunks);
-  sample_final_kernel<<<(rows + 127) / 128, 128, 0, s>>>((const __nv_bfloat16*)logits, ld, part, rows, num_chunks,
-                                                         out_tokens, out_logprobs);
   return (int)cudaGetLastError();
 }
 

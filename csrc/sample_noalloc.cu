@@ -1,9 +1,10 @@
 // accerl_sample_logits_noalloc: the token sampler for callers that cannot allocate device memory.
 //
 // This entry point has no counterpart in the reference, which samples inside its inference engine.
-// It is the sampler of rollout.cu (one Gumbel-max pass per bf16 logits row, log-probability of the
-// sampled token under the untempered distribution), but it takes no workspace argument and
-// allocates nothing: its per-call scratch is the file-scope device array below.
+// It is the sampler of sampler.cu (per-chunk partial sums, then an inverse-CDF draw per bf16 logits
+// row; log-probability of the sampled token under the untempered distribution; -inf logits allowed),
+// but it takes no workspace argument and allocates nothing: its per-call scratch is the file-scope
+// device array below. The prototype and return codes are declared in accerl_noalloc.h.
 //
 // Who needs it: a host runtime that links this library directly and calls the sampler from its
 // decode loop without a device allocator at hand. Typical cases are serving runtimes that reserve
@@ -16,7 +17,10 @@
 //  * rows <= 1024 per call. The scratch holds 1024 rows x 16 vocabulary chunks x 4 floats
 //    (256 KiB per device, in the module's static device memory). Larger calls are rejected with
 //    ACCERL_NOALLOC_TOO_MANY_ROWS (-30) before anything is launched; split them into batches.
-//  * V and ld must be multiples of 8 (-1 otherwise), as for accerl_sample_logits.
+//  * V and ld must be multiples of 8 and logits 16-byte aligned (ACCERL_NOALLOC_BAD_SHAPE, -1,
+//    otherwise), as for accerl_sample_logits. No top-k / top-p: those rows need accerl_sample_logits.
+//  * The device index must be below 64 (ACCERL_NOALLOC_BAD_DEVICE, -31, otherwise): the per-device
+//    address cache has 64 entries.
 //  * The scratch is shared by every call on a device. Calls that may overlap in time (different
 //    streams without an ordering event between them, or different host threads) race on it: issue
 //    them on one stream, or order them. Its contents persist from call to call; nothing in it has
@@ -29,27 +33,16 @@
 //    code above. On a negative code nothing was launched.
 #include <atomic>
 
-#include "common.cuh"
-
-namespace accerl {
-// defined in rollout.cu
-__global__ void sample_partial_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int V,
-                                      const float* __restrict__ temperature, const unsigned long long* __restrict__ seeds,
-                                      const long long* __restrict__ offsets, float* __restrict__ part, int num_chunks);
-__global__ void sample_final_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, const float* __restrict__ part,
-                                    int rows, int num_chunks, long long* __restrict__ out_tokens,
-                                    float* __restrict__ out_logprobs);
-}  // namespace accerl
+#include "accerl_noalloc.h"
+#include "sampler.cuh"
 
 namespace {
-constexpr int kNoAllocMaxRows = 1024;
+constexpr int kNoAllocMaxRows = ACCERL_NOALLOC_MAX_ROWS;
 constexpr int kNoAllocChunks = 16;
-constexpr int kNoAllocTooManyRows = -30;
-constexpr int kNoAllocBadDevice = -31;
 constexpr int kMaxDevices = 64;
 
-// [row][chunk][max, sumexp, best_score, best_idx]
-static __device__ __align__(256) float g_sampler_scratch[kNoAllocMaxRows * kNoAllocChunks * 4];
+// [row][chunk][max, sumexp, tempered sumexp, argmax index]
+static __device__ __align__(256) float g_sampler_scratch[kNoAllocMaxRows * kNoAllocChunks * accerl::kSamplePartFloats];
 
 std::atomic<float*> g_scratch_addr[kMaxDevices];
 }  // namespace
@@ -59,12 +52,12 @@ extern "C" int accerl_sample_logits_noalloc(const void* logits, long long ld, in
                                             long long* out_tokens, float* out_logprobs, cudaStream_t s) {
   using namespace accerl;
   if (rows == 0) return 0;
-  if (rows < 0 || rows > kNoAllocMaxRows) return kNoAllocTooManyRows;
-  if (V % 8 || ld % 8) return -1;
+  if (rows < 0 || rows > kNoAllocMaxRows) return ACCERL_NOALLOC_TOO_MANY_ROWS;
+  if (V <= 0 || V % 8 || ld % 8 || (reinterpret_cast<uintptr_t>(logits) & 15)) return ACCERL_NOALLOC_BAD_SHAPE;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
-  if (dev < 0 || dev >= kMaxDevices) return kNoAllocBadDevice;
+  if (dev < 0 || dev >= kMaxDevices) return ACCERL_NOALLOC_BAD_DEVICE;
   float* scratch = g_scratch_addr[dev].load(std::memory_order_acquire);
   if (scratch == nullptr) {
     void* p = nullptr;
@@ -73,9 +66,10 @@ extern "C" int accerl_sample_logits_noalloc(const void* logits, long long ld, in
     scratch = static_cast<float*>(p);
     g_scratch_addr[dev].store(scratch, std::memory_order_release);  // same value from every racing thread
   }
-  sample_partial_kernel<<<dim3(rows, kNoAllocChunks), 256, 0, s>>>((const __nv_bfloat16*)logits, ld, V, temperature,
-                                                                   seeds, offsets, scratch, kNoAllocChunks);
-  sample_final_kernel<<<(rows + 127) / 128, 128, 0, s>>>((const __nv_bfloat16*)logits, ld, scratch, rows,
-                                                         kNoAllocChunks, out_tokens, out_logprobs);
+  const auto* lg = static_cast<const __nv_bfloat16*>(logits);
+  sample_partial_kernel<<<dim3(rows, kNoAllocChunks), 256, 0, s>>>(lg, ld, V, temperature, nullptr, nullptr, scratch,
+                                                                   kNoAllocChunks);
+  sample_final_kernel<<<rows, 256, 0, s>>>(lg, ld, V, temperature, nullptr, nullptr, seeds, offsets, scratch,
+                                           kNoAllocChunks, out_tokens, out_logprobs);
   return static_cast<int>(cudaGetLastError());
 }

@@ -83,7 +83,7 @@ def test_pause_aborts_and_runner_resumes_with_new_version():
         await runner.wait_for_idle()
         partial = list(state.output_tokens)
         runner.version += 1
-        await eng.resume_generation()
+        await eng.resume_generation(version=runner.version)
         runner.resume()
         await task
         await eng.shutdown()
@@ -95,4 +95,46 @@ def test_pause_aborts_and_runner_resumes_with_new_version():
     assert state.output_versions[: len(partial)] == [0] * len(partial)
     assert set(state.output_versions[len(partial):]) <= {1}
     # greedy continuation after the abort equals an uninterrupted greedy run
+    assert state.output_tokens == uninterrupted
+
+
+def test_suspend_keeps_one_submission_and_tags_versions():
+    """Weight-sync pause in suspend mode: the request is parked (no abort, no resubmission), then
+    continues under the new version; greedy output equals an uninterrupted run."""
+    cfg, m, eng = make_engine(max_num_batched_tokens=64)
+    N = 300
+    _, _, eng_ref = make_engine(max_num_batched_tokens=64)
+
+    async def reference():
+        o = await collect(eng_ref, [3, 4, 5, 6], SamplingParams(temperature=0.0, max_tokens=N, ignore_eos=True), "ref")
+        await eng_ref.shutdown()
+        return o.outputs[0].token_ids
+
+    uninterrupted = asyncio.run(reference())
+
+    async def run():
+        runner = InterruptibleGenerationRunner(eng, temperature=0.0, top_p=1.0, stop_sequences=None,
+                                               collect_logprobs=True)
+        runner.stop_sequences = None
+        state = OnlineGenerationState(index=0, input_ids=[3, 4, 5, 6], requested_max_tokens=N)
+        task = asyncio.create_task(runner.generate(state))
+        while eng.stats["generated_tokens"] < 5:
+            await asyncio.sleep(0.0005)
+        runner.pause()
+        await eng.pause_generation(mode="suspend", clear_cache=True)
+        before = eng.stats["generated_tokens"]
+        await asyncio.sleep(0.05)
+        assert eng.stats["generated_tokens"] == before  # nothing runs while paused
+        runner.version += 1
+        await eng.resume_generation(version=runner.version)
+        runner.resume()
+        await task
+        await eng.shutdown()
+        return state, before
+
+    state, before = asyncio.run(run())
+    assert state.stop_reason == "length" and len(state.output_tokens) == N
+    assert eng.stats["aborted"] == 0 and eng.stats["suspended"] == 1
+    assert state.output_versions == [0] * before + [1] * (N - before)
+    assert len(state.output_logprobs) == N
     assert state.output_tokens == uninterrupted

@@ -409,6 +409,100 @@ def test_sampler_greedy_and_distribution():
     assert torch.allclose(freq, probs, atol=0.03)
 
 
+def _masked_logits(rows, V, seed=0):
+    """Rows with -inf entries: whole leading chunks masked, scattered masks, and one row with a
+    single finite logit."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(rows, V, generator=g) * 2
+    x[0, : V // 2] = float("-inf")  # leading chunks entirely -inf
+    x[1, torch.rand(V, generator=g) < 0.9] = float("-inf")
+    x[2, :] = float("-inf")
+    x[2, V - 3] = 1.5  # only one finite logit, in the last chunk
+    x[3, 1::2] = float("-inf")
+    return x.bfloat16().to(DEV)
+
+
+@pytest.mark.parametrize("temp", [0.0, 1.0, 0.7])
+def test_sampler_minus_inf_logits(temp):
+    rows, V = 8, 151936
+    logits = _masked_logits(rows, V)
+    t = torch.full((rows,), temp, device=DEV)
+    seeds = torch.arange(rows, device=DEV, dtype=torch.int64) + 11
+    offs = torch.zeros(rows, device=DEV, dtype=torch.int64)
+    tok, lp = ops.sample(logits, t, seeds, offs)
+    assert torch.isfinite(lp).all(), lp
+    assert torch.isfinite(logits.float().gather(1, tok.view(-1, 1))).all()  # never a masked token
+    want = torch.log_softmax(logits.float(), -1).gather(1, tok.view(-1, 1)).squeeze(1)
+    torch.testing.assert_close(lp, want, atol=2e-3, rtol=1e-4)
+    assert int(tok[2]) == V - 3
+
+
+def test_sampler_all_masked_row_has_no_nan():
+    logits = torch.full((2, 4096), float("-inf"), device=DEV).bfloat16()
+    logits[1, 7] = 0.0
+    tok, lp = ops.sample(logits, torch.ones(2, device=DEV), torch.zeros(2, device=DEV, dtype=torch.int64),
+                         torch.zeros(2, device=DEV, dtype=torch.int64))
+    assert not torch.isnan(lp).any()
+    assert int(tok[0]) == 0 and float(lp[0]) == float("-inf")
+    assert int(tok[1]) == 7 and abs(float(lp[1])) < 1e-6
+
+
+def _filtered_probs(x, temp, k, p):
+    z = x.float() / temp
+    if 0 < k < z.numel():
+        z = z.masked_fill(z < torch.topk(z, k).values[-1], float("-inf"))
+    probs = torch.softmax(z, -1)
+    if p < 1:
+        sp, order = torch.sort(probs, descending=True)
+        keep = (torch.cumsum(sp, 0) - sp) < p
+        probs = torch.zeros_like(probs).scatter_(0, order, sp * keep)
+        probs = probs / probs.sum()
+    return probs
+
+
+@pytest.mark.parametrize("k,p", [(5, 1.0), (0, 0.8), (6, 0.7), (1, 1.0), (0, 0.05)])
+def test_sampler_top_k_top_p_distribution(k, p):
+    V, n = 4096, 20000
+    base = torch.full((V,), -6.0)
+    base[:12] = torch.tensor([2.0, 1.6, 1.5, 1.2, 1.0, 0.9, 0.5, 0.3, 0.2, 0.0, -0.5, -1.0])
+    base = base.bfloat16()
+    logits = base.to(DEV).repeat(n, 1)
+    temp = 0.9
+    tok, lp = ops.sample(logits, torch.full((n,), temp, device=DEV), torch.arange(n, device=DEV),
+                         torch.full((n,), 3, device=DEV, dtype=torch.int64),
+                         top_k=torch.full((n,), k, dtype=torch.int32), top_p=torch.full((n,), p))
+    want = _filtered_probs(base, temp, k, p)
+    freq = torch.bincount(tok.cpu(), minlength=V).float() / n
+    assert float(freq[want == 0].sum()) == 0.0  # nothing outside the kept set
+    assert torch.allclose(freq, want, atol=0.015), (freq[:12], want[:12])
+    full = torch.log_softmax(base.float(), -1)
+    torch.testing.assert_close(lp.cpu(), full[tok.cpu()], atol=2e-3, rtol=1e-4)
+
+
+def test_sampler_mixed_rows_filtered_and_plain():
+    """Rows with and without filters in one call: plain rows equal a call without filter arrays."""
+    rows, V = 64, 151936
+    logits = (torch.randn(rows, V, device=DEV) * 3).bfloat16()
+    t = torch.rand(rows, device=DEV) + 0.5
+    t[::9] = 0.0
+    seeds = torch.randint(0, 2**62, (rows,), device=DEV)
+    offs = torch.arange(rows, device=DEV, dtype=torch.int64)
+    top_k = torch.zeros(rows, dtype=torch.int32)
+    top_p = torch.ones(rows)
+    top_k[1::4] = 20
+    top_p[2::4] = 0.5
+    tok, lp = ops.sample(logits, t, seeds, offs, top_k=top_k, top_p=top_p)
+    tok0, lp0 = ops.sample(logits, t, seeds, offs)
+    plain = ((top_k == 0) & (top_p == 1.0)) | (t.cpu() <= 0)
+    assert torch.equal(tok[plain.to(DEV)], tok0[plain.to(DEV)])
+    for i in torch.nonzero(top_k > 0).flatten().tolist():
+        if float(t[i]) > 0:
+            kth = torch.topk(logits[i].float(), 20).values[-1]
+            assert float(logits[i, tok[i]].float()) >= float(kth)
+    want = torch.log_softmax(logits.float(), -1).gather(1, tok.view(-1, 1)).squeeze(1)
+    torch.testing.assert_close(lp, want, atol=2e-3, rtol=1e-4)
+
+
 @pytest.mark.parametrize("splits", [2, 4, 0])
 def test_gemm_split_k_accumulate(splits):
     M, N, K = 256, 512, 4096

@@ -209,11 +209,16 @@ def test_replay_fifo_eviction_and_counters():
     assert stats["size"] == 2 and stats["total_samples_evicted"] == 0
     stats = rb.add_samples([3, 4, 5])
     assert stats["size"] == 3 and stats["total_samples_evicted"] == 2 and stats["total_samples_added"] == 5
-    assert list(rb.samples) == [3, 4, 5]
+    assert rb.snapshot() == [3, 4, 5]
     got = rb.sample(10)
     assert sorted(got) == [3, 4, 5] and len(rb) == 3  # sampling does not remove
     assert rb.get_stats()["total_samples_sampled"] == 3
     assert rb.sample(0) == []
+    # one call larger than the ring keeps its newest samples in order
+    stats = rb.add_samples([6, 7, 8, 9, 10])
+    assert rb.snapshot() == [8, 9, 10] and stats["total_samples_evicted"] == 7
+    rb.add_samples([11])
+    assert rb.snapshot() == [9, 10, 11]
 
 
 def test_rollout_stats_window_and_active_workers():

@@ -1,6 +1,7 @@
 """The allocation-free sampler entry point ``accerl_sample_logits_noalloc`` (exported C symbol,
-called through ctypes) against the workspace-taking sampler on the same inputs, on two calls in a
-row (its static scratch keeps its contents between calls), plus its row-limit rejection."""
+called through ctypes; prototype in csrc/accerl_noalloc.h) against the workspace-taking sampler on
+the same inputs, on two calls in a row (its static scratch keeps its contents between calls), on
+logits with -inf entries, plus its row-limit rejection."""
 
 import ctypes
 
@@ -46,6 +47,38 @@ def test_noalloc_sampler_matches_workspace_sampler():
         torch.cuda.synchronize()
         assert torch.equal(tokens, tok_ref)
         torch.testing.assert_close(lps, lp_ref, rtol=1e-5, atol=1e-5)
+
+
+def test_noalloc_sampler_minus_inf_logits():
+    """-inf logits (leading chunks masked, a row with one finite logit): finite log-probabilities
+    equal to log_softmax at the sampled token, and the same tokens as the workspace sampler."""
+    from accerl_agent_b200 import ops
+
+    fn = _symbol()
+    rows, V = 6, 151936
+    g = torch.Generator(device="cpu").manual_seed(3)
+    x = torch.randn(rows, V, generator=g) * 2
+    x[0, : V // 2] = float("-inf")
+    x[1, torch.rand(V, generator=g) < 0.95] = float("-inf")
+    x[2, :] = float("-inf")
+    x[2, 17] = 0.25
+    logits = x.bfloat16().cuda()
+    temperature = torch.tensor([1.0, 0.8, 1.0, 0.0, 1.3, 1.0], device="cuda")
+    seeds = torch.arange(rows, device="cuda", dtype=torch.int64) * 7 + 1
+    offsets = torch.zeros(rows, device="cuda", dtype=torch.int64)
+    tok_ref, lp_ref = ops.sample(logits, temperature, seeds, offsets)
+    want_all = torch.log_softmax(logits.float(), -1)
+    for _ in range(2):
+        tokens = torch.full((rows,), -1, dtype=torch.int64, device="cuda")
+        lps = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+        assert _call(fn, logits, rows, temperature, seeds, offsets, tokens, lps) == 0
+        torch.cuda.synchronize()
+        assert torch.isfinite(lps).all()
+        assert torch.equal(tokens, tok_ref)
+        want = want_all.gather(1, tokens.view(-1, 1)).squeeze(1)
+        torch.testing.assert_close(lps, want, atol=2e-3, rtol=1e-4)
+        torch.testing.assert_close(lps, lp_ref, rtol=1e-5, atol=1e-5)
+        assert int(tokens[2]) == 17
 
 
 def test_noalloc_sampler_rejects_more_rows_than_its_scratch():
