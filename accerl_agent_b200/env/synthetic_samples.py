@@ -78,3 +78,10 @@ def synthetic_rl_samples(num_groups: int, group_size: int = 8, seed: int = 0, wi
                                 old_logprobs=old, advantage=float(adv), token_advantages=tok_adv,
                                 response_indices=resp, output_versions=versions))
     return out
+
+
+def benchmark_pool(rank: int, samples: int, window: int) -> List[RLSample]:
+    """The trainer benchmark's per-rank replay pool: seeded synthetic text-game episodes in GRPO
+    groups of 8 with 16-token actions and a ``window``-token history (seed 1000 + rank)."""
+    groups = (samples + 7) // 8
+    return synthetic_rl_samples(groups, group_size=8, seed=1000 + rank, window=window, action_tokens=16)

@@ -121,21 +121,27 @@ class ShardedAdamW:
             dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
         return self._sumsq
 
-    def step(self, lr: Optional[float] = None) -> torch.Tensor:
+    def step(self, lr: Optional[float] = None, timer=None) -> torch.Tensor:
         """Reduce, clip (global norm ``max_grad_norm``), update and re-gather. Returns the float64
-        sum of squared gradients (a device tensor; no host sync)."""
+        sum of squared gradients (a device tensor; no host sync). ``timer`` (a
+        ``utils.timing.PhaseTimer``) marks the end of each phase."""
         if lr is not None:
             self.lr = lr
         if self.fused:
-            return self._fused_step()
+            return self._fused_step(timer)
+        mark = timer.mark if timer is not None else (lambda name: None)
         self.reduce_gradients()
+        mark("reduce_scatter")
         sumsq = self.global_grad_sumsq()
+        mark("norm_allreduce")
         self.step_count += 1
         ops.adamw_step(self.master, self.exp_avg, self.exp_avg_sq, self.grad_shard, self.param_shard, sumsq,
                        self.lr, self.betas[0], self.betas[1], self.eps, self.weight_decay, self.max_grad_norm,
                        self.step_count)
         self._local_step(sumsq)
+        mark("adamw")
         self.all_gather_params()
+        mark("all_gather")
         return sumsq
 
     def _local_step(self, sumsq: torch.Tensor) -> None:
@@ -146,27 +152,34 @@ class ShardedAdamW:
                        self.lr, self.betas[0], self.betas[1], self.eps, self.weight_decay, self.max_grad_norm,
                        self.step_count)  # (the kernel zeroes the gradients it consumed)
 
-    def _fused_step(self) -> torch.Tensor:
+    def _fused_step(self, timer=None) -> torch.Tensor:
         import math
 
+        mark = timer.mark if timer is not None else (lambda name: None)
         native = ops.native()
         self._sumsq.zero_()
         # every peer has finished accumulating its gradients before anyone reads them
         dist.all_reduce(self._barrier_flag, group=self.group)
+        mark("barrier_grads_ready")
         native.rs_sumsq(self._grad_peers.ptrs, self.rank, self.shard_numel, self.grad_shard, self._sumsq)
         if self.has_local:
             ops.grad_sumsq(self.local_grads, self._sumsq)
+        mark("rs_sumsq")
         # the norm all-reduce also guarantees every peer has finished reading this rank's gradients
         dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
+        mark("norm_allreduce")
         self.step_count += 1
         self._local_step(self._sumsq)
         self.model.grads.zero_()
+        mark("grad_zero")
         b1, b2 = self.betas
         native.adamw_push(self.master, self.exp_avg, self.exp_avg_sq, self.grad_shard, self._param_peers.ptrs,
                           self.rank, self._sumsq, self.lr, b1, b2, self.eps, self.weight_decay, self.max_grad_norm,
                           1.0 - b1 ** self.step_count, math.sqrt(1.0 - b2 ** self.step_count))
+        mark("adamw_push")
         # every peer's parameter pushes into this rank's buffer land before the next forward
         dist.all_reduce(self._barrier_flag, group=self.group)
+        mark("barrier_params_ready")
         return self._sumsq
 
     def all_gather_params(self) -> None:

@@ -21,9 +21,8 @@ def main():
     ap.add_argument("--model", default="qwen2.5-1.5b")
     ap.add_argument("--json", default=None)
     a = ap.parse_args()
-    from bench import synthetic_pool
-
     from .core.config import make_args
+    from .env.synthetic_samples import benchmark_pool
     from .replay import ReplayBuffer
     from .trainer.worker import TrainWorker
 
@@ -32,7 +31,7 @@ def main():
                      train_logprob_mode="response_only_lm_head", learning_rate=1e-6, lr_warmup_steps=0,
                      max_steps=10**6, dtype="bfloat16", fsdp_world_size=1, device="cuda")
     rb = ReplayBuffer(args.replay_capacity, seed=0)
-    rb.add_samples(synthetic_pool(0, args.replay_capacity, 8192))
+    rb.add_samples(benchmark_pool(0, args.replay_capacity, 8192))
     w = TrainWorker(args, replay_buffer=rb, device=torch.device("cuda", 0))
     w.train_until_next_sync(1)
     packs, gtok = w.stage_window()

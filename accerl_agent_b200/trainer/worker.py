@@ -45,6 +45,7 @@ from ..core.sample import IGNORE_INDEX, PreparedVarlenPack, RLSample
 from ..models.config import resolve_model_config
 from ..models.hf_io import load_hf_checkpoint, save_hf_checkpoint, vllm_weight_metadata
 from ..models.transformer import build_model
+from ..parallel import balance
 from ..parallel.fsdp import ShardedAdamW, dist_ready
 from ..parallel.expert_parallel import ExpertParallel, expert_partition
 
@@ -82,6 +83,23 @@ class DevicePack:
     old_lp: torch.Tensor
     adv: torch.Tensor
     h2d_bytes: int
+    # backing buffers: int64 [ids | positions | labels | prediction indices], float32 [old lp | adv],
+    # int32 cu_seqlens (what moves when a pack is computed on another rank)
+    raw: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None
+
+    @staticmethod
+    def from_raw(ints: torch.Tensor, floats: torch.Tensor, cu: torch.Tensor, max_seqlen: int,
+                 h2d_bytes: int = 0) -> "DevicePack":
+        n = floats.numel() // 2
+        T = (ints.numel() - 2 * n) // 2
+        batch = {
+            "input_ids": ints[:T],
+            "position_ids": ints[T : 2 * T],
+            "target_labels": ints[2 * T : 2 * T + n],
+            "prediction_indices": ints[2 * T + n :],
+            "cu_seqlens": cu,
+        }
+        return DevicePack(batch, max_seqlen, floats[:n], floats[n:], h2d_bytes, (ints, floats, cu))
 
 
 class PinnedStager:
@@ -138,6 +156,8 @@ class TrainWorker:
         self.args = args
         self.rank = rank
         self.fsdp_world_size = fsdp_world_size
+        self.balance_packs = bool(getattr(args, "balance_packs", True))
+        self.last_balance: Dict[str, float] = {}
         self.replay_buffer = replay_buffer
         self.device = device or pick_device(getattr(args, "device", "auto"))
         if self.device.type == "cuda":
@@ -294,6 +314,13 @@ class TrainWorker:
             pack_cpu_ms=(time.perf_counter() - t0) * 1e3,
         )
 
+    @staticmethod
+    def pack_to_device_bytes(pack: PreparedVarlenPack) -> int:
+        """Host->device bytes of ``pack_to_device(pack)``."""
+        T = int(pack.batch["input_ids"].numel())
+        n = int(pack.batch["target_indices"].numel())
+        return (2 * T + 2 * n) * 8 + 2 * n * 4 + int(pack.batch["cu_seqlens"].numel()) * 4
+
     def pack_to_device(self, pack: PreparedVarlenPack) -> DevicePack:
         """Stage a CPU pack in pinned memory and copy it to the device (async on the current stream)."""
         b = pack.batch
@@ -320,23 +347,15 @@ class TrainWorker:
         floats[n:].copy_(adv)
         cu_h = self.stager.buffer("i32", b["cu_seqlens"].numel(), torch.int32)
         cu_h.copy_(b["cu_seqlens"])
-        nb = non_blocking = self.device.type == "cuda"
-        ints_d = ints.to(self.device, non_blocking=nb)
-        floats_d = floats.to(self.device, non_blocking=nb)
-        cu_d = cu_h.to(self.device, non_blocking=nb)
+        if self.device.type == "cuda":
+            ints_d = ints.to(self.device, non_blocking=True)
+            floats_d = floats.to(self.device, non_blocking=True)
+            cu_d = cu_h.to(self.device, non_blocking=True)
+        else:  # the staging buffers are reused: CPU packs own copies
+            ints_d, floats_d, cu_d = ints.clone(), floats.clone(), cu_h.clone()
         self.stager.release()
         h2d = ints.numel() * 8 + floats.numel() * 4 + cu_h.numel() * 4
-        batch = {
-            "input_ids": ints_d[:T],
-            "position_ids": ints_d[T : 2 * T],
-            "target_labels": ints_d[2 * T : 2 * T + n],
-            "prediction_indices": ints_d[2 * T + n :],
-            "cu_seqlens": cu_d,
-        }
-        if not non_blocking:
-            batch = {k: v.clone() for k, v in batch.items()}
-            floats_d = floats_d.clone()
-        return DevicePack(batch, pack.max_seqlen, floats_d[:n], floats_d[n:], h2d)
+        return DevicePack.from_raw(ints_d, floats_d, cu_d, pack.max_seqlen, h2d)
 
     def _prepare_varlen_optimizer_window(self, trainer_version: float) -> List[PreparedVarlenPack]:
         window = None
@@ -365,55 +384,92 @@ class TrainWorker:
             return self.device
         return torch.device("cpu")
 
-    def run_varlen_step_on_device(self, packs: List[DevicePack], global_tokens: int) -> torch.Tensor:
-        """Forward/backward of already-staged packs; returns the float64[3] statistics (device)."""
+    def run_varlen_step_on_device(self, packs: List[DevicePack], global_tokens: int, timer=None) -> torch.Tensor:
+        """Forward/backward of already-staged packs; returns the float64[3] statistics (device).
+        ``timer`` (a ``utils.timing.PhaseTimer``) marks forward and backward of every pack."""
         stats = torch.zeros(3, dtype=torch.float64, device=self.device)
         scale = 1.0 / float(global_tokens)
         for dp in packs:
             lp, ctx = self.model.forward_logprobs(dp.batch, dp.max_seqlen)
             dlp, st = ops.policy_loss(lp, dp.old_lp, dp.adv, self.obj_cfg, loss_scale=scale)
+            if timer is not None:
+                timer.mark("forward")
             self.model.backward_from_logprobs(dlp, ctx)
             stats += st.to(stats.device)
+            if timer is not None:
+                timer.mark("backward")
             self.train_micro_step += 1
             del ctx, lp, dlp
         return stats
 
-    def stage_window(self, trainer_version: float = 0.0) -> Tuple[List[DevicePack], int]:
-        """Prepare one optimizer window and leave its packs resident on the device (benchmarks)."""
-        window = self._prepare_varlen_optimizer_window(trainer_version)
-        packs = []
-        for p in window:
-            dp = self.pack_to_device(p)
-            dp.batch = {k: v.clone() for k, v in dp.batch.items()}
-            dp.old_lp, dp.adv = dp.old_lp.clone(), dp.adv.clone()
-            packs.append(dp)
-        tok = torch.tensor([sum(p.valid_token_count for p in window)], dtype=torch.int64, device=self._comm_device())
-        return packs, int(self._all_reduce(tok).item())
+    def _balance_window(self, window: List[PreparedVarlenPack]) -> Tuple[List[Any], int]:
+        """Spread the window's packs over the ranks by estimated work (``parallel/balance.py``).
+        Returns this rank's work list -- its own CPU packs still to be staged, and packs received from
+        other ranks as ``DevicePack`` -- and the global target-token count (every rank's packs)."""
+        local_tokens = sum(p.valid_token_count for p in window)
+        if self.fsdp_world_size == 1 or not dist_ready():
+            return list(window), local_tokens
+        meta = np.zeros((len(window), 5), dtype=np.float64)
+        for i, p in enumerate(window):
+            lens = np.diff(p.batch["cu_seqlens"].numpy().astype(np.int64))
+            meta[i] = (balance.pack_cost(self.cfg, lens, p.valid_token_count), p.total_tokens, p.valid_token_count,
+                       len(lens), p.max_seqlen)
+        meta_all = balance.gather_meta(meta)  # also replaces the global target-token all-reduce
+        global_tokens = int(round(meta_all[:, :, 2].sum()))
+        if not self.balance_packs:
+            return list(window), global_tokens
+        assign, moves = balance.plan(meta_all)
+        outgoing = {mv.index: self.pack_to_device(window[mv.index]).raw for mv in moves if mv.src == self.rank}
+        received = balance.exchange(moves, self.rank, outgoing, self.device)
+        max_len = {(mv.src, mv.index): mv.max_seqlen for mv in moves}
+        work: List[Any] = []
+        for owner, i in assign[self.rank]:
+            if owner == self.rank:
+                work.append(window[i])
+            else:
+                work.append(DevicePack.from_raw(*received[(owner, i)], max_len[(owner, i)]))
+        self.last_balance = {"moved_in": sum(1 for o, _ in assign[self.rank] if o != self.rank),
+                             "rank_cost": float(sum(meta_all[o, i, 0] for o, i in assign[self.rank])),
+                             "mean_cost": float(meta_all[:, :, 0].sum() / self.fsdp_world_size)}
+        return work, global_tokens
 
-    def train_step_on_device(self, packs: List[DevicePack], global_tokens: int) -> torch.Tensor:
+    def stage_window(self, trainer_version: float = 0.0) -> Tuple[List[DevicePack], int]:
+        """Prepare one optimizer window (balanced over the ranks) and leave its packs resident on the
+        device (benchmarks)."""
+        window = self._prepare_varlen_optimizer_window(trainer_version)
+        work, global_tokens = self._balance_window(window)
+        packs = []
+        for item in work:
+            dp = item if isinstance(item, DevicePack) else self.pack_to_device(item)
+            packs.append(DevicePack.from_raw(*(t.clone() for t in dp.raw), dp.max_seqlen, dp.h2d_bytes))
+        return packs, global_tokens
+
+    def train_step_on_device(self, packs: List[DevicePack], global_tokens: int, timer=None) -> torch.Tensor:
         """One optimizer step over device-resident packs: forward/backward of every pack, the
-        statistics all-reduce and the sharded AdamW step (no host<->device traffic)."""
-        stats = self.run_varlen_step_on_device(packs, global_tokens)
+        statistics all-reduce and the sharded AdamW step (no host<->device traffic). ``timer``
+        (a ``utils.timing.PhaseTimer``, first mark already taken) splits the step into phases."""
+        stats = self.run_varlen_step_on_device(packs, global_tokens, timer)
         if self.fsdp_world_size > 1:
             self._all_reduce(stats)
-        self.optimizer.step(self.current_lr())
+            if timer is not None:
+                timer.mark("stats_allreduce")
+        self.optimizer.step(self.current_lr(), timer=timer)
         self.optimizer_step += 1
         return stats
 
     def _run_varlen_optimizer_step(self, trainer_version: float) -> Dict[str, float]:
         with nvtx.range("train/prepare_window"):
             window = self._prepare_varlen_optimizer_window(trainer_version)
-        local_tokens = sum(p.valid_token_count for p in window)
-        tok = torch.tensor([local_tokens], dtype=torch.int64, device=self._comm_device())
-        global_tokens = int(self._all_reduce(tok).item())
+        with nvtx.range("train/balance"):
+            work, global_tokens = self._balance_window(window)
         if global_tokens <= 0:
             raise RuntimeError("Global Varlen optimizer window contains no valid response tokens.")
         stats = torch.zeros(3, dtype=torch.float64, device=self.device)
-        h2d = 0
+        h2d = sum(self.pack_to_device_bytes(p) for p in window if not any(p is w for w in work))
         scale = 1.0 / float(global_tokens)
-        for pack in window:
+        for pack in work:
             with nvtx.range("train/h2d"):
-                dp = self.pack_to_device(pack)
+                dp = pack if isinstance(pack, DevicePack) else self.pack_to_device(pack)
             h2d += dp.h2d_bytes
             with nvtx.range("train/forward"):
                 lp, ctx = self.model.forward_logprobs(dp.batch, dp.max_seqlen)

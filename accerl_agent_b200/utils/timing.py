@@ -53,3 +53,43 @@ def max_over_ranks(value: float) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+class PhaseTimer:
+    """CUDA events recorded on the current stream at named points of a step; ``durations()`` gives
+    the device time between consecutive marks (ms), summed over repeats of the same phase name.
+
+    Used to split a multi-GPU optimizer step into compute and each collective phase per rank."""
+
+    def __init__(self):
+        self._marks: List = []
+
+    def mark(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self._marks.append((name, ev))
+
+    def durations(self) -> dict:
+        out: dict = {}
+        for (_, a), (name, b) in zip(self._marks, self._marks[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+    def reset(self) -> None:
+        self._marks = []
+
+
+def gather_phases(local: dict) -> dict:
+    """Per-phase max / min / mean over ranks of a ``PhaseTimer.durations()`` dict (every rank must
+    call it; identity on one rank)."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return {k: {"max": v, "min": v, "mean": v} for k, v in local.items()}
+    allv: List[dict] = [None] * dist.get_world_size()
+    dist.all_gather_object(allv, local)
+    out = {}
+    for k in local:
+        vals = [d.get(k, 0.0) for d in allv]
+        out[k] = {"max": max(vals), "min": min(vals), "mean": sum(vals) / len(vals)}
+    return out

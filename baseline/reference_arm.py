@@ -167,9 +167,9 @@ def run_reference(a):
     addr = os.environ.get("MASTER_ADDR", "127.0.0.1")
     port = int(os.environ.get("MASTER_PORT", "29517"))
     replay = at.ReplayBufferActor.remote(capacity=args.replay_capacity)
-    from bench import synthetic_pool
+    from accerl_agent_b200.env.synthetic_samples import benchmark_pool
 
-    pool = synthetic_pool(rank, 256, a.max_length)
+    pool = benchmark_pool(rank, 256, a.max_length)
     replay.add_samples.remote([at.RLSample(**asdict(s)) for s in pool[: args.replay_capacity]])
     try:
         worker = at.FSDPTrainWorker(args, rank, world, addr, port, replay)

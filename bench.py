@@ -49,10 +49,9 @@ def dist_env():
 
 
 def synthetic_pool(rank: int, samples: int, window: int):
-    from accerl_agent_b200.env.synthetic_samples import synthetic_rl_samples
+    from accerl_agent_b200.env.synthetic_samples import benchmark_pool
 
-    groups = (samples + 7) // 8
-    return synthetic_rl_samples(groups, group_size=8, seed=1000 + rank, window=window, action_tokens=16)
+    return benchmark_pool(rank, samples, window)
 
 
 def emit(line: dict):
@@ -71,7 +70,7 @@ def run_native(a):
     from accerl_agent_b200.replay import ReplayBuffer
     from accerl_agent_b200.trainer.worker import TrainWorker
     from accerl_agent_b200.utils.clocks import ClockSampler
-    from accerl_agent_b200.utils.timing import max_over_ranks
+    from accerl_agent_b200.utils.timing import PhaseTimer, gather_phases, max_over_ranks
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -107,17 +106,29 @@ def run_native(a):
     barrier()
     launches0 = ops.LAUNCHES[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # per-rank phase split of the multi-GPU step (event records only; no synchronisation is added)
+    timer = PhaseTimer() if world > 1 else None
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
         start.record()
         for packs, gtok in staged:
-            trainer.train_step_on_device(packs, gtok)
+            if timer is not None:
+                timer.mark("step_start")
+            trainer.train_step_on_device(packs, gtok, timer=timer)
         end.record()
         torch.cuda.synchronize()
         barrier()
     launches = (ops.LAUNCHES[0] - launches0) / a.steps
     dev_ms = max_over_ranks(start.elapsed_time(end))
+    phases = None
+    if timer is not None:
+        per_phase = {k: v / a.steps for k, v in timer.durations().items() if k != "step_start"}
+        lens = [(dp.batch["cu_seqlens"][1:] - dp.batch["cu_seqlens"][:-1]).double() for packs, _ in staged
+                for dp in packs]
+        per_phase["tokens"] = sum(float(x.sum()) for x in lens) / a.steps
+        per_phase["attn_sum_len_sq_1e6"] = sum(float((x * x).sum()) for x in lens) / a.steps / 1e6
+        phases = {k: {kk: round(vv, 3) for kk, vv in v.items()} for k, v in gather_phases(per_phase).items()}
     tokens = sum(g for _, g in staged)
     total_tokens_local = sum(int(dp.batch["input_ids"].numel()) for packs, _ in staged for dp in packs)
     total_tokens = total_tokens_local
@@ -183,6 +194,7 @@ def run_native(a):
                 "d2h_bytes_per_step": 3 * 8 + 2 * 8 + 8,
             },
             "gpu_launches": int(launches),
+            **({"phases_ms_per_step": phases} if phases is not None else {}),
             "clocks": {"sm_mhz": cs.get("sm_mhz"), "sm_max_mhz": cs.get("sm_max_mhz"),
                        "reasons": cs.get("reasons", []), "samples": cs.get("samples", 0),
                        "e2e_region": clocks2.summary()},

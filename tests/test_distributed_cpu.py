@@ -311,3 +311,66 @@ def test_expert_partitioned_trainer_resumes_the_same_optimisation(tmp_path):
         assert part and resumed == 2 and sa == sb == 3
         assert diff < 1e-6, diff
         assert "model-experts-00002-of-00002.safetensors" in files and "optimizer_rank00001.pt" in files
+
+
+def _balance_worker(rank, port, balance_packs, out):
+    from accerl_agent_b200.core.config import make_args
+    from accerl_agent_b200.replay import ReplayBuffer
+    from accerl_agent_b200.trainer.worker import TrainWorker
+
+    try:
+        os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        args = make_args(model_path="tiny-qwen2", train_packing="varlen", train_token_budget=96, max_length=96,
+                         tw_history_token_window=96, batch_size=1, grad_accum_steps=4, device="cpu", dtype="float32",
+                         min_replay_size_per_rank=4, replay_sample_timeout_seconds=5.0, learning_rate=1e-3,
+                         replay_wait_sleep_seconds=0.01, balance_packs=balance_packs, seed=3)
+        rb = ReplayBuffer(4, seed=rank)
+        g = torch.Generator().manual_seed(100 + rank)
+        # rank 0 draws long episodes, rank 1 short ones: the unbalanced window is skewed
+        for L in ((90, 80, 85, 70) if rank == 0 else (12, 16, 20, 10)):
+            ids = torch.randint(3, 4096, (L,), generator=g).tolist()
+            rb.add_samples([RLSample("grpo", ids, [1] * L, [-100] * (L - 6) + ids[L - 6:], [-6.0] * L,
+                                     0.5 - rank, [0.0] * L, [-1] * (L - 6) + [0] * 6, [0])])
+        w = TrainWorker(args, rank=rank, fsdp_world_size=2, replay_buffer=rb, device=torch.device("cpu"))
+        w.model.init_weights(seed=7)
+        w.optimizer.refresh_master_from_params()
+        summary = w.train_until_next_sync(1)
+        out.put((rank, (w.model.params.detach().clone(), dict(w.last_balance), summary["segment_valid_tokens"])))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException as exc:
+        out.put((rank, repr(exc)))
+        raise
+
+
+def _run_balance(flag):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_balance_worker, args=(r, port, flag, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, payload = q.get(timeout=240)
+        assert not isinstance(payload, str), payload
+        res[r] = payload
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    return res
+
+
+def test_pack_balancing_moves_packs_and_keeps_the_step():
+    """Spreading the window's packs over the ranks by estimated work moves packs from the rank with
+    the long episodes and gives the same optimizer step (parameters, global token count) as computing
+    every pack where it was drawn."""
+    bal, plain = _run_balance(True), _run_balance(False)
+    moved = bal[0][1].get("moved_in", 0) + bal[1][1].get("moved_in", 0)
+    assert moved > 0
+    assert abs(bal[0][1]["rank_cost"] - bal[1][1]["rank_cost"]) < abs(bal[0][1]["mean_cost"]) * 0.5
+    assert plain[0][1] == {} and plain[1][1] == {}
+    for r in range(2):
+        assert bal[r][2] == plain[r][2]
+        torch.testing.assert_close(bal[r][0], plain[r][0], atol=1e-6, rtol=1e-5)
