@@ -111,6 +111,9 @@ def build_parser() -> argparse.ArgumentParser:
       help="With --expert-parallel: each rank stores only its routed experts (weights, gradients, optimizer "
            "state), or every rank keeps the whole expert stack.")
     a("--weight-sync", default="ipc", choices=("ipc", "nccl"), help="Trainer->rollout weight transfer path.")
+    a("--rollout-worker-procs", type=int, default=None,
+      help="Processes that run each engine's rollout workers (default: one per worker; 0: the workers run as "
+           "asyncio tasks inside the engine process).")
     a("--no-balance-packs", dest="balance_packs", action="store_false",
       help="Varlen training: compute every pack on the rank that drew it instead of spreading each "
            "optimizer window's packs over the trainer ranks by estimated work.")

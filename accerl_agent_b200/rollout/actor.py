@@ -1,8 +1,10 @@
 """Inference process actor: one generation engine (one GPU) plus the rollout workers it serves.
 
-Rollout workers are asyncio tasks in the same process as the engine, so a request costs no
-inter-process hop; they push finished samples to the sample queue of trainer rank
-``worker_id % fsdp_world_size`` and episode records to the driver's statistics queue.
+Rollout workers run in their own processes by default (``--rollout-worker-procs``, one per worker
+as the reference's actors do) and send their requests over a Unix socket (``rollout/remote.py``);
+with ``--rollout-worker-procs 0`` they are asyncio tasks inside the engine process. Either way they
+push finished samples to the sample queue of trainer rank ``worker_id % fsdp_world_size`` and
+episode records to the driver's statistics queue.
 """
 
 from __future__ import annotations
@@ -21,7 +23,6 @@ class InferenceActor:
         actors joined through ``tp_port``; this rank schedules and broadcasts every step."""
         from ..trainer.actor import _load_tokenizer
         from .inference import InferenceService
-        from .worker import RolloutWorker
 
         if device_index is not None and torch.cuda.is_available():
             device = torch.device("cuda", device_index)
@@ -45,32 +46,31 @@ class InferenceActor:
 
             tp_groups = init_tp_groups(0, args.infer_tp_size, tp_port, device)
         self.service = InferenceService(args, device, tokenizer=tokenizer, tp_groups=tp_groups)
-        world = len(replay_queues)
+        procs = getattr(args, "rollout_worker_procs", None)
+        procs = len(worker_ids) if procs is None else int(procs)
+        self.remote = None
+        self.workers: List[Any] = []
+        if procs > 0 and worker_ids:
+            from .remote import WorkerProcesses
 
-        def sink_for(wid):
-            q = replay_queues[wid % world]
-            return lambda samples: q.put(samples)
-
-        def stats_sink(*rec):
-            stats_queue.put(rec)
-
-        if args.env == "gsm8k":
-            from .math_worker import MathRolloutWorker, load_math_examples
-
-            examples = load_math_examples(args)
-            self.workers = [MathRolloutWorker(args, self.service, wid, sink_for(wid), stats_sink, tokenizer=tokenizer,
-                                              examples=examples) for wid in worker_ids]
+            self.remote = WorkerProcesses(args, self.service, list(worker_ids), replay_queues, stats_queue,
+                                          min(procs, len(worker_ids)))
         else:
-            self.workers = [RolloutWorker(args, self.service, wid, sink_for(wid), stats_sink, tokenizer=tokenizer)
-                            for wid in worker_ids]
+            from .remote import make_workers
+
+            self.workers = make_workers(args, self.service, list(worker_ids), replay_queues, stats_queue, tokenizer)
         self.tasks: List[asyncio.Task] = []
 
     async def start_workers(self) -> int:
+        if self.remote is not None:
+            return await self.remote.start()
         self.tasks = [asyncio.create_task(w.run()) for w in self.workers]
         return len(self.tasks)
 
     async def check_workers(self) -> Optional[str]:
         """None while every worker runs; otherwise a description of the first one that exited."""
+        if self.remote is not None:
+            return self.remote.check()
         for w, t in zip(self.workers, self.tasks):
             if t.done():
                 exc = t.exception()
@@ -78,6 +78,8 @@ class InferenceActor:
         return None
 
     async def stop_workers(self, timeout: float) -> Dict[str, int]:
+        if self.remote is not None:
+            return await self.remote.stop(timeout)
         for w in self.workers:
             await w.stop()
         done, pending = await asyncio.wait(self.tasks, timeout=timeout) if self.tasks else (set(), set())
@@ -101,6 +103,8 @@ class InferenceActor:
         return self.service.get_stats()
 
     async def shutdown(self) -> Dict[str, Any]:
+        if self.remote is not None and self.remote.procs:
+            await self.remote.stop(1.0)
         for w in self.workers:
             await w.stop()
         for t in self.tasks:

@@ -324,3 +324,37 @@ def test_history_prompt_keeps_last_turns():
     assert "pre4" in p and "a4" in p and "dance" in p and "a3" not in p and "start" not in p
     p0 = history_prompt("start", infos, [], None, history_steps=0)
     assert "start" in p0
+
+
+def test_engine_socket_transport_round_trip(tmp_path):
+    """Rollout worker processes reach the engine over a Unix socket: concurrent requests are answered
+    in completion order with tokens, log-probs, versions and stop reason; an engine error fails only
+    its own request; a closed server fails pending requests instead of hanging them."""
+    from accerl_agent_b200.rollout.remote import EngineClient, EngineRequestServer
+
+    class Service:
+        async def request_batch(self, ids, max_tokens):
+            if ids[0] == 666:
+                raise ValueError("bad prompt")
+            await asyncio.sleep(0.01 * (5 - len(ids)))  # shorter prompts finish later
+            return InferenceResult([ids[-1] + 1] * max_tokens, [-0.5] * max_tokens, [3] * max_tokens, "length")
+
+    async def scenario():
+        server = EngineRequestServer(Service(), str(tmp_path / "e.sock"))
+        await server.start()
+        client = EngineClient(server.path)
+        await client.connect()
+        results = await asyncio.gather(*(client.request_batch(list(range(n)), n) for n in (1, 2, 3, 4)))
+        with pytest.raises(RuntimeError, match="bad prompt"):
+            await client.request_batch([666], 2)
+        ok = await client.request_batch([7, 8], 1)
+        await server.close()
+        with pytest.raises(ConnectionError):
+            await asyncio.wait_for(client.request_batch([1], 1), 5)
+        await client.close()
+        return results, ok
+
+    results, ok = run(scenario())
+    for n, r in zip((1, 2, 3, 4), results):
+        assert r.output_tokens == [n] * n and r.output_versions == [3] * n and r.stop_reason == "length"
+    assert ok.output_tokens == [9]
