@@ -154,8 +154,9 @@ def load_game_files(game_dir: str, pattern: str, seed: int, limit: Optional[int]
     return files
 
 
-def make_textworld_env(game_file: str, max_episode_steps: int):
-    """Register and build one TextWorld gym env (imports ``textworld`` on demand)."""
+def make_textworld_env(game_file: str, max_episode_steps: int, policy_commands: bool = False):
+    """Register and build one TextWorld gym env (imports ``textworld`` on demand). ``policy_commands``
+    also requests the game's walkthrough (debugging only: it reveals the solution)."""
     try:
         import textworld
         import textworld.gym
@@ -163,7 +164,7 @@ def make_textworld_env(game_file: str, max_episode_steps: int):
         raise RuntimeError("TextWorld games need the 'textworld' package; use --env synthetic otherwise") from exc
     infos = textworld.EnvInfos(
         objective=True, inventory=True, admissible_commands=True, score=True,
-        max_score=True, won=True, lost=True, moves=True,
+        max_score=True, won=True, lost=True, moves=True, policy_commands=policy_commands,
     )
     env_id = textworld.gym.register_game(game_file, request_infos=infos, max_episode_steps=max_episode_steps)
     return textworld.gym.make(env_id)

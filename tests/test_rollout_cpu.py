@@ -358,3 +358,39 @@ def test_engine_socket_transport_round_trip(tmp_path):
     for n, r in zip((1, 2, 3, 4), results):
         assert r.output_tokens == [n] * n and r.output_versions == [3] * n and r.stop_reason == "length"
     assert ok.output_tokens == [9]
+
+
+def test_rule_based_textworld_sanity_run():
+    """The rule-based TextWorld sanity script on a fake game: walkthrough first, then coin, movement,
+    look; stops when the game is done."""
+    from accerl_agent_b200.textworld_gym import play, rule_action
+
+    assert rule_action({"policy_commands": ["open box"], "admissible_commands": ["go north"]}) == "open box"
+    assert rule_action({"admissible_commands": ["look", "go west", "take coin from table"]}) == "take coin from table"
+    assert rule_action({"admissible_commands": ["inventory", "look", "go east"]}) == "go east"
+    assert rule_action({"admissible_commands": ["inventory", "look"]}) == "look"
+    assert rule_action({"admissible_commands": ["inventory"]}) == "inventory"
+    assert rule_action({}) == "look"
+
+    class Game:
+        def __init__(self):
+            self.t = 0
+            self.closed = False
+
+        def reset(self):
+            return "room", {"objective": "find the coin", "admissible_commands": ["look", "go north"]}
+
+        def step(self, action):
+            self.t += 1
+            won = action == "take coin"
+            return f"obs{self.t}", int(won), won, {"won": won, "lost": False,
+                                                  "admissible_commands": ["take coin"] if self.t == 2 else ["go north"]}
+
+        def close(self):
+            self.closed = True
+
+    g = Game()
+    res = play(g, 20, log=lambda s: None)
+    assert res["actions"] == ["go north", "go north", "take coin"] and res["won"] and res["done"] and g.closed
+    res = play(Game(), 2, log=lambda s: None)
+    assert res["steps"] == 2 and not res["done"]
