@@ -11,7 +11,9 @@ Equivalence is decided here, in order:
      trailing periods and spacing removed; ``\\frac{a}{b}`` -> ``a/b``);
   2. both sides parse as numbers (integers, decimals, fractions, percentages, scientific notation)
      and agree to a relative tolerance of 1e-4 (percent answers also match their fraction);
-  3. with ``fast=False``: both sides parse as sympy expressions whose difference simplifies to 0.
+  3. with ``fast=False``: the LaTeX is rewritten into sympy syntax (nested fractions, roots, powers,
+     constants, mixed numbers) and compared symbolically, then numerically; ``\\pm`` answers and
+     ``\\{...\\}`` sets compare as unordered lists, tuples in order, intervals with their brackets.
 ``math_verify`` (when installed) is consulted last in slow mode, like the reference's fallback chain.
 """
 
@@ -144,20 +146,194 @@ def _numbers_equal(pred: str, gt: str) -> bool:
     return False
 
 
+def _braced(s: str, i: int):
+    """(content, index after the closing brace) of the brace group opening at s[i] == '{'."""
+    depth = 0
+    for j in range(i, len(s)):
+        if s[j] == "{":
+            depth += 1
+        elif s[j] == "}":
+            depth -= 1
+            if depth == 0:
+                return s[i + 1 : j], j + 1
+    return s[i + 1 :], len(s)
+
+
+def _arg(s: str, i: int):
+    """One LaTeX macro argument starting at s[i] (after spaces): a brace group or a single token."""
+    while i < len(s) and s[i] == " ":
+        i += 1
+    if i >= len(s):
+        return "", i
+    if s[i] == "{":
+        return _braced(s, i)
+    if s[i] == "\\":
+        m = re.match(r"\\[a-zA-Z]+", s[i:])
+        if m:
+            return m.group(0), i + len(m.group(0))
+    return s[i], i + 1
+
+
+_LATEX_WORDS = {
+    "\\pi": "pi", "\\infty": "oo", "\\cdot": "*", "\\times": "*", "\\div": "/", "\\ln": "log",
+    "\\log": "log", "\\sin": "sin", "\\cos": "cos", "\\tan": "tan", "\\exp": "exp", "\\e": "E",
+}
+
+
+def latex_to_sympy_text(s: str) -> str:
+    """Rewrite a LaTeX math answer into text that sympy's parser reads: nested ``\\frac`` /
+    ``\\dfrac`` / ``\\tfrac``, ``\\sqrt[n]{x}``, braces after ``^``, ``\\pi``, ``\\infty``, products,
+    ``\\left`` / ``\\right`` sizing, and mixed numbers (``2\\frac{1}{2}`` = 5/2)."""
+    s = _strip_wrappers(str(s))
+    for tok in ("\\left", "\\right", "\\!", "\\,", "\\;", "\\:", "\\displaystyle", "$"):
+        s = s.replace(tok, "")
+    s = s.replace("\\{", "{").replace("\\}", "}")
+    out = []
+    i = 0
+    while i < len(s):
+        if s.startswith("\\sqrt", i):
+            i += 5
+            index = None
+            if i < len(s) and s[i] == "[":
+                k = s.index("]", i)
+                index, i = s[i + 1 : k], k + 1
+            body, i = _arg(s, i)
+            body = latex_to_sympy_text(body)
+            out.append(f"(({body})**(1/({latex_to_sympy_text(index)})))" if index else f"sqrt({body})")
+            continue
+        m = re.match(r"\\[dt]?frac", s[i:])
+        if m:
+            num, j = _arg(s, i + len(m.group(0)))
+            den, j = _arg(s, j)
+            num_t, den_t = latex_to_sympy_text(num), latex_to_sympy_text(den)
+            # mixed number: an integer written right before a fraction of integers
+            prev = "".join(out).rstrip()
+            lead = re.search(r"(?:^|[^\w.)])(\d+)$", prev)
+            if lead and num_t.strip().isdigit() and den_t.strip().isdigit():
+                out = [prev[: len(prev) - len(lead.group(1))], f"({lead.group(1)}+({num_t})/({den_t}))"]
+            else:
+                out.append(f"(({num_t})/({den_t}))")
+            i = j
+            continue
+        if s[i] == "^":
+            body, i = _arg(s, i + 1)
+            out.append(f"**({latex_to_sympy_text(body)})")
+            continue
+        m = re.match(r"\\[a-zA-Z]+", s[i:])
+        if m:
+            word = m.group(0)
+            out.append(_LATEX_WORDS.get(word, word[1:]))
+            i += len(word)
+            continue
+        out.append(s[i])
+        i += 1
+    text = "".join(out).replace("{", "(").replace("}", ")")
+    return text
+
+
+def _split_top(s: str, sep: str = ","):
+    parts, depth, cur = [], 0, ""
+    for ch in s:
+        if ch in "([{":
+            depth += 1
+        elif ch in ")]}":
+            depth -= 1
+        if ch == sep and depth == 0:
+            parts.append(cur)
+            cur = ""
+        else:
+            cur += ch
+    parts.append(cur)
+    return [p.strip() for p in parts]
+
+
+def _parse_sympy(text: str):
+    import sympy
+    from sympy.parsing.sympy_parser import (convert_xor, implicit_multiplication_application, parse_expr,
+                                            standard_transformations)
+
+    tr = standard_transformations + (implicit_multiplication_application, convert_xor)
+    text = text.strip()
+    if "=" in text:  # "x = 3" -> 3; an equation of expressions compares as lhs - rhs
+        lhs, rhs = text.split("=", 1)
+        if re.fullmatch(r"\s*[a-zA-Z]\s*", lhs):
+            text = rhs
+        else:
+            return sympy.simplify(parse_expr(lhs, transformations=tr) - parse_expr(rhs, transformations=tr))
+    return parse_expr(text, transformations=tr, evaluate=True)
+
+
+def _expr_equal(a_text: str, b_text: str) -> bool:
+    import sympy
+
+    a, b = _parse_sympy(a_text), _parse_sympy(b_text)
+    try:
+        if sympy.simplify(a - b) == 0:
+            return True
+    except Exception:
+        pass
+    try:
+        fa, fb = complex(sympy.N(a)), complex(sympy.N(b))
+        return abs(fa - fb) <= 1e-6 * max(1.0, abs(fa), abs(fb))
+    except Exception:
+        return False
+
+
+def _plus_minus(text: str):
+    if "\\pm" not in text:
+        return None
+    lhs, rhs = text.split("\\pm", 1)
+    return [f"{lhs}+{rhs}", f"{lhs}-{rhs}"]
+
+
 def _sympy_equal(pred: str, gt: str) -> bool:
+    """LaTeX-aware symbolic comparison: single expressions, ``\\pm`` pairs, ordered tuples, unordered
+    sets (``\\{...\\}`` or bare comma lists) and intervals (bracket types must match)."""
     try:
-        import sympy
-        from sympy.parsing.sympy_parser import (implicit_multiplication_application, parse_expr,
-                                                standard_transformations)
+        import sympy  # noqa: F401
     except Exception:
         return False
-    tr = standard_transformations + (implicit_multiplication_application,)
     try:
-        a = parse_expr(pred.replace("^", "**"), transformations=tr, evaluate=True)
-        b = parse_expr(gt.replace("^", "**"), transformations=tr, evaluate=True)
-        return bool(sympy.simplify(a - b) == 0)
+        pm_p, pm_g = _plus_minus(pred), _plus_minus(gt)
+        if pm_p or pm_g:
+            ps = pm_p or _split_top(pred)
+            gs = pm_g or _split_top(gt)
+            return _lists_equal(ps, gs, ordered=False)
+        p, g = latex_to_sympy_text(pred).strip(), latex_to_sympy_text(gt).strip()
+        interval = re.compile(r"^([\[(])(.*)([\])])$")
+        mp, mg = interval.match(p), interval.match(g)
+        if mp and mg and len(_split_top(mp.group(2))) == 2 and len(_split_top(mg.group(2))) == 2:
+            if mp.group(1) + mp.group(3) != mg.group(1) + mg.group(3) and "(" not in (mp.group(1) + mg.group(1)):
+                return False
+            ordered = True
+            return (mp.group(1) == mg.group(1) and mp.group(3) == mg.group(3)
+                    and _lists_equal(_split_top(mp.group(2)), _split_top(mg.group(2)), ordered))
+        is_set = pred.strip().startswith("\\{") or gt.strip().startswith("\\{")
+        if is_set:
+            p, g = p.strip("() "), g.strip("() ")
+        ps, gs = _split_top(p), _split_top(g)
+        if len(ps) > 1 or len(gs) > 1:
+            return _lists_equal(ps, gs, ordered=not is_set and not (len(ps) > 1 and len(gs) > 1 and
+                                                                    not p.startswith("(")))
+        return _expr_equal(p, g)
     except Exception:
         return False
+
+
+def _lists_equal(ps, gs, ordered: bool) -> bool:
+    if len(ps) != len(gs):
+        return False
+    ps = [latex_to_sympy_text(x) for x in ps]
+    gs = [latex_to_sympy_text(x) for x in gs]
+    if ordered:
+        return all(_expr_equal(a, b) for a, b in zip(ps, gs))
+    left = list(gs)
+    for a in ps:
+        hit = next((k for k, b in enumerate(left) if _expr_equal(a, b)), None)
+        if hit is None:
+            return False
+        left.pop(hit)
+    return True
 
 
 def _math_verify_equal(pred: str, gt: str) -> bool:
@@ -181,7 +357,7 @@ def grade_answer(pred: str, gt: str, fast: bool = True) -> bool:
         return True
     if fast:
         return False
-    return _sympy_equal(p, g) or _math_verify_equal(pred, gt)
+    return _sympy_equal(pred, gt) or _math_verify_equal(pred, gt)
 
 
 def r1_zero_reward_fn(response: str, ground_truth: Union[str, int, float, Iterable], fast: bool = True) -> Dict[str, float]:

@@ -116,3 +116,25 @@ def test_gsm8k_loop_end_to_end_cpu(tmp_path):
     for r in steps:
         assert "Rollout/GlobalRewardSumMean" in r and "Rollout/AbortRate" in r
     assert steps[0]["Infer/TokensPerSec"] > 0
+
+
+@pytest.mark.parametrize("pred,gt,want", [
+    (r"\frac{\sqrt{3}}{2}", r"\dfrac{\sqrt3}{2}", True),
+    (r"\frac{1}{\frac{1}{2}}", "2", True),
+    (r"2\frac{1}{2}", "5/2", True),
+    (r"\sqrt[3]{8}", "2", True),
+    (r"x^{2}+2x+1", "(x+1)^2", True),
+    (r"\pi/2", r"\frac{\pi}{2}", True),
+    (r"3 \pm \sqrt{2}", r"3-\sqrt2, 3+\sqrt2", True),
+    (r"\{1, 2, 3\}", r"\{3,1,2\}", True),
+    (r"(1, 2)", r"(2, 1)", False),
+    (r"[0, 1)", r"[0,1)", True),
+    (r"[0, 1)", r"[0,1]", False),
+    (r"x = 5", "5", True),
+    (r"2\sqrt{2}", r"\sqrt{8}", True),
+    (r"\frac{3}{4}", "0.76", False),
+])
+def test_grader_latex_equivalence(pred, gt, want):
+    from accerl_agent_b200.rewards.math_grader import grade_answer
+
+    assert grade_answer(pred, gt, fast=False) is want
