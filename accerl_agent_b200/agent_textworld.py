@@ -88,6 +88,33 @@ def sync_weights(engines, trainers, scope: str) -> Dict[str, float]:
     return {"elapsed_s": elapsed, "device_ms": dev_ms, "bytes": nbytes}
 
 
+def check_rollout_side(engines, followers) -> None:
+    """Raise if a rollout worker, an engine process or a tensor-parallel engine rank has failed."""
+    for e in engines:
+        if not e.alive:
+            raise RuntimeError("an inference engine process exited")
+        err = get(e.check_workers.remote(), timeout=60)
+        if err:
+            raise RuntimeError(f"A rollout worker exited unexpectedly: {err}")
+    for fs in followers:
+        for f in fs:
+            err = f.check()
+            if err:
+                raise RuntimeError(f"A tensor-parallel engine rank failed: {err}")
+
+
+def _await_training(pending, engines, followers, poll_s: float = 5.0):
+    """Results of the trainers' segment calls. While they run, the rollout side is checked every
+    ``poll_s`` seconds: trainers waiting for samples from a dead engine would otherwise wait forever."""
+    import concurrent.futures as cf
+
+    while True:
+        _, rest = cf.wait(pending, timeout=poll_s, return_when=cf.ALL_COMPLETED)
+        if not rest:
+            return get(pending)
+        check_rollout_side(engines, followers)
+
+
 def run_train(args) -> Dict[str, float]:
     import multiprocessing as mp
 
@@ -136,18 +163,11 @@ def run_train(args) -> Dict[str, float]:
         last_ckpt = None
         reached_max = False
         while not reached_max:
-            for e in engines:
-                err = get(e.check_workers.remote())
-                if err:
-                    raise RuntimeError(f"A rollout worker exited unexpectedly: {err}")
-            for fs in followers:
-                for f in fs:
-                    err = f.check()
-                    if err:
-                        raise RuntimeError(f"A tensor-parallel engine rank failed: {err}")
+            check_rollout_side(engines, followers)
             infer_start = sum(s["total_tokens"] for s in get([e.get_stats.remote() for e in engines]))
             t0 = time.perf_counter()
-            summaries = get([t.train_until_next_sync.remote(args.sync_every_optimizer_steps) for t in trainers])
+            pending = [t.train_until_next_sync.remote(args.sync_every_optimizer_steps) for t in trainers]
+            summaries = _await_training(pending, engines, followers)
             elapsed = time.perf_counter() - t0
             infer_end = sum(s["total_tokens"] for s in get([e.get_stats.remote() for e in engines]))
             while True:
