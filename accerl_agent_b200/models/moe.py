@@ -18,26 +18,49 @@ import torch
 from .. import ops
 
 
-def route(model, layer: int, h: torch.Tensor, counts: bool = False):
+def gate_pair(model, layer: int, grads: bool = False) -> Optional[torch.Tensor]:
+    """[router weight; shared-expert gate weight] as one [E + 1, H] view of the flat parameter (or
+    fp32 gradient) buffer, or None when the layer has no shared expert or the two are not adjacent."""
+    p = f"model.layers.{layer}.mlp."
+    slots = model.layout.slots
+    a, b = slots.get(p + "gate.weight"), slots.get(p + "shared_expert_gate.weight")
+    if a is None or b is None or a.offset + a.numel != b.offset or a.trainable != b.trainable:
+        return None
+    E, H = a.shape
+    if grads:
+        if not a.trainable or model.grads is None:
+            return None
+        return model.grads[a.grad_offset : a.grad_offset + (E + 1) * H].view(E + 1, H)
+    return model.params[a.offset : a.offset + (E + 1) * H].view(E + 1, H)
+
+
+def route(model, layer: int, h: torch.Tensor, counts: bool = False, shared_gate: Optional[list] = None):
     """Router probabilities, top-k weights and expert ids (and, with ``counts``, rows per expert).
 
     On the GPU the logits come from the tcgen05 GEMM (fp32 out, rounded to bf16 as the reference's
     bf16 linear gives them) and one fused kernel does softmax, top-k, renormalisation and the
-    per-expert counts (``moe_router_kernel``, HF ``Qwen2MoeTopKRouter``)."""
+    per-expert counts (``moe_router_kernel``, HF ``Qwen2MoeTopKRouter``). When ``shared_gate`` is a
+    list and the layer has a shared expert, the same GEMM also computes the shared-expert gate logit
+    (column E over ``gate_pair``) and the kernel appends sigmoid of it ([T] fp32) to the list."""
     cfg = model.cfg
     p = f"model.layers.{layer}.mlp."
     Wg = model.w(p + "gate.weight")
     E, k = cfg.num_experts, cfg.num_experts_per_tok
     if h.is_cuda and h.dtype == torch.bfloat16 and E <= 128 and k <= 8 and h.shape[0] > 0:
         T = h.shape[0]
-        ld = (E + 3) // 4 * 4
-        logits = ops.workspace(h.device, "router_logits", T * ld).view(T, ld)[:, :E]
-        ops.gemm(h, Wg, logits, out_dtype=torch.float32)
+        pair = gate_pair(model, layer) if shared_gate is not None else None
+        ncol = E + (1 if pair is not None else 0)
+        ld = (ncol + 3) // 4 * 4
+        logits = ops.workspace(h.device, "router_logits", T * ld).view(T, ld)[:, :ncol]
+        ops.gemm(h, pair if pair is not None else Wg, logits, out_dtype=torch.float32)
         probs = torch.empty(T, E, dtype=torch.float32, device=h.device)
         topw = torch.empty(T, k, dtype=torch.float32, device=h.device)
         topi = torch.empty(T, k, dtype=torch.long, device=h.device)
         cnt = torch.zeros(E, dtype=torch.int32, device=h.device)
-        ops.native().moe_router(logits, E, k, bool(cfg.norm_topk_prob), probs, topw, topi, cnt)
+        sg = torch.empty(T, dtype=torch.float32, device=h.device) if pair is not None else None
+        ops.native().moe_router(logits, E, k, bool(cfg.norm_topk_prob), probs, topw, topi, cnt, sg)
+        if sg is not None:
+            shared_gate.append(sg)
         return (probs, topw, topi, cnt) if counts else (probs, topw, topi)
     logits = (h @ Wg.t()).float()
     probs = torch.softmax(logits, dim=-1)
@@ -227,8 +250,10 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     k = cfg.num_experts_per_tok
     ep = getattr(model, "expert_parallel", None)
     if ep is None and h.is_cuda and h.dtype == torch.bfloat16:
-        probs, topw, topi, counts = route(model, layer, h, counts=True)
-        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi, counts)
+        shared_gate: list = []
+        probs, topw, topi, counts = route(model, layer, h, counts=True, shared_gate=shared_gate)
+        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi, counts,
+                                   sg=shared_gate[0].view(-1, 1) if shared_gate else None)
     probs, topw, topi = route(model, layer, h)
     w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
@@ -285,7 +310,9 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     return out, cache
 
 
-def _shared_expert(model, layer: int, h: torch.Tensor, cache):
+def _shared_expert(model, layer: int, h: torch.Tensor, cache, sg: Optional[torch.Tensor] = None):
+    """Shared expert output and its sigmoid gate ([T, 1] fp32; computed here unless the router
+    kernel already produced it)."""
     cfg = model.cfg
     if cfg.shared_expert_intermediate_size <= 0:
         return None, None
@@ -296,13 +323,14 @@ def _shared_expert(model, layer: int, h: torch.Tensor, cache):
     else:
         sact, sgu = ops.linear_swiglu(h, model.w(p + "shared_expert.gate_up_proj.weight"))
     sy = ops.linear(sact, model.w(p + "shared_expert.down_proj.weight"))
-    sg = torch.sigmoid((h @ model.w(p + "shared_expert_gate.weight").t()).float())
+    if sg is None:
+        sg = torch.sigmoid((h @ model.w(p + "shared_expert_gate.weight").t()).float())
     if cache is not None:
         cache.update(sgu=sgu, sact=sact, sy=sy, sg=sg)
     return sy, sg
 
 
-def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi, counts=None):
+def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi, counts=None, sg=None):
     """CUDA path without host synchronisation: device-side padded layout, grouped GEMMs over the
     bounded tile count, fused combine. Training (``save``) zeroes the padded input rows because the
     weight-gradient contraction runs over them; inference leaves them uninitialised (their output
@@ -327,13 +355,60 @@ def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw,
     w_pairs = torch.empty(n_pairs, dtype=torch.float32, device=h.device)
     w_pairs[order] = torch.where(valid, w_sorted, torch.zeros_like(w_sorted))
     cache: Dict[str, torch.Tensor] = {}
-    sy, sg = _shared_expert(model, layer, h, cache if save else None)
+    sy, sg = _shared_expert(model, layer, h, cache if save else None, sg)
     out = ops.moe_combine(ys_full, pos_pairs, w_pairs, k, residual=residual, shared=sy, sg=sg)
     if save:
         cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=xs[:R], gu=gu, act=act,
                      ys=ys_full, pos_pairs=pos_pairs, w_pairs=w_pairs)
         cache["layout"] = lay  # type: ignore[assignment]
     return out, cache
+
+
+def _router_shared_backward_device(model, layer: int, m, h: torch.Tensor, dx3: torch.Tensor, dw: torch.Tensor,
+                                   dh: torch.Tensor) -> torch.Tensor:
+    """GPU backward of the router and the shared expert, added into ``dh`` ([T, H] fp32).
+
+    ``moe_router_bwd`` (one warp per token) turns the routing-weight gradients into router-logit
+    gradients and, with a shared expert, appends the gate-logit gradient as column E and writes the
+    gate-scaled output gradient dsy. Two tcgen05 GEMMs against [router; shared gate] (one
+    [E + 1, H] view of the flat buffers) then give the input gradient and the weight gradients of
+    both; the shared expert's MLP backward follows from dsy."""
+    cfg = model.cfg
+    p = f"model.layers.{layer}.mlp."
+    T, H = dx3.shape
+    E, k = cfg.num_experts, cfg.num_experts_per_tok
+    shared = cfg.shared_expert_intermediate_size > 0
+    pair = gate_pair(model, layer) if shared else None
+    E_pad = (E + 1 + 63) // 64 * 64
+    dlog = ops.workspace(dx3.device, "router_dlogits", T * E_pad, dtype=torch.bfloat16).view(T, E_pad)
+    dsy = torch.empty_like(dx3) if shared else None
+    sg = m["sg"].reshape(-1).float().contiguous() if shared else None
+    ops.native().moe_router_bwd(m["probs"], m["topi"], m["topw"].float().contiguous(),
+                                dw.reshape(-1, k).float().contiguous(), bool(cfg.norm_topk_prob),
+                                dx3 if shared else None, m["sy"] if shared else None, sg, dlog, dsy)
+    if shared:
+        if pair is None:
+            raise RuntimeError("the shared-expert gate must follow the router in the parameter layout")
+        ncol, W, G = E + 1, pair, gate_pair(model, layer, grads=True)
+    else:
+        ncol, W, G = E, model.w(p + "gate.weight"), model.g(p + "gate.weight")
+    ops.gemm(dlog[:, :ncol], W, dh, b_mn=True, beta=1.0, out_dtype=torch.float32)  # dh += dlogits [W]
+    if G is not None:
+        ops.linear_wgrad(dlog[:, :ncol], h, G, accumulate=True)
+    if shared:
+        dsact = ops.linear_dgrad(dsy, model.w(p + "shared_expert.down_proj.weight"))
+        g = model.g(p + "shared_expert.down_proj.weight")
+        if g is not None:
+            ops.linear_wgrad(dsy, m["sact"], g)
+        dsgu = ops.swiglu_backward(dsact, m["sgu"])
+        ops.gemm(dsgu, model.w(p + "shared_expert.gate_up_proj.weight"), dh, b_mn=True, beta=1.0,
+                 out_dtype=torch.float32)
+        g = model.g(p + "shared_expert.gate_up_proj.weight")
+        if g is not None:
+            ops.linear_wgrad(dsgu, h, g)
+    out = torch.empty(T, H, dtype=dx3.dtype, device=dx3.device)
+    ops.native().splitk_finish(dh, None, None, out)
+    return out
 
 
 def moe_backward(model, layer: int, dx3: torch.Tensor, c) -> torch.Tensor:
@@ -362,6 +437,8 @@ def moe_backward(model, layer: int, dx3: torch.Tensor, c) -> torch.Tensor:
         dxs = experts_backward(model, layer, dys, m["xs"], m["gu"], m["act"], bounds)
     # every pair's input-gradient row back to its token (unit weights)
     dh = ops.moe_combine(dxs, pos_pairs, torch.ones_like(w_pairs), k).float()
+    if dx3.is_cuda and dx3.dtype == torch.bfloat16:
+        return _router_shared_backward_device(model, layer, m, h, dx3c, dw, dh)
     # router
     dtopw = dw.view(-1, k)
     topw = m["topw"]

@@ -42,13 +42,15 @@ def parameter_specs(cfg: ModelConfig) -> List[Tuple[str, Tuple[int, ...]]]:
             E, Im = cfg.num_experts, cfg.moe_intermediate_size
             El = cfg.local_experts or E
             specs.append((p + "mlp.gate.weight", (E, H)))
+            if cfg.shared_expert_intermediate_size > 0:
+                # right after the router so that [router; shared gate] is one [E + 1, H] matrix
+                specs.append((p + "mlp.shared_expert_gate.weight", (1, H)))
             specs.append((p + "mlp.experts.gate_up_proj", (El, 2 * Im, H)))
             specs.append((p + "mlp.experts.down_proj", (El, H, Im)))
             if cfg.shared_expert_intermediate_size > 0:
                 Is = cfg.shared_expert_intermediate_size
                 specs.append((p + "mlp.shared_expert.gate_up_proj.weight", (2 * Is, H)))
                 specs.append((p + "mlp.shared_expert.down_proj.weight", (H, Is)))
-                specs.append((p + "mlp.shared_expert_gate.weight", (1, H)))
         else:
             specs.append((p + "mlp.gate_up_proj.weight", (2 * cfg.intermediate_size, H)))
             specs.append((p + "mlp.down_proj.weight", (H, cfg.intermediate_size)))
@@ -324,9 +326,9 @@ class CausalLM:
         x, caches = self.forward_hidden(ids, pos, cu, max_seqlen, save)
         hN, rstdN = ops.rmsnorm(x, self.w("model.norm.weight"), self.cfg.rms_norm_eps)
         rows = hN.index_select(0, pred_idx)
-        logits = ops.linear(rows, self.w(self.lm_head_name))
-        lp, lse, ent = ops.logsoftmax_label(logits, labels, with_entropy=with_entropy)
-        ctx = ForwardCtx(ids, pos, cu, max_seqlen, caches, x, rstdN, pred_idx, rows, logits, labels, lse,
+        # vocabulary-chunked LM head: no [targets, vocab] logits tensor is built
+        lp, lse, ent = ops.lm_head_logprobs(rows, self.w(self.lm_head_name), labels, with_entropy=with_entropy)
+        ctx = ForwardCtx(ids, pos, cu, max_seqlen, caches, x, rstdN, pred_idx, rows, None, labels, lse,
                          self.first_trainable_layer)
         if with_entropy:
             ctx.entropy = ent  # type: ignore[attr-defined]
@@ -335,14 +337,12 @@ class CausalLM:
     # ---------------------------------------------------------------- backward
     def backward_from_logprobs(self, dlp: torch.Tensor, ctx: ForwardCtx) -> None:
         cfg = self.cfg
-        dlogits = ops.logsoftmax_label_backward(ctx.logits, ctx.labels, ctx.lse, dlp.float())
         W = self.w(self.lm_head_name)
         gW = self.g(self.lm_head_name)
-        if gW is not None:
-            ops.linear_wgrad(dlogits, ctx.rows, gW, accumulate=True)
-        if self.first_trainable_layer >= cfg.num_hidden_layers and self.g("model.norm.weight") is None:
+        need_drows = not (self.first_trainable_layer >= cfg.num_hidden_layers and self.g("model.norm.weight") is None)
+        drows = ops.lm_head_backward(ctx.rows, W, ctx.labels, ctx.lse, dlp.float(), gW, need_drows)
+        if not need_drows:
             return
-        drows = ops.linear_dgrad(dlogits, W)
         dhN = torch.zeros_like(ctx.x_final)
         dhN.index_copy_(0, ctx.pred_idx, drows)
         dx = ops.rmsnorm_backward(dhN, ctx.x_final, self.w("model.norm.weight"), ctx.rstd_final,

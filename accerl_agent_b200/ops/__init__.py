@@ -75,6 +75,8 @@ __all__ = [
     "attention_varlen_backward",
     "logsoftmax_label",
     "logsoftmax_label_backward",
+    "lm_head_logprobs",
+    "lm_head_backward",
     "policy_loss",
     "grad_sumsq",
     "adamw_step",
@@ -434,13 +436,77 @@ def logsoftmax_label(logits: torch.Tensor, labels: torch.Tensor, with_entropy: b
 def logsoftmax_label_backward(logits: torch.Tensor, labels: torch.Tensor, lse: torch.Tensor, grad: torch.Tensor):
     """Overwrites ``logits`` with d(logits) = grad * (onehot - softmax)."""
     if logits.is_cuda:
-        native().logsoftmax_label_bwd(logits, labels, lse, grad)
+        native().logsoftmax_label_bwd(logits, labels, lse, grad, 0)
         return logits
     probs = torch.exp(logits.float() - lse.unsqueeze(1))
     d = -probs * grad.unsqueeze(1)
     d[torch.arange(logits.shape[0]), labels] += grad
     logits.copy_(d.to(logits.dtype))
     return logits
+
+
+# Vocabulary columns per chunk of the response-only LM head: the [rows, chunk] bf16 buffer is all that
+# is ever materialised of the logits (36 MB for 1100 rows), instead of [rows, 151936].
+LM_HEAD_CHUNK = 16384
+
+
+def lm_head_logprobs(rows: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, with_entropy: bool = False,
+                     chunk: int = LM_HEAD_CHUNK):
+    """Response-only LM head (accerl_agent/agent_textworld.py:855-871, ``logits_to_keep`` +
+    cross-entropy): per row the label log-probability of ``rows @ w^T``, its log-sum-exp and,
+    optionally, the entropy. On the GPU the vocabulary is processed in chunks: a tcgen05 GEMM writes one
+    [rows, chunk] tile of logits, which a kernel folds into a running (max, sum exp, sum exp * x,
+    label logit) per row. Returns (logprob, lse, entropy or None), all fp32."""
+    if not rows.is_cuda:
+        lp, lse, ent = logsoftmax_label(linear(rows, w), labels, with_entropy)
+        return lp, lse, ent
+    n, V = rows.shape[0], w.shape[0]
+    state = workspace(rows.device, "lm_head_state", 4 * n).view(n, 4)
+    buf = workspace(rows.device, "lm_head_chunk", n * min(chunk, V), dtype=rows.dtype)
+    for c0 in range(0, V, chunk):
+        cw = min(chunk, V - c0)
+        logits = buf[: n * cw].view(n, cw)
+        linear(rows, w[c0 : c0 + cw], out=logits)
+        native().lse_chunk(logits, labels, c0, c0 == 0, state)
+    lp = torch.empty(n, dtype=torch.float32, device=rows.device)
+    lse = torch.empty_like(lp)
+    ent = torch.empty_like(lp) if with_entropy else None
+    native().lse_finish(state, lp, lse, ent)
+    return lp, lse, ent
+
+
+def lm_head_backward(rows: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, lse: torch.Tensor,
+                     grad: torch.Tensor, grad_w: Optional[torch.Tensor] = None, need_drows: bool = True,
+                     chunk: int = LM_HEAD_CHUNK) -> Optional[torch.Tensor]:
+    """Backward of ``lm_head_logprobs`` for d(logprob) = ``grad``: recomputes every logits chunk,
+    turns it in place into d(logits) = grad * (onehot - softmax), accumulates ``grad_w`` (fp32 [V, H],
+    optional) and, with ``need_drows``, returns d(rows) (accumulated in fp32 over the chunks)."""
+    if not rows.is_cuda:
+        logits = linear(rows, w)
+        dlogits = logsoftmax_label_backward(logits, labels, lse, grad)
+        if grad_w is not None:
+            linear_wgrad(dlogits, rows, grad_w, accumulate=True)
+        return linear_dgrad(dlogits, w) if need_drows else None
+    n, V = rows.shape[0], w.shape[0]
+    buf = workspace(rows.device, "lm_head_chunk", n * min(chunk, V), dtype=rows.dtype)
+    dacc = None
+    if need_drows:
+        dacc = workspace(rows.device, "lm_head_drows", n * rows.shape[1]).view(n, rows.shape[1])
+        dacc.zero_()
+    for c0 in range(0, V, chunk):
+        cw = min(chunk, V - c0)
+        logits = buf[: n * cw].view(n, cw)
+        linear(rows, w[c0 : c0 + cw], out=logits)
+        native().logsoftmax_label_bwd(logits, labels, lse, grad, c0)
+        if grad_w is not None:
+            linear_wgrad(logits, rows, grad_w[c0 : c0 + cw], accumulate=True)
+        if need_drows:
+            gemm(logits, w[c0 : c0 + cw], dacc, b_mn=True, beta=1.0, out_dtype=torch.float32, splits=1)
+    if not need_drows:
+        return None
+    drows = torch.empty(n, rows.shape[1], dtype=rows.dtype, device=rows.device)
+    native().splitk_finish(dacc, None, None, drows)
+    return drows
 
 
 def policy_loss(lp, old_lp, adv, cfg, loss_scale: float):

@@ -261,6 +261,9 @@ class GenerationEngine:
         self._abort_all("abort")
 
     def _run_loop(self) -> None:
+        # the CUDA current device is per thread: this thread launches on the engine's GPU
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
         while True:
             with self._lock:
                 while not self._stop and self._inflight is None and (

@@ -19,6 +19,7 @@ import itertools
 import multiprocessing as mp
 import os
 import pickle
+import sys
 import threading
 import traceback
 from typing import Any, Callable, Dict, Iterable, List, Optional, Sequence, Tuple
@@ -37,6 +38,20 @@ def _resolve(factory):
         mod, _, attr = factory.rpartition(":")
         return getattr(importlib.import_module(mod), attr)
     return factory
+
+
+def _current_cuda_device() -> Optional[int]:
+    torch = sys.modules.get("torch")
+    if torch is None or not torch.cuda.is_initialized():
+        return None
+    return torch.cuda.current_device()
+
+
+def _select_cuda_device(device: Optional[int]) -> None:
+    if device is not None:
+        import torch
+
+        torch.cuda.set_device(device)
 
 
 def _actor_main(factory, args, kwargs, conn, env: Dict[str, str]):
@@ -58,7 +73,12 @@ def _actor_main(factory, args, kwargs, conn, env: Dict[str, str]):
 
     loop = asyncio.new_event_loop()
     asyncio.set_event_loop(loop)
-    sync_pool = cf.ThreadPoolExecutor(max_workers=1, thread_name_prefix="actor-sync")
+    # Plain methods run on a pool thread. The CUDA current device is per thread, so that thread takes
+    # the device the constructor selected (an actor drives one GPU); otherwise kernels launched from it
+    # would go to device 0.
+    device = _current_cuda_device()
+    sync_pool = cf.ThreadPoolExecutor(max_workers=1, thread_name_prefix="actor-sync",
+                                      initializer=_select_cuda_device, initargs=(device,))
     stopping = asyncio.Event()
 
     async def handle(call_id, method, a, k):

@@ -38,7 +38,22 @@ def parse():
     ap.add_argument("--token-budget", type=int, default=16384)
     ap.add_argument("--max-length", type=int, default=8192)
     ap.add_argument("--model", default="qwen2.5-1.5b")
+    ap.add_argument("--expert-parallel", action="store_true",
+                    help="MoE models: experts partitioned over the ranks, token dispatch/combine over NVLink")
     return ap.parse_args()
+
+
+def model_desc(name: str) -> str:
+    if name == "qwen2.5-1.5b":
+        return MODEL_DESC
+    from accerl_agent_b200.models.config import get_preset
+
+    c = get_preset(name)
+    moe = (f", {c.num_experts} experts top-{c.num_experts_per_tok} (I{c.moe_intermediate_size}"
+           f"{f', shared {c.shared_expert_intermediate_size}' if c.shared_expert_intermediate_size else ''})"
+           if c.num_experts else f", I{c.intermediate_size}")
+    return (f"{name}-shape {'MoE' if c.num_experts else 'dense'} ({c.num_hidden_layers}L, H{c.hidden_size}, "
+            f"{c.num_attention_heads}q/{c.num_key_value_heads}kv heads{moe}, V{c.vocab_size})")
 
 
 def dist_env():
@@ -83,7 +98,7 @@ def run_native(a):
         tw_history_token_window=a.max_length, batch_size=a.batch_size, grad_accum_steps=a.grad_accum_steps,
         train_logprob_mode="response_only_lm_head", rl_algorithm="grpo", clip_mode="ppo", clip_eps=0.2,
         learning_rate=1e-6, lr_warmup_steps=0, max_steps=10**6, dtype="bfloat16", fsdp_world_size=world,
-        device="cuda", seed=42,
+        device="cuda", seed=42, expert_parallel=a.expert_parallel,
     )
     pool = synthetic_pool(rank, 256, a.max_length)
     replay = ReplayBuffer(args.replay_capacity, seed=rank)
@@ -175,12 +190,12 @@ def run_native(a):
             "data": "synthetic (seeded synthetic text-game episodes, random-init weights)",
             "impl": "native",
             "config": {
-                "model": MODEL_DESC,
+                "model": model_desc(a.model),
                 "global_batch": a.batch_size * a.grad_accum_steps * world,
                 "seq_len": a.max_length,
                 "token_budget_per_pack": a.token_budget,
                 "grad_accum_steps": a.grad_accum_steps,
-                "parallelism": f"fsdp{world}",
+                "parallelism": f"fsdp{world}" + (f"+ep{world}" if a.expert_parallel and world > 1 else ""),
                 "algorithm": "grpo advantages + ppo clip 0.2, varlen packing, response-only LM head",
                 "l2": "inputs larger than L2 (GBs of weights/activations per step); no flush needed",
             },

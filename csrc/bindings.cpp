@@ -41,8 +41,11 @@ int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w,
                            cudaStream_t s);
 int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* pos, const float* w, long long T, int k,
                            int H, void* dys, float* dw, long long R, cudaStream_t s);
-int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs,
-                      float* topw, long long* topi, int* counts, cudaStream_t s);
+int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs, float* topw,
+                      long long* topi, int* counts, float* sg, cudaStream_t s);
+int accerl_moe_router_bwd(const float* probs, const long long* topi, const float* topw, const float* dw, int T, int E,
+                          int k, int norm_topk, const void* dout, const void* sy, const float* sg, int H, void* dgrad,
+                          int E_pad, void* dsy, cudaStream_t s);
 int accerl_weight_pull(const long long* desc, const long long* unit_start, int n_desc, long long n_units,
                        const void* src, void* dst, cudaStream_t s);
 int accerl_splitk_finish(const float* acc, long long lda, const void* bias, const void* residual, long long ldr,
@@ -63,7 +66,10 @@ int accerl_embedding_bwd(const long long* ids, const void* dout, float* grad, in
 int accerl_logsoftmax_label_fwd(const void* logits, long long ld, const long long* labels, float* logprob, float* lse,
                                 float* entropy, int rows, int V, cudaStream_t s);
 int accerl_logsoftmax_label_bwd(void* logits, long long ld, const long long* labels, const float* lse,
-                                const float* grad, int rows, int V, cudaStream_t s);
+                                const float* grad, int rows, int V, long long label_offset, cudaStream_t s);
+int accerl_lse_chunk(const void* logits, long long ld, const long long* labels, long long c0, int rows, int V,
+                     int first, float* state, cudaStream_t s);
+int accerl_lse_finish(const float* state, int rows, float* logprob, float* lse, float* entropy, cudaStream_t s);
 int accerl_policy_loss(const float* lp, const float* old_lp, const float* adv, float* dlp, double* stats, int n,
                        int mode, float clip_eps, float gipo_sigma, float tau_pos, float tau_neg, float kl_coef,
                        float loss_scale, cudaStream_t s);
@@ -194,6 +200,7 @@ void gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn, at::Te
 void gemm_rope(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
                const at::Tensor& pos, int64_t rope_cols, double theta, const c10::optional<at::Tensor>& status,
                int64_t block_n, int64_t max_ctas) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(x));
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_BF16(w);
@@ -211,6 +218,7 @@ void gemm_rope(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const 
 // h = silu(x Wg^T) * (x Wu^T) for w = [Wg; Wu] ([2I, K]); gu (optional, [M, 2I]) keeps the gate|up outputs.
 void gemm_glu(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& gu, at::Tensor& h,
               const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(x));
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_BF16(w);
@@ -231,6 +239,7 @@ void gemm_glu(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::
 // dgu = SwiGLU backward of (dy Wd) given gu; dy [M, K], wd [K, I] (the down projection), gu/dgu [M, 2I].
 void gemm_dglu(const at::Tensor& dy, const at::Tensor& wd, const at::Tensor& gu, at::Tensor& dgu,
                const c10::optional<at::Tensor>& status, int64_t block_n, int64_t max_ctas) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(dy));
   CHECK_CUDA(dy);
   CHECK_BF16(dy);
   CHECK_BF16(wd);
@@ -253,6 +262,7 @@ void grouped_gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn
                   const c10::optional<at::Tensor>& row_start, const c10::optional<at::Tensor>& rows,
                   int64_t num_groups, int64_t b_group_stride, int64_t c_group_stride,
                   const c10::optional<at::Tensor>& status, const c10::optional<at::Tensor>& row_dst) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(a));
   CHECK_BF16(a);
   CHECK_BF16(b);
   auto iptr = [](const c10::optional<at::Tensor>& t) -> const int* {
@@ -270,6 +280,7 @@ void grouped_gemm(const at::Tensor& a, bool a_mn, const at::Tensor& b, bool b_mn
 
 void weight_pull(const at::Tensor& desc, const at::Tensor& unit_start, int64_t n_units, int64_t src_addr,
                  at::Tensor& dst) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(desc));
   CHECK_BF16(dst);
   TORCH_CHECK(desc.scalar_type() == at::kLong && unit_start.scalar_type() == at::kLong, "weight_pull: int64 plans");
   check(accerl_weight_pull(reinterpret_cast<const long long*>(desc.data_ptr<int64_t>()),
@@ -282,6 +293,7 @@ void weight_pull(const at::Tensor& desc, const at::Tensor& unit_start, int64_t n
 void tp_allreduce(const at::Tensor& peer_data, const at::Tensor& peer_flags, int64_t rank, int64_t slot,
                   int64_t slot_elems, int64_t n, const c10::optional<at::Tensor>& residual, at::Tensor& out,
                   at::Tensor& ctr, at::Tensor& status) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(peer_data));
   CHECK_BF16(out);
   TORCH_CHECK(ctr.scalar_type() == at::kInt && ctr.numel() >= 2, "tp_allreduce: int32 counter pair");
   if (residual.has_value()) CHECK_BF16(*residual);
@@ -295,20 +307,29 @@ void tp_allreduce(const at::Tensor& peer_data, const at::Tensor& peer_flags, int
 
 // Router: logits fp32 [T, >=E] -> probs [T, E], topw [T, k], topi int64 [T, k]; counts int32 [E] += rows.
 void moe_router(const at::Tensor& logits, int64_t E, int64_t k, bool norm_topk, at::Tensor& probs, at::Tensor& topw,
-                at::Tensor& topi, at::Tensor& counts) {
+                at::Tensor& topi, at::Tensor& counts, const c10::optional<at::Tensor>& sg) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(logits));
   CHECK_F32(logits);
   CHECK_F32(probs);
   CHECK_F32(topw);
   TORCH_CHECK(topi.scalar_type() == at::kLong && counts.scalar_type() == at::kInt, "moe_router: topi int64, counts int32");
+  float* sgp = nullptr;
+  if (sg.has_value()) {
+    CHECK_F32(*sg);
+    TORCH_CHECK(logits.size(1) > E, "moe_router: the shared-gate logit is column E of the logits");
+    sgp = sg->data_ptr<float>();
+  }
   check(accerl_moe_router(logits.data_ptr<float>(), ld_of(logits), logits.size(0), E, k, norm_topk,
                           probs.data_ptr<float>(), topw.data_ptr<float>(),
-                          reinterpret_cast<long long*>(topi.data_ptr<int64_t>()), counts.data_ptr<int>(), cur_stream()),
+                          reinterpret_cast<long long*>(topi.data_ptr<int64_t>()), counts.data_ptr<int>(), sgp,
+                          cur_stream()),
         "moe_router");
 }
 
 void moe_combine_fwd(const at::Tensor& ys, const at::Tensor& pos, const at::Tensor& w, int64_t k,
                      const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& shared,
                      const c10::optional<at::Tensor>& sg, at::Tensor& out) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(ys));
   CHECK_BF16(ys);
   CHECK_BF16(out);
   CHECK_F32(w);
@@ -327,6 +348,7 @@ void moe_combine_fwd(const at::Tensor& ys, const at::Tensor& pos, const at::Tens
 
 void moe_combine_bwd(const at::Tensor& dout, const at::Tensor& ys, const at::Tensor& pos, const at::Tensor& w,
                      int64_t k, at::Tensor& dys, at::Tensor& dw) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(dout));
   CHECK_BF16(dout);
   CHECK_BF16(ys);
   CHECK_BF16(dys);
@@ -341,6 +363,7 @@ void moe_combine_bwd(const at::Tensor& dout, const at::Tensor& ys, const at::Ten
 }
 
 void row_scatter(const at::Tensor& src, const c10::optional<at::Tensor>& src_row, const at::Tensor& dst_addr) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(src));
   CHECK_BF16(src);
   check(accerl_row_scatter(src.data_ptr(), ld_of(src),
                            src_row.has_value() ? reinterpret_cast<const long long*>(src_row->data_ptr<int64_t>())
@@ -352,6 +375,7 @@ void row_scatter(const at::Tensor& src, const c10::optional<at::Tensor>& src_row
 
 void splitk_finish(const at::Tensor& acc, const c10::optional<at::Tensor>& bias,
                    const c10::optional<at::Tensor>& residual, at::Tensor& out) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(acc));
   CHECK_F32(acc);
   CHECK_BF16(out);
   check(accerl_splitk_finish(acc.data_ptr<float>(), ld_of(acc), opt_ptr(bias), opt_ptr(residual),
@@ -362,6 +386,7 @@ void splitk_finish(const at::Tensor& acc, const c10::optional<at::Tensor>& bias,
 
 at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, const c10::optional<at::Tensor>& rstd,
                        double eps) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(x));
   CHECK_CUDA(x);
   CHECK_BF16(x);
   CHECK_BF16(w);
@@ -377,6 +402,7 @@ at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, 
 void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
                  const c10::optional<at::Tensor>& dx_accum, at::Tensor& dx, const c10::optional<at::Tensor>& dw,
                  const c10::optional<at::Tensor>& workspace, bool dw_accumulate) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(dy));
   CHECK_BF16(dy);
   CHECK_BF16(x);
   CHECK_F32(rstd);
@@ -399,6 +425,7 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
 }
 
 void bias_grad(const at::Tensor& dy, at::Tensor& db, at::Tensor& workspace, bool accumulate) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(dy));
   CHECK_BF16(dy);
   CHECK_F32(db);
   const int rows = dy.size(0), N = dy.size(1);
@@ -409,6 +436,7 @@ void bias_grad(const at::Tensor& dy, at::Tensor& db, at::Tensor& workspace, bool
 }
 
 void rope(at::Tensor& qkv, const at::Tensor& pos, int64_t n_rot_heads, int64_t head_dim, double theta, bool inverse) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(qkv));
   CHECK_BF16(qkv);
   CHECK_I64(pos);
   TORCH_CHECK(pos.is_contiguous() && pos.numel() == qkv.size(0), "rope: positions must be [T]");
@@ -418,18 +446,21 @@ void rope(at::Tensor& qkv, const at::Tensor& pos, int64_t n_rot_heads, int64_t h
 }
 
 void swiglu_fwd(const at::Tensor& gu, at::Tensor& h) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(gu));
   CHECK_BF16(gu);
   TORCH_CHECK(gu.is_contiguous() && h.is_contiguous(), "swiglu: contiguous");
   check(accerl_swiglu_fwd(gu.data_ptr(), h.data_ptr(), gu.size(0), h.size(1), cur_stream()), "swiglu_fwd");
 }
 
 void swiglu_bwd(const at::Tensor& dh, const at::Tensor& gu, at::Tensor& dgu) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(dh));
   TORCH_CHECK(dh.is_contiguous() && gu.is_contiguous() && dgu.is_contiguous(), "swiglu_bwd: contiguous");
   check(accerl_swiglu_bwd(dh.data_ptr(), gu.data_ptr(), dgu.data_ptr(), gu.size(0), dh.size(1), cur_stream()),
         "swiglu_bwd");
 }
 
 void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(ids));
   CHECK_I64(ids);
   CHECK_BF16(table);
   TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embedding: contiguous");
@@ -439,6 +470,7 @@ void embedding_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& o
 }
 
 void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& grad) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(ids));
   CHECK_I64(ids);
   CHECK_F32(grad);
   check(accerl_embedding_bwd(reinterpret_cast<long long*>(ids.data_ptr<int64_t>()), dout.data_ptr(), grad.data_ptr<float>(), ids.numel(),
@@ -448,6 +480,7 @@ void embedding_bwd(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& gr
 
 void logsoftmax_label_fwd(const at::Tensor& logits, const at::Tensor& labels, at::Tensor& logprob, at::Tensor& lse,
                           const c10::optional<at::Tensor>& entropy) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(logits));
   CHECK_BF16(logits);
   CHECK_I64(labels);
   float* ent = entropy.has_value() ? entropy->data_ptr<float>() : nullptr;
@@ -457,15 +490,37 @@ void logsoftmax_label_fwd(const at::Tensor& logits, const at::Tensor& labels, at
         "logsoftmax_label_fwd");
 }
 
-void logsoftmax_label_bwd(at::Tensor& logits, const at::Tensor& labels, const at::Tensor& lse, const at::Tensor& grad) {
-  check(accerl_logsoftmax_label_bwd(logits.data_ptr(), ld_of(logits), reinterpret_cast<long long*>(labels.data_ptr<int64_t>()), lse.data_ptr<float>(),
-                                    grad.data_ptr<float>(), logits.size(0), logits.size(1), cur_stream()),
+void logsoftmax_label_bwd(at::Tensor& logits, const at::Tensor& labels, const at::Tensor& lse, const at::Tensor& grad,
+                          int64_t label_offset) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(logits));
+  CHECK_BF16(logits);
+  check(accerl_logsoftmax_label_bwd(logits.data_ptr(), ld_of(logits), reinterpret_cast<long long*>(labels.data_ptr<int64_t>()),
+                                    lse.data_ptr<float>(), grad.data_ptr<float>(), logits.size(0), logits.size(1),
+                                    label_offset, cur_stream()),
         "logsoftmax_label_bwd");
+}
+
+void lse_chunk(const at::Tensor& logits, const at::Tensor& labels, int64_t c0, bool first, at::Tensor& state) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(logits));
+  CHECK_BF16(logits);
+  CHECK_F32(state);
+  check(accerl_lse_chunk(logits.data_ptr(), ld_of(logits), reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                         c0, logits.size(0), logits.size(1), first ? 1 : 0, state.data_ptr<float>(), cur_stream()),
+        "lse_chunk");
+}
+
+void lse_finish(const at::Tensor& state, at::Tensor& logprob, at::Tensor& lse, const c10::optional<at::Tensor>& entropy) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(state));
+  CHECK_F32(state);
+  check(accerl_lse_finish(state.data_ptr<float>(), logprob.size(0), logprob.data_ptr<float>(), lse.data_ptr<float>(),
+                          entropy.has_value() ? entropy->data_ptr<float>() : nullptr, cur_stream()),
+        "lse_finish");
 }
 
 void policy_loss(const at::Tensor& lp, const at::Tensor& old_lp, const at::Tensor& adv, at::Tensor& dlp,
                  at::Tensor& stats, int64_t mode, double clip_eps, double gipo_sigma, double tau_pos, double tau_neg,
                  double kl_coef, double loss_scale) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(lp));
   CHECK_F32(lp);
   CHECK_F32(old_lp);
   CHECK_F32(adv);
@@ -477,6 +532,7 @@ void policy_loss(const at::Tensor& lp, const at::Tensor& old_lp, const at::Tenso
 }
 
 void sumsq(const at::Tensor& g, at::Tensor& out) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(g));
   CHECK_F32(g);
   TORCH_CHECK(out.scalar_type() == at::kDouble, "sumsq: out must be float64");
   check(accerl_sumsq(g.data_ptr<float>(), g.numel(), out.data_ptr<double>(), cur_stream()), "sumsq");
@@ -485,6 +541,7 @@ void sumsq(const at::Tensor& g, at::Tensor& out) {
 void adamw(at::Tensor& master, at::Tensor& m, at::Tensor& v, at::Tensor& grad, at::Tensor& param,
            const at::Tensor& sumsq_t, double lr, double beta1, double beta2, double eps, double weight_decay,
            double max_norm, double bc1, double bc2_sqrt) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(master));
   CHECK_F32(master);
   CHECK_BF16(param);
   TORCH_CHECK(master.numel() == param.numel() && grad.numel() == param.numel(), "adamw: size mismatch");
@@ -499,6 +556,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
               const at::Tensor& cu_seqlens, const c10::optional<at::Tensor>& cu_seqlens_k, int64_t max_seqlen,
               int64_t Hq, int64_t Hkv, double scale, bool causal, const c10::optional<at::Tensor>& status,
               const c10::optional<at::Tensor>& block_table) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(q));
   CHECK_BF16(q);
   CHECK_BF16(k);
   CHECK_BF16(v);
@@ -530,6 +588,7 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
               at::Tensor& dk, at::Tensor& dv, const at::Tensor& cu_seqlens, int64_t max_seqlen, int64_t Hq, int64_t Hkv,
               double scale, bool causal, const c10::optional<at::Tensor>& status,
               const c10::optional<at::Tensor>& rope_pos, double rope_theta) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(q));
   CHECK_F32(delta);
   if (rope_pos.has_value())
     TORCH_CHECK(rope_pos->scalar_type() == at::kLong && rope_pos->numel() == q.size(0), "attn_bwd: rope_pos int64 [T]");
@@ -551,6 +610,7 @@ void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tens
                   const at::Tensor& block_table, const at::Tensor& seq_lens, at::Tensor& out, at::Tensor& part_o,
                   at::Tensor& part_ml, int64_t Hq, int64_t Hkv, int64_t num_splits, double scale, int64_t impl,
                   const c10::optional<at::Tensor>& status) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(q));
   CHECK_BF16(q);
   CHECK_I32(block_table);
   CHECK_I32(seq_lens);
@@ -577,6 +637,7 @@ void paged_decode(const at::Tensor& q, const at::Tensor& k_cache, const at::Tens
 
 void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cache, at::Tensor& v_cache,
                     const at::Tensor& slot_mapping, int64_t Hkv) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(k));
   CHECK_I32(slot_mapping);
   check(accerl_kv_cache_write(k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
                               slot_mapping.data_ptr<int>(), k.size(0), Hkv, ld_of(k), ld_of(v),
@@ -628,6 +689,7 @@ void enable_peer_access(int64_t peer) { check(accerl_enable_peer_access(static_c
 
 // peer_ptrs: int64 device tensor [world] of base addresses (fp32 full gradient buffers)
 void rs_sumsq(const at::Tensor& peer_ptrs, int64_t rank, int64_t shard, at::Tensor& out, at::Tensor& sumsq) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(peer_ptrs));
   CHECK_F32(out);
   TORCH_CHECK(peer_ptrs.scalar_type() == at::kLong && peer_ptrs.is_cuda(), "peer_ptrs: int64 cuda tensor");
   check(accerl_rs_sumsq(reinterpret_cast<const float* const*>(peer_ptrs.data_ptr<int64_t>()), peer_ptrs.numel(),
@@ -638,6 +700,7 @@ void rs_sumsq(const at::Tensor& peer_ptrs, int64_t rank, int64_t shard, at::Tens
 void adamw_push(at::Tensor& master, at::Tensor& m, at::Tensor& v, const at::Tensor& grad, const at::Tensor& peer_ptrs,
                 int64_t rank, const at::Tensor& sumsq_t, double lr, double beta1, double beta2, double eps,
                 double weight_decay, double max_norm, double bc1, double bc2_sqrt) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(master));
   CHECK_F32(master);
   check(accerl_adamw_push(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(),
                           reinterpret_cast<void* const*>(peer_ptrs.data_ptr<int64_t>()), peer_ptrs.numel(), rank,
@@ -650,6 +713,7 @@ void sample_logits(const at::Tensor& logits, const at::Tensor& temperature, cons
                    const at::Tensor& offsets, at::Tensor& out_tokens, at::Tensor& out_logprobs, at::Tensor& part,
                    int64_t num_chunks, const c10::optional<at::Tensor>& top_k,
                    const c10::optional<at::Tensor>& top_p) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(logits));
   CHECK_BF16(logits);
   CHECK_F32(temperature);
   const int* tk = nullptr;
@@ -691,6 +755,24 @@ std::vector<std::tuple<std::string, int64_t, int64_t>> debug_status(bool reset) 
   return out;
 }
 
+void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::Tensor& topw, const at::Tensor& dw,
+                    bool norm_topk, const c10::optional<at::Tensor>& dout, const c10::optional<at::Tensor>& sy,
+                    const c10::optional<at::Tensor>& sg, at::Tensor& dgrad, const c10::optional<at::Tensor>& dsy) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(probs));
+  CHECK_F32(probs);
+  CHECK_F32(topw);
+  CHECK_F32(dw);
+  CHECK_BF16(dgrad);
+  const int T = probs.size(0), E = probs.size(1), k = topi.size(1);
+  const bool shared = sy.has_value();
+  check(accerl_moe_router_bwd(probs.data_ptr<float>(), reinterpret_cast<const long long*>(topi.data_ptr<int64_t>()),
+                              topw.data_ptr<float>(), dw.data_ptr<float>(), T, E, k, norm_topk ? 1 : 0,
+                              shared ? dout->data_ptr() : nullptr, shared ? sy->data_ptr() : nullptr,
+                              shared ? sg->data_ptr<float>() : nullptr, shared ? sy->size(1) : 0, dgrad.data_ptr(),
+                              dgrad.size(1), shared ? dsy->data_ptr() : nullptr, cur_stream()),
+        "moe_router_bwd");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("debug_status", &debug_status, "debug-checks build: (unit, code, index) per kernel file");
   m.doc() = "accerl_agent_b200 sm_100a kernels";
@@ -703,6 +785,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &grouped_gemm);
   m.def("row_scatter", &row_scatter);
   m.def("weight_pull", &weight_pull);
+  m.def("moe_router_bwd", &moe_router_bwd);
   m.def("moe_router", &moe_router);
   m.def("moe_combine_fwd", &moe_combine_fwd);
   m.def("moe_combine_bwd", &moe_combine_bwd);
@@ -721,6 +804,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd", &embedding_bwd);
   m.def("logsoftmax_label_fwd", &logsoftmax_label_fwd);
   m.def("logsoftmax_label_bwd", &logsoftmax_label_bwd);
+  m.def("lse_chunk", &lse_chunk);
+  m.def("lse_finish", &lse_finish);
   m.def("policy_loss", &policy_loss);
   m.def("sumsq", &sumsq);
   m.def("adamw", &adamw);

@@ -106,14 +106,16 @@ __global__ void __launch_bounds__(THREADS) logsoftmax_label_fwd_kernel(const __n
 }
 
 // dlogits = g[row] * (onehot(label) - softmax); written over the logits buffer.
+// The logits may be one vocabulary chunk [label_offset, label_offset + V) of the full row: the label's
+// one-hot term applies only when the label falls in the chunk.
 __global__ void logsoftmax_label_bwd_kernel(__nv_bfloat16* __restrict__ logits, long long ld,
                                             const long long* __restrict__ labels, const float* __restrict__ lse,
-                                            const float* __restrict__ grad, int V) {
+                                            const float* __restrict__ grad, int V, long long label_offset) {
   const int row = blockIdx.x;
   __nv_bfloat16* l = logits + row * ld;
   const float z = lse[row];
   const float g = grad[row];
-  const long long lab = labels[row];
+  const long long lab = labels[row] - label_offset;
   for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
     uint4 v = *reinterpret_cast<const uint4*>(l + c);
     uint32_t vw[4] = {v.x, v.y, v.z, v.w};
@@ -128,6 +130,76 @@ __global__ void logsoftmax_label_bwd_kernel(__nv_bfloat16* __restrict__ logits, 
     }
     *reinterpret_cast<uint4*>(l + c) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
   }
+}
+
+// One vocabulary chunk of the response-only LM head: logits [rows, V] of columns [c0, c0 + V). Folds
+// the chunk into each row's running (max m, sum exp(x - m), sum exp(x - m) x, label logit); first
+// chunk initialises the state. One CTA per row; the full [rows, vocab] logits never exist.
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) lse_chunk_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
+                                                           const long long* __restrict__ labels, long long c0,
+                                                           int V, int first, float* __restrict__ state) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* l = logits + row * ld;
+  float m = -INFINITY, sum = 0.f, t = 0.f;
+  for (int c = threadIdx.x * 8; c < V; c += THREADS * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(l + c);
+    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 q = unpack_bf16x2(vw[i]);
+      f[2 * i] = q.x;
+      f[2 * i + 1] = q.y;
+    }
+    float lm = f[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) lm = fmaxf(lm, f[i]);
+    const float mn = fmaxf(m, lm);
+    const float a = (m == -INFINITY) ? 0.f : __expf(m - mn);
+    sum *= a;
+    t *= a;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float e = __expf(f[i] - mn);
+      sum += e;
+      t += e * f[i];
+    }
+    m = mn;
+  }
+  block_reduce_max_sum<THREADS>(m, sum, t);
+  if (threadIdx.x == 0) {
+    float* st = state + 4ll * row;  // [m, sum, t, label logit]
+    const long long lab = labels[row] - c0;
+    const bool has_label = lab >= 0 && lab < V;
+    if (first) {
+      st[0] = m;
+      st[1] = sum;
+      st[2] = t;
+      st[3] = has_label ? __bfloat162float(l[lab]) : 0.f;
+    } else {
+      const float m0 = st[0];
+      const float mn = fmaxf(m0, m);
+      const float a0 = (m0 == -INFINITY) ? 0.f : __expf(m0 - mn);
+      const float a1 = (m == -INFINITY) ? 0.f : __expf(m - mn);
+      st[0] = mn;
+      st[1] = st[1] * a0 + sum * a1;
+      st[2] = st[2] * a0 + t * a1;
+      if (has_label) st[3] = __bfloat162float(l[lab]);
+    }
+  }
+}
+
+// Row results from the folded state: label log-probability, log-sum-exp and (optionally) entropy.
+__global__ void lse_finish_kernel(const float* __restrict__ state, int rows, float* __restrict__ logprob,
+                                  float* __restrict__ lse_out, float* __restrict__ entropy) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const float* st = state + 4ll * row;
+  const float lse = st[0] + logf(st[1]);
+  logprob[row] = st[3] - lse;
+  lse_out[row] = lse;
+  if (entropy) entropy[row] = lse - st[2] / st[1];
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -265,10 +337,27 @@ extern "C" int accerl_logsoftmax_label_fwd(const void* logits, long long ld, con
 }
 
 extern "C" int accerl_logsoftmax_label_bwd(void* logits, long long ld, const long long* labels, const float* lse,
-                                           const float* grad, int rows, int V, cudaStream_t s) {
+                                           const float* grad, int rows, int V, long long label_offset,
+                                           cudaStream_t s) {
   if (V % 8 || ld % 8) return -1;
   if (rows == 0) return 0;
-  logsoftmax_label_bwd_kernel<<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, labels, lse, grad, V);
+  logsoftmax_label_bwd_kernel<<<rows, 512, 0, s>>>((__nv_bfloat16*)logits, ld, labels, lse, grad, V, label_offset);
+  return (int)cudaGetLastError();
+}
+
+// Fold the vocabulary chunk [c0, c0 + V) held in logits into the per-row state (4 floats per row).
+extern "C" int accerl_lse_chunk(const void* logits, long long ld, const long long* labels, long long c0, int rows,
+                                int V, int first, float* state, cudaStream_t s) {
+  if (V % 8 || ld % 8) return -1;
+  if (rows == 0) return 0;
+  lse_chunk_kernel<512><<<rows, 512, 0, s>>>((const __nv_bfloat16*)logits, ld, labels, c0, V, first, state);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_lse_finish(const float* state, int rows, float* logprob, float* lse, float* entropy,
+                                 cudaStream_t s) {
+  if (rows == 0) return 0;
+  lse_finish_kernel<<<(rows + 255) / 256, 256, 0, s>>>(state, rows, logprob, lse, entropy);
   return (int)cudaGetLastError();
 }
 

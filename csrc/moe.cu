@@ -150,9 +150,11 @@ __global__ void moe_combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, c
 // bf16 as the reference's bf16 linear produces them) -> softmax over E experts -> top-k (largest
 // first, lower expert id on ties) -> optional renormalisation of the k weights; per-expert routed
 // row counts accumulate into `counts` (zeroed by the caller). E <= 128, k <= 8.
+// With sg != null, column E of the logits is the shared-expert gate logit: sg[t] = sigmoid of it
+// (rounded to bf16 first, as the reference's bf16 gate linear gives it).
 __global__ void moe_router_kernel(const float* __restrict__ logits, long long ldl, int T, int E, int k, int norm_topk,
                                   float* __restrict__ probs, float* __restrict__ topw, long long* __restrict__ topi,
-                                  int* __restrict__ counts) {
+                                  int* __restrict__ counts, float* __restrict__ sg) {
   const int t = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -210,6 +212,10 @@ __global__ void moe_router_kernel(const float* __restrict__ logits, long long ld
     for (int j = 0; j < 4; ++j)
       if (lane + 32 * j == bi) v[j] = -1.f;
   }
+  if (sg != nullptr && lane == 0) {
+    const float z = __bfloat162float(__float2bfloat16(logits[static_cast<long long>(t) * ldl + E]));
+    sg[t] = 1.f / (1.f + expf(-z));
+  }
   if (lane == 0) {
     const float scale = norm_topk ? 1.f / wsum : 1.f;
     for (int r = 0; r < k; ++r) {
@@ -220,9 +226,106 @@ __global__ void moe_router_kernel(const float* __restrict__ logits, long long ld
   }
 }
 
+// Router backward, one warp per token (the reverse of moe_router_kernel plus the shared-expert gate):
+//   d(top-k weights) dw -> (renormalised: (dw - <dw, topw>) / sum of the k probabilities) ->
+//   scattered onto the k chosen experts -> softmax backward: dlogits = p * (dp - <dp, p>).
+// With a shared expert (sy != null): dsg = <dout, sy> * sg * (1 - sg) is stored as column E of the
+// gradient row, so that one GEMM against [gate weight; shared-gate weight] gives both input-gradient
+// terms, and dsy = sg * dout (bf16), the shared expert's output gradient. Columns past E (+1) are
+// zero. dgrad: [T, E_pad] bf16 with E_pad a multiple of 8 (>= E + 1 with a shared expert).
+__global__ void moe_router_bwd_kernel(const float* __restrict__ probs, const long long* __restrict__ topi,
+                                      const float* __restrict__ topw, const float* __restrict__ dw, int T, int E,
+                                      int k, int norm_topk, const __nv_bfloat16* __restrict__ dout,
+                                      const __nv_bfloat16* __restrict__ sy, const float* __restrict__ sg, int H,
+                                      __nv_bfloat16* __restrict__ dgrad, int E_pad, __nv_bfloat16* __restrict__ dsy) {
+  const int t = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const long long tk = static_cast<long long>(t) * k;
+  // gradient of the chosen probabilities
+  float dpk = 0.f, wk = 0.f;
+  int ek = -1;
+  if (lane < k) {
+    ek = static_cast<int>(topi[tk + lane]);
+    dpk = dw[tk + lane];
+    wk = topw[tk + lane];
+  }
+  if (norm_topk) {
+    const float pk = lane < k ? probs[static_cast<long long>(t) * E + ek] : 0.f;
+    const float S = warp_sum(pk);
+    const float c = warp_sum(dpk * wk);
+    dpk = S > 0.f ? (dpk - c) / S : 0.f;
+  }
+  // dp over all experts (zero outside the k chosen ones); lane holds experts lane + 32 j
+  float p[4], dp[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane + 32 * j;
+    p[j] = e < E ? probs[static_cast<long long>(t) * E + e] : 0.f;
+    dp[j] = 0.f;
+  }
+  for (int r = 0; r < k; ++r) {
+    const int er = __shfl_sync(0xffffffffu, ek, r);
+    const float gr = __shfl_sync(0xffffffffu, dpk, r);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (lane + 32 * j == er) dp[j] += gr;
+  }
+  float dot = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) dot += dp[j] * p[j];
+  dot = warp_sum(dot);
+  __nv_bfloat16* row = dgrad + static_cast<long long>(t) * E_pad;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E) row[e] = __float2bfloat16(p[j] * (dp[j] - dot));
+  }
+  int first_pad = E;
+  if (sy != nullptr) {
+    const float g = sg[t];
+    const __nv_bfloat16* drow = dout + static_cast<long long>(t) * H;
+    const __nv_bfloat16* srow = sy + static_cast<long long>(t) * H;
+    __nv_bfloat16* dsrow = dsy + static_cast<long long>(t) * H;
+    float acc = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      const uint4 dv = *reinterpret_cast<const uint4*>(drow + c);
+      const uint4 sv = *reinterpret_cast<const uint4*>(srow + c);
+      const uint32_t dwv[4] = {dv.x, dv.y, dv.z, dv.w};
+      const uint32_t swv[4] = {sv.x, sv.y, sv.z, sv.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = unpack_bf16x2(dwv[i]);
+        const float2 b = unpack_bf16x2(swv[i]);
+        acc += a.x * b.x + a.y * b.y;
+        ow[i] = pack_bf16x2(a.x * g, a.y * g);
+      }
+      *reinterpret_cast<uint4*>(dsrow + c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) row[E] = __float2bfloat16(acc * g * (1.f - g));
+    first_pad = E + 1;
+  }
+  for (int e = first_pad + lane; e < E_pad; e += 32) row[e] = __float2bfloat16(0.f);
+}
+
 }  // namespace accerl
 
 using namespace accerl;
+
+extern "C" int accerl_moe_router_bwd(const float* probs, const long long* topi, const float* topw, const float* dw,
+                                     int T, int E, int k, int norm_topk, const void* dout, const void* sy,
+                                     const float* sg, int H, void* dgrad, int E_pad, void* dsy, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (E < 1 || E > 128 || k < 1 || k > kMoeMaxK || k > 32 || E_pad % 8 || E_pad < E + (sy ? 1 : 0)) return -1;
+  if (sy && (H % 8 || !dout || !sg || !dsy)) return -1;
+  const long long threads = static_cast<long long>(T) * 32;
+  moe_router_bwd_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      probs, topi, topw, dw, T, E, k, norm_topk, (const __nv_bfloat16*)dout, (const __nv_bfloat16*)sy, sg, H,
+      (__nv_bfloat16*)dgrad, E_pad, (__nv_bfloat16*)dsy);
+  return (int)cudaGetLastError();
+}
 
 extern "C" int accerl_moe_combine_fwd(const void* ys, const long long* pos, const float* w, long long T, int k, int H,
                                       const void* residual, const void* shared, const float* sg, void* out,
@@ -247,12 +350,12 @@ extern "C" int accerl_moe_combine_bwd(const void* dout, const void* ys, const lo
 }
 
 extern "C" int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs,
-                                 float* topw, long long* topi, int* counts, cudaStream_t s) {
+                                 float* topw, long long* topi, int* counts, float* sg, cudaStream_t s) {
   if (T <= 0) return 0;
   if (E < 1 || E > 128 || k < 1 || k > kMoeMaxK || k > E) return -1;
   const long long threads = static_cast<long long>(T) * 32;
   moe_router_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(logits, ldl, T, E, k, norm_topk, probs, topw,
-                                                                       topi, counts);
+                                                                       topi, counts, sg);
   return (int)cudaGetLastError();
 }
 

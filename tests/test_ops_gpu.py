@@ -646,3 +646,77 @@ def test_gemm_rope_epilogue(block_n):
     assert torch.equal(got[:, (Hq + Hkv) * D :], want[:, (Hq + Hkv) * D :])  # v
     got2 = ops.linear_rope(x, w, bias, pos, Hq + Hkv, D, 1e6)
     assert torch.equal(got2, got) or block_n != 0
+
+
+@pytest.mark.parametrize("n,V,chunk", [(300, 151936, 16384), (64, 4096, 1024), (7, 1000, 256)])
+def test_lm_head_chunked_matches_fp32_oracle(n, V, chunk):
+    """Vocabulary-chunked response-only LM head (logprob, lse, entropy; d(rows), d(W)) against fp32
+    autograd over the full logits."""
+    H = 256
+    g = torch.Generator(device="cpu").manual_seed(n)
+    rows = (torch.randn(n, H, generator=g) * 0.5).bfloat16().to(DEV)
+    W = (torch.randn(V, H, generator=g) * 0.05).bfloat16().to(DEV)
+    labels = torch.randint(0, V, (n,), generator=g).to(DEV)
+    grad = torch.randn(n, generator=g).to(DEV)
+    lp, lse, ent = ops.lm_head_logprobs(rows, W, labels, with_entropy=True, chunk=chunk)
+    gW = torch.zeros(V, H, device=DEV)
+    drows = ops.lm_head_backward(rows, W, labels, lse, grad, gW, True, chunk=chunk)
+    x = rows.float().requires_grad_(True)
+    w = W.float().requires_grad_(True)
+    logp = torch.log_softmax(x @ w.t(), -1)
+    lp_ref = logp.gather(1, labels.view(-1, 1)).squeeze(1)
+    ent_ref = -(logp.exp() * logp).sum(-1)
+    (lp_ref * grad).sum().backward()
+    torch.testing.assert_close(lp, lp_ref.detach(), atol=2e-2, rtol=2e-3)
+    torch.testing.assert_close(ent, ent_ref.detach(), atol=2e-2, rtol=2e-3)
+    assert _rel(drows.float(), x.grad) < 2e-2
+    assert _rel(gW, w.grad) < 2e-2
+
+
+def test_lm_head_never_builds_full_logits():
+    n, H, V = 2048, 1536, 151936
+    rows = torch.randn(n, H, device=DEV).bfloat16()
+    W = (torch.randn(V, H, device=DEV) * 0.02).bfloat16()
+    labels = torch.randint(0, V, (n,), device=DEV)
+    ops.lm_head_logprobs(rows, W, labels)  # workspaces allocated once
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    lp, lse, _ = ops.lm_head_logprobs(rows, W, labels)
+    gW = torch.zeros(V, H, device=DEV)
+    torch.cuda.synchronize()
+    base2 = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    ops.lm_head_backward(rows, W, labels, lse, torch.ones(n, device=DEV), gW)
+    torch.cuda.synchronize()
+    full_logits = n * V * 2  # 622 MB
+    assert torch.cuda.max_memory_allocated() - base2 < full_logits // 4
+    assert torch.isfinite(lp).all()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_native_ops_follow_their_tensors_device_from_any_thread():
+    """The CUDA current device is per thread: a thread that never selected a device (current device
+    0) still launches the native kernels of cuda:1 tensors on cuda:1."""
+    import threading
+
+    dev = torch.device("cuda", 1)
+    x = torch.randn(64, 256, device=dev).bfloat16()
+    w = (torch.rand(256, device=dev) + 0.5).bfloat16()
+    W = (torch.randn(128, 256, device=dev) * 0.05).bfloat16()
+    out = {}
+
+    def run():
+        out["device"] = torch.cuda.current_device()
+        y, _ = ops.rmsnorm(x, w, 1e-6)
+        out["y"] = y
+        out["z"] = ops.linear(y, W)
+        torch.cuda.synchronize(dev)
+
+    t = threading.Thread(target=run)
+    t.start()
+    t.join()
+    assert out["device"] == 0
+    want = ref.rmsnorm(x.float().cpu(), w.float().cpu(), 1e-6)[0]
+    assert _rel(out["y"].float().cpu(), want) < 2e-2
+    assert _rel(out["z"].float().cpu(), want @ W.float().cpu().t()) < 3e-2
