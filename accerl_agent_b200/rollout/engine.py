@@ -132,6 +132,8 @@ class GenerationEngine:
         groups of a tensor-parallel engine (NCCL for the activations' all-reduce, gloo for the step
         commands the leader, group rank 0, broadcasts); rank r then holds the r-th shard of every
         tensor-parallel weight and ranks > 0 run ``serve_follower``."""
+        if device.type == "cuda" and device.index is None:  # the step thread selects this exact GPU
+            device = torch.device("cuda", torch.cuda.current_device())
         self.full_cfg = cfg
         self.tp_group = tp_group
         self.cmd_group = cmd_group
