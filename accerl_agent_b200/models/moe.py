@@ -164,7 +164,8 @@ def padded_layout_from_pads(pads, device):
 
 def device_padded_layout(topi: torch.Tensor, num_experts: int, lo: int = 0, El: Optional[int] = None,
                          counts: Optional[torch.Tensor] = None):
-    """Grouped-GEMM layout computed on the device, with no host synchronisation.
+    """Grouped-GEMM layout from torch device ops, with no host synchronisation (the formulation that
+    ``device_dispatch`` computes in two kernel launches; kept as its oracle and for CPU tensors).
 
     The pairs ``(token, slot)`` of ``topi`` are sorted by expert; experts ``[lo, lo + El)`` get row
     segments padded to SEG rows, laid out back to back. Sizes are bounded on the host without reading
@@ -251,8 +252,8 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
     ep = getattr(model, "expert_parallel", None)
     if ep is None and h.is_cuda and h.dtype == torch.bfloat16:
         shared_gate: list = []
-        probs, topw, topi, counts = route(model, layer, h, counts=True, shared_gate=shared_gate)
-        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi, counts,
+        probs, topw, topi = route(model, layer, h, shared_gate=shared_gate)
+        return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi,
                                    sg=shared_gate[0].view(-1, 1) if shared_gate else None)
     probs, topw, topi = route(model, layer, h)
     w_act = topw.to(h.dtype)
@@ -330,8 +331,34 @@ def _shared_expert(model, layer: int, h: torch.Tensor, cache, sg: Optional[torch
     return sy, sg
 
 
-def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi, counts=None, sg=None):
-    """CUDA path without host synchronisation: device-side padded layout, grouped GEMMs over the
+def device_dispatch(topi: torch.Tensor, topw: torch.Tensor, h: torch.Tensor, num_experts: int, lo: int, El: int,
+                    zero_pad: bool):
+    """Dispatch in two kernel launches (``moe_layout``), with no host synchronisation and no sort.
+
+    Gives the padded layout of experts ``[lo, lo + El)`` (the same rows as ``device_padded_layout``:
+    an expert's pairs in token-major order), every (token, slot) pair's row and its weight (rounded
+    to the activation dtype; 0 for pairs routed outside the range, whose row is ``total``), and the
+    expert inputs ``xs[row] = h[token]``. With ``zero_pad`` the padding rows of ``xs`` are zero.
+    Returns ``(xs, pos_pairs, w_pairs, lay)``."""
+    n = topi.numel()
+    dev = h.device
+    total = ((n + El * (SEG - 1) + SEG - 1) // SEG) * SEG
+    tiles = total // SEG
+    xs = torch.empty(total, h.shape[1], dtype=h.dtype, device=dev)
+    meta = torch.empty(tiles + 2 * El + num_experts, dtype=torch.int32, device=dev)
+    te, rs, rows, cnt = (meta[:tiles], meta[tiles : tiles + El], meta[tiles + El : tiles + 2 * El],
+                         meta[tiles + 2 * El :])
+    pos = torch.empty(n, dtype=torch.long, device=dev)
+    w = torch.empty(n, dtype=torch.float32, device=dev)
+    hist = ops.workspace(dev, "moe_layout_hist", ((n + 1023) // 1024) * num_experts, dtype=torch.int32)
+    ops.native().moe_layout(topi.contiguous(), topw.float().contiguous(), h.contiguous(), num_experts, lo, El, total,
+                            xs, bool(zero_pad), hist, pos, w, te, rs, rows, cnt)
+    lay = {"total": total, "num_groups": El, "tile_expert": te, "row_start": rs, "rows": rows, "counts": cnt}
+    return xs, pos, w, lay
+
+
+def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw, topi, sg=None):
+    """CUDA path without host synchronisation: one-pass device dispatch, grouped GEMMs over the
     bounded tile count, fused combine. Training (``save``) zeroes the padded input rows because the
     weight-gradient contraction runs over them; inference leaves them uninitialised (their output
     rows are never read)."""
@@ -339,27 +366,17 @@ def _moe_forward_device(model, layer: int, h, residual, save: bool, probs, topw,
     k = cfg.num_experts_per_tok
     El = cfg.local_experts if cfg.local_experts is not None else cfg.num_experts
     lo = cfg.expert_offset if El != cfg.num_experts else 0
-    order, rows, valid, lay = device_padded_layout(topi, cfg.num_experts, lo, El, counts)
+    xs, pos_pairs, w_pairs, lay = device_dispatch(topi, topw, h, cfg.num_experts, lo, El, zero_pad=save)
     R = lay["total"]
-    tok = torch.div(order, k, rounding_mode="floor")
-    alloc = torch.zeros if save else torch.empty
-    xs = alloc(R + 1, h.shape[1], dtype=h.dtype, device=h.device)
-    xs.index_copy_(0, rows, h.index_select(0, tok))
     ys_full = torch.empty(R + 1, cfg.hidden_size, dtype=h.dtype, device=h.device)
     ys_full[R].zero_()  # the row of pairs that do not run here (weight 0)
-    ys, gu, act = experts_forward_grouped(model, layer, xs[:R], lay, out=ys_full[:R])
-    n_pairs = topi.numel()
-    pos_pairs = torch.empty(n_pairs, dtype=torch.long, device=h.device)
-    pos_pairs[order] = rows
-    w_sorted = topw.to(h.dtype).reshape(-1).float().index_select(0, order)
-    w_pairs = torch.empty(n_pairs, dtype=torch.float32, device=h.device)
-    w_pairs[order] = torch.where(valid, w_sorted, torch.zeros_like(w_sorted))
+    ys, gu, act = experts_forward_grouped(model, layer, xs, lay, out=ys_full[:R])
     cache: Dict[str, torch.Tensor] = {}
     sy, sg = _shared_expert(model, layer, h, cache if save else None, sg)
     out = ops.moe_combine(ys_full, pos_pairs, w_pairs, k, residual=residual, shared=sy, sg=sg)
     if save:
-        cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=xs[:R], gu=gu, act=act,
-                     ys=ys_full, pos_pairs=pos_pairs, w_pairs=w_pairs)
+        cache.update(probs=probs, topw=topw, topi=topi, xs=xs, gu=gu, act=act, ys=ys_full, pos_pairs=pos_pairs,
+                     w_pairs=w_pairs)
         cache["layout"] = lay  # type: ignore[assignment]
     return out, cache
 

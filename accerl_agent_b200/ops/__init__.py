@@ -82,6 +82,7 @@ __all__ = [
     "adamw_step",
     "paged_decode",
     "kv_cache_write",
+    "qkv_rope_cache",
     "sample",
     "workspace",
 ]
@@ -620,6 +621,29 @@ def paged_decode(q, k_cache, v_cache, block_table, seq_lens, n_heads, n_kv_heads
         out.copy_(res)
         return out
     return res
+
+
+def qkv_rope_cache(qkv, pos, slot_mapping, k_cache, v_cache, n_q_heads: int, n_kv_heads: int, theta: float,
+                   q_norm=None, k_norm=None, eps: float = 1e-6):
+    """The engine's step after the qkv projection, in place on ``qkv`` [T, (Hq + 2 Hkv) * D]: per-head
+    RMSNorm of q and k (with ``q_norm``/``k_norm``, Qwen3), rotary embedding of q and k at ``pos``,
+    and the k and v heads into the paged caches at ``slot_mapping`` (rows with slot < 0 skip). One
+    kernel on the GPU (head dim 128); elsewhere the separate ops in the same order."""
+    D = k_cache.shape[-1]
+    if qkv.is_cuda and qkv.dtype == torch.bfloat16 and D == 128:
+        native().qkv_rope_cache(qkv, pos.reshape(-1), slot_mapping, k_cache, v_cache, n_q_heads, n_kv_heads,
+                                float(theta), q_norm, k_norm, float(eps))
+        return qkv
+    T = qkv.shape[0]
+    qd, kd = n_q_heads * D, n_kv_heads * D
+    if q_norm is not None:
+        qn, _ = rmsnorm(qkv[:, :qd].reshape(T * n_q_heads, D).clone(), q_norm, eps)
+        kn, _ = rmsnorm(qkv[:, qd : qd + kd].reshape(T * n_kv_heads, D).clone(), k_norm, eps)
+        qkv[:, :qd].copy_(qn.view(T, qd))
+        qkv[:, qd : qd + kd].copy_(kn.view(T, kd))
+    rope_(qkv, pos, n_q_heads + n_kv_heads, D, theta)
+    kv_cache_write(qkv[:, qd : qd + kd], qkv[:, qd + kd :], k_cache, v_cache, slot_mapping, n_kv_heads)
+    return qkv
 
 
 def kv_cache_write(k, v, k_cache, v_cache, slot_mapping, n_kv_heads):

@@ -718,15 +718,12 @@ class GenerationEngine:
             h1, _ = ops.rmsnorm(x, m.w(p + "input_layernorm.weight"), cfg.rms_norm_eps)
             bias = m.w(p + "self_attn.qkv_proj.bias") if cfg.qkv_bias else None
             qkv = ops.linear(h1, m.w(p + "self_attn.qkv_proj.weight"), bias=bias)
-            if cfg.qk_norm:
-                m._qk_norm_forward(layer, qkv)
-            ops.rope_(qkv, pos_d, Hq + Hkv, D, cfg.rope_theta)
-            q = qkv[:, : cfg.q_dim]
-            k = qkv[:, cfg.q_dim : cfg.q_dim + cfg.kv_dim]
-            v = qkv[:, cfg.q_dim + cfg.kv_dim :]
             kc, vc = self.k_cache[layer], self.v_cache[layer]
-            ops.kv_cache_write(k, v, kc, vc, slots_d, Hkv)
-            attn = attn_fn(layer, q, kc, vc)
+            qn = m.w(p + "self_attn.q_norm.weight") if cfg.qk_norm else None
+            kn = m.w(p + "self_attn.k_norm.weight") if cfg.qk_norm else None
+            # qk-norm, RoPE and the cache write in one kernel
+            ops.qkv_rope_cache(qkv, pos_d, slots_d, kc, vc, Hq, Hkv, cfg.rope_theta, qn, kn, cfg.rms_norm_eps)
+            attn = attn_fn(layer, qkv[:, : cfg.q_dim], kc, vc)
             x = self._row_parallel(attn, m.w(p + "self_attn.o_proj.weight"), x)
             h2, _ = ops.rmsnorm(x, m.w(p + "post_attention_layernorm.weight"), cfg.rms_norm_eps)
             if cfg.layer_is_moe(layer):

@@ -43,6 +43,9 @@ int accerl_moe_combine_bwd(const void* dout, const void* ys, const long long* po
                            int H, void* dys, float* dw, long long R, cudaStream_t s);
 int accerl_moe_router(const float* logits, long long ldl, int T, int E, int k, int norm_topk, float* probs, float* topw,
                       long long* topi, int* counts, float* sg, cudaStream_t s);
+int accerl_moe_layout(const long long* topi, const float* topw, long long n, int k, int E, int lo, int El,
+                      long long total, const void* h, int H, void* xs, int zero_pad, int* hist, long long* pos, float* w,
+                      int* tile_expert, int* row_start, int* seg_rows, int* counts, cudaStream_t s);
 int accerl_moe_router_bwd(const float* probs, const long long* topi, const float* topw, const float* dw, int T, int E,
                           int k, int norm_topk, const void* dout, const void* sy, const float* sg, int H, void* dgrad,
                           int E_pad, void* dsy, cudaStream_t s);
@@ -110,6 +113,9 @@ int accerl_rs_sumsq(const float* const* peers, int world, int rank, long long sh
 int accerl_adamw_push(float* master, float* m, float* v, const float* grad, void* const* peer_params, int world,
                       int rank, long long shard, const double* sumsq, float lr, float beta1, float beta2, float eps,
                       float weight_decay, float max_norm, float bc1, float bc2_sqrt, cudaStream_t s);
+int accerl_qkv_rope_cache(void* qkv, long long ld, const long long* pos, const int* slots, int T, int Hq, int Hkv,
+                          float theta, const void* q_norm, const void* k_norm, float eps, void* k_cache, void* v_cache,
+                          long long num_slots, cudaStream_t s);
 int accerl_kv_cache_write(const void* k, const void* v, void* k_cache, void* v_cache, const int* slot_mapping, int T,
                           int Hkv, long long ldk, long long ldv, long long num_slots, cudaStream_t s);
 int accerl_sample_logits(const void* logits, long long ld, int rows, int V, const float* temperature,
@@ -645,6 +651,37 @@ void kv_cache_write(const at::Tensor& k, const at::Tensor& v, at::Tensor& k_cach
         "kv_cache_write");
 }
 
+void qkv_rope_cache(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& slot_mapping, at::Tensor& k_cache,
+                    at::Tensor& v_cache, int64_t Hq, int64_t Hkv, double theta, const c10::optional<at::Tensor>& q_norm,
+                    const c10::optional<at::Tensor>& k_norm, double eps) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(qkv));
+  CHECK_BF16(qkv);
+  CHECK_BF16(k_cache);
+  CHECK_BF16(v_cache);
+  CHECK_I64(pos);
+  CHECK_I32(slot_mapping);
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) == (Hq + 2 * Hkv) * 128,
+              "qkv_rope_cache: qkv rows [Hq | Hkv | Hkv] heads of 128");
+  TORCH_CHECK(pos.numel() == qkv.size(0) && slot_mapping.numel() == qkv.size(0) && pos.is_contiguous() &&
+                  slot_mapping.is_contiguous(), "qkv_rope_cache: one position and slot per row");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.size(-1) == 128 &&
+                  k_cache.size(-2) == Hkv && k_cache.sizes() == v_cache.sizes(),
+              "qkv_rope_cache: caches [blocks, block_size, Hkv, 128]");
+  TORCH_CHECK(q_norm.has_value() == k_norm.has_value(), "qkv_rope_cache: both or neither qk-norm weights");
+  if (q_norm.has_value()) {
+    CHECK_BF16(*q_norm);
+    CHECK_BF16(*k_norm);
+    TORCH_CHECK(q_norm->numel() == 128 && k_norm->numel() == 128 && q_norm->is_contiguous() && k_norm->is_contiguous(),
+                "qkv_rope_cache: qk-norm weights of 128");
+  }
+  check(accerl_qkv_rope_cache(qkv.data_ptr(), ld_of(qkv), reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()),
+                              slot_mapping.data_ptr<int>(), qkv.size(0), Hq, Hkv, static_cast<float>(theta),
+                              q_norm.has_value() ? q_norm->data_ptr() : nullptr,
+                              k_norm.has_value() ? k_norm->data_ptr() : nullptr, static_cast<float>(eps),
+                              k_cache.data_ptr(), v_cache.data_ptr(), k_cache.numel() / (Hkv * 128), cur_stream()),
+        "qkv_rope_cache");
+}
+
 // CUDA IPC of a tensor's allocation. The handle covers the caching-allocator segment that holds the
 // tensor; the tensor's byte offset inside it travels with the handle. Peers open it on THEIR current
 // device with lazy peer access, so the mapping lives in the context their kernels run in. Errors are
@@ -773,6 +810,43 @@ void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::T
         "moe_router_bwd");
 }
 
+void moe_layout(const at::Tensor& topi, const at::Tensor& topw, const at::Tensor& h, int64_t E, int64_t lo, int64_t El,
+                int64_t total, at::Tensor& xs, bool zero_pad, at::Tensor& hist, at::Tensor& pos, at::Tensor& w,
+                at::Tensor& tile_expert, at::Tensor& row_start, at::Tensor& seg_rows,
+                const c10::optional<at::Tensor>& counts) {
+  const c10::cuda::OptionalCUDAGuard device_guard(at::device_of(topi));
+  CHECK_F32(topw);
+  CHECK_BF16(h);
+  CHECK_BF16(xs);
+  TORCH_CHECK(topi.scalar_type() == at::kLong && topi.is_contiguous() && topw.is_contiguous() &&
+                  topi.numel() == topw.numel() && topi.dim() == 2,
+              "moe_layout: topi [T, k] int64 and topw [T, k] fp32, contiguous");
+  const int64_t n = topi.numel(), k = topi.size(1), H = h.size(1);
+  TORCH_CHECK(h.is_contiguous() && h.size(0) * k == n && xs.is_contiguous() && xs.size(1) == H && xs.size(0) >= total,
+              "moe_layout: h [T, H] and xs [>= total, H] contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(h.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(xs.data_ptr()) % 16 == 0,
+              "moe_layout: 16-byte aligned rows");
+  TORCH_CHECK(hist.scalar_type() == at::kInt && hist.numel() >= ((n + 1023) / 1024) * E, "moe_layout: hist scratch");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.numel() == n && w.scalar_type() == at::kFloat && w.numel() == n,
+              "moe_layout: pos int64 / w fp32 per pair");
+  TORCH_CHECK(tile_expert.scalar_type() == at::kInt && tile_expert.numel() >= total / 128 &&
+                  row_start.scalar_type() == at::kInt && row_start.numel() >= El &&
+                  seg_rows.scalar_type() == at::kInt && seg_rows.numel() >= El,
+              "moe_layout: int32 layout outputs");
+  int* cp = nullptr;
+  if (counts.has_value()) {
+    TORCH_CHECK(counts->scalar_type() == at::kInt && counts->numel() >= E, "moe_layout: counts int32 [E]");
+    cp = counts->data_ptr<int>();
+  }
+  check(accerl_moe_layout(reinterpret_cast<const long long*>(topi.data_ptr<int64_t>()), topw.data_ptr<float>(), n,
+                          static_cast<int>(k), static_cast<int>(E), static_cast<int>(lo), static_cast<int>(El), total,
+                          h.data_ptr(), static_cast<int>(H), xs.data_ptr(), zero_pad ? 1 : 0, hist.data_ptr<int>(),
+                          reinterpret_cast<long long*>(pos.data_ptr<int64_t>()), w.data_ptr<float>(),
+                          tile_expert.data_ptr<int>(), row_start.data_ptr<int>(), seg_rows.data_ptr<int>(), cp,
+                          cur_stream()),
+        "moe_layout");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("debug_status", &debug_status, "debug-checks build: (unit, code, index) per kernel file");
   m.doc() = "accerl_agent_b200 sm_100a kernels";
@@ -786,6 +860,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("row_scatter", &row_scatter);
   m.def("weight_pull", &weight_pull);
   m.def("moe_router_bwd", &moe_router_bwd);
+  m.def("moe_layout", &moe_layout);
+  m.def("qkv_rope_cache", &qkv_rope_cache);
   m.def("moe_router", &moe_router);
   m.def("moe_combine_fwd", &moe_combine_fwd);
   m.def("moe_combine_bwd", &moe_combine_bwd);

@@ -310,6 +310,142 @@ __global__ void moe_router_bwd_kernel(const float* __restrict__ probs, const lon
   for (int e = first_pad + lane; e < E_pad; e += 32) row[e] = __float2bfloat16(0.f);
 }
 
+// Dispatch layout in two launches, with no host synchronisation and no sort.
+// The (token, slot) pairs are numbered token-major, p = t * k + j. Block b owns pairs
+// [b * 1024, (b + 1) * 1024). An expert's rows are its pairs in increasing p (a stable counting
+// sort), so a pair's rank within its expert is
+//   (its expert's pairs in earlier blocks) + (in earlier warps of its block) + (in lower lanes).
+// Experts [lo, lo + El) own row segments padded to kLayoutSeg rows, back to back from row 0; a pair
+// routed elsewhere (a tensor-parallel engine shard) gets row `total` and weight 0.
+constexpr int kLayoutPairs = 1024;
+constexpr int kLayoutSeg = 128;
+constexpr int kLayoutMaxE = 256;
+
+__global__ void __launch_bounds__(kLayoutPairs) moe_layout_hist_kernel(const long long* __restrict__ topi, long long n,
+                                                                      int E, int* __restrict__ hist) {
+  __shared__ int h[kLayoutMaxE];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const long long p = static_cast<long long>(blockIdx.x) * kLayoutPairs + threadIdx.x;
+  if (p < n) {
+    const long long e = topi[p];
+    if (e >= 0 && e < E) atomicAdd(&h[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[static_cast<long long>(blockIdx.x) * E + e] = h[e];
+}
+
+// Shared memory: before[E], tot[E], start[El], end[El], wrank[32][E] (ints).
+__global__ void __launch_bounds__(kLayoutPairs) moe_layout_place_kernel(
+    const long long* __restrict__ topi, const float* __restrict__ topw, long long n, int k, int E, int lo, int El,
+    long long total, const int* __restrict__ hist, int nblocks, const __nv_bfloat16* __restrict__ h, int H,
+    __nv_bfloat16* __restrict__ xs, int zero_pad, long long* __restrict__ pos, float* __restrict__ w,
+    int* __restrict__ tile_expert, int* __restrict__ row_start, int* __restrict__ seg_rows, int* __restrict__ counts) {
+  extern __shared__ int sm[];
+  int* before = sm;
+  int* tot = before + E;
+  int* start = tot + E;
+  int* end = start + El;
+  int* wrank = end + El;  // [32][E]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 32 * E; i += blockDim.x) wrank[i] = 0;
+  for (int e = tid; e < E; e += blockDim.x) {  // coalesced over e, one pass over the histogram rows
+    int b4 = 0, s = 0;
+    for (int b = 0; b < nblocks; ++b) {
+      const int v = hist[static_cast<long long>(b) * E + e];
+      b4 += b < static_cast<int>(blockIdx.x) ? v : 0;
+      s += v;
+    }
+    before[e] = b4;
+    tot[e] = s;
+  }
+  __syncthreads();
+  if (warp == 0) {  // padded segment sizes and their exclusive prefix sum over the local experts
+    const int per = (El + 31) / 32, a = min(El, lane * per), z = min(El, a + per);
+    int run = 0;
+    for (int i = a; i < z; ++i) run += (tot[lo + i] + kLayoutSeg - 1) / kLayoutSeg * kLayoutSeg;
+    int incl = run;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int at = incl - run;
+    for (int i = a; i < z; ++i) {
+      const int pad = (tot[lo + i] + kLayoutSeg - 1) / kLayoutSeg * kLayoutSeg;
+      start[i] = at;
+      at += pad;
+      end[i] = at;
+    }
+  }
+  // this block's pairs: rank among the same expert's pairs of this warp, and per-warp counts
+  const long long p = static_cast<long long>(blockIdx.x) * kLayoutPairs + tid;
+  long long e = p < n ? topi[p] : -1;
+  if (e < 0 || e >= E) e = -1;
+  const unsigned same = __match_any_sync(0xffffffffu, static_cast<int>(e));
+  const int lane_rank = __popc(same & ((1u << lane) - 1u));
+  __syncthreads();  // wrank zeroed, start/end written
+  if (e >= 0 && lane_rank == 0) wrank[warp * E + e] = __popc(same);
+  __syncthreads();
+  for (int x = tid; x < E; x += blockDim.x) {  // exclusive prefix over the warps
+    int run = 0;
+    for (int v = 0; v < 32; ++v) {
+      const int c = wrank[v * E + x];
+      wrank[v * E + x] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  long long row = total;
+  if (e >= lo && e < lo + El) row = start[e - lo] + before[e] + wrank[warp * E + e] + lane_rank;
+  if (p < n) {
+    pos[p] = row;
+    w[p] = row < total ? __bfloat162float(__float2bfloat16(topw[p])) : 0.f;
+  }
+  if (blockIdx.x == 0) {
+    for (int i = tid; i < El; i += blockDim.x) {
+      row_start[i] = start[i];
+      seg_rows[i] = end[i] - start[i];
+    }
+    if (counts)
+      for (int i = tid; i < E; i += blockDim.x) counts[i] = tot[i];
+    const long long tiles = total / kLayoutSeg;
+    for (long long t = tid; t < tiles; t += blockDim.x) {  // first segment whose end is past the tile
+      const long long r = t * kLayoutSeg;
+      int lo_i = 0, hi_i = El;
+      while (lo_i < hi_i) {
+        const int mid = (lo_i + hi_i) >> 1;
+        if (end[mid] <= r) lo_i = mid + 1; else hi_i = mid;
+      }
+      tile_expert[t] = lo_i < El ? lo_i : -1;
+    }
+  }
+  // gather: every pair of this warp copies its token's row of h into its row of xs (16 B per lane)
+  const int vec = H / 8;
+  for (int j = 0; j < 32; ++j) {
+    const long long rj = __shfl_sync(0xffffffffu, row, j);
+    const long long pj = static_cast<long long>(blockIdx.x) * kLayoutPairs + warp * 32 + j;
+    if (pj >= n || rj >= total) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(h + (pj / k) * static_cast<long long>(H));
+    uint4* dst = reinterpret_cast<uint4*>(xs + rj * static_cast<long long>(H));
+    for (int c = lane; c < vec; c += 32) dst[c] = src[c];
+  }
+  if (!zero_pad) return;
+  // training: rows of a segment past its expert's pairs, and the tiles past the last segment, are
+  // zero (the weight-gradient contraction runs over them)
+  const long long gw = static_cast<long long>(blockIdx.x) * 32 + warp, nw = static_cast<long long>(gridDim.x) * 32;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (long long r = gw; r < total; r += nw) {
+    int lo_i = 0, hi_i = El;
+    while (lo_i < hi_i) {
+      const int mid = (lo_i + hi_i) >> 1;
+      if (end[mid] <= r) lo_i = mid + 1; else hi_i = mid;
+    }
+    if (lo_i < El && r - start[lo_i] < tot[lo + lo_i]) continue;
+    uint4* dst = reinterpret_cast<uint4*>(xs + r * static_cast<long long>(H));
+    for (int c = lane; c < vec; c += 32) dst[c] = z;
+  }
+}
+
 }  // namespace accerl
 
 using namespace accerl;
@@ -356,6 +492,26 @@ extern "C" int accerl_moe_router(const float* logits, long long ldl, int T, int 
   const long long threads = static_cast<long long>(T) * 32;
   moe_router_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(logits, ldl, T, E, k, norm_topk, probs, topw,
                                                                        topi, counts, sg);
+  return (int)cudaGetLastError();
+}
+
+// hist: [ceil(n / 1024), E] int32 scratch. total must be a multiple of 128 that holds every padded
+// segment (n + El * 127 rounded up always does); tile_expert has total / 128 entries.
+extern "C" int accerl_moe_layout(const long long* topi, const float* topw, long long n, int k, int E, int lo, int El,
+                                 long long total, const void* h, int H, void* xs, int zero_pad, int* hist,
+                                 long long* pos, float* w, int* tile_expert, int* row_start, int* seg_rows,
+                                 int* counts, cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (E < 1 || E > kLayoutMaxE || k < 1 || El < 1 || lo < 0 || lo + El > E || H % 8 || total % kLayoutSeg ||
+      total < n + static_cast<long long>(El) * (kLayoutSeg - 1) || total > INT32_MAX)
+    return -1;
+  const long long blocks = (n + kLayoutPairs - 1) / kLayoutPairs;
+  if (blocks > INT32_MAX) return -1;
+  moe_layout_hist_kernel<<<(unsigned)blocks, kLayoutPairs, 0, s>>>(topi, n, E, hist);
+  const int smem = (34 * E + 2 * El) * static_cast<int>(sizeof(int));
+  moe_layout_place_kernel<<<(unsigned)blocks, kLayoutPairs, smem, s>>>(
+      topi, topw, n, k, E, lo, El, total, hist, static_cast<int>(blocks), (const __nv_bfloat16*)h, H,
+      (__nv_bfloat16*)xs, zero_pad, pos, w, tile_expert, row_start, seg_rows, counts);
   return (int)cudaGetLastError();
 }
 

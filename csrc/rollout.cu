@@ -178,6 +178,91 @@ __global__ void kv_cache_write_kernel(const __nv_bfloat16* __restrict__ k, const
   }
 }
 
+// Fused post-projection step of the engine's attention layers, one block per token row of the
+// fused qkv projection [Hq*128 | Hkv*128 | Hkv*128]:
+//   (Qwen3) per-head RMSNorm of the q and k heads, in place;
+//   rotary embedding (rotate-half) of the q and k heads, in place;
+//   the rotated k heads and the v heads into the paged caches at slots[t] (rows with slot < 0 skip).
+// This replaces four launches (two RMSNorms, RoPE, cache write) and their round trips through
+// memory. Every rounding matches the separate kernels: RMSNorm sums the squares in the order of
+// rmsnorm_fwd_kernel (eight per lane, then a butterfly; the lanes it leaves idle add zeros) and
+// rounds the normalised value before the weight; RoPE rounds cos/sin and its outputs to bf16.
+// A half-warp owns one head: lane l holds elements [8l, 8l + 8), and its rotation partner
+// (element d +- 64) sits on lane l +- 8.
+__global__ void __launch_bounds__(256) qkv_rope_cache_kernel(
+    __nv_bfloat16* __restrict__ qkv, long long ld, const long long* __restrict__ pos, const int* __restrict__ slots,
+    int Hq, int Hkv, float log2_theta, const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm,
+    float eps, __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, long long num_slots) {
+  __shared__ float cs[kDHead];  // [64] cos, [64] sin
+  const int t = blockIdx.x;
+  const float p = static_cast<float>(pos[t]);
+  for (int i = threadIdx.x; i < kDHead / 2; i += blockDim.x) {
+    float c, sn;
+    rope_cos_sin(p, i, kDHead, log2_theta, c, sn);
+    cs[i] = c;
+    cs[kDHead / 2 + i] = sn;
+  }
+  __syncthreads();
+  const int slot = slots[t];
+  const bool cache = slot >= 0 && ACCERL_DBG_OK(slot < num_slots, kDbgKvSlot, slot);
+  const int hl = threadIdx.x & 15;          // lane within the half-warp
+  const int half_id = threadIdx.x >> 4;     // 16 half-warps per block
+  const unsigned hmask = (threadIdx.x & 16) ? 0xffff0000u : 0x0000ffffu;
+  __nv_bfloat16* row = qkv + t * ld;
+  const int n_heads = Hq + 2 * Hkv;
+  for (int h = half_id; h < n_heads; h += blockDim.x >> 4) {
+    uint4* src = reinterpret_cast<uint4*>(row + h * kDHead) + hl;
+    uint4 v = *src;
+    if (h >= Hq + Hkv) {  // v head: to the cache only
+      if (cache) reinterpret_cast<uint4*>(v_cache + (static_cast<long long>(slot) * Hkv + (h - Hq - Hkv)) * kDHead)[hl] = v;
+      continue;
+    }
+    const __nv_bfloat16* nw = h < Hq ? q_norm : k_norm;
+    uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+    if (nw) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(vw[i]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+      // rmsnorm_fwd_kernel's butterfly starts at offset 16, which only adds the zeros of its idle lanes
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(hmask, ss, o, 16);
+      const float r = rsqrtf(ss / static_cast<float>(kDHead) + eps);
+      const uint4 wv = reinterpret_cast<const uint4*>(nw)[hl];
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16x2(vw[i]);
+        const float2 g = unpack_bf16x2(ww[i]);
+        const float2 n = unpack_bf16x2(pack_bf16x2(f.x * r, f.y * r));
+        vw[i] = pack_bf16x2(n.x * g.x, n.y * g.y);
+      }
+    }
+    // rotation: the partner lane holds the other half of every pair
+    uint32_t pw[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pw[i] = __shfl_xor_sync(hmask, vw[i], 8, 16);
+    const bool first = hl < 8;
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 mine = unpack_bf16x2(vw[i]), other = unpack_bf16x2(pw[i]);
+      const int d = (hl & 7) * 8 + 2 * i;  // frequency index of the pair's first element
+      const float c0 = cs[d], c1 = cs[d + 1], s0 = cs[kDHead / 2 + d], s1 = cs[kDHead / 2 + d + 1];
+      if (first) {  // x1 (mine) * c - x2 (other) * s
+        o[i] = pack_bf16x2(mine.x * c0 - other.x * s0, mine.y * c1 - other.y * s1);
+      } else {      // x2 (mine) * c + x1 (other) * s
+        o[i] = pack_bf16x2(mine.x * c0 + other.x * s0, mine.y * c1 + other.y * s1);
+      }
+    }
+    v = make_uint4(o[0], o[1], o[2], o[3]);
+    *src = v;
+    if (h >= Hq && cache) reinterpret_cast<uint4*>(k_cache + (static_cast<long long>(slot) * Hkv + (h - Hq)) * kDHead)[hl] = v;
+  }
+}
+
 }  // namespace accerl
 
 using namespace accerl;
@@ -226,6 +311,19 @@ extern "C" int accerl_kv_cache_write(const void* k, const void* v, void* k_cache
   if ((ldk | ldv) & 7) return -1;
   kv_cache_write_kernel<<<T, 128, 0, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (__nv_bfloat16*)k_cache,
                                           (__nv_bfloat16*)v_cache, slot_mapping, T, Hkv, ldk, ldv, num_slots);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int accerl_qkv_rope_cache(void* qkv, long long ld, const long long* pos, const int* slots, int T, int Hq,
+                                     int Hkv, float theta, const void* q_norm, const void* k_norm, float eps,
+                                     void* k_cache, void* v_cache, long long num_slots, cudaStream_t s) {
+  if (T == 0) return 0;
+  if ((ld & 7) || Hq < 1 || Hkv < 1 || ld < static_cast<long long>(Hq + 2 * Hkv) * kDHead || !(theta > 0.f) ||
+      (!q_norm) != (!k_norm))
+    return -1;
+  qkv_rope_cache_kernel<<<T, 256, 0, s>>>((__nv_bfloat16*)qkv, ld, pos, slots, Hq, Hkv, log2f(theta),
+                                          (const __nv_bfloat16*)q_norm, (const __nv_bfloat16*)k_norm, eps,
+                                          (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, num_slots);
   return (int)cudaGetLastError();
 }
 

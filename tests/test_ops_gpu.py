@@ -628,6 +628,80 @@ def test_moe_router_kernel(E, k, norm):
     assert torch.equal(cnt.long(), torch.bincount(topi.reshape(-1), minlength=E))
 
 
+@pytest.mark.parametrize("T,E,k,lo,El,skew", [(1000, 60, 4, 0, 60, False), (4099, 128, 8, 0, 128, True),
+                                                (2500, 64, 2, 16, 24, False), (3, 8, 2, 0, 8, False)])
+def test_moe_dispatch_kernel(T, E, k, lo, El, skew):
+    """One-pass dispatch (``moe_layout`` kernels) against the torch formulation of the same layout:
+    identical rows for every (token, slot) pair (stable within an expert), tile map, segment starts and
+    sizes, counts; weights rounded to bf16 (0 outside the shard's range); xs rows equal their token's
+    hidden row and padding rows are zero."""
+    from accerl_agent_b200.models.moe import device_dispatch, device_padded_layout
+
+    g = torch.Generator().manual_seed(T)
+    if skew:  # most pairs on a few experts: segments much longer than one 1024-pair block
+        scores = torch.rand(T, E, generator=g) + (torch.arange(E) < 3).float() * 2
+    else:
+        scores = torch.rand(T, E, generator=g)
+    topi = scores.topk(k, -1).indices.to(DEV)
+    topw = torch.rand(T, k, generator=g).to(DEV)
+    H = 256
+    h = torch.randn(T, H, device=DEV).bfloat16()
+    for _ in range(2):  # the histogram scratch keeps the last call's contents
+        xs, pos, w, lay = device_dispatch(topi, topw, h, E, lo, El, zero_pad=True)
+        torch.cuda.synchronize()
+        order, rows, valid, ref = device_padded_layout(topi, E, lo, El)
+        assert lay["total"] == ref["total"]
+        want_pos = torch.empty_like(pos)
+        want_pos[order] = rows
+        assert torch.equal(pos, want_pos)
+        for key in ("tile_expert", "row_start", "rows"):
+            assert torch.equal(lay[key], ref[key].to(torch.int32)), key
+        assert torch.equal(lay["counts"].long(), torch.bincount(topi.reshape(-1), minlength=E))
+        ok = pos < lay["total"]
+        want_w = torch.where(ok, topw.reshape(-1).bfloat16().float(), torch.zeros_like(w))
+        assert torch.equal(w, want_w)
+        tok = torch.arange(T * k, device=DEV) // k
+        assert torch.equal(xs[pos[ok]], h[tok[ok]])
+        used = torch.zeros(lay["total"], dtype=torch.bool, device=DEV)
+        used[pos[ok]] = True
+        assert bool((xs[~used] == 0).all())
+
+
+@pytest.mark.parametrize("Hq,Hkv,qk_norm", [(6, 2, False), (16, 4, True), (7, 1, True)])
+def test_qkv_rope_cache_fused(Hq, Hkv, qk_norm):
+    """The engine's fused post-projection kernel (qk-norm, RoPE, paged cache write) against the
+    separate kernels it replaces, run in the same order; rows with slot -1 leave the caches alone."""
+    T, D, blocks, bs = 300, 128, 64, 16
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).bfloat16()
+    pos = torch.randint(0, 30000, (T,), device=DEV)
+    slots = torch.randperm(blocks * bs, device=DEV)[:T].to(torch.int32)
+    slots[::7] = -1
+    qn = (1 + 0.1 * torch.randn(D, device=DEV)).bfloat16() if qk_norm else None
+    kn = (1 + 0.1 * torch.randn(D, device=DEV)).bfloat16() if qk_norm else None
+    kc = torch.full((blocks, bs, Hkv, D), 7.0, device=DEV).bfloat16()
+    vc = kc.clone()
+    want_qkv, want_kc, want_vc = qkv.clone(), kc.clone(), vc.clone()
+    qd, kd = Hq * D, Hkv * D
+    if qk_norm:
+        a, _ = ops.rmsnorm(want_qkv[:, :qd].reshape(T * Hq, D).clone(), qn, 1e-6)
+        b, _ = ops.rmsnorm(want_qkv[:, qd : qd + kd].reshape(T * Hkv, D).clone(), kn, 1e-6)
+        want_qkv[:, :qd].copy_(a.view(T, qd))
+        want_qkv[:, qd : qd + kd].copy_(b.view(T, kd))
+    ops.rope_(want_qkv, pos, Hq + Hkv, D, 1e6)
+    ops.kv_cache_write(want_qkv[:, qd : qd + kd], want_qkv[:, qd + kd :], want_kc, want_vc, slots, Hkv)
+    got = qkv.clone()
+    ops.native().qkv_rope_cache(got, pos, slots, kc, vc, Hq, Hkv, 1e6, qn, kn, 1e-6)
+    torch.cuda.synchronize()
+    for g, w in ((got, want_qkv), (kc, want_kc), (vc, want_vc)):
+        # same roundings in the same order; a contraction of a*b - c*d into an FMA may differ by one
+        # bf16 step on rare elements
+        torch.testing.assert_close(g.float(), w.float(), atol=1e-6, rtol=2 ** -7)
+        assert (g != w).float().mean().item() < 1e-3
+    untouched = torch.ones(blocks * bs, dtype=torch.bool, device=DEV)
+    untouched[slots[slots >= 0].long()] = False
+    assert bool((kc.view(-1, Hkv, D)[untouched] == 7.0).all()) and bool((vc.view(-1, Hkv, D)[untouched] == 7.0).all())
+
+
 @pytest.mark.parametrize("block_n", [0, 256, 128, -256])
 def test_gemm_rope_epilogue(block_n):
     """qkv projection with the rotary embedding in the epilogue equals the projection followed by the
