@@ -64,8 +64,8 @@ def exchange_weight_handles(trainers, engines, followers, timeout: float = 600.0
     handles = None
     for i, e in enumerate(engines):
         handle = get(trainers[i % len(trainers)].export_weights_handle.remote(), timeout=timeout)
-        if isinstance(handle, dict) and handle.get("partition"):
-            # expert-partitioned trainers: every engine rank maps every trainer (experts come from owners)
+        if isinstance(handle, dict) and (handle.get("partition") or handle.get("zero3")):
+            # expert-partitioned or layer-sharded trainers: every engine rank maps every trainer
             if handles is None:
                 handles = get([t.export_weights_handle.remote() for t in trainers], timeout=timeout)
             handle = handles

@@ -105,6 +105,10 @@ def build_parser() -> argparse.ArgumentParser:
     a("--device", default="auto", help="auto | cpu | cuda")
     a("--kv-cache-gb", type=float, default=None, help="KV cache size per rollout GPU (default: 60%% of free memory).")
     a("--kv-block-size", type=int, default=16)
+    a("--shard-params", action="store_true",
+      help="Shard parameters, gradients and optimizer state over the FSDP ranks per decoder layer "
+           "(all-gathered before each layer's forward and backward, gradients reduce-scattered after "
+           "it, as FSDP full sharding does); for models whose compute copy does not fit on every rank.")
     a("--expert-parallel", action="store_true",
       help="MoE models: partition the experts over the trainer ranks (token dispatch/combine over NVLink).")
     a("--expert-storage", default="partitioned", choices=("partitioned", "replicated"),

@@ -196,8 +196,17 @@ def load_hf_checkpoint(model, path: str, strict: bool = True) -> None:
     else:
         state = read_hf_state(path)
     used = set()
+    _load_views(cfg, state, model.named_parameters(), path, strict, used)
+    if strict and not partitioned:
+        extra = [n for n in state if n not in used and not (cfg.tie_word_embeddings and n == "lm_head.weight")]
+        if extra:
+            raise KeyError(f"unexpected tensors in checkpoint: {extra[:5]}")
+
+
+def _load_views(cfg: ModelConfig, state, named_views, path: str, strict: bool, used: set) -> None:
+    """Copy the checkpoint tensors of ``state`` into the fused-layout ``(name, view)`` pairs."""
     with torch.no_grad():
-        for name, view in model.named_parameters():
+        for name, view in named_views:
             if (name.endswith("mlp.experts.gate_up_proj") or name.endswith("mlp.experts.down_proj")) and name in state:
                 src = state[name]
                 if src.shape[0] != view.shape[0]:
@@ -216,10 +225,67 @@ def load_hf_checkpoint(model, path: str, strict: bool = True) -> None:
                     raise ValueError(f"{hf_name}: checkpoint shape {tuple(src.shape)} != model {tuple(dst.shape)}")
                 dst.copy_(src.to(dst.dtype))
                 used.add(hf_name)
-    if strict and not partitioned:
-        extra = [n for n in state if n not in used and not (cfg.tie_word_embeddings and n == "lm_head.weight")]
-        if extra:
-            raise KeyError(f"unexpected tensors in checkpoint: {extra[:5]}")
+
+
+def save_hf_checkpoint_sharded(sharding, out_dir: str, dtype: Optional[torch.dtype] = None) -> List[str]:
+    """HF checkpoint of layer-sharded parameters (``parallel/zero3.py``): every unit is all-gathered
+    once (a collective over the ranks) and rank ``u % W`` writes unit ``u`` as its own file, so the
+    writes run in parallel with no rank holding more than one unit; rank 0 writes config and index."""
+    from safetensors.torch import save_file
+
+    cfg, units, rank, world = sharding.cfg, sharding.units, sharding.rank, sharding.world
+    os.makedirs(out_dir, exist_ok=True)
+    n = len(units)
+    fname = lambda i: f"model-{i + 1:05d}-of-{n:05d}.safetensors"  # noqa: E731
+    index = {u.name: i for i, u in enumerate(units)}
+    written: List[str] = []
+
+    def write(u, views):
+        i = index[u.name]
+        if i % world != rank:
+            return
+        tensors = {}
+        for name in u.names:
+            for hf, t in hf_items(cfg, name, views[name]):
+                tt = t.detach() if dtype is None else t.detach().to(dtype)
+                tensors[hf] = tt.to("cpu").contiguous()
+        save_file(tensors, os.path.join(out_dir, fname(i)), metadata={"format": "pt"})
+        written.append(fname(i))
+
+    sharding.for_each_unit_gathered(write)
+    if rank == 0:
+        cfg.save(out_dir)
+        weight_map, total = {}, 0
+        meta = torch.empty(sharding.layout.total_numel, dtype=dtype or sharding.dtype, device="meta")
+        for i, u in enumerate(units):
+            for name in u.names:
+                s = sharding.layout.slots[name]
+                for hf, t in hf_items(cfg, name, meta[s.offset : s.offset + s.numel].view(s.shape)):
+                    weight_map[hf] = fname(i)
+                    total += t.numel() * t.element_size()
+        with open(os.path.join(out_dir, "model.safetensors.index.json"), "w", encoding="utf-8") as f:
+            json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f, indent=2)
+    return written
+
+
+def load_hf_checkpoint_sharded(sharding, path: str, strict: bool = True) -> None:
+    """Fill this rank's shards of layer-sharded parameters from an HF checkpoint (unit by unit; only
+    the files of each unit are read)."""
+    cfg = sharding.cfg
+    used: set = set()
+
+    def fill(u, views):
+        meta = torch.empty(sharding.layout.total_numel, dtype=sharding.dtype, device="meta")
+        wanted = []
+        for name in u.names:
+            s = sharding.layout.slots[name]
+            wanted += [hf for hf, _ in hf_items(cfg, name, meta[s.offset : s.offset + s.numel].view(s.shape))]
+            if ".mlp.experts." in name:
+                wanted.append(name)
+        state = read_hf_state(path, wanted)
+        _load_views(cfg, state, [(name, views[name]) for name in u.names], path, strict, used)
+
+    sharding.for_each_unit_gathered(fill, write_back=True)
 
 
 def vllm_weight_metadata(model, trainable_only: bool = False):

@@ -19,19 +19,17 @@ from .. import ops
 
 
 def gate_pair(model, layer: int, grads: bool = False) -> Optional[torch.Tensor]:
-    """[router weight; shared-expert gate weight] as one [E + 1, H] view of the flat parameter (or
-    fp32 gradient) buffer, or None when the layer has no shared expert or the two are not adjacent."""
+    """[router weight; shared-expert gate weight] as one [E + 1, H] view of the parameter (or fp32
+    gradient) storage, or None when the layer has no shared expert or the two are not adjacent."""
     p = f"model.layers.{layer}.mlp."
-    slots = model.layout.slots
-    a, b = slots.get(p + "gate.weight"), slots.get(p + "shared_expert_gate.weight")
-    if a is None or b is None or a.offset + a.numel != b.offset or a.trainable != b.trainable:
+    get = model.g if grads else model.w
+    if p + "shared_expert_gate.weight" not in model.layout.slots:
+        return None
+    a, b = get(p + "gate.weight"), get(p + "shared_expert_gate.weight")
+    if a is None or b is None or a.data_ptr() + a.numel() * a.element_size() != b.data_ptr():
         return None
     E, H = a.shape
-    if grads:
-        if not a.trainable or model.grads is None:
-            return None
-        return model.grads[a.grad_offset : a.grad_offset + (E + 1) * H].view(E + 1, H)
-    return model.params[a.offset : a.offset + (E + 1) * H].view(E + 1, H)
+    return a.as_strided((E + 1, H), (H, 1))
 
 
 def route(model, layer: int, h: torch.Tensor, counts: bool = False, shared_gate: Optional[list] = None):

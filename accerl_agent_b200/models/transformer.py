@@ -191,6 +191,19 @@ class CausalLM:
         self.rebind(params, grads)
         self.first_trainable_layer = self._first_trainable_layer()
         self.gradient_checkpointing = False
+        self.units = None  # layer-sharded parameters (parallel/zero3.py) bind views around each layer
+
+    @classmethod
+    def without_buffers(cls, cfg: ModelConfig, layout: "ParamLayout") -> "CausalLM":
+        """A model whose views are bound unit by unit by layer-sharded parameters (no flat buffers)."""
+        self = cls.__new__(cls)
+        self.cfg, self.layout = cfg, layout
+        self.params = self.grads = None
+        self._views, self._gviews = {}, {}
+        self.first_trainable_layer = 0
+        self.gradient_checkpointing = False
+        self.units = None
+        return self
 
     # ---------------------------------------------------------------- parameters
     def rebind(self, params: torch.Tensor, grads: Optional[torch.Tensor]) -> None:
@@ -225,27 +238,33 @@ class CausalLM:
 
     def init_weights(self, seed: int = 0, std: float = 0.02) -> None:
         """Random init (normal(0, std) matrices, unit norms, zero biases), deterministic per seed."""
+        if self.units is not None:
+            self.units.init_weights(seed, std)
+            return
         dev = self.params.device
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
-        cfg = self.cfg
-        partial = cfg.local_experts is not None and cfg.local_experts != cfg.num_experts
         with torch.no_grad():
             for name in self.layout.order:
-                v = self._views[name]
-                if name.endswith("norm.weight") or "layernorm" in name:
-                    v.fill_(1.0)
-                elif name.endswith(".bias"):
-                    v.zero_()
-                elif partial and is_expert_param(name):
-                    # draw the whole expert stack and keep this rank's experts: every partition of the
-                    # experts holds exactly the values of the unpartitioned model
-                    full = torch.randn((cfg.num_experts,) + tuple(v.shape[1:]), generator=gen, dtype=torch.float32,
-                                       device=dev) * std
-                    v.copy_(full[cfg.expert_offset : cfg.expert_offset + v.shape[0]].to(v.dtype))
-                else:
-                    chunk = torch.randn(v.shape, generator=gen, dtype=torch.float32, device=dev) * std
-                    v.copy_(chunk.to(v.dtype))
+                self._init_param(name, self._views[name], gen, std)
+
+    def _init_param(self, name: str, v: torch.Tensor, gen: torch.Generator, std: float) -> None:
+        cfg = self.cfg
+        partial = cfg.local_experts is not None and cfg.local_experts != cfg.num_experts
+        dev = v.device
+        if name.endswith("norm.weight") or "layernorm" in name:
+            v.fill_(1.0)
+        elif name.endswith(".bias"):
+            v.zero_()
+        elif partial and is_expert_param(name):
+            # draw the whole expert stack and keep this rank's experts: every partition of the
+            # experts holds exactly the values of the unpartitioned model
+            full = torch.randn((cfg.num_experts,) + tuple(v.shape[1:]), generator=gen, dtype=torch.float32,
+                               device=dev) * std
+            v.copy_(full[cfg.expert_offset : cfg.expert_offset + v.shape[0]].to(v.dtype))
+        else:
+            chunk = torch.randn(v.shape, generator=gen, dtype=torch.float32, device=dev) * std
+            v.copy_(chunk.to(v.dtype))
 
     # ---------------------------------------------------------------- forward
     def _layer_forward(self, layer: int, x: torch.Tensor, pos, cu, max_seqlen, save: bool):
@@ -300,10 +319,15 @@ class CausalLM:
         return {"q_raw": q_raw, "k_raw": k_raw, "rq": rq, "rk": rk}
 
     def forward_hidden(self, ids: torch.Tensor, pos: torch.Tensor, cu: torch.Tensor, max_seqlen: int, save: bool):
+        units = self.units
+        if units is not None:
+            units.begin_forward()
         x = ops.embedding(ids, self.w("model.embed_tokens.weight"))
         caches: List[Optional[LayerCache]] = []
         start_save = self.first_trainable_layer
         for layer in range(self.cfg.num_hidden_layers):
+            if units is not None:
+                units.before_forward(layer)
             keep = save and layer >= start_save
             if keep and self.gradient_checkpointing:
                 x_in = x
@@ -337,11 +361,16 @@ class CausalLM:
     # ---------------------------------------------------------------- backward
     def backward_from_logprobs(self, dlp: torch.Tensor, ctx: ForwardCtx) -> None:
         cfg = self.cfg
+        units = self.units
+        if units is not None:
+            units.begin_backward()
         W = self.w(self.lm_head_name)
         gW = self.g(self.lm_head_name)
         need_drows = not (self.first_trainable_layer >= cfg.num_hidden_layers and self.g("model.norm.weight") is None)
         drows = ops.lm_head_backward(ctx.rows, W, ctx.labels, ctx.lse, dlp.float(), gW, need_drows)
         if not need_drows:
+            if units is not None:
+                units.end_backward()
             return
         dhN = torch.zeros_like(ctx.x_final)
         dhN.index_copy_(0, ctx.pred_idx, drows)
@@ -350,14 +379,20 @@ class CausalLM:
         for layer in range(cfg.num_hidden_layers - 1, -1, -1):
             if layer < self.first_trainable_layer:
                 break
+            if units is not None:
+                units.before_backward(layer)
             cache = ctx.layers[layer]
             if cache is not None and cache.h1 is None:  # gradient checkpointing: recompute this layer
                 _, cache = self._layer_forward(layer, cache.x, ctx.pos, ctx.cu, ctx.max_seqlen, save=True)
             dx = self._layer_backward(layer, dx, cache, ctx)
             ctx.layers[layer] = None
+            if units is not None:
+                units.after_backward(layer)
         gE = self.g("model.embed_tokens.weight")
         if gE is not None and self.first_trainable_layer == 0:
             ops.embedding_backward(ctx.ids, dx, gE)
+        if units is not None:
+            units.end_backward()
 
     def _layer_backward(self, layer: int, dx3: torch.Tensor, c: LayerCache, ctx: ForwardCtx) -> torch.Tensor:
         cfg = self.cfg

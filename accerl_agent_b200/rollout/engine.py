@@ -413,6 +413,16 @@ class GenerationEngine:
         self._weight_maps = maps
         self._weight_src = [(src.get("tensor"), src.get("addr")) for src in sources]
 
+    def set_weight_plans(self, plans_by_scope, sources) -> None:
+        """Precomputed copy plans, one per source buffer and scope (layer-sharded trainers: every
+        element is pulled from the trainer that stores it). ``sources`` lists dicts with ``tensor``
+        or ``addr``."""
+        from .weight_map import descs_tensor
+
+        self._weight_maps = {scope: [(pl, descs_tensor(pl, self.device) if self.device.type == "cuda" and pl else None)
+                                     for pl in plans] for scope, plans in plans_by_scope.items()}
+        self._weight_src = [(src.get("tensor"), src.get("addr")) for src in sources]
+
     def pull_weights(self, scope: str = "all") -> int:
         """Copy this engine's slice of the registered trainer buffer into its weights (every TP rank
         pulls its own shard). Returns the bytes this rank copied."""

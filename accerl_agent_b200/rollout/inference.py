@@ -215,6 +215,30 @@ def _open_handle(handle, device: torch.device, opened: List[int]):
     return tensor, None, int(tensor.numel())
 
 
+def _attach_sharded_sources(engine: GenerationEngine, cfg, device: torch.device, handles, opened: List[int]) -> int:
+    """Layer-sharded trainers (``parallel/zero3.py``): map every trainer's shard buffer and pull each
+    element from the trainer that stores it."""
+    from ..models.transformer import ParamLayout
+    from ..parallel.zero3 import build_units, shard_pieces
+    from .weight_map import build_weight_map_sharded
+
+    world = int(handles[0]["world"])
+    handles = sorted(handles, key=lambda h: int(h["trainer_rank"]))
+    if [int(h["trainer_rank"]) for h in handles] != list(range(world)):
+        raise ValueError("layer-sharded weight sync needs the handle of every trainer rank")
+    full = ParamLayout.build(cfg, "full", pad_to=1)
+    pieces = shard_pieces(build_units(full, world), world)
+    srcs, total = [], 0
+    for h in handles:
+        tensor, addr, numel = _open_handle(h, device, opened)
+        srcs.append({"tensor": tensor, "addr": addr})
+        total += numel
+    plans = {scope: build_weight_map_sharded(cfg, full, pieces, world, engine.layout, engine.tp_rank, engine.tp, scope)
+             for scope in ("all", "trainable")}
+    engine.set_weight_plans(plans, srcs)
+    return total
+
+
 def attach_weight_source(engine: GenerationEngine, args, device: torch.device, handle, opened: List[int]) -> int:
     """Open a trainer's exported parameter handle on ``device`` and register it with ``engine``. A list
     of handles (one per trainer rank, from expert-partitioned trainers) registers every buffer: routed
@@ -223,6 +247,8 @@ def attach_weight_source(engine: GenerationEngine, args, device: torch.device, h
 
     handles = handle if isinstance(handle, list) else [handle]
     cfg = engine.full_cfg
+    if isinstance(handles[0], dict) and handles[0].get("zero3"):
+        return _attach_sharded_sources(engine, cfg, device, handles, opened)
     srcs, total = [], 0
     for h in handles:
         part = bool(isinstance(h, dict) and h.get("partition"))

@@ -164,6 +164,48 @@ def build_weight_map_multi(cfg: ModelConfig, sources, dst_layout, tp_rank: int =
     return [coalesce(pl) for pl in plans]
 
 
+def split_by_pieces(descs: List[CopyDesc], pieces, n_sources: int) -> List[List[CopyDesc]]:
+    """Copy plans against a source spread over several buffers. ``descs`` address one virtual flat
+    source; ``pieces`` (sorted ``(start, end, source, shift)``) say that virtual elements
+    ``[start, end)`` live in buffer ``source`` at ``element - start + shift``. The rows of a 2-D copy
+    that lie inside one piece move as one 2-D copy from that buffer; a row that crosses a piece
+    boundary is cut into 1-row copies. Returns one plan per source."""
+    import bisect
+
+    starts = [pc[0] for pc in pieces]
+    plans: List[List[CopyDesc]] = [[] for _ in range(n_sources)]
+    for d in descs:
+        ld, R, C = d.src_ld, d.rows, d.cols
+        first, last = d.src_off, d.src_off + (R - 1) * ld + C
+        k = max(bisect.bisect_right(starts, first) - 1, 0)
+        while k < len(pieces) and pieces[k][0] < last:
+            a, b, src, shift = pieces[k]
+            k += 1
+            if b <= first:
+                continue
+            i0 = max(0, -(-(a - d.src_off) // ld))  # first row starting at or after a
+            i1 = min(R, (b - C - d.src_off) // ld + 1) if b - C - d.src_off >= 0 else 0  # rows ending by b
+            if i0 < i1:
+                plans[src].append(CopyDesc(d.src_off + i0 * ld - a + shift, ld, d.dst_off + i0 * d.dst_ld, d.dst_ld,
+                                           i1 - i0, C))
+            for i in sorted({(a - d.src_off) // ld, (b - 1 - d.src_off) // ld}):
+                if not 0 <= i < R or i0 <= i < i1:
+                    continue  # outside the copy, or already moved whole
+                r0 = d.src_off + i * ld
+                lo, hi = max(r0, a), min(r0 + C, b)
+                if lo < hi:
+                    n = hi - lo
+                    plans[src].append(CopyDesc(lo - a + shift, n, d.dst_off + i * d.dst_ld + (lo - r0), n, 1, n))
+    return [coalesce(pl) for pl in plans]
+
+
+def build_weight_map_sharded(cfg: ModelConfig, full_layout, pieces, n_sources: int, dst_layout, tp_rank: int = 0,
+                             tp_size: int = 1, scope: str = "all") -> List[List[CopyDesc]]:
+    """Copy plans from layer-sharded trainers (``parallel/zero3.py``): the plan of the unsharded
+    layout, split by where each element lives (``shard_pieces``). Returns one plan per trainer."""
+    return split_by_pieces(build_weight_map(cfg, full_layout, dst_layout, tp_rank, tp_size, scope), pieces, n_sources)
+
+
 def coalesce(descs: List[CopyDesc]) -> List[CopyDesc]:
     """Merge copies that are contiguous in both buffers into single 1-D copies (identical layouts
     collapse to one copy per contiguous run)."""

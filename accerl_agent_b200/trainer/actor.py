@@ -45,7 +45,7 @@ class TrainerActor:
         self.worker = TrainWorker(args, rank, world, master_addr, master_port, replay_buffer=self.replay,
                                   device=device, tokenizer=_load_tokenizer(args))
         if device.type == "cpu":
-            self.worker.model.params.share_memory_()
+            self.worker.flat_weights("all").share_memory_()
         self._queue = sample_queue
         self._stop = False
         self._drain = threading.Thread(target=self._drain_samples, daemon=True)
@@ -74,6 +74,8 @@ class TrainerActor:
         return self.worker.get_weight_metadata(scope)
 
     def weight_numel(self, scope: str = "all") -> int:
+        if self.worker.sharding is not None:
+            return int(self.worker.sharding.full_numel())
         return int(self.worker.flat_weights(scope).numel())
 
     def export_weights_handle(self):
@@ -83,10 +85,13 @@ class TrainerActor:
         expert-partitioned storage (the handle then says which rank of how many it is)."""
         from torch.multiprocessing.reductions import reduce_tensor
 
-        params = self.worker.model.params
+        params = self.worker.flat_weights("all")
         mcfg = self.worker.model.cfg
         part = {}
-        if mcfg.local_experts is not None and mcfg.local_experts != mcfg.num_experts:
+        if self.worker.sharding is not None:
+            # layer-sharded trainers: this buffer holds this rank's shard of every unit
+            part = {"zero3": True, "trainer_rank": self.worker.rank, "world": self.worker.fsdp_world_size}
+        elif mcfg.local_experts is not None and mcfg.local_experts != mcfg.num_experts:
             # expert-partitioned storage: the engine needs every rank's buffer and where its experts sit
             part = {"partition": True, "trainer_rank": self.worker.rank, "world": self.worker.fsdp_world_size}
         if params.is_cuda:

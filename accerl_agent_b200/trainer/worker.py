@@ -180,18 +180,36 @@ class TrainWorker:
         # only its routed experts; the replicated part is laid out first and sharded by the optimizer
         self.expert_partitioned = use_ep and getattr(args, "expert_storage", "partitioned") == "partitioned"
         model_cfg = expert_partition(self.cfg, rank, fsdp_world_size) if self.expert_partitioned else self.cfg
-        self.model = build_model(model_cfg, args.train_mode, self.device, self.dtype, pad_to=fsdp_world_size,
-                                 experts_last=self.expert_partitioned)
-        self.model.gradient_checkpointing = bool(args.gradient_checkpointing)
-        if os.path.isdir(args.model_path) and any(
-            f.endswith(".safetensors") for f in os.listdir(args.model_path)
-        ):
-            load_hf_checkpoint(self.model, args.model_path)
+        has_ckpt = os.path.isdir(args.model_path) and any(f.endswith(".safetensors") for f in os.listdir(args.model_path))
+        self.sharding = None
+        if getattr(args, "shard_params", False):
+            # parameters, gradients and optimizer state sharded per layer (parallel/zero3.py)
+            if use_ep:
+                raise ValueError("--shard-params cannot be combined with --expert-parallel")
+            if args.train_mode != "full":
+                raise ValueError("--shard-params needs --train-mode full")
+            from ..models.hf_io import load_hf_checkpoint_sharded
+            from ..parallel.zero3 import LayerShardedParams, ShardedParamAdamW
+
+            self.sharding = LayerShardedParams(self.cfg, self.device, self.dtype)
+            self.model = self.sharding.model
+            self.model.gradient_checkpointing = bool(args.gradient_checkpointing)
+            if has_ckpt:
+                load_hf_checkpoint_sharded(self.sharding, args.model_path)
+            else:
+                self.model.init_weights(seed=args.seed)
+            self.optimizer = ShardedParamAdamW(self.sharding, lr=args.learning_rate, weight_decay=args.weight_decay)
         else:
-            self.model.init_weights(seed=args.seed)
-        if self.model.layout.trainable_numel == 0:
-            raise RuntimeError(f"No trainable parameters found for mode: {args.train_mode}")
-        self.optimizer = ShardedAdamW(self.model, lr=args.learning_rate, weight_decay=args.weight_decay)
+            self.model = build_model(model_cfg, args.train_mode, self.device, self.dtype, pad_to=fsdp_world_size,
+                                     experts_last=self.expert_partitioned)
+            self.model.gradient_checkpointing = bool(args.gradient_checkpointing)
+            if has_ckpt:
+                load_hf_checkpoint(self.model, args.model_path)
+            else:
+                self.model.init_weights(seed=args.seed)
+            if self.model.layout.trainable_numel == 0:
+                raise RuntimeError(f"No trainable parameters found for mode: {args.train_mode}")
+            self.optimizer = ShardedAdamW(self.model, lr=args.learning_rate, weight_decay=args.weight_decay)
         if use_ep:
             if getattr(args, "train_packing", "padded") == "varlen" and args.train_token_budget:
                 max_tokens = int(args.train_token_budget)
@@ -663,11 +681,18 @@ class TrainWorker:
     def get_weight_metadata(self, scope: str = "all"):
         if scope not in ("all", "trainable"):
             raise ValueError(f"Unsupported weight scope: {scope!r}")
-        return vllm_weight_metadata(self.model, trainable_only=scope == "trainable")
+        model = self.model
+        if self.sharding is not None:  # names and shapes only: a model over meta storage
+            model = build_model(self.cfg, "full", torch.device("meta"), self.dtype, with_grads=False)
+        return vllm_weight_metadata(model, trainable_only=scope == "trainable")
 
     def flat_weights(self, scope: str = "all") -> torch.Tensor:
         """The full bf16 compute copy in fused layout. Trainable parameters form a contiguous prefix,
         so a trainable-scope sync is a single contiguous range."""
+        if self.sharding is not None:  # this rank's shards of every unit (the engine maps every rank)
+            if scope not in ("all", "trainable"):
+                raise ValueError(f"Unsupported weight scope: {scope!r}")
+            return self.sharding.local
         if scope == "trainable":
             return self.model.params[: self.model.layout.trainable_numel]
         if scope == "all":
@@ -694,7 +719,12 @@ class TrainWorker:
             dist.barrier()
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
-        save_hf_checkpoint(self.model, out, rank=self.rank, world=self.fsdp_world_size)
+        if self.sharding is not None:
+            from ..models.hf_io import save_hf_checkpoint_sharded
+
+            save_hf_checkpoint_sharded(self.sharding, out)
+        else:
+            save_hf_checkpoint(self.model, out, rank=self.rank, world=self.fsdp_world_size)
         if save_optimizer:
             torch.save({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in self.optimizer.state_dict().items()},
                        os.path.join(out, f"optimizer_rank{self.rank:05d}.pt"))
@@ -721,7 +751,12 @@ class TrainWorker:
 
     def load_checkpoint(self, path: str) -> None:
         """Resume: weights from the HF files, optimizer shards and counters when present."""
-        load_hf_checkpoint(self.model, path)
+        if self.sharding is not None:
+            from ..models.hf_io import load_hf_checkpoint_sharded
+
+            load_hf_checkpoint_sharded(self.sharding, path)
+        else:
+            load_hf_checkpoint(self.model, path)
         self.optimizer.refresh_master_from_params()
         opt = os.path.join(path, f"optimizer_rank{self.rank:05d}.pt")
         if os.path.exists(opt):
