@@ -261,11 +261,13 @@ def run_train(args) -> Dict[str, float]:
                 except Exception as exc:
                     print(f"[cleanup] Ignoring engine follower shutdown error: {exc!r}")
                 f.stop_process()
+        # every trainer rank leaves its process group at the same time: destroying the group waits
+        # for the other ranks, so closing them one after another would wait out each timeout
+        try:
+            get([t.close.remote() for t in trainers], timeout=60)
+        except Exception as exc:
+            print(f"[cleanup] Ignoring trainer close error: {exc!r}")
         for t in trainers:
-            try:
-                get(t.close.remote(), timeout=60)
-            except Exception as exc:
-                print(f"[cleanup] Ignoring trainer close error: {exc!r}")
             t.stop_process()
         writer.close()
     return final

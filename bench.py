@@ -40,6 +40,8 @@ def parse():
     ap.add_argument("--model", default="qwen2.5-1.5b")
     ap.add_argument("--expert-parallel", action="store_true",
                     help="MoE models: experts partitioned over the ranks, token dispatch/combine over NVLink")
+    ap.add_argument("--shard-params", action="store_true",
+                    help="parameters, gradients and optimizer state sharded per layer (FSDP full sharding)")
     return ap.parse_args()
 
 
@@ -98,7 +100,7 @@ def run_native(a):
         tw_history_token_window=a.max_length, batch_size=a.batch_size, grad_accum_steps=a.grad_accum_steps,
         train_logprob_mode="response_only_lm_head", rl_algorithm="grpo", clip_mode="ppo", clip_eps=0.2,
         learning_rate=1e-6, lr_warmup_steps=0, max_steps=10**6, dtype="bfloat16", fsdp_world_size=world,
-        device="cuda", seed=42, expert_parallel=a.expert_parallel,
+        device="cuda", seed=42, expert_parallel=a.expert_parallel, shard_params=a.shard_params,
     )
     pool = synthetic_pool(rank, 256, a.max_length)
     replay = ReplayBuffer(args.replay_capacity, seed=rank)
@@ -195,7 +197,8 @@ def run_native(a):
                 "seq_len": a.max_length,
                 "token_budget_per_pack": a.token_budget,
                 "grad_accum_steps": a.grad_accum_steps,
-                "parallelism": f"fsdp{world}" + (f"+ep{world}" if a.expert_parallel and world > 1 else ""),
+                "parallelism": f"fsdp{world}" + (f"+ep{world}" if a.expert_parallel and world > 1 else "")
+                               + ("-full-shard" if a.shard_params else ""),
                 "algorithm": "grpo advantages + ppo clip 0.2, varlen packing, response-only LM head",
                 "l2": "inputs larger than L2 (GBs of weights/activations per step); no flush needed",
             },
