@@ -36,7 +36,7 @@ def _full_params(w):
     return out
 
 
-def _worker(rank, port, model_path, sharded, ckpt, out):
+def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False):
     from accerl_agent_b200.core.config import make_args
     from accerl_agent_b200.replay import ReplayBuffer
     from accerl_agent_b200.trainer.worker import TrainWorker
@@ -47,7 +47,8 @@ def _worker(rank, port, model_path, sharded, ckpt, out):
         args = make_args(model_path=model_path, train_packing="varlen", train_token_budget=64, max_length=64,
                          tw_history_token_window=64, batch_size=1, grad_accum_steps=2, device="cpu",
                          shard_params=sharded, min_replay_size_per_rank=1, replay_sample_timeout_seconds=5.0,
-                         replay_wait_sleep_seconds=0.05, dtype="float32", learning_rate=1e-3, lr_warmup_steps=0)
+                         replay_wait_sleep_seconds=0.05, dtype="float32", learning_rate=1e-3, lr_warmup_steps=0,
+                         gradient_checkpointing=checkpointing)
         rb = ReplayBuffer(8, seed=rank)
         g = torch.Generator().manual_seed(5 + rank)
         for i in range(2):
@@ -70,11 +71,12 @@ def _worker(rank, port, model_path, sharded, ckpt, out):
         raise
 
 
-def _run(model_path, sharded, ckpt=None):
+def _run(model_path, sharded, ckpt=None, checkpointing=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, port, model_path, sharded, ckpt, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, model_path, sharded, ckpt, q, checkpointing))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -125,6 +127,23 @@ def test_layer_sharded_trainer_matches_replicated(model_path, tmp_path):
     sp.for_each_unit_gathered(lambda u, views: back.update({n: views[n].clone() for n in u.names}))
     for n, v in back.items():
         assert torch.equal(v, sh[0][2][n]), n
+
+
+def test_layer_sharded_tied_embeddings_with_recomputation(tmp_path):
+    """Tied embeddings (the head unit holds only the final norm; the embedding unit serves both ends)
+    with gradient checkpointing (each layer's forward is recomputed inside its backward, while the
+    layer is gathered): the same weights as replicated parameters."""
+    from accerl_agent_b200.models.config import get_preset
+
+    cfg = get_preset("tiny-qwen2")
+    cfg.tie_word_embeddings = True
+    path = str(tmp_path / "tied")
+    cfg.save(path)
+    sh = _run(path, True, checkpointing=True)
+    rep = _run(path, False, checkpointing=True)
+    assert "lm_head.weight" not in rep[0][2]
+    for n, w in rep[0][2].items():
+        assert torch.allclose(sh[0][2][n], w, atol=2e-5, rtol=1e-4), n
 
 
 def test_shard_copy_plans_assemble_the_engine_weights():
