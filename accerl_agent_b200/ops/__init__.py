@@ -33,14 +33,16 @@ class _Checked:
     def __getattr__(self, name):
         fn = getattr(self._ext, name)
         per_call = KERNELS_PER_CALL.get(name, 1)
+        last_error = self._ext.last_error
 
         def call(*args):
             fn(*args)
             LAUNCHES[0] += per_call
-            rc, msg = self._ext.last_error()
+            rc, msg = last_error()
             if rc != 0:
                 raise RuntimeError(f"native op {name} failed (code {rc}): {msg}")
 
+        self.__dict__[name] = call  # later lookups find the wrapper without __getattr__
         return call
 
 

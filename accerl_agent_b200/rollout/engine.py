@@ -322,9 +322,10 @@ class GenerationEngine:
         released, its tokens kept) and continues after ``resume_generation``, recomputing its prompt
         and tokens so far under whatever weights were loaded meanwhile."""
         def _pause():
-            with self._step_lock:
-                self._flush()
+            # one step-lock section: no step can launch between completing the one in flight and
+            # parking the requests
             with self._step_lock, self._lock:
+                self._flush()
                 self.paused = True
                 if mode == "abort":
                     self._abort_all("abort")

@@ -102,7 +102,7 @@ def test_suspend_keeps_one_submission_and_tags_versions():
     """Weight-sync pause in suspend mode: the request is parked (no abort, no resubmission), then
     continues under the new version; greedy output equals an uninterrupted run."""
     cfg, m, eng = make_engine(max_num_batched_tokens=64)
-    N = 300
+    N = 900  # long enough that the pause lands mid-generation even on a loaded host
     _, _, eng_ref = make_engine(max_num_batched_tokens=64)
 
     async def reference():
@@ -133,6 +133,7 @@ def test_suspend_keeps_one_submission_and_tags_versions():
         return state, before
 
     state, before = asyncio.run(run())
+    assert before < N, "the request finished before the pause"
     assert state.stop_reason == "length" and len(state.output_tokens) == N
     assert eng.stats["aborted"] == 0 and eng.stats["suspended"] == 1
     assert state.output_versions == [0] * before + [1] * (N - before)
