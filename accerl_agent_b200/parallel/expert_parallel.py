@@ -121,58 +121,56 @@ class ExpertParallel:
         dist.all_reduce(self._flag, group=self.group)
 
     def plan(self, counts: torch.Tensor) -> Dict:
-        """Exchange the per-expert counts and derive every row's destination (both directions)."""
+        """Exchange the per-expert counts and derive every row's destination (both directions). The
+        arithmetic on the ``W x E`` count matrix runs vectorised on the host (it sits between the
+        router of a layer and its dispatch, while the GPU waits)."""
+        import numpy as np
+
         W, E = self.world, self.E
         c_local = counts.to(torch.int64).reshape(1, E)
         c_all = torch.empty(W, E, dtype=torch.int64, device=counts.device)
         dist.all_gather_into_tensor(c_all, c_local, group=self.group) if counts.is_cuda else dist.all_gather(
             list(c_all.chunk(W)), c_local, group=self.group)
-        C = c_all.cpu().tolist()
-        # owner-side padded layout of every rank (needed by sources to address rows)
-        seg_rows = [[sum(C[s][self.lo_of[d] + el] for s in range(W)) for el in range(self.nloc[d])] for d in range(W)]
-        seg_pad = [[((r + SEG - 1) // SEG) * SEG for r in rows] for rows in seg_rows]
-        seg_start = []
+        C = c_all.cpu().numpy()
+        # owner-side padded layout of every expert: rows from all sources, padded to whole tiles,
+        # segments back to back inside each owner's range
+        col = C.sum(0)
+        pad = (col + SEG - 1) // SEG * SEG
+        start = np.zeros(E, dtype=np.int64)
+        owner_rows = np.zeros(W, dtype=np.int64)
         for d in range(W):
-            st, acc = [], 0
-            for pdd in seg_pad[d]:
-                st.append(acc)
-                acc += pdd
-            seg_start.append(st)
+            lo, n = self.lo_of[d], self.nloc[d]
+            cs = np.cumsum(pad[lo : lo + n])
+            start[lo : lo + n] = cs - pad[lo : lo + n]
+            owner_rows[d] = cs[-1] if n else 0
         if self.p2p:
             # every rank sees the same C, so an overflow raises on all ranks before any row moves
-            if max(sum(row) for row in C) > self.cap_comb:
-                raise RuntimeError(f"expert-parallel batch of {max(sum(r) for r in C) // self.k} tokens exceeds "
+            if int(C.sum(1).max()) > self.cap_comb:
+                raise RuntimeError(f"expert-parallel batch of {int(C.sum(1).max()) // self.k} tokens exceeds "
                                    f"max_tokens={self.max_tokens}")
-            if max(sum(pads) for pads in seg_pad) > self.cap_recv:
+            if int(owner_rows.max()) > self.cap_recv:
                 raise RuntimeError("expert-parallel receive buffer overflow")
-        # source side: destination row of the first row of each expert segment of this rank
         me = self.rank
-        base = []
-        for e in range(E):
-            d = self.owner[e]
-            el = e - self.lo_of[d]
-            base.append(seg_start[d][el] + sum(C[s][e] for s in range(me)))
-        # owner side: for each block (local expert, source) its rows and the source's slot
-        blk_row, blk_len, blk_src, blk_slot = [], [], [], []
-        for el in range(self.E_loc):
-            e = self.lo + el
-            r = seg_start[me][el]
-            for s in range(W):
-                n = C[s][e]
-                if n:
-                    blk_row.append(r)
-                    blk_len.append(n)
-                    blk_src.append(s)
-                    blk_slot.append(sum(C[s][:e]))
-                r += n
-        pads = seg_pad[me]
+        # source side: destination row of the first row of each expert segment of this rank
+        base = start + C[:me].sum(0)
+        # owner side: one block per (local expert, source) with rows, in expert-major then source order
+        sl = slice(self.lo, self.lo + self.E_loc)
+        sub = C[:, sl].T  # [E_loc, W]
+        row0 = start[sl][:, None] + np.cumsum(sub, axis=1) - sub
+        slot0 = (np.cumsum(C, axis=1) - C)[:, sl].T  # rows of source s before expert e in its sorted order
+        src = np.broadcast_to(np.arange(W), sub.shape)
+        keep = sub.reshape(-1) > 0
+        blk_row = row0.reshape(-1)[keep].tolist()
+        blk_len = sub.reshape(-1)[keep].tolist()
+        blk_src = src.reshape(-1)[keep].tolist()
+        blk_slot = slot0.reshape(-1)[keep].tolist()
+        pads = pad[sl].tolist()
         lay = moe_mod.padded_layout_from_pads(pads, self.device)
-        plan = {"C": C, "base": base, "lay": lay, "blocks": (blk_row, blk_len, blk_src, blk_slot),
-                "n_send": sum(C[me]), "R": lay["total"]}
+        plan = {"C": C, "base": base.tolist(), "lay": lay, "blocks": (blk_row, blk_len, blk_src, blk_slot),
+                "n_send": int(C[me].sum()), "R": lay["total"]}
         if self.transport == "all_to_all":
-            own = lambda d: range(self.lo_of[d], self.lo_of[d] + self.nloc[d])  # noqa: E731
-            plan["send_splits"] = [sum(C[me][e] for e in own(d)) for d in range(W)]
-            plan["recv_splits"] = [sum(C[s][e] for e in own(me)) for s in range(W)]
+            plan["send_splits"] = [int(C[me, self.lo_of[d] : self.lo_of[d] + self.nloc[d]].sum()) for d in range(W)]
+            plan["recv_splits"] = [int(C[s, sl].sum()) for s in range(W)]
             # all_to_all delivers source-major blocks; their rows in the expert-major padded layout
             order = sorted(range(len(blk_len)), key=lambda b: (blk_src[b], blk_row[b]))
             plan["recv_idx"] = self._expand([blk_row[b] for b in order], [blk_len[b] for b in order])

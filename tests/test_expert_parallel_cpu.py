@@ -189,3 +189,57 @@ def test_expert_partitioned_storage_matches_full_model():
             if n.endswith("experts.gate_up_proj") or n.endswith("experts.down_proj"):
                 want = want[lo : lo + nloc]
             assert torch.allclose(torch.from_numpy(w), want, atol=1e-6, rtol=1e-5), n
+
+
+def _plan_reference(C, nloc, lo_of, me, seg):
+    """Loop form of the expert-parallel plan arithmetic (owner layout, source bases, owner blocks)."""
+    W, E = len(C), len(C[0])
+    seg_rows = [[sum(C[s][lo_of[d] + el] for s in range(W)) for el in range(nloc[d])] for d in range(W)]
+    seg_pad = [[(r + seg - 1) // seg * seg for r in rows] for rows in seg_rows]
+    seg_start = []
+    for d in range(W):
+        st, acc = [], 0
+        for p in seg_pad[d]:
+            st.append(acc)
+            acc += p
+        seg_start.append(st)
+    owner = [d for d in range(W) for _ in range(nloc[d])]
+    base = [seg_start[owner[e]][e - lo_of[owner[e]]] + sum(C[s][e] for s in range(me)) for e in range(E)]
+    blocks = ([], [], [], [])
+    for el in range(nloc[me]):
+        e = lo_of[me] + el
+        r = seg_start[me][el]
+        for s in range(W):
+            n = C[s][e]
+            if n:
+                for lst, v in zip(blocks, (r, n, s, sum(C[s][:e]))):
+                    lst.append(v)
+            r += n
+    return base, blocks, seg_pad[me]
+
+
+def test_vectorised_plan_matches_the_loop_form(monkeypatch):
+    """The vectorised plan gives the loop form's destination rows, owner blocks and padded layout for
+    uneven expert partitions and empty experts."""
+    import random
+
+    import torch.distributed as dist
+
+    from accerl_agent_b200.parallel.expert_parallel import SEG, ExpertParallel, expert_ranges
+
+    rnd = random.Random(1)
+    for W, E in ((2, 6), (8, 60), (3, 10), (4, 128)):
+        C = [[rnd.choice([0, 0, rnd.randint(1, 300)]) for _ in range(E)] for _ in range(W)]
+        monkeypatch.setattr(dist, "all_gather",
+                            lambda lst, t, group=None: [x.copy_(torch.tensor([C[i]])) for i, x in enumerate(lst)])
+        for me in range(W):
+            ep = ExpertParallel.__new__(ExpertParallel)
+            ep.world, ep.rank, ep.E, ep.k, ep.group = W, me, E, 4, None
+            ep.nloc, ep.lo_of = expert_ranges(E, W)
+            ep.E_loc, ep.lo = ep.nloc[me], ep.lo_of[me]
+            ep.device, ep.transport, ep.p2p = torch.device("cpu"), "emulated", False
+            plan = ep.plan(torch.tensor(C[me]))
+            base, blocks, pads = _plan_reference(C, ep.nloc, ep.lo_of, me, SEG)
+            assert plan["base"] == base
+            assert tuple(plan["blocks"]) == blocks
+            assert plan["lay"]["rows"].tolist() == pads and plan["n_send"] == sum(C[me])
