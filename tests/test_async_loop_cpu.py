@@ -11,9 +11,12 @@ from accerl_agent_b200.agent_textworld import main
 from accerl_agent_b200.runtime.actors import ActorDied, ActorError, get, spawn_actor
 
 
-def test_async_loop_end_to_end_cpu(tmp_path):
+@pytest.mark.parametrize("shard_params", [False, True])
+def test_async_loop_end_to_end_cpu(tmp_path, shard_params):
+    """With ``--shard-params`` the engine pulls every weight from the trainer rank that stores it; the
+    small old/new KL shows that it samples with the trainers' weights either way."""
     log = tmp_path / "run"
-    main([
+    main(["--shard-params"] * shard_params + [
         "--model-path", "tiny-qwen2", "--env", "synthetic", "--device", "cpu", "--fsdp-world-size", "2",
         "--infer-size", "1", "--num-rollout-workers", "2", "--rollout-batch-size", "2",
         "--tw-max-episode-steps", "4", "--tw-history-token-window", "256", "--max-length", "256",
@@ -35,7 +38,8 @@ def test_async_loop_end_to_end_cpu(tmp_path):
     ck = log / "checkpoints" / "latest"
     state = json.load(open(ck / "trainer_state.json"))
     assert state["optimizer_step"] == 2 and state["fsdp_world_size"] == 2
-    assert (ck / "model.safetensors").exists() and (ck / "config.json").exists()
+    assert (ck / "config.json").exists()
+    assert (ck / "model.safetensors.index.json").exists() if shard_params else (ck / "model.safetensors").exists()
 
 
 class Flaky:
