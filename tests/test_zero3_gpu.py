@@ -58,6 +58,7 @@ def _worker(rank, port, sharded, q):
             m.init_weights(seed=0)
             opt = ShardedAdamW(m, lr=1e-3, weight_decay=0.01)
             stored = m.params.numel()
+        grads = {}
         for step in range(3):
             packs = [_batch(100 * step + 10 * rank + i, dev) for i in range(2)]
             total = 4 * 80
@@ -67,6 +68,19 @@ def _worker(rank, port, sharded, q):
                 adv = b["sample_advantages"][b["sequence_ids"][tgt]]
                 dlp, _ = ops.policy_loss(lp, b["old_logprobs"][tgt], adv, ObjectiveConfig(), loss_scale=1.0 / total)
                 m.backward_from_logprobs(dlp, ctx)
+            if step == 0:  # the gradient summed over ranks and packs, before the optimizer consumes it
+                if sharded:
+                    for u in sp.units:
+                        full = torch.empty(u.numel, dtype=torch.float32, device=dev)
+                        dist.all_gather_into_tensor(full, sp.local_grads[u.base : u.base + u.shard].contiguous())
+                        for n in u.names:
+                            sl = sp.layout.slots[n]
+                            grads[n] = full[sl.offset - u.lo : sl.offset - u.lo + sl.numel].cpu()
+                else:
+                    g = m.grads.clone()
+                    dist.all_reduce(g)
+                    for n, sl in m.layout.slots.items():
+                        grads[n] = g[sl.grad_offset : sl.grad_offset + sl.numel].cpu()
             opt.step(1e-3)
         torch.cuda.synchronize()
         full = {}
@@ -75,7 +89,7 @@ def _worker(rank, port, sharded, q):
         else:
             full = {n: v.float().cpu() for n, v in m.named_parameters()}
         ops.check_status(dev)
-        q.put((rank, (stored, {n: v.numpy() for n, v in full.items()})))
+        q.put((rank, (stored, {n: v.numpy() for n, v in full.items()}, {n: v.numpy() for n, v in grads.items()})))
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as exc:
@@ -109,10 +123,24 @@ def test_layer_sharded_training_matches_replicated_on_two_gpus():
     sh = _run(True)
     for r in (0, 1):
         assert sh[r][0] < 0.6 * rep[r][0]
+        # the reduced gradient of the first window: the same sums in another order (fp32)
+        for n, g in rep[r][2].items():
+            a, b = torch.from_numpy(sh[r][2][n]), torch.from_numpy(g)
+            assert (a - b).norm().item() <= 1e-4 * b.norm().item() + 1e-9, n
+        # weights after three AdamW steps (lr 1e-3): Adam normalises each element's update, so an
+        # element whose gradient is rounding noise steps in a direction set by that noise. The key
+        # bias is such a parameter: adding a constant to every key of a head leaves the softmax
+        # unchanged, so its gradient is zero up to rounding; it is left out. Everything else agrees
+        # to bf16 rounding, with at most a few elements a step or two apart.
+        cfg = _cfg()
         for n, w in rep[r][1].items():
             a, b = torch.from_numpy(sh[r][1][n]), torch.from_numpy(w)
-            # bf16 weights; gradient sums in a different order may round one step apart
-            assert torch.allclose(a, b, atol=2e-3, rtol=2e-2), n
-            assert (a - b).abs().max().item() <= 4e-3, n
+            if n.endswith("qkv_proj.bias"):
+                keep = torch.ones_like(b, dtype=torch.bool)
+                keep[cfg.q_dim : cfg.q_dim + cfg.kv_dim] = False
+                a, b = a[keep], b[keep]
+            d = (a - b).abs()
+            assert d.max().item() <= 7e-3, n
+            assert (d > 2e-3 + 2e-2 * b.abs()).float().mean().item() <= 0.01, n
     for n in sh[0][1]:
         assert (sh[0][1][n] == sh[1][1][n]).all(), n
