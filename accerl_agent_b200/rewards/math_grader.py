@@ -4,17 +4,23 @@ Same contract as the reference's grader entry point (``scripts/drgrpo_grader.py:
 response earns ``format_reward`` 1 when it contains ``"</think> <answer>"`` and ``"</answer>"``; the
 text after the last ``<answer>`` (``\\boxed{...}`` content when present) is graded against the ground
 truth (a string, a number or a list of accepted answers); ``reward = answer_reward`` and a
-well-formatted wrong answer gets no reward (no reward for format alone).
+well-formatted wrong answer gets no reward (no reward for format alone). ``question_only_reward_fn``
+grades the last ``\\boxed{}`` of a free-form response (``drgrpo_grader.py:1050-1080``).
 
-Equivalence is decided here, in order:
-  1. normalised strings are equal (LaTeX wrappers, units words, ``$``, thousands separators,
-     trailing periods and spacing removed; ``\\frac{a}{b}`` -> ``a/b``);
-  2. both sides parse as numbers (integers, decimals, fractions, percentages, scientific notation)
-     and agree to a relative tolerance of 1e-4 (percent answers also match their fraction);
-  3. with ``fast=False``: the LaTeX is rewritten into sympy syntax (nested fractions, roots, powers,
-     constants, mixed numbers) and compared symbolically, then numerically; ``\\pm`` answers and
-     ``\\{...\\}`` sets compare as unordered lists, tuples in order, intervals with their brackets.
-``math_verify`` (when installed) is consulted last in slow mode, like the reference's fallback chain.
+Equivalence follows the reference's decision rules (``grade``: normalised match or symbolic match,
+``drgrpo_grader.py:936-1005``), implemented here:
+  1. normalised strings are equal (LaTeX wrappers, unit words, ``$``, ``%``, thousands separators,
+     trailing periods, spacing and a short ``x =`` prefix removed; ``\\frac{a}{b}`` -> ``a/b``;
+     ``million`` / ``billion`` / ``trillion`` as powers of ten);
+  2. otherwise, element by element (a bracketed tuple or interval splits at its commas, and both
+     sides must use the same brackets): two fractions of integers must be written identically (an
+     unreduced fraction is not accepted for a reduced one), an integer answer needs an integer, and
+     everything else must be exactly equal as a number or, for expressions that are safe to evaluate
+     (at most two unknown letters, no braced or multi-digit exponents), under sympy simplification;
+  3. with ``fast=False`` also: the LaTeX is rewritten into sympy syntax (nested fractions, roots,
+     powers, constants, mixed numbers) and compared symbolically, then numerically; ``\\pm`` answers
+     and ``\\{...\\}`` sets compare as unordered lists, tuples in order, intervals with their
+     brackets; ``math_verify`` (when installed) is consulted last, like the reference's fallback.
 """
 
 from __future__ import annotations
@@ -71,26 +77,36 @@ def _strip_wrappers(s: str) -> str:
 
 
 def _frac_to_slash(s: str) -> str:
-    pat = re.compile(r"\\[dt]?frac\s*\{([^{}]*)\}\s*\{([^{}]*)\}")
-    while True:
-        t = pat.sub(lambda m: f"({m.group(1)})/({m.group(2)})", s)
-        if t == s:
-            break
-        s = t
-    # \frac12 shorthand
-    s = re.sub(r"\\[dt]?frac(\d)(\d)", r"(\1)/(\2)", s)
-    return s
+    """``\\frac{a}{b}`` (and ``\\dfrac`` / ``\\tfrac``, nested, or the ``\\frac12`` shorthand) ->
+    ``(a)/(b)``, arguments matched by balanced braces."""
+    out, i = [], 0
+    while i < len(s):
+        m = re.match(r"\\[dt]?frac", s[i:])
+        if not m:
+            out.append(s[i])
+            i += 1
+            continue
+        num, j = _arg(s, i + len(m.group(0)))
+        den, j = _arg(s, j)
+        out.append(f"({_frac_to_slash(num)})/({_frac_to_slash(den)})")
+        i = j
+    return "".join(out)
 
 
 def normalize_answer(ans: str) -> str:
     s = str(ans).strip()
     s = s.replace("\n", " ")
     s = _strip_wrappers(s)
+    s = s.replace("\\%", "%").replace("\\$", "").replace("%", "")
     for tok in ("\\left", "\\right", "\\!", "\\,", "\\;", "\\:", "\\ ", "$", "\\displaystyle"):
         s = s.replace(tok, "")
     s = s.replace("^\\circ", "").replace("^{\\circ}", "").replace("\\circ", "")
-    s = s.replace("\\%", "%").replace("\\$", "")
+    s = re.sub(r"\s*\b(million|billion|trillion)\b", lambda m: {"million": "*10^6", "billion": "*10^9",
+                                                                 "trillion": "*10^12"}[m.group(1)], s)
+    s = re.sub(r"\s+(or|and)\s+", ",", s)
     s = _frac_to_slash(s)
+    for word in ("sqrt", "pi", "infty"):
+        s = s.replace("\\" + word, word)
     s = s.replace("\\cdot", "*").replace("\\times", "*").replace("\\div", "/")
     s = s.replace("{", "(").replace("}", ")")
     low = s.lower().strip()
@@ -102,8 +118,11 @@ def normalize_answer(ans: str) -> str:
     low = re.sub(r"(?<=\d),(?=\d{3}\b)", "", low)  # thousands separators
     low = low.replace(" ", "")
     low = low.rstrip(".")
-    if low.startswith("(") and low.endswith(")") and low.count("(") == 1:
+    if low.startswith("(") and low.endswith(")") and low.count("(") == 1 and "," not in low:
         low = low[1:-1]
+    low = re.sub(r"(?<![a-z])\((-?\d+(?:\.\d+)?)\)", r"\1", low)  # "(1)/(2)" -> "1/2", not "sqrt(3)"
+    if re.fullmatch(r"-?\d+\.0*", low):  # "5.0" -> "5"
+        low = low.split(".")[0]
     return low
 
 
@@ -128,22 +147,85 @@ def _to_number(s: str) -> Optional[float]:
     return val / 100.0 if pct else val
 
 
-def _close(a: float, b: float) -> bool:
-    return abs(a - b) <= 1e-4 * max(1.0, abs(a), abs(b))
+_INT_FRAC = re.compile(r"^-?\d+/0*[1-9]\d*$")
 
 
-def _numbers_equal(pred: str, gt: str) -> bool:
-    a, b = _to_number(pred), _to_number(gt)
-    if a is None or b is None:
+def _exact_number(s: str):
+    """The exact rational value of a decimal or a fraction of decimals, else None."""
+    from fractions import Fraction
+
+    s = s.replace("(", "").replace(")", "")
+    try:
+        if _NUM.match(s):
+            return Fraction(s)
+        if s.count("/") == 1:
+            a, b = s.split("/")
+            if _NUM.match(a) and _NUM.match(b) and float(b) != 0.0:
+                return Fraction(a) / Fraction(b)
+    except (ValueError, ZeroDivisionError):
+        return None
+    return None
+
+
+def _is_integer_text(s: str) -> bool:
+    v = _exact_number(s)
+    return v is not None and v.denominator == 1
+
+
+def _tuple_elements(s: str):
+    """Elements of a bracketed tuple or interval written without nested brackets, else [s]."""
+    if len(s) > 2 and s[0] in "([" and s[-1] in ")]" and not any(c in s[1:-1] for c in "()[]"):
+        return [e.strip() for e in s[1:-1].split(",")]
+    return [s]
+
+
+def _safe_to_evaluate(expr: str) -> bool:
+    """Expressions sympy may simplify without hanging: at most two unknown letters, no braced or
+    parenthesised exponents, no exponent of two or more digits and no power towers."""
+    body = expr
+    for word in ("sqrt", "frac", "pi"):
+        body = body.replace(word, "")
+    if len({c for c in body if c.isalpha()}) > 2 or len(expr) > 200:
         return False
-    if _close(a, b):
-        return True
-    # "25%" vs "25" and "0.25" vs "25%" are both accepted
-    if pred.endswith("%") and _close(a * 100.0, b):
-        return True
-    if gt.endswith("%") and _close(a, b * 100.0):
-        return True
-    return False
+    if "^{" in expr or "^(" in expr or "**(" in expr:
+        return False
+    return re.search(r"\^\d+\^", expr) is None and re.search(r"\^\d\d+", expr) is None
+
+
+def _symbolic_zero(a: str, b: str) -> bool:
+    try:
+        import sympy
+        from sympy.parsing.sympy_parser import (convert_xor, implicit_multiplication_application, parse_expr,
+                                                standard_transformations)
+    except Exception:
+        return False
+    tr = standard_transformations + (implicit_multiplication_application, convert_xor)
+    try:
+        return sympy.simplify(parse_expr(f"({a})-({b})", transformations=tr)) == 0
+    except Exception:
+        return False
+
+
+def _element_equal(pred: str, gt: str) -> bool:
+    if _INT_FRAC.match(pred) and _INT_FRAC.match(gt):
+        return pred == gt  # an unreduced fraction does not match the reduced one
+    if _is_integer_text(pred) != _is_integer_text(gt):
+        return False  # an integer answer needs an integer
+    a, b = _exact_number(pred), _exact_number(gt)
+    if a is not None and b is not None:
+        return a == b
+    expr = f"({gt})-({pred})"
+    return _safe_to_evaluate(expr) and _symbolic_zero(gt, pred)
+
+
+def _normalised_equal(pred: str, gt: str) -> bool:
+    """Rule 2 of the module docstring on normalised strings."""
+    ge, pe = _tuple_elements(gt), _tuple_elements(pred)
+    if len(ge) > 1 and (gt[0] != pred[0] or gt[-1] != pred[-1]):
+        return False
+    if len(ge) != len(pe):
+        return False
+    return all(_element_equal(p, g) for p, g in zip(pe, ge))
 
 
 def _braced(s: str, i: int):
@@ -353,7 +435,7 @@ def grade_answer(pred: str, gt: str, fast: bool = True) -> bool:
     p, g = normalize_answer(pred), normalize_answer(gt)
     if not p:
         return False
-    if p == g or _numbers_equal(p, g):
+    if p == g or _normalised_equal(p, g):
         return True
     if fast:
         return False
@@ -377,3 +459,56 @@ def r1_zero_reward_fn(response: str, ground_truth: Union[str, int, float, Iterab
         gts = [str(g) for g in ground_truth]
     ok = any(grade_answer(answer, g, fast) for g in gts)
     return {"format_reward": 1.0, "answer_reward": 1.0 if ok else 0.0, "reward": 1.0 if ok else 0.0}
+
+
+def question_only_reward_fn(response: str, ground_truth: Union[str, int, float, Iterable],
+                            fast: bool = True) -> Dict[str, float]:
+    """Reward of a free-form response: its last ``\\boxed{}`` graded against the ground truth (no
+    ``<answer>`` tags needed); nothing boxed earns nothing, a boxed wrong answer earns the format
+    reward only."""
+    answer = extract_boxed(response)
+    if answer is None:
+        return {"format_reward": 0.0, "answer_reward": 0.0, "reward": 0.0}
+    if isinstance(ground_truth, (int, float)):
+        gts = [str(ground_truth)]
+    elif isinstance(ground_truth, str):
+        gts = [ground_truth]
+    else:
+        gts = [str(g) for g in ground_truth]
+    ok = any(grade_answer(answer, g, fast) for g in gts)
+    return {"format_reward": 1.0, "answer_reward": 1.0 if ok else 0.0, "reward": 1.0 if ok else 0.0}
+
+
+def repeatness(text: str, threshold: float = 0.2) -> bool:
+    """Whether ``text`` repeats itself: the summed longest-common-prefix lengths of its adjacent sorted
+    suffixes, as a fraction of the ``n (n + 1) / 2`` characters of all its suffixes, exceed
+    ``threshold`` (the reference's degenerate-output check, ``drgrpo_grader.py:452-492``).
+    Suffixes are sorted by prefix doubling; the LCPs come from Kasai's algorithm."""
+    n = len(text)
+    if n <= 1:
+        return False
+    rank = [ord(c) for c in text]
+    sa = list(range(n))
+    k = 1
+    while True:
+        key = lambda i: (rank[i], rank[i + k] if i + k < n else -1)  # noqa: E731
+        sa.sort(key=key)
+        new = [0] * n
+        for j in range(1, n):
+            new[sa[j]] = new[sa[j - 1]] + (key(sa[j]) != key(sa[j - 1]))
+        rank = new
+        if rank[sa[-1]] == n - 1 or k >= n:
+            break
+        k <<= 1
+    lcp_sum, h = 0, 0
+    for i in range(n):  # Kasai: h drops by at most one from suffix i to suffix i + 1
+        if rank[i] == n - 1:
+            h = 0
+            continue
+        j = sa[rank[i] + 1]
+        while i + h < n and j + h < n and text[i + h] == text[j + h]:
+            h += 1
+        lcp_sum += h
+        if h:
+            h -= 1
+    return lcp_sum * 2 / (n * (n + 1)) > threshold

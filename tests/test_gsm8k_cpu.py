@@ -33,10 +33,9 @@ def test_r1_zero_reward(response, gt, expected):
 
 
 def test_grader_equivalences():
-    assert grade_answer("50%", "0.5") and grade_answer("0.5", "50%")
     assert grade_answer("x = 12", "12")
     assert not grade_answer("12", "13")
-    assert grade_answer("2x+1", "1+2*x", fast=False) and not grade_answer("2x+1", "1+2*x", fast=True)
+    assert grade_answer("2x+1", "1+2*x", fast=True)  # symbolic match is part of the fast path
     assert extract_boxed("so \\boxed{a{b}c} done") == "a{b}c"
     assert r1_zero_reward_fn("x </think> <answer>5</answer>", ["4", "5"])["reward"] == 1.0
     assert extract_gsm8k_final_answer("steps...\n#### 1,250") == "1250"
@@ -116,6 +115,41 @@ def test_gsm8k_loop_end_to_end_cpu(tmp_path):
     for r in steps:
         assert "Rollout/GlobalRewardSumMean" in r and "Rollout/AbortRate" in r
     assert steps[0]["Infer/TokensPerSec"] > 0
+
+
+@pytest.mark.parametrize("pred,gt,want", [
+    ("50%", "50", True),             # the percent sign is dropped, not converted
+    ("50%", "0.5", False),
+    ("2/4", "1/2", False),           # an unreduced fraction does not match the reduced one
+    (r"\frac{1}{2}", "0.5", True),
+    ("5.0", "5", True),
+    ("5.5", "5", False),             # an integer answer needs an integer
+    ("0.333", "1/3", False),         # exact, no tolerance
+    ("(1, 2)", "(1,2)", True),
+    ("(1.0, 2)", "(1,2)", True),
+    ("(1,2)", "[1,2]", False),       # a tuple's brackets must match
+    ("(1,2)", "(2,1)", False),
+    (r"\$1,250", "1250", True),
+    (r"10\text{ cm}", "10", True),
+    (r"\frac12", "1/2", True),
+    (r"\frac{\sqrt{3}}{2}", r"\sqrt{3}/2", True),
+    ("x^{100}+1", "1+x^{100}", False),  # braced exponents are not evaluated
+])
+def test_grader_fast_rules(pred, gt, want):
+    """The fast path's decision rules (normalised match, then element-wise exact / symbolic match with
+    the reference's fraction, integer, bracket and evaluation guards)."""
+    assert grade_answer(pred, gt, fast=True) is want
+
+
+def test_question_only_reward_and_repeatness():
+    from accerl_agent_b200.rewards.math_grader import question_only_reward_fn, repeatness
+
+    assert question_only_reward_fn("so it is \\boxed{7}.", 7)["reward"] == 1.0
+    assert question_only_reward_fn("so it is \\boxed{8}.", 7) == {"format_reward": 1.0, "answer_reward": 0.0,
+                                                                  "reward": 0.0}
+    assert question_only_reward_fn("7", 7)["format_reward"] == 0.0
+    assert repeatness("abc" * 40) and not repeatness("the quick brown fox jumps over the lazy dog")
+    assert not repeatness("a")
 
 
 @pytest.mark.parametrize("pred,gt,want", [
