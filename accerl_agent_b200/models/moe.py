@@ -253,6 +253,8 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
         probs, topw, topi = route(model, layer, h, shared_gate=shared_gate)
         return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi,
                                    sg=shared_gate[0].view(-1, 1) if shared_gate else None)
+    if ep is not None:
+        return _moe_forward_ep(model, layer, h, residual, save, ep)
     probs, topw, topi = route(model, layer, h)
     w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
@@ -306,6 +308,44 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
             cache["ep_state"] = ep_state  # type: ignore[assignment]
         if lay is not None:
             cache["layout"] = lay  # type: ignore[assignment]
+    return out, cache
+
+
+def _moe_forward_ep(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save: bool, ep):
+    """Expert-parallel forward with one host synchronisation per layer, hidden behind GPU work.
+
+    The router kernel gives the per-expert counts on the device; their all-gather and the copy of the
+    ``W x E`` count matrix to pinned host memory are queued first, then the sort of the pairs and the
+    shared expert. The host waits only for the copy, so it computes the dispatch plan while the GPU
+    runs the shared expert; the exchange, the expert GEMMs and the combine follow."""
+    import numpy as np
+
+    cfg = model.cfg
+    k = cfg.num_experts_per_tok
+    shared_gate: list = []
+    probs, topw, topi, counts = route(model, layer, h, counts=True, shared_gate=shared_gate)
+    pending = ep.exchange_counts(counts)
+    flat = topi.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    e_sorted = flat.index_select(0, order)
+    tok = torch.div(order, k, rounding_mode="floor")
+    cache: Dict[str, torch.Tensor] = {}
+    sy, sg = _shared_expert(model, layer, h, cache if save else None,
+                            shared_gate[0].view(-1, 1) if shared_gate else None)
+    C = ep.wait_counts(pending)
+    bounds = [0] + np.cumsum(C[ep.rank]).tolist()
+    ys, ep_state = ep.forward(model, layer, h, tok, e_sorted, counts, bounds, C=C)
+    n_pairs = topi.numel()
+    pos_pairs = torch.empty(n_pairs, dtype=torch.long, device=h.device)
+    pos_pairs[order] = torch.arange(n_pairs, device=h.device)
+    w_pairs = torch.empty(n_pairs, dtype=torch.float32, device=h.device)
+    w_pairs[order] = topw.to(h.dtype).reshape(-1).float().index_select(0, order)
+    out = ops.moe_combine(ys, pos_pairs, w_pairs, k, residual=residual, shared=sy, sg=sg)
+    if save:
+        cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=None, gu=None, act=None, ys=ys,
+                     pos_pairs=pos_pairs, w_pairs=w_pairs)
+        cache["bounds"] = torch.tensor(bounds)
+        cache["ep_state"] = ep_state  # type: ignore[assignment]
     return out, cache
 
 

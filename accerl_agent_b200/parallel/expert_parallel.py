@@ -120,18 +120,39 @@ class ExpertParallel:
     def _barrier(self) -> None:
         dist.all_reduce(self._flag, group=self.group)
 
-    def plan(self, counts: torch.Tensor) -> Dict:
-        """Exchange the per-expert counts and derive every row's destination (both directions). The
-        arithmetic on the ``W x E`` count matrix runs vectorised on the host (it sits between the
-        router of a layer and its dispatch, while the GPU waits)."""
-        import numpy as np
-
+    def exchange_counts(self, counts: torch.Tensor):
+        """Queue the all-gather of every rank's per-expert counts and, on the GPU, their copy into
+        pinned host memory; ``wait_counts`` returns the ``W x E`` matrix. Work queued in between runs
+        while the host waits."""
         W, E = self.world, self.E
         c_local = counts.to(torch.int64).reshape(1, E)
         c_all = torch.empty(W, E, dtype=torch.int64, device=counts.device)
-        dist.all_gather_into_tensor(c_all, c_local, group=self.group) if counts.is_cuda else dist.all_gather(
-            list(c_all.chunk(W)), c_local, group=self.group)
-        C = c_all.cpu().numpy()
+        if not counts.is_cuda:
+            dist.all_gather(list(c_all.chunk(W)), c_local, group=self.group)
+            return c_all, None
+        dist.all_gather_into_tensor(c_all, c_local, group=self.group)
+        if getattr(self, "_pinned", None) is None:
+            self._pinned = torch.empty(W, E, dtype=torch.int64, pin_memory=True)
+        self._pinned.copy_(c_all, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return self._pinned, ev
+
+    @staticmethod
+    def wait_counts(pending):
+        host, ev = pending
+        if ev is not None:
+            ev.synchronize()
+        return host.numpy().copy()
+
+    def plan(self, counts: torch.Tensor, C=None) -> Dict:
+        """Derive every row's destination (both directions) from the ``W x E`` count matrix ``C``
+        (exchanged here when not given). The arithmetic runs vectorised on the host."""
+        import numpy as np
+
+        W, E = self.world, self.E
+        if C is None:
+            C = self.wait_counts(self.exchange_counts(counts))
         # owner-side padded layout of every expert: rows from all sources, padded to whole tiles,
         # segments back to back inside each owner's range
         col = C.sum(0)
@@ -289,10 +310,11 @@ class ExpertParallel:
         return Wgu, Wd, (None if gWgu is None else gWgu[sl]), (None if gWd is None else gWd[sl])
 
     def forward(self, model, layer: int, h: torch.Tensor, tok: torch.Tensor, e_sorted: torch.Tensor,
-                counts: torch.Tensor, bounds: List[int]):
+                counts: torch.Tensor, bounds: List[int], C=None):
         """Dispatch ``h[tok]`` (sorted by expert), run the local experts, combine. Returns the
-        unweighted expert outputs in this rank's sorted order plus the state backward needs."""
-        plan = self.plan(counts)
+        unweighted expert outputs in this rank's sorted order plus the state backward needs. ``C``:
+        the exchanged count matrix, when the caller already has it."""
+        plan = self.plan(counts, C)
         self._source_maps(plan, e_sorted, bounds)
         self._owner_maps(plan)
         xs_loc = self._send_to_owners(h, tok, plan)
