@@ -36,14 +36,14 @@ def _full_params(w):
     return out
 
 
-def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False):
+def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False, world=2):
     from accerl_agent_b200.core.config import make_args
     from accerl_agent_b200.replay import ReplayBuffer
     from accerl_agent_b200.trainer.worker import TrainWorker
 
     try:
         os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
-        dist.init_process_group("gloo", rank=rank, world_size=2)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
         args = make_args(model_path=model_path, train_packing="varlen", train_token_budget=64, max_length=64,
                          tw_history_token_window=64, batch_size=1, grad_accum_steps=2, device="cpu",
                          shard_params=sharded, min_replay_size_per_rank=1, replay_sample_timeout_seconds=5.0,
@@ -56,7 +56,7 @@ def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False):
             ids = torch.randint(3, 4096, (L,), generator=g).tolist()
             rb.add_samples([RLSample("grpo", ids, [1] * L, [-100] * 12 + ids[12:], [-6.0] * L, 0.5 - rank + 0.3 * i,
                                      [0.0] * L, [-1] * 12 + [0] * (L - 12), [0])])
-        w = TrainWorker(args, rank=rank, fsdp_world_size=2, replay_buffer=rb, device=torch.device("cpu"))
+        w = TrainWorker(args, rank=rank, fsdp_world_size=world, replay_buffer=rb, device=torch.device("cpu"))
         n_local = int(w.flat_weights("all").numel())
         w.train_until_next_sync(2)
         params = _full_params(w)
@@ -71,16 +71,16 @@ def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False):
         raise
 
 
-def _run(model_path, sharded, ckpt=None, checkpointing=False):
+def _run(model_path, sharded, ckpt=None, checkpointing=False, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, port, model_path, sharded, ckpt, q, checkpointing))
-             for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, port, model_path, sharded, ckpt, q, checkpointing, world))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         r, payload = q.get(timeout=300)
         assert not isinstance(payload, str), payload
         n_local, steps, params = payload
@@ -144,6 +144,15 @@ def test_layer_sharded_tied_embeddings_with_recomputation(tmp_path):
     assert "lm_head.weight" not in rep[0][2]
     for n, w in rep[0][2].items():
         assert torch.allclose(sh[0][2][n], w, atol=2e-5, rtol=1e-4), n
+
+
+def test_layer_sharded_three_ranks():
+    """An odd number of ranks (units padded to a multiple of 3 x 64 elements, a third per rank)."""
+    sh = _run("tiny-qwen2", True, world=3)
+    rep = _run("tiny-qwen2", False, world=3)
+    assert sh[0][0] < 0.4 * rep[0][0]
+    for n, w in rep[2][2].items():
+        assert torch.allclose(sh[2][2][n], w, atol=2e-5, rtol=1e-4), n
 
 
 def test_shard_copy_plans_assemble_the_engine_weights():
