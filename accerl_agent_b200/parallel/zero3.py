@@ -24,7 +24,9 @@ The model object binds its parameter (and gradient) views to whichever buffer ho
 moment, so the layer code is the same as with resident parameters. On CPU ranks (gloo) the
 collectives run synchronously (reduce-scatter as an all-reduce).
 
-Supported: full training (``--train-mode full``), dense and MoE models without expert parallelism.
+Supported: every ``--train-mode`` (frozen units are gathered for the forward and the backward that
+passes through them but get no gradient or optimizer state), dense and MoE models without expert
+parallelism.
 """
 
 from __future__ import annotations
@@ -49,6 +51,7 @@ class Unit:
     shard: int  # numel // world
     base: int  # start of this rank's shard in the local buffers
     layer: int  # decoder layer, -1 for the embedding and head units
+    trainable: bool = True
 
     def pinned(self) -> bool:
         return self.layer < 0
@@ -60,33 +63,41 @@ def _unit_key(name: str) -> str:
     return "embed" if name == "model.embed_tokens.weight" else "head"
 
 
-def build_units(layout: ParamLayout, world: int) -> List[Unit]:
-    """The units of ``layout`` (a full-training layout), each a contiguous range of it."""
+def build_units(layout: ParamLayout, world: int, trainable: Optional[Dict[str, bool]] = None) -> List[Unit]:
+    """The units of ``layout`` (laid out in parameter order, as ``ParamLayout.build(cfg, "full")``
+    does), each a contiguous range of it. ``trainable`` (name -> flag, default all) splits a unit
+    where the flag changes (the final norm and the LM head of the head unit under ``--train-mode
+    lm_head``); a decoder layer is trained whole or not at all. Local storage holds the trainable
+    units' shards first, so the optimizer works on one prefix."""
     slots = sorted(layout.slots.values(), key=lambda s: s.offset)
-    if any(not s.trainable for s in slots):
-        raise ValueError("layer-sharded parameters need --train-mode full")
-    groups: Dict[str, List] = {}
-    order: List[str] = []
+    flag = (lambda n: True) if trainable is None else (lambda n: bool(trainable[n]))
+    groups: List[List] = []
+    seen: set = set()
     for s in slots:
         k = _unit_key(s.name)
-        if k not in groups:
-            groups[k] = []
-            order.append(k)
-        elif order[-1] != k:
+        if groups and _unit_key(groups[-1][0].name) == k and flag(groups[-1][0].name) == flag(s.name):
+            groups[-1].append(s)
+            continue
+        if k in seen and _unit_key(groups[-1][0].name) != k:
             raise ValueError(f"parameters of unit {k} are not contiguous in the layout")
-        groups[k].append(s)
+        if k in seen and k.startswith("layer."):
+            raise ValueError(f"decoder layer {k} is partly trainable")
+        seen.add(k)
+        groups.append([s])
     q = ALIGN * max(world, 1)
     units: List[Unit] = []
-    base = 0
-    for k in order:
-        ss = groups[k]
+    for ss in groups:
+        k = _unit_key(ss[0].name)
         lo = ss[0].offset
         hi = ss[-1].offset + (ss[-1].numel + ALIGN - 1) // ALIGN * ALIGN
         numel = (hi - lo + q - 1) // q * q
-        shard = numel // max(world, 1)
-        units.append(Unit(k, [s.name for s in ss], lo, hi - lo, numel, shard, base,
-                          int(k.split(".")[1]) if k.startswith("layer.") else -1))
-        base += shard
+        name = k if sum(_unit_key(g[0].name) == k for g in groups) == 1 else f"{k}.{ss[0].name}"
+        units.append(Unit(name, [s.name for s in ss], lo, hi - lo, numel, numel // max(world, 1), 0,
+                          int(k.split(".")[1]) if k.startswith("layer.") else -1, flag(ss[0].name)))
+    base = 0
+    for u in sorted(units, key=lambda u: not u.trainable):  # stable: trainable units first
+        u.base = base
+        base += u.shard
     return units
 
 
@@ -106,16 +117,19 @@ def shard_pieces(units: List[Unit], world: int):
 class LayerShardedParams:
     """Sharded storage of one rank plus the gather / reduce-scatter schedule around the layers."""
 
-    def __init__(self, cfg, device: torch.device, dtype: torch.dtype, group=None):
+    def __init__(self, cfg, device: torch.device, dtype: torch.dtype, group=None, train_mode: str = "full"):
         self.cfg = cfg
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = device
         self.dtype = dtype
-        self.layout = ParamLayout.build(cfg, "full", pad_to=1)
-        self.units = build_units(self.layout, self.world)
+        self.layout = sharded_layout(cfg, train_mode)
+        self.units = build_units(self.layout, self.world, {n: s.trainable for n, s in self.layout.slots.items()})
         self.layer_unit = {u.layer: u for u in self.units if not u.pinned()}
+        self.n_trainable = sum(u.shard for u in self.units if u.trainable)  # the optimizer's prefix
+        if self.n_trainable == 0:
+            raise RuntimeError(f"No trainable parameters found for mode: {train_mode}")
         n_local = sum(u.shard for u in self.units)
         self.local = torch.zeros(n_local, dtype=dtype, device=device)
         self.local_grads = torch.zeros(n_local, dtype=torch.float32, device=device)
@@ -137,6 +151,8 @@ class LayerShardedParams:
         self.params_dirty = True  # shards changed since the pinned units were gathered
         self.model = CausalLM.without_buffers(cfg, self.layout)
         self.model.units = self
+        trained = [u.layer for u in self.units if u.trainable and not u.pinned()]
+        self.model.first_trainable_layer = min(trained) if trained else cfg.num_hidden_layers
 
     # ---------------------------------------------------------------- views
     def _bind(self, u: Unit, pbuf: torch.Tensor, gbuf: Optional[torch.Tensor]) -> None:
@@ -145,7 +161,7 @@ class LayerShardedParams:
             s = self.layout.slots[name]
             o = s.offset - u.lo
             m._views[name] = pbuf[o : o + s.numel].view(s.shape)
-            if gbuf is not None:
+            if gbuf is not None and u.trainable:
                 m._gviews[name] = gbuf[o : o + s.numel].view(s.shape)
 
     def shard_of(self, u: Unit) -> torch.Tensor:
@@ -227,7 +243,7 @@ class LayerShardedParams:
 
     def begin_backward(self) -> None:
         for u in self.units:
-            if u.pinned():
+            if u.pinned() and u.trainable:
                 self.pin_g[u.name].zero_()
 
     def before_backward(self, layer: int) -> None:
@@ -236,14 +252,17 @@ class LayerShardedParams:
         if self.cuda and self._rs_done[b] is not None:
             torch.cuda.current_stream(self.device).wait_event(self._rs_done[b])
         u = self.layer_unit[layer]
-        self.gbuf[b][: u.numel].zero_()
+        if u.trainable:
+            self.gbuf[b][: u.numel].zero_()
         self._bind(u, self.pbuf[b], self.gbuf[b])
-        if layer - 1 in self.layer_unit:
-            self._issue_layer_gather(layer - 1)
+        if layer - 1 in self.layer_unit and layer - 1 >= self.model.first_trainable_layer:
+            self._issue_layer_gather(layer - 1)  # the backward stops below the first trained layer
 
     def after_backward(self, layer: int) -> None:
         b = layer % 2
         u = self.layer_unit[layer]
+        if not u.trainable:
+            return
         if self.cuda:
             self.comm.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm):
@@ -261,12 +280,12 @@ class LayerShardedParams:
             self.comm.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm):
                 for u in self.units:
-                    if u.pinned():
+                    if u.pinned() and u.trainable:
                         self._reduce_scatter_add(u, self.pin_g[u.name], self.pin_tmp[u.name])
             torch.cuda.current_stream(self.device).wait_stream(self.comm)
         else:
             for u in self.units:
-                if u.pinned():
+                if u.pinned() and u.trainable:
                     self._reduce_scatter_add(u, self.pin_g[u.name], self.pin_tmp[u.name])
 
     def invalidate(self) -> None:
@@ -299,7 +318,7 @@ class LayerShardedParams:
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed)
         order = [n for u in self.units for n in u.names]
-        if order != [n for n in self.layout.order]:
+        if order != list(self.layout.order):
             raise RuntimeError("unit order differs from the parameter order")
 
         def fill(u, views):
@@ -328,13 +347,15 @@ class ShardedParamAdamW:
         self.eps = eps
         self.max_grad_norm = max_grad_norm
         self.step_count = 0
-        self.master = sharding.local.detach().float().clone()
+        self.params = sharding.local[: sharding.n_trainable]
+        self.grads = sharding.local_grads[: sharding.n_trainable]
+        self.master = self.params.detach().float().clone()
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
         self._sumsq = torch.zeros(1, dtype=torch.float64, device=sharding.device)
 
     def refresh_master_from_params(self) -> None:
-        self.master.copy_(self.sharding.local.float())
+        self.master.copy_(self.params.float())
 
     def step(self, lr: Optional[float] = None, timer=None) -> torch.Tensor:
         if lr is not None:
@@ -342,12 +363,12 @@ class ShardedParamAdamW:
         mark = timer.mark if timer is not None else (lambda name: None)
         sh = self.sharding
         self._sumsq.zero_()
-        ops.grad_sumsq(sh.local_grads, self._sumsq)
+        ops.grad_sumsq(self.grads, self._sumsq)
         if self.world > 1:
             dist.all_reduce(self._sumsq, op=dist.ReduceOp.SUM, group=self.group)
         mark("norm_allreduce")
         self.step_count += 1
-        ops.adamw_step(self.master, self.exp_avg, self.exp_avg_sq, sh.local_grads, sh.local, self._sumsq, self.lr,
+        ops.adamw_step(self.master, self.exp_avg, self.exp_avg_sq, self.grads, self.params, self._sumsq, self.lr,
                        self.betas[0], self.betas[1], self.eps, self.weight_decay, self.max_grad_norm,
                        self.step_count)  # (the kernel zeroes the gradient shard)
         sh.invalidate()
@@ -362,8 +383,18 @@ class ShardedParamAdamW:
         self.master.copy_(state["master"])
         self.exp_avg.copy_(state["exp_avg"])
         self.exp_avg_sq.copy_(state["exp_avg_sq"])
-        self.sharding.local.copy_(self.master.to(self.sharding.local.dtype))
+        self.params.copy_(self.master.to(self.params.dtype))
         self.sharding.invalidate()
+
+
+def sharded_layout(cfg, train_mode: str = "full") -> ParamLayout:
+    """The full layout in parameter order (every parameter at its ``"full"``-mode offset) with the
+    trainable flags of ``train_mode``; trainers and engines build the same units from it."""
+    layout = ParamLayout.build(cfg, "full", pad_to=1)
+    flags = ParamLayout.build(cfg, train_mode, pad_to=1).slots
+    for name, s in layout.slots.items():
+        s.trainable = flags[name].trainable
+    return layout
 
 
 def bytes_per_rank(num_params: int, world: int, sharded: bool) -> float:
@@ -374,4 +405,5 @@ def bytes_per_rank(num_params: int, world: int, sharded: bool) -> float:
     return 6.0 * num_params + 12.0 * num_params / world
 
 
-__all__ = ["Unit", "build_units", "shard_pieces", "LayerShardedParams", "ShardedParamAdamW", "bytes_per_rank"]
+__all__ = ["Unit", "build_units", "shard_pieces", "sharded_layout", "LayerShardedParams", "ShardedParamAdamW",
+           "bytes_per_rank"]

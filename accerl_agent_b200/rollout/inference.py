@@ -218,16 +218,15 @@ def _open_handle(handle, device: torch.device, opened: List[int]):
 def _attach_sharded_sources(engine: GenerationEngine, cfg, device: torch.device, handles, opened: List[int]) -> int:
     """Layer-sharded trainers (``parallel/zero3.py``): map every trainer's shard buffer and pull each
     element from the trainer that stores it."""
-    from ..models.transformer import ParamLayout
-    from ..parallel.zero3 import build_units, shard_pieces
+    from ..parallel.zero3 import build_units, shard_pieces, sharded_layout
     from .weight_map import build_weight_map_sharded
 
     world = int(handles[0]["world"])
     handles = sorted(handles, key=lambda h: int(h["trainer_rank"]))
     if [int(h["trainer_rank"]) for h in handles] != list(range(world)):
         raise ValueError("layer-sharded weight sync needs the handle of every trainer rank")
-    full = ParamLayout.build(cfg, "full", pad_to=1)
-    pieces = shard_pieces(build_units(full, world), world)
+    full = sharded_layout(cfg, handles[0].get("train_mode", "full"))
+    pieces = shard_pieces(build_units(full, world, {n: s.trainable for n, s in full.slots.items()}), world)
     srcs, total = [], 0
     for h in handles:
         tensor, addr, numel = _open_handle(h, device, opened)

@@ -75,7 +75,10 @@ class TrainerActor:
 
     def weight_numel(self, scope: str = "all") -> int:
         if self.worker.sharding is not None:
-            return int(self.worker.sharding.full_numel())
+            sh = self.worker.sharding
+            if scope == "trainable":
+                return int(sum(s.numel for s in sh.layout.slots.values() if s.trainable))
+            return int(sh.full_numel())
         return int(self.worker.flat_weights(scope).numel())
 
     def export_weights_handle(self):
@@ -90,7 +93,8 @@ class TrainerActor:
         part = {}
         if self.worker.sharding is not None:
             # layer-sharded trainers: this buffer holds this rank's shard of every unit
-            part = {"zero3": True, "trainer_rank": self.worker.rank, "world": self.worker.fsdp_world_size}
+            part = {"zero3": True, "trainer_rank": self.worker.rank, "world": self.worker.fsdp_world_size,
+                    "train_mode": self.worker.args.train_mode}
         elif mcfg.local_experts is not None and mcfg.local_experts != mcfg.num_experts:
             # expert-partitioned storage: the engine needs every rank's buffer and where its experts sit
             part = {"partition": True, "trainer_rank": self.worker.rank, "world": self.worker.fsdp_world_size}

@@ -186,12 +186,10 @@ class TrainWorker:
             # parameters, gradients and optimizer state sharded per layer (parallel/zero3.py)
             if use_ep:
                 raise ValueError("--shard-params cannot be combined with --expert-parallel")
-            if args.train_mode != "full":
-                raise ValueError("--shard-params needs --train-mode full")
             from ..models.hf_io import load_hf_checkpoint_sharded
             from ..parallel.zero3 import LayerShardedParams, ShardedParamAdamW
 
-            self.sharding = LayerShardedParams(self.cfg, self.device, self.dtype)
+            self.sharding = LayerShardedParams(self.cfg, self.device, self.dtype, train_mode=args.train_mode)
             self.model = self.sharding.model
             self.model.gradient_checkpointing = bool(args.gradient_checkpointing)
             if has_ckpt:
@@ -690,9 +688,11 @@ class TrainWorker:
         """The full bf16 compute copy in fused layout. Trainable parameters form a contiguous prefix,
         so a trainable-scope sync is a single contiguous range."""
         if self.sharding is not None:  # this rank's shards of every unit (the engine maps every rank)
-            if scope not in ("all", "trainable"):
-                raise ValueError(f"Unsupported weight scope: {scope!r}")
-            return self.sharding.local
+            if scope == "trainable":
+                return self.sharding.local[: self.sharding.n_trainable]
+            if scope == "all":
+                return self.sharding.local
+            raise ValueError(f"Unsupported weight scope: {scope!r}")
         if scope == "trainable":
             return self.model.params[: self.model.layout.trainable_numel]
         if scope == "all":

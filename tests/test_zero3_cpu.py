@@ -36,7 +36,7 @@ def _full_params(w):
     return out
 
 
-def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False, world=2):
+def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False, world=2, train_mode="full"):
     from accerl_agent_b200.core.config import make_args
     from accerl_agent_b200.replay import ReplayBuffer
     from accerl_agent_b200.trainer.worker import TrainWorker
@@ -48,7 +48,7 @@ def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False, wor
                          tw_history_token_window=64, batch_size=1, grad_accum_steps=2, device="cpu",
                          shard_params=sharded, min_replay_size_per_rank=1, replay_sample_timeout_seconds=5.0,
                          replay_wait_sleep_seconds=0.05, dtype="float32", learning_rate=1e-3, lr_warmup_steps=0,
-                         gradient_checkpointing=checkpointing)
+                         gradient_checkpointing=checkpointing, train_mode=train_mode)
         rb = ReplayBuffer(8, seed=rank)
         g = torch.Generator().manual_seed(5 + rank)
         for i in range(2):
@@ -71,11 +71,12 @@ def _worker(rank, port, model_path, sharded, ckpt, out, checkpointing=False, wor
         raise
 
 
-def _run(model_path, sharded, ckpt=None, checkpointing=False, world=2):
+def _run(model_path, sharded, ckpt=None, checkpointing=False, world=2, train_mode="full"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, port, model_path, sharded, ckpt, q, checkpointing, world))
+    procs = [ctx.Process(target=_worker, args=(r, port, model_path, sharded, ckpt, q, checkpointing, world,
+                                                 train_mode))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -153,6 +154,23 @@ def test_layer_sharded_three_ranks():
     assert sh[0][0] < 0.4 * rep[0][0]
     for n, w in rep[2][2].items():
         assert torch.allclose(sh[2][2][n], w, atol=2e-5, rtol=1e-4), n
+
+
+@pytest.mark.parametrize("train_mode", ["last_layer", "lm_head"])
+def test_layer_sharded_partial_train_modes(train_mode):
+    """Frozen units are gathered but get no gradient or optimizer state: the trained parameters move
+    exactly as with replicated parameters and the frozen ones keep their initial values."""
+    sh = _run("tiny-qwen2", True, train_mode=train_mode)
+    rep = _run("tiny-qwen2", False, train_mode=train_mode)
+    for n, w in rep[0][2].items():
+        assert torch.allclose(sh[0][2][n], w, atol=2e-5, rtol=1e-4), n
+    from accerl_agent_b200.models.config import get_preset
+    from accerl_agent_b200.models.transformer import build_model
+
+    init = build_model(get_preset("tiny-qwen2"), "full", torch.device("cpu"), torch.float32)
+    init.init_weights(seed=42)
+    moved = [n for n, v in init.named_parameters() if not torch.equal(v, sh[0][2][n])]
+    assert moved and all(("lm_head" in n) or (train_mode == "last_layer" and "layers.1." in n) for n in moved)
 
 
 def test_shard_copy_plans_assemble_the_engine_weights():
