@@ -265,20 +265,43 @@ class TrainWorker:
         if dist_ready():
             dist.destroy_process_group()
 
-    def _wait_for_warmup(self) -> Dict[str, int]:
-        stats = self.get_replay_stats()
-        deadline = None
-        if self.args.replay_sample_timeout_seconds > 0:
-            deadline = time.monotonic() + self.args.replay_sample_timeout_seconds
-        while stats["size"] < self.args.min_replay_size_per_rank:
+    def _poll(self, attempt, describe):
+        """Call ``attempt()`` until it returns something truthy, sleeping ``--replay-wait-sleep-seconds``
+        between calls; after ``--replay-sample-timeout-seconds`` (0: no limit) raise TimeoutError with
+        the message ``describe()`` builds."""
+        limit = self.args.replay_sample_timeout_seconds
+        deadline = time.monotonic() + limit if limit > 0 else None
+        while True:
+            got = attempt()
+            if got:
+                return got
             if deadline is not None and time.monotonic() >= deadline:
-                raise TimeoutError(
-                    f"Timed out waiting for replay warmup: rank={self.rank} size={stats['size']} "
-                    f"min_replay_size_per_rank={self.args.min_replay_size_per_rank} stats={stats}"
-                )
+                raise TimeoutError(describe())
             time.sleep(self.args.replay_wait_sleep_seconds)
-            stats = self.get_replay_stats()
-        return stats
+
+    def _wait_for_warmup(self) -> Dict[str, int]:
+        need = self.args.min_replay_size_per_rank
+
+        def ready():
+            st = self.get_replay_stats()
+            return st if st["size"] >= need else None
+
+        def describe():
+            st = self.get_replay_stats()
+            return (f"Timed out waiting for replay warmup: rank={self.rank} size={st['size']} "
+                    f"min_replay_size_per_rank={need} stats={st}")
+
+        return self._poll(ready, describe)
+
+    def _draw_prepared(self, n: int, into: List[RLSample], limit: Optional[int] = None) -> int:
+        """Draw ``n`` replay samples, append the ones that survive preparation to ``into`` (at most
+        ``limit`` in total); returns how many were drawn."""
+        drawn = self.replay_buffer.sample(n)
+        for s in drawn:
+            prepared = prepare_rl_sample(s, self.args.rl_algorithm, self.args.max_length)
+            if prepared is not None and (limit is None or len(into) < limit):
+                into.append(prepared)
+        return len(drawn)
 
     def _all_reduce(self, t: torch.Tensor, op=None) -> torch.Tensor:
         if dist_ready() and self.fsdp_world_size > 1:
@@ -289,23 +312,12 @@ class TrainWorker:
     def _next_varlen_cpu_pack(self, trainer_version: float) -> PreparedVarlenPack:
         t0 = time.perf_counter()
         self._wait_for_warmup()
-        deadline = None
-        if self.args.replay_sample_timeout_seconds > 0:
-            deadline = time.monotonic() + self.args.replay_sample_timeout_seconds
-        while not self.pending_prepared_samples:
-            sampled = self.replay_buffer.sample(self.args.train_pack_candidate_pool_size)
-            for s in sampled:
-                prepared = prepare_rl_sample(s, self.args.rl_algorithm, self.args.max_length)
-                if prepared is not None:
-                    self.pending_prepared_samples.append(prepared)
-            if self.pending_prepared_samples:
-                break
-            if deadline is not None and time.monotonic() >= deadline:
-                raise TimeoutError(
-                    f"Timed out waiting for valid replay candidates: rank={self.rank} "
-                    f"target={self.args.train_pack_candidate_pool_size} stats={self.get_replay_stats()}"
-                )
-            time.sleep(self.args.replay_wait_sleep_seconds)
+        pool = self.args.train_pack_candidate_pool_size
+        if not self.pending_prepared_samples:
+            # candidates carry over between packs; refill only when every candidate was used
+            self._poll(lambda: self._draw_prepared(pool, self.pending_prepared_samples) and self.pending_prepared_samples,
+                       lambda: f"Timed out waiting for valid replay candidates: rank={self.rank} target={pool} "
+                               f"stats={self.get_replay_stats()}")
         selected, remaining = select_varlen_pack(
             self.pending_prepared_samples, self.args.train_token_budget, self.args.batch_size
         )
@@ -535,30 +547,13 @@ class TrainWorker:
     # ------------------------------------------------------------------ padded path
     def _next_padded_batch(self, trainer_version: float) -> Tuple[List[RLSample], float]:
         self._wait_for_warmup()
+        bs = self.args.batch_size
         collected: List[RLSample] = []
-        while len(collected) < self.args.batch_size:
-            need = self.args.batch_size - len(collected)
-            deadline = None
-            if self.args.replay_sample_timeout_seconds > 0:
-                deadline = time.monotonic() + self.args.replay_sample_timeout_seconds
-            sampled: List[RLSample] = []
-            while not sampled:
-                sampled = self.replay_buffer.sample(need)
-                if sampled:
-                    break
-                if deadline is not None and time.monotonic() >= deadline:
-                    raise TimeoutError(
-                        f"Timed out waiting for replay samples: rank={self.rank} have={len(collected)} "
-                        f"need={self.args.batch_size} stats={self.get_replay_stats()}"
-                    )
-                time.sleep(self.args.replay_wait_sleep_seconds)
-            for s in sampled:
-                prepared = prepare_rl_sample(s, self.args.rl_algorithm, self.args.max_length)
-                if prepared is not None:
-                    collected.append(prepared)
-                    if len(collected) >= self.args.batch_size:
-                        break
-        samples = collected[: self.args.batch_size]
+        while len(collected) < bs:  # each draw may lose samples to preparation; draw again for the rest
+            self._poll(lambda: self._draw_prepared(bs - len(collected), collected, limit=bs),
+                       lambda: f"Timed out waiting for replay samples: rank={self.rank} have={len(collected)} "
+                               f"need={bs} stats={self.get_replay_stats()}")
+        samples = collected[:bs]
         lag_sum, count = version_lag_stats(samples, trainer_version)
         return samples, lag_sum / count
 
