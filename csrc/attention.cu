@@ -72,12 +72,30 @@ struct AttnFwdParams {
   int max_blocks, block_size;
 };
 
+// Work order of the varlen kernels, launched as a (max_tiles * Hq) x num_seqs grid: blocks start in
+// increasing linear index, and the linear index is read tile-major -- tile rank outermost, then the
+// sequence, then the head -- so the longest-running tiles of EVERY sequence of a pack start first
+// (causal: the last query tiles in the forward, the first key tiles in the backward) instead of one
+// sequence after the other, which left the long tiles of the last sequences running alone at the end.
+struct TileSeqHead {
+  int tile, seq, head;
+};
+
+ACCERL_DEVINL TileSeqHead tile_major(int Hq) {
+  // the grid has far fewer than 2^32 blocks (tiles x heads x sequences of one pack)
+  const unsigned lin = blockIdx.y * gridDim.x + blockIdx.x;
+  const unsigned per_tile = static_cast<unsigned>(Hq) * gridDim.y;
+  const unsigned r = lin % per_tile;
+  return {static_cast<int>(lin / per_tile), static_cast<int>(r / Hq), static_cast<int>(r % Hq)};
+}
+
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnFwdParams p) {
-  const int head = blockIdx.x % p.Hq;
-  const int q_tile = p.max_tiles - 1 - static_cast<int>(blockIdx.x / p.Hq);
-  const int b = blockIdx.y;
+  const TileSeqHead at = tile_major(p.Hq);
+  const int head = at.head;
+  const int q_tile = p.max_tiles - 1 - at.tile;
+  const int b = at.seq;
   const int seq_start = p.cu[b];
   const int len = p.cu[b + 1] - seq_start;
   if (q_tile * kTile >= len) return;
@@ -1067,9 +1085,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     const __grid_constant__ CUtensorMap tmDQ, const AttnBwdParams p) {
-  const int head = blockIdx.x % p.Hq;
-  const int kt = static_cast<int>(blockIdx.x / p.Hq);
-  const int b = blockIdx.y;
+  const TileSeqHead at = tile_major(p.Hq);
+  const int head = at.head;
+  const int kt = at.tile;
+  const int b = at.seq;
   const int seq_start = p.cu[b];
   const int len = p.cu[b + 1] - seq_start;
   if (kt * kTile >= len) return;
@@ -1350,9 +1369,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_q64_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                         const __grid_constant__ CUtensorMap tmDQ, const AttnBwdParams p) {
-  const int head = blockIdx.x % p.Hq;
-  const int kt = static_cast<int>(blockIdx.x / p.Hq);
-  const int b = blockIdx.y;
+  const TileSeqHead at = tile_major(p.Hq);
+  const int head = at.head;
+  const int kt = at.tile;
+  const int b = at.seq;
   const int seq_start = p.cu[b];
   const int len = p.cu[b + 1] - seq_start;
   if (kt * kTile >= len) return;
