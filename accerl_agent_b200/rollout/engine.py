@@ -283,6 +283,10 @@ class GenerationEngine:
 
     # ------------------------------------------------------------------ public async API
     async def generate(self, prompt: Dict[str, List[int]], sampling_params: SamplingParams, request_id: str):
+        if getattr(sampling_params, "frequency_penalty", 0.0):
+            # accepted by the vLLM-shaped parameter object but not applied by this engine's sampler:
+            # refuse instead of sampling without it
+            raise ValueError("frequency_penalty is not supported by the native engine")
         if self._thread is None:
             self.start()
         loop = asyncio.get_running_loop()

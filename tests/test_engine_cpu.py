@@ -4,6 +4,7 @@ in-flight requests, and the interruptible runner resubmits prompt + partial outp
 
 import asyncio
 
+import pytest
 import torch
 
 from accerl_agent_b200.models.config import get_preset
@@ -139,3 +140,18 @@ def test_suspend_keeps_one_submission_and_tags_versions():
     assert state.output_versions == [0] * before + [1] * (N - before)
     assert len(state.output_logprobs) == N
     assert state.output_tokens == uninterrupted
+
+
+def test_unsupported_sampling_parameter_is_refused():
+    """A frequency penalty is not applied by the engine's sampler, so a request asking for one fails
+    instead of silently sampling without it."""
+    _, _, eng = make_engine()
+
+    async def run():
+        with pytest.raises(ValueError, match="frequency_penalty"):
+            async for _ in eng.generate({"prompt_token_ids": [3, 4]},
+                                        SamplingParams(max_tokens=2, frequency_penalty=0.5), "fp"):
+                pass
+        await eng.shutdown()
+
+    asyncio.run(run())
