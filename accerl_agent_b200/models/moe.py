@@ -245,48 +245,34 @@ def experts_backward_grouped(model, layer: int, dys_pad, xs_pad, gu, act, lay):
 
 
 def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save: bool):
+    """MoE MLP of one layer: ``residual + sum_j w_j expert_j(h) (+ shared expert)``. Three paths:
+    expert parallelism (``_moe_forward_ep``), the CUDA bf16 path (``_moe_forward_device``), and the
+    host path below (CPU tensors, other dtypes) with per-expert loops."""
     cfg = model.cfg
     k = cfg.num_experts_per_tok
     ep = getattr(model, "expert_parallel", None)
-    if ep is None and h.is_cuda and h.dtype == torch.bfloat16:
+    if ep is not None:
+        return _moe_forward_ep(model, layer, h, residual, save, ep)
+    if h.is_cuda and h.dtype == torch.bfloat16:
         shared_gate: list = []
         probs, topw, topi = route(model, layer, h, shared_gate=shared_gate)
         return _moe_forward_device(model, layer, h, residual, save, probs, topw, topi,
                                    sg=shared_gate[0].view(-1, 1) if shared_gate else None)
-    if ep is not None:
-        return _moe_forward_ep(model, layer, h, residual, save, ep)
     probs, topw, topi = route(model, layer, h)
     w_act = topw.to(h.dtype)
     order, counts, bounds = _expert_segments(topi, cfg.num_experts)
     El = cfg.local_experts
-    if ep is None and El is not None and El != cfg.num_experts:
+    if El is not None and El != cfg.num_experts:
         # tensor-parallel engine shard: only the (token, slot) pairs routed to this rank's experts;
-        # the caller all-reduces the partial outputs of the ranks (with expert parallelism every pair
-        # is dispatched to its owner instead)
+        # the caller all-reduces the partial outputs of the ranks
         lo = cfg.expert_offset
         a, b = bounds[lo], bounds[lo + El]
         order, counts = order[a:b], counts[lo : lo + El]
         bounds = [x - a for x in bounds[lo : lo + El + 1]]
     tok = torch.div(order, k, rounding_mode="floor")
-    lay = None
-    ep_state = None
-    if ep is not None:
-        e_sorted = topi.reshape(-1).index_select(0, order)
-        ys, ep_state = ep.forward(model, layer, h, tok, e_sorted, counts, bounds)
-        rows = torch.arange(order.numel(), device=h.device)
-        xs = gu = act = None
-    elif h.is_cuda and h.dtype == torch.bfloat16:
-        lay = padded_layout(counts.tolist(), h.device)
-        # row of every (token, slot) pair inside its expert's padded segment
-        seg = torch.tensor([lay["starts"][e] - bounds[e] for e in range(len(counts))], device=h.device)
-        rows = torch.arange(order.numel(), device=h.device) + seg.repeat_interleave(counts)
-        xs = torch.zeros(lay["total"], h.shape[1], dtype=h.dtype, device=h.device)
-        xs.index_copy_(0, rows, h.index_select(0, tok))
-        ys, gu, act = experts_forward_grouped(model, layer, xs, lay)
-    else:
-        xs = h.index_select(0, tok)
-        ys, gu, act = experts_forward(model, layer, xs, bounds)
-        rows = torch.arange(order.numel(), device=h.device)
+    xs = h.index_select(0, tok)
+    ys, gu, act = experts_forward(model, layer, xs, bounds)
+    rows = torch.arange(order.numel(), device=h.device)
     # per (token, slot) pair in token-major order: its row in ``ys`` and its weight (pairs this rank
     # does not run keep weight 0)
     n_pairs = topi.numel()
@@ -304,10 +290,6 @@ def moe_forward(model, layer: int, h: torch.Tensor, residual: torch.Tensor, save
         cache.update(probs=probs, topw=topw, topi=topi, order=order, tok=tok, xs=xs, gu=gu, act=act, ys=ys,
                      pos_pairs=pos_pairs, w_pairs=w_pairs)
         cache["bounds"] = torch.tensor(bounds)
-        if ep_state is not None:
-            cache["ep_state"] = ep_state  # type: ignore[assignment]
-        if lay is not None:
-            cache["layout"] = lay  # type: ignore[assignment]
     return out, cache
 
 
