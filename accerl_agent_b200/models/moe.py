@@ -11,7 +11,7 @@ exchanged between ranks before and after the expert GEMMs.
 
 from __future__ import annotations
 
-from typing import Dict, Optional, Tuple
+from typing import Dict, Optional
 
 import torch
 

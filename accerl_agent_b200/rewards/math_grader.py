@@ -129,24 +129,6 @@ def normalize_answer(ans: str) -> str:
 _NUM = re.compile(r"^[+-]?(\d+(\.\d*)?|\.\d+)(e[+-]?\d+)?$")
 
 
-def _to_number(s: str) -> Optional[float]:
-    s = s.strip()
-    pct = s.endswith("%")
-    if pct:
-        s = s[:-1]
-    s = s.replace("(", "").replace(")", "")
-    val: Optional[float] = None
-    if _NUM.match(s):
-        val = float(s)
-    elif s.count("/") == 1:
-        a, b = s.split("/")
-        if _NUM.match(a) and _NUM.match(b) and float(b) != 0.0:
-            val = float(a) / float(b)
-    if val is None:
-        return None
-    return val / 100.0 if pct else val
-
-
 _INT_FRAC = re.compile(r"^-?\d+/0*[1-9]\d*$")
 
 
