@@ -32,7 +32,7 @@ parallelism.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, List, Optional
+from typing import Callable, Dict, List, Optional
 
 import torch
 import torch.distributed as dist
@@ -146,8 +146,12 @@ class LayerShardedParams:
         self.nccl = dist.is_initialized() and dist.get_backend(group) == "nccl"
         self.comm = torch.cuda.Stream(device) if self.cuda else None
         self.resident: List[Optional[int]] = [None, None]  # layer held by each ping-pong buffer
-        self._gather_work: List[Optional[object]] = [None, None]
-        self._rs_done = [None, None]  # events: the reduce-scatter that last read each gradient buffer
+        # per ping-pong buffer: how the compute stream waits for its pending gather (None: nothing
+        # pending), and the event of the reduce-scatter that last read its gradient buffer
+        self._gather_wait: List[Optional[Callable[[], None]]] = [None, None]
+        self._gather_ev = [torch.cuda.Event() for _ in range(2)] if self.cuda else [None, None]
+        self._rs_done = [torch.cuda.Event() for _ in range(2)] if self.cuda else [None, None]
+        self._rs_pending = [False, False]
         self.params_dirty = True  # shards changed since the pinned units were gathered
         self.model = CausalLM.without_buffers(cfg, self.layout)
         self.model.units = self
@@ -211,9 +215,13 @@ class LayerShardedParams:
         if self.cuda:
             self.comm.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm):
-                self._gather_work[b] = self._gather(u, self.pbuf[b], async_op=True)
-                if self._gather_work[b] is None:  # a single rank: the copy ran on the comm stream
-                    self._gather_work[b] = "stream"
+                work = self._gather(u, self.pbuf[b], async_op=True)
+                if work is not None:
+                    self._gather_wait[b] = work.wait  # waits on the current (compute) stream
+                else:  # a single rank: the copy ran on the comm stream
+                    ev = self._gather_ev[b]
+                    ev.record(self.comm)
+                    self._gather_wait[b] = lambda ev=ev: torch.cuda.current_stream(self.device).wait_event(ev)
         else:
             self._gather(u, self.pbuf[b], async_op=False)
         self.resident[b] = layer
@@ -222,13 +230,10 @@ class LayerShardedParams:
         b = layer % 2
         if self.resident[b] != layer:
             self._issue_layer_gather(layer)
-        w = self._gather_work[b]
-        if w is not None:
-            if w == "stream":
-                torch.cuda.current_stream(self.device).wait_stream(self.comm)
-            else:
-                w.wait()
-            self._gather_work[b] = None
+        wait = self._gather_wait[b]
+        if wait is not None:
+            wait()
+            self._gather_wait[b] = None
 
     # ---------------------------------------------------------------- hooks called by the model
     def begin_forward(self) -> None:
@@ -249,7 +254,7 @@ class LayerShardedParams:
     def before_backward(self, layer: int) -> None:
         b = layer % 2
         self._await_layer(layer)
-        if self.cuda and self._rs_done[b] is not None:
+        if self.cuda and self._rs_pending[b]:
             torch.cuda.current_stream(self.device).wait_event(self._rs_done[b])
         u = self.layer_unit[layer]
         if u.trainable:
@@ -267,9 +272,8 @@ class LayerShardedParams:
             self.comm.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm):
                 self._reduce_scatter_add(u, self.gbuf[b], self.gtmp[b])
-                ev = torch.cuda.Event()
-                ev.record(self.comm)
-                self._rs_done[b] = ev
+                self._rs_done[b].record(self.comm)
+                self._rs_pending[b] = True
         else:
             self._reduce_scatter_add(u, self.gbuf[b], self.gtmp[b])
         for name in u.names:
