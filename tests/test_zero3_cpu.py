@@ -233,3 +233,34 @@ def test_split_by_pieces_random_copies():
         for r, pl in enumerate(split_by_pieces([d], pieces, 3)):
             apply_map_torch(bufs[r], got, pl)
         assert torch.equal(want, got)
+
+
+@pytest.mark.parametrize("train_mode,tied", [("full", False), ("lm_head", False), ("last_layer", False),
+                                             ("lm_head", True)])
+def test_units_cover_the_layout_and_split_by_trainability(train_mode, tied):
+    """Units tile the parameter layout without gaps, every unit is trained whole or frozen whole, a
+    decoder layer is one unit, and the trainable units' shards come first in local storage."""
+    from accerl_agent_b200.models.config import get_preset
+    from accerl_agent_b200.parallel.zero3 import build_units, sharded_layout
+
+    cfg = get_preset("tiny-qwen2")
+    cfg.tie_word_embeddings = tied
+    layout = sharded_layout(cfg, train_mode)
+    flags = {n: s.trainable for n, s in layout.slots.items()}
+    units = build_units(layout, 3, flags)
+    ordered = sorted(units, key=lambda u: u.lo)
+    assert ordered[0].lo == 0
+    for a, b in zip(ordered, ordered[1:]):
+        assert a.lo + a.span == b.lo
+    assert [n for u in ordered for n in u.names] == list(layout.order)
+    for u in units:
+        assert {flags[n] for n in u.names} == {u.trainable}
+        assert u.numel % (3 * 64) == 0 and u.shard * 3 == u.numel
+    layers = [u.layer for u in units if u.layer >= 0]
+    assert sorted(layers) == list(range(cfg.num_hidden_layers))
+    n_train = sum(u.shard for u in units if u.trainable)
+    assert all(u.base < n_train for u in units if u.trainable) and all(u.base >= n_train for u in units
+                                                                       if not u.trainable)
+    if train_mode == "lm_head":
+        trained = {n for u in units if u.trainable for n in u.names}
+        assert trained == ({"model.embed_tokens.weight"} if tied else {"lm_head.weight"})
